@@ -1,0 +1,199 @@
+/*
+ * orthrus_b200.h — C ABI of the Blackwell (sm_100a) kernels behind the Orthrus dual-view path.
+ *
+ * The Python drop-in modules (orthrus_training_b200.modeling_orthrus / objective / decoding) call
+ * these entry points through ctypes; any other host (C++, a cgo or JNI binding) can call them the
+ * same way. Conventions shared by every entry point:
+ *   - plain device pointers and sizes, no framework types; every buffer is allocated by the caller
+ *     (outputs and, where a *_workspace_bytes query exists, scratch memory);
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); work is enqueued asynchronously;
+ *   - the return value is a status: ORTHRUS_OK, or a negative ORTHRUS_E* code for bad arguments or a
+ *     failed launch. Kernels never trap: a device-side wait that runs out of time (2 s) records a
+ *     bit in the device error word, read with orthrus_device_error();
+ *   - dtype codes: ORTHRUS_BF16 (tensor-core path) or ORTHRUS_F32 (exact fp32 path on CUDA cores);
+ *   - no global mutable state besides the device error word.
+ *
+ * Each entry point names the reference interface it replaces (paths inside the reference project
+ * ekonst41/orthrus-training).
+ */
+#ifndef ORTHRUS_B200_H
+#define ORTHRUS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------------------------ */
+#define ORTHRUS_OK 0
+#define ORTHRUS_EINVAL (-1)       /* bad argument: shape, pointer alignment, unsupported size   */
+#define ORTHRUS_ECUDA (-2)        /* a CUDA runtime call or kernel launch failed                */
+#define ORTHRUS_EWORKSPACE (-3)   /* caller workspace smaller than *_workspace_bytes reported    */
+#define ORTHRUS_EDEVICE (-4)      /* orthrus_device_error found the device error word non-zero   */
+
+/* ---- device error word bits ------------------------------------------------------------- */
+#define ORTHRUS_ERR_TIMEOUT 1u    /* a bounded wait (mbarrier / flag) ran out of time            */
+#define ORTHRUS_ERR_BOUNDS 2u     /* a device-side index check failed; the access was skipped    */
+
+/* ---- dtypes ----------------------------------------------------------------------------- */
+#define ORTHRUS_BF16 0
+#define ORTHRUS_F32 1
+
+/* ---- attention mask modes (orthrus_attn_fwd / orthrus_attn_bwd) ------------------------- */
+/* Query t of batch b sees source-1 keys [0, e1) and source-2 keys [s2, e2):                   */
+#define ORTHRUS_MASK_CAUSAL 0  /* e1 = t + 1 + offset[b] (offset NULL = 0); no source 2         */
+#define ORTHRUS_MASK_DUAL 1    /* blk = t / block: e1 = min(anchors[b, blk], L1),               */
+                               /* [s2, e2) = [blk*block, blk*block + block)                     */
+#define ORTHRUS_MASK_DRAFT 2   /* e1 = offset[b]; [s2, e2) = [0, min(L2, limit2[b]))             */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int orthrus_version(void);
+
+/* Reads the device error word of `device` (synchronizes that device) into *word; clears it when
+ * `clear` is non-zero. Returns ORTHRUS_OK, or ORTHRUS_EDEVICE when the word was non-zero. */
+int orthrus_device_error(int device, unsigned int* word, int clear);
+
+/* ---- dense GEMM building block (tcgen05) ------------------------------------------------- */
+/* C[M, N] = A[M, K] @ B^T, bf16 inputs, fp32 accumulation in tensor memory.
+ *   b_kn = 0: B is [N, K] row-major (ldb >= K); b_kn = 1: B is [K, N] row-major (ldb >= N).
+ *   c_f32 = 1 writes fp32 C, else bf16. Leading dimensions are in elements and multiples of 8.
+ *   The per-element reduction order depends on (N, K) only, never on M: results for a row are
+ *   bit-identical whatever M is (used for lossless decoding).
+ * Replaces the cuBLAS GEMM of F.linear / torch.mm (orthrus/objective.py:139-149,303-313,384). */
+size_t orthrus_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int orthrus_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                      int64_t M, int64_t N, int64_t K, int b_kn, int c_f32, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Same contract for fp32 (or bf16-in, fp32-accumulate) operands on CUDA cores, B as [N, K]:
+ * exact fp32 arithmetic with a fixed reduction order that does not depend on M. */
+size_t orthrus_gemm_simt_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int orthrus_gemm_simt(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                      int64_t M, int64_t N, int64_t K, int dtype, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* ---- q/k RMSNorm + RoPE + head-major layout (fused prologue of the attention) ------------- */
+/* qkv: [rows = B*T, (Hq + 2*Hkv) * hd] token-major projection output (q | k | v columns).
+ * positions: [B, T] int64 RoPE positions. Writes
+ *   q_out [B, Hq, T, D]            (norm + RoPE), D = padded head dim (>= hd, zero padding)
+ *   k_out [B, Hkv, cap, D] at row offset[b] + t (norm + RoPE), v_out likewise (copy);
+ *   rstd [rows, Hq + Hkv] fp32 (saved for the backward; may be NULL).
+ * offset may be NULL (0). cap >= offset[b] + T. dtype applies to qkv and all outputs.
+ * Replaces _attention_inputs (orthrus/objective.py:136-143) and the q/k norm + apply_rotary_pos_emb
+ * of OrthrusAttention.forward (orthrus/modeling_orthrus.py:153-159) plus DynamicCache.update. */
+int orthrus_qkv_prep_fwd(const void* qkv, const int64_t* positions, const void* q_norm_w,
+                         const void* k_norm_w, int64_t B, int64_t T, int Hq, int Hkv, int hd, int D,
+                         float eps, float theta, void* q_out, void* k_out, void* v_out, int64_t cap,
+                         const int32_t* offset, float* rstd, int dtype, void* stream);
+
+/* Backward of orthrus_qkv_prep_fwd for training (offset 0, cap = T):
+ *   dq [B, Hq, T, D] fp32, dk [B, Hkv, T, D] fp32, dv [B, Hkv, T, D] fp32 (any may be NULL = 0)
+ *   -> dqkv [rows, (Hq + 2 Hkv) hd] (dtype), dq_norm_w / dk_norm_w [hd] fp32 (overwritten).
+ * workspace: orthrus_qkv_prep_bwd_workspace_bytes(). */
+size_t orthrus_qkv_prep_bwd_workspace_bytes(int64_t B, int64_t T, int hd);
+int orthrus_qkv_prep_bwd(const void* qkv, const int64_t* positions, const void* q_norm_w,
+                         const void* k_norm_w, const float* rstd, const float* dq, const float* dk,
+                         const float* dv, int64_t B, int64_t T, int Hq, int Hkv, int hd, int D,
+                         float theta, void* dqkv, float* dq_norm_w, float* dk_norm_w,
+                         void* workspace, size_t workspace_bytes, int dtype, void* stream);
+
+/* ---- dual-view attention --------------------------------------------------------------- */
+/* Per-anchor tile map of the dual-view mask (K3): for every 128-query tile of each row,
+ * tilemap[b, tile] = {number of source-1 key tiles to visit, first source-2 key, source-2 keys}.
+ * anchors [B, A] int64 sorted per row, block = K. Output int32 [B, ceil(A*K/128), 4].
+ * Replaces build_block_mask / create_block_mask (orthrus/modeling_orthrus.py:58-74) and
+ * skip_ar_key_grads (orthrus/objective.py:168-198): the backward never visits source-1 keys
+ * for dK/dV. */
+int orthrus_attn_tilemap(const int64_t* anchors, int64_t B, int64_t A, int block, int64_t L1,
+                         int32_t* tilemap, void* stream);
+
+/* Forward. q [B, Hq, Tq, D]; source 1: k1/v1 with row pitch D, head stride s1h, batch stride s1b
+ * (elements), L1 rows; source 2: k2/v2 (stride s2h, s2b, L2 rows; NULL when unused).
+ * o: token-major [B, Tq, Hq, hd] (the o_proj input), lse [B, Hq, Tq] fp32 (may be NULL).
+ * mask: ORTHRUS_MASK_* with anchors [B, A] int64 (DUAL), offset [B] int32 (CAUSAL/DRAFT) and
+ * limit2 [B] int32 (DRAFT, may be NULL). scale = 1/sqrt(hd).
+ * bf16 runs the tcgen05 tile kernel (D = 128 or 64); fp32 runs the exact CUDA-core kernel.
+ * Replaces F.scaled_dot_product_attention (orthrus/objective.py:155), flex_attention with the
+ * dual-pass BlockMask (orthrus/objective.py:163; orthrus/modeling_orthrus.py:77-85) and the
+ * generation-time attention of OrthrusAttention (orthrus/modeling_orthrus.py:167-188). */
+int orthrus_attn_fwd(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b,
+                     int64_t L1, const void* k2, const void* v2, int64_t s2h, int64_t s2b,
+                     int64_t L2, int64_t B, int Hq, int Hkv, int64_t Tq, int hd, int D, float scale,
+                     int mask, const int64_t* anchors, int64_t A, int block, const int32_t* offset,
+                     const int32_t* limit2, void* o, float* lse, int dtype, void* stream);
+
+/* Backward of the DUAL mask (training): from do_ [B, Tq, Hq, hd] (token-major), o, lse, q and the
+ * two sources, writes dq [B, Hq, Tq, D] fp32 and dk2 / dv2 [B, Hkv, L2, D] fp32 (source-2 keys
+ * only: source-1 keys are the frozen teacher's and get no gradient).
+ * workspace: orthrus_attn_bwd_workspace_bytes(). */
+size_t orthrus_attn_bwd_workspace_bytes(int64_t B, int Hq, int64_t Tq);
+int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b,
+                     int64_t L1, const void* k2, const void* v2, int64_t s2h, int64_t s2b,
+                     int64_t L2, int64_t B, int Hq, int Hkv, int64_t Tq, int hd, int D, float scale,
+                     const int64_t* anchors, int64_t A, int block, const void* o, const float* lse,
+                     const void* do_, float* dq, float* dk2, float* dv2, void* workspace,
+                     size_t workspace_bytes, int dtype, void* stream);
+
+/* ---- fused LM head + log-softmax + KL(teacher || student) ------------------------------- */
+/* total = sum_r w_r KL(softmax(W t[index[r]]) || softmax(W s[r])), kl_rows[r], agree[r] (top-1
+ * match, lowest index wins ties), and, when grad != NULL, grad[r] = w_r (p_s - p_t)[r] @ W
+ * (the d(total)/d(student) that the reference saves for backward).
+ * student [n, d], teacher [m, d] (unique target rows), index [n] non-decreasing in [0, m),
+ * weight [V, d], row_weight [n] fp32 or NULL (w = 1), offsets [n] int64 (block offset of each row)
+ * or NULL; per-offset outputs kl_by_offset [num_offsets] fp32 and agree_by_offset
+ * [num_offsets] int64 when offsets != NULL. Logits are never written to memory; the bf16
+ * probability difference of chunk_rows rows at a time lives in the workspace.
+ * Replaces FusedLinearForwardKL (orthrus/objective.py:338-392) with _logits / kl_chunk
+ * (:303-332) and the stats of orthrus_loss (:440-452). */
+size_t orthrus_lmhead_kl_workspace_bytes(int64_t n, int64_t m, int64_t V, int64_t d,
+                                         int64_t chunk_rows, int dtype);
+int orthrus_lmhead_kl_fwd(const void* student, int64_t n, const void* teacher, int64_t m,
+                          const int64_t* index, const void* weight, int64_t V, int64_t d,
+                          const float* row_weight, const int64_t* offsets, int num_offsets,
+                          float* total, float* kl_rows, uint8_t* agree, void* grad,
+                          float* kl_by_offset, int64_t* agree_by_offset, int64_t chunk_rows,
+                          void* workspace, size_t workspace_bytes, int dtype, void* stream);
+
+/* grad_student[i] = grad[i] * grad_total[0], count elements (FusedLinearForwardKL.backward,
+ * orthrus/objective.py:389-392). */
+int orthrus_lmhead_kl_bwd(const void* grad, const float* grad_total, void* grad_student,
+                          int64_t count, int dtype, void* stream);
+
+/* ---- parallel block decoding ----------------------------------------------------------- */
+/* Row-wise argmax of fp32 logits [R, V] (lowest index on ties, as torch.argmax), R rows at
+ * row pitch ldl: out[r] int64. */
+int orthrus_argmax_rows(const float* logits, int64_t ldl, int64_t R, int64_t V, int64_t* out,
+                        void* stream);
+
+/* Draft step (K7) for B sequences: logits [B, K, V] fp32 of the diffusion pass over
+ * [anchor, mask x K-1]; writes verify_ids [B, K] = [anchor, argmax of positions 0..K-2].
+ * Sequences with done[b] != 0 are left untouched.
+ * Replaces the draft half of OrthrusLM.diffusion_generate (orthrus/modeling_orthrus.py:469-487)
+ * and ModelBackend.draft (orthrus/decoding.py:178-206). */
+int orthrus_decode_draft(const float* logits, int64_t B, int K, int64_t V, const int64_t* anchor,
+                         const uint8_t* done, int64_t* verify_ids, void* stream);
+
+/* Verify + greedy accept + rollback (K8) for B sequences, entirely on device:
+ *   ar = argmax(verify logits [B, K, V]); accepted = longest prefix with drafts == ar, limited to
+ *   block_len - 1 = min(K, max_len[b] - start[b]) - 1 and ending after an accepted EOS;
+ *   appends the kept tokens and the bonus token to out_tokens [B, out_cap] at out_len[b];
+ *   start[b] += accepted + 1 (the KV-cache length rollback: positions past it are dead);
+ *   anchor[b] = bonus; accepted_log[b, cycle[b]] = accepted; done[b] on EOS or max length.
+ * eos: int64 [n_eos] (n_eos may be 0).
+ * Replaces the verify / accept / truncate_cache half of OrthrusLM.diffusion_generate
+ * (orthrus/modeling_orthrus.py:489-533), decoding._verify / _advance / ModelBackend.commit
+ * (orthrus/decoding.py:248-264,336-369). */
+int orthrus_decode_verify_accept(const float* logits, int64_t B, int K, int64_t V,
+                                 const int64_t* verify_ids, const int64_t* eos, int n_eos,
+                                 const int32_t* max_len, int32_t* start, int64_t* anchor,
+                                 uint8_t* done, int64_t* out_tokens, int32_t* out_len,
+                                 int64_t out_cap, int32_t* accepted_log, int32_t* cycle,
+                                 int64_t log_cap, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ORTHRUS_B200_H */

@@ -1,0 +1,260 @@
+// q/k RMSNorm + RoPE + head-major layout, forward and backward.
+//
+// Reference math (orthrus/objective.py:128-143; transformers Qwen3RMSNorm / apply_rotary_pos_emb):
+//   y = w * (x * rsqrt(mean(x^2) + eps)), then rope(y) = y * cos + rotate_half(y) * sin with
+//   rotate_half(y) = [-y2, y1], angle(pos, i) = pos * inv_freq[i mod hd/2]. cos / sin are rounded to
+//   the activation dtype before use, as the reference's rotary embedding returns them in x.dtype.
+// One warp per (token row, head): the warp reads the head's hd values of the fused projection
+// output, reduces the sum of squares with shuffles (fixed order), and writes the normalised,
+// rotated row into the head-major [B, H, rows, D] buffer (D >= hd, zero padding) that the attention
+// kernels read with TMA. Values are also written into a KV cache at a per-sequence row offset.
+#pragma once
+
+#include "gemm_simt.cuh"
+
+namespace orthrus {
+
+template <typename T>
+__device__ __forceinline__ float round_to(float v) {
+  return to_f32<T>(from_f32<T>(v));
+}
+
+// kind: 0 = q heads, 1 = k heads, 2 = v heads
+template <typename T>
+__global__ void __launch_bounds__(256) qkv_prep_fwd_kernel(
+    const T* __restrict__ qkv, const int64_t* __restrict__ positions, const float* __restrict__ inv_freq,
+    const T* __restrict__ q_norm_w, const T* __restrict__ k_norm_w, int64_t B, int64_t Tn, int Hq, int Hkv,
+    int hd, int D, float eps, T* __restrict__ q_out, T* __restrict__ k_out, T* __restrict__ v_out, int64_t cap,
+    const int32_t* __restrict__ offset, float* __restrict__ rstd_out) {
+  __shared__ float buf[8][128];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int heads = Hq + 2 * Hkv;
+  const int64_t items = B * Tn * heads;
+  const int64_t item = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  if (item >= items) return;
+  const int64_t row = item / heads;
+  const int head = static_cast<int>(item % heads);
+  const int64_t b = row / Tn, t = row % Tn;
+  const int C = heads * hd;
+  const T* x = qkv + row * C + static_cast<int64_t>(head) * hd;
+  const int half = hd >> 1;
+  float* sh = buf[warp];
+
+  if (head >= Hq + Hkv) {  // v: copy into the (cache) layout
+    const int hv = head - Hq - Hkv;
+    const int64_t orow = (offset ? offset[b] : 0) + t;
+    T* dst = v_out + ((b * Hkv + hv) * cap + orow) * D;
+    for (int e = lane; e < D; e += 32) dst[e] = e < hd ? x[e] : from_f32<T>(0.f);
+    return;
+  }
+  const bool is_q = head < Hq;
+  const T* w = is_q ? q_norm_w : k_norm_w;
+  float ss = 0.f;
+  for (int e = lane; e < hd; e += 32) {
+    const float v = to_f32<T>(x[e]);
+    sh[e] = v;
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float rstd = rsqrtf(ss / static_cast<float>(hd) + eps);
+  __syncwarp();
+  // normalised and weighted, rounded to the activation dtype as the reference does
+  for (int e = lane; e < hd; e += 32) sh[e] = round_to<T>(to_f32<T>(w[e]) * round_to<T>(sh[e] * rstd));
+  __syncwarp();
+  const float pos = static_cast<float>(positions[row]);
+  T* dst;
+  if (is_q) {
+    dst = q_out + ((b * Hq + head) * Tn + t) * D;
+  } else {
+    const int64_t orow = (offset ? offset[b] : 0) + t;
+    dst = k_out + ((b * Hkv + (head - Hq)) * cap + orow) * D;
+  }
+  for (int e = lane; e < D; e += 32) {
+    float out = 0.f;
+    if (e < hd) {
+      const int i = e < half ? e : e - half;
+      const float ang = pos * inv_freq[i];
+      float c, s;
+      sincosf(ang, &s, &c);
+      c = round_to<T>(c);
+      s = round_to<T>(s);
+      const float rot = e < half ? -sh[e + half] : sh[e - half];
+      out = sh[e] * c + rot * s;
+    }
+    dst[e] = from_f32<T>(out);
+  }
+  if (rstd_out && lane == 0) rstd_out[row * (Hq + Hkv) + head] = rstd;
+}
+
+// Backward for q (kind 0) or k (kind 1) heads. Fixed work split: grid-stride over (row, head)
+// items with a grid that depends only on the problem size; each warp keeps its norm-weight
+// gradient partial in registers, the CTA sums its warps in order into part[blockIdx.x][hd].
+template <typename T>
+__global__ void __launch_bounds__(256) qkv_prep_bwd_kernel(
+    const T* __restrict__ qkv, const int64_t* __restrict__ positions, const float* __restrict__ inv_freq,
+    const T* __restrict__ norm_w, const float* __restrict__ rstd, const float* __restrict__ dy, int64_t B,
+    int64_t Tn, int Hq, int Hkv, int hd, int D, int kind, T* __restrict__ dqkv, float* __restrict__ part) {
+  __shared__ float gsh[8][128];
+  __shared__ float xsh[8][128];
+  __shared__ float wpart[8][128];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int heads = Hq + 2 * Hkv;
+  const int H = kind == 0 ? Hq : Hkv;
+  const int head0 = kind == 0 ? 0 : Hq;
+  const int64_t items = B * Tn * H;
+  const int C = heads * hd;
+  const int half = hd >> 1;
+  float wacc[4] = {0.f, 0.f, 0.f, 0.f};
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * 8;
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * 8 + warp; item < items; item += stride) {
+    const int64_t row = item / H;
+    const int h = static_cast<int>(item % H);
+    const int64_t b = row / Tn, t = row % Tn;
+    const T* x = qkv + row * C + static_cast<int64_t>(head0 + h) * hd;
+    const float* g = dy + ((b * H + h) * Tn + t) * D;
+    const float r = rstd[row * (Hq + Hkv) + head0 + h];
+    const float pos = static_cast<float>(positions[row]);
+    for (int e = lane; e < hd; e += 32) {
+      gsh[warp][e] = g[e];
+      xsh[warp][e] = to_f32<T>(x[e]) * r;  // xhat
+    }
+    __syncwarp();
+    // undo the rotation: g_j = dy_j c_j + dy_{j+h} s_{j+h} (j < h), dy_j c_j - dy_{j-h} s_{j-h}
+    float gn[4];
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int e = lane + 32 * k;
+      gn[k] = 0.f;
+      if (e < hd) {
+        const int i = e < half ? e : e - half;
+        float c, s;
+        sincosf(pos * inv_freq[i], &s, &c);
+        c = round_to<T>(c);
+        s = round_to<T>(s);
+        const float other = e < half ? gsh[warp][e + half] : -gsh[warp][e - half];
+        const float gr = gsh[warp][e] * c + other * s;
+        gn[k] = gr;
+        wacc[k] = fmaf(gr, xsh[warp][e], wacc[k]);
+        dot = fmaf(gr * to_f32<T>(norm_w[e]), xsh[warp][e], dot);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    const float mean = dot / static_cast<float>(hd);
+    T* out = dqkv + row * C + static_cast<int64_t>(head0 + h) * hd;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int e = lane + 32 * k;
+      if (e < hd) out[e] = from_f32<T>(r * (gn[k] * to_f32<T>(norm_w[e]) - xsh[warp][e] * mean));
+    }
+    __syncwarp();
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int e = lane + 32 * k;
+    if (e < 128) wpart[warp][e] = e < hd ? wacc[k] : 0.f;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < hd; e += blockDim.x) {
+    float acc = 0.f;
+    for (int w = 0; w < 8; ++w) acc += wpart[w][e];
+    part[static_cast<int64_t>(blockIdx.x) * hd + e] = acc;
+  }
+}
+
+template <typename T>
+__global__ void copy_v_grad_kernel(const float* __restrict__ dv, int64_t B, int64_t Tn, int Hq, int Hkv, int hd,
+                                   int D, T* __restrict__ dqkv) {
+  const int heads = Hq + 2 * Hkv;
+  const int64_t total = B * Tn * Hkv * hd;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int e = static_cast<int>(i % hd);
+    const int64_t rest = i / hd;
+    const int h = static_cast<int>(rest % Hkv);
+    const int64_t row = rest / Hkv;
+    const int64_t b = row / Tn, t = row % Tn;
+    const float v = dv ? dv[((b * Hkv + h) * Tn + t) * D + e] : 0.f;
+    dqkv[row * heads * hd + static_cast<int64_t>(Hq + Hkv + h) * hd + e] = from_f32<T>(v);
+  }
+}
+
+template <typename T>
+__global__ void zero_heads_kernel(int64_t rows, int heads, int hd, int head0, int nheads, T* __restrict__ dqkv) {
+  const int64_t total = rows * nheads * hd;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int e = static_cast<int>(i % hd);
+    const int64_t rest = i / hd;
+    const int h = static_cast<int>(rest % nheads);
+    const int64_t row = rest / nheads;
+    dqkv[row * heads * hd + static_cast<int64_t>(head0 + h) * hd + e] = from_f32<T>(0.f);
+  }
+}
+
+__global__ void sum_partials_kernel(const float* __restrict__ part, int nparts, int hd, float* __restrict__ out) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= hd) return;
+  float acc = 0.f;
+  for (int p = 0; p < nparts; ++p) acc += part[static_cast<int64_t>(p) * hd + e];
+  out[e] = acc;
+}
+
+constexpr int kPrepBwdBlocks = 592;  // fixed grid (4 x 148): a deterministic split of the items
+
+template <typename T>
+int qkv_prep_fwd_impl(const T* qkv, const int64_t* positions, const float* inv_freq, const T* qw, const T* kw,
+                      int64_t B, int64_t Tn, int Hq, int Hkv, int hd, int D, float eps, T* q_out, T* k_out,
+                      T* v_out, int64_t cap, const int32_t* offset, float* rstd, cudaStream_t stream) {
+  ORTHRUS_CHECK_ARG(qkv && positions && inv_freq && qw && kw && q_out && k_out && v_out);
+  ORTHRUS_CHECK_ARG(B > 0 && Tn > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0);
+  ORTHRUS_CHECK_ARG(hd >= 2 && hd % 2 == 0 && hd <= 128 && D >= hd && D <= 128 && cap >= Tn);
+  const int64_t items = B * Tn * (Hq + 2 * Hkv);
+  qkv_prep_fwd_kernel<T><<<static_cast<unsigned>(ceil_div(items, 8)), 256, 0, stream>>>(
+      qkv, positions, inv_freq, qw, kw, B, Tn, Hq, Hkv, hd, D, eps, q_out, k_out, v_out, cap, offset, rstd);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+inline size_t qkv_prep_bwd_ws(int hd) { return static_cast<size_t>(2) * kPrepBwdBlocks * hd * sizeof(float); }
+
+template <typename T>
+int qkv_prep_bwd_impl(const T* qkv, const int64_t* positions, const float* inv_freq, const T* qw, const T* kw,
+                      const float* rstd, const float* dq, const float* dk, const float* dv, int64_t B, int64_t Tn,
+                      int Hq, int Hkv, int hd, int D, T* dqkv, float* dqw, float* dkw, void* ws, size_t ws_bytes,
+                      cudaStream_t stream) {
+  ORTHRUS_CHECK_ARG(qkv && positions && inv_freq && qw && kw && rstd && dqkv && dqw && dkw);
+  ORTHRUS_CHECK_ARG(B > 0 && Tn > 0 && hd >= 2 && hd % 2 == 0 && hd <= 128 && D >= hd && D <= 128);
+  if (ws == nullptr || ws_bytes < qkv_prep_bwd_ws(hd)) return ORTHRUS_EWORKSPACE;
+  float* part_q = static_cast<float*>(ws);
+  float* part_k = part_q + static_cast<int64_t>(kPrepBwdBlocks) * hd;
+  const int heads = Hq + 2 * Hkv;
+  const int64_t rows = B * Tn;
+  if (dq) {
+    qkv_prep_bwd_kernel<T><<<kPrepBwdBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, qw, rstd, dq, B, Tn, Hq,
+                                                               Hkv, hd, D, 0, dqkv, part_q);
+    ORTHRUS_CHECK_LAUNCH();
+    sum_partials_kernel<<<1, 128, 0, stream>>>(part_q, kPrepBwdBlocks, hd, dqw);
+  } else {
+    zero_heads_kernel<T><<<592, 256, 0, stream>>>(rows, heads, hd, 0, Hq, dqkv);
+    ORTHRUS_CHECK_CUDA(cudaMemsetAsync(dqw, 0, hd * sizeof(float), stream));
+  }
+  ORTHRUS_CHECK_LAUNCH();
+  if (dk) {
+    qkv_prep_bwd_kernel<T><<<kPrepBwdBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, kw, rstd, dk, B, Tn, Hq,
+                                                               Hkv, hd, D, 1, dqkv, part_k);
+    ORTHRUS_CHECK_LAUNCH();
+    sum_partials_kernel<<<1, 128, 0, stream>>>(part_k, kPrepBwdBlocks, hd, dkw);
+  } else {
+    zero_heads_kernel<T><<<592, 256, 0, stream>>>(rows, heads, hd, Hq, Hkv, dqkv);
+    ORTHRUS_CHECK_CUDA(cudaMemsetAsync(dkw, 0, hd * sizeof(float), stream));
+  }
+  ORTHRUS_CHECK_LAUNCH();
+  copy_v_grad_kernel<T><<<592, 256, 0, stream>>>(dv, B, Tn, Hq, Hkv, hd, D, dqkv);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+}  // namespace orthrus

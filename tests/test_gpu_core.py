@@ -1,0 +1,155 @@
+"""GEMM and fused LM-head + KL kernels against the oracle / an fp32 torch reference (GPU only)."""
+
+import pytest
+import torch
+from conftest import load_golden
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _ops():
+    from orthrus_training_b200 import ops
+
+    return ops
+
+
+def _ref_mm(a, b, b_kn=False):
+    bb = b.double() if b_kn else b.double().t()
+    return (a.double() @ bb).float()
+
+
+@pytest.mark.parametrize("M,N,K,b_kn", [(300, 512, 320, False), (129, 384, 192, True),
+                                        (64, 1024, 4096, False), (257, 1024, 3072, True),
+                                        (1000, 256, 64, False)])
+@pytest.mark.parametrize("out_f32", [False, True])
+def test_gemm_bf16_tcgen05(M, N, K, b_kn, out_f32):
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    a = torch.randn(M, K, device=DEV, generator=g).bfloat16()
+    b = torch.randn(K, N, device=DEV, generator=g).bfloat16() if b_kn else torch.randn(
+        N, K, device=DEV, generator=g).bfloat16()
+    c = _ops().gemm(a, b, b_kn=b_kn, out_dtype=torch.float32 if out_f32 else torch.bfloat16)
+    torch.cuda.synchronize()
+    ref = _ref_mm(a, b, b_kn)
+    err = (c.float() - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    assert err <= (1e-5 if out_f32 else 8e-3) * scale + 1e-3, (err, scale)
+
+
+def test_gemm_bf16_is_batch_invariant():
+    g = torch.Generator(device=DEV).manual_seed(0)
+    w = torch.randn(1024, 3072, device=DEV, generator=g).bfloat16()
+    x = torch.randn(300, 3072, device=DEV, generator=g).bfloat16()
+    full = _ops().gemm(x, w, out_dtype=torch.float32)
+    for rows in (1, 7, 32, 129):
+        part = _ops().gemm(x[:rows].contiguous(), w, out_dtype=torch.float32)
+        assert torch.equal(part, full[:rows])
+
+
+def test_gemm_simt_fp32_exact_and_batch_invariant():
+    g = torch.Generator(device=DEV).manual_seed(1)
+    w = torch.randn(777, 1536, device=DEV, generator=g)
+    x = torch.randn(97, 1536, device=DEV, generator=g)
+    full = _ops().gemm(x, w)
+    ref = _ref_mm(x, w)
+    assert torch.allclose(full, ref, rtol=1e-5, atol=1e-4)
+    for rows in (1, 5, 32):
+        assert torch.equal(_ops().gemm(x[:rows].contiguous(), w), full[:rows])
+
+
+def _lmhead_case(n, m, V, d, dtype, seed, weighted):
+    g = torch.Generator().manual_seed(seed)
+    student = torch.randn(n, d, generator=g)
+    teacher = torch.randn(m, d, generator=g)
+    index = torch.randint(0, m, (n,), generator=g).sort().values
+    weight = torch.randn(V, d, generator=g) * 0.5
+    rw = torch.rand(n, generator=g) if weighted else None
+    if dtype == torch.bfloat16:  # the oracle sees the same bf16-rounded inputs
+        student, teacher, weight = student.bfloat16().float(), teacher.bfloat16().float(), \
+            weight.bfloat16().float()
+    return student, teacher, index, weight, rw
+
+
+@pytest.mark.parametrize("kind", ["plain", "weighted"])
+def test_lmhead_kl_fp32_matches_reference_kat(kind):
+    """The reference's own known-answer case (tests/test_objective.py:16-38) through the fp32
+    kernels: total / per-row KL 1e-5 relative, gradient 1e-4, agreement exact."""
+    k = load_golden("kl_kat.pt")[kind]
+    rw = k["row_weight"]
+    total, kl, agree, grad, _, _ = _ops().lmhead_kl(
+        k["student"].to(DEV), k["teacher"].to(DEV), k["index"].to(DEV), k["weight"].to(DEV),
+        None if rw is None else rw.to(DEV))
+    torch.cuda.synchronize()
+    assert torch.allclose(total.cpu(), k["total"], rtol=1e-5, atol=1e-5)
+    assert torch.allclose(kl.cpu(), k["kl_rows"], rtol=1e-5, atol=1e-6)
+    assert torch.equal(agree.cpu(), k["agree"])
+    assert torch.allclose(grad.cpu(), k["grad"], rtol=1e-4, atol=1e-6)
+
+
+@pytest.mark.parametrize("n,m,V,d,weighted", [(300, 200, 1000, 128, False), (517, 300, 5003, 192, True)])
+def test_lmhead_kl_bf16_matches_oracle(n, m, V, d, weighted):
+    s, t, idx, w, rw = _lmhead_case(n, m, V, d, torch.bfloat16, n + V, weighted)
+    offsets = torch.arange(n) % 7
+    total, kl, agree, grad, kbo, abo = _ops().lmhead_kl(
+        s.bfloat16().to(DEV), t.bfloat16().to(DEV), idx.to(DEV), w.bfloat16().to(DEV),
+        None if rw is None else rw.to(DEV), offsets.to(DEV), 7, chunk_rows=256)
+    torch.cuda.synchronize()
+    r_total, r_kl, r_agree, r_grad = O.fused_linear_forward_kl(s, t, idx, w, rw)
+    assert abs(total.item() - r_total.item()) <= 1e-2 * abs(r_total.item())
+    assert (kl.cpu() - r_kl).abs().max().item() <= 2e-2 * r_kl.abs().max().item() + 1e-3
+    assert (agree.cpu() == r_agree).float().mean().item() >= 0.99
+    assert (grad.float().cpu() - r_grad).abs().max().item() <= 2e-2 * r_grad.abs().max().item()
+    r_kbo = torch.zeros(7).index_add_(0, offsets, r_kl)
+    assert torch.allclose(kbo.cpu(), r_kbo, rtol=2e-2, atol=1e-3)
+    assert torch.equal(abo.cpu(), torch.bincount(offsets[agree.cpu()], minlength=7))
+
+
+def test_lmhead_kl_fp32_matches_oracle_ragged():
+    s, t, idx, w, rw = _lmhead_case(203, 77, 517, 40, torch.float32, 3, True)
+    total, kl, agree, grad, _, _ = _ops().lmhead_kl(s.to(DEV), t.to(DEV), idx.to(DEV), w.to(DEV),
+                                                    rw.to(DEV), chunk_rows=64)
+    torch.cuda.synchronize()
+    r_total, r_kl, r_agree, r_grad = O.fused_linear_forward_kl(s, t, idx, w, rw)
+    assert torch.allclose(total.cpu(), r_total, rtol=1e-5)
+    assert torch.allclose(kl.cpu(), r_kl, rtol=1e-5, atol=1e-6)
+    assert torch.equal(agree.cpu(), r_agree)
+    assert torch.allclose(grad.cpu(), r_grad, rtol=1e-4, atol=1e-6)
+
+
+def test_lmhead_kl_bf16_full_vocab_vs_torch_fp32():
+    """0.6B LM-head shape (V = 151936, d = 1024) against an fp32 torch computation on the GPU."""
+    n, m, V, d = 1536, 1100, 151936, 1024
+    g = torch.Generator(device=DEV).manual_seed(5)
+    s = torch.randn(n, d, device=DEV, generator=g).bfloat16()
+    t = torch.randn(m, d, device=DEV, generator=g).bfloat16()
+    idx = torch.randint(0, m, (n,), device=DEV, generator=g).sort().values
+    w = (torch.randn(V, d, device=DEV, generator=g) * 0.05).bfloat16()
+    total, kl, agree, grad, _, _ = _ops().lmhead_kl(s, t, idx, w)
+    ls = s.float() @ w.float().t()
+    lt = t.float() @ w.float().t()
+    lpt = lt.log_softmax(-1)[idx]
+    lps = ls.log_softmax(-1)
+    r_kl = (lpt.exp() * (lpt - lps)).sum(-1)
+    r_agree = ls.argmax(-1) == lt.argmax(-1)[idx]
+    r_grad = ((lps.exp() - lpt.exp()).bfloat16().float() @ w.float())
+    assert abs(total.item() - r_kl.sum().item()) <= 1e-2 * r_kl.sum().item()
+    assert (kl - r_kl).abs().max().item() <= 2e-2 * r_kl.abs().max().item()
+    assert (agree == r_agree).float().mean().item() >= 0.99
+    assert (grad.float() - r_grad).abs().max().item() <= 2e-2 * r_grad.abs().max().item() + 1e-4
+
+
+def test_lmhead_kl_deterministic():
+    s, t, idx, w, rw = _lmhead_case(400, 250, 3000, 128, torch.bfloat16, 9, True)
+    args = (s.bfloat16().to(DEV), t.bfloat16().to(DEV), idx.to(DEV), w.bfloat16().to(DEV), rw.to(DEV))
+    a = _ops().lmhead_kl(*args)
+    b = _ops().lmhead_kl(*args)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1]) and torch.equal(a[3], b[3])
+
+
+def test_no_device_error_left():
+    from orthrus_training_b200 import _lib
+
+    assert _lib.device_error(0) == 0
