@@ -74,34 +74,43 @@ int orthrus_gemm_simt(const void* A, int64_t lda, const void* B, int64_t ldb, vo
                       int64_t M, int64_t N, int64_t K, int dtype, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* RMSNorm of `rows` rows of length d: y = w * (x * rsqrt(mean(x^2) + eps)), the normalised value
+ * rounded to dtype before the weight multiply (transformers Qwen3RMSNorm, orthrus/objective.py:128-133).
+ * One warp per row, fixed reduction order. */
+int orthrus_rmsnorm(const void* x, const void* w, int64_t rows, int d, float eps, void* y, int dtype,
+                    void* stream);
+
 /* ---- q/k RMSNorm + RoPE + head-major layout (fused prologue of the attention) ------------- */
 /* qkv: [rows = B*T, (Hq + 2*Hkv) * hd] token-major projection output (q | k | v columns).
- * positions: [B, T] int64 RoPE positions. Writes
+ * positions: [B, T] int64 RoPE positions; inv_freq: [hd/2] fp32 RoPE inverse frequencies
+ * (1 / theta^(2i/hd), computed by the caller exactly as the rotary embedding does). Writes
  *   q_out [B, Hq, T, D]            (norm + RoPE), D = padded head dim (>= hd, zero padding)
  *   k_out [B, Hkv, cap, D] at row offset[b] + t (norm + RoPE), v_out likewise (copy);
  *   rstd [rows, Hq + Hkv] fp32 (saved for the backward; may be NULL).
  * offset may be NULL (0). cap >= offset[b] + T. dtype applies to qkv and all outputs.
  * Replaces _attention_inputs (orthrus/objective.py:136-143) and the q/k norm + apply_rotary_pos_emb
  * of OrthrusAttention.forward (orthrus/modeling_orthrus.py:153-159) plus DynamicCache.update. */
-int orthrus_qkv_prep_fwd(const void* qkv, const int64_t* positions, const void* q_norm_w,
-                         const void* k_norm_w, int64_t B, int64_t T, int Hq, int Hkv, int hd, int D,
-                         float eps, float theta, void* q_out, void* k_out, void* v_out, int64_t cap,
-                         const int32_t* offset, float* rstd, int dtype, void* stream);
+int orthrus_qkv_prep_fwd(const void* qkv, const int64_t* positions, const float* inv_freq,
+                         const void* q_norm_w, const void* k_norm_w, int64_t B, int64_t T, int Hq,
+                         int Hkv, int hd, int D, float eps, void* q_out, void* k_out, void* v_out,
+                         int64_t cap, const int32_t* offset, float* rstd, int dtype, void* stream);
 
 /* Backward of orthrus_qkv_prep_fwd for training (offset 0, cap = T):
  *   dq [B, Hq, T, D] fp32, dk [B, Hkv, T, D] fp32, dv [B, Hkv, T, D] fp32 (any may be NULL = 0)
  *   -> dqkv [rows, (Hq + 2 Hkv) hd] (dtype), dq_norm_w / dk_norm_w [hd] fp32 (overwritten).
  * workspace: orthrus_qkv_prep_bwd_workspace_bytes(). */
 size_t orthrus_qkv_prep_bwd_workspace_bytes(int64_t B, int64_t T, int hd);
-int orthrus_qkv_prep_bwd(const void* qkv, const int64_t* positions, const void* q_norm_w,
-                         const void* k_norm_w, const float* rstd, const float* dq, const float* dk,
-                         const float* dv, int64_t B, int64_t T, int Hq, int Hkv, int hd, int D,
-                         float theta, void* dqkv, float* dq_norm_w, float* dk_norm_w,
-                         void* workspace, size_t workspace_bytes, int dtype, void* stream);
+int orthrus_qkv_prep_bwd(const void* qkv, const int64_t* positions, const float* inv_freq,
+                         const void* q_norm_w, const void* k_norm_w, const float* rstd,
+                         const float* dq, const float* dk, const float* dv, int64_t B, int64_t T,
+                         int Hq, int Hkv, int hd, int D, void* dqkv, float* dq_norm_w,
+                         float* dk_norm_w, void* workspace, size_t workspace_bytes, int dtype,
+                         void* stream);
 
 /* ---- dual-view attention --------------------------------------------------------------- */
 /* Per-anchor tile map of the dual-view mask (K3): for every 128-query tile of each row,
- * tilemap[b, tile] = {number of source-1 key tiles to visit, first source-2 key, source-2 keys}.
+ * tilemap[b, tile] = {source-1 key tiles to visit, source-1 keys visible to the tile (largest
+ * anchor, clipped to L1), first and one-past-last source-2 key}.
  * anchors [B, A] int64 sorted per row, block = K. Output int32 [B, ceil(A*K/128), 4].
  * Replaces build_block_mask / create_block_mask (orthrus/modeling_orthrus.py:58-74) and
  * skip_ar_key_grads (orthrus/objective.py:168-198): the backward never visits source-1 keys
@@ -176,7 +185,8 @@ int orthrus_decode_draft(const float* logits, int64_t B, int K, int64_t V, const
                          const uint8_t* done, int64_t* verify_ids, void* stream);
 
 /* Verify + greedy accept + rollback (K8) for B sequences, entirely on device:
- *   ar = argmax(verify logits [B, K, V]); accepted = longest prefix with drafts == ar, limited to
+ *   ar_tokens [B, K] = argmax(verify logits [B, K, V]) (written, int64);
+ *   accepted = longest prefix with drafts == ar_tokens, limited to
  *   block_len - 1 = min(K, max_len[b] - start[b]) - 1 and ending after an accepted EOS;
  *   appends the kept tokens and the bonus token to out_tokens [B, out_cap] at out_len[b];
  *   start[b] += accepted + 1 (the KV-cache length rollback: positions past it are dead);
@@ -186,7 +196,8 @@ int orthrus_decode_draft(const float* logits, int64_t B, int K, int64_t V, const
  * (orthrus/modeling_orthrus.py:489-533), decoding._verify / _advance / ModelBackend.commit
  * (orthrus/decoding.py:248-264,336-369). */
 int orthrus_decode_verify_accept(const float* logits, int64_t B, int K, int64_t V,
-                                 const int64_t* verify_ids, const int64_t* eos, int n_eos,
+                                 const int64_t* verify_ids, int64_t* ar_tokens,
+                                 const int64_t* eos, int n_eos,
                                  const int32_t* max_len, int32_t* start, int64_t* anchor,
                                  uint8_t* done, int64_t* out_tokens, int32_t* out_len,
                                  int64_t out_cap, int32_t* accepted_log, int32_t* cycle,

@@ -29,11 +29,12 @@ _SIGNATURES = {
     "orthrus_gemm_simt_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
     "orthrus_gemm_simt": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int64, c_int64, c_int64,
                                   c_int, _P, c_size_t, _P]),
-    "orthrus_qkv_prep_fwd": (c_int, [_P, _P, _P, _P, c_int64, c_int64, c_int, c_int, c_int, c_int,
-                                     c_float, c_float, _P, _P, _P, c_int64, _P, _P, c_int, _P]),
+    "orthrus_rmsnorm": (c_int, [_P, _P, c_int64, c_int, c_float, _P, c_int, _P]),
+    "orthrus_qkv_prep_fwd": (c_int, [_P, _P, _P, _P, _P, c_int64, c_int64, c_int, c_int, c_int, c_int,
+                                     c_float, _P, _P, _P, c_int64, _P, _P, c_int, _P]),
     "orthrus_qkv_prep_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int]),
-    "orthrus_qkv_prep_bwd": (c_int, [_P, _P, _P, _P, _P, _P, _P, _P, c_int64, c_int64, c_int, c_int,
-                                     c_int, c_int, c_float, _P, _P, _P, _P, c_size_t, c_int, _P]),
+    "orthrus_qkv_prep_bwd": (c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, c_int64, c_int64, c_int,
+                                     c_int, c_int, c_int, _P, _P, _P, _P, c_size_t, c_int, _P]),
     "orthrus_attn_tilemap": (c_int, [_P, c_int64, c_int64, c_int, c_int64, _P, _P]),
     "orthrus_attn_fwd": (c_int, [_P, _P, _P, c_int64, c_int64, c_int64, _P, _P, c_int64, c_int64,
                                  c_int64, c_int64, c_int, c_int, c_int64, c_int, c_int, c_float, c_int,
@@ -50,8 +51,8 @@ _SIGNATURES = {
     "orthrus_lmhead_kl_bwd": (c_int, [_P, _P, _P, c_int64, c_int, _P]),
     "orthrus_argmax_rows": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P]),
     "orthrus_decode_draft": (c_int, [_P, c_int64, c_int, c_int64, _P, _P, _P, _P]),
-    "orthrus_decode_verify_accept": (c_int, [_P, c_int64, c_int, c_int64, _P, _P, c_int, _P, _P, _P,
-                                             _P, _P, _P, c_int64, _P, _P, c_int64, _P]),
+    "orthrus_decode_verify_accept": (c_int, [_P, c_int64, c_int, c_int64, _P, _P, _P, c_int, _P, _P,
+                                             _P, _P, _P, _P, c_int64, _P, _P, c_int64, _P]),
 }
 
 _lib = None

@@ -1,1 +1,787 @@
+// Dual-view attention on the 5th-generation tensor cores (bf16 in, fp32 accumulate in TMEM).
+//
+// Three kernels, all with the same CTA shape (192 threads: warp 0 = TMA producer, warp 1 = TMEM
+// owner and single-thread tcgen05.mma issuer, warps 2-5 = 128 "row" threads, one per TMEM lane):
+//
+//   attn_fwd_tc      CTA = 128 query rows of one head. Visits only the key tiles the mask can
+//                    reach (the per-anchor tile map: source-1 tiles below the largest anchor of
+//                    the tile, plus the own-block tile of source 2), S = Q K^T into one of two TMEM
+//                    buffers, online softmax in registers, P (bf16) to shared memory,
+//                    O_j = P V into one of two TMEM buffers, O += alpha-rescaled O_j in registers.
+//   attn_dq_tc       CTA = 128 query rows of one head: S = Q K^T and dP = dO V^T per visible key
+//                    tile, dS = P (dP - delta) to shared memory, dQ += dS K accumulated in TMEM.
+//   attn_dkdv_tc     CTA = 128 block keys of one KV head: for every query head of the group,
+//                    S^T = K Q^T, dP^T = V dO^T, then dV += P^T dO and dK += dS^T Q in TMEM. Only the
+//                    own-block keys get gradients: source-1 keys belong to the frozen teacher
+//                    (the reference's skip_ar_key_grads, orthrus/objective.py:168-198).
+//
+// Operand tiles are [128 rows][D] bf16 loaded by TMA as D/64 boxes of [128][64] with 128-byte
+// swizzle. The same tile is a K-major UMMA operand when the reduction runs over the head dim
+// (Q K^T, dO V^T) and an MN-major operand when it runs over the rows (P V, dS K, P^T dO, dS^T Q).
 #pragma once
+
+#include "attention_simt.cuh"
+
+namespace orthrus {
+
+constexpr int kAttnTileBytes = 128 * 64 * 2;  // one [128][64] bf16 box = 16 KB
+
+// K-major descriptor of k-step kk (16 elements) of a [128][D] tile stored as D/64 boxes.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t base, int kk) {
+  return umma_desc_sw128(base + (kk >> 2) * kAttnTileBytes + (kk & 3) * 32, 16, 1024);
+}
+// MN-major descriptor of k-step kk (16 rows) of a [128 rows][D] tile (D along MN).
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t base, int kk) {
+  return umma_desc_sw128(base + kk * 2048, kAttnTileBytes, 1024);
+}
+
+// Writes 32 consecutive bf16 values (columns c0..c0+31 of row r) into a K-major swizzled tile.
+__device__ __forceinline__ void store_row32_sw128(uint32_t tile_base, int r, int c0, const float* v) {
+  const uint32_t box = tile_base + (c0 >> 6) * kAttnTileBytes;
+  const int chunk0 = (c0 & 63) >> 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    st_shared_v4(box + sw128_offset(r, chunk0 + q), pack_bf16x2(v[8 * q], v[8 * q + 1]),
+                 pack_bf16x2(v[8 * q + 2], v[8 * q + 3]), pack_bf16x2(v[8 * q + 4], v[8 * q + 5]),
+                 pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+}
+
+struct AttnTiles {
+  int n1;        // source-1 tiles [0, n1)
+  int t2a, n2;   // source-2 tiles [t2a, t2a + n2)
+};
+
+// Row-thread part of the tile map: reduce the key ranges of the CTA's rows.
+__device__ __forceinline__ void attn_tile_map(const MaskParams& mp, int64_t b, int64_t q0, int64_t Tq, bool has2,
+                                              int row_thread, unsigned long long* red, AttnTiles* out) {
+  // red[0] = max e1, red[1] = min s2, red[2] = max e2
+  if (row_thread >= 0) {
+    const int64_t t = q0 + row_thread;
+    if (t < Tq) {
+      int64_t e1, s2, e2;
+      query_ranges(mp, b, t, e1, s2, e2);
+      atomicMax(&red[0], static_cast<unsigned long long>(e1));
+      if (has2 && e2 > s2) {
+        atomicMin(&red[1], static_cast<unsigned long long>(s2));
+        atomicMax(&red[2], static_cast<unsigned long long>(e2));
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    out->n1 = static_cast<int>((red[0] + 127) / 128);
+    if (red[2] > red[1]) {
+      out->t2a = static_cast<int>(red[1] / 128);
+      out->n2 = static_cast<int>((red[2] + 127) / 128) - out->t2a;
+    } else {
+      out->t2a = 0;
+      out->n2 = 0;
+    }
+  }
+  __syncthreads();
+}
+
+template <int D>
+struct FwdSmem {
+  static constexpr int BOXES = D / 64;
+  static constexpr int TILE = BOXES * kAttnTileBytes;  // [128][D]
+  static constexpr int STAGES = 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_KV = TILE;                         // stage s: K at +2s*TILE, V at +(2s+1)*TILE
+  static constexpr int OFF_P = OFF_KV + 2 * STAGES * TILE;    // P: [128][128] = 2 boxes
+  static constexpr int OFF_BAR = OFF_P + 2 * kAttnTileBytes;
+  static constexpr int SMEM = OFF_BAR + 512 + 1024;
+};
+
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK1,
+                       const __grid_constant__ CUtensorMap tmV1, const __grid_constant__ CUtensorMap tmK2,
+                       const __grid_constant__ CUtensorMap tmV2, int Hq, int Hkv, int64_t Tq, int hd,
+                       float scale_log2, MaskParams mp, bool has2, __nv_bfloat16* __restrict__ o,
+                       float* __restrict__ lse) {
+  using S = FwdSmem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_empty = bars + 7;   // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* p_empty = bars + 10;
+  uint64_t* o_full = bars + 11;   // [2]
+  uint64_t* o_empty = bars + 13;  // [2]
+  unsigned long long* red = reinterpret_cast<unsigned long long*>(bars + 16);  // [3]
+  AttnTiles* tiles = reinterpret_cast<AttnTiles*>(bars + 20);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * 128;
+  const int h = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int hk = h / (Hq / Hkv);
+  const int row_thread = warp >= 2 ? (warp & 3) * 32 + lane : -1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], 4);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(p_empty, 1);
+    red[0] = 0;
+    red[1] = ~0ull;
+    red[2] = 0;
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  __syncthreads();
+  attn_tile_map(mp, b, q0, Tq, has2, row_thread, red, tiles);
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n1 = tiles->n1, t2a = tiles->t2a;
+  const int nt = n1 + tiles->n2;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(q_full, S::TILE);
+#pragma unroll
+      for (int c = 0; c < S::BOXES; ++c)
+        tma_load_3d(smem + S::OFF_Q + c * kAttnTileBytes, &tmQ, q_full, c * 64, static_cast<int>(q0),
+                    static_cast<int>(b * Hq + h));
+      int issued = 0;
+      for (int j = 0; j < nt; ++j) {
+        const int s = j & 1;
+        if (*abort_flag || !mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        const bool src2 = j >= n1;
+        const int key0 = (src2 ? t2a + (j - n1) : j) * 128;
+        const CUtensorMap* mk = src2 ? &tmK2 : &tmK1;
+        const CUtensorMap* mv = src2 ? &tmV2 : &tmV1;
+        uint8_t* kt = smem + S::OFF_KV + (2 * s) * S::TILE;
+        uint8_t* vt = kt + S::TILE;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * S::TILE);
+#pragma unroll
+        for (int c = 0; c < S::BOXES; ++c) {
+          tma_load_3d(kt + c * kAttnTileBytes, mk, &kv_full[s], c * 64, key0, static_cast<int>(b * Hkv + hk));
+          tma_load_3d(vt + c * kAttnTileBytes, mv, &kv_full[s], c * 64, key0, static_cast<int>(b * Hkv + hk));
+        }
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        mbar_wait_short(q_full, 0);
+        for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait_short(&kv_full[j & 1], (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t idesc_o = umma_idesc_bf16(128, D, false, true);
+      const uint32_t q_base = smem_u32(smem + S::OFF_Q);
+      const uint32_t p_base = smem_u32(smem + S::OFF_P);
+      bool ok = mbar_wait(q_full, 0);
+      auto issue_pv = [&](int j) -> bool {
+        // O_j = P_j V_j into O buffer j & 1
+        if (!mbar_wait(p_full, j & 1)) return false;
+        if (!mbar_wait(&o_empty[j & 1], ((j >> 1) & 1) ^ 1)) return false;
+        tc_fence_after();
+        const uint32_t v_base = smem_u32(smem + S::OFF_KV + (2 * (j & 1) + 1) * S::TILE);
+        const uint32_t acc = tmem + 256 + (j & 1) * 128;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16(acc, desc_kmajor(p_base, kk), desc_mnmajor(v_base, kk), idesc_o, kk > 0 ? 1u : 0u);
+        umma_commit(&o_full[j & 1]);
+        umma_commit(&kv_empty[j & 1]);
+        umma_commit(p_empty);
+        return true;
+      };
+      for (int j = 0; ok && j < nt; ++j) {
+        if (*abort_flag || !mbar_wait(&kv_full[j & 1], (j >> 1) & 1) ||
+            !mbar_wait(&s_empty[j & 1], ((j >> 1) & 1) ^ 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(smem + S::OFF_KV + (2 * (j & 1)) * S::TILE);
+        const uint32_t acc = tmem + (j & 1) * 128;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_f16(acc, desc_kmajor(q_base, kk), desc_kmajor(k_base, kk), idesc_s, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[j & 1]);
+        if (j >= 1 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok && nt >= 1 && !issue_pv(nt - 1)) ok = false;
+      if (!ok) *abort_flag = 1;
+      umma_commit(p_empty);  // completes once all issued MMAs are done (drain on every path)
+    }
+  } else {
+    const int r = row_thread;
+    const int64_t t = q0 + r;
+    const bool live = t < Tq;
+    int64_t e1 = 0, s2 = 0, e2 = 0;
+    if (live) query_ranges(mp, b, t, e1, s2, e2);
+    if (!has2) e2 = s2 = 0;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t p_base = smem_u32(smem + S::OFF_P);
+    float m = -INFINITY, l = 0.f;
+    float acc[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) acc[i] = 0.f;
+    float alpha_prev = 0.f;
+    bool ok = true;
+    auto correction = [&](int j, float alpha) -> bool {
+      if (!mbar_wait(&o_full[j & 1], (j >> 1) & 1)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float x[32];
+        tmem_ld32(lane_base + 256 + (j & 1) * 128 + c * 32, x);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[c * 32 + i] = fmaf(acc[c * 32 + i], alpha, x[i]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[j & 1]);
+      return true;
+    };
+    for (int j = 0; j < nt; ++j) {
+      if (*abort_flag || !mbar_wait(&s_full[j & 1], (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool src2 = j >= n1;
+      const int64_t key0 = (src2 ? t2a + (j - n1) : j) * 128;
+      const int64_t lo = src2 ? s2 : 0, hi = src2 ? e2 : e1;
+      const uint32_t sb = lane_base + (j & 1) * 128;
+      // pass 1: masked row max (log2 units)
+      float tmax = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float x[32];
+        tmem_ld32(sb + c * 32, x);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int64_t key = key0 + c * 32 + i;
+          if (key >= lo && key < hi) tmax = fmaxf(tmax, x[i] * scale_log2);
+        }
+      }
+      const float m_new = fmaxf(m, tmax);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = exp2f(m - m_use);
+      // pass 2: P = exp2(s - m) to shared memory (after the previous P V has read the buffer)
+      if (!mbar_wait(p_empty, (j & 1) ^ 1)) {
+        ok = false;
+        break;
+      }
+      float rsum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float x[32];
+        tmem_ld32(sb + c * 32, x);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int64_t key = key0 + c * 32 + i;
+          const float p = (key >= lo && key < hi) ? exp2f(fmaf(x[i], scale_log2, -m_use)) : 0.f;
+          x[i] = p;
+          rsum += p;
+        }
+        store_row32_sw128(p_base, r, c * 32, x);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[j & 1]);
+      fence_proxy_async_smem();
+      mbar_arrive(p_full);
+      l = l * alpha + rsum;
+      m = m_new;
+      if (j >= 1 && !correction(j - 1, alpha_prev)) {
+        ok = false;
+        break;
+      }
+      alpha_prev = alpha;
+    }
+    if (ok && nt >= 1 && !correction(nt - 1, alpha_prev)) ok = false;
+    if (!ok) *abort_flag = 1;
+    if (ok && live) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = o + ((b * Tq + t) * Hq + h) * hd;
+      if (hd == D) {
+#pragma unroll
+        for (int i = 0; i < D; i += 8) {
+          uint4 pk = make_uint4(pack_bf16x2(acc[i] * inv, acc[i + 1] * inv), pack_bf16x2(acc[i + 2] * inv, acc[i + 3] * inv),
+                                pack_bf16x2(acc[i + 4] * inv, acc[i + 5] * inv), pack_bf16x2(acc[i + 6] * inv, acc[i + 7] * inv));
+          *reinterpret_cast<uint4*>(orow + i) = pk;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < D; ++i)
+          if (i < hd) orow[i] = __float2bfloat16_rn(acc[i] * inv);
+      }
+      if (lse) lse[(b * Hq + h) * Tq + t] = (m + log2f(l)) * kLn2;
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_free(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Backward: dQ
+// ------------------------------------------------------------------------------------------------
+
+template <int D>
+struct DqSmem {
+  static constexpr int BOXES = D / 64;
+  static constexpr int TILE = BOXES * kAttnTileBytes;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_DO = TILE;
+  static constexpr int OFF_KV = 2 * TILE;  // 2 stages of (K, V)
+  static constexpr int OFF_DS = OFF_KV + 4 * TILE;
+  static constexpr int OFF_BAR = OFF_DS + 2 * kAttnTileBytes;
+  static constexpr int SMEM = OFF_BAR + 512 + 1024;
+};
+
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    attn_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                      const __grid_constant__ CUtensorMap tmK1, const __grid_constant__ CUtensorMap tmV1,
+                      const __grid_constant__ CUtensorMap tmK2, const __grid_constant__ CUtensorMap tmV2, int Hq,
+                      int Hkv, int64_t Tq, int hd, float scale, MaskParams mp, bool has2,
+                      const float* __restrict__ lse, const float* __restrict__ delta, float* __restrict__ dq) {
+  using S = DqSmem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
+  uint64_t* in_full = bars + 0;   // Q and dO
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // S and dP ready
+  uint64_t* s_empty = bars + 6;   // S and dP read (4 warps)
+  uint64_t* ds_full = bars + 7;   // dS written (128 threads)
+  uint64_t* ds_empty = bars + 8;  // dS consumed by the dQ MMA
+  uint64_t* dq_full = bars + 9;
+  unsigned long long* red = reinterpret_cast<unsigned long long*>(bars + 16);
+  AttnTiles* tiles = reinterpret_cast<AttnTiles*>(bars + 20);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * 128;
+  const int h = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int hk = h / (Hq / Hkv);
+  const int row_thread = warp >= 2 ? (warp & 3) * 32 + lane : -1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(in_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, 4);
+    mbar_init(ds_full, 128);
+    mbar_init(ds_empty, 1);
+    mbar_init(dq_full, 1);
+    red[0] = 0;
+    red[1] = ~0ull;
+    red[2] = 0;
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  __syncthreads();
+  attn_tile_map(mp, b, q0, Tq, has2, row_thread, red, tiles);
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // S: [0,128), dP: [128,256), dQ: [256, 256+D)
+  const int n1 = tiles->n1, t2a = tiles->t2a;
+  const int nt = n1 + tiles->n2;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(in_full, 2 * S::TILE);
+#pragma unroll
+      for (int c = 0; c < S::BOXES; ++c) {
+        tma_load_3d(smem + S::OFF_Q + c * kAttnTileBytes, &tmQ, in_full, c * 64, static_cast<int>(q0),
+                    static_cast<int>(b * Hq + h));
+        tma_load_3d(smem + S::OFF_DO + c * kAttnTileBytes, &tmDO, in_full, c * 64 + h * hd, static_cast<int>(q0),
+                    static_cast<int>(b));
+      }
+      int issued = 0;
+      for (int j = 0; j < nt; ++j) {
+        const int s = j & 1;
+        if (*abort_flag || !mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        const bool src2 = j >= n1;
+        const int key0 = (src2 ? t2a + (j - n1) : j) * 128;
+        uint8_t* kt = smem + S::OFF_KV + (2 * s) * S::TILE;
+        uint8_t* vt = kt + S::TILE;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * S::TILE);
+#pragma unroll
+        for (int c = 0; c < S::BOXES; ++c) {
+          tma_load_3d(kt + c * kAttnTileBytes, src2 ? &tmK2 : &tmK1, &kv_full[s], c * 64, key0,
+                      static_cast<int>(b * Hkv + hk));
+          tma_load_3d(vt + c * kAttnTileBytes, src2 ? &tmV2 : &tmV1, &kv_full[s], c * 64, key0,
+                      static_cast<int>(b * Hkv + hk));
+        }
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        mbar_wait_short(in_full, 0);
+        for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait_short(&kv_full[j & 1], (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t idesc_q = umma_idesc_bf16(128, D, false, true);
+      const uint32_t q_base = smem_u32(smem + S::OFF_Q);
+      const uint32_t do_base = smem_u32(smem + S::OFF_DO);
+      const uint32_t ds_base = smem_u32(smem + S::OFF_DS);
+      bool ok = mbar_wait(in_full, 0);
+      for (int j = 0; ok && j < nt; ++j) {
+        if (*abort_flag || !mbar_wait(&kv_full[j & 1], (j >> 1) & 1) || !mbar_wait(s_empty, (j & 1) ^ 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(smem + S::OFF_KV + (2 * (j & 1)) * S::TILE);
+        const uint32_t v_base = k_base + S::TILE;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          umma_f16(tmem, desc_kmajor(q_base, kk), desc_kmajor(k_base, kk), idesc_s, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + 128, desc_kmajor(do_base, kk), desc_kmajor(v_base, kk), idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        // dQ += dS_j K_j once the row threads wrote dS_j
+        if (!mbar_wait(ds_full, j & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16(tmem + 256, desc_kmajor(ds_base, kk), desc_mnmajor(k_base, kk), idesc_q,
+                   (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(ds_empty);
+        umma_commit(&kv_empty[j & 1]);
+      }
+      if (!ok) *abort_flag = 1;
+      umma_commit(dq_full);
+    }
+  } else {
+    const int r = row_thread;
+    const int64_t t = q0 + r;
+    const bool live = t < Tq;
+    int64_t e1 = 0, s2 = 0, e2 = 0;
+    if (live) query_ranges(mp, b, t, e1, s2, e2);
+    if (!has2) e2 = s2 = 0;
+    const int64_t qi = (b * Hq + h) * Tq + (live ? t : 0);
+    const float L2e = live ? lse[qi] * kLog2e : 0.f;
+    const float dl = live ? delta[qi] : 0.f;
+    const float sl2 = scale * kLog2e;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t ds_base = smem_u32(smem + S::OFF_DS);
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      if (*abort_flag || !mbar_wait(s_full, j & 1) || !mbar_wait(ds_empty, (j & 1) ^ 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool src2 = j >= n1;
+      const int64_t key0 = (src2 ? t2a + (j - n1) : j) * 128;
+      const int64_t lo = src2 ? s2 : 0, hi = src2 ? e2 : e1;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float x[32], y[32];
+        tmem_ld32(lane_base + c * 32, x);
+        tmem_ld32(lane_base + 128 + c * 32, y);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int64_t key = key0 + c * 32 + i;
+          const float p = (key >= lo && key < hi) ? exp2f(fmaf(x[i], sl2, -L2e)) : 0.f;
+          x[i] = p * (y[i] - dl);
+        }
+        store_row32_sw128(ds_base, r, c * 32, x);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_empty);
+      fence_proxy_async_smem();
+      mbar_arrive(ds_full);
+    }
+    if (!ok) *abort_flag = 1;
+    const bool done_ok = mbar_wait(dq_full, 0);
+    tc_fence_after();
+    float* out = dq + qi * D;
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      float x[32];
+      tmem_ld32(lane_base + 256 + c * 32, x);
+      tmem_wait_ld();
+      if (live && ok && done_ok) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const int e = c * 32 + i;
+          float4 v = make_float4(nt > 0 ? x[i] * scale : 0.f, nt > 0 ? x[i + 1] * scale : 0.f,
+                                 nt > 0 ? x[i + 2] * scale : 0.f, nt > 0 ? x[i + 3] * scale : 0.f);
+          if (e >= hd) v = make_float4(0.f, 0.f, 0.f, 0.f);
+          *reinterpret_cast<float4*>(out + e) = v;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_free(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Backward: dK, dV of the own-block (source-2) keys
+// ------------------------------------------------------------------------------------------------
+
+template <int D>
+struct DkvSmem {
+  static constexpr int BOXES = D / 64;
+  static constexpr int TILE = BOXES * kAttnTileBytes;
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = TILE;
+  static constexpr int OFF_Q = 2 * TILE;
+  static constexpr int OFF_DO = 3 * TILE;
+  static constexpr int OFF_P = 4 * TILE;                     // P^T  [128 keys][128 queries]
+  static constexpr int OFF_DS = OFF_P + 2 * kAttnTileBytes;  // dS^T
+  static constexpr int MAX_GROUP = 8;  // query heads per KV head
+  static constexpr int OFF_STAT = OFF_DS + 2 * kAttnTileBytes;  // [group][lse*log2e | delta][128]
+  static constexpr int OFF_BAR = OFF_STAT + MAX_GROUP * 2 * 128 * 4;
+  static constexpr int SMEM = OFF_BAR + 512 + 1024;
+};
+
+// grid (ceil(L2 / 128), Hkv, B). Queries of the block keys [k0, k0 + 128) are rows [k0, k0 + 128).
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    attn_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                        const __grid_constant__ CUtensorMap tmK2, const __grid_constant__ CUtensorMap tmV2, int Hq,
+                        int Hkv, int64_t Tq, int64_t L2, int hd, int block, float scale,
+                        const float* __restrict__ lse, const float* __restrict__ delta, float* __restrict__ dk,
+                        float* __restrict__ dv) {
+  using S = DkvSmem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* in_full = bars + 1;    // Q_h, dO_h of the current head
+  uint64_t* in_empty = bars + 2;   // Q_h, dO_h consumed
+  uint64_t* s_full = bars + 3;     // S^T, dP^T
+  uint64_t* s_empty = bars + 4;    // read by the row threads
+  uint64_t* p_full = bars + 5;     // P^T, dS^T written (128 arrivals)
+  uint64_t* p_empty = bars + 6;    // consumed by the dV / dK MMAs
+  uint64_t* acc_full = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 13);
+  float* s_lse = reinterpret_cast<float*>(smem + S::OFF_STAT);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t k0 = static_cast<int64_t>(blockIdx.x) * 128;
+  const int hk = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int G = Hq / Hkv;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(in_full, 1);
+    mbar_init(in_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, 4);
+    mbar_init(p_full, 128);
+    mbar_init(p_empty, 1);
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp >= 2) {  // per-query statistics of every head of the group, read by all row threads
+    const int r = (warp & 3) * 32 + lane;
+    const int64_t tq = k0 + r;
+    for (int g = 0; g < G; ++g) {
+      const int h = hk * G + g;
+      const bool qlive = tq < Tq;
+      s_lse[g * 256 + r] = qlive ? lse[(b * Hq + h) * Tq + tq] * kLog2e : 0.f;
+      s_lse[g * 256 + 128 + r] = qlive ? delta[(b * Hq + h) * Tq + tq] : 0.f;
+    }
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // S^T [0,128) dP^T [128,256) dV [256,256+D) dK [384, 384+D)
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(kv_full, 2 * S::TILE);
+#pragma unroll
+      for (int c = 0; c < S::BOXES; ++c) {
+        tma_load_3d(smem + S::OFF_K + c * kAttnTileBytes, &tmK2, kv_full, c * 64, static_cast<int>(k0),
+                    static_cast<int>(b * Hkv + hk));
+        tma_load_3d(smem + S::OFF_V + c * kAttnTileBytes, &tmV2, kv_full, c * 64, static_cast<int>(k0),
+                    static_cast<int>(b * Hkv + hk));
+      }
+      int issued = 0;
+      for (int g = 0; g < G; ++g) {
+        const int h = hk * G + g;
+        if (*abort_flag || !mbar_wait(in_empty, (g & 1) ^ 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(in_full, 2 * S::TILE);
+#pragma unroll
+        for (int c = 0; c < S::BOXES; ++c) {
+          tma_load_3d(smem + S::OFF_Q + c * kAttnTileBytes, &tmQ, in_full, c * 64, static_cast<int>(k0),
+                      static_cast<int>(b * Hq + h));
+          tma_load_3d(smem + S::OFF_DO + c * kAttnTileBytes, &tmDO, in_full, c * 64 + h * hd,
+                      static_cast<int>(k0), static_cast<int>(b));
+        }
+        issued = g + 1;
+      }
+      if (*abort_flag) {
+        mbar_wait_short(kv_full, 0);
+        if (issued > 0) mbar_wait_short(in_full, (issued - 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t idesc_g = umma_idesc_bf16(128, D, false, true);
+      const uint32_t k_base = smem_u32(smem + S::OFF_K), v_base = smem_u32(smem + S::OFF_V);
+      const uint32_t q_base = smem_u32(smem + S::OFF_Q), do_base = smem_u32(smem + S::OFF_DO);
+      const uint32_t p_base = smem_u32(smem + S::OFF_P), ds_base = smem_u32(smem + S::OFF_DS);
+      bool ok = mbar_wait(kv_full, 0);
+      for (int g = 0; ok && g < G; ++g) {
+        if (*abort_flag || !mbar_wait(in_full, g & 1) || !mbar_wait(s_empty, (g & 1) ^ 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          umma_f16(tmem, desc_kmajor(k_base, kk), desc_kmajor(q_base, kk), idesc_s, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + 128, desc_kmajor(v_base, kk), desc_kmajor(do_base, kk), idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, g & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t acc = (g > 0 || kk > 0) ? 1u : 0u;
+          umma_f16(tmem + 256, desc_kmajor(p_base, kk), desc_mnmajor(do_base, kk), idesc_g, acc);
+          umma_f16(tmem + 384, desc_kmajor(ds_base, kk), desc_mnmajor(q_base, kk), idesc_g, acc);
+        }
+        umma_commit(p_empty);
+        umma_commit(in_empty);
+      }
+      if (!ok) *abort_flag = 1;
+      umma_commit(acc_full);
+    }
+  } else {
+    const int r = (warp & 3) * 32 + lane;  // key row inside the tile
+    const int64_t key = k0 + r;
+    const bool live = key < L2;
+    const int64_t kblk = key / block;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t p_base = smem_u32(smem + S::OFF_P), ds_base = smem_u32(smem + S::OFF_DS);
+    const float sl2 = scale * kLog2e;
+    bool ok = true;
+    for (int g = 0; g < G; ++g) {
+      const float* g_lse = s_lse + g * 256;
+      const float* g_delta = g_lse + 128;
+      // the P^T / dS^T buffers are free once the previous head's dV / dK MMAs completed
+      if (*abort_flag || !mbar_wait(p_empty, (g & 1) ^ 1) || !mbar_wait(s_full, g & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float x[32], y[32];
+        tmem_ld32(lane_base + c * 32, x);
+        tmem_ld32(lane_base + 128 + c * 32, y);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int qc = c * 32 + i;
+          const int64_t tq = k0 + qc;
+          const bool vis = live && tq < Tq && (tq / block) == kblk;
+          const float p = vis ? exp2f(fmaf(x[i], sl2, -g_lse[qc])) : 0.f;
+          x[i] = p;
+          y[i] = p * (y[i] - g_delta[qc]);
+        }
+        store_row32_sw128(p_base, r, c * 32, x);
+        store_row32_sw128(ds_base, r, c * 32, y);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_empty);
+      fence_proxy_async_smem();
+      mbar_arrive(p_full);
+    }
+    if (!ok) *abort_flag = 1;
+    const bool done_ok = mbar_wait(acc_full, 0);
+    tc_fence_after();
+    float* dvr = dv + ((b * Hkv + hk) * L2 + (live ? key : 0)) * D;
+    float* dkr = dk + ((b * Hkv + hk) * L2 + (live ? key : 0)) * D;
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      float x[32], y[32];
+      tmem_ld32(lane_base + 256 + c * 32, x);
+      tmem_ld32(lane_base + 384 + c * 32, y);
+      tmem_wait_ld();
+      if (live && ok && done_ok) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const int e = c * 32 + i;
+          float4 a = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+          float4 kq = make_float4(y[i] * scale, y[i + 1] * scale, y[i + 2] * scale, y[i + 3] * scale);
+          if (e >= hd) {
+            a = make_float4(0.f, 0.f, 0.f, 0.f);
+            kq = a;
+          }
+          *reinterpret_cast<float4*>(dvr + e) = a;
+          *reinterpret_cast<float4*>(dkr + e) = kq;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_free(tmem, 512);
+  }
+}
+
+}  // namespace orthrus

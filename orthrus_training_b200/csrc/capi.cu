@@ -105,3 +105,309 @@ int orthrus_lmhead_kl_bwd(const void* grad, const float* grad_total, void* grad_
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------
+// q/k prep, attention, decoding
+// ------------------------------------------------------------------------------------------------
+
+namespace {
+
+__global__ void attn_tilemap_kernel(const int64_t* __restrict__ anchors, int64_t B, int64_t A, int block,
+                                    int64_t L1, int32_t* __restrict__ out) {
+  const int64_t Tq = A * block;
+  const int64_t ntiles = (Tq + 127) / 128;
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i >= B * ntiles) return;
+  const int64_t b = i / ntiles, tile = i % ntiles;
+  const int64_t q0 = tile * 128, q1 = min(Tq, q0 + 128);
+  int64_t e1 = 0, s2 = INT64_MAX, e2 = 0;
+  for (int64_t blk = q0 / block; blk <= (q1 - 1) / block; ++blk) {
+    e1 = max(e1, min(L1, anchors[b * A + blk]));
+    s2 = min(s2, blk * block);
+    e2 = max(e2, (blk + 1) * block);
+  }
+  out[i * 4 + 0] = static_cast<int32_t>((e1 + 127) / 128);
+  out[i * 4 + 1] = static_cast<int32_t>(e1);
+  out[i * 4 + 2] = static_cast<int32_t>(s2);
+  out[i * 4 + 3] = static_cast<int32_t>(e2);
+}
+
+bool use_tensor_cores(int dtype, int hd, int D, int mask, const int32_t* offset) {
+  if (dtype != ORTHRUS_BF16 || hd != D || (D != 64 && D != 128)) return false;
+  if (mask == ORTHRUS_MASK_DUAL) return true;
+  return mask == ORTHRUS_MASK_CAUSAL && offset == nullptr;
+}
+
+template <typename Kern>
+int set_smem(Kern k, int bytes) {
+  ORTHRUS_CHECK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  return ORTHRUS_OK;
+}
+
+struct AttnMaps {
+  CUtensorMap q, k1, v1, k2, v2, dout;
+};
+
+bool make_attn_maps(AttnMaps& m, const void* q, const void* k1, const void* v1, int64_t s1h, int64_t L1,
+                    const void* k2, const void* v2, int64_t s2h, int64_t L2, int64_t B, int Hq, int Hkv,
+                    int64_t Tq, int hd, int D, const void* dout) {
+  bool ok = make_tmap_3d_bf16(&m.q, q, D, Tq, B * Hq, D, Tq * D, 64, 128) &&
+            make_tmap_3d_bf16(&m.k1, k1, D, L1, B * Hkv, D, s1h, 64, 128) &&
+            make_tmap_3d_bf16(&m.v1, v1, D, L1, B * Hkv, D, s1h, 64, 128);
+  if (k2 != nullptr)
+    ok = ok && make_tmap_3d_bf16(&m.k2, k2, D, L2, B * Hkv, D, s2h, 64, 128) &&
+         make_tmap_3d_bf16(&m.v2, v2, D, L2, B * Hkv, D, s2h, 64, 128);
+  else {
+    m.k2 = m.k1;
+    m.v2 = m.v1;
+  }
+  if (dout != nullptr)
+    ok = ok && make_tmap_3d_bf16(&m.dout, dout, static_cast<uint64_t>(Hq) * hd, Tq, B, static_cast<uint64_t>(Hq) * hd,
+                                 Tq * Hq * hd, 64, 128);
+  return ok;
+}
+
+}  // namespace
+
+extern "C" {
+
+int orthrus_qkv_prep_fwd(const void* qkv, const int64_t* positions, const float* inv_freq, const void* q_norm_w,
+                         const void* k_norm_w, int64_t B, int64_t T, int Hq, int Hkv, int hd, int D, float eps,
+                         void* q_out, void* k_out, void* v_out, int64_t cap, const int32_t* offset, float* rstd,
+                         int dtype, void* stream) {
+  if (dtype == ORTHRUS_BF16)
+    return qkv_prep_fwd_impl<__nv_bfloat16>(
+        static_cast<const __nv_bfloat16*>(qkv), positions, inv_freq, static_cast<const __nv_bfloat16*>(q_norm_w),
+        static_cast<const __nv_bfloat16*>(k_norm_w), B, T, Hq, Hkv, hd, D, eps, static_cast<__nv_bfloat16*>(q_out),
+        static_cast<__nv_bfloat16*>(k_out), static_cast<__nv_bfloat16*>(v_out), cap, offset, rstd, as_stream(stream));
+  if (dtype == ORTHRUS_F32)
+    return qkv_prep_fwd_impl<float>(static_cast<const float*>(qkv), positions, inv_freq,
+                                    static_cast<const float*>(q_norm_w), static_cast<const float*>(k_norm_w), B, T,
+                                    Hq, Hkv, hd, D, eps, static_cast<float*>(q_out), static_cast<float*>(k_out),
+                                    static_cast<float*>(v_out), cap, offset, rstd, as_stream(stream));
+  return ORTHRUS_EINVAL;
+}
+
+size_t orthrus_qkv_prep_bwd_workspace_bytes(int64_t, int64_t, int hd) { return qkv_prep_bwd_ws(hd); }
+
+int orthrus_qkv_prep_bwd(const void* qkv, const int64_t* positions, const float* inv_freq, const void* q_norm_w,
+                         const void* k_norm_w, const float* rstd, const float* dq, const float* dk, const float* dv,
+                         int64_t B, int64_t T, int Hq, int Hkv, int hd, int D, void* dqkv, float* dq_norm_w,
+                         float* dk_norm_w, void* workspace, size_t workspace_bytes, int dtype, void* stream) {
+  if (dtype == ORTHRUS_BF16)
+    return qkv_prep_bwd_impl<__nv_bfloat16>(
+        static_cast<const __nv_bfloat16*>(qkv), positions, inv_freq, static_cast<const __nv_bfloat16*>(q_norm_w),
+        static_cast<const __nv_bfloat16*>(k_norm_w), rstd, dq, dk, dv, B, T, Hq, Hkv, hd, D,
+        static_cast<__nv_bfloat16*>(dqkv), dq_norm_w, dk_norm_w, workspace, workspace_bytes, as_stream(stream));
+  if (dtype == ORTHRUS_F32)
+    return qkv_prep_bwd_impl<float>(static_cast<const float*>(qkv), positions, inv_freq,
+                                    static_cast<const float*>(q_norm_w), static_cast<const float*>(k_norm_w), rstd, dq,
+                                    dk, dv, B, T, Hq, Hkv, hd, D, static_cast<float*>(dqkv), dq_norm_w, dk_norm_w,
+                                    workspace, workspace_bytes, as_stream(stream));
+  return ORTHRUS_EINVAL;
+}
+
+int orthrus_attn_tilemap(const int64_t* anchors, int64_t B, int64_t A, int block, int64_t L1, int32_t* tilemap,
+                         void* stream) {
+  ORTHRUS_CHECK_ARG(anchors && tilemap && B > 0 && A > 0 && block > 0 && L1 >= 0);
+  const int64_t n = B * ceil_div(A * block, 128);
+  attn_tilemap_kernel<<<static_cast<unsigned>(ceil_div(n, 128)), 128, 0, as_stream(stream)>>>(anchors, B, A, block,
+                                                                                            L1, tilemap);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+int orthrus_attn_fwd(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b, int64_t L1,
+                     const void* k2, const void* v2, int64_t s2h, int64_t s2b, int64_t L2, int64_t B, int Hq, int Hkv,
+                     int64_t Tq, int hd, int D, float scale, int mask, const int64_t* anchors, int64_t A, int block,
+                     const int32_t* offset, const int32_t* limit2, void* o, float* lse, int dtype, void* stream) {
+  ORTHRUS_CHECK_ARG(q && k1 && v1 && o && B > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && Tq > 0 && L1 >= 0);
+  ORTHRUS_CHECK_ARG(hd > 0 && hd <= D && D <= 128 && mask >= 0 && mask <= 2);
+  ORTHRUS_CHECK_ARG(mask != ORTHRUS_MASK_DUAL || (anchors && A > 0 && block > 0 && k2 && v2));
+  ORTHRUS_CHECK_ARG(mask != ORTHRUS_MASK_DRAFT || k2 != nullptr);
+  ORTHRUS_CHECK_ARG(B < 65536 && Hq < 65536);
+  const bool has2 = k2 != nullptr && mask != ORTHRUS_MASK_CAUSAL;
+  MaskParams mp{mask, anchors, A, block, offset, limit2, L1, has2 ? L2 : 0};
+  cudaStream_t st = as_stream(stream);
+  if (use_tensor_cores(dtype, hd, D, mask, offset)) {
+    ORTHRUS_CHECK_ARG(s1b == Hkv * s1h && (!has2 || s2b == Hkv * s2h));
+    ORTHRUS_CHECK_ARG(aligned16(q) && aligned16(k1) && aligned16(v1) && aligned16(o));
+    AttnMaps m;
+    if (!make_attn_maps(m, q, k1, v1, s1h, L1, has2 ? k2 : nullptr, has2 ? v2 : nullptr, s2h, L2, B, Hq, Hkv, Tq,
+                        hd, D, nullptr))
+      return ORTHRUS_ECUDA;
+    dim3 grid(static_cast<unsigned>(ceil_div(Tq, 128)), Hq, static_cast<unsigned>(B));
+    const float sl2 = scale * kLog2e;
+    if (D == 128) {
+      if (set_smem(attn_fwd_tc_kernel<128>, FwdSmem<128>::SMEM)) return ORTHRUS_ECUDA;
+      attn_fwd_tc_kernel<128><<<grid, 192, FwdSmem<128>::SMEM, st>>>(m.q, m.k1, m.v1, m.k2, m.v2, Hq, Hkv, Tq, hd,
+                                                                       sl2, mp, has2, static_cast<__nv_bfloat16*>(o),
+                                                                       lse);
+    } else {
+      if (set_smem(attn_fwd_tc_kernel<64>, FwdSmem<64>::SMEM)) return ORTHRUS_ECUDA;
+      attn_fwd_tc_kernel<64><<<grid, 192, FwdSmem<64>::SMEM, st>>>(m.q, m.k1, m.v1, m.k2, m.v2, Hq, Hkv, Tq, hd, sl2,
+                                                                     mp, has2, static_cast<__nv_bfloat16*>(o), lse);
+    }
+    ORTHRUS_CHECK_LAUNCH();
+    return ORTHRUS_OK;
+  }
+  dim3 grid(static_cast<unsigned>(ceil_div(Tq, kSimtQ)), Hq, static_cast<unsigned>(B));
+  if (dtype == ORTHRUS_BF16) {
+    using T = __nv_bfloat16;
+    attn_fwd_simt_kernel<T><<<grid, 32 * kSimtQ, 0, st>>>(
+        static_cast<const T*>(q), static_cast<const T*>(k1), static_cast<const T*>(v1), s1h, s1b,
+        static_cast<const T*>(k2), static_cast<const T*>(v2), s2h, s2b, Hq, Hkv, Tq, hd, D, scale, mp,
+        static_cast<T*>(o), lse);
+  } else if (dtype == ORTHRUS_F32) {
+    attn_fwd_simt_kernel<float><<<grid, 32 * kSimtQ, 0, st>>>(
+        static_cast<const float*>(q), static_cast<const float*>(k1), static_cast<const float*>(v1), s1h, s1b,
+        static_cast<const float*>(k2), static_cast<const float*>(v2), s2h, s2b, Hq, Hkv, Tq, hd, D, scale, mp,
+        static_cast<float*>(o), lse);
+  } else {
+    return ORTHRUS_EINVAL;
+  }
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+size_t orthrus_attn_bwd_workspace_bytes(int64_t B, int Hq, int64_t Tq) {
+  return static_cast<size_t>(B) * Hq * Tq * sizeof(float);
+}
+
+int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b, int64_t L1,
+                     const void* k2, const void* v2, int64_t s2h, int64_t s2b, int64_t L2, int64_t B, int Hq, int Hkv,
+                     int64_t Tq, int hd, int D, float scale, const int64_t* anchors, int64_t A, int block,
+                     const void* o, const float* lse, const void* do_, float* dq, float* dk2, float* dv2,
+                     void* workspace, size_t workspace_bytes, int dtype, void* stream) {
+  ORTHRUS_CHECK_ARG(q && k1 && v1 && k2 && v2 && anchors && o && lse && do_ && dq && dk2 && dv2);
+  ORTHRUS_CHECK_ARG(B > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && Tq > 0 && hd > 0 && hd <= D && D <= 128);
+  ORTHRUS_CHECK_ARG(A > 0 && block > 0 && L2 >= Tq && B < 65536 && Hq < 65536);
+  if (workspace == nullptr || workspace_bytes < orthrus_attn_bwd_workspace_bytes(B, Hq, Tq)) return ORTHRUS_EWORKSPACE;
+  float* delta = static_cast<float*>(workspace);
+  cudaStream_t st = as_stream(stream);
+  MaskParams mp{ORTHRUS_MASK_DUAL, anchors, A, block, nullptr, nullptr, L1, L2};
+  const int64_t items = B * Tq * Hq;
+  const bool tc = use_tensor_cores(dtype, hd, D, ORTHRUS_MASK_DUAL, nullptr) && (128 % block == 0) &&
+                  (Hq / Hkv) <= DkvSmem<128>::MAX_GROUP;
+  if (dtype == ORTHRUS_BF16) {
+    using T = __nv_bfloat16;
+    attn_delta_kernel<T><<<static_cast<unsigned>(ceil_div(items, 8)), 256, 0, st>>>(
+        static_cast<const T*>(o), static_cast<const T*>(do_), B, Hq, Tq, hd, delta);
+  } else if (dtype == ORTHRUS_F32) {
+    attn_delta_kernel<float><<<static_cast<unsigned>(ceil_div(items, 8)), 256, 0, st>>>(
+        static_cast<const float*>(o), static_cast<const float*>(do_), B, Hq, Tq, hd, delta);
+  } else {
+    return ORTHRUS_EINVAL;
+  }
+  ORTHRUS_CHECK_LAUNCH();
+  if (tc) {
+    ORTHRUS_CHECK_ARG(s1b == Hkv * s1h && s2b == Hkv * s2h);
+    ORTHRUS_CHECK_ARG(aligned16(q) && aligned16(k1) && aligned16(v1) && aligned16(k2) && aligned16(v2) &&
+                      aligned16(do_) && aligned16(dq) && aligned16(dk2) && aligned16(dv2));
+    AttnMaps m;
+    if (!make_attn_maps(m, q, k1, v1, s1h, L1, k2, v2, s2h, L2, B, Hq, Hkv, Tq, hd, D, do_)) return ORTHRUS_ECUDA;
+    dim3 grid(static_cast<unsigned>(ceil_div(Tq, 128)), Hq, static_cast<unsigned>(B));
+    dim3 grid_kv(static_cast<unsigned>(ceil_div(L2, 128)), Hkv, static_cast<unsigned>(B));
+    if (D == 128) {
+      if (set_smem(attn_dq_tc_kernel<128>, DqSmem<128>::SMEM)) return ORTHRUS_ECUDA;
+      attn_dq_tc_kernel<128><<<grid, 192, DqSmem<128>::SMEM, st>>>(m.q, m.dout, m.k1, m.v1, m.k2, m.v2, Hq, Hkv, Tq,
+                                                                     hd, scale, mp, true, lse, delta, dq);
+      ORTHRUS_CHECK_LAUNCH();
+      if (set_smem(attn_dkdv_tc_kernel<128>, DkvSmem<128>::SMEM)) return ORTHRUS_ECUDA;
+      attn_dkdv_tc_kernel<128><<<grid_kv, 192, DkvSmem<128>::SMEM, st>>>(m.q, m.dout, m.k2, m.v2, Hq, Hkv, Tq, L2,
+                                                                           hd, block, scale, lse, delta, dk2, dv2);
+    } else {
+      if (set_smem(attn_dq_tc_kernel<64>, DqSmem<64>::SMEM)) return ORTHRUS_ECUDA;
+      attn_dq_tc_kernel<64><<<grid, 192, DqSmem<64>::SMEM, st>>>(m.q, m.dout, m.k1, m.v1, m.k2, m.v2, Hq, Hkv, Tq, hd,
+                                                                   scale, mp, true, lse, delta, dq);
+      ORTHRUS_CHECK_LAUNCH();
+      if (set_smem(attn_dkdv_tc_kernel<64>, DkvSmem<64>::SMEM)) return ORTHRUS_ECUDA;
+      attn_dkdv_tc_kernel<64><<<grid_kv, 192, DkvSmem<64>::SMEM, st>>>(m.q, m.dout, m.k2, m.v2, Hq, Hkv, Tq, L2, hd,
+                                                                         block, scale, lse, delta, dk2, dv2);
+    }
+    ORTHRUS_CHECK_LAUNCH();
+    return ORTHRUS_OK;
+  }
+  dim3 grid(static_cast<unsigned>(ceil_div(Tq, kSimtQ)), Hq, static_cast<unsigned>(B));
+  dim3 grid_kv(static_cast<unsigned>(ceil_div(L2, 8)), Hkv, static_cast<unsigned>(B));
+  if (dtype == ORTHRUS_BF16) {
+    using T = __nv_bfloat16;
+    attn_dq_simt_kernel<T><<<grid, 32 * kSimtQ, 0, st>>>(
+        static_cast<const T*>(q), static_cast<const T*>(k1), static_cast<const T*>(v1), s1h, s1b,
+        static_cast<const T*>(k2), static_cast<const T*>(v2), s2h, s2b, Hq, Hkv, Tq, hd, D, scale, mp, lse, delta,
+        static_cast<const T*>(do_), dq);
+    ORTHRUS_CHECK_LAUNCH();
+    attn_dkdv_block_simt_kernel<T><<<grid_kv, 256, 0, st>>>(static_cast<const T*>(q), static_cast<const T*>(k2),
+                                                            static_cast<const T*>(v2), s2h, s2b, Hq, Hkv, Tq, hd, D,
+                                                            scale, block, L2, lse, delta, static_cast<const T*>(do_),
+                                                            dk2, dv2);
+  } else {
+    attn_dq_simt_kernel<float><<<grid, 32 * kSimtQ, 0, st>>>(
+        static_cast<const float*>(q), static_cast<const float*>(k1), static_cast<const float*>(v1), s1h, s1b,
+        static_cast<const float*>(k2), static_cast<const float*>(v2), s2h, s2b, Hq, Hkv, Tq, hd, D, scale, mp, lse,
+        delta, static_cast<const float*>(do_), dq);
+    ORTHRUS_CHECK_LAUNCH();
+    attn_dkdv_block_simt_kernel<float><<<grid_kv, 256, 0, st>>>(
+        static_cast<const float*>(q), static_cast<const float*>(k2), static_cast<const float*>(v2), s2h, s2b, Hq, Hkv,
+        Tq, hd, D, scale, block, L2, lse, delta, static_cast<const float*>(do_), dk2, dv2);
+  }
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+int orthrus_argmax_rows(const float* logits, int64_t ldl, int64_t R, int64_t V, int64_t* out, void* stream) {
+  ORTHRUS_CHECK_ARG(logits && out && R >= 0 && V > 0 && ldl >= V);
+  if (R == 0) return ORTHRUS_OK;
+  argmax_rows_kernel<<<static_cast<unsigned>(R), 512, 0, as_stream(stream)>>>(logits, ldl, V, out);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+int orthrus_decode_draft(const float* logits, int64_t B, int K, int64_t V, const int64_t* anchor, const uint8_t* done,
+                         int64_t* verify_ids, void* stream) {
+  ORTHRUS_CHECK_ARG(logits && anchor && verify_ids && B > 0 && K >= 1 && V > 0 && B < 65536);
+  if (K == 1) return ORTHRUS_OK;
+  dim3 grid(K - 1, static_cast<unsigned>(B));
+  decode_draft_kernel<<<grid, 512, 0, as_stream(stream)>>>(logits, K, V, anchor, done, verify_ids);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+int orthrus_decode_verify_accept(const float* logits, int64_t B, int K, int64_t V, const int64_t* verify_ids,
+                                 int64_t* ar_tokens, const int64_t* eos, int n_eos, const int32_t* max_len,
+                                 int32_t* start, int64_t* anchor, uint8_t* done, int64_t* out_tokens,
+                                 int32_t* out_len, int64_t out_cap, int32_t* accepted_log, int32_t* cycle,
+                                 int64_t log_cap, void* stream) {
+  ORTHRUS_CHECK_ARG(logits && verify_ids && ar_tokens && max_len && start && anchor && done && out_tokens &&
+                    out_len && accepted_log && cycle && B > 0 && K >= 1 && V > 0);
+  ORTHRUS_CHECK_ARG(n_eos == 0 || eos != nullptr);
+  cudaStream_t st = as_stream(stream);
+  argmax_rows_kernel<<<static_cast<unsigned>(B * K), 512, 0, st>>>(logits, V, V, ar_tokens);
+  ORTHRUS_CHECK_LAUNCH();
+  decode_accept_kernel<<<static_cast<unsigned>(ceil_div(B, 128)), 128, 0, st>>>(
+      B, K, verify_ids, ar_tokens, eos, n_eos, max_len, start, anchor, done, out_tokens, out_len, out_cap,
+      accepted_log, cycle, log_cap);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+}  // extern "C"
+
+extern "C" int orthrus_rmsnorm(const void* x, const void* w, int64_t rows, int d, float eps, void* y, int dtype,
+                               void* stream) {
+  ORTHRUS_CHECK_ARG(x && w && y && rows >= 0 && d > 0);
+  if (rows == 0) return ORTHRUS_OK;
+  const unsigned blocks = static_cast<unsigned>(ceil_div(rows, 8));
+  if (dtype == ORTHRUS_BF16)
+    rmsnorm_kernel<__nv_bfloat16><<<blocks, 256, 0, as_stream(stream)>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), rows, d, eps,
+        static_cast<__nv_bfloat16*>(y));
+  else if (dtype == ORTHRUS_F32)
+    rmsnorm_kernel<float><<<blocks, 256, 0, as_stream(stream)>>>(static_cast<const float*>(x),
+                                                               static_cast<const float*>(w), rows, d, eps,
+                                                               static_cast<float*>(y));
+  else
+    return ORTHRUS_EINVAL;
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}

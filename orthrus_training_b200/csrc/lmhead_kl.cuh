@@ -21,9 +21,6 @@
 
 namespace orthrus {
 
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kLn2 = 0.6931471805599453f;
-
 // ------------------------------------------------------------------------------------------------
 // Pass 1 (bf16, tcgen05): per-row online max / sum-exp / argmax over a vocabulary range.
 // ------------------------------------------------------------------------------------------------

@@ -202,6 +202,28 @@ __global__ void sum_partials_kernel(const float* __restrict__ part, int nparts, 
   out[e] = acc;
 }
 
+// RMSNorm over rows of length d (the hidden size): y = w * round(x * rsqrt(mean(x^2) + eps)), one
+// warp per row with a fixed-order shuffle reduction, so a row's result never depends on the number
+// of rows (transformers Qwen3RMSNorm; orthrus/objective.py:128-133).
+template <typename T>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t rows,
+                                                      int d, float eps, T* __restrict__ y) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  if (r >= rows) return;
+  const T* xr = x + r * d;
+  float ss = 0.f;
+  for (int e = lane; e < d; e += 32) {
+    const float v = to_f32<T>(xr[e]);
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float rstd = rsqrtf(ss / static_cast<float>(d) + eps);
+  T* yr = y + r * d;
+  for (int e = lane; e < d; e += 32) yr[e] = from_f32<T>(to_f32<T>(w[e]) * round_to<T>(to_f32<T>(xr[e]) * rstd));
+}
+
 constexpr int kPrepBwdBlocks = 592;  // fixed grid (4 x 148): a deterministic split of the items
 
 template <typename T>

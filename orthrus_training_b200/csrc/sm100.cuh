@@ -22,6 +22,8 @@ namespace orthrus {
 __device__ unsigned int g_device_error = 0;
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: legitimate waits here take microseconds
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

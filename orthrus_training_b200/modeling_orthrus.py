@@ -1,0 +1,441 @@
+"""Orthrus dual-view model on the Blackwell kernels: drop-in for orthrus/modeling_orthrus.py.
+
+Same class names, parameter names (so reference checkpoints and state dicts load unchanged), config
+fields (a Qwen3 config plus ``block_size`` and ``mask_token_id``) and call signatures as the
+reference module. The arithmetic behind them runs in ``liborthrus_b200.so``:
+
+- q/k RMSNorm + RoPE + cache write: ``ops.qkv_prep`` (orthrus/modeling_orthrus.py:153-159),
+- attention: ``ops.attention_fwd`` with the causal, dual-view or draft mask
+  (orthrus/modeling_orthrus.py:58-85,167-188),
+- projections and the LM head: ``ops.gemm`` (tcgen05 for bf16, exact CUDA-core fp32), whose
+  per-row results do not depend on the number of rows, so a K-token verification reproduces a
+  one-token greedy pass bit for bit,
+- RMSNorm and the SwiGLU activation: row-local kernels of fixed reduction order.
+
+There is no CPU path: every forward requires CUDA tensors and the built library.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+from torch import nn
+
+from orthrus_training_b200 import ops
+from orthrus_training_b200._lib import MASK_CAUSAL, MASK_DRAFT, MASK_DUAL
+from orthrus_training_b200.kv_cache import KVCache
+
+try:  # the reference configures the model with a plain Qwen3Config plus two fields
+    from transformers import Qwen3Config as OrthrusConfig
+except ImportError:  # pragma: no cover - transformers is part of the image
+    OrthrusConfig = None
+
+DIFF_MODULES = ("q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm")
+DynamicCache = KVCache  # the cache class the reference passes around (transformers DynamicCache)
+
+
+def _theta(config) -> float:
+    theta = getattr(config, "rope_theta", None)
+    if theta is None:
+        theta = config.rope_parameters["rope_theta"]
+    return float(theta)
+
+
+def padded_head_dim(head_dim: int) -> int:
+    """Head dim as stored for the attention kernels: 64 or 128 (zero padded), or the head dim itself
+    when it is larger than 128 is not supported."""
+    if head_dim > 128:
+        raise ValueError("head_dim > 128 is not supported by the attention kernels")
+    return 64 if head_dim <= 64 else 128
+
+
+class RMSNorm(nn.Module):
+    """Qwen3RMSNorm parameters (transformers Qwen3RMSNorm); forward runs the row kernel."""
+
+    def __init__(self, hidden_size: int, eps: float = 1e-6):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(hidden_size))
+        self.variance_epsilon = eps
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return ops.rms_norm(x, self.weight, self.variance_epsilon)
+
+
+class OrthrusMLP(nn.Module):
+    def __init__(self, config):
+        super().__init__()
+        self.gate_proj = nn.Linear(config.hidden_size, config.intermediate_size, bias=False)
+        self.up_proj = nn.Linear(config.hidden_size, config.intermediate_size, bias=False)
+        self.down_proj = nn.Linear(config.intermediate_size, config.hidden_size, bias=False)
+
+
+class OrthrusAttention(nn.Module):
+    """Frozen autoregressive attention and its trainable diffusion twin (*_diff), with the
+    parameter layout of orthrus/modeling_orthrus.py:114-127."""
+
+    def __init__(self, config, layer_idx: int):
+        super().__init__()
+        self.layer_idx = layer_idx
+        self.head_dim = config.head_dim
+        self.num_heads = config.num_attention_heads
+        self.num_kv_heads = config.num_key_value_heads
+        self.scaling = self.head_dim ** -0.5
+        q_dim, kv_dim = self.num_heads * self.head_dim, self.num_kv_heads * self.head_dim
+        bias = bool(getattr(config, "attention_bias", False))
+        if bias:
+            raise ValueError("attention_bias is not supported (Qwen3 has no projection biases)")
+        for suffix in ("", "_diff"):
+            setattr(self, f"q_proj{suffix}", nn.Linear(config.hidden_size, q_dim, bias=False))
+            setattr(self, f"k_proj{suffix}", nn.Linear(config.hidden_size, kv_dim, bias=False))
+            setattr(self, f"v_proj{suffix}", nn.Linear(config.hidden_size, kv_dim, bias=False))
+            setattr(self, f"o_proj{suffix}", nn.Linear(q_dim, config.hidden_size, bias=False))
+            setattr(self, f"q_norm{suffix}", RMSNorm(self.head_dim, config.rms_norm_eps))
+            setattr(self, f"k_norm{suffix}", RMSNorm(self.head_dim, config.rms_norm_eps))
+
+    def view_weights(self, diffusion: bool):
+        s = "_diff" if diffusion else ""
+        g = lambda n: getattr(self, f"{n}{s}")  # noqa: E731
+        return g("q_proj").weight, g("k_proj").weight, g("v_proj").weight, g("o_proj").weight, \
+            g("q_norm").weight, g("k_norm").weight
+
+
+class OrthrusDecoderLayer(nn.Module):
+    def __init__(self, config, layer_idx: int):
+        super().__init__()
+        self.self_attn = OrthrusAttention(config, layer_idx)
+        self.mlp = OrthrusMLP(config)
+        self.input_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        self.post_attention_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+
+
+class OrthrusModel(nn.Module):
+    def __init__(self, config):
+        super().__init__()
+        self.config = config
+        self.embed_tokens = nn.Embedding(config.vocab_size, config.hidden_size)
+        self.layers = nn.ModuleList(
+            [OrthrusDecoderLayer(config, i) for i in range(config.num_hidden_layers)])
+        self.norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        self.gradient_checkpointing = False
+
+
+@dataclass
+class ModelOutput:
+    logits: torch.Tensor | None = None
+    last_hidden_state: torch.Tensor | None = None
+    past_key_values: KVCache | None = None
+    hidden_states: tuple = ()
+
+
+@dataclass
+class GenerationStats:
+    """Forward-pass accounting of one diffusion-mode generation (orthrus/modeling_orthrus.py:299-312)."""
+
+    new_tokens: int = 0
+    accepted: list[int] = field(default_factory=list)
+
+    @property
+    def cycles(self) -> int:
+        return len(self.accepted)
+
+    @property
+    def forward_passes(self) -> int:
+        return 1 + 2 * self.cycles
+
+
+class DualViewMask:
+    """The dual-pass training mask (orthrus/modeling_orthrus.py:58-74) as the attention kernels use
+    it: per-row sorted anchors plus the per-anchor tile map. ``mask_mod`` evaluates the reference's
+    definition for inspection (a query of block b sees AR keys strictly before anchors[:, b] and
+    every key of its own block)."""
+
+    def __init__(self, anchors: torch.Tensor, ar_len: int, block_size: int):
+        self.anchors = anchors
+        self.ar_len = ar_len
+        self.block_size = block_size
+        self.num_blocks = anchors.shape[1]
+        self._tilemap = None
+
+    def mask_mod(self, batch, head, q_idx, kv_idx):
+        blocks = self.num_blocks
+        block = (q_idx // self.block_size).clamp(max=blocks - 1)
+        ar_visible = (kv_idx < self.ar_len) & (kv_idx < self.anchors[batch, block])
+        same = (kv_idx >= self.ar_len) & ((kv_idx - self.ar_len) // self.block_size
+                                          == q_idx // self.block_size)
+        return ar_visible | same
+
+    @property
+    def tilemap(self) -> torch.Tensor:
+        """int32 [B, tiles of 128 queries, 4]: (source-1 tiles, visible source-1 keys, source-2
+        key range), computed on the device (orthrus_attn_tilemap)."""
+        if self._tilemap is None:
+            self._tilemap = ops.attention_tilemap(self.anchors, self.block_size, self.ar_len)
+        return self._tilemap
+
+
+def build_block_mask(anchors: torch.Tensor, ar_len: int, block_size: int) -> DualViewMask:
+    """Dual-pass mask for training (orthrus/modeling_orthrus.py:58-74)."""
+    return DualViewMask(anchors, ar_len, block_size)
+
+
+def diffusion_attention(q, k, v, block_mask: DualViewMask) -> torch.Tensor:
+    """Masked attention of the diffusion view over cat([AR keys, block keys])
+    (orthrus/modeling_orthrus.py:77-85): q [B, Hq, Q, hd], k/v [B, Hkv, ar_len + Q, hd] ->
+    [B, Hq, Q, hd]. Runs the dual-view kernel (tcgen05 for bf16 with hd 64/128)."""
+    ar = block_mask.ar_len
+    hd = q.shape[-1]
+    D = hd if hd in (64, 128) else padded_head_dim(hd)
+    pad = (lambda t: torch.nn.functional.pad(t, (0, D - hd))) if D != hd else (lambda t: t)
+    qp = pad(q).contiguous()
+    kp, vp = pad(k).contiguous(), pad(v).contiguous()
+    o, _ = ops.attention_fwd(qp, kp[:, :, :ar], vp[:, :, :ar], kp[:, :, ar:], vp[:, :, ar:],
+                             mask=MASK_DUAL, hd=hd, scale=hd ** -0.5,
+                             anchors=block_mask.anchors, block=block_mask.block_size, want_lse=False)
+    return o.transpose(1, 2)
+
+
+@torch.no_grad()
+def copy_diff_from_ar(model: nn.Module) -> None:
+    """Warm-start every diffusion twin from its frozen AR counterpart (orthrus/modeling_orthrus.py:88-94)."""
+    for module in model.modules():
+        if isinstance(module, OrthrusAttention):
+            for name in DIFF_MODULES:
+                getattr(module, f"{name}_diff").load_state_dict(getattr(module, name).state_dict())
+
+
+def freeze_to_diffusion(model: nn.Module) -> list[nn.Parameter]:
+    """Freeze the AR backbone; return the trainable diffusion parameters (orthrus/modeling_orthrus.py:97-104)."""
+    trainable = []
+    for name, param in model.named_parameters():
+        param.requires_grad_(any(f".{m}_diff." in name for m in DIFF_MODULES))
+        if param.requires_grad:
+            trainable.append(param)
+    return trainable
+
+
+def truncate_cache(cache: KVCache, length: int) -> None:
+    """Drop cached positions >= length (orthrus/modeling_orthrus.py:107-111): on the device cache this
+    only moves the committed length."""
+    excess = cache.get_seq_length() - length
+    if excess > 0:
+        cache.crop(-excess)
+
+
+class OrthrusLM(nn.Module):
+    """Qwen3 with the Orthrus diffusion twins (orthrus/modeling_orthrus.py:315-534)."""
+
+    _tied_weights_keys = {"lm_head.weight": "model.embed_tokens.weight"}
+
+    def __init__(self, config):
+        super().__init__()
+        self.config = config
+        self.model = OrthrusModel(config)
+        self.vocab_size = config.vocab_size
+        self.lm_head = nn.Linear(config.hidden_size, config.vocab_size, bias=False)
+        if getattr(config, "tie_word_embeddings", True):
+            self.lm_head.weight = self.model.embed_tokens.weight
+        self.init_weights()
+        self._inv_freq = None
+        self._packed = {}
+
+    # -- weights ------------------------------------------------------------------------------
+
+    @torch.no_grad()
+    def init_weights(self, std: float | None = None) -> None:
+        """Random init of a Qwen3 model: normal(0, initializer_range) weights, unit norms."""
+        std = std if std is not None else getattr(self.config, "initializer_range", 0.02)
+        for name, p in self.named_parameters():
+            if name.endswith("norm.weight") or ".q_norm" in name or ".k_norm" in name or \
+                    "layernorm" in name:
+                p.fill_(1.0)
+            else:
+                p.normal_(0.0, std)
+
+    @property
+    def is_gradient_checkpointing(self) -> bool:
+        return self.model.gradient_checkpointing
+
+    def gradient_checkpointing_enable(self, kwargs=None) -> None:
+        self.model.gradient_checkpointing = True
+
+    def inv_freq(self, device) -> torch.Tensor:
+        if self._inv_freq is None or self._inv_freq.device != torch.device(device):
+            self._inv_freq = ops.rope_inv_freq(self.config.head_dim, _theta(self.config), device)
+        return self._inv_freq
+
+    def packed_qkv(self, layer: int, diffusion: bool) -> torch.Tensor:
+        """[q; k; v] projection weights of a layer's view as one [(Hq+2Hkv) hd, d] matrix, cached
+        for inference (rebuilt when a weight's version changes)."""
+        attn = self.model.layers[layer].self_attn
+        wq, wk, wv, *_ = attn.view_weights(diffusion)
+        key = (layer, diffusion)
+        versions = (wq._version, wk._version, wv._version, wq.data_ptr())
+        hit = self._packed.get(key)
+        if hit is None or hit[0] != versions:
+            with torch.no_grad():
+                hit = (versions, torch.cat([wq, wk, wv], 0).contiguous())
+            self._packed[key] = hit
+        return hit[1]
+
+    # -- forward ------------------------------------------------------------------------------
+
+    @torch.no_grad()
+    def forward(
+        self,
+        input_ids: torch.LongTensor | None = None,
+        attention_mask: torch.Tensor | None = None,
+        position_ids: torch.LongTensor | None = None,
+        past_key_values: KVCache | None = None,
+        inputs_embeds: torch.FloatTensor | None = None,
+        labels: torch.LongTensor | None = None,
+        use_cache: bool | None = None,
+        cache_position: torch.LongTensor | None = None,
+        logits_to_keep: int | torch.Tensor = 0,
+        is_diffusion_pass: bool = False,
+        ar_seq_len: int | None = None,
+        flex_block_mask: DualViewMask | None = None,
+        **kwargs,
+    ) -> ModelOutput:
+        """OrthrusLM.forward (orthrus/modeling_orthrus.py:327-362) for inference: the AR view
+        (causal over the cache plus the new tokens, appended to the cache when use_cache) or the
+        diffusion view (twin projections over cat([cache[:ar_seq_len], block]); full attention, or
+        the dual-view training mask when flex_block_mask is given). Logits are fp32."""
+        if (input_ids is None) == (inputs_embeds is None):
+            raise ValueError("pass exactly one of input_ids or inputs_embeds")
+        if attention_mask is not None and attention_mask.dim() == 4:
+            raise ValueError("dense 4-D attention masks (tree verification) are not supported yet")
+        x = inputs_embeds if inputs_embeds is not None else self.model.embed_tokens(input_ids)
+        B, T, _ = x.shape
+        if use_cache and past_key_values is None:
+            past_key_values = KVCache(self.config, batch=B, device=x.device, dtype=x.dtype)
+        cache = past_key_values
+        seen = cache.get_seq_length() if cache is not None else 0
+        if position_ids is None:
+            position_ids = torch.arange(seen, seen + T, device=x.device)[None]
+        position_ids = position_ids.expand(B, T).contiguous()
+        if is_diffusion_pass:
+            if cache is None or ar_seq_len is None:
+                raise ValueError("the diffusion pass needs the AR cache (past_key_values) and ar_seq_len")
+            if cache.get_seq_length() != ar_seq_len:
+                raise ValueError(f"AR cache holds {cache.get_seq_length()} positions, expected {ar_seq_len}")
+        hidden = self._layers(x, position_ids, cache, is_diffusion_pass, ar_seq_len,
+                              flex_block_mask, bool(use_cache))
+        if cache is not None and use_cache and not is_diffusion_pass:
+            cache.length += T
+        if isinstance(logits_to_keep, int):
+            keep = hidden[:, -logits_to_keep:] if logits_to_keep else hidden
+        else:
+            keep = hidden[:, logits_to_keep]
+        logits = self.lm_logits(keep)
+        return ModelOutput(logits=logits, last_hidden_state=hidden,
+                           past_key_values=cache if use_cache else None, hidden_states=(hidden,))
+
+    def lm_logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        shape = hidden.shape[:-1]
+        h = hidden.reshape(-1, hidden.shape[-1]).contiguous()
+        w = self.lm_head.weight
+        if h.dtype == torch.bfloat16:
+            logits = ops.gemm(h, w, out_dtype=torch.float32)
+        else:
+            logits = ops.gemm(h, w)
+        return logits.view(*shape, -1)
+
+    def _layers(self, x, positions, cache, diffusion, ar_seq_len, block_mask, write_cache):
+        cfg = self.config
+        B, T, d = x.shape
+        Hq, Hkv, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        D = padded_head_dim(hd)
+        eps = cfg.rms_norm_eps
+        inv = self.inv_freq(x.device)
+        x = x.reshape(B * T, d).contiguous()
+        offset = None
+        if cache is not None:
+            offset = cache.offsets(B)
+        for i, layer in enumerate(self.model.layers[: cfg.num_hidden_layers]):
+            attn = layer.self_attn
+            _, _, _, wo, qn, kn = attn.view_weights(diffusion)
+            h = ops.rms_norm(x, layer.input_layernorm.weight, eps)
+            qkv = ops.gemm(h, self.packed_qkv(i, diffusion))
+            if diffusion:
+                q, k2, v2, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps)
+                k1, v1 = cache.keys(i), cache.values(i)
+                if block_mask is not None:
+                    o, _ = ops.attention_fwd(q, k1, v1, k2, v2, mask=MASK_DUAL, hd=hd,
+                                             scale=attn.scaling, anchors=block_mask.anchors,
+                                             block=block_mask.block_size, L1=ar_seq_len,
+                                             want_lse=False)
+                else:
+                    o, _ = ops.attention_fwd(q, k1, v1, k2, v2, mask=MASK_DRAFT, hd=hd,
+                                             scale=attn.scaling, offset=cache.offsets(B),
+                                             L1=ar_seq_len, want_lse=False)
+            elif cache is not None:
+                q, _, _, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps,
+                                          k_cache=cache.keys(i), v_cache=cache.values(i),
+                                          offset=offset)
+                o, _ = ops.attention_fwd(q, cache.keys(i), cache.values(i), mask=MASK_CAUSAL, hd=hd,
+                                         scale=attn.scaling, offset=offset, want_lse=False)
+            else:
+                q, k, v, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps)
+                o, _ = ops.attention_fwd(q, k, v, mask=MASK_CAUSAL, hd=hd, scale=attn.scaling,
+                                         want_lse=False)
+            x = ops.add(x, ops.gemm(o.reshape(B * T, Hq * hd), wo))
+            h = ops.rms_norm(x, layer.post_attention_layernorm.weight, eps)
+            mlp = layer.mlp
+            gu = ops.gemm(h, self._packed_mlp(i))
+            x = ops.add(x, ops.gemm(ops.silu_mul(gu), mlp.down_proj.weight))
+        x = ops.rms_norm(x, self.model.norm.weight, eps)
+        return x.view(B, T, d)
+
+    def _packed_mlp(self, layer: int) -> torch.Tensor:
+        mlp = self.model.layers[layer].mlp
+        key = (layer, "mlp")
+        versions = (mlp.gate_proj.weight._version, mlp.up_proj.weight._version,
+                    mlp.gate_proj.weight.data_ptr())
+        hit = self._packed.get(key)
+        if hit is None or hit[0] != versions:
+            with torch.no_grad():
+                hit = (versions, torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight], 0).contiguous())
+            self._packed[key] = hit
+        return hit[1]
+
+    # -- generation ---------------------------------------------------------------------------
+
+    @torch.inference_mode()
+    def generate(self, input_ids, max_new_tokens=None, max_length=None, temperature=0.0, top_k=20,
+                 top_p=0.8, eos_token_id=None, streamer=None, use_diffusion_mode=True, **kwargs):
+        """OrthrusLM.generate (orthrus/modeling_orthrus.py:364-402), greedy."""
+        eos_token_id = eos_token_id if eos_token_id is not None else self.config.eos_token_id
+        max_new_tokens = max_new_tokens or (max_length - input_ids.shape[1])
+        if not use_diffusion_mode:
+            from orthrus_training_b200.decoding import ar_generate_batch
+
+            return ar_generate_batch(self, input_ids, max_new_tokens, eos_token_id)
+        output, _ = self.diffusion_generate(input_ids, max_new_tokens, temperature=temperature,
+                                            top_k=top_k, top_p=top_p, eos_token_id=eos_token_id,
+                                            streamer=streamer)
+        return output
+
+    @torch.inference_mode()
+    def diffusion_generate(self, input_ids, max_new_tokens, temperature=0.0, top_k=20, top_p=0.8,
+                           eos_token_id=None, streamer=None):
+        """Project K tokens in parallel, verify them with the AR view, keep the agreed prefix
+        (orthrus/modeling_orthrus.py:404-534), greedy, with the cycle state on the device.
+        Batch size 1 here, as the reference; decoding.block_decode takes batches."""
+        if input_ids.shape[0] != 1:
+            raise ValueError("diffusion_generate supports batch size 1")
+        if temperature >= 1e-5:
+            raise ValueError("only greedy decoding (temperature 0) runs on the device path")
+        from orthrus_training_b200.decoding import block_decode
+
+        eos = {eos_token_id} if isinstance(eos_token_id, int) else set(eos_token_id or ())
+        result = block_decode(self, [input_ids[0].tolist()], max_new_tokens, eos)
+        tokens = result.tokens[0]
+        out = torch.tensor([input_ids[0].tolist() + tokens], device=input_ids.device)
+        stats = GenerationStats(new_tokens=len(tokens), accepted=result.accepted[0])
+        if streamer is not None:
+            streamer.put(input_ids)
+            if tokens:
+                streamer.put(torch.tensor(tokens))
+            streamer.end()
+        return out, stats

@@ -109,3 +109,192 @@ def lmhead_kl_backward(grad: torch.Tensor, grad_total: torch.Tensor) -> torch.Te
                                           grad.numel(), L.dtype_code(grad.dtype),
                                           L.stream_of(grad.device)), "lmhead_kl_bwd")
     return out
+
+
+# --- q/k norm + RoPE ---------------------------------------------------------------------------
+
+
+def rope_inv_freq(head_dim: int, theta: float, device) -> torch.Tensor:
+    """1 / theta^(2i/hd) in fp32, computed with the same torch ops as the rotary embedding of the
+    reference model (transformers Qwen3RotaryEmbedding, default rope)."""
+    exponent = torch.arange(0, head_dim, 2, dtype=torch.int64).to(dtype=torch.float) / head_dim
+    return (1.0 / (theta ** exponent)).to(device)
+
+
+def qkv_prep(qkv: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor, q_norm_w, k_norm_w,
+             B: int, T: int, Hq: int, Hkv: int, hd: int, D: int, eps: float, *, k_cache=None,
+             v_cache=None, offset=None, want_rstd=False):
+    """q/k RMSNorm + RoPE of the fused projection output qkv [B*T, (Hq+2Hkv)*hd].
+    Returns (q [B, Hq, T, D], k, v, rstd); k / v are [B, Hkv, T, D] unless caches
+    [B, Hkv, cap, D] are given, in which case rows offset[b] + t of the caches are written."""
+    _require_cuda(qkv, positions)
+    dt = qkv.dtype
+    dev = qkv.device
+    qkv = qkv.contiguous()
+    q = torch.empty(B, Hq, T, D, dtype=dt, device=dev)
+    if k_cache is None:
+        k_cache = torch.empty(B, Hkv, T, D, dtype=dt, device=dev)
+        v_cache = torch.empty(B, Hkv, T, D, dtype=dt, device=dev)
+    cap = k_cache.shape[2]
+    rstd = torch.empty(B * T, Hq + Hkv, dtype=torch.float32, device=dev) if want_rstd else None
+    L.check(L.lib().orthrus_qkv_prep_fwd(
+        qkv.data_ptr(), positions.contiguous().data_ptr(), inv_freq.data_ptr(),
+        q_norm_w.contiguous().data_ptr(), k_norm_w.contiguous().data_ptr(), B, T, Hq, Hkv, hd, D,
+        float(eps), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), cap, L.ptr(offset),
+        L.ptr(rstd), L.dtype_code(dt), L.stream_of(dev)), "qkv_prep_fwd")
+    return q, k_cache, v_cache, rstd
+
+
+def qkv_prep_backward(qkv, positions, inv_freq, q_norm_w, k_norm_w, rstd, dq, dk, dv, B, T, Hq, Hkv,
+                      hd, D):
+    """Gradients of qkv_prep (training layout): dq/dk/dv fp32 head-major -> (dqkv, dq_norm_w,
+    dk_norm_w)."""
+    dt = qkv.dtype
+    dev = qkv.device
+    dqkv = torch.empty_like(qkv)
+    dqw = torch.empty(hd, dtype=torch.float32, device=dev)
+    dkw = torch.empty(hd, dtype=torch.float32, device=dev)
+    lib = L.lib()
+    ws = torch.empty(int(lib.orthrus_qkv_prep_bwd_workspace_bytes(B, T, hd)), dtype=torch.uint8,
+                     device=dev)
+    L.check(lib.orthrus_qkv_prep_bwd(
+        qkv.data_ptr(), positions.contiguous().data_ptr(), inv_freq.data_ptr(),
+        q_norm_w.contiguous().data_ptr(), k_norm_w.contiguous().data_ptr(), rstd.data_ptr(),
+        L.ptr(dq), L.ptr(dk), L.ptr(dv), B, T, Hq, Hkv, hd, D, dqkv.data_ptr(), dqw.data_ptr(),
+        dkw.data_ptr(), ws.data_ptr(), ws.numel(), L.dtype_code(dt), L.stream_of(dev)),
+        "qkv_prep_bwd")
+    return dqkv, dqw, dkw
+
+
+# --- attention ---------------------------------------------------------------------------------
+
+
+def _src(t):
+    if t is None:
+        return 0, 0, 0
+    if t.stride(3) != 1 or t.stride(2) != t.shape[3]:
+        raise ValueError("attention sources must have contiguous rows of D elements")
+    return t.stride(1), t.stride(0), t.shape[2]
+
+
+def attention_fwd(q, k1, v1, k2=None, v2=None, *, mask: int, hd: int, scale: float,
+                  anchors=None, block: int = 0, offset=None, limit2=None, L1: int | None = None,
+                  want_lse: bool = True):
+    """Dual-view / causal / draft attention. q [B, Hq, Tq, D]; sources [B, Hkv, rows, D].
+    Returns (o [B, Tq, Hq, hd] token-major, lse [B, Hq, Tq] fp32 or None)."""
+    _require_cuda(q, k1, v1, k2, v2, anchors, offset, limit2)
+    B, Hq, Tq, D = q.shape
+    Hkv = k1.shape[1]
+    s1h, s1b, rows1 = _src(k1)
+    if v1.stride() != k1.stride():
+        raise ValueError("k1 and v1 must share strides")
+    s2h, s2b, L2 = _src(k2)
+    L1 = rows1 if L1 is None else L1
+    q = q.contiguous()
+    o = torch.empty(B, Tq, Hq, hd, dtype=q.dtype, device=q.device)
+    lse = torch.empty(B, Hq, Tq, dtype=torch.float32, device=q.device) if want_lse else None
+    A = anchors.shape[1] if anchors is not None else 0
+    if anchors is not None:
+        anchors = anchors.to(torch.int64).contiguous()
+    L.check(L.lib().orthrus_attn_fwd(
+        q.data_ptr(), k1.data_ptr(), v1.data_ptr(), s1h, s1b, L1, L.ptr(k2), L.ptr(v2), s2h, s2b,
+        L2, B, Hq, Hkv, Tq, hd, D, float(scale), mask, L.ptr(anchors), A, block, L.ptr(offset),
+        L.ptr(limit2), o.data_ptr(), L.ptr(lse), L.dtype_code(q.dtype), L.stream_of(q.device)),
+        "attn_fwd")
+    return o, lse
+
+
+def attention_bwd(q, k1, v1, k2, v2, anchors, block, o, lse, dout, *, hd: int, scale: float):
+    """Backward of the dual mask: (dq [B, Hq, Tq, D], dk2, dv2 [B, Hkv, L2, D]) fp32."""
+    B, Hq, Tq, D = q.shape
+    Hkv = k1.shape[1]
+    s1h, s1b, L1 = _src(k1)
+    s2h, s2b, L2 = _src(k2)
+    dev = q.device
+    dq = torch.empty(B, Hq, Tq, D, dtype=torch.float32, device=dev)
+    dk2 = torch.empty(B, Hkv, L2, D, dtype=torch.float32, device=dev)
+    dv2 = torch.empty(B, Hkv, L2, D, dtype=torch.float32, device=dev)
+    lib = L.lib()
+    ws = torch.empty(int(lib.orthrus_attn_bwd_workspace_bytes(B, Hq, Tq)), dtype=torch.uint8,
+                     device=dev)
+    anchors = anchors.to(torch.int64).contiguous()
+    dout = dout.contiguous()
+    L.check(lib.orthrus_attn_bwd(
+        q.data_ptr(), k1.data_ptr(), v1.data_ptr(), s1h, s1b, L1, k2.data_ptr(), v2.data_ptr(),
+        s2h, s2b, L2, B, Hq, Hkv, Tq, hd, D, float(scale), anchors.data_ptr(), anchors.shape[1],
+        block, o.data_ptr(), lse.data_ptr(), dout.data_ptr(), dq.data_ptr(), dk2.data_ptr(),
+        dv2.data_ptr(), ws.data_ptr(), ws.numel(), L.dtype_code(q.dtype), L.stream_of(dev)),
+        "attn_bwd")
+    return dq, dk2, dv2
+
+
+def attention_tilemap(anchors: torch.Tensor, block: int, L1: int) -> torch.Tensor:
+    """Per 128-query tile: (source-1 tiles, visible source-1 keys, source-2 key range) int32."""
+    _require_cuda(anchors)
+    anchors = anchors.to(torch.int64).contiguous()
+    B, A = anchors.shape
+    ntiles = (A * block + 127) // 128
+    out = torch.empty(B, ntiles, 4, dtype=torch.int32, device=anchors.device)
+    L.check(L.lib().orthrus_attn_tilemap(anchors.data_ptr(), B, A, block, L1, out.data_ptr(),
+                                         L.stream_of(anchors.device)), "attn_tilemap")
+    return out
+
+
+# --- decoding ----------------------------------------------------------------------------------
+
+
+def argmax_rows(logits: torch.Tensor) -> torch.Tensor:
+    """Row-wise argmax of fp32 logits [R, V] (lowest index on ties)."""
+    _require_cuda(logits)
+    if logits.dtype != torch.float32 or logits.stride(-1) != 1:
+        raise ValueError("argmax_rows takes row-major fp32 logits")
+    R, V = logits.shape
+    out = torch.empty(R, dtype=torch.int64, device=logits.device)
+    L.check(L.lib().orthrus_argmax_rows(logits.data_ptr(), logits.stride(0), R, V, out.data_ptr(),
+                                        L.stream_of(logits.device)), "argmax_rows")
+    return out
+
+
+def decode_draft(logits, anchor, done, verify_ids):
+    B, K, V = logits.shape
+    L.check(L.lib().orthrus_decode_draft(logits.data_ptr(), B, K, V, anchor.data_ptr(),
+                                         L.ptr(done), verify_ids.data_ptr(),
+                                         L.stream_of(logits.device)), "decode_draft")
+
+
+def decode_verify_accept(logits, verify_ids, ar_tokens, eos, max_len, start, anchor, done,
+                         out_tokens, out_len, accepted_log, cycle):
+    B, K, V = logits.shape
+    L.check(L.lib().orthrus_decode_verify_accept(
+        logits.data_ptr(), B, K, V, verify_ids.data_ptr(), ar_tokens.data_ptr(), L.ptr(eos),
+        0 if eos is None else eos.numel(), max_len.data_ptr(), start.data_ptr(), anchor.data_ptr(),
+        done.data_ptr(), out_tokens.data_ptr(), out_len.data_ptr(), out_tokens.shape[1],
+        accepted_log.data_ptr(), cycle.data_ptr(), accepted_log.shape[1],
+        L.stream_of(logits.device)), "decode_verify_accept")
+
+
+# --- row-local elementwise pieces ---------------------------------------------------------------
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """Qwen3RMSNorm over the last dim with a fixed per-row reduction order (no grad)."""
+    _require_cuda(x, weight)
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1]).contiguous()
+    y = torch.empty_like(x2)
+    w = weight.to(x.dtype).contiguous()
+    L.check(L.lib().orthrus_rmsnorm(x2.data_ptr(), w.data_ptr(), x2.shape[0], x2.shape[1],
+                                    float(eps), y.data_ptr(), L.dtype_code(x.dtype),
+                                    L.stream_of(x.device)), "rmsnorm")
+    return y.view(shape)
+
+
+def add(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """Residual add (elementwise, order-free)."""
+    return x + y
+
+
+def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    """SwiGLU activation of the fused [gate | up] projection: silu(gate) * up (tf Qwen3MLP)."""
+    half = gate_up.shape[-1] // 2
+    return torch.nn.functional.silu(gate_up[..., :half]) * gate_up[..., half:]
