@@ -1,0 +1,372 @@
+"""Benchmark of the Orthrus dual-view training step (Qwen3-0.6B shape) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the headline metric, train input tok/s): per GPU one micro-batch of 8 packed rows x 2048
+tokens (seed 1 + rank), 32 anchors per row, block K = 32, bf16, random-init Qwen3-0.6B-shape
+weights; a step = frozen causal teacher pass + diffusion-view forward/backward + fused LM-head KL +
+gradient all-reduce of the twins (N > 1) + clip + AdamW. Weak scaling: rows per GPU fixed.
+Synthetic data stand in for the reference's private dataset: rows of ~300-token prompts plus
+Geometric(mean 690) responses, Zipf(1.1) ids.
+
+Prints one JSON line (rank 0). `value` is measured with each step's rows already resident in HBM;
+`e2e` runs the same steps through the public API with the rows copied from pinned host memory and
+the loss read back every step. The activations of a step are far larger than the 126 MB L2, so no
+flush is needed between steps.
+
+--impl reference times the reference algorithm's CPU implementation (the fp32 CPU port in oracle/)
+on the host cores: each step is one 2048-token row of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+ROWS, SEQ, ANCHORS, BLOCK = 8, 2048, 32, 32
+MASK_TOKEN, REAL_VOCAB = 151669, 151669
+METRIC = "train input tok/s (Qwen3-0.6B dual-view step)"
+
+
+def qwen3_06b_config():
+    from transformers import Qwen3Config
+
+    cfg = Qwen3Config(vocab_size=151936, hidden_size=1024, intermediate_size=3072,
+                      num_hidden_layers=28, num_attention_heads=16, num_key_value_heads=8,
+                      head_dim=128, max_position_embeddings=40960, rms_norm_eps=1e-6,
+                      rope_theta=1e6, tie_word_embeddings=True)
+    cfg.rope_parameters = {"rope_theta": 1e6, "rope_type": "default"}
+    cfg.block_size = BLOCK
+    cfg.mask_token_id = MASK_TOKEN
+    return cfg
+
+
+def peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return {"bf16_tflops": d["bf16_tflops"], "bf16_tflops_sustained": d["bf16_tflops_sustained"],
+                "hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0,
+            "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_rows(seed: int):
+    from orthrus_training_b200.synthetic import packed_rows
+
+    return packed_rows(ROWS, SEQ, REAL_VOCAB, seed, ids="zipf", doc="prompt_response")
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def cpu_params(cfg, seed: int = 1) -> dict:
+    """Random-init fp32 parameters of the workload's model for the CPU port (twins trainable)."""
+    g = torch.Generator().manual_seed(seed)
+    d, inter, hd = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+    qd, kvd = cfg.num_attention_heads * hd, cfg.num_key_value_heads * hd
+    params = {}
+    emb = torch.randn(cfg.vocab_size, d, generator=g) * 0.02
+    params["model.embed_tokens.weight"] = emb
+    params["lm_head.weight"] = emb
+    params["model.norm.weight"] = torch.ones(d)
+    for i in range(cfg.num_hidden_layers):
+        p = f"model.layers.{i}."
+        for suf in ("", "_diff"):
+            for n, shape in (("q_proj", (qd, d)), ("k_proj", (kvd, d)), ("v_proj", (kvd, d)),
+                             ("o_proj", (d, qd))):
+                params[f"{p}self_attn.{n}{suf}.weight"] = (torch.randn(*shape, generator=g) * 0.02
+                                                           ).requires_grad_(bool(suf))
+            params[f"{p}self_attn.q_norm{suf}.weight"] = torch.ones(hd).requires_grad_(bool(suf))
+            params[f"{p}self_attn.k_norm{suf}.weight"] = torch.ones(hd).requires_grad_(bool(suf))
+        for n, shape in (("gate_proj", (inter, d)), ("up_proj", (inter, d)), ("down_proj", (d, inter))):
+            params[f"{p}mlp.{n}.weight"] = torch.randn(*shape, generator=g) * 0.02
+        params[f"{p}input_layernorm.weight"] = torch.ones(d)
+        params[f"{p}post_attention_layernorm.weight"] = torch.ones(d)
+    return params
+
+
+def cpu_baseline_sample() -> dict:
+    """The reference algorithm on the host cores: orthrus_loss forward + backward of one row of
+    the workload through the fp32 CPU port (oracle/), all host threads, one timed run after the
+    parameters are built (about 10-30 s of CPU work)."""
+    import oracle as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = qwen3_06b_config()
+    ocfg = O.OracleConfig.from_hf(cfg)
+    params = cpu_params(cfg)
+    ids, mask = make_rows(1)
+    ids, mask = ids[:1], mask[:1]
+    anchors, valid = O.sample_anchors(mask, BLOCK, ANCHORS, torch.Generator().manual_seed(0))
+    t0 = time.perf_counter()
+    loss, _ = O.orthrus_loss(params, ocfg, ids, mask, anchors, valid)
+    loss.backward()
+    sec = time.perf_counter() - t0
+    return {"value": round(SEQ / sec, 2), "unit": "input tok/s", "cores": threads, "kind": "port",
+            "sample": f"1 row x {SEQ} tokens, {ANCHORS} anchors, K={BLOCK}: fp32 orthrus_loss "
+                      f"fwd+bwd through the CPU port of the reference algorithm ({sec:.1f} s)"}
+
+
+def run_reference(args):
+    """--impl reference: the reference algorithm's CPU implementation timed on the host cores."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = qwen3_06b_config()
+    ocfg = O.OracleConfig.from_hf(cfg)
+    params = cpu_params(cfg)
+    ids, mask = make_rows(1)
+    times = []
+    for step in range(args.warmup + args.steps):
+        r = step % ROWS
+        row_ids, row_mask = ids[r: r + 1], mask[r: r + 1]
+        anchors, valid = O.sample_anchors(row_mask, BLOCK, ANCHORS, torch.Generator().manual_seed(step))
+        t0 = time.perf_counter()
+        loss, _ = O.orthrus_loss(params, ocfg, row_ids, row_mask, anchors, valid)
+        loss.backward()
+        for v in params.values():
+            v.grad = None
+        if step >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    value = SEQ / sec
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "input tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": "Qwen3-0.6B-shape dual-view train step, one "
+                                        "2048-token row per step on the host cores",
+                                        "rows": 1, "seq_len": SEQ, "anchors": ANCHORS, "block": BLOCK},
+        "cpu_baseline": {"value": value, "unit": "input tok/s", "cores": threads, "kind": "port",
+                         "sample": f"1 row x {SEQ} tokens per step, fp32 orthrus_loss fwd+bwd"},
+        "e2e": {"value": value, "unit": "input tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    from orthrus_training_b200 import _lib, ops
+    from orthrus_training_b200.modeling_orthrus import OrthrusLM, copy_diff_from_ar
+    from orthrus_training_b200.train_step import Trainer
+
+    torch.manual_seed(1)
+    cfg = qwen3_06b_config()
+    with torch.device(dev):
+        model = OrthrusLM(cfg).to(torch.bfloat16)
+    copy_diff_from_ar(model)
+    group = None
+    trainer = Trainer(model, lr=1e-4, total_steps=1000, num_anchors=ANCHORS, kl_chunk_size=4096,
+                      seed=1, world=world, rank=rank, group=group)
+    ids, mask = make_rows(1 + rank)
+    ids_dev, mask_dev = ids.to(dev), mask.to(dev)
+    ids_pin, mask_pin = ids.pin_memory(), mask.pin_memory()
+    h2d = ids.numel() * ids.element_size() + mask.numel() * mask.element_size()
+
+    for _ in range(args.warmup):
+        trainer.step([(ids_dev, mask_dev)])
+    barrier(world)
+
+    # device-resident inputs, kernel timing on
+    ops.TIMER = ops.KernelTimer()
+    launches0 = _lib.launch_count()
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        for _ in range(args.steps):
+            out = trainer.step([(ids_dev, mask_dev)])
+        e1.record()
+        barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    launches = (_lib.launch_count() - launches0) // max(args.steps, 1)
+    kernels = ops.TIMER.summary()
+    ops.TIMER = None
+    loss = float(out["loss"])
+
+    # end to end through the public API: rows from pinned host memory, loss read back each step
+    barrier(world)
+    f0, f1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    f0.record()
+    for _ in range(args.steps):
+        b_ids = ids_pin.to(dev, non_blocking=True)
+        b_mask = mask_pin.to(dev, non_blocking=True)
+        o = trainer.step([(b_ids, b_mask)])
+        float(o["loss"])
+    f1.record()
+    barrier(world)
+    ms_e2e = max_over_ranks(f0.elapsed_time(f1), world)
+
+    tokens = ROWS * SEQ * world * args.steps
+    value = tokens / (ms / 1e3)
+    pk = peaks()
+    dominant = max(kernels.items(), key=lambda kv: kv[1]["ms"]) if kernels else None
+    roofline = None
+    if dominant:
+        name, rec = dominant
+        per_launch_ms = rec["ms"] / rec["launches"]
+        achieved = rec["flops"] / rec["launches"] / (per_launch_ms / 1e3) / 1e12
+        peak = pk["bf16_tflops"]
+        traffic = None
+        tfile = ROOT / "profiles" / "traffic.json"
+        if tfile.exists():
+            traffic = json.loads(tfile.read_text()).get(name)
+        roofline = {"bound": "tensor", "kernel": name, "achieved": round(achieved, 1),
+                    "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                    "traffic": traffic, "peak_source": pk["source"],
+                    "ms_per_launch": round(per_launch_ms, 4), "launches_per_step": rec["launches"] // args.steps}
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "input tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded packed rows, Zipf(1.1) ids, random-init weights)",
+        "config": {"workload": "Qwen3-0.6B-shape dual-view train step: 8 rows x 2048 tokens per GPU, "
+                               "32 anchors/row, K=32, teacher pass + diffusion fwd/bwd + fused "
+                               "LM-head KL + AdamW on the twins", "global_batch": ROWS * world,
+                   "seq_len": SEQ, "parallelism": f"dp{world}",
+                   "l2": "inputs and activations exceed the 126 MB L2 (no flush needed)"},
+        "e2e": {"value": round(tokens / (ms_e2e / 1e3), 1), "unit": "input tok/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+        "gpu_launches": int(launches),
+        "roofline": roofline,
+        "kernels": {k: {"launches_per_step": v["launches"] // args.steps,
+                        "ms_per_step": round(v["ms"] / args.steps, 3),
+                        "tflops": round(v["flops"] / (v["ms"] / 1e3) / 1e12, 1) if v["ms"] else None}
+                    for k, v in kernels.items()},
+        "loss": round(loss, 5),
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample()
+    err = _lib.device_error(local)
+    if err:
+        line["device_error"] = err
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -11,7 +11,7 @@
  *     failed launch. Kernels never trap: a device-side wait that runs out of time (2 s) records a
  *     bit in the device error word, read with orthrus_device_error();
  *   - dtype codes: ORTHRUS_BF16 (tensor-core path) or ORTHRUS_F32 (exact fp32 path on CUDA cores);
- *   - no global mutable state besides the device error word.
+ *   - no global mutable state besides the device error word and a host-side launch counter.
  *
  * Each entry point names the reference interface it replaces (paths inside the reference project
  * ekonst41/orthrus-training).
@@ -50,6 +50,9 @@ extern "C" {
 
 /* Library version (major*10000 + minor*100 + patch). */
 int orthrus_version(void);
+
+/* Number of kernels this process has launched through the library so far (diagnostics). */
+unsigned long long orthrus_launch_count(void);
 
 /* Reads the device error word of `device` (synchronizes that device) into *word; clears it when
  * `clear` is non-zero. Returns ORTHRUS_OK, or ORTHRUS_EDEVICE when the word was non-zero. */

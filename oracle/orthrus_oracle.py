@@ -388,9 +388,12 @@ def forward_logits(params, cfg: OracleConfig, ids, positions, cache: OracleCache
 
 
 @torch.no_grad()
-def ar_generate(params, cfg: OracleConfig, prompt: torch.Tensor, max_new_tokens: int, eos=()):
+def ar_generate(params, cfg: OracleConfig, prompt: torch.Tensor, max_new_tokens: int, eos=(),
+                gaps: list | None = None):
     """Plain greedy decoding with the frozen AR view (orthrus/evaluate.py:59-76): prompt [1, P] ->
-    list of new tokens (stops after an EOS token or max_new_tokens)."""
+    list of new tokens (stops after an EOS token or max_new_tokens). When `gaps` is a list, the
+    top-1 minus top-2 logit gap of every token is appended to it (the reference returns the same
+    gaps to tell rounding ties from bugs)."""
     cache = OracleCache(cfg.num_layers)
     pos = torch.arange(prompt.shape[1])[None]
     logits = forward_logits(params, cfg, prompt, pos, cache)
@@ -398,6 +401,9 @@ def ar_generate(params, cfg: OracleConfig, prompt: torch.Tensor, max_new_tokens:
     while True:
         token = int(logits[0, -1].argmax())
         tokens.append(token)
+        if gaps is not None:
+            top2 = logits[0, -1].topk(2).values
+            gaps.append(float(top2[0] - top2[1]))
         if token in eos or len(tokens) == max_new_tokens:
             return tokens
         pos = torch.tensor([[cache.length()]])

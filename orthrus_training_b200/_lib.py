@@ -22,6 +22,7 @@ ERR_TIMEOUT, ERR_BOUNDS = 1, 2
 _P = c_void_p
 _SIGNATURES = {
     "orthrus_version": (c_int, []),
+    "orthrus_launch_count": (ctypes.c_ulonglong, []),
     "orthrus_device_error": (c_int, [c_int, ctypes.POINTER(c_uint), c_int]),
     "orthrus_gemm_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
     "orthrus_gemm_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int64, c_int64, c_int64,
@@ -108,6 +109,10 @@ def dtype_code(dtype: torch.dtype) -> int:
     if dtype == torch.float32:
         return F32
     raise ValueError(f"unsupported dtype {dtype}: the kernels take bfloat16 or float32")
+
+
+def launch_count() -> int:
+    return int(lib().orthrus_launch_count())
 
 
 def device_error(device: int = 0, clear: bool = True) -> int:

@@ -22,6 +22,8 @@ extern "C" {
 
 int orthrus_version(void) { return 100; }
 
+unsigned long long orthrus_launch_count(void) { return launch_counter().load(std::memory_order_relaxed); }
+
 int orthrus_device_error(int device, unsigned int* word, int clear) {
   ORTHRUS_CHECK_ARG(word != nullptr);
   int prev = 0;
@@ -140,7 +142,7 @@ bool use_tensor_cores(int dtype, int hd, int D, int mask, const int32_t* offset)
 
 template <typename Kern>
 int set_smem(Kern k, int bytes) {
-  ORTHRUS_CHECK_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  ORTHRUS_CHECK_CUDA(ensure_smem(k, bytes));
   return ORTHRUS_OK;
 }
 

@@ -228,11 +228,11 @@ int launch_gemm_tc(const CUtensorMap& ta, const CUtensorMap& tb, void* C, int64_
   float* part = splits > 1 ? ws : nullptr;
   if (out_f32) {
     auto kern = gemm_tc_kernel<BN, B_MN, true>;
-    ORTHRUS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM));
+    ORTHRUS_CHECK_CUDA(ensure_smem(kern, T::SMEM));
     kern<<<grid, 192, T::SMEM, stream>>>(ta, tb, C, ldc, part, M, N, K, kbps);
   } else {
     auto kern = gemm_tc_kernel<BN, B_MN, false>;
-    ORTHRUS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM));
+    ORTHRUS_CHECK_CUDA(ensure_smem(kern, T::SMEM));
     kern<<<grid, 192, T::SMEM, stream>>>(ta, tb, C, ldc, part, M, N, K, kbps);
   }
   ORTHRUS_CHECK_LAUNCH();

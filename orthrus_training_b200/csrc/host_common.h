@@ -7,6 +7,10 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <atomic>
+#include <mutex>
+#include <unordered_map>
+
 #include "orthrus_b200.h"
 
 namespace orthrus {
@@ -29,7 +33,33 @@ namespace orthrus {
     }                                                                                       \
   } while (0)
 
-#define ORTHRUS_CHECK_LAUNCH() ORTHRUS_CHECK_CUDA(cudaGetLastError())
+// Kernels launched by this process through the library (diagnostics: every launch site is followed
+// by exactly one ORTHRUS_CHECK_LAUNCH).
+inline std::atomic<unsigned long long>& launch_counter() {
+  static std::atomic<unsigned long long> n{0};
+  return n;
+}
+
+#define ORTHRUS_CHECK_LAUNCH()                                                  \
+  do {                                                                          \
+    orthrus::launch_counter().fetch_add(1, std::memory_order_relaxed);          \
+    ORTHRUS_CHECK_CUDA(cudaGetLastError());                                     \
+  } while (0)
+
+// Opts a kernel into `bytes` of dynamic shared memory once per process and kernel (the attribute
+// persists; repeating it on every launch would also add a driver call inside stream capture).
+template <typename Kern>
+inline cudaError_t ensure_smem(Kern kernel, int bytes) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, int> done;
+  const void* key = reinterpret_cast<const void*>(kernel);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done[key] = bytes;
+  return e;
+}
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

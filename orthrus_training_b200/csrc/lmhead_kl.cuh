@@ -749,8 +749,7 @@ int lmhead_kl_fwd_impl(const T* student, int64_t n, const T* teacher, int64_t m,
     const int vt = static_cast<int>(ceil_div(V, 256));
     const int tps = static_cast<int>(ceil_div(vt, p.stats_splits));
     const int splits = static_cast<int>(ceil_div(vt, tps));
-    ORTHRUS_CHECK_CUDA(cudaFuncSetAttribute(lmhead_stats_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            StatsTile::SMEM));
+    ORTHRUS_CHECK_CUDA(ensure_smem(lmhead_stats_tc_kernel, StatsTile::SMEM));
     dim3 grid(static_cast<unsigned>(ceil_div(R, 128)), splits);
     lmhead_stats_tc_kernel<<<grid, 192, StatsTile::SMEM, stream>>>(tmH, tmW, static_cast<int>(R), static_cast<int>(V),
                                                                    static_cast<int>(D), tps, pm, ps, pi);
@@ -786,8 +785,7 @@ int lmhead_kl_fwd_impl(const T* student, int64_t n, const T* teacher, int64_t m,
       const int vt = static_cast<int>(ceil_div(V, 128));
       const int tps = static_cast<int>(ceil_div(vt, p.diff_splits));
       splits = static_cast<int>(ceil_div(vt, tps));
-      ORTHRUS_CHECK_CUDA(cudaFuncSetAttribute(lmhead_diff_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              DiffTile::SMEM));
+      ORTHRUS_CHECK_CUDA(ensure_smem(lmhead_diff_tc_kernel, DiffTile::SMEM));
       dim3 grid(static_cast<unsigned>(ceil_div(rows, 128)), splits);
       lmhead_diff_tc_kernel<<<grid, 192, DiffTile::SMEM, stream>>>(tmS, tmT, tmW, tmD, rows, static_cast<int>(c0),
                                                                    static_cast<int>(V), static_cast<int>(D), tps,

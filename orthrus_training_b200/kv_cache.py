@@ -73,6 +73,9 @@ class KVCache:
                 lst[i] = new
         self.capacity = cap
 
+    def buffers(self) -> list[tuple[torch.Tensor, torch.Tensor]]:
+        return list(zip(self.k, self.v))
+
     def keys(self, layer: int) -> torch.Tensor:
         return self.k[layer]
 

@@ -319,8 +319,19 @@ class OrthrusLM(nn.Module):
                 raise ValueError("the diffusion pass needs the AR cache (past_key_values) and ar_seq_len")
             if cache.get_seq_length() != ar_seq_len:
                 raise ValueError(f"AR cache holds {cache.get_seq_length()} positions, expected {ar_seq_len}")
-        hidden = self._layers(x, position_ids, cache, is_diffusion_pass, ar_seq_len,
-                              flex_block_mask, bool(use_cache))
+        kv = cache.buffers() if cache is not None else None
+        if cache is not None:
+            cache.reserve(seen + T)
+            kv = cache.buffers()
+        offsets = cache.offsets(B) if cache is not None else None
+        if not is_diffusion_pass:
+            mode = "ar"
+            if not use_cache and cache is not None:
+                raise ValueError("an AR pass over a cache must append to it (use_cache=True)")
+        else:
+            mode = "dual" if flex_block_mask is not None else "draft"
+        hidden = self.run_layers(x, position_ids, mode, kv=kv, offsets=offsets, ar_len=ar_seq_len,
+                                 block_mask=flex_block_mask)
         if cache is not None and use_cache and not is_diffusion_pass:
             cache.length += T
         if isinstance(logits_to_keep, int):
@@ -341,49 +352,56 @@ class OrthrusLM(nn.Module):
             logits = ops.gemm(h, w)
         return logits.view(*shape, -1)
 
-    def _layers(self, x, positions, cache, diffusion, ar_seq_len, block_mask, write_cache):
+    def run_layers(self, x, positions, mode: str, *, kv=None, offsets=None, ar_len=None,
+                   limit2=None, block_mask=None):
+        """The decoder stack over x [B, T, d] at positions [B, T] (int64) -> final-norm hidden.
+
+        mode "ar":    AR view; with kv (per-layer [B, Hkv, cap, D] buffers) the new K/V are written
+                      at rows offsets[b] + t and queries attend causally over rows < offsets[b]+t+1
+                      (a verification or plain greedy pass); without kv, plain causal attention.
+        mode "draft": diffusion view over kv rows < offsets[b] plus the block's own keys
+                      [0, limit2[b]) (the generation-time draft, orthrus/modeling_orthrus.py:469-481).
+        mode "dual":  diffusion view with the training mask (block_mask) over kv rows < ar_len.
+        """
         cfg = self.config
         B, T, d = x.shape
         Hq, Hkv, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
         D = padded_head_dim(hd)
         eps = cfg.rms_norm_eps
         inv = self.inv_freq(x.device)
+        diffusion = mode != "ar"
         x = x.reshape(B * T, d).contiguous()
-        offset = None
-        if cache is not None:
-            offset = cache.offsets(B)
         for i, layer in enumerate(self.model.layers[: cfg.num_hidden_layers]):
             attn = layer.self_attn
             _, _, _, wo, qn, kn = attn.view_weights(diffusion)
             h = ops.rms_norm(x, layer.input_layernorm.weight, eps)
             qkv = ops.gemm(h, self.packed_qkv(i, diffusion))
-            if diffusion:
-                q, k2, v2, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps)
-                k1, v1 = cache.keys(i), cache.values(i)
-                if block_mask is not None:
-                    o, _ = ops.attention_fwd(q, k1, v1, k2, v2, mask=MASK_DUAL, hd=hd,
-                                             scale=attn.scaling, anchors=block_mask.anchors,
-                                             block=block_mask.block_size, L1=ar_seq_len,
-                                             want_lse=False)
-                else:
-                    o, _ = ops.attention_fwd(q, k1, v1, k2, v2, mask=MASK_DRAFT, hd=hd,
-                                             scale=attn.scaling, offset=cache.offsets(B),
-                                             L1=ar_seq_len, want_lse=False)
-            elif cache is not None:
+            if mode == "ar" and kv is not None:
+                kb, vb = kv[i]
                 q, _, _, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps,
-                                          k_cache=cache.keys(i), v_cache=cache.values(i),
-                                          offset=offset)
-                o, _ = ops.attention_fwd(q, cache.keys(i), cache.values(i), mask=MASK_CAUSAL, hd=hd,
-                                         scale=attn.scaling, offset=offset, want_lse=False)
-            else:
+                                          k_cache=kb, v_cache=vb, offset=offsets)
+                o, _ = ops.attention_fwd(q, kb, vb, mask=MASK_CAUSAL, hd=hd, scale=attn.scaling,
+                                         offset=offsets, want_lse=False)
+            elif mode == "ar":
                 q, k, v, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps)
                 o, _ = ops.attention_fwd(q, k, v, mask=MASK_CAUSAL, hd=hd, scale=attn.scaling,
                                          want_lse=False)
+            else:
+                q, k2, v2, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps)
+                kb, vb = kv[i]
+                if mode == "dual":
+                    o, _ = ops.attention_fwd(q, kb, vb, k2, v2, mask=MASK_DUAL, hd=hd,
+                                             scale=attn.scaling, anchors=block_mask.anchors,
+                                             block=block_mask.block_size, L1=ar_len,
+                                             want_lse=False)
+                else:
+                    o, _ = ops.attention_fwd(q, kb, vb, k2, v2, mask=MASK_DRAFT, hd=hd,
+                                             scale=attn.scaling, offset=offsets, limit2=limit2,
+                                             want_lse=False)
             x = ops.add(x, ops.gemm(o.reshape(B * T, Hq * hd), wo))
             h = ops.rms_norm(x, layer.post_attention_layernorm.weight, eps)
-            mlp = layer.mlp
             gu = ops.gemm(h, self._packed_mlp(i))
-            x = ops.add(x, ops.gemm(ops.silu_mul(gu), mlp.down_proj.weight))
+            x = ops.add(x, ops.gemm(ops.silu_mul(gu), layer.mlp.down_proj.weight))
         x = ops.rms_norm(x, self.model.norm.weight, eps)
         return x.view(B, T, d)
 

@@ -1,0 +1,290 @@
+"""Orthrus training objective on the Blackwell kernels: drop-in for orthrus/objective.py.
+
+Same functions, signatures and return values as the reference module. Both views run through
+``liborthrus_b200.so``:
+
+- teacher (frozen, no grad): per layer RMSNorm -> fused q|k|v projection -> q/k norm + RoPE
+  prologue -> causal tcgen05 attention -> o projection -> SwiGLU MLP; its K/V become the AR cache
+  (orthrus/objective.py:152-157,248-255);
+- student (diffusion view, autograd): twin q|k|v projection -> ``DualViewAttention`` (prologue +
+  dual-view tcgen05 attention with the per-anchor tile map; backward = dQ over every visible key
+  tile plus dK/dV of the own-block keys only, the reference's skip_ar_key_grads) -> twin o
+  projection -> frozen MLP (orthrus/objective.py:160-165,257-272);
+- KL: ``FusedLinearForwardKL`` over the fused LM-head + log-softmax + KL kernels, which also emit the
+  per-offset KL / agreement sums (orthrus/objective.py:298-392,440-452).
+
+Projection GEMMs of the training step use torch (cuBLAS) matmuls; every attention, norm + RoPE,
+LM-head and KL computation is a kernel of this package. There is no CPU path.
+"""
+
+from __future__ import annotations
+
+import logging
+
+import torch
+import torch.nn.functional as F
+
+from orthrus_training_b200 import ops
+from orthrus_training_b200._lib import MASK_CAUSAL, MASK_DUAL
+from orthrus_training_b200.modeling_orthrus import (
+    OrthrusLM,
+    build_block_mask,
+    diffusion_attention,  # noqa: F401  (re-exported like the reference module)
+    padded_head_dim,
+)
+
+log = logging.getLogger(__name__)
+
+SKIP_AR_KEY_GRADS = True  # always: the AR keys are the frozen teacher's and never get dK/dV
+
+
+def sample_anchors(assistant_mask: torch.Tensor, block_size: int, num_anchors: int,
+                   generator: torch.Generator) -> tuple[torch.Tensor, torch.Tensor]:
+    """Sorted anchors drawn without replacement from assistant positions in [1, L-K]; spare slots
+    repeat the last anchor and are invalid (orthrus/objective.py:37-63). The same torch RNG calls
+    as the reference, so one generator state yields the reference's anchors."""
+    batch, seq_len = assistant_mask.shape
+    slots = min(num_anchors, seq_len - block_size)
+    device = assistant_mask.device
+    positions = torch.arange(1, seq_len - block_size + 1, device=device)
+    anchors = torch.zeros((batch, slots), dtype=torch.long, device=device)
+    valid = torch.zeros((batch, slots), dtype=torch.bool, device=device)
+    for row in range(batch):
+        candidates = positions[assistant_mask[row, positions]]
+        has_targets = candidates.numel() > 0
+        if not has_targets:
+            candidates = positions
+        order = torch.randperm(candidates.numel(), generator=generator, device=device)
+        picked = candidates[order[:slots]].sort().values
+        anchors[row, : len(picked)] = picked
+        anchors[row, len(picked):] = picked[-1]
+        valid[row, : len(picked)] = has_targets
+    return anchors, valid
+
+
+def supervision_mask(assistant_mask, anchors, valid, block_size):
+    """keep[b, a, i]: target anchor+i+1 is an assistant token and the slot is valid
+    (orthrus/objective.py:66-73). Shape [batch, slots, K-1]."""
+    targets = anchors[:, :, None] + torch.arange(1, block_size, device=anchors.device)
+    keep = assistant_mask.gather(1, targets.flatten(1)).view_as(targets)
+    return keep & valid[:, :, None]
+
+
+def position_weights(block_size: int, gamma: float, device=None) -> torch.Tensor | None:
+    """exp(-i/gamma), i = 0..K-2, or None for gamma <= 0 (orthrus/objective.py:76-81)."""
+    if gamma <= 0:
+        return None
+    return torch.exp(-torch.arange(block_size - 1, device=device, dtype=torch.float32) / gamma)
+
+
+def _rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """Qwen3RMSNorm with autograd (orthrus/objective.py:128-133), for the student path."""
+    dtype = x.dtype
+    xf = x.float()
+    xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return weight * xf.to(dtype)
+
+
+class DualViewAttention(torch.autograd.Function):
+    """Diffusion-view attention of one layer from the twin projection output.
+
+    forward: q/k RMSNorm + RoPE prologue (orthrus_qkv_prep_fwd) of qkv [B*Q, (Hq+2Hkv) hd], then
+    the dual-view attention (orthrus_attn_fwd, mask DUAL) over source 1 = the teacher's K/V and
+    source 2 = the block's own K/V. Returns o [B*Q, Hq*hd] (the o_proj input).
+    backward: orthrus_attn_bwd (dQ for every visible key, dK/dV of the own-block keys only), then
+    orthrus_qkv_prep_bwd back to dqkv and the q/k norm weight gradients.
+    """
+
+    @staticmethod
+    def forward(ctx, qkv, q_norm_w, k_norm_w, ar_k, ar_v, positions, anchors, inv_freq, meta):
+        B, Q, Hq, Hkv, hd, D, K, eps = meta
+        q, k2, v2, rstd = ops.qkv_prep(qkv, positions, inv_freq, q_norm_w, k_norm_w, B, Q, Hq, Hkv,
+                                       hd, D, eps, want_rstd=True)
+        o, lse = ops.attention_fwd(q, ar_k, ar_v, k2, v2, mask=MASK_DUAL, hd=hd, scale=hd ** -0.5,
+                                   anchors=anchors, block=K)
+        ctx.save_for_backward(qkv, q_norm_w, k_norm_w, ar_k, ar_v, positions, anchors, inv_freq, q,
+                              k2, v2, o, lse, rstd)
+        ctx.meta = meta
+        return o.view(B * Q, Hq * hd)
+
+    @staticmethod
+    def backward(ctx, grad_o):
+        qkv, qn, kn, ar_k, ar_v, positions, anchors, inv, q, k2, v2, o, lse, rstd = ctx.saved_tensors
+        B, Q, Hq, Hkv, hd, D, K, eps = ctx.meta
+        dout = grad_o.contiguous().view(B, Q, Hq, hd).to(q.dtype)
+        dq, dk2, dv2 = ops.attention_bwd(q, ar_k, ar_v, k2, v2, anchors, K, o, lse, dout, hd=hd,
+                                         scale=hd ** -0.5)
+        dqkv, dqw, dkw = ops.qkv_prep_backward(qkv, positions, inv, qn, kn, rstd, dq, dk2, dv2, B,
+                                               Q, Hq, Hkv, hd, D)
+        return dqkv, dqw.to(qn.dtype), dkw.to(kn.dtype), None, None, None, None, None, None
+
+
+def _teacher_layer(model, i, x, pos, B, L, inv):
+    cfg = model.config
+    layer = model.model.layers[i]
+    attn = layer.self_attn
+    Hq, Hkv, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+    D = padded_head_dim(hd)
+    eps = cfg.rms_norm_eps
+    h = ops.rms_norm(x, layer.input_layernorm.weight, eps)
+    qkv = h @ model.packed_qkv(i, False).t()
+    q, k, v, _ = ops.qkv_prep(qkv, pos, inv, attn.q_norm.weight, attn.k_norm.weight, B, L, Hq, Hkv,
+                              hd, D, eps)
+    o, _ = ops.attention_fwd(q, k, v, mask=MASK_CAUSAL, hd=hd, scale=hd ** -0.5, want_lse=False)
+    x = x + o.view(B * L, Hq * hd) @ attn.o_proj.weight.t()
+    h = ops.rms_norm(x, layer.post_attention_layernorm.weight, eps)
+    x = x + ops.silu_mul(h @ model._packed_mlp(i).t()) @ layer.mlp.down_proj.weight.t()
+    return x, k, v
+
+
+def _diffusion_layer(model, i, x, ar_k, ar_v, positions, anchors, inv, B, Q):
+    cfg = model.config
+    layer = model.model.layers[i]
+    attn = layer.self_attn
+    Hq, Hkv, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+    eps = cfg.rms_norm_eps
+    meta = (B, Q, Hq, Hkv, hd, padded_head_dim(hd), cfg.block_size, eps)
+    h = _rms_norm(x, layer.input_layernorm.weight, eps)
+    w_qkv = torch.cat([attn.q_proj_diff.weight, attn.k_proj_diff.weight, attn.v_proj_diff.weight], 0)
+    qkv = F.linear(h, w_qkv)
+    o = DualViewAttention.apply(qkv, attn.q_norm_diff.weight, attn.k_norm_diff.weight, ar_k, ar_v,
+                                positions, anchors, inv, meta)
+    x = x + F.linear(o, attn.o_proj_diff.weight)
+    h = _rms_norm(x, layer.post_attention_layernorm.weight, eps)
+    gu = F.linear(h, model._packed_mlp(i))
+    return x + F.linear(ops.silu_mul(gu), layer.mlp.down_proj.weight)
+
+
+def model_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tensor,
+                 compiled: bool = False, kernel_options: dict | None = None):
+    """Final hidden states of the diffusion view over all anchor blocks [B, A*K, d] and of the
+    frozen AR view over the clean rows [B, L, d] (orthrus/objective.py:228-272). `compiled` and
+    `kernel_options` are accepted for signature compatibility; the kernels are fixed."""
+    cfg = model.config
+    if any(t != "full_attention" for t in getattr(cfg, "layer_types", ["full_attention"])
+           [: cfg.num_hidden_layers]):
+        raise ValueError("model_states supports full attention layers only (no sliding window)")
+    if not input_ids.is_cuda:
+        raise ValueError("model_states runs on CUDA tensors only (no CPU fallback)")
+    K = cfg.block_size
+    B, L = input_ids.shape
+    d = cfg.hidden_size
+    inv = model.inv_freq(input_ids.device)
+    embed = model.model.embed_tokens.weight
+    with torch.no_grad():
+        x = F.embedding(input_ids, embed).reshape(B * L, d)
+        pos = torch.arange(L, device=x.device)[None].expand(B, L).contiguous()
+        cache = []
+        for i in range(cfg.num_hidden_layers):
+            x, k, v = _teacher_layer(model, i, x, pos, B, L, inv)
+            cache.append((k, v))
+        teacher = ops.rms_norm(x, model.model.norm.weight, cfg.rms_norm_eps).view(B, L, d)
+    anchors = anchors.to(torch.int64).contiguous()
+    positions = (anchors[:, :, None] + torch.arange(K, device=anchors.device)).flatten(1).contiguous()
+    block_ids = torch.full((B, anchors.shape[1], K), cfg.mask_token_id, dtype=torch.long,
+                           device=anchors.device)
+    block_ids[:, :, 0] = input_ids.gather(1, anchors)
+    Q = anchors.shape[1] * K
+    x = F.embedding(block_ids.flatten(1), embed).reshape(B * Q, d)
+    checkpoint = model.is_gradient_checkpointing and torch.is_grad_enabled()
+    for i, (k, v) in enumerate(cache):
+        args = (model, i, x, k, v, positions, anchors, inv, B, Q)
+        if checkpoint:
+            x = torch.utils.checkpoint.checkpoint(_diffusion_layer, *args, use_reentrant=False)
+        else:
+            x = _diffusion_layer(*args)
+    student = _rms_norm(x, model.model.norm.weight, cfg.rms_norm_eps)
+    return student.view(B, Q, d), teacher
+
+
+@torch.no_grad()
+def reference_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tensor):
+    """model_states through the module forward (OrthrusLM.forward with the dual-view mask), as the
+    reference's reference_states (orthrus/objective.py:275-295)."""
+    K, mask_token_id = model.config.block_size, model.config.mask_token_id
+    B, L = input_ids.shape
+    teacher = model(input_ids=input_ids, use_cache=True, logits_to_keep=1)
+    positions = anchors[:, :, None] + torch.arange(K, device=anchors.device)
+    block_ids = torch.full_like(positions, mask_token_id)
+    block_ids[:, :, 0] = input_ids.gather(1, anchors)
+    student = model(input_ids=block_ids.flatten(1), position_ids=positions.flatten(1),
+                    past_key_values=teacher.past_key_values, use_cache=False, is_diffusion_pass=True,
+                    ar_seq_len=L, flex_block_mask=build_block_mask(anchors, L, K), logits_to_keep=1)
+    return student.last_hidden_state, teacher.last_hidden_state
+
+
+class _FusedKL(torch.autograd.Function):
+    """LM head + KL with the kernel's per-offset statistics; gradient computed in the forward."""
+
+    @staticmethod
+    def forward(ctx, student, teacher, index, weight, chunk_size, row_weight, offsets, num_offsets):
+        total, kl_rows, agree, grad, kbo, abo = ops.lmhead_kl(
+            student, teacher, index, weight, row_weight, offsets, num_offsets,
+            need_grad=ctx.needs_input_grad[0], chunk_rows=max(int(chunk_size), 128))
+        ctx.save_for_backward(grad)
+        outs = [kl_rows, agree] + ([kbo, abo] if offsets is not None else [])
+        ctx.mark_non_differentiable(*outs)
+        if offsets is None:
+            return total, kl_rows, agree
+        return total, kl_rows, agree, kbo, abo
+
+    @staticmethod
+    def backward(ctx, grad_total, *unused):
+        (grad,) = ctx.saved_tensors
+        if grad is None:
+            return (None,) * 8
+        return ops.lmhead_kl_backward(grad, grad_total), None, None, None, None, None, None, None
+
+
+class FusedLinearForwardKL:
+    """sum_r w_r KL(softmax(W teacher[index[r]]) || softmax(W student[r])), per-row KL and top-1
+    agreement (orthrus/objective.py:338-392). Same apply() signature and outputs (total,
+    kl_rows, agree), differentiable w.r.t. the student rows; `compiled` is ignored."""
+
+    @staticmethod
+    def apply(student, teacher, index, weight, chunk_size, compiled=False, row_weight=None):
+        return _FusedKL.apply(student, teacher, index, weight, chunk_size, row_weight, None, 0)
+
+
+def orthrus_loss(model: OrthrusLM, input_ids: torch.Tensor, assistant_mask: torch.Tensor,
+                 anchors: torch.Tensor, valid: torch.Tensor, kl_chunk_size: int,
+                 compiled: bool = False, kernel_options: dict | None = None, gamma: float = 0.0):
+    """Mean (or position-weighted mean) forward KL over supervised block positions and its
+    statistics (orthrus/objective.py:395-453)."""
+    K = model.config.block_size
+    batch, seq_len = input_ids.shape
+    student, teacher = model_states(model, input_ids, anchors, compiled, kernel_options)
+    hidden = student.shape[-1]
+    student = student.view(batch, -1, K, hidden)[:, :, :-1]
+    keep = supervision_mask(assistant_mask, anchors, valid, K)
+    targets = anchors[:, :, None] + torch.arange(K - 1, device=anchors.device)
+    targets = targets + seq_len * torch.arange(batch, device=anchors.device)[:, None, None]
+    positions, index = torch.unique(targets[keep], return_inverse=True)
+    order = torch.argsort(index, stable=True)
+    offsets = torch.arange(K - 1, device=keep.device).expand_as(keep)[keep][order]
+    weights = position_weights(K, gamma, keep.device)
+    row_weight = weights[offsets] if weights is not None else None
+    total, kl_rows, agree, kl_by_offset, agree_by_offset = _FusedKL.apply(
+        student[keep][order],
+        teacher.flatten(0, 1)[positions].to(student.dtype),
+        index[order],
+        model.lm_head.weight,
+        kl_chunk_size,
+        row_weight,
+        offsets,
+        K - 1,
+    )
+    count = keep.sum()
+    norm = row_weight.sum() if row_weight is not None else count.float()
+    stats = {
+        "tokens": count.detach(),
+        "kl_sum": kl_rows.sum(),
+        "weighted_kl_sum": total.detach(),
+        "weight_sum": norm.detach(),
+        "agree": agree.sum(),
+        "kl_by_offset": kl_by_offset,
+        "agree_by_offset": agree_by_offset,
+        "tokens_by_offset": torch.bincount(offsets, minlength=K - 1),
+        "valid_anchors": valid.float().mean(),
+    }
+    return total / norm.clamp_min(1e-6), stats

@@ -3,9 +3,41 @@ pointers and the current stream, check the status. No computation happens in Pyt
 
 from __future__ import annotations
 
+from collections import defaultdict
+
 import torch
 
 from orthrus_training_b200 import _lib as L
+
+
+class KernelTimer:
+    """CUDA-event timing of individual entry points on the stream they launch on, with the
+    algorithmic work (FLOPs) of each launch. Enabled by assigning an instance to ``ops.TIMER``."""
+
+    def __init__(self):
+        self.records = defaultdict(list)
+
+    def begin(self):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    def end(self, name, e0, work):
+        e1 = torch.cuda.Event(enable_timing=True)
+        e1.record()
+        self.records[name].append((e0, e1, work))
+
+    def summary(self) -> dict:
+        torch.cuda.synchronize()
+        out = {}
+        for name, recs in self.records.items():
+            ms = sum(a.elapsed_time(b) for a, b, _ in recs)
+            work = sum(float(w) for _, _, w in recs)
+            out[name] = {"launches": len(recs), "ms": ms, "flops": work}
+        return out
+
+
+TIMER: KernelTimer | None = None
 
 
 def _require_cuda(*tensors):
@@ -89,11 +121,14 @@ def lmhead_kl(student, teacher, index, weight, row_weight=None, offsets=None, nu
         row_weight = row_weight.to(torch.float32).contiguous()
     nbytes = lib.orthrus_lmhead_kl_workspace_bytes(n, m, V, dp, chunk_rows, code)
     ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev)
+    t0 = TIMER.begin() if TIMER is not None else None
     L.check(lib.orthrus_lmhead_kl_fwd(
         L.ptr(student), n, L.ptr(teacher), m, L.ptr(index), L.ptr(weight), V, dp, L.ptr(row_weight),
         L.ptr(offsets), int(num_offsets), L.ptr(total), L.ptr(kl_rows), L.ptr(agree), L.ptr(grad),
         L.ptr(kbo), L.ptr(abo), chunk_rows, L.ptr(ws), ws.numel(), code, L.stream_of(dev)),
         "lmhead_kl_fwd")
+    if t0 is not None:  # student logits + unique teacher logits + grad GEMM
+        TIMER.end("lmhead_kl", t0, 2.0 * d * V * ((2 if need_grad else 1) * n + m))
     if grad is not None and pad:
         grad = grad[:, :d]
     return total, kl_rows, agree.bool(), grad, kbo, abo
@@ -196,12 +231,27 @@ def attention_fwd(q, k1, v1, k2=None, v2=None, *, mask: int, hd: int, scale: flo
     A = anchors.shape[1] if anchors is not None else 0
     if anchors is not None:
         anchors = anchors.to(torch.int64).contiguous()
+    t0 = TIMER.begin() if TIMER is not None else None
     L.check(L.lib().orthrus_attn_fwd(
         q.data_ptr(), k1.data_ptr(), v1.data_ptr(), s1h, s1b, L1, L.ptr(k2), L.ptr(v2), s2h, s2b,
         L2, B, Hq, Hkv, Tq, hd, D, float(scale), mask, L.ptr(anchors), A, block, L.ptr(offset),
         L.ptr(limit2), o.data_ptr(), L.ptr(lse), L.dtype_code(q.dtype), L.stream_of(q.device)),
         "attn_fwd")
+    if t0 is not None:
+        TIMER.end(f"attn_fwd_{'dual' if mask == 1 else 'causal' if mask == 0 else 'draft'}", t0,
+                  attention_flops(mask, B, Hq, Tq, hd, anchors, block, L1))
     return o, lse
+
+
+def attention_flops(mask, B, Hq, Tq, hd, anchors=None, block=0, L1=0):
+    """Algorithmic forward FLOPs: 4 hd per (query, visible key) per head (2 for QK^T, 2 for PV);
+    a device scalar for the dual mask (anchors stay on the device)."""
+    if mask == 0:
+        return 4.0 * hd * Hq * B * Tq * (Tq + 1) / 2
+    if mask == 1:
+        vis = anchors.clamp(max=L1).sum() * block + anchors.numel() * block * block
+        return 4.0 * hd * Hq * vis
+    return 0.0
 
 
 def attention_bwd(q, k1, v1, k2, v2, anchors, block, o, lse, dout, *, hd: int, scale: float):
@@ -219,12 +269,15 @@ def attention_bwd(q, k1, v1, k2, v2, anchors, block, o, lse, dout, *, hd: int, s
                      device=dev)
     anchors = anchors.to(torch.int64).contiguous()
     dout = dout.contiguous()
+    t0 = TIMER.begin() if TIMER is not None else None
     L.check(lib.orthrus_attn_bwd(
         q.data_ptr(), k1.data_ptr(), v1.data_ptr(), s1h, s1b, L1, k2.data_ptr(), v2.data_ptr(),
         s2h, s2b, L2, B, Hq, Hkv, Tq, hd, D, float(scale), anchors.data_ptr(), anchors.shape[1],
         block, o.data_ptr(), lse.data_ptr(), dout.data_ptr(), dq.data_ptr(), dk2.data_ptr(),
         dv2.data_ptr(), ws.data_ptr(), ws.numel(), L.dtype_code(q.dtype), L.stream_of(dev)),
         "attn_bwd")
+    if t0 is not None:  # QK^T recompute, dP and dQ: 1.5x the forward FLOPs
+        TIMER.end("attn_bwd_dual", t0, 1.5 * attention_flops(1, B, Hq, Tq, hd, anchors, block, L1))
     return dq, dk2, dv2
 
 

@@ -1,0 +1,149 @@
+"""One optimizer step of Orthrus training, data-parallel over the GPUs of one node.
+
+Reference: the step body of orthrus/train.py:336-375 (gradient accumulation over micro-batches,
+clip_grad_norm_(1.0), skip the update when the norm is not finite, AdamW on the twins, LambdaLR
+with linear warmup + cosine to min_lr_ratio, lr_scale :71-76) and anchor_rng (:79-82).
+
+Data parallelism (new; the reference trains on one GPU): one process per GPU, disjoint packed rows
+per rank, and one collective, an all-reduce (average) of the trainable diffusion-view gradients
+only. The gradients live in one flat buffer per decoder layer; a post-accumulate-grad hook launches
+that layer's all-reduce as soon as its six twin gradients of the last micro-batch are complete,
+so communication overlaps the backward of the layers below. The frozen weights never move. The
+gradient norm for clipping / skipping is computed after the all-reduce, so every rank takes the
+same decision.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import math
+
+import torch
+import torch.distributed as dist
+
+from orthrus_training_b200.objective import orthrus_loss, sample_anchors
+
+
+def lr_scale(step: int, warmup: int, total: int, min_ratio: float) -> float:
+    """Linear warmup then cosine decay to min_ratio (orthrus/train.py:71-76)."""
+    if warmup > 0 and step < warmup:
+        return (step + 1) / warmup
+    progress = min(1.0, max(0.0, (step - warmup) / max(1, total - warmup)))
+    return min_ratio + (1.0 - min_ratio) * 0.5 * (1.0 + math.cos(math.pi * progress))
+
+
+def anchor_rng(seed: int, *keys, device) -> torch.Generator:
+    """Generator keyed by (seed, epoch, micro-batch) (orthrus/train.py:79-82)."""
+    digest = hashlib.sha256(":".join(map(str, (seed, *keys))).encode()).digest()
+    return torch.Generator(device=device).manual_seed(int.from_bytes(digest[:8], "little") >> 1)
+
+
+class GradBuckets:
+    """Flat per-layer gradient buffers of the trainable parameters with all-reduce hooks."""
+
+    def __init__(self, model, params: list[torch.nn.Parameter], world: int, group=None):
+        self.world = world
+        self.group = group
+        by_layer: dict[int, list] = {}
+        names = {id(p): n for n, p in model.named_parameters()}
+        for p in params:
+            name = names[id(p)]
+            layer = int(name.split("layers.")[1].split(".")[0]) if "layers." in name else -1
+            by_layer.setdefault(layer, []).append(p)
+        self.buckets = []
+        for layer in sorted(by_layer, reverse=True):  # backward reaches the last layer first
+            ps = by_layer[layer]
+            numel = sum(p.numel() for p in ps)
+            flat = torch.zeros(numel, dtype=ps[0].dtype, device=ps[0].device)
+            off = 0
+            for p in ps:
+                p.grad = flat[off: off + p.numel()].view_as(p)
+                off += p.numel()
+            self.buckets.append({"params": ps, "flat": flat, "ready": 0, "handle": None})
+        self.armed = False
+        if world > 1:
+            for bucket in self.buckets:
+                for p in bucket["params"]:
+                    p.register_post_accumulate_grad_hook(self._hook(bucket))
+
+    def _hook(self, bucket):
+        def fn(param):
+            if not self.armed:
+                return
+            bucket["ready"] += 1
+            if bucket["ready"] == len(bucket["params"]):
+                bucket["handle"] = dist.all_reduce(bucket["flat"], op=dist.ReduceOp.AVG,
+                                                   group=self.group, async_op=True)
+        return fn
+
+    def arm(self, on: bool) -> None:
+        """Only the last micro-batch of a step all-reduces."""
+        self.armed = on and self.world > 1
+        for b in self.buckets:
+            b["ready"] = 0
+            b["handle"] = None
+
+    def wait(self) -> None:
+        for b in self.buckets:
+            if b["handle"] is not None:
+                b["handle"].wait()
+                b["handle"] = None
+        self.armed = False
+
+    def zero(self) -> None:
+        for b in self.buckets:
+            b["flat"].zero_()
+
+
+class Trainer:
+    """Optimizer state and the step of one rank."""
+
+    def __init__(self, model, *, lr=1e-4, betas=(0.9, 0.95), weight_decay=0.0, total_steps=1000,
+                 warmup_ratio=0.05, min_lr_ratio=0.1, max_grad_norm=1.0, num_anchors=32,
+                 kl_chunk_size=4096, gamma=0.0, seed=42, world=1, rank=0, group=None):
+        from orthrus_training_b200.modeling_orthrus import freeze_to_diffusion
+
+        self.model = model
+        self.params = freeze_to_diffusion(model)
+        self.buckets = GradBuckets(model, self.params, world, group)
+        fused = all(p.is_cuda for p in self.params)
+        self.optimizer = torch.optim.AdamW(self.params, lr=lr, betas=betas,
+                                           weight_decay=weight_decay, fused=fused)
+        warmup = int(total_steps * warmup_ratio)
+        self.scheduler = torch.optim.lr_scheduler.LambdaLR(
+            self.optimizer, lambda s: lr_scale(s, warmup, total_steps, min_lr_ratio))
+        self.max_grad_norm = max_grad_norm
+        self.num_anchors = num_anchors
+        self.kl_chunk_size = kl_chunk_size
+        self.gamma = gamma
+        self.seed = seed
+        self.world, self.rank = world, rank
+        self.step_index = 0
+        self.skipped = 0
+
+    def step(self, micro_batches: list[tuple[torch.Tensor, torch.Tensor]], epoch: int = 0) -> dict:
+        """One optimizer step over this rank's micro-batches [(input_ids, assistant_mask), ...]
+        (already on the device). Returns loss (device tensor), grad_norm, skipped."""
+        model = self.model
+        accum = len(micro_batches)
+        self.buckets.zero()
+        losses = []
+        for j, (ids, mask) in enumerate(micro_batches):
+            self.buckets.arm(j == accum - 1)
+            index = (self.step_index * accum + j) * self.world + self.rank  # global micro-batch
+            rng = anchor_rng(self.seed, epoch, index, device=ids.device)
+            anchors, valid = sample_anchors(mask, model.config.block_size, self.num_anchors, rng)
+            loss, stats = orthrus_loss(model, ids, mask, anchors, valid, self.kl_chunk_size,
+                                       gamma=self.gamma)
+            (loss / accum).backward()
+            losses.append(loss.detach())
+        self.buckets.wait()
+        grad_norm = torch.nn.utils.clip_grad_norm_(self.params, self.max_grad_norm)
+        finite = bool(torch.isfinite(grad_norm))
+        if finite:
+            self.optimizer.step()
+        else:
+            self.skipped += 1
+        self.scheduler.step()
+        self.step_index += 1
+        return {"loss": torch.stack(losses).mean(), "grad_norm": grad_norm, "skipped": not finite}
