@@ -148,6 +148,26 @@ int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h,
                      const void* do_, float* dq, float* dk2, float* dv2, void* workspace,
                      size_t workspace_bytes, int dtype, void* stream);
 
+/* The same backward for callers that must not allocate device memory at all: no workspace
+ * argument, and no cudaMalloc, cudaFree or allocating library call inside. It exists for hosts
+ * that cannot hand this library a workspace: a runtime that owns every device byte in its own pool
+ * (an embedding service behind cgo / JNI), or a hot loop where cudaMalloc's implicit device
+ * synchronisation is not acceptable. This entry point has no counterpart in the reference.
+ * Its scratch (one fp32 per query row per head) is a fixed array compiled into the library, held
+ * by every GPU that loads it until the process exits, so B * Hq * Tq must not exceed
+ * ORTHRUS_ATTN_BWD_NOALLOC_MAX_ROWS (262144 rows = 1 MiB); larger sizes return ORTHRUS_EINVAL.
+ * The first call on a device looks up the array's device address with that device current; make
+ * that first call before any stream capture. Every call reuses the same array and fully rewrites
+ * the part it reads, so nothing needs clearing, but calls that overlap on the GPU (two streams,
+ * two threads) race on it. Arguments and outputs as orthrus_attn_bwd. */
+#define ORTHRUS_ATTN_BWD_NOALLOC_MAX_ROWS 262144
+int orthrus_attn_bwd_noalloc(const void* q, const void* k1, const void* v1, int64_t s1h,
+                             int64_t s1b, int64_t L1, const void* k2, const void* v2, int64_t s2h,
+                             int64_t s2b, int64_t L2, int64_t B, int Hq, int Hkv, int64_t Tq,
+                             int hd, int D, float scale, const int64_t* anchors, int64_t A,
+                             int block, const void* o, const float* lse, const void* do_,
+                             float* dq, float* dk2, float* dv2, int dtype, void* stream);
+
 /* ---- fused LM head + log-softmax + KL(teacher || student) ------------------------------- */
 /* total = sum_r w_r KL(softmax(W t[index[r]]) || softmax(W s[r])), kl_rows[r], agree[r] (top-1
  * match, lowest index wins ties), and, when grad != NULL, grad[r] = w_r (p_s - p_t)[r] @ W

@@ -44,6 +44,10 @@ _SIGNATURES = {
     "orthrus_attn_bwd": (c_int, [_P, _P, _P, c_int64, c_int64, c_int64, _P, _P, c_int64, c_int64,
                                  c_int64, c_int64, c_int, c_int, c_int64, c_int, c_int, c_float, _P,
                                  c_int64, c_int, _P, _P, _P, _P, _P, _P, _P, c_size_t, c_int, _P]),
+    "orthrus_attn_bwd_noalloc": (c_int, [_P, _P, _P, c_int64, c_int64, c_int64, _P, _P, c_int64,
+                                         c_int64, c_int64, c_int64, c_int, c_int, c_int64, c_int,
+                                         c_int, c_float, _P, c_int64, c_int, _P, _P, _P, _P, _P, _P,
+                                         c_int, _P]),
     "orthrus_lmhead_kl_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int64,
                                                      c_int]),
     "orthrus_lmhead_kl_fwd": (c_int, [_P, c_int64, _P, c_int64, _P, _P, c_int64, c_int64, _P, _P,

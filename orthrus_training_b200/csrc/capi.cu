@@ -413,3 +413,57 @@ extern "C" int orthrus_rmsnorm(const void* x, const void* w, int64_t rows, int d
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
 }
+
+// ------------------------------------------------------------------------------------------------
+// Attention backward without any allocation
+// ------------------------------------------------------------------------------------------------
+//
+// For callers that cannot allocate device memory (see orthrus_attn_bwd_noalloc in the header):
+// the per-query scratch of the backward (delta = rowsum(dO * O), one fp32 per query row per head)
+// lives in a fixed array of this translation unit instead of a caller workspace.
+
+namespace {
+
+static __device__ __align__(256) float g_attn_bwd_noalloc_scratch[ORTHRUS_ATTN_BWD_NOALLOC_MAX_ROWS];
+
+constexpr int kMaxDevices = 64;
+
+// Device address of the scratch array on the current device. Host code only sees a host-side
+// stand-in under the array's name, so the address is looked up once per device (with that device
+// current) through cudaGetSymbolAddress and cached.
+void* noalloc_scratch_on_current_device() {
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_attn_bwd_noalloc_scratch) != cudaSuccess) return nullptr;
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+
+}  // namespace
+
+extern "C" int orthrus_attn_bwd_noalloc(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b,
+                                        int64_t L1, const void* k2, const void* v2, int64_t s2h, int64_t s2b,
+                                        int64_t L2, int64_t B, int Hq, int Hkv, int64_t Tq, int hd, int D,
+                                        float scale, const int64_t* anchors, int64_t A, int block, const void* o,
+                                        const float* lse, const void* do_, float* dq, float* dk2, float* dv2,
+                                        int dtype, void* stream) {
+  ORTHRUS_CHECK_ARG(B > 0 && Hq > 0 && Tq > 0);
+  if (B * static_cast<int64_t>(Hq) * Tq > ORTHRUS_ATTN_BWD_NOALLOC_MAX_ROWS) {
+    if (getenv("ORTHRUS_DEBUG"))
+      fprintf(stderr, "orthrus_attn_bwd_noalloc: B*Hq*Tq = %lld exceeds the %d rows of fixed scratch\n",
+              static_cast<long long>(B * static_cast<int64_t>(Hq) * Tq), ORTHRUS_ATTN_BWD_NOALLOC_MAX_ROWS);
+    return ORTHRUS_EINVAL;
+  }
+  void* scratch = noalloc_scratch_on_current_device();
+  if (scratch == nullptr) return ORTHRUS_ECUDA;
+  // every row of delta the kernels read is written first by the delta kernel: nothing to clear
+  return orthrus_attn_bwd(q, k1, v1, s1h, s1b, L1, k2, v2, s2h, s2b, L2, B, Hq, Hkv, Tq, hd, D, scale, anchors, A,
+                          block, o, lse, do_, dq, dk2, dv2, scratch, sizeof(g_attn_bwd_noalloc_scratch), dtype,
+                          stream);
+}

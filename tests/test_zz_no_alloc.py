@@ -1,0 +1,105 @@
+"""The attention backward entry point that allocates nothing (orthrus_attn_bwd_noalloc).
+
+Some hosts cannot give this library device memory: a runtime that keeps every device byte in its
+own pool, or a hot loop that must not pay cudaMalloc's device synchronisation. For them the
+backward takes its per-query scratch from a fixed array inside the library. This test calls it
+through the C ABI and checks it against orthrus_attn_bwd (which takes a caller workspace) on two
+calls in a row, so a second call that reuses the array's old contents is covered too. It lives in
+the last collected test file.
+"""
+
+import ctypes
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _case(dtype, hd, seed):
+    from orthrus_training_b200 import ops
+
+    B, Hq, Hkv, L, A, K = 2, 4, 2, 300, 8, 32
+    g = torch.Generator().manual_seed(seed)
+    Tq = A * K
+    q = torch.randn(B, Hq, Tq, hd, generator=g).to(DEV, dtype)
+    k1 = torch.randn(B, Hkv, L, hd, generator=g).to(DEV, dtype)
+    v1 = torch.randn(B, Hkv, L, hd, generator=g).to(DEV, dtype)
+    k2 = torch.randn(B, Hkv, Tq, hd, generator=g).to(DEV, dtype)
+    v2 = torch.randn(B, Hkv, Tq, hd, generator=g).to(DEV, dtype)
+    anchors = torch.stack([torch.randperm(L - K, generator=g)[:A].add(1).sort().values
+                           for _ in range(B)]).to(DEV)
+    scale = 1.0 / math.sqrt(hd)
+    o, lse = ops.attention_fwd(q, k1, v1, k2, v2, mask=1, hd=hd, scale=scale, anchors=anchors, block=K)
+    dout = torch.randn(B, Tq, Hq, hd, generator=g).to(DEV, dtype)
+    return dict(q=q, k1=k1, v1=v1, k2=k2, v2=v2, anchors=anchors, o=o, lse=lse, dout=dout,
+                B=B, Hq=Hq, Hkv=Hkv, Tq=Tq, L=L, A=A, K=K, hd=hd, scale=scale)
+
+
+def _outputs(c):
+    dq = torch.full((c["B"], c["Hq"], c["Tq"], c["hd"]), float("nan"), device=DEV)
+    dk = torch.full((c["B"], c["Hkv"], c["Tq"], c["hd"]), float("nan"), device=DEV)
+    dv = torch.full_like(dk, float("nan"))
+    return dq, dk, dv
+
+
+def _common_args(c):
+    q, k1, k2 = c["q"], c["k1"], c["k2"]
+    return [q.data_ptr(), k1.data_ptr(), c["v1"].data_ptr(), k1.stride(1), k1.stride(0), c["L"],
+            k2.data_ptr(), c["v2"].data_ptr(), k2.stride(1), k2.stride(0), c["Tq"], c["B"], c["Hq"],
+            c["Hkv"], c["Tq"], c["hd"], c["hd"], ctypes.c_float(c["scale"]), c["anchors"].data_ptr(),
+            c["A"], c["K"], c["o"].data_ptr(), c["lse"].data_ptr(), c["dout"].data_ptr()]
+
+
+def _with_workspace(c, code):
+    from orthrus_training_b200 import _lib
+
+    lib = _lib.lib()
+    dq, dk, dv = _outputs(c)
+    nbytes = lib.orthrus_attn_bwd_workspace_bytes(c["B"], c["Hq"], c["Tq"])
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+    st = lib.orthrus_attn_bwd(*_common_args(c), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                              ws.data_ptr(), nbytes, code, torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    return dq, dk, dv
+
+
+def _without_allocation(c, code):
+    from orthrus_training_b200 import _lib
+
+    dq, dk, dv = _outputs(c)
+    st = _lib.lib().orthrus_attn_bwd_noalloc(*_common_args(c), dq.data_ptr(), dk.data_ptr(),
+                                            dv.data_ptr(), code, torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    return dq, dk, dv
+
+
+@pytest.mark.parametrize("dtype,hd", [(torch.bfloat16, 128), (torch.float32, 32)])
+def test_noalloc_backward_matches_workspace_backward_twice(dtype, hd):
+    from orthrus_training_b200 import _lib
+
+    code = _lib.dtype_code(dtype)
+    tol = 3e-2 if dtype == torch.bfloat16 else 2e-5  # the attention tests' tolerances
+    for seed in (0, 1):  # two calls in a row; the second reuses the fixed scratch
+        c = _case(dtype, hd, seed)
+        ref = _with_workspace(c, code)
+        got = _without_allocation(c, code)
+        torch.cuda.synchronize()
+        for a, r in zip(got, ref):
+            assert torch.isfinite(a).all()
+            assert (a - r).abs().max().item() <= tol * max(1.0, r.abs().max().item())
+    assert _lib.device_error(0) == 0
+
+
+def test_noalloc_rejects_sizes_beyond_the_fixed_scratch():
+    from orthrus_training_b200 import _lib
+
+    c = _case(torch.bfloat16, 128, 2)
+    args = _common_args(c)
+    args[11] = 1 + 262144 // (c["Hq"] * c["Tq"])  # B large enough to exceed the scratch rows
+    dq, dk, dv = _outputs(c)
+    st = _lib.lib().orthrus_attn_bwd_noalloc(*args, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                                            _lib.BF16, torch.cuda.current_stream().cuda_stream)
+    assert st == _lib.EINVAL
