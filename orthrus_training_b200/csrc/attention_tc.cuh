@@ -785,3 +785,566 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 }  // namespace orthrus
+
+namespace orthrus {
+
+// ------------------------------------------------------------------------------------------------
+// Forward, two query heads per CTA (ping-pong)
+// ------------------------------------------------------------------------------------------------
+//
+// CTA = 128 query rows of the two query heads 2p, 2p+1 that share one KV head (GQA group size
+// even), 320 threads: warp 0 TMA, warp 1 MMA issue, warps 2-5 softmax of head 2p, warps 6-9
+// softmax of head 2p+1. Each K / V tile is loaded once for both heads. TMEM: S of head h in
+// columns [128h, 128h+128), the O accumulator of head h in [256+128h, ...). While one head's rows
+// run their softmax, the tensor core works on the other head's QK^T / PV.
+//
+// O is accumulated by the MMA itself in TMEM across key tiles. P is computed against a per-row
+// reference max m_ref that is only raised when a tile's max exceeds it by more than 2^8 (then the
+// row rescales its own O row in TMEM and its running sum); the final O / l uses the same reference,
+// so the result is exact while rescales stay rare.
+
+template <int D>
+struct Fwd2Smem {
+  static constexpr int BOXES = D / 64;
+  static constexpr int TILE = BOXES * kAttnTileBytes;  // [128][D]
+  static constexpr int OFF_Q = 0;                       // Q of head h at h * TILE
+  static constexpr int OFF_K = 2 * TILE;                // two K buffers
+  static constexpr int OFF_V = 4 * TILE;                // one V buffer
+  static constexpr int OFF_P = 5 * TILE;                // P of head h at OFF_P + h * 32 KB
+  static constexpr int OFF_BAR = OFF_P + 4 * kAttnTileBytes;
+  static constexpr int SMEM = OFF_BAR + 512 + 1024;
+};
+
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 256 between rescales
+
+template <int D>
+__global__ void __launch_bounds__(320, 1)
+    attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK1,
+                        const __grid_constant__ CUtensorMap tmV1, const __grid_constant__ CUtensorMap tmK2,
+                        const __grid_constant__ CUtensorMap tmV2, int Hq, int Hkv, int64_t Tq, int hd,
+                        float scale_log2, MaskParams mp, bool has2, __nv_bfloat16* __restrict__ o,
+                        float* __restrict__ lse) {
+  using S = Fwd2Smem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;
+  uint64_t* v_empty = bars + 6;
+  uint64_t* s_full = bars + 7;   // [2] per head
+  uint64_t* p_full = bars + 9;   // [2] per head (128 arrivals)
+  uint64_t* p_empty = bars + 11; // [2] per head: PV of the head completed
+  uint64_t* mma_done = bars + 13;
+  unsigned long long* red = reinterpret_cast<unsigned long long*>(bars + 16);
+  AttnTiles* tiles = reinterpret_cast<AttnTiles*>(bars + 20);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t q0 = static_cast<int64_t>(gridDim.x - 1 - blockIdx.x) * 128;  // heavy tiles first
+  const int pair = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int G = Hq / Hkv;
+  const int hk = (2 * pair) / G;
+  const int wg = warp >= 2 ? (warp - 2) / 4 : -1;  // softmax warpgroup = head of the pair
+  const int row = warp >= 2 ? (warp & 3) * 32 + lane : -1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&p_empty[i], 1);
+    }
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
+    mbar_init(mma_done, 1);
+    red[0] = 0;
+    red[1] = ~0ull;
+    red[2] = 0;
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  __syncthreads();
+  attn_tile_map(mp, b, q0, Tq, has2, wg == 0 ? row : -1, red, tiles);
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n1 = tiles->n1, t2a = tiles->t2a;
+  const int nt = n1 + tiles->n2;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(q_full, 2 * S::TILE);
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c = 0; c < S::BOXES; ++c)
+          tma_load_3d(smem + S::OFF_Q + h * S::TILE + c * kAttnTileBytes, &tmQ, q_full, c * 64,
+                      static_cast<int>(q0), static_cast<int>(b * Hq + 2 * pair + h));
+      int k_issued = 0, v_issued = 0;
+      for (int j = 0; j < nt; ++j) {
+        const bool src2 = j >= n1;
+        const int key0 = (src2 ? t2a + (j - n1) : j) * 128;
+        const int z = static_cast<int>(b * Hkv + hk);
+        if (*abort_flag || !mbar_wait(&k_empty[j & 1], ((j >> 1) & 1) ^ 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* kt = smem + S::OFF_K + (j & 1) * S::TILE;
+        mbar_arrive_expect_tx(&k_full[j & 1], S::TILE);
+#pragma unroll
+        for (int c = 0; c < S::BOXES; ++c)
+          tma_load_3d(kt + c * kAttnTileBytes, src2 ? &tmK2 : &tmK1, &k_full[j & 1], c * 64, key0, z);
+        k_issued = j + 1;
+        if (!mbar_wait(v_empty, (j & 1) ^ 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(v_full, S::TILE);
+#pragma unroll
+        for (int c = 0; c < S::BOXES; ++c)
+          tma_load_3d(smem + S::OFF_V + c * kAttnTileBytes, src2 ? &tmV2 : &tmV1, v_full, c * 64, key0, z);
+        v_issued = j + 1;
+      }
+      if (*abort_flag) {
+        mbar_wait_short(q_full, 0);
+        for (int j = max(0, k_issued - 2); j < k_issued; ++j) mbar_wait_short(&k_full[j & 1], (j >> 1) & 1);
+        if (v_issued > 0) mbar_wait_short(v_full, (v_issued - 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t idesc_o = umma_idesc_bf16(128, D, false, true);
+      bool ok = mbar_wait(q_full, 0) && (nt == 0 || mbar_wait(&k_full[0], 0));
+      auto issue_s = [&](int h, int j) {
+        const uint32_t q_base = smem_u32(smem + S::OFF_Q + h * S::TILE);
+        const uint32_t k_base = smem_u32(smem + S::OFF_K + (j & 1) * S::TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_f16(tmem + h * 128, desc_kmajor(q_base, kk), desc_kmajor(k_base, kk), idesc_s, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[h]);
+      };
+      if (ok && nt > 0) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; ok && j < nt; ++j) {
+        for (int h = 0; h < 2; ++h) {
+          if (*abort_flag || !mbar_wait(&p_full[h], j & 1) || (h == 0 && !mbar_wait(v_full, j & 1))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t p_base = smem_u32(smem + S::OFF_P + h * 2 * kAttnTileBytes);
+          const uint32_t v_base = smem_u32(smem + S::OFF_V);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tmem + 256 + h * 128, desc_kmajor(p_base, kk), desc_mnmajor(v_base, kk), idesc_o,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&p_empty[h]);
+          if (h == 1) umma_commit(v_empty);
+          if (j + 1 < nt) {
+            if (h == 0 && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(h, j + 1);
+            if (h == 1) umma_commit(&k_empty[(j + 1) & 1]);
+          }
+        }
+      }
+      if (!ok) *abort_flag = 1;
+      // drain on its own barrier: no MMA may still run when the CTA frees its TMEM
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0);
+    }
+  } else {
+    const int h = wg;
+    const int64_t t = q0 + row;
+    const bool live = t < Tq;
+    int64_t e1 = 0, s2 = 0, e2 = 0;
+    if (live) query_ranges(mp, b, t, e1, s2, e2);
+    if (!has2) e2 = s2 = 0;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t s_col = lane_base + h * 128;
+    const uint32_t o_col = lane_base + 256 + h * 128;
+    const uint32_t p_base = smem_u32(smem + S::OFF_P + h * 2 * kAttnTileBytes);
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      if (*abort_flag || !mbar_wait(&s_full[h], j & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[128];
+      tmem_ld32(s_col + 0, s);
+      tmem_ld32(s_col + 32, s + 32);
+      tmem_ld32(s_col + 64, s + 64);
+      tmem_ld32(s_col + 96, s + 96);
+      tmem_wait_ld();
+      const bool src2 = j >= n1;
+      const int64_t key0 = (src2 ? t2a + (j - n1) : j) * 128;
+      const int64_t lo = (src2 ? s2 : 0) - key0, hi = (src2 ? e2 : e1) - key0;  // visible columns
+      const bool full = lo <= 0 && hi >= 128;
+      float tmax = -INFINITY;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          s[i] *= scale_log2;
+          tmax = fmaxf(tmax, s[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          s[i] = (i >= lo && i < hi) ? s[i] * scale_log2 : -INFINITY;
+          tmax = fmaxf(tmax, s[i]);
+        }
+      }
+      // the previous P V of this head must be done before P and O are touched again
+      if (j > 0 && !mbar_wait(&p_empty[h], (j - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      if (tmax > m_ref + kRescaleThreshold) {
+        if (m_ref != -INFINITY) {
+          const float alpha = exp2f(m_ref - tmax);
+          l *= alpha;
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < D / 16; ++c) {
+            float x[16];
+            tmem_ld16(o_col + c * 16, x);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) x[i] *= alpha;
+            tmem_st16(o_col + c * 16, x);
+          }
+          tmem_wait_st();
+        }
+        m_ref = tmax;
+      }
+      const float mu = m_ref == -INFINITY ? 0.f : m_ref;
+      float rsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float* x = s + 32 * c;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          x[i] = exp2f(x[i] - mu);
+          rsum += x[i];
+        }
+        store_row32_sw128(p_base, row, c * 32, x);
+      }
+      l += rsum;
+      tc_fence_before();
+      fence_proxy_async_smem();
+      mbar_arrive(&p_full[h]);
+    }
+    if (!ok) *abort_flag = 1;
+    const bool done = ok && nt > 0 && mbar_wait(&p_empty[h], (nt - 1) & 1);
+    tc_fence_after();
+    float acc[D];
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) tmem_ld32(o_col + c * 32, acc + 32 * c);
+    tmem_wait_ld();
+    if (done && live) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int hh = 2 * pair + h;
+      __nv_bfloat16* orow = o + ((b * Tq + t) * Hq + hh) * hd;
+      if (hd == D) {
+#pragma unroll
+        for (int i = 0; i < D; i += 8) {
+          uint4 pk = make_uint4(pack_bf16x2(acc[i] * inv, acc[i + 1] * inv), pack_bf16x2(acc[i + 2] * inv, acc[i + 3] * inv),
+                                pack_bf16x2(acc[i + 4] * inv, acc[i + 5] * inv), pack_bf16x2(acc[i + 6] * inv, acc[i + 7] * inv));
+          *reinterpret_cast<uint4*>(orow + i) = pk;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < D; ++i)
+          if (i < hd) orow[i] = __float2bfloat16_rn(acc[i] * inv);
+      }
+      if (lse) lse[(b * Hq + hh) * Tq + t] = (m_ref + log2f(l)) * kLn2;
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_free(tmem, 512);
+  }
+}
+
+}  // namespace orthrus
+
+namespace orthrus {
+
+// ------------------------------------------------------------------------------------------------
+// Backward dQ, two query heads per CTA (ping-pong), 64-key tiles
+// ------------------------------------------------------------------------------------------------
+//
+// CTA = 128 query rows of the heads 2p, 2p+1 sharing one KV head; 320 threads (warp 0 TMA, warp 1
+// MMA, warps 2-5 / 6-9 the rows of head 2p / 2p+1). Key tiles of 64 so that both heads fit in TMEM:
+// head h owns S [64h .. +64), dP [128 + 64h .. +64) and its dQ accumulator [256 + 128h .. +128).
+// Per tile: S = Q K^T, dP = dO V^T (N = 64), then dS = P (dP - delta) (bf16, [128][64] swizzled
+// in shared memory) and dQ += dS K (K as the MN-major operand). While one head's rows compute dS,
+// the tensor core runs the other head's MMAs.
+
+constexpr int kKeyBox64 = 64 * 64 * 2;  // one [64 rows][64] bf16 box = 8 KB
+
+__device__ __forceinline__ uint64_t desc_kmajor_rows64(uint32_t base, int kk) {  // [64][D] tile
+  return umma_desc_sw128(base + (kk >> 2) * kKeyBox64 + (kk & 3) * 32, 16, 1024);
+}
+__device__ __forceinline__ uint64_t desc_mnmajor_rows64(uint32_t base, int kk) {  // [64 rows][D]
+  return umma_desc_sw128(base + kk * 2048, kKeyBox64, 1024);
+}
+
+template <int D>
+struct Dq2Smem {
+  static constexpr int BOXES = D / 64;
+  static constexpr int QT = BOXES * kAttnTileBytes;  // [128][D]
+  static constexpr int KT = BOXES * kKeyBox64;       // [64][D]
+  static constexpr int OFF_Q = 0;                    // Q of head h at h * QT
+  static constexpr int OFF_DO = 2 * QT;              // dO of head h
+  static constexpr int OFF_KV = 4 * QT;              // stage s: K at s * 2KT, V at s * 2KT + KT
+  static constexpr int OFF_DS = OFF_KV + 4 * KT;     // dS of head h: [128][64] = 16 KB
+  static constexpr int OFF_BAR = OFF_DS + 2 * kAttnTileBytes;
+  static constexpr int SMEM = OFF_BAR + 512 + 1024;
+};
+
+template <int D>
+__global__ void __launch_bounds__(320, 1)
+    attn_dq_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                       const __grid_constant__ CUtensorMap tmK1, const __grid_constant__ CUtensorMap tmV1,
+                       const __grid_constant__ CUtensorMap tmK2, const __grid_constant__ CUtensorMap tmV2, int Hq,
+                       int Hkv, int64_t Tq, int hd, float scale, MaskParams mp, bool has2,
+                       const float* __restrict__ lse, const float* __restrict__ delta, float* __restrict__ dq) {
+  using S = Dq2Smem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
+  uint64_t* in_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2] per head: S and dP ready
+  uint64_t* ds_full = bars + 7;   // [2] per head (128 arrivals)
+  uint64_t* ds_empty = bars + 9;  // [2] per head: dQ MMA consumed dS
+  uint64_t* mma_done = bars + 11;
+  unsigned long long* red = reinterpret_cast<unsigned long long*>(bars + 16);
+  AttnTiles* tiles = reinterpret_cast<AttnTiles*>(bars + 20);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t q0 = static_cast<int64_t>(gridDim.x - 1 - blockIdx.x) * 128;
+  const int pair = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int G = Hq / Hkv;
+  const int hk = (2 * pair) / G;
+  const int wg = warp >= 2 ? (warp - 2) / 4 : -1;
+  const int row = warp >= 2 ? (warp & 3) * 32 + lane : -1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(in_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&ds_full[i], 128);
+      mbar_init(&ds_empty[i], 1);
+    }
+    mbar_init(mma_done, 1);
+    red[0] = 0;
+    red[1] = ~0ull;
+    red[2] = 0;
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  __syncthreads();
+  attn_tile_map(mp, b, q0, Tq, has2, wg == 0 ? row : -1, red, tiles);
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // 64-key tiles: source 1 covers [0, 64 * n1b), source 2 [64 * t2b, 64 * (t2b + n2b))
+  const int n1b = static_cast<int>((red[0] + 63) / 64);
+  const int t2b = red[2] > red[1] ? static_cast<int>(red[1] / 64) : 0;
+  const int n2b = red[2] > red[1] ? static_cast<int>((red[2] + 63) / 64) - t2b : 0;
+  const int nt = n1b + n2b;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(in_full, 4 * S::QT);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int hh = 2 * pair + h;
+#pragma unroll
+        for (int c = 0; c < S::BOXES; ++c) {
+          tma_load_3d(smem + S::OFF_Q + h * S::QT + c * kAttnTileBytes, &tmQ, in_full, c * 64,
+                      static_cast<int>(q0), static_cast<int>(b * Hq + hh));
+          tma_load_3d(smem + S::OFF_DO + h * S::QT + c * kAttnTileBytes, &tmDO, in_full, c * 64 + hh * hd,
+                      static_cast<int>(q0), static_cast<int>(b));
+        }
+      }
+      int issued = 0;
+      for (int j = 0; j < nt; ++j) {
+        const int s = j & 1;
+        if (*abort_flag || !mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        const bool src2 = j >= n1b;
+        const int key0 = (src2 ? t2b + (j - n1b) : j) * 64;
+        uint8_t* kt = smem + S::OFF_KV + s * 2 * S::KT;
+        uint8_t* vt = kt + S::KT;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * S::KT);
+#pragma unroll
+        for (int c = 0; c < S::BOXES; ++c) {
+          tma_load_3d(kt + c * kKeyBox64, src2 ? &tmK2 : &tmK1, &kv_full[s], c * 64, key0,
+                      static_cast<int>(b * Hkv + hk));
+          tma_load_3d(vt + c * kKeyBox64, src2 ? &tmV2 : &tmV1, &kv_full[s], c * 64, key0,
+                      static_cast<int>(b * Hkv + hk));
+        }
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        mbar_wait_short(in_full, 0);
+        for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait_short(&kv_full[j & 1], (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(128, 64, false, false);
+      constexpr uint32_t idesc_q = umma_idesc_bf16(128, D, false, true);
+      auto issue_s = [&](int h, int j) {
+        const uint32_t q_base = smem_u32(smem + S::OFF_Q + h * S::QT);
+        const uint32_t do_base = smem_u32(smem + S::OFF_DO + h * S::QT);
+        const uint32_t k_base = smem_u32(smem + S::OFF_KV + (j & 1) * 2 * S::KT);
+        const uint32_t v_base = k_base + S::KT;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          umma_f16(tmem + h * 64, desc_kmajor(q_base, kk), desc_kmajor_rows64(k_base, kk), idesc_s,
+                   kk > 0 ? 1u : 0u);
+          umma_f16(tmem + 128 + h * 64, desc_kmajor(do_base, kk), desc_kmajor_rows64(v_base, kk), idesc_s,
+                   kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[h]);
+      };
+      bool ok = mbar_wait(in_full, 0) && (nt == 0 || mbar_wait(&kv_full[0], 0));
+      if (ok && nt > 0) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
+      for (int j = 0; ok && j < nt; ++j) {
+        for (int h = 0; h < 2; ++h) {
+          if (*abort_flag || !mbar_wait(&ds_full[h], j & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t ds_base = smem_u32(smem + S::OFF_DS + h * kAttnTileBytes);
+          const uint32_t k_base = smem_u32(smem + S::OFF_KV + (j & 1) * 2 * S::KT);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tmem + 256 + h * 128, desc_kmajor(ds_base, kk), desc_mnmajor_rows64(k_base, kk), idesc_q,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&ds_empty[h]);
+          if (h == 1) umma_commit(&kv_empty[j & 1]);
+          if (j + 1 < nt) {
+            if (h == 0 && !mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(h, j + 1);
+          }
+        }
+      }
+      if (!ok) *abort_flag = 1;
+      // drain on its own barrier: no MMA may still run when the CTA frees its TMEM
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0);
+    }
+  } else {
+    const int h = wg;
+    const int hh = 2 * pair + h;
+    const int64_t t = q0 + row;
+    const bool live = t < Tq;
+    int64_t e1 = 0, s2 = 0, e2 = 0;
+    if (live) query_ranges(mp, b, t, e1, s2, e2);
+    if (!has2) e2 = s2 = 0;
+    const int64_t qi = (b * Hq + hh) * Tq + (live ? t : 0);
+    const float L2e = live ? lse[qi] * kLog2e : 0.f;
+    const float dl = live ? delta[qi] : 0.f;
+    const float sl2 = scale * kLog2e;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t ds_base = smem_u32(smem + S::OFF_DS + h * kAttnTileBytes);
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      if (*abort_flag || !mbar_wait(&s_full[h], j & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float x[64], y[64];
+      tmem_ld32(lane_base + h * 64, x);
+      tmem_ld32(lane_base + h * 64 + 32, x + 32);
+      tmem_ld32(lane_base + 128 + h * 64, y);
+      tmem_ld32(lane_base + 128 + h * 64 + 32, y + 32);
+      tmem_wait_ld();
+      const bool src2 = j >= n1b;
+      const int64_t key0 = (src2 ? t2b + (j - n1b) : j) * 64;
+      const int64_t lo = (src2 ? s2 : 0) - key0, hi = (src2 ? e2 : e1) - key0;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float p = (i >= lo && i < hi) ? exp2f(fmaf(x[i], sl2, -L2e)) : 0.f;
+        x[i] = p * (y[i] - dl);
+      }
+      if (j > 0 && !mbar_wait(&ds_empty[h], (j - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      store_row32_sw128(ds_base, row, 0, x);
+      store_row32_sw128(ds_base, row, 32, x + 32);
+      tc_fence_before();
+      fence_proxy_async_smem();
+      mbar_arrive(&ds_full[h]);
+    }
+    if (!ok) *abort_flag = 1;
+    const bool done = ok && nt > 0 && mbar_wait(&ds_empty[h], (nt - 1) & 1);
+    tc_fence_after();
+    float* out = dq + qi * D;
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      float v[32];
+      tmem_ld32(lane_base + 256 + h * 128 + c * 32, v);
+      tmem_wait_ld();
+      if (live && done) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const int e = c * 32 + i;
+          float4 w4 = make_float4(v[i] * scale, v[i + 1] * scale, v[i + 2] * scale, v[i + 3] * scale);
+          if (e >= hd) w4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          *reinterpret_cast<float4*>(out + e) = w4;
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_free(tmem, 512);
+  }
+}
+
+}  // namespace orthrus

@@ -152,13 +152,13 @@ struct AttnMaps {
 
 bool make_attn_maps(AttnMaps& m, const void* q, const void* k1, const void* v1, int64_t s1h, int64_t L1,
                     const void* k2, const void* v2, int64_t s2h, int64_t L2, int64_t B, int Hq, int Hkv,
-                    int64_t Tq, int hd, int D, const void* dout) {
+                    int64_t Tq, int hd, int D, const void* dout, uint32_t key_box = 128) {
   bool ok = make_tmap_3d_bf16(&m.q, q, D, Tq, B * Hq, D, Tq * D, 64, 128) &&
-            make_tmap_3d_bf16(&m.k1, k1, D, L1, B * Hkv, D, s1h, 64, 128) &&
-            make_tmap_3d_bf16(&m.v1, v1, D, L1, B * Hkv, D, s1h, 64, 128);
+            make_tmap_3d_bf16(&m.k1, k1, D, L1, B * Hkv, D, s1h, 64, key_box) &&
+            make_tmap_3d_bf16(&m.v1, v1, D, L1, B * Hkv, D, s1h, 64, key_box);
   if (k2 != nullptr)
-    ok = ok && make_tmap_3d_bf16(&m.k2, k2, D, L2, B * Hkv, D, s2h, 64, 128) &&
-         make_tmap_3d_bf16(&m.v2, v2, D, L2, B * Hkv, D, s2h, 64, 128);
+    ok = ok && make_tmap_3d_bf16(&m.k2, k2, D, L2, B * Hkv, D, s2h, 64, key_box) &&
+         make_tmap_3d_bf16(&m.v2, v2, D, L2, B * Hkv, D, s2h, 64, key_box);
   else {
     m.k2 = m.k1;
     m.v2 = m.v1;
@@ -238,8 +238,22 @@ int orthrus_attn_fwd(const void* q, const void* k1, const void* v1, int64_t s1h,
     if (!make_attn_maps(m, q, k1, v1, s1h, L1, has2 ? k2 : nullptr, has2 ? v2 : nullptr, s2h, L2, B, Hq, Hkv, Tq,
                         hd, D, nullptr))
       return ORTHRUS_ECUDA;
-    dim3 grid(static_cast<unsigned>(ceil_div(Tq, 128)), Hq, static_cast<unsigned>(B));
     const float sl2 = scale * kLog2e;
+    if ((Hq / Hkv) % 2 == 0) {  // two query heads of one KV head per CTA
+      dim3 grid2(static_cast<unsigned>(ceil_div(Tq, 128)), Hq / 2, static_cast<unsigned>(B));
+      if (D == 128) {
+        if (set_smem(attn_fwd_tc2_kernel<128>, Fwd2Smem<128>::SMEM)) return ORTHRUS_ECUDA;
+        attn_fwd_tc2_kernel<128><<<grid2, 320, Fwd2Smem<128>::SMEM, st>>>(
+            m.q, m.k1, m.v1, m.k2, m.v2, Hq, Hkv, Tq, hd, sl2, mp, has2, static_cast<__nv_bfloat16*>(o), lse);
+      } else {
+        if (set_smem(attn_fwd_tc2_kernel<64>, Fwd2Smem<64>::SMEM)) return ORTHRUS_ECUDA;
+        attn_fwd_tc2_kernel<64><<<grid2, 320, Fwd2Smem<64>::SMEM, st>>>(
+            m.q, m.k1, m.v1, m.k2, m.v2, Hq, Hkv, Tq, hd, sl2, mp, has2, static_cast<__nv_bfloat16*>(o), lse);
+      }
+      ORTHRUS_CHECK_LAUNCH();
+      return ORTHRUS_OK;
+    }
+    dim3 grid(static_cast<unsigned>(ceil_div(Tq, 128)), Hq, static_cast<unsigned>(B));
     if (D == 128) {
       if (set_smem(attn_fwd_tc_kernel<128>, FwdSmem<128>::SMEM)) return ORTHRUS_ECUDA;
       attn_fwd_tc_kernel<128><<<grid, 192, FwdSmem<128>::SMEM, st>>>(m.q, m.k1, m.v1, m.k2, m.v2, Hq, Hkv, Tq, hd,
@@ -310,6 +324,32 @@ int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h,
     if (!make_attn_maps(m, q, k1, v1, s1h, L1, k2, v2, s2h, L2, B, Hq, Hkv, Tq, hd, D, do_)) return ORTHRUS_ECUDA;
     dim3 grid(static_cast<unsigned>(ceil_div(Tq, 128)), Hq, static_cast<unsigned>(B));
     dim3 grid_kv(static_cast<unsigned>(ceil_div(L2, 128)), Hkv, static_cast<unsigned>(B));
+    if ((Hq / Hkv) % 2 == 0) {  // dQ with two query heads per CTA and 64-key tiles
+      AttnMaps m64;
+      if (!make_attn_maps(m64, q, k1, v1, s1h, L1, k2, v2, s2h, L2, B, Hq, Hkv, Tq, hd, D, do_, 64))
+        return ORTHRUS_ECUDA;
+      dim3 grid2(static_cast<unsigned>(ceil_div(Tq, 128)), Hq / 2, static_cast<unsigned>(B));
+      if (D == 128) {
+        if (set_smem(attn_dq_tc2_kernel<128>, Dq2Smem<128>::SMEM)) return ORTHRUS_ECUDA;
+        attn_dq_tc2_kernel<128><<<grid2, 320, Dq2Smem<128>::SMEM, st>>>(
+            m64.q, m64.dout, m64.k1, m64.v1, m64.k2, m64.v2, Hq, Hkv, Tq, hd, scale, mp, true, lse, delta, dq);
+        ORTHRUS_CHECK_LAUNCH();
+        if (set_smem(attn_dkdv_tc_kernel<128>, DkvSmem<128>::SMEM)) return ORTHRUS_ECUDA;
+        attn_dkdv_tc_kernel<128><<<grid_kv, 192, DkvSmem<128>::SMEM, st>>>(m.q, m.dout, m.k2, m.v2, Hq, Hkv, Tq,
+                                                                             L2, hd, block, scale, lse, delta, dk2,
+                                                                             dv2);
+      } else {
+        if (set_smem(attn_dq_tc2_kernel<64>, Dq2Smem<64>::SMEM)) return ORTHRUS_ECUDA;
+        attn_dq_tc2_kernel<64><<<grid2, 320, Dq2Smem<64>::SMEM, st>>>(
+            m64.q, m64.dout, m64.k1, m64.v1, m64.k2, m64.v2, Hq, Hkv, Tq, hd, scale, mp, true, lse, delta, dq);
+        ORTHRUS_CHECK_LAUNCH();
+        if (set_smem(attn_dkdv_tc_kernel<64>, DkvSmem<64>::SMEM)) return ORTHRUS_ECUDA;
+        attn_dkdv_tc_kernel<64><<<grid_kv, 192, DkvSmem<64>::SMEM, st>>>(m.q, m.dout, m.k2, m.v2, Hq, Hkv, Tq, L2,
+                                                                           hd, block, scale, lse, delta, dk2, dv2);
+      }
+      ORTHRUS_CHECK_LAUNCH();
+      return ORTHRUS_OK;
+    }
     if (D == 128) {
       if (set_smem(attn_dq_tc_kernel<128>, DqSmem<128>::SMEM)) return ORTHRUS_ECUDA;
       attn_dq_tc_kernel<128><<<grid, 192, DqSmem<128>::SMEM, st>>>(m.q, m.dout, m.k1, m.v1, m.k2, m.v2, Hq, Hkv, Tq,
