@@ -79,9 +79,26 @@ int orthrus_gemm_simt(const void* A, int64_t lda, const void* B, int64_t ldb, vo
 
 /* RMSNorm of `rows` rows of length d: y = w * (x * rsqrt(mean(x^2) + eps)), the normalised value
  * rounded to dtype before the weight multiply (transformers Qwen3RMSNorm, orthrus/objective.py:128-133).
- * One warp per row, fixed reduction order. */
-int orthrus_rmsnorm(const void* x, const void* w, int64_t rows, int d, float eps, void* y, int dtype,
-                    void* stream);
+ * One warp per row, fixed reduction order. rstd [rows] fp32 receives rsqrt(mean(x^2) + eps) when
+ * not NULL (for the backward). */
+int orthrus_rmsnorm(const void* x, const void* w, int64_t rows, int d, float eps, void* y,
+                    float* rstd, int dtype, void* stream);
+
+/* Backward of orthrus_rmsnorm with respect to x (the norm weights of the model are frozen):
+ * dx = rstd * (w dy - xhat * mean(w dy xhat)), xhat = x * rstd, from the rstd [rows] fp32 the
+ * forward wrote.
+ * Replaces the autograd backward of _rms_norm (orthrus/objective.py:128-133). */
+int orthrus_rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy,
+                        int64_t rows, int d, void* dx, int dtype, void* stream);
+
+/* SwiGLU activation of the fused [gate | up] projection gate_up [rows, 2 * inter]:
+ * out [rows, inter] = silu(gate) * up (silu rounded to dtype first, as F.silu(gate) * up), and its
+ * backward dgate_up [rows, 2 * inter] from dout [rows, inter]. inter must be a multiple of 8 (bf16)
+ * / 4 (fp32). Replaces the activation of _mlp_residual (orthrus/objective.py:146-149). */
+int orthrus_swiglu_fwd(const void* gate_up, int64_t rows, int inter, void* out, int dtype,
+                       void* stream);
+int orthrus_swiglu_bwd(const void* gate_up, const void* dout, int64_t rows, int inter,
+                       void* dgate_up, int dtype, void* stream);
 
 /* ---- q/k RMSNorm + RoPE + head-major layout (fused prologue of the attention) ------------- */
 /* qkv: [rows = B*T, (Hq + 2*Hkv) * hd] token-major projection output (q | k | v columns).

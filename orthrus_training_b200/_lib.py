@@ -30,7 +30,10 @@ _SIGNATURES = {
     "orthrus_gemm_simt_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
     "orthrus_gemm_simt": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int64, c_int64, c_int64,
                                   c_int, _P, c_size_t, _P]),
-    "orthrus_rmsnorm": (c_int, [_P, _P, c_int64, c_int, c_float, _P, c_int, _P]),
+    "orthrus_rmsnorm": (c_int, [_P, _P, c_int64, c_int, c_float, _P, _P, c_int, _P]),
+    "orthrus_rmsnorm_bwd": (c_int, [_P, _P, _P, _P, c_int64, c_int, _P, c_int, _P]),
+    "orthrus_swiglu_fwd": (c_int, [_P, c_int64, c_int, _P, c_int, _P]),
+    "orthrus_swiglu_bwd": (c_int, [_P, _P, c_int64, c_int, _P, c_int, _P]),
     "orthrus_qkv_prep_fwd": (c_int, [_P, _P, _P, _P, _P, c_int64, c_int64, c_int, c_int, c_int, c_int,
                                      c_float, _P, _P, _P, c_int64, _P, _P, c_int, _P]),
     "orthrus_qkv_prep_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int]),

@@ -13,6 +13,7 @@
 #include "gemm_tc.cuh"
 #include "lmhead_kl.cuh"
 #include "qkv_prep.cuh"
+#include "rowwise.cuh"
 
 using namespace orthrus;
 
@@ -435,19 +436,101 @@ int orthrus_decode_verify_accept(const float* logits, int64_t B, int K, int64_t 
 
 }  // extern "C"
 
-extern "C" int orthrus_rmsnorm(const void* x, const void* w, int64_t rows, int d, float eps, void* y, int dtype,
-                               void* stream) {
+extern "C" int orthrus_rmsnorm(const void* x, const void* w, int64_t rows, int d, float eps, void* y, float* rstd,
+                               int dtype, void* stream) {
   ORTHRUS_CHECK_ARG(x && w && y && rows >= 0 && d > 0);
   if (rows == 0) return ORTHRUS_OK;
   const unsigned blocks = static_cast<unsigned>(ceil_div(rows, 8));
+  const bool vec = aligned16(x) && aligned16(w) && aligned16(y) && d % (dtype == ORTHRUS_BF16 ? 256 : 128) == 0;
+  if (dtype == ORTHRUS_BF16) {
+    using T = __nv_bfloat16;
+    if (vec)
+      rmsnorm_fwd_vec_kernel<T><<<blocks, 256, 0, as_stream(stream)>>>(
+          static_cast<const T*>(x), static_cast<const T*>(w), rows, d, eps, static_cast<T*>(y), rstd);
+    else
+      rmsnorm_kernel<T><<<blocks, 256, 0, as_stream(stream)>>>(static_cast<const T*>(x), static_cast<const T*>(w), rows,
+                                                              d, eps, static_cast<T*>(y), rstd);
+  } else if (dtype == ORTHRUS_F32) {
+    if (vec)
+      rmsnorm_fwd_vec_kernel<float><<<blocks, 256, 0, as_stream(stream)>>>(
+          static_cast<const float*>(x), static_cast<const float*>(w), rows, d, eps, static_cast<float*>(y), rstd);
+    else
+      rmsnorm_kernel<float><<<blocks, 256, 0, as_stream(stream)>>>(static_cast<const float*>(x),
+                                                                 static_cast<const float*>(w), rows, d, eps,
+                                                                 static_cast<float*>(y), rstd);
+  } else {
+    return ORTHRUS_EINVAL;
+  }
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+extern "C" int orthrus_rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy, int64_t rows,
+                                   int d, void* dx, int dtype, void* stream) {
+  ORTHRUS_CHECK_ARG(x && w && rstd && dy && dx && rows >= 0 && d > 0);
+  if (rows == 0) return ORTHRUS_OK;
+  const unsigned blocks = static_cast<unsigned>(ceil_div(rows, 8));
+  const bool vec = aligned16(x) && aligned16(w) && aligned16(dy) && aligned16(dx) &&
+                   d % (dtype == ORTHRUS_BF16 ? 256 : 128) == 0;
+  if (dtype == ORTHRUS_BF16) {
+    using T = __nv_bfloat16;
+    if (vec)
+      rmsnorm_bwd_vec_kernel<T><<<blocks, 256, 0, as_stream(stream)>>>(
+          static_cast<const T*>(x), static_cast<const T*>(w), rstd, static_cast<const T*>(dy), rows, d,
+          static_cast<T*>(dx));
+    else
+      rmsnorm_bwd_kernel<T><<<blocks, 256, 0, as_stream(stream)>>>(
+          static_cast<const T*>(x), static_cast<const T*>(w), rstd, static_cast<const T*>(dy), rows, d,
+          static_cast<T*>(dx));
+  } else if (dtype == ORTHRUS_F32) {
+    if (vec)
+      rmsnorm_bwd_vec_kernel<float><<<blocks, 256, 0, as_stream(stream)>>>(
+          static_cast<const float*>(x), static_cast<const float*>(w), rstd, static_cast<const float*>(dy), rows, d,
+          static_cast<float*>(dx));
+    else
+      rmsnorm_bwd_kernel<float><<<blocks, 256, 0, as_stream(stream)>>>(
+          static_cast<const float*>(x), static_cast<const float*>(w), rstd, static_cast<const float*>(dy), rows, d,
+          static_cast<float*>(dx));
+  } else {
+    return ORTHRUS_EINVAL;
+  }
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+extern "C" int orthrus_swiglu_fwd(const void* gate_up, int64_t rows, int inter, void* out, int dtype, void* stream) {
+  ORTHRUS_CHECK_ARG(gate_up && out && rows >= 0 && inter > 0 && aligned16(gate_up) && aligned16(out));
+  ORTHRUS_CHECK_ARG(inter % (dtype == ORTHRUS_BF16 ? 8 : 4) == 0);
+  if (rows == 0) return ORTHRUS_OK;
+  const int64_t items = rows * inter / (dtype == ORTHRUS_BF16 ? 8 : 4);
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(ceil_div(items, 256), 148 * 16));
   if (dtype == ORTHRUS_BF16)
-    rmsnorm_kernel<__nv_bfloat16><<<blocks, 256, 0, as_stream(stream)>>>(
-        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), rows, d, eps,
-        static_cast<__nv_bfloat16*>(y));
+    swiglu_fwd_kernel<__nv_bfloat16><<<blocks, 256, 0, as_stream(stream)>>>(
+        static_cast<const __nv_bfloat16*>(gate_up), rows, inter, static_cast<__nv_bfloat16*>(out));
   else if (dtype == ORTHRUS_F32)
-    rmsnorm_kernel<float><<<blocks, 256, 0, as_stream(stream)>>>(static_cast<const float*>(x),
-                                                               static_cast<const float*>(w), rows, d, eps,
-                                                               static_cast<float*>(y));
+    swiglu_fwd_kernel<float><<<blocks, 256, 0, as_stream(stream)>>>(static_cast<const float*>(gate_up), rows, inter,
+                                                                     static_cast<float*>(out));
+  else
+    return ORTHRUS_EINVAL;
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+extern "C" int orthrus_swiglu_bwd(const void* gate_up, const void* dout, int64_t rows, int inter, void* dgate_up,
+                                  int dtype, void* stream) {
+  ORTHRUS_CHECK_ARG(gate_up && dout && dgate_up && rows >= 0 && inter > 0);
+  ORTHRUS_CHECK_ARG(aligned16(gate_up) && aligned16(dout) && aligned16(dgate_up));
+  ORTHRUS_CHECK_ARG(inter % (dtype == ORTHRUS_BF16 ? 8 : 4) == 0);
+  if (rows == 0) return ORTHRUS_OK;
+  const int64_t items = rows * inter / (dtype == ORTHRUS_BF16 ? 8 : 4);
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(ceil_div(items, 256), 148 * 16));
+  if (dtype == ORTHRUS_BF16)
+    swiglu_bwd_kernel<__nv_bfloat16><<<blocks, 256, 0, as_stream(stream)>>>(
+        static_cast<const __nv_bfloat16*>(gate_up), static_cast<const __nv_bfloat16*>(dout), rows, inter,
+        static_cast<__nv_bfloat16*>(dgate_up));
+  else if (dtype == ORTHRUS_F32)
+    swiglu_bwd_kernel<float><<<blocks, 256, 0, as_stream(stream)>>>(
+        static_cast<const float*>(gate_up), static_cast<const float*>(dout), rows, inter, static_cast<float*>(dgate_up));
   else
     return ORTHRUS_EINVAL;
   ORTHRUS_CHECK_LAUNCH();

@@ -207,7 +207,8 @@ __global__ void sum_partials_kernel(const float* __restrict__ part, int nparts, 
 // of rows (transformers Qwen3RMSNorm; orthrus/objective.py:128-133).
 template <typename T>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, int64_t rows,
-                                                      int d, float eps, T* __restrict__ y) {
+                                                      int d, float eps, T* __restrict__ y,
+                                                      float* __restrict__ rstd_out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + warp;
   if (r >= rows) return;
@@ -222,9 +223,176 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, c
   const float rstd = rsqrtf(ss / static_cast<float>(d) + eps);
   T* yr = y + r * d;
   for (int e = lane; e < d; e += 32) yr[e] = from_f32<T>(to_f32<T>(w[e]) * round_to<T>(to_f32<T>(xr[e]) * rstd));
+  if (rstd_out != nullptr && lane == 0) rstd_out[r] = rstd;
 }
 
 constexpr int kPrepBwdBlocks = 592;  // fixed grid (4 x 148): a deterministic split of the items
+
+// ------------------------------------------------------------------------------------------------
+// Row-parallel prologue for head dims 32 / 64 / 128: one CTA per token row computes the row's
+// RoPE cos / sin table once in shared memory (they depend on the position only, not on the head),
+// then eight warps handle the row's heads. A lane owns HD/32 contiguous elements of a head; the
+// RoPE partner of element e (e +- HD/2) belongs to lane ^ 16 at the same slot.
+// ------------------------------------------------------------------------------------------------
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(256) qkv_prep_fwd_row_kernel(
+    const T* __restrict__ qkv, const int64_t* __restrict__ positions, const float* __restrict__ inv_freq,
+    const T* __restrict__ q_norm_w, const T* __restrict__ k_norm_w, int64_t Tn, int Hq, int Hkv, int D, float eps,
+    T* __restrict__ q_out, T* __restrict__ k_out, T* __restrict__ v_out, int64_t cap,
+    const int32_t* __restrict__ offset, float* __restrict__ rstd_out) {
+  constexpr int NE = HD / 32;
+  constexpr int HALF = HD / 2;
+  __shared__ float cs[HALF], sn[HALF];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = blockIdx.x;
+  const int64_t b = row / Tn, t = row % Tn;
+  const float pos = static_cast<float>(positions[row]);
+  for (int i = threadIdx.x; i < HALF; i += blockDim.x) {
+    float s, c;
+    sincosf(pos * inv_freq[i], &s, &c);
+    cs[i] = round_to<T>(c);
+    sn[i] = round_to<T>(s);
+  }
+  __syncthreads();
+  const int heads = Hq + 2 * Hkv;
+  const T* xrow = qkv + row * static_cast<int64_t>(heads) * HD;
+  const int64_t orow_kv = (offset ? offset[b] : 0) + t;
+  for (int head = warp; head < heads; head += 8) {
+    const T* x = xrow + head * HD;
+    float v[NE];
+#pragma unroll
+    for (int k = 0; k < NE; ++k) v[k] = to_f32<T>(x[lane * NE + k]);
+    T* dst;
+    if (head >= Hq + Hkv) {
+      dst = v_out + ((b * Hkv + (head - Hq - Hkv)) * cap + orow_kv) * D;
+    } else {
+      const bool is_q = head < Hq;
+      const T* w = is_q ? q_norm_w : k_norm_w;
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < NE; ++k) ss = fmaf(v[k], v[k], ss);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      const float rstd = rsqrtf(ss / static_cast<float>(HD) + eps);
+#pragma unroll
+      for (int k = 0; k < NE; ++k) v[k] = round_to<T>(to_f32<T>(w[lane * NE + k]) * round_to<T>(v[k] * rstd));
+#pragma unroll
+      for (int k = 0; k < NE; ++k) {
+        const float partner = __shfl_xor_sync(0xffffffffu, v[k], 16);
+        const int e = lane * NE + k;
+        const int i = e < HALF ? e : e - HALF;
+        const float rot = e < HALF ? -partner : partner;
+        v[k] = v[k] * cs[i] + rot * sn[i];
+      }
+      if (rstd_out != nullptr && lane == 0) rstd_out[row * (Hq + Hkv) + head] = rstd;
+      dst = is_q ? q_out + ((b * Hq + head) * Tn + t) * D
+                 : k_out + ((b * Hkv + (head - Hq)) * cap + orow_kv) * D;
+    }
+#pragma unroll
+    for (int k = 0; k < NE; ++k) dst[lane * NE + k] = from_f32<T>(v[k]);
+    for (int e = HD + lane; e < D; e += 32) dst[e] = from_f32<T>(0.f);
+  }
+}
+
+// Backward of the row prologue (training layout: offset 0, cap = T). Fixed grid of kPrepBwdBlocks
+// CTAs, rows strided over the CTAs, heads over the warps in a fixed order, so the norm-weight
+// gradient partials part_q / part_k [block][HD] are deterministic.
+template <typename T, int HD>
+__global__ void __launch_bounds__(256) qkv_prep_bwd_row_kernel(
+    const T* __restrict__ qkv, const int64_t* __restrict__ positions, const float* __restrict__ inv_freq,
+    const T* __restrict__ q_norm_w, const T* __restrict__ k_norm_w, const float* __restrict__ rstd,
+    const float* __restrict__ dq, const float* __restrict__ dk, const float* __restrict__ dv, int64_t rows,
+    int64_t Tn, int Hq, int Hkv, int D, T* __restrict__ dqkv, float* __restrict__ part_q,
+    float* __restrict__ part_k) {
+  constexpr int NE = HD / 32;
+  constexpr int HALF = HD / 2;
+  __shared__ float cs[HALF], sn[HALF];
+  __shared__ float wpart[2][8][HD];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int heads = Hq + 2 * Hkv;
+  float wq[NE], wk[NE];
+#pragma unroll
+  for (int k = 0; k < NE; ++k) wq[k] = wk[k] = 0.f;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int64_t b = row / Tn, t = row % Tn;
+    const float pos = static_cast<float>(positions[row]);
+    __syncthreads();  // the previous row's table is no longer read
+    for (int i = threadIdx.x; i < HALF; i += blockDim.x) {
+      float s, c;
+      sincosf(pos * inv_freq[i], &s, &c);
+      cs[i] = round_to<T>(c);
+      sn[i] = round_to<T>(s);
+    }
+    __syncthreads();
+    for (int head = warp; head < heads; head += 8) {
+      T* out = dqkv + row * static_cast<int64_t>(heads) * HD + head * HD;
+      if (head >= Hq + Hkv) {
+        const int h = head - Hq - Hkv;
+        const float* g = dv ? dv + ((b * Hkv + h) * Tn + t) * D : nullptr;
+#pragma unroll
+        for (int k = 0; k < NE; ++k) out[lane * NE + k] = from_f32<T>(g ? g[lane * NE + k] : 0.f);
+        continue;
+      }
+      const bool is_q = head < Hq;
+      const int h = is_q ? head : head - Hq;
+      const float* gsrc = is_q ? dq : dk;
+      if (gsrc == nullptr) {
+#pragma unroll
+        for (int k = 0; k < NE; ++k) out[lane * NE + k] = from_f32<T>(0.f);
+        continue;
+      }
+      const float* g = gsrc + ((b * (is_q ? Hq : Hkv) + h) * Tn + t) * D;
+      const T* x = qkv + row * static_cast<int64_t>(heads) * HD + head * HD;
+      const T* w = is_q ? q_norm_w : k_norm_w;
+      const float r = rstd[row * (Hq + Hkv) + head];
+      float gv[NE], xh[NE], gr[NE];
+#pragma unroll
+      for (int k = 0; k < NE; ++k) {
+        gv[k] = g[lane * NE + k];
+        xh[k] = to_f32<T>(x[lane * NE + k]) * r;
+      }
+      float dot = 0.f;
+#pragma unroll
+      for (int k = 0; k < NE; ++k) {
+        const float partner = __shfl_xor_sync(0xffffffffu, gv[k], 16);
+        const int e = lane * NE + k;
+        const int i = e < HALF ? e : e - HALF;
+        const float other = e < HALF ? partner : -partner;
+        gr[k] = gv[k] * cs[i] + other * sn[i];
+        dot = fmaf(gr[k] * to_f32<T>(w[e]), xh[k], dot);
+        if (is_q)
+          wq[k] = fmaf(gr[k], xh[k], wq[k]);
+        else
+          wk[k] = fmaf(gr[k], xh[k], wk[k]);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+      const float mean = dot / static_cast<float>(HD);
+#pragma unroll
+      for (int k = 0; k < NE; ++k) {
+        const int e = lane * NE + k;
+        out[e] = from_f32<T>(r * (gr[k] * to_f32<T>(w[e]) - xh[k] * mean));
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NE; ++k) {
+    wpart[0][warp][lane * NE + k] = wq[k];
+    wpart[1][warp][lane * NE + k] = wk[k];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < HD; e += blockDim.x) {
+    float aq = 0.f, ak = 0.f;
+    for (int w = 0; w < 8; ++w) {
+      aq += wpart[0][w][e];
+      ak += wpart[1][w][e];
+    }
+    part_q[static_cast<int64_t>(blockIdx.x) * HD + e] = aq;
+    part_k[static_cast<int64_t>(blockIdx.x) * HD + e] = ak;
+  }
+}
+
 
 template <typename T>
 int qkv_prep_fwd_impl(const T* qkv, const int64_t* positions, const float* inv_freq, const T* qw, const T* kw,
@@ -233,6 +401,20 @@ int qkv_prep_fwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
   ORTHRUS_CHECK_ARG(qkv && positions && inv_freq && qw && kw && q_out && k_out && v_out);
   ORTHRUS_CHECK_ARG(B > 0 && Tn > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0);
   ORTHRUS_CHECK_ARG(hd >= 2 && hd % 2 == 0 && hd <= 128 && D >= hd && D <= 128 && cap >= Tn);
+  if (hd == 128 || hd == 64 || hd == 32) {
+    const unsigned rows = static_cast<unsigned>(B * Tn);
+    if (hd == 128)
+      qkv_prep_fwd_row_kernel<T, 128><<<rows, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, Tn, Hq, Hkv, D, eps,
+                                                               q_out, k_out, v_out, cap, offset, rstd);
+    else if (hd == 64)
+      qkv_prep_fwd_row_kernel<T, 64><<<rows, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, Tn, Hq, Hkv, D, eps,
+                                                              q_out, k_out, v_out, cap, offset, rstd);
+    else
+      qkv_prep_fwd_row_kernel<T, 32><<<rows, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, Tn, Hq, Hkv, D, eps,
+                                                              q_out, k_out, v_out, cap, offset, rstd);
+    ORTHRUS_CHECK_LAUNCH();
+    return ORTHRUS_OK;
+  }
   const int64_t items = B * Tn * (Hq + 2 * Hkv);
   qkv_prep_fwd_kernel<T><<<static_cast<unsigned>(ceil_div(items, 8)), 256, 0, stream>>>(
       qkv, positions, inv_freq, qw, kw, B, Tn, Hq, Hkv, hd, D, eps, q_out, k_out, v_out, cap, offset, rstd);
@@ -254,6 +436,23 @@ int qkv_prep_bwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
   float* part_k = part_q + static_cast<int64_t>(kPrepBwdBlocks) * hd;
   const int heads = Hq + 2 * Hkv;
   const int64_t rows = B * Tn;
+  if (hd == 128 || hd == 64 || hd == 32) {
+    if (hd == 128)
+      qkv_prep_bwd_row_kernel<T, 128><<<kPrepBwdBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rstd, dq, dk,
+                                                                          dv, rows, Tn, Hq, Hkv, D, dqkv, part_q, part_k);
+    else if (hd == 64)
+      qkv_prep_bwd_row_kernel<T, 64><<<kPrepBwdBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rstd, dq, dk,
+                                                                         dv, rows, Tn, Hq, Hkv, D, dqkv, part_q, part_k);
+    else
+      qkv_prep_bwd_row_kernel<T, 32><<<kPrepBwdBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rstd, dq, dk,
+                                                                         dv, rows, Tn, Hq, Hkv, D, dqkv, part_q, part_k);
+    ORTHRUS_CHECK_LAUNCH();
+    sum_partials_kernel<<<1, 128, 0, stream>>>(part_q, kPrepBwdBlocks, hd, dqw);
+    ORTHRUS_CHECK_LAUNCH();
+    sum_partials_kernel<<<1, 128, 0, stream>>>(part_k, kPrepBwdBlocks, hd, dkw);
+    ORTHRUS_CHECK_LAUNCH();
+    return ORTHRUS_OK;
+  }
   if (dq) {
     qkv_prep_bwd_kernel<T><<<kPrepBwdBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, qw, rstd, dq, B, Tn, Hq,
                                                                Hkv, hd, D, 0, dqkv, part_q);

@@ -77,12 +77,41 @@ def position_weights(block_size: int, gamma: float, device=None) -> torch.Tensor
     return torch.exp(-torch.arange(block_size - 1, device=device, dtype=torch.float32) / gamma)
 
 
+class _RMSNorm(torch.autograd.Function):
+    """Qwen3RMSNorm (orthrus/objective.py:128-133) on the row kernels: forward saves rstd, backward
+    returns dx only (the norm weights of the model are frozen)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        y, rstd = ops.rms_norm(x, weight, eps, want_rstd=True)
+        ctx.save_for_backward(x, weight, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight, rstd = ctx.saved_tensors
+        return ops.rms_norm_backward(x, weight, rstd, dy), None, None
+
+
+class _SwiGLU(torch.autograd.Function):
+    """silu(gate) * up of the fused [gate | up] projection (orthrus/objective.py:146-149)."""
+
+    @staticmethod
+    def forward(ctx, gate_up):
+        ctx.save_for_backward(gate_up)
+        return ops.silu_mul(gate_up)
+
+    @staticmethod
+    def backward(ctx, dout):
+        (gate_up,) = ctx.saved_tensors
+        return ops.silu_mul_backward(gate_up, dout)
+
+
 def _rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    """Qwen3RMSNorm with autograd (orthrus/objective.py:128-133), for the student path."""
-    dtype = x.dtype
-    xf = x.float()
-    xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
-    return weight * xf.to(dtype)
+    """Qwen3RMSNorm with autograd for the student path (frozen weight)."""
+    if weight.requires_grad:
+        raise ValueError("the RMSNorm weights of the dual-view model are frozen")
+    return _RMSNorm.apply(x, weight, eps)
 
 
 class DualViewAttention(torch.autograd.Function):
@@ -152,7 +181,7 @@ def _diffusion_layer(model, i, x, ar_k, ar_v, positions, anchors, inv, B, Q):
     x = x + F.linear(o, attn.o_proj_diff.weight)
     h = _rms_norm(x, layer.post_attention_layernorm.weight, eps)
     gu = F.linear(h, model._packed_mlp(i))
-    return x + F.linear(ops.silu_mul(gu), layer.mlp.down_proj.weight)
+    return x + F.linear(_SwiGLU.apply(gu), layer.mlp.down_proj.weight)
 
 
 def model_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tensor,

@@ -329,17 +329,33 @@ def decode_verify_accept(logits, verify_ids, ar_tokens, eos, max_len, start, anc
 # --- row-local elementwise pieces ---------------------------------------------------------------
 
 
-def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    """Qwen3RMSNorm over the last dim with a fixed per-row reduction order (no grad)."""
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, want_rstd: bool = False):
+    """Qwen3RMSNorm over the last dim with a fixed per-row reduction order (no autograd).
+    Returns y, or (y, rstd fp32 [rows]) with want_rstd."""
     _require_cuda(x, weight)
     shape = x.shape
     x2 = x.reshape(-1, shape[-1]).contiguous()
     y = torch.empty_like(x2)
     w = weight.to(x.dtype).contiguous()
+    rstd = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device) if want_rstd else None
     L.check(L.lib().orthrus_rmsnorm(x2.data_ptr(), w.data_ptr(), x2.shape[0], x2.shape[1],
-                                    float(eps), y.data_ptr(), L.dtype_code(x.dtype),
+                                    float(eps), y.data_ptr(), L.ptr(rstd), L.dtype_code(x.dtype),
                                     L.stream_of(x.device)), "rmsnorm")
-    return y.view(shape)
+    return (y.view(shape), rstd) if want_rstd else y.view(shape)
+
+
+def rms_norm_backward(x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor,
+                      dy: torch.Tensor) -> torch.Tensor:
+    """dx of rms_norm (the weight is frozen)."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1]).contiguous()
+    dy2 = dy.reshape(-1, shape[-1]).contiguous().to(x.dtype)
+    w = weight.to(x.dtype).contiguous()
+    dx = torch.empty_like(x2)
+    L.check(L.lib().orthrus_rmsnorm_bwd(x2.data_ptr(), w.data_ptr(), rstd.data_ptr(), dy2.data_ptr(),
+                                        x2.shape[0], x2.shape[1], dx.data_ptr(),
+                                        L.dtype_code(x.dtype), L.stream_of(x.device)), "rmsnorm_bwd")
+    return dx.view(shape)
 
 
 def add(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
@@ -348,6 +364,25 @@ def add(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
 
 
 def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
-    """SwiGLU activation of the fused [gate | up] projection: silu(gate) * up (tf Qwen3MLP)."""
-    half = gate_up.shape[-1] // 2
-    return torch.nn.functional.silu(gate_up[..., :half]) * gate_up[..., half:]
+    """SwiGLU activation of the fused [gate | up] projection output (orthrus_swiglu_fwd)."""
+    _require_cuda(gate_up)
+    shape = gate_up.shape
+    g2 = gate_up.reshape(-1, shape[-1]).contiguous()
+    inter = shape[-1] // 2
+    out = torch.empty(g2.shape[0], inter, dtype=gate_up.dtype, device=gate_up.device)
+    L.check(L.lib().orthrus_swiglu_fwd(g2.data_ptr(), g2.shape[0], inter, out.data_ptr(),
+                                       L.dtype_code(gate_up.dtype), L.stream_of(gate_up.device)),
+            "swiglu_fwd")
+    return out.view(*shape[:-1], inter)
+
+
+def silu_mul_backward(gate_up: torch.Tensor, dout: torch.Tensor) -> torch.Tensor:
+    shape = gate_up.shape
+    g2 = gate_up.reshape(-1, shape[-1]).contiguous()
+    inter = shape[-1] // 2
+    d2 = dout.reshape(-1, inter).contiguous().to(gate_up.dtype)
+    dgu = torch.empty_like(g2)
+    L.check(L.lib().orthrus_swiglu_bwd(g2.data_ptr(), d2.data_ptr(), g2.shape[0], inter,
+                                       dgu.data_ptr(), L.dtype_code(gate_up.dtype),
+                                       L.stream_of(gate_up.device)), "swiglu_bwd")
+    return dgu.view(shape)
