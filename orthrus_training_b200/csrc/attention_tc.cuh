@@ -46,6 +46,18 @@ __device__ __forceinline__ void store_row32_sw128(uint32_t tile_base, int r, int
                  pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
 }
 
+// How the columns [c0, c0 + width) of a score tile meet the visible ranges [lo, hi) of the 32 rows
+// of this warp: 0 = no row sees any of them, 1 = every row sees all of them, 2 = mixed. The answer
+// is the same in every lane, so a branch on it may hold warp-collective TMEM loads. All 32 lanes
+// must call it.
+__device__ __forceinline__ int chunk_kind_warp(int64_t lo, int64_t hi, int c0, int width) {
+  const bool none = hi <= c0 || lo >= c0 + width || hi <= lo;
+  const bool full = lo <= c0 && hi >= c0 + width;
+  if (__all_sync(0xffffffffu, none)) return 0;
+  if (__all_sync(0xffffffffu, full)) return 1;
+  return 2;
+}
+
 struct AttnTiles {
   int n1;        // source-1 tiles [0, n1)
   int t2a, n2;   // source-2 tiles [t2a, t2a + n2)
@@ -713,6 +725,9 @@ __global__ void __launch_bounds__(192, 1)
     const int64_t key = k0 + r;
     const bool live = key < L2;
     const int64_t kblk = key / block;
+    // the queries that see this key: its own block, [lo, hi) as columns of the tile
+    const int64_t lo = live ? kblk * block - k0 : 0;
+    const int64_t hi = live ? min((kblk + 1) * block, Tq) - k0 : 0;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const uint32_t p_base = smem_u32(smem + S::OFF_P), ds_base = smem_u32(smem + S::OFF_DS);
     const float sl2 = scale * kLog2e;
@@ -729,17 +744,22 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float x[32], y[32];
-        tmem_ld32(lane_base + c * 32, x);
-        tmem_ld32(lane_base + 128 + c * 32, y);
-        tmem_wait_ld();
+        const int kind = chunk_kind_warp(lo, hi, 32 * c, 32);  // warp-uniform
+        if (kind == 0) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int qc = c * 32 + i;
-          const int64_t tq = k0 + qc;
-          const bool vis = live && tq < Tq && (tq / block) == kblk;
-          const float p = vis ? exp2f(fmaf(x[i], sl2, -g_lse[qc])) : 0.f;
-          x[i] = p;
-          y[i] = p * (y[i] - g_delta[qc]);
+          for (int i = 0; i < 32; ++i) x[i] = y[i] = 0.f;
+        } else {
+          tmem_ld32(lane_base + c * 32, x);
+          tmem_ld32(lane_base + 128 + c * 32, y);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int qc = c * 32 + i;
+            const bool vis = kind == 1 || (qc >= lo && qc < hi);
+            const float p = vis ? exp2f(fmaf(x[i], sl2, -g_lse[qc])) : 0.f;
+            x[i] = p;
+            y[i] = p * (y[i] - g_delta[qc]);
+          }
         }
         store_row32_sw128(p_base, r, c * 32, x);
         store_row32_sw128(ds_base, r, c * 32, y);
@@ -808,8 +828,7 @@ struct Fwd2Smem {
   static constexpr int BOXES = D / 64;
   static constexpr int TILE = BOXES * kAttnTileBytes;  // [128][D]
   static constexpr int OFF_Q = 0;                       // Q of head h at h * TILE
-  static constexpr int OFF_K = 2 * TILE;                // two K buffers
-  static constexpr int OFF_V = 4 * TILE;                // one V buffer
+  static constexpr int OFF_RING = 2 * TILE;             // three slots: K(0), V(0), K(1), V(1), ...
   static constexpr int OFF_P = 5 * TILE;                // P of head h at OFF_P + h * 32 KB
   static constexpr int OFF_BAR = OFF_P + 4 * kAttnTileBytes;
   static constexpr int SMEM = OFF_BAR + 512 + 1024;
@@ -829,10 +848,8 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;
-  uint64_t* v_empty = bars + 6;
+  uint64_t* slot_full = bars + 1;   // [3] ring slot loaded
+  uint64_t* slot_empty = bars + 4;  // [3] ring slot consumed by the MMAs of both heads
   uint64_t* s_full = bars + 7;   // [2] per head
   uint64_t* p_full = bars + 9;   // [2] per head (128 arrivals)
   uint64_t* p_empty = bars + 11; // [2] per head: PV of the head completed
@@ -853,15 +870,15 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&slot_full[i], 1);
+      mbar_init(&slot_empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&p_empty[i], 1);
     }
-    mbar_init(v_full, 1);
-    mbar_init(v_empty, 1);
     mbar_init(mma_done, 1);
     red[0] = 0;
     red[1] = ~0ull;
@@ -886,45 +903,42 @@ __global__ void __launch_bounds__(320, 1)
         for (int c = 0; c < S::BOXES; ++c)
           tma_load_3d(smem + S::OFF_Q + h * S::TILE + c * kAttnTileBytes, &tmQ, q_full, c * 64,
                       static_cast<int>(q0), static_cast<int>(b * Hq + 2 * pair + h));
-      int k_issued = 0, v_issued = 0;
-      for (int j = 0; j < nt; ++j) {
+      // K and V tiles share a ring of three slots in the order K(0), V(0), K(1), V(1), ...: every
+      // load may start as soon as the tile two places ahead of it has been consumed
+      int issued = 0;
+      const int z = static_cast<int>(b * Hkv + hk);
+      for (int idx = 0; idx < 2 * nt; ++idx) {
+        const int j = idx >> 1, slot = idx % 3, use = idx / 3;
         const bool src2 = j >= n1;
         const int key0 = (src2 ? t2a + (j - n1) : j) * 128;
-        const int z = static_cast<int>(b * Hkv + hk);
-        if (*abort_flag || !mbar_wait(&k_empty[j & 1], ((j >> 1) & 1) ^ 1)) {
+        if (*abort_flag || !mbar_wait(&slot_empty[slot], (use & 1) ^ 1)) {
           *abort_flag = 1;
           break;
         }
-        uint8_t* kt = smem + S::OFF_K + (j & 1) * S::TILE;
-        mbar_arrive_expect_tx(&k_full[j & 1], S::TILE);
+        const CUtensorMap* map = (idx & 1) ? (src2 ? &tmV2 : &tmV1) : (src2 ? &tmK2 : &tmK1);
+        uint8_t* dst = smem + S::OFF_RING + slot * S::TILE;
+        mbar_arrive_expect_tx(&slot_full[slot], S::TILE);
 #pragma unroll
         for (int c = 0; c < S::BOXES; ++c)
-          tma_load_3d(kt + c * kAttnTileBytes, src2 ? &tmK2 : &tmK1, &k_full[j & 1], c * 64, key0, z);
-        k_issued = j + 1;
-        if (!mbar_wait(v_empty, (j & 1) ^ 1)) {
-          *abort_flag = 1;
-          break;
-        }
-        mbar_arrive_expect_tx(v_full, S::TILE);
-#pragma unroll
-        for (int c = 0; c < S::BOXES; ++c)
-          tma_load_3d(smem + S::OFF_V + c * kAttnTileBytes, src2 ? &tmV2 : &tmV1, v_full, c * 64, key0, z);
-        v_issued = j + 1;
+          tma_load_3d(dst + c * kAttnTileBytes, map, &slot_full[slot], c * 64, key0, z);
+        issued = idx + 1;
       }
       if (*abort_flag) {
         mbar_wait_short(q_full, 0);
-        for (int j = max(0, k_issued - 2); j < k_issued; ++j) mbar_wait_short(&k_full[j & 1], (j >> 1) & 1);
-        if (v_issued > 0) mbar_wait_short(v_full, (v_issued - 1) & 1);
+        for (int idx = max(0, issued - 3); idx < issued; ++idx) mbar_wait_short(&slot_full[idx % 3], (idx / 3) & 1);
       }
     }
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, false, false);
       constexpr uint32_t idesc_o = umma_idesc_bf16(128, D, false, true);
-      bool ok = mbar_wait(q_full, 0) && (nt == 0 || mbar_wait(&k_full[0], 0));
+      // ring position of K(j) is 2j, of V(j) 2j + 1: slot = position % 3, use = position / 3
+      auto ring = [&](int pos) { return smem_u32(smem + S::OFF_RING + (pos % 3) * S::TILE); };
+      auto ring_full = [&](int pos) { return mbar_wait(&slot_full[pos % 3], (pos / 3) & 1); };
+      bool ok = mbar_wait(q_full, 0) && (nt == 0 || ring_full(0));
       auto issue_s = [&](int h, int j) {
         const uint32_t q_base = smem_u32(smem + S::OFF_Q + h * S::TILE);
-        const uint32_t k_base = smem_u32(smem + S::OFF_K + (j & 1) * S::TILE);
+        const uint32_t k_base = ring(2 * j);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
           umma_f16(tmem + h * 128, desc_kmajor(q_base, kk), desc_kmajor(k_base, kk), idesc_s, kk > 0 ? 1u : 0u);
@@ -934,31 +948,31 @@ __global__ void __launch_bounds__(320, 1)
         tc_fence_after();
         issue_s(0, 0);
         issue_s(1, 0);
-        umma_commit(&k_empty[0]);
+        umma_commit(&slot_empty[0]);
       }
       for (int j = 0; ok && j < nt; ++j) {
         for (int h = 0; h < 2; ++h) {
-          if (*abort_flag || !mbar_wait(&p_full[h], j & 1) || (h == 0 && !mbar_wait(v_full, j & 1))) {
+          if (*abort_flag || !mbar_wait(&p_full[h], j & 1) || (h == 0 && !ring_full(2 * j + 1))) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t p_base = smem_u32(smem + S::OFF_P + h * 2 * kAttnTileBytes);
-          const uint32_t v_base = smem_u32(smem + S::OFF_V);
+          const uint32_t v_base = ring(2 * j + 1);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
             umma_f16(tmem + 256 + h * 128, desc_kmajor(p_base, kk), desc_mnmajor(v_base, kk), idesc_o,
                      (j > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&p_empty[h]);
-          if (h == 1) umma_commit(v_empty);
+          if (h == 1) umma_commit(&slot_empty[(2 * j + 1) % 3]);
           if (j + 1 < nt) {
-            if (h == 0 && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) {
+            if (h == 0 && !ring_full(2 * j + 2)) {
               ok = false;
               break;
             }
             tc_fence_after();
             issue_s(h, j + 1);
-            if (h == 1) umma_commit(&k_empty[(j + 1) & 1]);
+            if (h == 1) umma_commit(&slot_empty[(2 * j + 2) % 3]);
           }
         }
       }
@@ -996,56 +1010,59 @@ __global__ void __launch_bounds__(320, 1)
       const int64_t key0 = (src2 ? t2a + (j - n1) : j) * 128;
       const int64_t lo = (src2 ? s2 : 0) - key0, hi = (src2 ? e2 : e1) - key0;  // visible columns
       const bool full = lo <= 0 && hi >= 128;
-      float tmax = -INFINITY;
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
       if (full) {
 #pragma unroll
         for (int i = 0; i < 128; ++i) {
           s[i] *= scale_log2;
-          tmax = fmaxf(tmax, s[i]);
+          mx[i & 3] = fmaxf(mx[i & 3], s[i]);
         }
       } else {
 #pragma unroll
         for (int i = 0; i < 128; ++i) {
           s[i] = (i >= lo && i < hi) ? s[i] * scale_log2 : -INFINITY;
-          tmax = fmaxf(tmax, s[i]);
+          mx[i & 3] = fmaxf(mx[i & 3], s[i]);
         }
       }
+      const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       // the previous P V of this head must be done before P and O are touched again
       if (j > 0 && !mbar_wait(&p_empty[h], (j - 1) & 1)) {
         ok = false;
         break;
       }
+      // raise the reference max only when the tile max exceeds it by more than the threshold;
+      // O is rescaled after P is written, when the row of S no longer occupies registers
+      float alpha = 1.f;
       if (tmax > m_ref + kRescaleThreshold) {
-        if (m_ref != -INFINITY) {
-          const float alpha = exp2f(m_ref - tmax);
-          l *= alpha;
-          tc_fence_after();
-#pragma unroll 1
-          for (int c = 0; c < D / 16; ++c) {
-            float x[16];
-            tmem_ld16(o_col + c * 16, x);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) x[i] *= alpha;
-            tmem_st16(o_col + c * 16, x);
-          }
-          tmem_wait_st();
-        }
+        if (m_ref != -INFINITY) alpha = exp2f(m_ref - tmax);
         m_ref = tmax;
       }
       const float mu = m_ref == -INFINITY ? 0.f : m_ref;
-      float rsum = 0.f;
+      float sm[4] = {0.f, 0.f, 0.f, 0.f};  // independent chains
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float* x = s + 32 * c;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           x[i] = exp2f(x[i] - mu);
-          rsum += x[i];
+          sm[i & 3] += x[i];
         }
         store_row32_sw128(p_base, row, c * 32, x);
       }
-      l += rsum;
+      l = fmaf(l, alpha, (sm[0] + sm[1]) + (sm[2] + sm[3]));
+      if (alpha != 1.f) {
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < D / 16; ++c) {
+          float x[16];
+          tmem_ld16(o_col + c * 16, x);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) x[i] *= alpha;
+          tmem_st16(o_col + c * 16, x);
+        }
+        tmem_wait_st();
+      }
       tc_fence_before();
       fence_proxy_async_smem();
       mbar_arrive(&p_full[h]);
@@ -1295,19 +1312,34 @@ __global__ void __launch_bounds__(320, 1)
         break;
       }
       tc_fence_after();
-      float x[64], y[64];
-      tmem_ld32(lane_base + h * 64, x);
-      tmem_ld32(lane_base + h * 64 + 32, x + 32);
-      tmem_ld32(lane_base + 128 + h * 64, y);
-      tmem_ld32(lane_base + 128 + h * 64 + 32, y + 32);
-      tmem_wait_ld();
       const bool src2 = j >= n1b;
       const int64_t key0 = (src2 ? t2b + (j - n1b) : j) * 64;
       const int64_t lo = (src2 ? s2 : 0) - key0, hi = (src2 ? e2 : e1) - key0;
+      float x[64];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float p = (i >= lo && i < hi) ? exp2f(fmaf(x[i], sl2, -L2e)) : 0.f;
-        x[i] = p * (y[i] - dl);
+      for (int c = 0; c < 2; ++c) {
+        const int kind = chunk_kind_warp(lo, hi, 32 * c, 32);  // warp-uniform
+        float* xc = x + 32 * c;
+        if (kind == 0) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) xc[i] = 0.f;
+          continue;
+        }
+        float y[32];
+        tmem_ld32(lane_base + h * 64 + 32 * c, xc);
+        tmem_ld32(lane_base + 128 + h * 64 + 32 * c, y);
+        tmem_wait_ld();
+        if (kind == 1) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) xc[i] = exp2f(fmaf(xc[i], sl2, -L2e)) * (y[i] - dl);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = 32 * c + i;
+            const float p = (col >= lo && col < hi) ? exp2f(fmaf(xc[i], sl2, -L2e)) : 0.f;
+            xc[i] = p * (y[i] - dl);
+          }
+        }
       }
       if (j > 0 && !mbar_wait(&ds_empty[h], (j - 1) & 1)) {
         ok = false;

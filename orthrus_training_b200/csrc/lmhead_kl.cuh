@@ -153,23 +153,43 @@ __global__ void __launch_bounds__(192, 1)
         const int col0 = v0 + c * 32;
         const int nvalid = min(32, V - col0);
         if (nvalid <= 0) continue;
-        float cm = -INFINITY;
-        int ci = col0;
+        // chunk max and its first column: four independent chains (column j in chain j % 4, each
+        // keeping its first maximum), then merged preferring the lower column on ties
+        float cmv[4];
+        int civ[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          cmv[u] = -INFINITY;
+          civ[u] = 32;
+        }
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          if (j < nvalid && x[j] > cm) {
-            cm = x[j];
-            ci = col0 + j;
+          if (j < nvalid && x[j] > cmv[j & 3]) {
+            cmv[j & 3] = x[j];
+            civ[j & 3] = j;
           }
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+          if (cmv[u + 2] > cmv[u] || (cmv[u + 2] == cmv[u] && civ[u + 2] < civ[u])) {
+            cmv[u] = cmv[u + 2];
+            civ[u] = civ[u + 2];
+          }
+        if (cmv[1] > cmv[0] || (cmv[1] == cmv[0] && civ[1] < civ[0])) {
+          cmv[0] = cmv[1];
+          civ[0] = civ[1];
+        }
+        const float cm = cmv[0];
         if (cm > m) {
           s *= exp2f((m - cm) * kLog2e);
           m = cm;
-          idx = ci;
+          idx = col0 + civ[0];
         }
         const float ml = m * kLog2e;
+        float sv[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          if (j < nvalid) s += exp2f(fmaf(x[j], kLog2e, -ml));
+          if (j < nvalid) sv[j & 3] += exp2f(fmaf(x[j], kLog2e, -ml));
+        s += (sv[0] + sv[1]) + (sv[2] + sv[3]);
       }
       tc_fence_before();
       __syncwarp();
@@ -370,6 +390,7 @@ __global__ void __launch_bounds__(192, 1)
         const int col0 = v0 + c * 32;
         const int nvalid = min(32, V - col0);
         uint32_t packed[16];
+        float klv[4] = {0.f, 0.f, 0.f, 0.f};  // independent chains, summed at the end of the chunk
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
           float d2[2];
@@ -379,11 +400,12 @@ __global__ void __launch_bounds__(192, 1)
             const float bb = xt[j + u] - lt_off;  // log p_t
             const float ps = exp2f(a * kLog2e), pt = exp2f(bb * kLog2e);
             const bool ok = (j + u) < nvalid;
-            kl += ok ? pt * (bb - a) : 0.f;
+            klv[(j + u) & 3] += ok ? pt * (bb - a) : 0.f;
             d2[u] = ok ? w * (ps - pt) : 0.f;
           }
           packed[j / 2] = pack_bf16x2(d2[0], d2[1]);
         }
+        kl += (klv[0] + klv[1]) + (klv[2] + klv[3]);
         // chunk c covers bytes [c*64, c*64+64) of this row in a 256-byte row split over two
         // 128-byte-swizzled boxes of 64 columns each
         const uint32_t box = out_base + (c >> 1) * (128 * 128);

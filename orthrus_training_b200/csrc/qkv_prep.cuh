@@ -194,12 +194,17 @@ __global__ void zero_heads_kernel(int64_t rows, int heads, int hd, int head0, in
   }
 }
 
+// out[e] = sum over p of part[p][e]: one warp per element, lane l adds the partials l, l + 32, ...
+// in order, then a fixed butterfly (the result does not depend on timing). Grid ceil(hd / 8) x 256.
 __global__ void sum_partials_kernel(const float* __restrict__ part, int nparts, int hd, float* __restrict__ out) {
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  const int e = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
   if (e >= hd) return;
   float acc = 0.f;
-  for (int p = 0; p < nparts; ++p) acc += part[static_cast<int64_t>(p) * hd + e];
-  out[e] = acc;
+  for (int p = lane; p < nparts; p += 32) acc += part[static_cast<int64_t>(p) * hd + e];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) out[e] = acc;
 }
 
 // RMSNorm over rows of length d (the hidden size): y = w * round(x * rsqrt(mean(x^2) + eps)), one
@@ -235,6 +240,66 @@ constexpr int kPrepBwdBlocks = 592;  // fixed grid (4 x 148): a deterministic sp
 // RoPE partner of element e (e +- HD/2) belongs to lane ^ 16 at the same slot.
 // ------------------------------------------------------------------------------------------------
 
+// N consecutive elements as one vector access when N * sizeof(T) is 4, 8 or 16 bytes (the address
+// aligned to that size), element by element otherwise.
+template <typename T, int N>
+__device__ __forceinline__ void load_elems(const T* p, float* v) {
+  constexpr int BYTES = N * static_cast<int>(sizeof(T));
+  if constexpr (BYTES != 4 && BYTES != 8 && BYTES != 16) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = to_f32<T>(p[i]);
+  } else {
+    uint32_t w[BYTES / 4];
+    if constexpr (BYTES == 16) {
+      const uint4 r = *reinterpret_cast<const uint4*>(p);
+      w[0] = r.x; w[1] = r.y; w[2] = r.z; w[3] = r.w;
+    } else if constexpr (BYTES == 8) {
+      const uint2 r = *reinterpret_cast<const uint2*>(p);
+      w[0] = r.x; w[1] = r.y;
+    } else {
+      w[0] = *reinterpret_cast<const uint32_t*>(p);
+    }
+    if constexpr (sizeof(T) == 2) {
+#pragma unroll
+      for (int i = 0; i < N / 2; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; ++i) v[i] = __uint_as_float(w[i]);
+    }
+  }
+}
+
+template <typename T, int N>
+__device__ __forceinline__ void store_elems(T* p, const float* v) {
+  constexpr int BYTES = N * static_cast<int>(sizeof(T));
+  if constexpr (BYTES != 4 && BYTES != 8 && BYTES != 16) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) p[i] = from_f32<T>(v[i]);
+  } else {
+    uint32_t w[BYTES / 4];
+    if constexpr (sizeof(T) == 2) {
+#pragma unroll
+      for (int i = 0; i < N / 2; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; ++i) w[i] = __float_as_uint(v[i]);
+    }
+    if constexpr (BYTES == 16)
+      *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+    else if constexpr (BYTES == 8)
+      *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
+    else
+      *reinterpret_cast<uint32_t*>(p) = w[0];
+  }
+}
+
+// One CTA per token row, 8 warps; warp w owns the heads w, w + 8, w + 16, w + 24 of each group of
+// 32 and loads all of them before it computes, so four head rows per warp are in flight at once.
+// Lane l holds the elements [l * NE, l * NE + NE) of a head as one vector access.
+// Requires 16-byte aligned tensors and D % 8 == 0 (checked by the host).
 template <typename T, int HD>
 __global__ void __launch_bounds__(256) qkv_prep_fwd_row_kernel(
     const T* __restrict__ qkv, const int64_t* __restrict__ positions, const float* __restrict__ inv_freq,
@@ -243,55 +308,73 @@ __global__ void __launch_bounds__(256) qkv_prep_fwd_row_kernel(
     const int32_t* __restrict__ offset, float* __restrict__ rstd_out) {
   constexpr int NE = HD / 32;
   constexpr int HALF = HD / 2;
+  constexpr int PER_WARP = 4;
   __shared__ float cs[HALF], sn[HALF];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = blockIdx.x;
   const int64_t b = row / Tn, t = row % Tn;
-  const float pos = static_cast<float>(positions[row]);
-  for (int i = threadIdx.x; i < HALF; i += blockDim.x) {
-    float s, c;
-    sincosf(pos * inv_freq[i], &s, &c);
-    cs[i] = round_to<T>(c);
-    sn[i] = round_to<T>(s);
-  }
-  __syncthreads();
   const int heads = Hq + 2 * Hkv;
   const T* xrow = qkv + row * static_cast<int64_t>(heads) * HD;
+  // the loads of this warp's first heads go out before the RoPE table is built
+  float v[PER_WARP][NE];
+#pragma unroll
+  for (int j = 0; j < PER_WARP; ++j) {
+    const int head = warp + 8 * j;
+    if (head < heads) load_elems<T, NE>(xrow + head * HD + lane * NE, v[j]);
+  }
+  const float pos = static_cast<float>(positions[row]);
+  for (int i = threadIdx.x; i < HALF; i += blockDim.x) {
+    float sv, cv;
+    sincosf(pos * inv_freq[i], &sv, &cv);
+    cs[i] = round_to<T>(cv);
+    sn[i] = round_to<T>(sv);
+  }
+  float wq[NE], wk[NE];
+  load_elems<T, NE>(q_norm_w + lane * NE, wq);
+  load_elems<T, NE>(k_norm_w + lane * NE, wk);
+  __syncthreads();
   const int64_t orow_kv = (offset ? offset[b] : 0) + t;
-  for (int head = warp; head < heads; head += 8) {
-    const T* x = xrow + head * HD;
-    float v[NE];
+  for (int h0 = warp; h0 < heads; h0 += 8 * PER_WARP) {
+    if (h0 != warp) {
 #pragma unroll
-    for (int k = 0; k < NE; ++k) v[k] = to_f32<T>(x[lane * NE + k]);
-    T* dst;
-    if (head >= Hq + Hkv) {
-      dst = v_out + ((b * Hkv + (head - Hq - Hkv)) * cap + orow_kv) * D;
-    } else {
-      const bool is_q = head < Hq;
-      const T* w = is_q ? q_norm_w : k_norm_w;
-      float ss = 0.f;
-#pragma unroll
-      for (int k = 0; k < NE; ++k) ss = fmaf(v[k], v[k], ss);
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-      const float rstd = rsqrtf(ss / static_cast<float>(HD) + eps);
-#pragma unroll
-      for (int k = 0; k < NE; ++k) v[k] = round_to<T>(to_f32<T>(w[lane * NE + k]) * round_to<T>(v[k] * rstd));
-#pragma unroll
-      for (int k = 0; k < NE; ++k) {
-        const float partner = __shfl_xor_sync(0xffffffffu, v[k], 16);
-        const int e = lane * NE + k;
-        const int i = e < HALF ? e : e - HALF;
-        const float rot = e < HALF ? -partner : partner;
-        v[k] = v[k] * cs[i] + rot * sn[i];
+      for (int j = 0; j < PER_WARP; ++j) {
+        const int head = h0 + 8 * j;
+        if (head < heads) load_elems<T, NE>(xrow + head * HD + lane * NE, v[j]);
       }
-      if (rstd_out != nullptr && lane == 0) rstd_out[row * (Hq + Hkv) + head] = rstd;
-      dst = is_q ? q_out + ((b * Hq + head) * Tn + t) * D
-                 : k_out + ((b * Hkv + (head - Hq)) * cap + orow_kv) * D;
     }
 #pragma unroll
-    for (int k = 0; k < NE; ++k) dst[lane * NE + k] = from_f32<T>(v[k]);
-    for (int e = HD + lane; e < D; e += 32) dst[e] = from_f32<T>(0.f);
+    for (int j = 0; j < PER_WARP; ++j) {
+      const int head = h0 + 8 * j;  // warp-uniform
+      if (head >= heads) break;
+      float* x = v[j];
+      T* dst;
+      if (head >= Hq + Hkv) {
+        dst = v_out + ((b * Hkv + (head - Hq - Hkv)) * cap + orow_kv) * D;
+      } else {
+        const bool is_q = head < Hq;
+        float ss = 0.f;
+#pragma unroll
+        for (int k = 0; k < NE; ++k) ss = fmaf(x[k], x[k], ss);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        const float rstd = rsqrtf(ss / static_cast<float>(HD) + eps);
+#pragma unroll
+        for (int k = 0; k < NE; ++k) x[k] = round_to<T>((is_q ? wq[k] : wk[k]) * round_to<T>(x[k] * rstd));
+#pragma unroll
+        for (int k = 0; k < NE; ++k) {
+          const float partner = __shfl_xor_sync(0xffffffffu, x[k], 16);
+          const int e = lane * NE + k;
+          const int i = e < HALF ? e : e - HALF;
+          const float rot = e < HALF ? -partner : partner;
+          x[k] = x[k] * cs[i] + rot * sn[i];
+        }
+        if (rstd_out != nullptr && lane == 0) rstd_out[row * (Hq + Hkv) + head] = rstd;
+        dst = is_q ? q_out + ((b * Hq + head) * Tn + t) * D
+                   : k_out + ((b * Hkv + (head - Hq)) * cap + orow_kv) * D;
+      }
+      store_elems<T, NE>(dst + lane * NE, x);
+      for (int e = HD + lane; e < D; e += 32) dst[e] = from_f32<T>(0.f);
+    }
   }
 }
 
@@ -307,72 +390,84 @@ __global__ void __launch_bounds__(256) qkv_prep_bwd_row_kernel(
     float* __restrict__ part_k) {
   constexpr int NE = HD / 32;
   constexpr int HALF = HD / 2;
+  constexpr int PER_WARP = 4;  // head rows of one warp in flight at once
   __shared__ float cs[HALF], sn[HALF];
   __shared__ float wpart[2][8][HD];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int heads = Hq + 2 * Hkv;
-  float wq[NE], wk[NE];
+  float wq[NE], wk[NE], nq[NE], nk[NE];
 #pragma unroll
   for (int k = 0; k < NE; ++k) wq[k] = wk[k] = 0.f;
+  load_elems<T, NE>(q_norm_w + lane * NE, nq);
+  load_elems<T, NE>(k_norm_w + lane * NE, nk);
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const int64_t b = row / Tn, t = row % Tn;
     const float pos = static_cast<float>(positions[row]);
     __syncthreads();  // the previous row's table is no longer read
     for (int i = threadIdx.x; i < HALF; i += blockDim.x) {
-      float s, c;
-      sincosf(pos * inv_freq[i], &s, &c);
-      cs[i] = round_to<T>(c);
-      sn[i] = round_to<T>(s);
+      float sv, cv;
+      sincosf(pos * inv_freq[i], &sv, &cv);
+      cs[i] = round_to<T>(cv);
+      sn[i] = round_to<T>(sv);
     }
     __syncthreads();
-    for (int head = warp; head < heads; head += 8) {
-      T* out = dqkv + row * static_cast<int64_t>(heads) * HD + head * HD;
-      if (head >= Hq + Hkv) {
-        const int h = head - Hq - Hkv;
-        const float* g = dv ? dv + ((b * Hkv + h) * Tn + t) * D : nullptr;
+    for (int h0 = warp; h0 < heads; h0 += 8 * PER_WARP) {
+      // loads of up to PER_WARP heads first: the incoming gradient and, for q / k, the input row
+      float gv[PER_WARP][NE], xv[PER_WARP][NE], rr[PER_WARP];
 #pragma unroll
-        for (int k = 0; k < NE; ++k) out[lane * NE + k] = from_f32<T>(g ? g[lane * NE + k] : 0.f);
-        continue;
-      }
-      const bool is_q = head < Hq;
-      const int h = is_q ? head : head - Hq;
-      const float* gsrc = is_q ? dq : dk;
-      if (gsrc == nullptr) {
+      for (int j = 0; j < PER_WARP; ++j) {
+        const int head = h0 + 8 * j;
+        rr[j] = 0.f;
+        if (head >= heads) continue;
+        const bool is_v = head >= Hq + Hkv, is_q = head < Hq;
+        const int h = is_v ? head - Hq - Hkv : is_q ? head : head - Hq;
+        const float* gsrc = is_v ? dv : is_q ? dq : dk;
+        if (gsrc != nullptr) {
+          load_elems<float, NE>(gsrc + ((b * (is_q ? Hq : Hkv) + h) * Tn + t) * D + lane * NE, gv[j]);
+        } else {
 #pragma unroll
-        for (int k = 0; k < NE; ++k) out[lane * NE + k] = from_f32<T>(0.f);
-        continue;
-      }
-      const float* g = gsrc + ((b * (is_q ? Hq : Hkv) + h) * Tn + t) * D;
-      const T* x = qkv + row * static_cast<int64_t>(heads) * HD + head * HD;
-      const T* w = is_q ? q_norm_w : k_norm_w;
-      const float r = rstd[row * (Hq + Hkv) + head];
-      float gv[NE], xh[NE], gr[NE];
-#pragma unroll
-      for (int k = 0; k < NE; ++k) {
-        gv[k] = g[lane * NE + k];
-        xh[k] = to_f32<T>(x[lane * NE + k]) * r;
-      }
-      float dot = 0.f;
-#pragma unroll
-      for (int k = 0; k < NE; ++k) {
-        const float partner = __shfl_xor_sync(0xffffffffu, gv[k], 16);
-        const int e = lane * NE + k;
-        const int i = e < HALF ? e : e - HALF;
-        const float other = e < HALF ? partner : -partner;
-        gr[k] = gv[k] * cs[i] + other * sn[i];
-        dot = fmaf(gr[k] * to_f32<T>(w[e]), xh[k], dot);
-        if (is_q)
-          wq[k] = fmaf(gr[k], xh[k], wq[k]);
-        else
-          wk[k] = fmaf(gr[k], xh[k], wk[k]);
+          for (int k = 0; k < NE; ++k) gv[j][k] = 0.f;
+        }
+        if (!is_v && gsrc != nullptr) {
+          load_elems<T, NE>(qkv + row * static_cast<int64_t>(heads) * HD + head * HD + lane * NE, xv[j]);
+          rr[j] = rstd[row * (Hq + Hkv) + head];
+        }
       }
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-      const float mean = dot / static_cast<float>(HD);
+      for (int j = 0; j < PER_WARP; ++j) {
+        const int head = h0 + 8 * j;  // warp-uniform
+        if (head >= heads) break;
+        T* out = dqkv + row * static_cast<int64_t>(heads) * HD + head * HD + lane * NE;
+        const bool is_v = head >= Hq + Hkv, is_q = head < Hq;
+        const float* gsrc = is_v ? dv : is_q ? dq : dk;
+        if (is_v || gsrc == nullptr) {
+          store_elems<T, NE>(out, gv[j]);  // dV passes through; a missing gradient is zero
+          continue;
+        }
+        const float r = rr[j];
+        const float* w = is_q ? nq : nk;
+        float xh[NE], gr[NE], o[NE];
+        float dot = 0.f;
 #pragma unroll
-      for (int k = 0; k < NE; ++k) {
-        const int e = lane * NE + k;
-        out[e] = from_f32<T>(r * (gr[k] * to_f32<T>(w[e]) - xh[k] * mean));
+        for (int k = 0; k < NE; ++k) {
+          xh[k] = xv[j][k] * r;
+          const float partner = __shfl_xor_sync(0xffffffffu, gv[j][k], 16);
+          const int e = lane * NE + k;
+          const int i = e < HALF ? e : e - HALF;
+          const float other = e < HALF ? partner : -partner;
+          gr[k] = gv[j][k] * cs[i] + other * sn[i];
+          dot = fmaf(gr[k] * w[k], xh[k], dot);
+          if (is_q)
+            wq[k] = fmaf(gr[k], xh[k], wq[k]);
+          else
+            wk[k] = fmaf(gr[k], xh[k], wk[k]);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+        const float mean = dot / static_cast<float>(HD);
+#pragma unroll
+        for (int k = 0; k < NE; ++k) o[k] = r * (gr[k] * w[k] - xh[k] * mean);
+        store_elems<T, NE>(out, o);
       }
     }
   }
@@ -401,7 +496,10 @@ int qkv_prep_fwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
   ORTHRUS_CHECK_ARG(qkv && positions && inv_freq && qw && kw && q_out && k_out && v_out);
   ORTHRUS_CHECK_ARG(B > 0 && Tn > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0);
   ORTHRUS_CHECK_ARG(hd >= 2 && hd % 2 == 0 && hd <= 128 && D >= hd && D <= 128 && cap >= Tn);
-  if (hd == 128 || hd == 64 || hd == 32) {
+  // the row kernel makes vector accesses: 16-byte aligned tensors and rows of D % 8 == 0 elements
+  const bool vec_ok = D % 8 == 0 && aligned16(qkv) && aligned16(qw) && aligned16(kw) && aligned16(q_out) &&
+                      aligned16(k_out) && aligned16(v_out);
+  if (vec_ok && (hd == 128 || hd == 64 || hd == 32)) {
     const unsigned rows = static_cast<unsigned>(B * Tn);
     if (hd == 128)
       qkv_prep_fwd_row_kernel<T, 128><<<rows, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, Tn, Hq, Hkv, D, eps,
@@ -436,7 +534,9 @@ int qkv_prep_bwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
   float* part_k = part_q + static_cast<int64_t>(kPrepBwdBlocks) * hd;
   const int heads = Hq + 2 * Hkv;
   const int64_t rows = B * Tn;
-  if (hd == 128 || hd == 64 || hd == 32) {
+  const bool vec_ok = D % 8 == 0 && aligned16(qkv) && aligned16(qw) && aligned16(kw) && aligned16(dqkv) &&
+                      (!dq || aligned16(dq)) && (!dk || aligned16(dk)) && (!dv || aligned16(dv));
+  if (vec_ok && (hd == 128 || hd == 64 || hd == 32)) {
     if (hd == 128)
       qkv_prep_bwd_row_kernel<T, 128><<<kPrepBwdBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rstd, dq, dk,
                                                                           dv, rows, Tn, Hq, Hkv, D, dqkv, part_q, part_k);
@@ -447,9 +547,9 @@ int qkv_prep_bwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
       qkv_prep_bwd_row_kernel<T, 32><<<kPrepBwdBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rstd, dq, dk,
                                                                          dv, rows, Tn, Hq, Hkv, D, dqkv, part_q, part_k);
     ORTHRUS_CHECK_LAUNCH();
-    sum_partials_kernel<<<1, 128, 0, stream>>>(part_q, kPrepBwdBlocks, hd, dqw);
+    sum_partials_kernel<<<(hd + 7) / 8, 256, 0, stream>>>(part_q, kPrepBwdBlocks, hd, dqw);
     ORTHRUS_CHECK_LAUNCH();
-    sum_partials_kernel<<<1, 128, 0, stream>>>(part_k, kPrepBwdBlocks, hd, dkw);
+    sum_partials_kernel<<<(hd + 7) / 8, 256, 0, stream>>>(part_k, kPrepBwdBlocks, hd, dkw);
     ORTHRUS_CHECK_LAUNCH();
     return ORTHRUS_OK;
   }
@@ -457,7 +557,7 @@ int qkv_prep_bwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
     qkv_prep_bwd_kernel<T><<<kPrepBwdBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, qw, rstd, dq, B, Tn, Hq,
                                                                Hkv, hd, D, 0, dqkv, part_q);
     ORTHRUS_CHECK_LAUNCH();
-    sum_partials_kernel<<<1, 128, 0, stream>>>(part_q, kPrepBwdBlocks, hd, dqw);
+    sum_partials_kernel<<<(hd + 7) / 8, 256, 0, stream>>>(part_q, kPrepBwdBlocks, hd, dqw);
   } else {
     zero_heads_kernel<T><<<592, 256, 0, stream>>>(rows, heads, hd, 0, Hq, dqkv);
     ORTHRUS_CHECK_CUDA(cudaMemsetAsync(dqw, 0, hd * sizeof(float), stream));
@@ -467,7 +567,7 @@ int qkv_prep_bwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
     qkv_prep_bwd_kernel<T><<<kPrepBwdBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, kw, rstd, dk, B, Tn, Hq,
                                                                Hkv, hd, D, 1, dqkv, part_k);
     ORTHRUS_CHECK_LAUNCH();
-    sum_partials_kernel<<<1, 128, 0, stream>>>(part_k, kPrepBwdBlocks, hd, dkw);
+    sum_partials_kernel<<<(hd + 7) / 8, 256, 0, stream>>>(part_k, kPrepBwdBlocks, hd, dkw);
   } else {
     zero_heads_kernel<T><<<592, 256, 0, stream>>>(rows, heads, hd, Hq, Hkv, dqkv);
     ORTHRUS_CHECK_CUDA(cudaMemsetAsync(dkw, 0, hd * sizeof(float), stream));

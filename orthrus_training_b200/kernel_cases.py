@@ -1,0 +1,113 @@
+"""Stand-alone cases of the hot kernels at the shapes of one Qwen3-0.6B training row group.
+
+``python -m orthrus_training_b200.kernel_cases <case> [--iters N] [--warmup W]`` runs one case on
+``cuda:0`` and prints, per entry point, its CUDA-event time per call and its algorithmic
+throughput (the FLOP counts of ``ops.attention_flops`` and of the LM-head GEMMs). The same cases,
+with small ``--iters``, are the programs the ncu captures profile: each keeps a few GB on the
+device and launches its kernels a handful of times.
+
+Cases (B = 8 rows of 2048 tokens, 16 query / 8 KV heads of 128, A = 32 anchors, K = 32):
+  causal   teacher attention forward, causal over 2048 keys       (orthrus/objective.py:155)
+  dual     dual-view attention forward, Tq = A*K queries over the AR prefix and own blocks
+                                                                   (orthrus/objective.py:163)
+  dualbwd  dual-view attention forward, then backward (dQ; dK/dV of the own-block keys)
+  lmhead   fused LM head + KL: 2048 student rows against 1400 teacher rows, V = 151936, d = 1024
+                                                                   (orthrus/objective.py:338-392)
+"""
+
+from __future__ import annotations
+
+import argparse
+import math
+
+import torch
+
+from . import ops
+
+B, HQ, HKV, L, A, K, HD = 8, 16, 8, 2048, 32, 32, 128
+LM_N, LM_M, LM_V, LM_D = 2048, 1400, 151936, 1024
+
+
+def _attention_inputs(gen, dev):
+    Tq = A * K
+    q = torch.randn(B, HQ, Tq, HD, device=dev, generator=gen).bfloat16()
+    k1 = torch.randn(B, HKV, L, HD, device=dev, generator=gen).bfloat16()
+    v1 = torch.randn(B, HKV, L, HD, device=dev, generator=gen).bfloat16()
+    k2 = torch.randn(B, HKV, Tq, HD, device=dev, generator=gen).bfloat16()
+    v2 = torch.randn(B, HKV, Tq, HD, device=dev, generator=gen).bfloat16()
+    anchors = torch.stack([torch.randperm(L - K, device=dev, generator=gen)[:A].add(1).sort().values
+                           for _ in range(B)])
+    return q, k1, v1, k2, v2, anchors
+
+
+def _time(fn, iters: int, warmup: int) -> float:
+    """Milliseconds per call of ``fn``: CUDA events around ``iters`` back-to-back calls."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def run(case: str, iters: int, warmup: int) -> dict:
+    """{entry point: {"ms_per_call", "tflops"}} for one case."""
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    sc = 1.0 / math.sqrt(HD)
+    timed = []  # (name, fn, algorithmic FLOPs per call)
+    if case == "causal":
+        q = torch.randn(B, HQ, L, HD, device=dev, generator=gen).bfloat16()
+        k = torch.randn(B, HKV, L, HD, device=dev, generator=gen).bfloat16()
+        v = torch.randn_like(k)
+        timed.append(("attn_fwd_causal", lambda: ops.attention_fwd(q, k, v, mask=0, hd=HD, scale=sc),
+                      ops.attention_flops(0, B, HQ, L, HD)))
+    elif case in ("dual", "dualbwd"):
+        q, k1, v1, k2, v2, anchors = _attention_inputs(gen, dev)
+        fwd = lambda: ops.attention_fwd(q, k1, v1, k2, v2, mask=1, hd=HD, scale=sc, anchors=anchors, block=K)
+        flops = float(ops.attention_flops(1, B, HQ, A * K, HD, anchors, K, L))
+        timed.append(("attn_fwd_dual", fwd, flops))
+        if case == "dualbwd":
+            o, lse = fwd()
+            dout = torch.randn(B, A * K, HQ, HD, device=dev, generator=gen).bfloat16()
+            timed.append(("attn_bwd_dual",
+                          lambda: ops.attention_bwd(q, k1, v1, k2, v2, anchors, K, o, lse, dout, hd=HD, scale=sc),
+                          1.5 * flops))
+    elif case == "lmhead":
+        s = torch.randn(LM_N, LM_D, device=dev, generator=gen).bfloat16()
+        t = torch.randn(LM_M, LM_D, device=dev, generator=gen).bfloat16()
+        idx = torch.randint(0, LM_M, (LM_N,), device=dev, generator=gen).sort().values
+        w = (torch.randn(LM_V, LM_D, device=dev, generator=gen) * 0.05).bfloat16()
+        # logits of the student and unique teacher rows once each, plus the grad GEMM diff @ W
+        timed.append(("lmhead_kl", lambda: ops.lmhead_kl(s, t, idx, w),
+                      2.0 * LM_D * LM_V * (2 * LM_N + LM_M)))
+    else:
+        raise ValueError(f"unknown case {case!r}")
+    out = {}
+    for name, fn, flops in timed:
+        ms = _time(fn, iters, warmup)
+        out[name] = {"ms_per_call": round(ms, 4), "tflops": round(flops / (ms / 1e3) / 1e12, 1)}
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("case", choices=["causal", "dual", "dualbwd", "lmhead"])
+    ap.add_argument("--iters", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=2)
+    args = ap.parse_args()
+    for name, rec in run(args.case, args.iters, args.warmup).items():
+        print(f"{name}: {rec['ms_per_call']:.3f} ms/call, {rec['tflops']} TF/s algorithmic", flush=True)
+    from . import _lib
+    err = _lib.device_error(0)
+    print("device error word", err)
+    if err:
+        raise SystemExit(1)
+
+
+if __name__ == "__main__":
+    main()

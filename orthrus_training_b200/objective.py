@@ -160,9 +160,10 @@ def _teacher_layer(model, i, x, pos, B, L, inv):
     q, k, v, _ = ops.qkv_prep(qkv, pos, inv, attn.q_norm.weight, attn.k_norm.weight, B, L, Hq, Hkv,
                               hd, D, eps)
     o, _ = ops.attention_fwd(q, k, v, mask=MASK_CAUSAL, hd=hd, scale=hd ** -0.5, want_lse=False)
-    x = x + o.view(B * L, Hq * hd) @ attn.o_proj.weight.t()
+    # residual adds ride in the GEMM epilogue (beta = 1)
+    x = torch.addmm(x, o.view(B * L, Hq * hd), attn.o_proj.weight.t())
     h = ops.rms_norm(x, layer.post_attention_layernorm.weight, eps)
-    x = x + ops.silu_mul(h @ model._packed_mlp(i).t()) @ layer.mlp.down_proj.weight.t()
+    x = torch.addmm(x, ops.silu_mul(h @ model._packed_mlp(i).t()), layer.mlp.down_proj.weight.t())
     return x, k, v
 
 
@@ -178,10 +179,10 @@ def _diffusion_layer(model, i, x, ar_k, ar_v, positions, anchors, inv, B, Q):
     qkv = F.linear(h, w_qkv)
     o = DualViewAttention.apply(qkv, attn.q_norm_diff.weight, attn.k_norm_diff.weight, ar_k, ar_v,
                                 positions, anchors, inv, meta)
-    x = x + F.linear(o, attn.o_proj_diff.weight)
+    x = torch.addmm(x, o, attn.o_proj_diff.weight.t())
     h = _rms_norm(x, layer.post_attention_layernorm.weight, eps)
     gu = F.linear(h, model._packed_mlp(i))
-    return x + F.linear(_SwiGLU.apply(gu), layer.mlp.down_proj.weight)
+    return torch.addmm(x, _SwiGLU.apply(gu), layer.mlp.down_proj.weight.t())
 
 
 def model_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tensor,
