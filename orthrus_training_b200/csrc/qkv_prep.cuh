@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, c
   if (rstd_out != nullptr && lane == 0) rstd_out[r] = rstd;
 }
 
-constexpr int kPrepBwdBlocks = 592;  // fixed grid (4 x 148): a deterministic split of the items
+constexpr int kPrepBwdBlocks = 444;  // fixed grid (3 x 148, one wave): a deterministic split of the items
 
 // ------------------------------------------------------------------------------------------------
 // Row-parallel prologue for head dims 32 / 64 / 128: one CTA per token row computes the row's
@@ -296,55 +296,59 @@ __device__ __forceinline__ void store_elems(T* p, const float* v) {
   }
 }
 
-// One CTA per token row, 8 warps; warp w owns the heads w, w + 8, w + 16, w + 24 of each group of
-// 32 and loads all of them before it computes, so four head rows per warp are in flight at once.
-// Lane l holds the elements [l * NE, l * NE + NE) of a head as one vector access.
-// Requires 16-byte aligned tensors and D % 8 == 0 (checked by the host).
+// This lane's cos / sin of the RoPE angle for its elements e = lane * NE + k (pair index
+// e mod HD/2), rounded to the activation dtype as the reference's rotary table is.
 template <typename T, int HD>
-__global__ void __launch_bounds__(256) qkv_prep_fwd_row_kernel(
+__device__ __forceinline__ void rope_lane_table(float pos, const float* __restrict__ inv_freq, int lane, float* cs,
+                                                float* sn) {
+  constexpr int NE = HD / 32;
+#pragma unroll
+  for (int k = 0; k < NE; ++k) {
+    const int i = (lane * NE + k) & (HD / 2 - 1);
+    float sv, cv;
+    sincosf(pos * inv_freq[i], &sv, &cv);
+    cs[k] = round_to<T>(cv);
+    sn[k] = round_to<T>(sv);
+  }
+}
+
+// One warp per token row (8 rows per CTA), no shared memory: every lane builds the RoPE table of
+// its own elements, then the warp walks the row's heads PER at a time, all PER head rows loaded
+// before any is computed. Lane l holds the elements [l * NE, l * NE + NE) of a head as one vector
+// access. Requires 16-byte aligned tensors and D % 8 == 0 (checked by the host).
+template <typename T, int HD>
+__global__ void __launch_bounds__(256, 4) qkv_prep_fwd_row_kernel(
     const T* __restrict__ qkv, const int64_t* __restrict__ positions, const float* __restrict__ inv_freq,
-    const T* __restrict__ q_norm_w, const T* __restrict__ k_norm_w, int64_t Tn, int Hq, int Hkv, int D, float eps,
-    T* __restrict__ q_out, T* __restrict__ k_out, T* __restrict__ v_out, int64_t cap,
+    const T* __restrict__ q_norm_w, const T* __restrict__ k_norm_w, int64_t rows, int64_t Tn, int Hq, int Hkv,
+    int D, float eps, T* __restrict__ q_out, T* __restrict__ k_out, T* __restrict__ v_out, int64_t cap,
     const int32_t* __restrict__ offset, float* __restrict__ rstd_out) {
   constexpr int NE = HD / 32;
   constexpr int HALF = HD / 2;
-  constexpr int PER_WARP = 4;
-  __shared__ float cs[HALF], sn[HALF];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row = blockIdx.x;
+  constexpr int PER = HD == 128 ? 4 : 8;  // head rows in flight per warp within 64 registers
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
   const int64_t b = row / Tn, t = row % Tn;
   const int heads = Hq + 2 * Hkv;
   const T* xrow = qkv + row * static_cast<int64_t>(heads) * HD;
-  // the loads of this warp's first heads go out before the RoPE table is built
-  float v[PER_WARP][NE];
+  float v[PER][NE];
 #pragma unroll
-  for (int j = 0; j < PER_WARP; ++j) {
-    const int head = warp + 8 * j;
-    if (head < heads) load_elems<T, NE>(xrow + head * HD + lane * NE, v[j]);
-  }
-  const float pos = static_cast<float>(positions[row]);
-  for (int i = threadIdx.x; i < HALF; i += blockDim.x) {
-    float sv, cv;
-    sincosf(pos * inv_freq[i], &sv, &cv);
-    cs[i] = round_to<T>(cv);
-    sn[i] = round_to<T>(sv);
-  }
-  float wq[NE], wk[NE];
+  for (int j = 0; j < PER; ++j)
+    if (j < heads) load_elems<T, NE>(xrow + j * HD + lane * NE, v[j]);
+  float cs[NE], sn[NE], wq[NE], wk[NE];
+  rope_lane_table<T, HD>(static_cast<float>(positions[row]), inv_freq, lane, cs, sn);
   load_elems<T, NE>(q_norm_w + lane * NE, wq);
   load_elems<T, NE>(k_norm_w + lane * NE, wk);
-  __syncthreads();
   const int64_t orow_kv = (offset ? offset[b] : 0) + t;
-  for (int h0 = warp; h0 < heads; h0 += 8 * PER_WARP) {
-    if (h0 != warp) {
+  for (int h0 = 0; h0 < heads; h0 += PER) {
+    if (h0 > 0) {
 #pragma unroll
-      for (int j = 0; j < PER_WARP; ++j) {
-        const int head = h0 + 8 * j;
-        if (head < heads) load_elems<T, NE>(xrow + head * HD + lane * NE, v[j]);
-      }
+      for (int j = 0; j < PER; ++j)
+        if (h0 + j < heads) load_elems<T, NE>(xrow + (h0 + j) * HD + lane * NE, v[j]);
     }
 #pragma unroll
-    for (int j = 0; j < PER_WARP; ++j) {
-      const int head = h0 + 8 * j;  // warp-uniform
+    for (int j = 0; j < PER; ++j) {
+      const int head = h0 + j;  // warp-uniform
       if (head >= heads) break;
       float* x = v[j];
       T* dst;
@@ -363,10 +367,8 @@ __global__ void __launch_bounds__(256) qkv_prep_fwd_row_kernel(
 #pragma unroll
         for (int k = 0; k < NE; ++k) {
           const float partner = __shfl_xor_sync(0xffffffffu, x[k], 16);
-          const int e = lane * NE + k;
-          const int i = e < HALF ? e : e - HALF;
-          const float rot = e < HALF ? -partner : partner;
-          x[k] = x[k] * cs[i] + rot * sn[i];
+          const float rot = (lane * NE + k) < HALF ? -partner : partner;
+          x[k] = x[k] * cs[k] + rot * sn[k];
         }
         if (rstd_out != nullptr && lane == 0) rstd_out[row * (Hq + Hkv) + head] = rstd;
         dst = is_q ? q_out + ((b * Hq + head) * Tn + t) * D
@@ -382,7 +384,7 @@ __global__ void __launch_bounds__(256) qkv_prep_fwd_row_kernel(
 // CTAs, rows strided over the CTAs, heads over the warps in a fixed order, so the norm-weight
 // gradient partials part_q / part_k [block][HD] are deterministic.
 template <typename T, int HD>
-__global__ void __launch_bounds__(256) qkv_prep_bwd_row_kernel(
+__global__ void __launch_bounds__(256, 3) qkv_prep_bwd_row_kernel(
     const T* __restrict__ qkv, const int64_t* __restrict__ positions, const float* __restrict__ inv_freq,
     const T* __restrict__ q_norm_w, const T* __restrict__ k_norm_w, const float* __restrict__ rstd,
     const float* __restrict__ dq, const float* __restrict__ dk, const float* __restrict__ dv, int64_t rows,
@@ -390,8 +392,7 @@ __global__ void __launch_bounds__(256) qkv_prep_bwd_row_kernel(
     float* __restrict__ part_k) {
   constexpr int NE = HD / 32;
   constexpr int HALF = HD / 2;
-  constexpr int PER_WARP = 4;  // head rows of one warp in flight at once
-  __shared__ float cs[HALF], sn[HALF];
+  constexpr int PER = HD == 128 ? 2 : 4;  // head rows in flight per warp within 80 registers
   __shared__ float wpart[2][8][HD];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int heads = Hq + 2 * Hkv;
@@ -400,23 +401,18 @@ __global__ void __launch_bounds__(256) qkv_prep_bwd_row_kernel(
   for (int k = 0; k < NE; ++k) wq[k] = wk[k] = 0.f;
   load_elems<T, NE>(q_norm_w + lane * NE, nq);
   load_elems<T, NE>(k_norm_w + lane * NE, nk);
-  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+  // one warp per row; rows strided over the fixed grid in a fixed order (deterministic partials)
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp; row < rows;
+       row += static_cast<int64_t>(gridDim.x) * 8) {
     const int64_t b = row / Tn, t = row % Tn;
-    const float pos = static_cast<float>(positions[row]);
-    __syncthreads();  // the previous row's table is no longer read
-    for (int i = threadIdx.x; i < HALF; i += blockDim.x) {
-      float sv, cv;
-      sincosf(pos * inv_freq[i], &sv, &cv);
-      cs[i] = round_to<T>(cv);
-      sn[i] = round_to<T>(sv);
-    }
-    __syncthreads();
-    for (int h0 = warp; h0 < heads; h0 += 8 * PER_WARP) {
-      // loads of up to PER_WARP heads first: the incoming gradient and, for q / k, the input row
-      float gv[PER_WARP][NE], xv[PER_WARP][NE], rr[PER_WARP];
+    float cs[NE], sn[NE];
+    rope_lane_table<T, HD>(static_cast<float>(positions[row]), inv_freq, lane, cs, sn);
+    for (int h0 = 0; h0 < heads; h0 += PER) {
+      // loads of up to PER heads first: the incoming gradient and, for q / k, the input row
+      float gv[PER][NE], xv[PER][NE], rr[PER];
 #pragma unroll
-      for (int j = 0; j < PER_WARP; ++j) {
-        const int head = h0 + 8 * j;
+      for (int j = 0; j < PER; ++j) {
+        const int head = h0 + j;
         rr[j] = 0.f;
         if (head >= heads) continue;
         const bool is_v = head >= Hq + Hkv, is_q = head < Hq;
@@ -434,8 +430,8 @@ __global__ void __launch_bounds__(256) qkv_prep_bwd_row_kernel(
         }
       }
 #pragma unroll
-      for (int j = 0; j < PER_WARP; ++j) {
-        const int head = h0 + 8 * j;  // warp-uniform
+      for (int j = 0; j < PER; ++j) {
+        const int head = h0 + j;  // warp-uniform
         if (head >= heads) break;
         T* out = dqkv + row * static_cast<int64_t>(heads) * HD + head * HD + lane * NE;
         const bool is_v = head >= Hq + Hkv, is_q = head < Hq;
@@ -452,10 +448,8 @@ __global__ void __launch_bounds__(256) qkv_prep_bwd_row_kernel(
         for (int k = 0; k < NE; ++k) {
           xh[k] = xv[j][k] * r;
           const float partner = __shfl_xor_sync(0xffffffffu, gv[j][k], 16);
-          const int e = lane * NE + k;
-          const int i = e < HALF ? e : e - HALF;
-          const float other = e < HALF ? partner : -partner;
-          gr[k] = gv[j][k] * cs[i] + other * sn[i];
+          const float other = (lane * NE + k) < HALF ? partner : -partner;
+          gr[k] = gv[j][k] * cs[k] + other * sn[k];
           dot = fmaf(gr[k] * w[k], xh[k], dot);
           if (is_q)
             wq[k] = fmaf(gr[k], xh[k], wq[k]);
@@ -500,15 +494,16 @@ int qkv_prep_fwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
   const bool vec_ok = D % 8 == 0 && aligned16(qkv) && aligned16(qw) && aligned16(kw) && aligned16(q_out) &&
                       aligned16(k_out) && aligned16(v_out);
   if (vec_ok && (hd == 128 || hd == 64 || hd == 32)) {
-    const unsigned rows = static_cast<unsigned>(B * Tn);
+    const int64_t rows = B * Tn;
+    const unsigned grid = static_cast<unsigned>(ceil_div(rows, 8));  // one warp per row
     if (hd == 128)
-      qkv_prep_fwd_row_kernel<T, 128><<<rows, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, Tn, Hq, Hkv, D, eps,
+      qkv_prep_fwd_row_kernel<T, 128><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
                                                                q_out, k_out, v_out, cap, offset, rstd);
     else if (hd == 64)
-      qkv_prep_fwd_row_kernel<T, 64><<<rows, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, Tn, Hq, Hkv, D, eps,
+      qkv_prep_fwd_row_kernel<T, 64><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
                                                               q_out, k_out, v_out, cap, offset, rstd);
     else
-      qkv_prep_fwd_row_kernel<T, 32><<<rows, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, Tn, Hq, Hkv, D, eps,
+      qkv_prep_fwd_row_kernel<T, 32><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
                                                               q_out, k_out, v_out, cap, offset, rstd);
     ORTHRUS_CHECK_LAUNCH();
     return ORTHRUS_OK;
