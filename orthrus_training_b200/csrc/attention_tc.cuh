@@ -756,7 +756,7 @@ __global__ void __launch_bounds__(192, 1)
           for (int i = 0; i < 32; ++i) {
             const int qc = c * 32 + i;
             const bool vis = kind == 1 || (qc >= lo && qc < hi);
-            const float p = vis ? exp2f(fmaf(x[i], sl2, -g_lse[qc])) : 0.f;
+            const float p = vis ? ex2_approx(fmaf(x[i], sl2, -g_lse[qc])) : 0.f;
             x[i] = p;
             y[i] = p * (y[i] - g_delta[qc]);
           }
@@ -1010,21 +1010,20 @@ __global__ void __launch_bounds__(320, 1)
       const int64_t key0 = (src2 ? t2a + (j - n1) : j) * 128;
       const int64_t lo = (src2 ? s2 : 0) - key0, hi = (src2 ? e2 : e1) - key0;  // visible columns
       const bool full = lo <= 0 && hi >= 128;
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
+      // row max of the raw scores (scale > 0 commutes with max), four independent chains
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       if (full) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          s[i] *= scale_log2;
-          mx[i & 3] = fmaxf(mx[i & 3], s[i]);
-        }
+        for (int i = 0; i < 128; ++i) mx[i & 3] = fmaxf(mx[i & 3], s[i]);
       } else {
 #pragma unroll
         for (int i = 0; i < 128; ++i) {
-          s[i] = (i >= lo && i < hi) ? s[i] * scale_log2 : -INFINITY;
+          s[i] = (i >= lo && i < hi) ? s[i] : -INFINITY;
           mx[i & 3] = fmaxf(mx[i & 3], s[i]);
         }
       }
-      const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      const float rmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      const float tmax = rmax == -INFINITY ? -INFINITY : rmax * scale_log2;
       // the previous P V of this head must be done before P and O are touched again
       if (j > 0 && !mbar_wait(&p_empty[h], (j - 1) & 1)) {
         ok = false;
@@ -1044,7 +1043,7 @@ __global__ void __launch_bounds__(320, 1)
         float* x = s + 32 * c;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          x[i] = exp2f(x[i] - mu);
+          x[i] = ex2_approx(fmaf(x[i], scale_log2, -mu));
           sm[i & 3] += x[i];
         }
         store_row32_sw128(p_base, row, c * 32, x);
@@ -1331,12 +1330,12 @@ __global__ void __launch_bounds__(320, 1)
         tmem_wait_ld();
         if (kind == 1) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) xc[i] = exp2f(fmaf(xc[i], sl2, -L2e)) * (y[i] - dl);
+          for (int i = 0; i < 32; ++i) xc[i] = ex2_approx(fmaf(xc[i], sl2, -L2e)) * (y[i] - dl);
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int col = 32 * c + i;
-            const float p = (col >= lo && col < hi) ? exp2f(fmaf(xc[i], sl2, -L2e)) : 0.f;
+            const float p = (col >= lo && col < hi) ? ex2_approx(fmaf(xc[i], sl2, -L2e)) : 0.f;
             xc[i] = p * (y[i] - dl);
           }
         }

@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(192, 1)
         float sv[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          if (j < nvalid) sv[j & 3] += exp2f(fmaf(x[j], kLog2e, -ml));
+          if (j < nvalid) sv[j & 3] += ex2_approx(fmaf(x[j], kLog2e, -ml));
         s += (sv[0] + sv[1]) + (sv[2] + sv[3]);
       }
       tc_fence_before();
@@ -398,7 +398,7 @@ __global__ void __launch_bounds__(192, 1)
           for (int u = 0; u < 2; ++u) {
             const float a = xs[j + u] - ls_off;  // log p_s
             const float bb = xt[j + u] - lt_off;  // log p_t
-            const float ps = exp2f(a * kLog2e), pt = exp2f(bb * kLog2e);
+            const float ps = ex2_approx(a * kLog2e), pt = ex2_approx(bb * kLog2e);
             const bool ok = (j + u) < nvalid;
             klv[(j + u) & 3] += ok ? pt * (bb - a) : 0.f;
             d2[u] = ok ? w * (ps - pt) : 0.f;
