@@ -81,9 +81,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete; false after kWaitLimitNs (error recorded).
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Slow path of mbar_wait, out of line so that the hot loops carry no call unless the first
+// try_wait (which itself suspends the thread for a while) came back empty.
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = global_timer_ns();
   while (true) {
 #pragma unroll 1
@@ -94,6 +94,11 @@ __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
       return false;
     }
   }
+}
+
+// Waits for the phase with the given parity to complete; false after kWaitLimitNs (error recorded).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity);
 }
 
 // Same wait with a short limit, used only while draining after an error.
