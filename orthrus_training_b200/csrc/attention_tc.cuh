@@ -1379,322 +1379,3 @@ __global__ void __launch_bounds__(320, 1)
 }
 
 }  // namespace orthrus
-
-namespace orthrus {
-
-// ------------------------------------------------------------------------------------------------
-// Forward, two query heads per CTA, 64-key tiles with S double-buffered per head
-// ------------------------------------------------------------------------------------------------
-//
-// CTA = 128 query rows of the heads 2p, 2p+1 sharing one KV head; 320 threads (warp 0 TMA, warp 1
-// MMA issue, warps 2-5 / 6-9 the rows of head 2p / 2p+1). TMEM: S of head h, buffer u in columns
-// [64 (2h + u), +64); the O accumulator of head h in [256 + 128h, +128). With two S buffers per
-// head the MMA warp computes S(j + 1) of a head while its rows run the softmax of tile j, so a
-// head's rows never wait for a QK^T; the P V of tile j and the QK^T of tile j + 2 follow as soon as
-// P(j) is in shared memory. K and V tiles of 64 rows share a ring of six slots (K(0), V(0), K(1),
-// ...). P of head h, buffer u is a [128][64] bf16 swizzled box.
-
-template <int D>
-struct Fwd3Smem {
-  static constexpr int BOXES = D / 64;
-  static constexpr int QT = BOXES * kAttnTileBytes;  // [128][D]
-  static constexpr int KT = BOXES * kKeyBox64;       // [64][D]
-  static constexpr int SLOTS = 6;
-  static constexpr int OFF_Q = 0;                    // Q of head h at h * QT
-  static constexpr int OFF_RING = 2 * QT;            // slot s at s * KT
-  static constexpr int OFF_P = OFF_RING + SLOTS * KT;  // P of head h, buffer u at (2h + u) * 16 KB
-  static constexpr int OFF_BAR = OFF_P + 4 * kAttnTileBytes;
-  static constexpr int SMEM = OFF_BAR + 512 + 1024;
-};
-
-template <int D>
-__global__ void __launch_bounds__(320, 1)
-    attn_fwd_tc3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK1,
-                        const __grid_constant__ CUtensorMap tmV1, const __grid_constant__ CUtensorMap tmK2,
-                        const __grid_constant__ CUtensorMap tmV2, int Hq, int Hkv, int64_t Tq, int hd,
-                        float scale_log2, MaskParams mp, bool has2, __nv_bfloat16* __restrict__ o,
-                        float* __restrict__ lse) {
-  using S = Fwd3Smem<D>;
-  constexpr int NS = S::SLOTS;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
-  uint64_t* q_full = bars + 0;
-  uint64_t* slot_full = bars + 1;    // [NS]
-  uint64_t* slot_empty = bars + 7;   // [NS] consumed by the MMAs of both heads
-  uint64_t* s_full = bars + 13;      // [h][u]
-  uint64_t* p_full = bars + 17;      // [h][u] (128 arrivals)
-  uint64_t* p_empty = bars + 21;     // [h][u] the P V reading P[h][u] completed
-  uint64_t* mma_done = bars + 25;
-  unsigned long long* red = reinterpret_cast<unsigned long long*>(bars + 28);
-  AttnTiles* tiles = reinterpret_cast<AttnTiles*>(bars + 32);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 36);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 37);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t q0 = static_cast<int64_t>(gridDim.x - 1 - blockIdx.x) * 128;  // heavy tiles first
-  const int pair = blockIdx.y;
-  const int64_t b = blockIdx.z;
-  const int G = Hq / Hkv;
-  const int hk = (2 * pair) / G;
-  const int wg = warp >= 2 ? (warp - 2) / 4 : -1;  // softmax warpgroup = head of the pair
-  const int row = warp >= 2 ? (warp & 3) * 32 + lane : -1;
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int i = 0; i < NS; ++i) {
-      mbar_init(&slot_full[i], 1);
-      mbar_init(&slot_empty[i], 1);
-    }
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
-      mbar_init(&p_empty[i], 1);
-    }
-    mbar_init(mma_done, 1);
-    red[0] = 0;
-    red[1] = ~0ull;
-    red[2] = 0;
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 1) tmem_alloc(tmem_slot, 512);
-  __syncthreads();
-  attn_tile_map(mp, b, q0, Tq, has2, wg == 0 ? row : -1, red, tiles);
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  // 64-key tiles: source 1 covers [0, 64 * n1), source 2 [64 * t2a, 64 * (t2a + n2))
-  const int n1 = static_cast<int>((red[0] + 63) / 64);
-  const int t2a = red[2] > red[1] ? static_cast<int>(red[1] / 64) : 0;
-  const int n2 = red[2] > red[1] ? static_cast<int>((red[2] + 63) / 64) - t2a : 0;
-  const int nt = n1 + n2;
-
-  if (warp == 0) {
-    if (elect_one()) {
-      mbar_arrive_expect_tx(q_full, 2 * S::QT);
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int c = 0; c < S::BOXES; ++c)
-          tma_load_3d(smem + S::OFF_Q + h * S::QT + c * kAttnTileBytes, &tmQ, q_full, c * 64,
-                      static_cast<int>(q0), static_cast<int>(b * Hq + 2 * pair + h));
-      // ring positions: K(j) at 2j, V(j) at 2j + 1; a slot is reused once its tile was consumed
-      int issued = 0;
-      const int z = static_cast<int>(b * Hkv + hk);
-      for (int pos = 0; pos < 2 * nt; ++pos) {
-        const int j = pos >> 1, slot = pos % NS, use = pos / NS;
-        const bool src2 = j >= n1;
-        const int key0 = (src2 ? t2a + (j - n1) : j) * 64;
-        if (*abort_flag || !mbar_wait(&slot_empty[slot], (use & 1) ^ 1)) {
-          *abort_flag = 1;
-          break;
-        }
-        const CUtensorMap* map = (pos & 1) ? (src2 ? &tmV2 : &tmV1) : (src2 ? &tmK2 : &tmK1);
-        uint8_t* dst = smem + S::OFF_RING + slot * S::KT;
-        mbar_arrive_expect_tx(&slot_full[slot], S::KT);
-#pragma unroll
-        for (int c = 0; c < S::BOXES; ++c) tma_load_3d(dst + c * kKeyBox64, map, &slot_full[slot], c * 64, key0, z);
-        issued = pos + 1;
-      }
-      if (*abort_flag) {
-        mbar_wait_short(q_full, 0);
-        for (int pos = max(0, issued - NS); pos < issued; ++pos)
-          mbar_wait_short(&slot_full[pos % NS], (pos / NS) & 1);
-      }
-    }
-  } else if (warp == 1) {
-    if (elect_one()) {
-      constexpr uint32_t idesc_s = umma_idesc_bf16(128, 64, false, false);
-      constexpr uint32_t idesc_o = umma_idesc_bf16(128, D, false, true);
-      auto ring = [&](int pos) { return smem_u32(smem + S::OFF_RING + (pos % NS) * S::KT); };
-      auto ring_full = [&](int pos) { return mbar_wait(&slot_full[pos % NS], (pos / NS) & 1); };
-      auto issue_s = [&](int h, int j) {  // S(j) of head h into buffer j & 1
-        const uint32_t q_base = smem_u32(smem + S::OFF_Q + h * S::QT);
-        const uint32_t k_base = ring(2 * j);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_f16(tmem + 64 * (2 * h + (j & 1)), desc_kmajor(q_base, kk), desc_kmajor_rows64(k_base, kk), idesc_s,
-                   kk > 0 ? 1u : 0u);
-        umma_commit(&s_full[2 * h + (j & 1)]);
-      };
-      bool ok = mbar_wait(q_full, 0);
-      // prologue: S(0) and S(1) of both heads
-      for (int j = 0; ok && j < 2 && j < nt; ++j) {
-        if (!ring_full(2 * j)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        issue_s(0, j);
-        issue_s(1, j);
-        umma_commit(&slot_empty[(2 * j) % NS]);
-      }
-      for (int j = 0; ok && j < nt; ++j) {
-        const int u = j & 1;
-        for (int h = 0; h < 2; ++h) {
-          if (*abort_flag || !mbar_wait(&p_full[2 * h + u], (j >> 1) & 1) || (h == 0 && !ring_full(2 * j + 1))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t p_base = smem_u32(smem + S::OFF_P + (2 * h + u) * kAttnTileBytes);
-          const uint32_t v_base = ring(2 * j + 1);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_f16(tmem + 256 + h * 128, desc_kmajor(p_base, kk), desc_mnmajor_rows64(v_base, kk), idesc_o,
-                     (j > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&p_empty[2 * h + u]);
-          if (h == 1) umma_commit(&slot_empty[(2 * j + 1) % NS]);
-          // S buffer u of this head is free: its rows loaded S(j) before they wrote P(j)
-          if (j + 2 < nt) {
-            if (h == 0 && !ring_full(2 * j + 4)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_s(h, j + 2);
-            if (h == 1) umma_commit(&slot_empty[(2 * j + 4) % NS]);
-          }
-        }
-      }
-      if (!ok) *abort_flag = 1;
-      // drain on its own barrier: no MMA may still run when the CTA frees its TMEM
-      umma_commit(mma_done);
-      mbar_wait(mma_done, 0);
-    }
-  } else {
-    const int h = wg;
-    const int64_t t = q0 + row;
-    const bool live = t < Tq;
-    int64_t e1 = 0, s2 = 0, e2 = 0;
-    if (live) query_ranges(mp, b, t, e1, s2, e2);
-    if (!has2) e2 = s2 = 0;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const uint32_t o_col = lane_base + 256 + h * 128;
-    float m_ref = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nt; ++j) {
-      const int u = j & 1;
-      if (*abort_flag || !mbar_wait(&s_full[2 * h + u], (j >> 1) & 1)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const bool src2 = j >= n1;
-      const int64_t key0 = (src2 ? t2a + (j - n1) : j) * 64;
-      const int64_t lo = (src2 ? s2 : 0) - key0, hi = (src2 ? e2 : e1) - key0;  // visible columns
-      int kind[2];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) kind[c] = chunk_kind_warp(lo, hi, 32 * c, 32);  // warp-uniform
-      float x[64];
-      const uint32_t s_col = lane_base + 64 * (2 * h + u);
-#pragma unroll
-      for (int c = 0; c < 2; ++c)
-        if (kind[c] != 0) tmem_ld32(s_col + 32 * c, x + 32 * c);
-      tmem_wait_ld();
-      // row max of the raw scores over the visible columns, four independent chains
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float* xc = x + 32 * c;
-        if (kind[c] == 1) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], xc[i]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = 32 * c + i;
-            xc[i] = (kind[c] == 2 && col >= lo && col < hi) ? xc[i] : -INFINITY;
-            mx[i & 3] = fmaxf(mx[i & 3], xc[i]);
-          }
-        }
-      }
-      const float rmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-      const float tmax = rmax == -INFINITY ? -INFINITY : rmax * scale_log2;
-      float alpha = 1.f;
-      if (tmax > m_ref + kRescaleThreshold) {
-        if (m_ref != -INFINITY) alpha = exp2f(m_ref - tmax);
-        m_ref = tmax;
-      }
-      const float mu = m_ref == -INFINITY ? 0.f : m_ref;
-      float sm[4] = {0.f, 0.f, 0.f, 0.f};  // independent chains
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float* xc = x + 32 * c;
-        if (kind[c] == 0) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) xc[i] = 0.f;
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            xc[i] = ex2_approx(fmaf(xc[i], scale_log2, -mu));  // masked columns hold -inf: 0
-            sm[i & 3] += xc[i];
-          }
-        }
-      }
-      // P buffer u was last read by the P V of tile j - 2
-      if (j >= 2 && !mbar_wait(&p_empty[2 * h + u], ((j - 2) >> 1) & 1)) {
-        ok = false;
-        break;
-      }
-      const uint32_t p_base = smem_u32(smem + S::OFF_P + (2 * h + u) * kAttnTileBytes);
-      store_row32_sw128(p_base, row, 0, x);
-      store_row32_sw128(p_base, row, 32, x + 32);
-      l = fmaf(l, alpha, (sm[0] + sm[1]) + (sm[2] + sm[3]));
-      if (alpha != 1.f) {
-        // O holds the P V of every tile before j: wait for the last of them, then rescale it
-        if (j >= 1 && !mbar_wait(&p_empty[2 * h + (u ^ 1)], ((j - 1) >> 1) & 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < D / 16; ++c) {
-          float y[16];
-          tmem_ld16(o_col + c * 16, y);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) y[i] *= alpha;
-          tmem_st16(o_col + c * 16, y);
-        }
-        tmem_wait_st();
-      }
-      tc_fence_before();
-      fence_proxy_async_smem();
-      mbar_arrive(&p_full[2 * h + u]);
-    }
-    if (!ok) *abort_flag = 1;
-    const bool done = ok && nt > 0 && mbar_wait(&p_empty[2 * h + ((nt - 1) & 1)], ((nt - 1) >> 1) & 1);
-    tc_fence_after();
-    float acc[D];
-#pragma unroll
-    for (int c = 0; c < D / 32; ++c) tmem_ld32(o_col + c * 32, acc + 32 * c);
-    tmem_wait_ld();
-    if (done && live) {
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      const int hh = 2 * pair + h;
-      __nv_bfloat16* orow = o + ((b * Tq + t) * Hq + hh) * hd;
-      if (hd == D) {
-#pragma unroll
-        for (int i = 0; i < D; i += 8) {
-          uint4 pk = make_uint4(pack_bf16x2(acc[i] * inv, acc[i + 1] * inv), pack_bf16x2(acc[i + 2] * inv, acc[i + 3] * inv),
-                                pack_bf16x2(acc[i + 4] * inv, acc[i + 5] * inv), pack_bf16x2(acc[i + 6] * inv, acc[i + 7] * inv));
-          *reinterpret_cast<uint4*>(orow + i) = pk;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < D; ++i)
-          if (i < hd) orow[i] = __float2bfloat16_rn(acc[i] * inv);
-      }
-      if (lse) lse[(b * Hq + hh) * Tq + t] = (m_ref + log2f(l)) * kLn2;
-    }
-    tc_fence_before();
-  }
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_free(tmem, 512);
-  }
-}
-
-}  // namespace orthrus

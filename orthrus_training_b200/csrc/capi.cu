@@ -240,32 +240,7 @@ int orthrus_attn_fwd(const void* q, const void* k1, const void* v1, int64_t s1h,
                         hd, D, nullptr))
       return ORTHRUS_ECUDA;
     const float sl2 = scale * kLog2e;
-    // ORTHRUS_FWD_KEY_TILE=128 selects the 128-key-tile forward (a comparison point for profiling)
-    static const bool wide_tiles = [] {
-      const char* e = std::getenv("ORTHRUS_FWD_KEY_TILE");
-      return e != nullptr && std::atoi(e) == 128;
-    }();
-    if ((Hq / Hkv) % 2 == 0 && !wide_tiles) {  // two query heads of one KV head per CTA, 64-key tiles
-      AttnMaps m64;
-      if (!make_attn_maps(m64, q, k1, v1, s1h, L1, has2 ? k2 : nullptr, has2 ? v2 : nullptr, s2h, L2, B, Hq, Hkv,
-                          Tq, hd, D, nullptr, 64))
-        return ORTHRUS_ECUDA;
-      dim3 grid2(static_cast<unsigned>(ceil_div(Tq, 128)), Hq / 2, static_cast<unsigned>(B));
-      if (D == 128) {
-        if (set_smem(attn_fwd_tc3_kernel<128>, Fwd3Smem<128>::SMEM)) return ORTHRUS_ECUDA;
-        attn_fwd_tc3_kernel<128><<<grid2, 320, Fwd3Smem<128>::SMEM, st>>>(
-            m64.q, m64.k1, m64.v1, m64.k2, m64.v2, Hq, Hkv, Tq, hd, sl2, mp, has2, static_cast<__nv_bfloat16*>(o),
-            lse);
-      } else {
-        if (set_smem(attn_fwd_tc3_kernel<64>, Fwd3Smem<64>::SMEM)) return ORTHRUS_ECUDA;
-        attn_fwd_tc3_kernel<64><<<grid2, 320, Fwd3Smem<64>::SMEM, st>>>(
-            m64.q, m64.k1, m64.v1, m64.k2, m64.v2, Hq, Hkv, Tq, hd, sl2, mp, has2, static_cast<__nv_bfloat16*>(o),
-            lse);
-      }
-      ORTHRUS_CHECK_LAUNCH();
-      return ORTHRUS_OK;
-    }
-    if ((Hq / Hkv) % 2 == 0) {  // 128-key tiles
+    if ((Hq / Hkv) % 2 == 0) {  // two query heads of one KV head per CTA
       dim3 grid2(static_cast<unsigned>(ceil_div(Tq, 128)), Hq / 2, static_cast<unsigned>(B));
       if (D == 128) {
         if (set_smem(attn_fwd_tc2_kernel<128>, Fwd2Smem<128>::SMEM)) return ORTHRUS_ECUDA;
