@@ -46,6 +46,15 @@ __device__ __forceinline__ void store_row32_sw128(uint32_t tile_base, int r, int
                  pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
 }
 
+// Same store from 16 words that already hold the 32 values as bf16 pairs.
+__device__ __forceinline__ void store_row32_sw128_packed(uint32_t tile_base, int r, int c0, const uint32_t* w) {
+  const uint32_t box = tile_base + (c0 >> 6) * kAttnTileBytes;
+  const int chunk0 = (c0 & 63) >> 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    st_shared_v4(box + sw128_offset(r, chunk0 + q), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+}
+
 // How the columns [c0, c0 + width) of a score tile meet the visible ranges [lo, hi) of the 32 rows
 // of this warp: 0 = no row sees any of them, 1 = every row sees all of them, 2 = mixed. The answer
 // is the same in every lane, so a branch on it may hold warp-collective TMEM loads. All 32 lanes
@@ -854,6 +863,7 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* p_full = bars + 9;   // [2] per head (128 arrivals)
   uint64_t* p_empty = bars + 11; // [2] per head: PV of the head completed
   uint64_t* mma_done = bars + 13;
+  uint64_t* s_free = bars + 14;  // [2] per head: the rows loaded S (128 arrivals)
   unsigned long long* red = reinterpret_cast<unsigned long long*>(bars + 16);
   AttnTiles* tiles = reinterpret_cast<AttnTiles*>(bars + 20);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
@@ -878,6 +888,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&p_empty[i], 1);
+      mbar_init(&s_free[i], 128);
     }
     mbar_init(mma_done, 1);
     red[0] = 0;
@@ -950,8 +961,19 @@ __global__ void __launch_bounds__(320, 1)
         issue_s(1, 0);
         umma_commit(&slot_empty[0]);
       }
+      // per tile j: QK^T of tile j + 1 as soon as the rows of a head have loaded S(j) (it runs
+      // under their softmax), then P V of tile j once P(j) is in shared memory
       for (int j = 0; ok && j < nt; ++j) {
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; ok && h < 2 && j + 1 < nt; ++h) {
+          if (*abort_flag || !mbar_wait(&s_free[h], j & 1) || (h == 0 && !ring_full(2 * j + 2))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s(h, j + 1);
+          if (h == 1) umma_commit(&slot_empty[(2 * j + 2) % 3]);
+        }
+        for (int h = 0; ok && h < 2; ++h) {
           if (*abort_flag || !mbar_wait(&p_full[h], j & 1) || (h == 0 && !ring_full(2 * j + 1))) {
             ok = false;
             break;
@@ -965,15 +987,6 @@ __global__ void __launch_bounds__(320, 1)
                      (j > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&p_empty[h]);
           if (h == 1) umma_commit(&slot_empty[(2 * j + 1) % 3]);
-          if (j + 1 < nt) {
-            if (h == 0 && !ring_full(2 * j + 2)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_s(h, j + 1);
-            if (h == 1) umma_commit(&slot_empty[(2 * j + 2) % 3]);
-          }
         }
       }
       if (!ok) *abort_flag = 1;
@@ -1006,6 +1019,8 @@ __global__ void __launch_bounds__(320, 1)
       tmem_ld32(s_col + 64, s + 64);
       tmem_ld32(s_col + 96, s + 96);
       tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_free[h]);  // the MMA warp may overwrite S with the next tile's scores
       const bool src2 = j >= n1;
       const int64_t key0 = (src2 ? t2a + (j - n1) : j) * 128;
       const int64_t lo = (src2 ? s2 : 0) - key0, hi = (src2 ? e2 : e1) - key0;  // visible columns
@@ -1024,30 +1039,31 @@ __global__ void __launch_bounds__(320, 1)
       }
       const float rmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       const float tmax = rmax == -INFINITY ? -INFINITY : rmax * scale_log2;
-      // the previous P V of this head must be done before P and O are touched again
-      if (j > 0 && !mbar_wait(&p_empty[h], (j - 1) & 1)) {
-        ok = false;
-        break;
-      }
-      // raise the reference max only when the tile max exceeds it by more than the threshold;
-      // O is rescaled after P is written, when the row of S no longer occupies registers
+      // raise the reference max only when the tile max exceeds it by more than the threshold
       float alpha = 1.f;
       if (tmax > m_ref + kRescaleThreshold) {
         if (m_ref != -INFINITY) alpha = exp2f(m_ref - tmax);
         m_ref = tmax;
       }
       const float mu = m_ref == -INFINITY ? 0.f : m_ref;
+      // P = exp2(s * scale - m_ref) as bf16 pairs in registers, before any wait
       float sm[4] = {0.f, 0.f, 0.f, 0.f};  // independent chains
+      uint32_t pk[64];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float* x = s + 32 * c;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          x[i] = ex2_approx(fmaf(x[i], scale_log2, -mu));
-          sm[i & 3] += x[i];
-        }
-        store_row32_sw128(p_base, row, c * 32, x);
+      for (int i = 0; i < 128; i += 2) {
+        const float p0 = ex2_approx(fmaf(s[i], scale_log2, -mu));
+        const float p1 = ex2_approx(fmaf(s[i + 1], scale_log2, -mu));
+        sm[i & 3] += p0;
+        sm[(i + 1) & 3] += p1;
+        pk[i / 2] = pack_bf16x2(p0, p1);
       }
+      // the previous P V of this head must be done before P and O are touched again
+      if (j > 0 && !mbar_wait(&p_empty[h], (j - 1) & 1)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) store_row32_sw128_packed(p_base, row, c * 32, pk + 16 * c);
       l = fmaf(l, alpha, (sm[0] + sm[1]) + (sm[2] + sm[3]));
       if (alpha != 1.f) {
         tc_fence_after();

@@ -11,8 +11,8 @@ Cases (B = 8 rows of 2048 tokens, 16 query / 8 KV heads of 128, A = 32 anchors, 
   dual     dual-view attention forward, Tq = A*K queries over the AR prefix and own blocks
                                                                    (orthrus/objective.py:163)
   dualbwd  dual-view attention forward, then backward (dQ; dK/dV of the own-block keys)
-  lmhead   fused LM head + KL: 2048 student rows against 1400 teacher rows, V = 151936, d = 1024
-                                                                   (orthrus/objective.py:338-392)
+  lmhead   fused LM head + KL of one step: 7936 = 8 * 32 * 31 student rows against 7936 teacher
+           rows, V = 151936, d = 1024                              (orthrus/objective.py:338-392)
 """
 
 from __future__ import annotations
@@ -25,7 +25,7 @@ import torch
 from . import ops
 
 B, HQ, HKV, L, A, K, HD = 8, 16, 8, 2048, 32, 32, 128
-LM_N, LM_M, LM_V, LM_D = 2048, 1400, 151936, 1024
+LM_N, LM_M, LM_V, LM_D = B * A * (K - 1), B * A * (K - 1), 151936, 1024
 
 
 def _attention_inputs(gen, dev):
