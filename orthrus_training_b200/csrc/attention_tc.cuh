@@ -914,19 +914,22 @@ __global__ void __launch_bounds__(320, 1)
         for (int c = 0; c < S::BOXES; ++c)
           tma_load_3d(smem + S::OFF_Q + h * S::TILE + c * kAttnTileBytes, &tmQ, q_full, c * 64,
                       static_cast<int>(q0), static_cast<int>(b * Hq + 2 * pair + h));
-      // K and V tiles share a ring of three slots in the order K(0), V(0), K(1), V(1), ...: every
-      // load may start as soon as the tile two places ahead of it has been consumed
+      // K and V tiles share a ring of three slots with K one tile ahead of V: K(0), K(1), V(0),
+      // K(2), V(1), ..., V(nt - 1). A load may start once the tile three places before it in this
+      // order has been consumed, so K(j + 1) is in flight while tile j - 1 is still being read.
       int issued = 0;
       const int z = static_cast<int>(b * Hkv + hk);
       for (int idx = 0; idx < 2 * nt; ++idx) {
-        const int j = idx >> 1, slot = idx % 3, use = idx / 3;
+        const bool is_v = idx == 2 * nt - 1 || (idx > 0 && (idx & 1) == 0);
+        const int j = idx == 2 * nt - 1 ? nt - 1 : is_v ? (idx - 2) / 2 : (idx + 1) / 2;
+        const int slot = idx % 3, use = idx / 3;
         const bool src2 = j >= n1;
         const int key0 = (src2 ? t2a + (j - n1) : j) * 128;
         if (*abort_flag || !mbar_wait(&slot_empty[slot], (use & 1) ^ 1)) {
           *abort_flag = 1;
           break;
         }
-        const CUtensorMap* map = (idx & 1) ? (src2 ? &tmV2 : &tmV1) : (src2 ? &tmK2 : &tmK1);
+        const CUtensorMap* map = is_v ? (src2 ? &tmV2 : &tmV1) : (src2 ? &tmK2 : &tmK1);
         uint8_t* dst = smem + S::OFF_RING + slot * S::TILE;
         mbar_arrive_expect_tx(&slot_full[slot], S::TILE);
 #pragma unroll
@@ -943,13 +946,15 @@ __global__ void __launch_bounds__(320, 1)
     if (elect_one()) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, false, false);
       constexpr uint32_t idesc_o = umma_idesc_bf16(128, D, false, true);
-      // ring position of K(j) is 2j, of V(j) 2j + 1: slot = position % 3, use = position / 3
+      // ring positions (slot = position % 3, use = position / 3) in the producer's order
+      auto kpos = [&](int j) { return j == 0 ? 0 : 2 * j - 1; };
+      auto vpos = [&](int j) { return j == nt - 1 ? 2 * nt - 1 : 2 * j + 2; };
       auto ring = [&](int pos) { return smem_u32(smem + S::OFF_RING + (pos % 3) * S::TILE); };
       auto ring_full = [&](int pos) { return mbar_wait(&slot_full[pos % 3], (pos / 3) & 1); };
       bool ok = mbar_wait(q_full, 0) && (nt == 0 || ring_full(0));
       auto issue_s = [&](int h, int j) {
         const uint32_t q_base = smem_u32(smem + S::OFF_Q + h * S::TILE);
-        const uint32_t k_base = ring(2 * j);
+        const uint32_t k_base = ring(kpos(j));
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
           umma_f16(tmem + h * 128, desc_kmajor(q_base, kk), desc_kmajor(k_base, kk), idesc_s, kk > 0 ? 1u : 0u);
@@ -965,28 +970,28 @@ __global__ void __launch_bounds__(320, 1)
       // under their softmax), then P V of tile j once P(j) is in shared memory
       for (int j = 0; ok && j < nt; ++j) {
         for (int h = 0; ok && h < 2 && j + 1 < nt; ++h) {
-          if (*abort_flag || !mbar_wait(&s_free[h], j & 1) || (h == 0 && !ring_full(2 * j + 2))) {
+          if (*abort_flag || !mbar_wait(&s_free[h], j & 1) || (h == 0 && !ring_full(kpos(j + 1)))) {
             ok = false;
             break;
           }
           tc_fence_after();
           issue_s(h, j + 1);
-          if (h == 1) umma_commit(&slot_empty[(2 * j + 2) % 3]);
+          if (h == 1) umma_commit(&slot_empty[kpos(j + 1) % 3]);
         }
         for (int h = 0; ok && h < 2; ++h) {
-          if (*abort_flag || !mbar_wait(&p_full[h], j & 1) || (h == 0 && !ring_full(2 * j + 1))) {
+          if (*abort_flag || !mbar_wait(&p_full[h], j & 1) || (h == 0 && !ring_full(vpos(j)))) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t p_base = smem_u32(smem + S::OFF_P + h * 2 * kAttnTileBytes);
-          const uint32_t v_base = ring(2 * j + 1);
+          const uint32_t v_base = ring(vpos(j));
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
             umma_f16(tmem + 256 + h * 128, desc_kmajor(p_base, kk), desc_mnmajor(v_base, kk), idesc_o,
                      (j > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&p_empty[h]);
-          if (h == 1) umma_commit(&slot_empty[(2 * j + 1) % 3]);
+          if (h == 1) umma_commit(&slot_empty[vpos(j) % 3]);
         }
       }
       if (!ok) *abort_flag = 1;
