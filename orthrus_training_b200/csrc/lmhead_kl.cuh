@@ -36,8 +36,8 @@ struct StatsTile {
 
 __global__ void __launch_bounds__(192, 1)
     lmhead_stats_tc_kernel(const __grid_constant__ CUtensorMap tmH, const __grid_constant__ CUtensorMap tmW,
-                           int R, int V, int D, int tiles_per_split, float* __restrict__ part_m,
-                           float* __restrict__ part_s, int* __restrict__ part_i) {
+                           int R, int V, int D, int tiles_per_split, int rtiles, int units,
+                           float* __restrict__ part_m, float* __restrict__ part_s, int* __restrict__ part_i) {
   using T = StatsTile;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -51,13 +51,16 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = blockIdx.x * T::BM;
-  const int split = blockIdx.y;
   const int vtiles = (V + T::BN - 1) / T::BN;
-  const int t0 = split * tiles_per_split;
-  const int t1 = min(vtiles, t0 + tiles_per_split);
-  const int ntiles = max(t1 - t0, 0);
   const int KB = (D + T::BK - 1) / T::BK;
+  // persistent CTAs: work unit u = (row tile u % rtiles, vocabulary split u / rtiles), taken
+  // round-robin; the stage and accumulator counters run on across units
+  auto unit_tiles = [&](int u, int& row0, int& split, int& t0) {
+    row0 = (u % rtiles) * T::BM;
+    split = u / rtiles;
+    t0 = split * tiles_per_split;
+    return max(min(vtiles, t0 + tiles_per_split) - t0, 0);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < T::STAGES; ++s) {
@@ -81,19 +84,23 @@ __global__ void __launch_bounds__(192, 1)
       prefetch_tensormap(&tmH);
       prefetch_tensormap(&tmW);
       int it = 0, issued = 0;
-      for (int t = 0; t < ntiles && !*abort_flag; ++t) {
-        const int v0 = (t0 + t) * T::BN;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
-          const int s = it % T::STAGES;
-          const uint32_t ph = (it / T::STAGES) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1)) {
-            *abort_flag = 1;
-            break;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+        int row0, split, t0;
+        const int ntiles = unit_tiles(u, row0, split, t0);
+        for (int t = 0; t < ntiles && !*abort_flag; ++t) {
+          const int v0 = (t0 + t) * T::BN;
+          for (int kb = 0; kb < KB; ++kb, ++it) {
+            const int s = it % T::STAGES;
+            const uint32_t ph = (it / T::STAGES) & 1;
+            if (!mbar_wait(&empty[s], ph ^ 1)) {
+              *abort_flag = 1;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[s], T::STAGE_BYTES);
+            tma_load_2d(sA + s * T::A_BYTES, &tmH, &full[s], kb * T::BK, row0);
+            tma_load_2d(sB + s * T::B_BYTES, &tmW, &full[s], kb * T::BK, v0);
+            issued = it + 1;
           }
-          mbar_arrive_expect_tx(&full[s], T::STAGE_BYTES);
-          tma_load_2d(sA + s * T::A_BYTES, &tmH, &full[s], kb * T::BK, row0);
-          tma_load_2d(sB + s * T::B_BYTES, &tmW, &full[s], kb * T::BK, v0);
-          issued = it + 1;
         }
       }
       if (*abort_flag)
@@ -103,42 +110,50 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t idesc = umma_idesc_bf16(128, T::BN, false, false);
-      int it = 0;
-      for (int t = 0; t < ntiles && !*abort_flag; ++t) {
-        const int b = t & 1;
-        const uint32_t acc = tmem + b * T::BN;
-        if (!mbar_wait(&acc_empty[b], ((t >> 1) & 1) ^ 1)) {
-          *abort_flag = 1;
-          break;
-        }
-        tc_fence_after();
-        for (int kb = 0; kb < KB; ++kb, ++it) {
-          const int s = it % T::STAGES;
-          const uint32_t ph = (it / T::STAGES) & 1;
-          if (!mbar_wait(&full[s], ph)) {
+      int it = 0, tt = 0;  // stage counter, accumulator tile counter (across units)
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+        int row0, split, t0;
+        const int ntiles = unit_tiles(u, row0, split, t0);
+        for (int t = 0; t < ntiles && !*abort_flag; ++t, ++tt) {
+          const int b = tt & 1;
+          const uint32_t acc = tmem + b * T::BN;
+          if (!mbar_wait(&acc_empty[b], ((tt >> 1) & 1) ^ 1)) {
             *abort_flag = 1;
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + s * T::A_BYTES);
-          const uint32_t b_base = smem_u32(sB + s * T::B_BYTES);
+          for (int kb = 0; kb < KB; ++kb, ++it) {
+            const int s = it % T::STAGES;
+            const uint32_t ph = (it / T::STAGES) & 1;
+            if (!mbar_wait(&full[s], ph)) {
+              *abort_flag = 1;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(sA + s * T::A_BYTES);
+            const uint32_t b_base = smem_u32(sB + s * T::B_BYTES);
 #pragma unroll
-          for (int k = 0; k < T::BK / 16; ++k)
-            umma_f16(acc, umma_desc_sw128(a_base + k * 32, 16, 1024), umma_desc_sw128(b_base + k * 32, 16, 1024),
-                     idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          umma_commit(&empty[s]);
+            for (int k = 0; k < T::BK / 16; ++k)
+              umma_f16(acc, umma_desc_sw128(a_base + k * 32, 16, 1024), umma_desc_sw128(b_base + k * 32, 16, 1024),
+                       idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_commit(&empty[s]);
+          }
+          umma_commit(&acc_full[b]);
         }
-        umma_commit(&acc_full[b]);
       }
     }
   } else {
     const int quarter = warp & 3;
+    int tt = 0;
+    for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+    int row0, split, t0;
+    const int ntiles = unit_tiles(u, row0, split, t0);
     const int row = row0 + quarter * 32 + lane;
     float m = -INFINITY, s = 0.f;
     int idx = 0;
-    for (int t = 0; t < ntiles; ++t) {
-      const int b = t & 1;
-      if (*abort_flag || !mbar_wait(&acc_full[b], (t >> 1) & 1)) {
+    for (int t = 0; t < ntiles; ++t, ++tt) {
+      const int b = tt & 1;
+      if (*abort_flag || !mbar_wait(&acc_full[b], (tt >> 1) & 1)) {
         *abort_flag = 1;
         break;
       }
@@ -200,6 +215,7 @@ __global__ void __launch_bounds__(192, 1)
       part_s[static_cast<int64_t>(split) * R + row] = s;
       part_i[static_cast<int64_t>(split) * R + row] = idx;
     }
+    }
   }
   __syncthreads();
   if (warp == 1) {
@@ -250,7 +266,7 @@ struct DiffTile {
 __global__ void __launch_bounds__(192, 1)
     lmhead_diff_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmT,
                           const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmD,
-                          int rows, int c0, int V, int D, int tiles_per_split,
+                          int rows, int c0, int V, int D, int tiles_per_split, int rtiles, int units,
                           const float* __restrict__ lse_s, const float* __restrict__ lse_t_rows,
                           const float* __restrict__ row_weight, float* __restrict__ kl_part) {
   using T = DiffTile;
@@ -268,13 +284,16 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rt0 = blockIdx.x * T::BM;  // row offset inside the chunk
-  const int split = blockIdx.y;
   const int vtiles = (V + T::BN - 1) / T::BN;
-  const int t0 = split * tiles_per_split;
-  const int t1 = min(vtiles, t0 + tiles_per_split);
-  const int ntiles = max(t1 - t0, 0);
   const int KB = (D + T::BK - 1) / T::BK;
+  // persistent CTAs: work unit u = (row tile u % rtiles, vocabulary split u / rtiles), taken
+  // round-robin; stage, accumulator and staging-buffer counters run on across units
+  auto unit_tiles = [&](int u, int& rt0, int& split, int& t0) {
+    rt0 = (u % rtiles) * T::BM;  // row offset inside the chunk
+    split = u / rtiles;
+    t0 = split * tiles_per_split;
+    return max(min(vtiles, t0 + tiles_per_split) - t0, 0);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < T::STAGES; ++s) {
@@ -301,21 +320,25 @@ __global__ void __launch_bounds__(192, 1)
       prefetch_tensormap(&tmT);
       prefetch_tensormap(&tmW);
       int it = 0, issued = 0;
-      for (int t = 0; t < ntiles && !*abort_flag; ++t) {
-        const int v0 = (t0 + t) * T::BN;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
-          const int s = it % T::STAGES;
-          const uint32_t ph = (it / T::STAGES) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1)) {
-            *abort_flag = 1;
-            break;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+        int rt0, split, t0;
+        const int ntiles = unit_tiles(u, rt0, split, t0);
+        for (int t = 0; t < ntiles && !*abort_flag; ++t) {
+          const int v0 = (t0 + t) * T::BN;
+          for (int kb = 0; kb < KB; ++kb, ++it) {
+            const int s = it % T::STAGES;
+            const uint32_t ph = (it / T::STAGES) & 1;
+            if (!mbar_wait(&empty[s], ph ^ 1)) {
+              *abort_flag = 1;
+              break;
+            }
+            uint8_t* st = stages + s * T::STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[s], T::STAGE_BYTES);
+            tma_load_2d(st, &tmS, &full[s], kb * T::BK, c0 + rt0);
+            tma_load_2d(st + T::T_BYTES, &tmT, &full[s], kb * T::BK, c0 + rt0);
+            tma_load_2d(st + 2 * T::T_BYTES, &tmW, &full[s], kb * T::BK, v0);
+            issued = it + 1;
           }
-          uint8_t* st = stages + s * T::STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[s], T::STAGE_BYTES);
-          tma_load_2d(st, &tmS, &full[s], kb * T::BK, c0 + rt0);
-          tma_load_2d(st + T::T_BYTES, &tmT, &full[s], kb * T::BK, c0 + rt0);
-          tma_load_2d(st + 2 * T::T_BYTES, &tmW, &full[s], kb * T::BK, v0);
-          issued = it + 1;
         }
       }
       if (*abort_flag)
@@ -325,11 +348,14 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t idesc = umma_idesc_bf16(128, T::BN, false, false);
-      int it = 0;
-      for (int t = 0; t < ntiles && !*abort_flag; ++t) {
-        const int b = t & 1;
+      int it = 0, tt = 0;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+      int rt0, split, t0;
+      const int ntiles = unit_tiles(u, rt0, split, t0);
+      for (int t = 0; t < ntiles && !*abort_flag; ++t, ++tt) {
+        const int b = tt & 1;
         const uint32_t acc_s = tmem + b * 256, acc_t = acc_s + 128;
-        if (!mbar_wait(&acc_empty[b], ((t >> 1) & 1) ^ 1)) {
+        if (!mbar_wait(&acc_empty[b], ((tt >> 1) & 1) ^ 1)) {
           *abort_flag = 1;
           break;
         }
@@ -354,26 +380,31 @@ __global__ void __launch_bounds__(192, 1)
         }
         umma_commit(&acc_full[b]);
       }
+      }
     }
   } else {
     const int quarter = warp & 3;
     const int lrow = quarter * 32 + lane;  // row inside the tile (TMEM lane)
+    const bool leader = (threadIdx.x == 64);
+    int tt = 0;
+    for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+    int rt0, split, t0;
+    const int ntiles = unit_tiles(u, rt0, split, t0);
     const int crow = rt0 + lrow;           // row inside the chunk
     const bool live = crow < rows;
     const float ls_off = live ? lse_s[c0 + crow] : 0.f;
     const float lt_off = live ? lse_t_rows[c0 + crow] : 0.f;
     const float w = (live && row_weight != nullptr) ? row_weight[c0 + crow] : 1.f;
-    const bool leader = (threadIdx.x == 64);
     float kl = 0.f;
-    for (int t = 0; t < ntiles; ++t) {
-      const int b = t & 1;
-      if (*abort_flag || !mbar_wait(&acc_full[b], (t >> 1) & 1)) {
+    for (int t = 0; t < ntiles; ++t, ++tt) {
+      const int b = tt & 1;
+      if (*abort_flag || !mbar_wait(&acc_full[b], (tt >> 1) & 1)) {
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
       // The staging buffer of this tile was last stored two tiles ago: wait until TMA read it.
-      if (!mbar_wait(&freed[b], ((t >> 1) & 1) ^ 1)) {
+      if (!mbar_wait(&freed[b], ((tt >> 1) & 1) ^ 1)) {
         *abort_flag = 1;
         break;
       }
@@ -420,7 +451,7 @@ __global__ void __launch_bounds__(192, 1)
       fence_proxy_async_smem();
       mbar_arrive(&staged[b]);
       if (leader) {
-        if (!mbar_wait(&staged[b], (t >> 1) & 1)) {
+        if (!mbar_wait(&staged[b], (tt >> 1) & 1)) {
           *abort_flag = 1;
           break;
         }
@@ -429,11 +460,12 @@ __global__ void __launch_bounds__(192, 1)
         tma_store_commit();
         // at most the store just issued may still be reading: the other buffer is free again
         asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-        if (t >= 1) mbar_arrive(&freed[b ^ 1]);
+        if (tt >= 1) mbar_arrive(&freed[b ^ 1]);
       }
     }
-    if (leader) tma_store_wait_all();
     if (live) kl_part[static_cast<int64_t>(split) * rows + crow] = kl;
+    }
+    if (leader) tma_store_wait_all();
   }
   __syncthreads();
   if (warp == 1) {
@@ -670,6 +702,25 @@ struct LmheadPlan {
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Vocabulary splits for a persistent grid of `sms` CTAs over rtiles x splits work units: the
+// smallest split count (at most max_splits) whose units fill the last round of CTAs to within 1 %
+// of the best achievable, so no SM idles through a partial last round.
+inline int pick_splits(int64_t rtiles, int64_t vtiles, int sms, int max_splits) {
+  const int hi = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(vtiles, max_splits)));
+  auto eff = [&](int s) {
+    const int64_t tps = ceil_div(vtiles, s), actual = ceil_div(vtiles, tps);
+    const int64_t units = rtiles * actual;
+    return static_cast<double>(units) / static_cast<double>(ceil_div(units, sms) * sms);
+  };
+  double best = 0.0;
+  for (int s = 1; s <= hi; ++s) best = std::max(best, eff(s));
+  for (int s = 1; s <= hi; ++s)
+    if (eff(s) >= best - 0.01) return s;
+  return hi;
+}
+
+constexpr int kLmheadMaxSplits = 64;
+
 inline LmheadPlan lmhead_plan(int64_t n, int64_t m, int64_t V, int64_t D, int64_t chunk_rows, int dtype) {
   LmheadPlan p{};
   p.n = n;
@@ -685,10 +736,8 @@ inline LmheadPlan lmhead_plan(int64_t n, int64_t m, int64_t V, int64_t D, int64_
   const int64_t R = n + m;
   const int sms = num_sms();
   if (dtype == ORTHRUS_BF16) {
-    const int64_t rtiles = ceil_div(R, 128), vt = ceil_div(V, 256);
-    p.stats_splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(vt, ceil_div(2 * sms, rtiles))));
-    const int64_t ctiles = ceil_div(chunk, 128), vt2 = ceil_div(V, 128);
-    p.diff_splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(vt2, ceil_div(sms, ctiles))));
+    p.stats_splits = pick_splits(ceil_div(R, 128), ceil_div(V, 256), sms, kLmheadMaxSplits);
+    p.diff_splits = kLmheadMaxSplits;  // workspace bound; each chunk picks its own count
   } else {
     const int64_t rtiles = ceil_div(R, 64), vt = ceil_div(V, 64);
     p.stats_splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(vt, ceil_div(4 * sms, rtiles))));
@@ -771,10 +820,13 @@ int lmhead_kl_fwd_impl(const T* student, int64_t n, const T* teacher, int64_t m,
     const int vt = static_cast<int>(ceil_div(V, 256));
     const int tps = static_cast<int>(ceil_div(vt, p.stats_splits));
     const int splits = static_cast<int>(ceil_div(vt, tps));
+    const int rtiles = static_cast<int>(ceil_div(R, 128));
+    const int units = rtiles * splits;
     ORTHRUS_CHECK_CUDA(ensure_smem(lmhead_stats_tc_kernel, StatsTile::SMEM));
-    dim3 grid(static_cast<unsigned>(ceil_div(R, 128)), splits);
+    const unsigned grid = static_cast<unsigned>(std::min(units, num_sms()));  // persistent, one CTA per SM
     lmhead_stats_tc_kernel<<<grid, 192, StatsTile::SMEM, stream>>>(tmH, tmW, static_cast<int>(R), static_cast<int>(V),
-                                                                   static_cast<int>(D), tps, pm, ps, pi);
+                                                                   static_cast<int>(D), tps, rtiles, units, pm, ps,
+                                                                   pi);
     ORTHRUS_CHECK_LAUNCH();
     lmhead_stats_combine_kernel<<<static_cast<unsigned>(ceil_div(R, 256)), 256, 0, stream>>>(
         pm, ps, pi, static_cast<int>(R), splits, lse, amax);
@@ -805,13 +857,15 @@ int lmhead_kl_fwd_impl(const T* student, int64_t n, const T* teacher, int64_t m,
       if (!make_tmap_2d_bf16(&tmW, weight, D, V, D, 64, 128)) return ORTHRUS_ECUDA;
       if (!make_tmap_2d_bf16(&tmD, diff, V, rows, Vp, 64, 128)) return ORTHRUS_ECUDA;
       const int vt = static_cast<int>(ceil_div(V, 128));
-      const int tps = static_cast<int>(ceil_div(vt, p.diff_splits));
+      const int rtiles = static_cast<int>(ceil_div(rows, 128));
+      const int tps = static_cast<int>(ceil_div(vt, pick_splits(rtiles, vt, num_sms(), p.diff_splits)));
       splits = static_cast<int>(ceil_div(vt, tps));
+      const int units = rtiles * splits;
       ORTHRUS_CHECK_CUDA(ensure_smem(lmhead_diff_tc_kernel, DiffTile::SMEM));
-      dim3 grid(static_cast<unsigned>(ceil_div(rows, 128)), splits);
+      const unsigned grid = static_cast<unsigned>(std::min(units, num_sms()));  // persistent, one CTA per SM
       lmhead_diff_tc_kernel<<<grid, 192, DiffTile::SMEM, stream>>>(tmS, tmT, tmW, tmD, rows, static_cast<int>(c0),
                                                                    static_cast<int>(V), static_cast<int>(D), tps,
-                                                                   lse, lset, row_weight, klp);
+                                                                   rtiles, units, lse, lset, row_weight, klp);
       ORTHRUS_CHECK_LAUNCH();
     } else {
       const int vt = static_cast<int>(ceil_div(V, 64));
