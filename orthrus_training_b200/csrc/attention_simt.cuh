@@ -160,6 +160,32 @@ __global__ void attn_delta_kernel(const T* __restrict__ o, const T* __restrict__
   if (lane == 0) delta[(b * Hq + h) * Tq + t] = acc;
 }
 
+// Same delta for bf16 rows of 128: 16 lanes per (b, t, h) item, one 16-byte load of O and of dO
+// per lane, then a fixed butterfly over the 16 lanes. 256 threads = 16 items per block.
+__global__ void attn_delta128_bf16_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
+                                          int64_t B, int Hq, int64_t Tq, float* __restrict__ delta) {
+  const int sub = threadIdx.x & 15;
+  const int64_t item = static_cast<int64_t>(blockIdx.x) * 16 + (threadIdx.x >> 4);  // (b, t, h)
+  const bool live = item < B * Tq * Hq;
+  const int64_t it = live ? item : 0;
+  const uint4 a = *reinterpret_cast<const uint4*>(o + it * 128 + sub * 8);
+  const uint4 g = *reinterpret_cast<const uint4*>(dout + it * 128 + sub * 8);
+  const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, gw[4] = {g.x, g.y, g.z, g.w};
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    acc = fmaf(__uint_as_float(aw[i] << 16), __uint_as_float(gw[i] << 16), acc);
+    acc = fmaf(__uint_as_float(aw[i] & 0xffff0000u), __uint_as_float(gw[i] & 0xffff0000u), acc);
+  }
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (live && sub == 0) {
+    const int h = static_cast<int>(item % Hq);
+    const int64_t bt = item / Hq;
+    delta[(bt / Tq * Hq + h) * Tq + bt % Tq] = acc;
+  }
+}
+
 // dQ for every query (all visible keys of both sources), fp32 out [B, Hq, Tq, D].
 template <typename T>
 __global__ void __launch_bounds__(32 * kSimtQ) attn_dq_simt_kernel(

@@ -306,7 +306,10 @@ int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h,
   const int64_t items = B * Tq * Hq;
   const bool tc = use_tensor_cores(dtype, hd, D, ORTHRUS_MASK_DUAL, nullptr) && (128 % block == 0) &&
                   (Hq / Hkv) <= DkvSmem<128>::MAX_GROUP;
-  if (dtype == ORTHRUS_BF16) {
+  if (dtype == ORTHRUS_BF16 && hd == 128 && aligned16(o) && aligned16(do_)) {
+    attn_delta128_bf16_kernel<<<static_cast<unsigned>(ceil_div(items, 16)), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(do_), B, Hq, Tq, delta);
+  } else if (dtype == ORTHRUS_BF16) {
     using T = __nv_bfloat16;
     attn_delta_kernel<T><<<static_cast<unsigned>(ceil_div(items, 8)), 256, 0, st>>>(
         static_cast<const T*>(o), static_cast<const T*>(do_), B, Hq, Tq, hd, delta);

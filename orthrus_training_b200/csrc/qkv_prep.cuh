@@ -312,77 +312,77 @@ __device__ __forceinline__ void rope_lane_table(float pos, const float* __restri
   }
 }
 
-// One warp per token row (8 rows per CTA), no shared memory: every lane builds the RoPE table of
-// its own elements, then the warp walks the row's heads PER at a time, all PER head rows loaded
-// before any is computed. Lane l holds the elements [l * NE, l * NE + NE) of a head as one vector
-// access. Requires 16-byte aligned tensors and D % 8 == 0 (checked by the host).
+// One warp per token row, 8 rows per CTA. Lane 0 of each warp pulls the row's q|k|v slice (all
+// heads, heads * HD elements) into shared memory with one bulk async copy, so a CTA has 8 rows in
+// flight at once whatever the register budget; meanwhile every lane builds the RoPE table of its
+// own elements in registers. The warp then walks the heads from shared memory (lane l owns the
+// elements [l * NE, l * NE + NE) of a head) and writes q / k / v with vector stores.
+// Requires 16-byte aligned tensors and D % 8 == 0 (checked by the host); dynamic shared memory
+// 8 * heads * HD * sizeof(T) + 64 bytes.
 template <typename T, int HD>
-__global__ void __launch_bounds__(256, 4) qkv_prep_fwd_row_kernel(
+__global__ void __launch_bounds__(256) qkv_prep_fwd_row_kernel(
     const T* __restrict__ qkv, const int64_t* __restrict__ positions, const float* __restrict__ inv_freq,
     const T* __restrict__ q_norm_w, const T* __restrict__ k_norm_w, int64_t rows, int64_t Tn, int Hq, int Hkv,
     int D, float eps, T* __restrict__ q_out, T* __restrict__ k_out, T* __restrict__ v_out, int64_t cap,
     const int32_t* __restrict__ offset, float* __restrict__ rstd_out) {
   constexpr int NE = HD / 32;
   constexpr int HALF = HD / 2;
-  constexpr int PER = HD == 128 ? 4 : 8;  // head rows in flight per warp within 64 registers
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const int64_t b = row / Tn, t = row % Tn;
+  extern __shared__ __align__(128) uint8_t prep_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int heads = Hq + 2 * Hkv;
-  const T* xrow = qkv + row * static_cast<int64_t>(heads) * HD;
-  float v[PER][NE];
-#pragma unroll
-  for (int j = 0; j < PER; ++j)
-    if (j < heads) load_elems<T, NE>(xrow + j * HD + lane * NE, v[j]);
+  const uint32_t row_bytes = static_cast<uint32_t>(heads) * HD * sizeof(T);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(prep_smem);
+  T* xs = reinterpret_cast<T*>(prep_smem + 64 + warp * row_bytes);
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  if (row >= rows) return;
+  if (lane == 0) {
+    mbar_init(&bars[warp], 1);
+    fence_barrier_init();
+    mbar_arrive_expect_tx(&bars[warp], row_bytes);
+    bulk_load(xs, qkv + row * static_cast<int64_t>(heads) * HD, row_bytes, &bars[warp]);
+  }
+  const int64_t b = row / Tn, t = row % Tn;
   float cs[NE], sn[NE], wq[NE], wk[NE];
   rope_lane_table<T, HD>(static_cast<float>(positions[row]), inv_freq, lane, cs, sn);
   load_elems<T, NE>(q_norm_w + lane * NE, wq);
   load_elems<T, NE>(k_norm_w + lane * NE, wk);
   const int64_t orow_kv = (offset ? offset[b] : 0) + t;
-  for (int h0 = 0; h0 < heads; h0 += PER) {
-    if (h0 > 0) {
+  __syncwarp();
+  if (!mbar_wait(&bars[warp], 0)) {  // error recorded: drain the copy (bounded) and leave the row
+    mbar_wait_short(&bars[warp], 0);
+    return;
+  }
+  for (int head = 0; head < heads; ++head) {
+    float x[NE];
+    load_elems<T, NE>(xs + head * HD + lane * NE, x);
+    T* dst;
+    if (head >= Hq + Hkv) {
+      dst = v_out + ((b * Hkv + (head - Hq - Hkv)) * cap + orow_kv) * D;
+    } else {
+      const bool is_q = head < Hq;
+      float ss = 0.f;
 #pragma unroll
-      for (int j = 0; j < PER; ++j)
-        if (h0 + j < heads) load_elems<T, NE>(xrow + (h0 + j) * HD + lane * NE, v[j]);
-    }
+      for (int k = 0; k < NE; ++k) ss = fmaf(x[k], x[k], ss);
 #pragma unroll
-    for (int j = 0; j < PER; ++j) {
-      const int head = h0 + j;  // warp-uniform
-      if (head >= heads) break;
-      float* x = v[j];
-      T* dst;
-      if (head >= Hq + Hkv) {
-        dst = v_out + ((b * Hkv + (head - Hq - Hkv)) * cap + orow_kv) * D;
-      } else {
-        const bool is_q = head < Hq;
-        float ss = 0.f;
+      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      const float rstd = rsqrtf(ss / static_cast<float>(HD) + eps);
 #pragma unroll
-        for (int k = 0; k < NE; ++k) ss = fmaf(x[k], x[k], ss);
+      for (int k = 0; k < NE; ++k) x[k] = round_to<T>((is_q ? wq[k] : wk[k]) * round_to<T>(x[k] * rstd));
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-        const float rstd = rsqrtf(ss / static_cast<float>(HD) + eps);
-#pragma unroll
-        for (int k = 0; k < NE; ++k) x[k] = round_to<T>((is_q ? wq[k] : wk[k]) * round_to<T>(x[k] * rstd));
-#pragma unroll
-        for (int k = 0; k < NE; ++k) {
-          const float partner = __shfl_xor_sync(0xffffffffu, x[k], 16);
-          const float rot = (lane * NE + k) < HALF ? -partner : partner;
-          x[k] = x[k] * cs[k] + rot * sn[k];
-        }
-        if (rstd_out != nullptr && lane == 0) rstd_out[row * (Hq + Hkv) + head] = rstd;
-        dst = is_q ? q_out + ((b * Hq + head) * Tn + t) * D
-                   : k_out + ((b * Hkv + (head - Hq)) * cap + orow_kv) * D;
+      for (int k = 0; k < NE; ++k) {
+        const float partner = __shfl_xor_sync(0xffffffffu, x[k], 16);
+        const float rot = (lane * NE + k) < HALF ? -partner : partner;
+        x[k] = x[k] * cs[k] + rot * sn[k];
       }
-      store_elems<T, NE>(dst + lane * NE, x);
-      for (int e = HD + lane; e < D; e += 32) dst[e] = from_f32<T>(0.f);
+      if (rstd_out != nullptr && lane == 0) rstd_out[row * (Hq + Hkv) + head] = rstd;
+      dst = is_q ? q_out + ((b * Hq + head) * Tn + t) * D
+                 : k_out + ((b * Hkv + (head - Hq)) * cap + orow_kv) * D;
     }
+    store_elems<T, NE>(dst + lane * NE, x);
+    for (int e = HD + lane; e < D; e += 32) dst[e] = from_f32<T>(0.f);
   }
 }
 
-// Backward of the row prologue (training layout: offset 0, cap = T). Fixed grid of kPrepBwdBlocks
-// CTAs, rows strided over the CTAs, heads over the warps in a fixed order, so the norm-weight
-// gradient partials part_q / part_k [block][HD] are deterministic.
 template <typename T, int HD>
 __global__ void __launch_bounds__(256, 3) qkv_prep_bwd_row_kernel(
     const T* __restrict__ qkv, const int64_t* __restrict__ positions, const float* __restrict__ inv_freq,
@@ -492,18 +492,24 @@ int qkv_prep_fwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
   ORTHRUS_CHECK_ARG(hd >= 2 && hd % 2 == 0 && hd <= 128 && D >= hd && D <= 128 && cap >= Tn);
   // the row kernel makes vector accesses: 16-byte aligned tensors and rows of D % 8 == 0 elements
   const bool vec_ok = D % 8 == 0 && aligned16(qkv) && aligned16(qw) && aligned16(kw) && aligned16(q_out) &&
-                      aligned16(k_out) && aligned16(v_out);
+                      aligned16(k_out) && aligned16(v_out) &&
+                      64 + 8 * (Hq + 2 * Hkv) * hd * static_cast<int>(sizeof(T)) <= 227 * 1024;
   if (vec_ok && (hd == 128 || hd == 64 || hd == 32)) {
     const int64_t rows = B * Tn;
     const unsigned grid = static_cast<unsigned>(ceil_div(rows, 8));  // one warp per row
+    const int smem = 64 + 8 * (Hq + 2 * Hkv) * hd * static_cast<int>(sizeof(T));
+    cudaError_t e = hd == 128  ? ensure_smem(qkv_prep_fwd_row_kernel<T, 128>, smem)
+                    : hd == 64 ? ensure_smem(qkv_prep_fwd_row_kernel<T, 64>, smem)
+                               : ensure_smem(qkv_prep_fwd_row_kernel<T, 32>, smem);
+    ORTHRUS_CHECK_CUDA(e);
     if (hd == 128)
-      qkv_prep_fwd_row_kernel<T, 128><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
+      qkv_prep_fwd_row_kernel<T, 128><<<grid, 256, smem, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
                                                                q_out, k_out, v_out, cap, offset, rstd);
     else if (hd == 64)
-      qkv_prep_fwd_row_kernel<T, 64><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
+      qkv_prep_fwd_row_kernel<T, 64><<<grid, 256, smem, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
                                                               q_out, k_out, v_out, cap, offset, rstd);
     else
-      qkv_prep_fwd_row_kernel<T, 32><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
+      qkv_prep_fwd_row_kernel<T, 32><<<grid, 256, smem, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
                                                               q_out, k_out, v_out, cap, offset, rstd);
     ORTHRUS_CHECK_LAUNCH();
     return ORTHRUS_OK;
