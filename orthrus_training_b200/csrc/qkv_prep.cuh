@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, c
   if (rstd_out != nullptr && lane == 0) rstd_out[r] = rstd;
 }
 
-constexpr int kPrepBwdBlocks = 148;  // fixed grid (one CTA per B200 SM): a deterministic split of the items
+constexpr int kPrepBwdBlocks = 444;  // fixed grid (3 x 148, one wave): a deterministic split of the items
 
 // ------------------------------------------------------------------------------------------------
 // Row-parallel prologue for head dims 32 / 64 / 128: one CTA per token row computes the row's
@@ -312,84 +312,79 @@ __device__ __forceinline__ void rope_lane_table(float pos, const float* __restri
   }
 }
 
-// One warp per token row, 8 rows per CTA. Lane 0 of each warp pulls the row's q|k|v slice (all
-// heads, heads * HD elements) into shared memory with one bulk async copy, so a CTA has 8 rows in
-// flight at once whatever the register budget; meanwhile every lane builds the RoPE table of its
-// own elements in registers. The warp then walks the heads from shared memory (lane l owns the
-// elements [l * NE, l * NE + NE) of a head) and writes q / k / v with vector stores.
-// Requires 16-byte aligned tensors and D % 8 == 0 (checked by the host); dynamic shared memory
-// 8 * heads * HD * sizeof(T) + 64 bytes.
+// One warp per token row (8 rows per CTA), no shared memory: every lane builds the RoPE table of
+// its own elements, then the warp walks the row's heads PER at a time, all PER head rows loaded
+// before any is computed. Lane l holds the elements [l * NE, l * NE + NE) of a head as one vector
+// access. Requires 16-byte aligned tensors and D % 8 == 0 (checked by the host).
 template <typename T, int HD>
-__global__ void __launch_bounds__(256) qkv_prep_fwd_row_kernel(
+__global__ void __launch_bounds__(256, 4) qkv_prep_fwd_row_kernel(
     const T* __restrict__ qkv, const int64_t* __restrict__ positions, const float* __restrict__ inv_freq,
     const T* __restrict__ q_norm_w, const T* __restrict__ k_norm_w, int64_t rows, int64_t Tn, int Hq, int Hkv,
     int D, float eps, T* __restrict__ q_out, T* __restrict__ k_out, T* __restrict__ v_out, int64_t cap,
     const int32_t* __restrict__ offset, float* __restrict__ rstd_out) {
   constexpr int NE = HD / 32;
   constexpr int HALF = HD / 2;
-  extern __shared__ __align__(128) uint8_t prep_smem[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int heads = Hq + 2 * Hkv;
-  const uint32_t row_bytes = static_cast<uint32_t>(heads) * HD * sizeof(T);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(prep_smem);
-  T* xs = reinterpret_cast<T*>(prep_smem + 64 + warp * row_bytes);
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  constexpr int PER = HD == 128 ? 4 : 8;  // head rows in flight per warp within 64 registers
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
-  if (lane == 0) {
-    mbar_init(&bars[warp], 1);
-    fence_barrier_init();
-    mbar_arrive_expect_tx(&bars[warp], row_bytes);
-    bulk_load(xs, qkv + row * static_cast<int64_t>(heads) * HD, row_bytes, &bars[warp]);
-  }
   const int64_t b = row / Tn, t = row % Tn;
+  const int heads = Hq + 2 * Hkv;
+  const T* xrow = qkv + row * static_cast<int64_t>(heads) * HD;
+  float v[PER][NE];
+#pragma unroll
+  for (int j = 0; j < PER; ++j)
+    if (j < heads) load_elems<T, NE>(xrow + j * HD + lane * NE, v[j]);
   float cs[NE], sn[NE], wq[NE], wk[NE];
   rope_lane_table<T, HD>(static_cast<float>(positions[row]), inv_freq, lane, cs, sn);
   load_elems<T, NE>(q_norm_w + lane * NE, wq);
   load_elems<T, NE>(k_norm_w + lane * NE, wk);
   const int64_t orow_kv = (offset ? offset[b] : 0) + t;
-  __syncwarp();
-  if (!mbar_wait(&bars[warp], 0)) {  // error recorded: drain the copy (bounded) and leave the row
-    mbar_wait_short(&bars[warp], 0);
-    return;
-  }
-  for (int head = 0; head < heads; ++head) {
-    float x[NE];
-    load_elems<T, NE>(xs + head * HD + lane * NE, x);
-    T* dst;
-    if (head >= Hq + Hkv) {
-      dst = v_out + ((b * Hkv + (head - Hq - Hkv)) * cap + orow_kv) * D;
-    } else {
-      const bool is_q = head < Hq;
-      float ss = 0.f;
+  for (int h0 = 0; h0 < heads; h0 += PER) {
+    if (h0 > 0) {
 #pragma unroll
-      for (int k = 0; k < NE; ++k) ss = fmaf(x[k], x[k], ss);
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-      const float rstd = rsqrtf(ss / static_cast<float>(HD) + eps);
-#pragma unroll
-      for (int k = 0; k < NE; ++k) x[k] = round_to<T>((is_q ? wq[k] : wk[k]) * round_to<T>(x[k] * rstd));
-#pragma unroll
-      for (int k = 0; k < NE; ++k) {
-        const float partner = __shfl_xor_sync(0xffffffffu, x[k], 16);
-        const float rot = (lane * NE + k) < HALF ? -partner : partner;
-        x[k] = x[k] * cs[k] + rot * sn[k];
-      }
-      if (rstd_out != nullptr && lane == 0) rstd_out[row * (Hq + Hkv) + head] = rstd;
-      dst = is_q ? q_out + ((b * Hq + head) * Tn + t) * D
-                 : k_out + ((b * Hkv + (head - Hq)) * cap + orow_kv) * D;
+      for (int j = 0; j < PER; ++j)
+        if (h0 + j < heads) load_elems<T, NE>(xrow + (h0 + j) * HD + lane * NE, v[j]);
     }
-    store_elems<T, NE>(dst + lane * NE, x);
-    for (int e = HD + lane; e < D; e += 32) dst[e] = from_f32<T>(0.f);
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int head = h0 + j;  // warp-uniform
+      if (head >= heads) break;
+      float* x = v[j];
+      T* dst;
+      if (head >= Hq + Hkv) {
+        dst = v_out + ((b * Hkv + (head - Hq - Hkv)) * cap + orow_kv) * D;
+      } else {
+        const bool is_q = head < Hq;
+        float ss = 0.f;
+#pragma unroll
+        for (int k = 0; k < NE; ++k) ss = fmaf(x[k], x[k], ss);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        const float rstd = rsqrtf(ss / static_cast<float>(HD) + eps);
+#pragma unroll
+        for (int k = 0; k < NE; ++k) x[k] = round_to<T>((is_q ? wq[k] : wk[k]) * round_to<T>(x[k] * rstd));
+#pragma unroll
+        for (int k = 0; k < NE; ++k) {
+          const float partner = __shfl_xor_sync(0xffffffffu, x[k], 16);
+          const float rot = (lane * NE + k) < HALF ? -partner : partner;
+          x[k] = x[k] * cs[k] + rot * sn[k];
+        }
+        if (rstd_out != nullptr && lane == 0) rstd_out[row * (Hq + Hkv) + head] = rstd;
+        dst = is_q ? q_out + ((b * Hq + head) * Tn + t) * D
+                   : k_out + ((b * Hkv + (head - Hq)) * cap + orow_kv) * D;
+      }
+      store_elems<T, NE>(dst + lane * NE, x);
+      for (int e = HD + lane; e < D; e += 32) dst[e] = from_f32<T>(0.f);
+    }
   }
 }
 
-// One warp per token row, rows strided over a fixed grid of kPrepBwdBlocks CTAs in a fixed order
-// (deterministic norm-weight partials). For each row the warp pulls, with bulk async copies, the
-// q|k|v input row and the fp32 incoming gradient of every head into its own shared-memory slice,
-// builds the RoPE table of its elements in registers meanwhile, then computes every head from
-// shared memory. Dynamic shared memory: 64 + 8 * heads * HD * (sizeof(T) + 4) bytes.
+// Backward of the row prologue (training layout: offset 0, cap = T). Fixed grid of kPrepBwdBlocks
+// CTAs, rows strided over the CTAs, heads over the warps in a fixed order, so the norm-weight
+// gradient partials part_q / part_k [block][HD] are deterministic.
 template <typename T, int HD>
-__global__ void __launch_bounds__(256, 1) qkv_prep_bwd_row_kernel(
+__global__ void __launch_bounds__(256, 3) qkv_prep_bwd_row_kernel(
     const T* __restrict__ qkv, const int64_t* __restrict__ positions, const float* __restrict__ inv_freq,
     const T* __restrict__ q_norm_w, const T* __restrict__ k_norm_w, const float* __restrict__ rstd,
     const float* __restrict__ dq, const float* __restrict__ dk, const float* __restrict__ dv, int64_t rows,
@@ -397,99 +392,78 @@ __global__ void __launch_bounds__(256, 1) qkv_prep_bwd_row_kernel(
     float* __restrict__ part_k) {
   constexpr int NE = HD / 32;
   constexpr int HALF = HD / 2;
-  extern __shared__ __align__(128) uint8_t prep_smem[];
+  constexpr int PER = HD == 128 ? 2 : 4;  // head rows in flight per warp within 80 registers
   __shared__ float wpart[2][8][HD];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int heads = Hq + 2 * Hkv;
-  const uint32_t xbytes = static_cast<uint32_t>(heads) * HD * sizeof(T);
-  const uint32_t gbytes = HD * 4;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(prep_smem) + warp;
-  T* xs = reinterpret_cast<T*>(prep_smem + 64 + warp * (xbytes + heads * gbytes));
-  float* gs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + xbytes);
-  const bool need_x = dq != nullptr || dk != nullptr;
-  uint32_t total = need_x ? xbytes : 0;
-  for (int head = 0; head < heads; ++head) {
-    const float* gsrc = head >= Hq + Hkv ? dv : head < Hq ? dq : dk;
-    if (gsrc != nullptr) total += gbytes;
-  }
   float wq[NE], wk[NE], nq[NE], nk[NE];
 #pragma unroll
   for (int k = 0; k < NE; ++k) wq[k] = wk[k] = 0.f;
   load_elems<T, NE>(q_norm_w + lane * NE, nq);
   load_elems<T, NE>(k_norm_w + lane * NE, nk);
-  if (lane == 0) {
-    mbar_init(bar, 1);
-    fence_barrier_init();
-  }
-  __syncwarp();
-  bool ok = true;
-  int iter = 0;
-  for (int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp; ok && row < rows;
-       row += static_cast<int64_t>(gridDim.x) * 8, ++iter) {
+  // one warp per row; rows strided over the fixed grid in a fixed order (deterministic partials)
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp; row < rows;
+       row += static_cast<int64_t>(gridDim.x) * 8) {
     const int64_t b = row / Tn, t = row % Tn;
-    if (total > 0) {
-      if (lane == 0) {
-        mbar_arrive_expect_tx(bar, total);
-        if (need_x) bulk_load(xs, qkv + row * static_cast<int64_t>(heads) * HD, xbytes, bar);
-      }
-      __syncwarp();
-      for (int head = lane; head < heads; head += 32) {
+    float cs[NE], sn[NE];
+    rope_lane_table<T, HD>(static_cast<float>(positions[row]), inv_freq, lane, cs, sn);
+    for (int h0 = 0; h0 < heads; h0 += PER) {
+      // loads of up to PER heads first: the incoming gradient and, for q / k, the input row
+      float gv[PER][NE], xv[PER][NE], rr[PER];
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        const int head = h0 + j;
+        rr[j] = 0.f;
+        if (head >= heads) continue;
         const bool is_v = head >= Hq + Hkv, is_q = head < Hq;
         const int h = is_v ? head - Hq - Hkv : is_q ? head : head - Hq;
         const float* gsrc = is_v ? dv : is_q ? dq : dk;
-        if (gsrc != nullptr)
-          bulk_load(gs + head * HD, gsrc + ((b * (is_q ? Hq : Hkv) + h) * Tn + t) * D, gbytes, bar);
+        if (gsrc != nullptr) {
+          load_elems<float, NE>(gsrc + ((b * (is_q ? Hq : Hkv) + h) * Tn + t) * D + lane * NE, gv[j]);
+        } else {
+#pragma unroll
+          for (int k = 0; k < NE; ++k) gv[j][k] = 0.f;
+        }
+        if (!is_v && gsrc != nullptr) {
+          load_elems<T, NE>(qkv + row * static_cast<int64_t>(heads) * HD + head * HD + lane * NE, xv[j]);
+          rr[j] = rstd[row * (Hq + Hkv) + head];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        const int head = h0 + j;  // warp-uniform
+        if (head >= heads) break;
+        T* out = dqkv + row * static_cast<int64_t>(heads) * HD + head * HD + lane * NE;
+        const bool is_v = head >= Hq + Hkv, is_q = head < Hq;
+        const float* gsrc = is_v ? dv : is_q ? dq : dk;
+        if (is_v || gsrc == nullptr) {
+          store_elems<T, NE>(out, gv[j]);  // dV passes through; a missing gradient is zero
+          continue;
+        }
+        const float r = rr[j];
+        const float* w = is_q ? nq : nk;
+        float xh[NE], gr[NE], o[NE];
+        float dot = 0.f;
+#pragma unroll
+        for (int k = 0; k < NE; ++k) {
+          xh[k] = xv[j][k] * r;
+          const float partner = __shfl_xor_sync(0xffffffffu, gv[j][k], 16);
+          const float other = (lane * NE + k) < HALF ? partner : -partner;
+          gr[k] = gv[j][k] * cs[k] + other * sn[k];
+          dot = fmaf(gr[k] * w[k], xh[k], dot);
+          if (is_q)
+            wq[k] = fmaf(gr[k], xh[k], wq[k]);
+          else
+            wk[k] = fmaf(gr[k], xh[k], wk[k]);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+        const float mean = dot / static_cast<float>(HD);
+#pragma unroll
+        for (int k = 0; k < NE; ++k) o[k] = r * (gr[k] * w[k] - xh[k] * mean);
+        store_elems<T, NE>(out, o);
       }
     }
-    float cs[NE], sn[NE];
-    rope_lane_table<T, HD>(static_cast<float>(positions[row]), inv_freq, lane, cs, sn);
-    if (total > 0 && !mbar_wait(bar, iter & 1)) {  // error recorded: drain (bounded) and stop
-      mbar_wait_short(bar, iter & 1);
-      ok = false;
-      break;
-    }
-    for (int head = 0; head < heads; ++head) {
-      T* out = dqkv + row * static_cast<int64_t>(heads) * HD + head * HD + lane * NE;
-      const bool is_v = head >= Hq + Hkv, is_q = head < Hq;
-      const float* gsrc = is_v ? dv : is_q ? dq : dk;
-      float gv[NE];
-      if (gsrc != nullptr) {
-        load_elems<float, NE>(gs + head * HD + lane * NE, gv);
-      } else {
-#pragma unroll
-        for (int k = 0; k < NE; ++k) gv[k] = 0.f;
-      }
-      if (is_v || gsrc == nullptr) {
-        store_elems<T, NE>(out, gv);  // dV passes through; a missing gradient is zero
-        continue;
-      }
-      float xv[NE];
-      load_elems<T, NE>(xs + head * HD + lane * NE, xv);
-      const float r = rstd[row * (Hq + Hkv) + head];
-      const float* w = is_q ? nq : nk;
-      float xh[NE], gr[NE], o[NE];
-      float dot = 0.f;
-#pragma unroll
-      for (int k = 0; k < NE; ++k) {
-        xh[k] = xv[k] * r;
-        const float partner = __shfl_xor_sync(0xffffffffu, gv[k], 16);
-        const float other = (lane * NE + k) < HALF ? partner : -partner;
-        gr[k] = gv[k] * cs[k] + other * sn[k];
-        dot = fmaf(gr[k] * w[k], xh[k], dot);
-        if (is_q)
-          wq[k] = fmaf(gr[k], xh[k], wq[k]);
-        else
-          wk[k] = fmaf(gr[k], xh[k], wk[k]);
-      }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-      const float mean = dot / static_cast<float>(HD);
-#pragma unroll
-      for (int k = 0; k < NE; ++k) o[k] = r * (gr[k] * w[k] - xh[k] * mean);
-      store_elems<T, NE>(out, o);
-    }
-    fence_proxy_async_smem();  // this lane's reads of the slice are ordered before the next copies
-    __syncwarp();
   }
 #pragma unroll
   for (int k = 0; k < NE; ++k) {
@@ -518,24 +492,18 @@ int qkv_prep_fwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
   ORTHRUS_CHECK_ARG(hd >= 2 && hd % 2 == 0 && hd <= 128 && D >= hd && D <= 128 && cap >= Tn);
   // the row kernel makes vector accesses: 16-byte aligned tensors and rows of D % 8 == 0 elements
   const bool vec_ok = D % 8 == 0 && aligned16(qkv) && aligned16(qw) && aligned16(kw) && aligned16(q_out) &&
-                      aligned16(k_out) && aligned16(v_out) &&
-                      64 + 8 * (Hq + 2 * Hkv) * hd * static_cast<int>(sizeof(T)) <= 227 * 1024;
+                      aligned16(k_out) && aligned16(v_out);
   if (vec_ok && (hd == 128 || hd == 64 || hd == 32)) {
     const int64_t rows = B * Tn;
     const unsigned grid = static_cast<unsigned>(ceil_div(rows, 8));  // one warp per row
-    const int smem = 64 + 8 * (Hq + 2 * Hkv) * hd * static_cast<int>(sizeof(T));
-    cudaError_t e = hd == 128  ? ensure_smem(qkv_prep_fwd_row_kernel<T, 128>, smem)
-                    : hd == 64 ? ensure_smem(qkv_prep_fwd_row_kernel<T, 64>, smem)
-                               : ensure_smem(qkv_prep_fwd_row_kernel<T, 32>, smem);
-    ORTHRUS_CHECK_CUDA(e);
     if (hd == 128)
-      qkv_prep_fwd_row_kernel<T, 128><<<grid, 256, smem, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
+      qkv_prep_fwd_row_kernel<T, 128><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
                                                                q_out, k_out, v_out, cap, offset, rstd);
     else if (hd == 64)
-      qkv_prep_fwd_row_kernel<T, 64><<<grid, 256, smem, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
+      qkv_prep_fwd_row_kernel<T, 64><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
                                                               q_out, k_out, v_out, cap, offset, rstd);
     else
-      qkv_prep_fwd_row_kernel<T, 32><<<grid, 256, smem, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
+      qkv_prep_fwd_row_kernel<T, 32><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
                                                               q_out, k_out, v_out, cap, offset, rstd);
     ORTHRUS_CHECK_LAUNCH();
     return ORTHRUS_OK;
@@ -561,22 +529,17 @@ int qkv_prep_bwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
   float* part_k = part_q + static_cast<int64_t>(kPrepBwdBlocks) * hd;
   const int heads = Hq + 2 * Hkv;
   const int64_t rows = B * Tn;
-  const int smem = 64 + 8 * heads * hd * static_cast<int>(sizeof(T) + 4);
   const bool vec_ok = D % 8 == 0 && aligned16(qkv) && aligned16(qw) && aligned16(kw) && aligned16(dqkv) &&
-                      (!dq || aligned16(dq)) && (!dk || aligned16(dk)) && (!dv || aligned16(dv)) &&
-                      smem + 8 * 2 * hd * 4 <= 227 * 1024;
+                      (!dq || aligned16(dq)) && (!dk || aligned16(dk)) && (!dv || aligned16(dv));
   if (vec_ok && (hd == 128 || hd == 64 || hd == 32)) {
-    ORTHRUS_CHECK_CUDA(hd == 128  ? ensure_smem(qkv_prep_bwd_row_kernel<T, 128>, smem)
-                       : hd == 64 ? ensure_smem(qkv_prep_bwd_row_kernel<T, 64>, smem)
-                                  : ensure_smem(qkv_prep_bwd_row_kernel<T, 32>, smem));
     if (hd == 128)
-      qkv_prep_bwd_row_kernel<T, 128><<<kPrepBwdBlocks, 256, smem, stream>>>(qkv, positions, inv_freq, qw, kw, rstd, dq, dk,
+      qkv_prep_bwd_row_kernel<T, 128><<<kPrepBwdBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rstd, dq, dk,
                                                                           dv, rows, Tn, Hq, Hkv, D, dqkv, part_q, part_k);
     else if (hd == 64)
-      qkv_prep_bwd_row_kernel<T, 64><<<kPrepBwdBlocks, 256, smem, stream>>>(qkv, positions, inv_freq, qw, kw, rstd, dq, dk,
+      qkv_prep_bwd_row_kernel<T, 64><<<kPrepBwdBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rstd, dq, dk,
                                                                          dv, rows, Tn, Hq, Hkv, D, dqkv, part_q, part_k);
     else
-      qkv_prep_bwd_row_kernel<T, 32><<<kPrepBwdBlocks, 256, smem, stream>>>(qkv, positions, inv_freq, qw, kw, rstd, dq, dk,
+      qkv_prep_bwd_row_kernel<T, 32><<<kPrepBwdBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rstd, dq, dk,
                                                                          dv, rows, Tn, Hq, Hkv, D, dqkv, part_q, part_k);
     ORTHRUS_CHECK_LAUNCH();
     sum_partials_kernel<<<(hd + 7) / 8, 256, 0, stream>>>(part_q, kPrepBwdBlocks, hd, dqw);

@@ -13,6 +13,8 @@ Cases (B = 8 rows of 2048 tokens, 16 query / 8 KV heads of 128, A = 32 anchors, 
   dualbwd  dual-view attention forward, then backward (dQ; dK/dV of the own-block keys)
   lmhead   fused LM head + KL of one step: 7936 = 8 * 32 * 31 student rows against 7936 teacher
            rows, V = 151936, d = 1024                              (orthrus/objective.py:338-392)
+  prologue q/k RMSNorm + RoPE + head-major scatter of the teacher's fused q|k|v projection
+           (16384 rows of 32 heads x 128), forward and backward    (orthrus/objective.py:136-143)
 """
 
 from __future__ import annotations
@@ -85,23 +87,42 @@ def run(case: str, iters: int, warmup: int) -> dict:
         # logits of the student and unique teacher rows once each, plus the grad GEMM diff @ W
         timed.append(("lmhead_kl", lambda: ops.lmhead_kl(s, t, idx, w),
                       2.0 * LM_D * LM_V * (2 * LM_N + LM_M)))
+    elif case == "prologue":
+        rows, H = B * L, HQ + 2 * HKV
+        qkv = torch.randn(rows, H * HD, device=dev, generator=gen).bfloat16()
+        pos = torch.arange(L, device=dev).repeat(B)
+        inv = ops.rope_inv_freq(HD, 1_000_000.0, dev)
+        qw = (1 + 0.1 * torch.randn(HD, device=dev, generator=gen)).bfloat16()
+        kw = (1 + 0.1 * torch.randn(HD, device=dev, generator=gen)).bfloat16()
+        q, k, v, rstd = ops.qkv_prep(qkv, pos, inv, qw, kw, B, L, HQ, HKV, HD, HD, 1e-6, want_rstd=True)
+        dq, dk, dv = (torch.randn(t.shape, device=dev, generator=gen) for t in (q, k, v))
+        nbytes = 2 * rows * H * HD * 2  # bf16 in and out
+        timed.append(("qkv_prep_fwd", lambda: ops.qkv_prep(qkv, pos, inv, qw, kw, B, L, HQ, HKV, HD, HD, 1e-6),
+                      nbytes))
+        timed.append(("qkv_prep_bwd", lambda: ops.qkv_prep_backward(qkv, pos, inv, qw, kw, rstd, dq, dk, dv, B, L,
+                                                                    HQ, HKV, HD, HD),
+                      rows * H * HD * (2 + 4 + 2)))
     else:
         raise ValueError(f"unknown case {case!r}")
     out = {}
-    for name, fn, flops in timed:
+    for name, fn, work in timed:
         ms = _time(fn, iters, warmup)
-        out[name] = {"ms_per_call": round(ms, 4), "tflops": round(flops / (ms / 1e3) / 1e12, 1)}
+        if case == "prologue":  # HBM-bound: work is bytes moved
+            out[name] = {"ms_per_call": round(ms, 4), "gbs": round(work / (ms / 1e3) / 1e9, 1)}
+        else:
+            out[name] = {"ms_per_call": round(ms, 4), "tflops": round(work / (ms / 1e3) / 1e12, 1)}
     return out
 
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("case", choices=["causal", "dual", "dualbwd", "lmhead"])
+    ap.add_argument("case", choices=["causal", "dual", "dualbwd", "lmhead", "prologue"])
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=2)
     args = ap.parse_args()
     for name, rec in run(args.case, args.iters, args.warmup).items():
-        print(f"{name}: {rec['ms_per_call']:.3f} ms/call, {rec['tflops']} TF/s algorithmic", flush=True)
+        rate = f"{rec['gbs']} GB/s" if "gbs" in rec else f"{rec['tflops']} TF/s algorithmic"
+        print(f"{name}: {rec['ms_per_call']:.3f} ms/call, {rate}", flush=True)
     from . import _lib
     err = _lib.device_error(0)
     print("device error word", err)
