@@ -19,6 +19,22 @@ __device__ __forceinline__ float round_to(float v) {
   return to_f32<T>(from_f32<T>(v));
 }
 
+// Rounds the N values to T in place; bf16 pairs go through one packed conversion each.
+template <typename T, int N>
+__device__ __forceinline__ void round_all(float* v) {
+  if constexpr (sizeof(T) == 2 && N % 2 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 2) {
+      const uint32_t p = pack_bf16x2(v[i], v[i + 1]);
+      v[i] = __uint_as_float(p << 16);
+      v[i + 1] = __uint_as_float(p & 0xffff0000u);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = round_to<T>(v[i]);
+  }
+}
+
 // kind: 0 = q heads, 1 = k heads, 2 = v heads
 template <typename T>
 __global__ void __launch_bounds__(256) qkv_prep_fwd_kernel(
@@ -363,7 +379,11 @@ __global__ void __launch_bounds__(256, 4) qkv_prep_fwd_row_kernel(
         for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
         const float rstd = rsqrtf(ss / static_cast<float>(HD) + eps);
 #pragma unroll
-        for (int k = 0; k < NE; ++k) x[k] = round_to<T>((is_q ? wq[k] : wk[k]) * round_to<T>(x[k] * rstd));
+        for (int k = 0; k < NE; ++k) x[k] *= rstd;
+        round_all<T, NE>(x);
+#pragma unroll
+        for (int k = 0; k < NE; ++k) x[k] *= is_q ? wq[k] : wk[k];
+        round_all<T, NE>(x);
 #pragma unroll
         for (int k = 0; k < NE; ++k) {
           const float partner = __shfl_xor_sync(0xffffffffu, x[k], 16);
