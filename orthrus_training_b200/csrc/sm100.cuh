@@ -111,7 +111,7 @@ __device__ __noinline__ bool mbar_wait_short(uint64_t* bar, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor), no multicast anywhere in this library
+// TMA (cp.async.bulk.tensor): every CTA loads only its own tiles
 // ---------------------------------------------------------------------------------------------
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
@@ -141,7 +141,7 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
 }
 
 // Untiled bulk copy of `bytes` (a multiple of 16) from global to shared memory, completing on an
-// mbarrier. Both addresses 16-byte aligned; no multicast.
+// mbarrier. Both addresses 16-byte aligned; the copy serves this CTA only.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
