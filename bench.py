@@ -40,16 +40,9 @@ METRIC = "train input tok/s (Qwen3-0.6B dual-view step)"
 
 
 def qwen3_06b_config():
-    from transformers import Qwen3Config
+    from orthrus_training_b200.synthetic import qwen3_06b_config as cfg06b
 
-    cfg = Qwen3Config(vocab_size=151936, hidden_size=1024, intermediate_size=3072,
-                      num_hidden_layers=28, num_attention_heads=16, num_key_value_heads=8,
-                      head_dim=128, max_position_embeddings=40960, rms_norm_eps=1e-6,
-                      rope_theta=1e6, tie_word_embeddings=True)
-    cfg.rope_parameters = {"rope_theta": 1e6, "rope_type": "default"}
-    cfg.block_size = BLOCK
-    cfg.mask_token_id = MASK_TOKEN
-    return cfg
+    return cfg06b(BLOCK, MASK_TOKEN)
 
 
 def peaks() -> dict:
@@ -201,6 +194,96 @@ def cpu_baseline_sample() -> dict:
     return {"value": round(SEQ / sec, 2), "unit": "input tok/s", "cores": threads, "kind": "port",
             "sample": f"1 row x {SEQ} tokens, {ANCHORS} anchors, K={BLOCK}: fp32 orthrus_loss "
                       f"fwd+bwd through the CPU port of the reference algorithm ({sec:.1f} s)"}
+
+
+def run_decode(args):
+    """--decode: parallel block decoding of the 0.6B shape (random init) on cuda:0. For each batch
+    size, prompts of U[128, 512] Zipf ids, 512 new tokens, K = 32:
+    - plain: the diffusion drafts of a random-init model are rejected, so every cycle commits one
+      token (TPF below 1 is expected and is not a quality figure);
+    - scripted: the drafts are the greedy continuation with seeded edits (the device analogue of
+      the reference tests' ScriptedBackend), which exercises accept / rollback; the output must
+      equal the plain run's tokens.
+    One JSON line per configuration; achieved HBM bandwidth per pass = (weights + the KV read at
+    the mean context) / time per pass. A CPU line times the reference algorithm (the oracle port,
+    fp32) on a bounded sample."""
+    import numpy as np
+
+    from orthrus_training_b200.decoding import block_decode
+    from orthrus_training_b200.modeling_orthrus import OrthrusLM, copy_diff_from_ar
+    from orthrus_training_b200.synthetic import zipf_ids
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    dtype = torch.bfloat16 if args.decode_dtype == "bf16" else torch.float32
+    torch.manual_seed(2)
+    cfg = qwen3_06b_config()
+    with torch.device(dev):
+        model = OrthrusLM(cfg).to(dtype)
+    copy_diff_from_ar(model)
+    model.eval()
+    K, new = BLOCK, args.decode_new
+    L, Hkv, hd = cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim
+    esize = 2 if dtype == torch.bfloat16 else 4
+    weight_bytes = sum(p.numel() for n, p in model.named_parameters()
+                       if not any(f".{m}_diff." in n for m in ("q_proj", "k_proj", "v_proj", "o_proj",
+                                                                 "q_norm", "k_norm"))) * esize
+    kv_per_token = 2 * L * Hkv * hd * esize
+    pk = peaks()
+    with torch.inference_mode():
+        block_decode(model, [[1, 2, 3, 4] * 40], 16)  # kernel set-up outside the timed runs
+    for batch in args.decode_batch:
+        rng = np.random.default_rng(2 + batch)
+        prompts = [zipf_ids(rng, int(rng.integers(128, 513)), REAL_VOCAB).tolist() for _ in range(batch)]
+        with torch.inference_mode():
+            plain = block_decode(model, prompts, new)
+            ref = plain.tokens
+            # scripted drafts: the true continuation after each anchor, 5 % of tokens edited
+            table = torch.zeros(batch, new, K - 1, dtype=torch.int64)
+            erng = np.random.default_rng(7 + batch)
+            for b, toks in enumerate(ref):
+                for i in range(new):
+                    nxt = toks[i + 1: i + K]
+                    row = [t if erng.random() >= 0.05 else int(erng.integers(0, REAL_VOCAB)) for t in nxt]
+                    table[b, i, : len(row)] = torch.tensor(row, dtype=torch.int64)
+            scripted = block_decode(model, prompts, new, draft_table=table.to(dev))
+        lossless = scripted.tokens == ref
+        for name, res in (("plain", plain), ("scripted", scripted)):
+            dec_s = res.seconds - res.prefill_seconds
+            gen = res.total_tokens
+            cycles = max(res.cycles)
+            per_pass = dec_s / max(2 * cycles, 1)
+            mean_ctx = sum(len(p) for p in prompts) / batch + new / 2
+            pass_bytes = weight_bytes + kv_per_token * mean_ctx * batch
+            gbs = pass_bytes / per_pass / 1e9
+            print(json.dumps({
+                "metric": "decode tok/s (Qwen3-0.6B-shape Orthrus block decode, greedy)", "mode": name,
+                "value": round(gen / dec_s, 1), "unit": "generated tok/s", "batch": batch,
+                "new_tokens": new, "K": K, "dtype": args.decode_dtype, "tpf": round(res.tpf, 3),
+                "mean_accepted": round(sum(sum(a) for a in res.accepted) / max(sum(res.cycles), 1), 3),
+                "ms_per_pass": round(per_pass * 1e3, 4),
+                "hbm": {"bytes_per_pass": int(pass_bytes), "achieved_gbs": round(gbs, 1),
+                        "peak_gbs": pk["hbm_gbs"], "frac": round(gbs / pk["hbm_gbs"], 4)},
+                "lossless_vs_plain_greedy": bool(lossless) if name == "scripted" else True,
+                "prefill_s": round(res.prefill_seconds, 3), "data": "synthetic Zipf(1.1) prompts, random-init weights",
+            }), flush=True)
+    if not args.no_cpu_baseline:
+        import oracle as O
+
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        ocfg = O.OracleConfig.from_hf(cfg)
+        params = {k: v.detach() for k, v in cpu_params(cfg, seed=2).items()}
+        prompt = torch.tensor([zipf_ids(np.random.default_rng(2), 128, REAL_VOCAB).tolist()])
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            toks, _ = O.diffusion_generate(params, ocfg, prompt, 8)
+        sec = time.perf_counter() - t0
+        print(json.dumps({"metric": "decode tok/s (reference algorithm on the host cores)",
+                          "value": round(8 / sec, 3), "unit": "generated tok/s", "cores": threads,
+                          "kind": "port", "sample": f"batch 1, 128-token prompt, 8 new tokens, K={BLOCK}, "
+                                                     f"fp32 diffusion_generate of the CPU port ({sec:.1f} s)"}),
+              flush=True)
 
 
 def run_reference(args):
@@ -359,10 +442,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode", action="store_true", help="measure parallel block decoding instead")
+    ap.add_argument("--decode-batch", type=int, nargs="+", default=[1, 32])
+    ap.add_argument("--decode-new", type=int, default=512)
+    ap.add_argument("--decode-dtype", default="bf16", choices=["bf16", "fp32"])
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if args.impl == "reference":
+    if args.decode:
+        run_decode(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -59,3 +59,18 @@ def packed_rows(
         else:
             input_ids[r] = rng.integers(0, real_vocab, seq_len)
     return torch.from_numpy(input_ids), torch.from_numpy(mask)
+
+
+def qwen3_06b_config(block_size: int = 32, mask_token_id: int = 151669):
+    """The Qwen3-0.6B architecture (28 layers, d 1024, 16 query / 8 KV heads of 128, MLP 3072,
+    vocabulary 151936 tied) with the Orthrus block size and mask token, for random-init runs."""
+    from transformers import Qwen3Config
+
+    cfg = Qwen3Config(vocab_size=151936, hidden_size=1024, intermediate_size=3072,
+                      num_hidden_layers=28, num_attention_heads=16, num_key_value_heads=8,
+                      head_dim=128, max_position_embeddings=40960, rms_norm_eps=1e-6,
+                      rope_theta=1e6, tie_word_embeddings=True)
+    cfg.rope_parameters = {"rope_theta": 1e6, "rope_type": "default"}
+    cfg.block_size = block_size
+    cfg.mask_token_id = mask_token_id
+    return cfg
