@@ -135,10 +135,13 @@ __global__ void attn_tilemap_kernel(const int64_t* __restrict__ anchors, int64_t
   out[i * 4 + 3] = static_cast<int32_t>(e2);
 }
 
-bool use_tensor_cores(int dtype, int hd, int D, int mask, const int32_t* offset) {
-  if (dtype != ORTHRUS_BF16 || hd != D || (D != 64 && D != 128)) return false;
-  if (mask == ORTHRUS_MASK_DUAL) return true;
-  return mask == ORTHRUS_MASK_CAUSAL && offset == nullptr;
+// bf16 rows of 64 or 128 take the tensor-core kernels for every mask. A row's result there does
+// not depend on the other rows of its tile (key tiles that a row cannot see contribute exact
+// zeros), so a K-token verification reproduces the one-token pass bit for bit. Keys past a
+// sequence's cached length must be finite (the caches start zeroed).
+bool use_tensor_cores(int dtype, int hd, int D, int mask, const int32_t*) {
+  return dtype == ORTHRUS_BF16 && hd == D && (D == 64 || D == 128) && mask >= ORTHRUS_MASK_CAUSAL &&
+         mask <= ORTHRUS_MASK_DRAFT;
 }
 
 template <typename Kern>
