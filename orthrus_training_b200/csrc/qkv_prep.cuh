@@ -337,35 +337,39 @@ __global__ void __launch_bounds__(256, 4) qkv_prep_fwd_row_kernel(
     const T* __restrict__ qkv, const int64_t* __restrict__ positions, const float* __restrict__ inv_freq,
     const T* __restrict__ q_norm_w, const T* __restrict__ k_norm_w, int64_t rows, int64_t Tn, int Hq, int Hkv,
     int D, float eps, T* __restrict__ q_out, T* __restrict__ k_out, T* __restrict__ v_out, int64_t cap,
-    const int32_t* __restrict__ offset, float* __restrict__ rstd_out) {
+    const int32_t* __restrict__ offset, float* __restrict__ rstd_out, int wpr) {
   constexpr int NE = HD / 32;
   constexpr int HALF = HD / 2;
   constexpr int PER = HD == 128 ? 4 : 8;  // head rows in flight per warp within 64 registers
   const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  // wpr warps share a row (few rows: decode); warp `sub` of a row takes the heads sub, sub + wpr,
+  // ... with the same per-head arithmetic, so the result does not depend on wpr
+  const int warp = threadIdx.x >> 5, sub = warp % wpr;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (8 / wpr) + warp / wpr;
   if (row >= rows) return;
   const int64_t b = row / Tn, t = row % Tn;
   const int heads = Hq + 2 * Hkv;
+  const int nmine = (heads - sub + wpr - 1) / wpr;  // heads of this warp
   const T* xrow = qkv + row * static_cast<int64_t>(heads) * HD;
   float v[PER][NE];
 #pragma unroll
   for (int j = 0; j < PER; ++j)
-    if (j < heads) load_elems<T, NE>(xrow + j * HD + lane * NE, v[j]);
+    if (j < nmine) load_elems<T, NE>(xrow + (sub + wpr * j) * HD + lane * NE, v[j]);
   float cs[NE], sn[NE], wq[NE], wk[NE];
   rope_lane_table<T, HD>(static_cast<float>(positions[row]), inv_freq, lane, cs, sn);
   load_elems<T, NE>(q_norm_w + lane * NE, wq);
   load_elems<T, NE>(k_norm_w + lane * NE, wk);
   const int64_t orow_kv = (offset ? offset[b] : 0) + t;
-  for (int h0 = 0; h0 < heads; h0 += PER) {
+  for (int h0 = 0; h0 < nmine; h0 += PER) {
     if (h0 > 0) {
 #pragma unroll
       for (int j = 0; j < PER; ++j)
-        if (h0 + j < heads) load_elems<T, NE>(xrow + (h0 + j) * HD + lane * NE, v[j]);
+        if (h0 + j < nmine) load_elems<T, NE>(xrow + (sub + wpr * (h0 + j)) * HD + lane * NE, v[j]);
     }
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-      const int head = h0 + j;  // warp-uniform
-      if (head >= heads) break;
+      if (h0 + j >= nmine) break;  // warp-uniform
+      const int head = sub + wpr * (h0 + j);
       float* x = v[j];
       T* dst;
       if (head >= Hq + Hkv) {
@@ -515,16 +519,17 @@ int qkv_prep_fwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
                       aligned16(k_out) && aligned16(v_out);
   if (vec_ok && (hd == 128 || hd == 64 || hd == 32)) {
     const int64_t rows = B * Tn;
-    const unsigned grid = static_cast<unsigned>(ceil_div(rows, 8));  // one warp per row
+    const int wpr = rows < 4 * 148 * 8 ? 8 : 1;  // few rows: a CTA per row, its 8 warps share the heads
+    const unsigned grid = static_cast<unsigned>(ceil_div(rows, 8 / wpr));
     if (hd == 128)
       qkv_prep_fwd_row_kernel<T, 128><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
-                                                               q_out, k_out, v_out, cap, offset, rstd);
+                                                               q_out, k_out, v_out, cap, offset, rstd, wpr);
     else if (hd == 64)
       qkv_prep_fwd_row_kernel<T, 64><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
-                                                              q_out, k_out, v_out, cap, offset, rstd);
+                                                              q_out, k_out, v_out, cap, offset, rstd, wpr);
     else
       qkv_prep_fwd_row_kernel<T, 32><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
-                                                              q_out, k_out, v_out, cap, offset, rstd);
+                                                              q_out, k_out, v_out, cap, offset, rstd, wpr);
     ORTHRUS_CHECK_LAUNCH();
     return ORTHRUS_OK;
   }
