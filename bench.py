@@ -251,8 +251,8 @@ def run_decode(args):
         for name, res in (("plain", plain), ("scripted", scripted)):
             dec_s = res.seconds - res.prefill_seconds
             gen = res.total_tokens
-            cycles = max(res.cycles)
-            per_pass = dec_s / max(2 * cycles, 1)
+            # one batched cycle = a draft pass and a verify pass; time the replayed cycles only
+            per_pass = res.steady_seconds / max(2 * res.steady_cycles, 1)
             mean_ctx = sum(len(p) for p in prompts) / batch + new / 2
             pass_bytes = weight_bytes + kv_per_token * mean_ctx * batch
             gbs = pass_bytes / per_pass / 1e9

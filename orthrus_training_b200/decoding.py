@@ -261,6 +261,8 @@ class BlockDecodeResult:
     passes: list[int]
     seconds: float
     prefill_seconds: float
+    steady_seconds: float = 0.0  # the replayed cycles only (after prefill, set-up and capture)
+    steady_cycles: int = 0       # batched cycles replayed in steady_seconds
 
     @property
     def total_tokens(self) -> int:
@@ -370,6 +372,9 @@ def block_decode(model, prompts: list[list[int]], max_new_tokens: int, eos=(), *
             st.cycle_once()
         # capture recorded but did not run the cycle
     cycles_run = 1 if use_graph else 0
+    torch.cuda.synchronize(dev)
+    t_steady = time.perf_counter()
+    first_steady = cycles_run
     max_cycles = max_new_tokens + 1
     while cycles_run < max_cycles:
         if int(st.done.min().item()) == 1:
@@ -390,7 +395,8 @@ def block_decode(model, prompts: list[list[int]], max_new_tokens: int, eos=(), *
     accepted = [log[b][: cyc[b]] for b in range(B)]
     return BlockDecodeResult(tokens=tokens, accepted=accepted, cycles=cyc,
                              passes=[1 + 2 * c for c in cyc], seconds=t2 - t0,
-                             prefill_seconds=t1 - t0)
+                             prefill_seconds=t1 - t0, steady_seconds=t2 - t_steady,
+                             steady_cycles=cycles_run - first_steady)
 
 
 @torch.inference_mode()
