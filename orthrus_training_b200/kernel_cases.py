@@ -15,6 +15,9 @@ Cases (B = 8 rows of 2048 tokens, 16 query / 8 KV heads of 128, A = 32 anchors, 
            rows, V = 151936, d = 1024                              (orthrus/objective.py:338-392)
   prologue q/k RMSNorm + RoPE + head-major scatter of the teacher's fused q|k|v projection
            (16384 rows of 32 heads x 128), forward and backward    (orthrus/objective.py:136-143)
+  sweep    dual-view attention forward + backward over L in {1024, 2048, 4096, 8192}, K in
+           {16, 32, 64}, A in {8, 32, 64} (batch filling 16384 query tokens, capped at 65536 keys
+           per head), and the fused LM head + KL over N in {4096, 16384, 65536} student rows
 """
 
 from __future__ import annotations
@@ -114,12 +117,63 @@ def run(case: str, iters: int, warmup: int) -> dict:
     return out
 
 
+def sweep(iters: int, warmup: int) -> list[dict]:
+    """One line per configuration: attention (dual view, fwd and bwd) and LM head + KL."""
+    dev = torch.device("cuda", 0)
+    sc = 1.0 / math.sqrt(HD)
+    out = []
+    for L1 in (1024, 2048, 4096, 8192):
+        for K1 in (16, 32, 64):
+            for A1 in (8, 32, 64):
+                if A1 * K1 > L1:
+                    continue
+                B1 = max(1, min(16384 // (A1 * K1), 65536 // L1))
+                gen = torch.Generator(device=dev).manual_seed(L1 + K1 + A1)
+                Tq = A1 * K1
+                q = torch.randn(B1, HQ, Tq, HD, device=dev, generator=gen).bfloat16()
+                k1 = torch.randn(B1, HKV, L1, HD, device=dev, generator=gen).bfloat16()
+                v1 = torch.randn_like(k1)
+                k2 = torch.randn(B1, HKV, Tq, HD, device=dev, generator=gen).bfloat16()
+                v2 = torch.randn_like(k2)
+                anchors = torch.stack([torch.randperm(L1 - K1, device=dev, generator=gen)[:A1].add(1).sort().values
+                                       for _ in range(B1)])
+                fwd = lambda: ops.attention_fwd(q, k1, v1, k2, v2, mask=1, hd=HD, scale=sc, anchors=anchors,
+                                                block=K1)
+                flops = float(ops.attention_flops(1, B1, HQ, Tq, HD, anchors, K1, L1))
+                o, lse = fwd()
+                dout = torch.randn(B1, Tq, HQ, HD, device=dev, generator=gen).bfloat16()
+                bwd = lambda: ops.attention_bwd(q, k1, v1, k2, v2, anchors, K1, o, lse, dout, hd=HD, scale=sc)
+                tf, tb = _time(fwd, iters, warmup), _time(bwd, iters, warmup)
+                out.append({"case": "attention", "L": L1, "K": K1, "A": A1, "B": B1, "query_tokens": B1 * Tq,
+                            "fwd_ms": round(tf, 4), "fwd_tflops": round(flops / tf / 1e9, 1),
+                            "bwd_ms": round(tb, 4), "bwd_tflops": round(1.5 * flops / tb / 1e9, 1)})
+                del q, k1, v1, k2, v2, o, lse, dout
+    for n in (4096, 16384, 65536):
+        gen = torch.Generator(device=dev).manual_seed(n)
+        s = torch.randn(n, LM_D, device=dev, generator=gen).bfloat16()
+        t = torch.randn(n, LM_D, device=dev, generator=gen).bfloat16()
+        idx = torch.arange(n, device=dev)
+        w = (torch.randn(LM_V, LM_D, device=dev, generator=gen) * 0.05).bfloat16()
+        ms = _time(lambda: ops.lmhead_kl(s, t, idx, w), max(1, iters // 4), max(1, warmup // 2))
+        flops = 2.0 * LM_D * LM_V * (2 * n + n)
+        out.append({"case": "lmhead_kl", "N": n, "teacher_rows": n, "ms": round(ms, 3),
+                    "tflops": round(flops / ms / 1e9, 1)})
+        del s, t, w
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("case", choices=["causal", "dual", "dualbwd", "lmhead", "prologue"])
+    ap.add_argument("case", choices=["causal", "dual", "dualbwd", "lmhead", "prologue", "sweep"])
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=2)
     args = ap.parse_args()
+    if args.case == "sweep":
+        import json
+
+        for rec in sweep(args.iters, args.warmup):
+            print(json.dumps(rec), flush=True)
+        return
     for name, rec in run(args.case, args.iters, args.warmup).items():
         rate = f"{rec['gbs']} GB/s" if "gbs" in rec else f"{rec['tflops']} TF/s algorithmic"
         print(f"{name}: {rec['ms_per_call']:.3f} ms/call, {rate}", flush=True)
