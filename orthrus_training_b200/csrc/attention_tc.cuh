@@ -1070,7 +1070,9 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) store_row32_sw128_packed(p_base, row, c * 32, pk + 16 * c);
       l = fmaf(l, alpha, (sm[0] + sm[1]) + (sm[2] + sm[3]));
-      if (alpha != 1.f) {
+      // TMEM loads and stores are warp-collective: the whole warp rescales when any of its rows
+      // must (rows that need none multiply by exactly 1)
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < D / 16; ++c) {

@@ -117,11 +117,11 @@ def run(case: str, iters: int, warmup: int) -> dict:
     return out
 
 
-def sweep(iters: int, warmup: int) -> list[dict]:
-    """One line per configuration: attention (dual view, fwd and bwd) and LM head + KL."""
+def sweep(iters: int, warmup: int):
+    """Yields one record per configuration as it is measured: attention (dual view, fwd and bwd),
+    then LM head + KL."""
     dev = torch.device("cuda", 0)
     sc = 1.0 / math.sqrt(HD)
-    out = []
     for L1 in (1024, 2048, 4096, 8192):
         for K1 in (16, 32, 64):
             for A1 in (8, 32, 64):
@@ -144,9 +144,9 @@ def sweep(iters: int, warmup: int) -> list[dict]:
                 dout = torch.randn(B1, Tq, HQ, HD, device=dev, generator=gen).bfloat16()
                 bwd = lambda: ops.attention_bwd(q, k1, v1, k2, v2, anchors, K1, o, lse, dout, hd=HD, scale=sc)
                 tf, tb = _time(fwd, iters, warmup), _time(bwd, iters, warmup)
-                out.append({"case": "attention", "L": L1, "K": K1, "A": A1, "B": B1, "query_tokens": B1 * Tq,
-                            "fwd_ms": round(tf, 4), "fwd_tflops": round(flops / tf / 1e9, 1),
-                            "bwd_ms": round(tb, 4), "bwd_tflops": round(1.5 * flops / tb / 1e9, 1)})
+                yield {"case": "attention", "L": L1, "K": K1, "A": A1, "B": B1, "query_tokens": B1 * Tq,
+                       "fwd_ms": round(tf, 4), "fwd_tflops": round(flops / tf / 1e9, 1),
+                       "bwd_ms": round(tb, 4), "bwd_tflops": round(1.5 * flops / tb / 1e9, 1)}
                 del q, k1, v1, k2, v2, o, lse, dout
     for n in (4096, 16384, 65536):
         gen = torch.Generator(device=dev).manual_seed(n)
@@ -156,10 +156,9 @@ def sweep(iters: int, warmup: int) -> list[dict]:
         w = (torch.randn(LM_V, LM_D, device=dev, generator=gen) * 0.05).bfloat16()
         ms = _time(lambda: ops.lmhead_kl(s, t, idx, w), max(1, iters // 4), max(1, warmup // 2))
         flops = 2.0 * LM_D * LM_V * (2 * n + n)
-        out.append({"case": "lmhead_kl", "N": n, "teacher_rows": n, "ms": round(ms, 3),
-                    "tflops": round(flops / ms / 1e9, 1)})
+        yield {"case": "lmhead_kl", "N": n, "teacher_rows": n, "ms": round(ms, 3),
+               "tflops": round(flops / ms / 1e9, 1)}
         del s, t, w
-    return out
 
 
 def main():

@@ -74,6 +74,29 @@ def test_dual_view_attention_forward_backward(dtype, hd, L, A, K):
         assert err <= (3e-2 if dtype == torch.bfloat16 else 2e-5) * max(1.0, r.abs().max().item()), (name, err)
 
 
+def test_dual_view_rescale_in_some_rows_of_a_warp():
+    """The forward raises a row's reference max (and rescales its O accumulator in TMEM) only when
+    a tile max exceeds it by 2^8. Here the rows of the first block see one AR key and an own block
+    with large scores, so they rescale, while the rows of the next block (same warp) do not: the
+    rescale must still be correct when only part of a warp needs it."""
+    B, Hq, Hkv, L, A, K, hd = 1, 4, 2, 300, 8, 16, 128
+    dtype = torch.bfloat16
+    ts, _ = _dual_case(B, Hq, Hkv, L, A, K, hd, dtype, seed=11)
+    anchors = torch.tensor([[1, 40, 80, 120, 160, 200, 240, 280]])
+    k2 = ts[3].clone()
+    k2[:, :, :K] *= 6.0  # the own block of the first anchor: scores about 6x larger
+    ts = [ts[0], ts[1], ts[2], k2.to(dtype).float(), ts[4]]
+    dev = [t.to(DEV).to(dtype) for t in ts]
+    o, _ = _ops().attention_fwd(dev[0], dev[1], dev[2], dev[3], dev[4], mask=1, hd=hd,
+                                scale=1.0 / math.sqrt(hd), anchors=anchors.to(DEV), block=K)
+    ref, _ = _oracle_dual(ts, anchors, L, K)
+    got = o.float().cpu().transpose(1, 2)
+    assert (got - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+    from orthrus_training_b200 import _lib
+
+    assert _lib.device_error(0) == 0
+
+
 @pytest.mark.parametrize("dtype,hd", [(torch.bfloat16, 128), (torch.float32, 32), (torch.bfloat16, 64)])
 def test_teacher_causal_attention(dtype, hd):
     B, Hq, Hkv, T = 2, 4, 2, 333
