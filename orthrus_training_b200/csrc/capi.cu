@@ -294,6 +294,35 @@ size_t orthrus_attn_bwd_workspace_bytes(int64_t B, int Hq, int64_t Tq) {
   return static_cast<size_t>(B) * Hq * Tq * sizeof(float);
 }
 
+namespace {
+
+// A second stream per device, with a fork and a join event, so that the dK/dV kernel of the
+// backward runs beside the dQ kernel and fills the SMs its last partial wave leaves idle. Created
+// on the first backward on each device; the join makes the caller's stream wait for the side
+// stream, so the caller sees one ordered call (stream capture records it as a fork and a join).
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+SideStream* side_stream_on_current_device() {
+  static std::mutex mu;
+  static SideStream side[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  SideStream& s = side[dev];
+  if (s.stream == nullptr) {
+    if (cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+    if (cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming) != cudaSuccess)
+      return nullptr;
+  }
+  return &s;
+}
+
+}  // namespace
+
 int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b, int64_t L1,
                      const void* k2, const void* v2, int64_t s2h, int64_t s2b, int64_t L2, int64_t B, int Hq, int Hkv,
                      int64_t Tq, int hd, int D, float scale, const int64_t* anchors, int64_t A, int block,
@@ -336,25 +365,32 @@ int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h,
       if (!make_attn_maps(m64, q, k1, v1, s1h, L1, k2, v2, s2h, L2, B, Hq, Hkv, Tq, hd, D, do_, 64))
         return ORTHRUS_ECUDA;
       dim3 grid2(static_cast<unsigned>(ceil_div(Tq, 128)), Hq / 2, static_cast<unsigned>(B));
+      // dQ on the caller's stream, dK/dV on the side stream (both only read delta and the inputs)
+      SideStream* side = side_stream_on_current_device();
+      if (side == nullptr) return ORTHRUS_ECUDA;
+      ORTHRUS_CHECK_CUDA(cudaEventRecord(side->fork, st));
       if (D == 128) {
         if (set_smem(attn_dq_tc2_kernel<128>, Dq2Smem<128>::SMEM)) return ORTHRUS_ECUDA;
+        if (set_smem(attn_dkdv_tc_kernel<128>, DkvSmem<128>::SMEM)) return ORTHRUS_ECUDA;
         attn_dq_tc2_kernel<128><<<grid2, 320, Dq2Smem<128>::SMEM, st>>>(
             m64.q, m64.dout, m64.k1, m64.v1, m64.k2, m64.v2, Hq, Hkv, Tq, hd, scale, mp, true, lse, delta, dq);
         ORTHRUS_CHECK_LAUNCH();
-        if (set_smem(attn_dkdv_tc_kernel<128>, DkvSmem<128>::SMEM)) return ORTHRUS_ECUDA;
-        attn_dkdv_tc_kernel<128><<<grid_kv, 192, DkvSmem<128>::SMEM, st>>>(m.q, m.dout, m.k2, m.v2, Hq, Hkv, Tq,
-                                                                             L2, hd, block, scale, lse, delta, dk2,
-                                                                             dv2);
+        ORTHRUS_CHECK_CUDA(cudaStreamWaitEvent(side->stream, side->fork, 0));
+        attn_dkdv_tc_kernel<128><<<grid_kv, 192, DkvSmem<128>::SMEM, side->stream>>>(
+            m.q, m.dout, m.k2, m.v2, Hq, Hkv, Tq, L2, hd, block, scale, lse, delta, dk2, dv2);
       } else {
         if (set_smem(attn_dq_tc2_kernel<64>, Dq2Smem<64>::SMEM)) return ORTHRUS_ECUDA;
+        if (set_smem(attn_dkdv_tc_kernel<64>, DkvSmem<64>::SMEM)) return ORTHRUS_ECUDA;
         attn_dq_tc2_kernel<64><<<grid2, 320, Dq2Smem<64>::SMEM, st>>>(
             m64.q, m64.dout, m64.k1, m64.v1, m64.k2, m64.v2, Hq, Hkv, Tq, hd, scale, mp, true, lse, delta, dq);
         ORTHRUS_CHECK_LAUNCH();
-        if (set_smem(attn_dkdv_tc_kernel<64>, DkvSmem<64>::SMEM)) return ORTHRUS_ECUDA;
-        attn_dkdv_tc_kernel<64><<<grid_kv, 192, DkvSmem<64>::SMEM, st>>>(m.q, m.dout, m.k2, m.v2, Hq, Hkv, Tq, L2,
-                                                                           hd, block, scale, lse, delta, dk2, dv2);
+        ORTHRUS_CHECK_CUDA(cudaStreamWaitEvent(side->stream, side->fork, 0));
+        attn_dkdv_tc_kernel<64><<<grid_kv, 192, DkvSmem<64>::SMEM, side->stream>>>(
+            m.q, m.dout, m.k2, m.v2, Hq, Hkv, Tq, L2, hd, block, scale, lse, delta, dk2, dv2);
       }
       ORTHRUS_CHECK_LAUNCH();
+      ORTHRUS_CHECK_CUDA(cudaEventRecord(side->join, side->stream));
+      ORTHRUS_CHECK_CUDA(cudaStreamWaitEvent(st, side->join, 0));
       return ORTHRUS_OK;
     }
     if (D == 128) {
