@@ -286,6 +286,25 @@ def run_decode(args):
               flush=True)
 
 
+def step_roofline(cfg, kernels: dict, steps: int, ms_per_step: float, pk: dict) -> dict:
+    """The whole step against its algorithmic work per GPU: projection GEMMs of the teacher
+    (forward over every token) and of the diffusion view (forward, dX, and dW of the twins only),
+    plus the attention and LM-head FLOPs the kernels counted in the timed region."""
+    d, inter, L = cfg.hidden_size, cfg.intermediate_size, cfg.num_hidden_layers
+    qkv = (cfg.num_attention_heads + 2 * cfg.num_key_value_heads) * cfg.head_dim * d
+    o = d * cfg.num_attention_heads * cfg.head_dim
+    per_layer = qkv + o + 3 * d * inter
+    teacher_tokens, student_tokens = ROWS * SEQ, ROWS * ANCHORS * BLOCK
+    linear = 2.0 * L * (teacher_tokens * per_layer + 2 * student_tokens * per_layer
+                        + student_tokens * (qkv + o))
+    kernel_flops = sum(v["flops"] for v in kernels.values()) / steps
+    total = linear + kernel_flops
+    achieved = total / (ms_per_step / 1e3) / 1e12
+    return {"tflop_per_step": round(total / 1e12, 2), "achieved": round(achieved, 1),
+            "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+            "frac": round(achieved / pk["bf16_tflops_sustained"], 4), "peak_kind": "sustained"}
+
+
 def run_reference(args):
     """--impl reference: the reference algorithm's CPU implementation timed on the host cores."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -414,6 +433,7 @@ def run_ours(args):
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
         "gpu_launches": int(launches),
         "roofline": roofline,
+        "step_roofline": step_roofline(cfg, kernels, args.steps, ms / args.steps, pk),
         "kernels": {k: {"launches_per_step": v["launches"] // args.steps,
                         "ms_per_step": round(v["ms"] / args.steps, 3),
                         "tflops": round(v["flops"] / (v["ms"] / 1e3) / 1e12, 1) if v["ms"] else None}
