@@ -119,15 +119,18 @@ def test_lmhead_kl_fp32_matches_oracle_ragged():
     assert torch.allclose(grad.cpu(), r_grad, rtol=1e-4, atol=1e-6)
 
 
-def test_lmhead_kl_bf16_full_vocab_vs_torch_fp32():
-    """0.6B LM-head shape (V = 151936, d = 1024) against an fp32 torch computation on the GPU."""
-    n, m, V, d = 1536, 1100, 151936, 1024
+@pytest.mark.parametrize("n,m,chunk_rows", [(1536, 1100, 4096), (3000, 3000, 2048)])
+def test_lmhead_kl_bf16_full_vocab_vs_torch_fp32(n, m, chunk_rows):
+    """0.6B LM-head shape (V = 151936, d = 1024) against an fp32 torch computation on the GPU. The
+    second case gives every persistent CTA several (row tile, vocabulary split) units in both passes
+    and splits the student rows into two chunks."""
+    V, d = 151936, 1024
     g = torch.Generator(device=DEV).manual_seed(5)
     s = torch.randn(n, d, device=DEV, generator=g).bfloat16()
     t = torch.randn(m, d, device=DEV, generator=g).bfloat16()
     idx = torch.randint(0, m, (n,), device=DEV, generator=g).sort().values
     w = (torch.randn(V, d, device=DEV, generator=g) * 0.05).bfloat16()
-    total, kl, agree, grad, _, _ = _ops().lmhead_kl(s, t, idx, w)
+    total, kl, agree, grad, _, _ = _ops().lmhead_kl(s, t, idx, w, chunk_rows=chunk_rows)
     ls = s.float() @ w.float().t()
     lt = t.float() @ w.float().t()
     lpt = lt.log_softmax(-1)[idx]
