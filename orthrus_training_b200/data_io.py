@@ -1,0 +1,153 @@
+"""The on-disk formats on either side of the training step, in the reference's layout.
+
+- Packed rows (orthrus/data.py:72-86): ``input_ids.npy`` (int32 [rows, seq_len]) and
+  ``assistant_mask.npy`` (uint8, same shape) in one directory, the mask written last so that its
+  presence marks a complete set; read memory-mapped.
+- Micro-batch order (orthrus/data.py:89-103): one permutation of the rows per (seed, epoch) from
+  ``numpy.random.default_rng([seed, epoch])``, cut into consecutive micro-batches, each sorted by
+  row id (sequential reads of the memory map), resumable at a micro-batch index. Restated with the
+  same generator calls so that a run resumed here sees the rows the reference would have fed.
+- Training checkpoints (orthrus/checkpoint.py:27,68-97): a directory holding
+  ``trainable.safetensors`` (the diffusion twins under their parameter names),
+  ``optimizer.pt`` (optimizer and scheduler state) and ``trainer_state.json``, written to
+  ``<path>.tmp`` and renamed when complete. Checkpoints move between the reference and this
+  package unchanged, since the parameter names are the same.
+
+``DevicePrefetcher`` is this package's loader side: it copies each micro-batch into pinned host
+buffers and on to the GPU on a copy stream, one micro-batch ahead of the step that consumes it.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import shutil
+from pathlib import Path
+from typing import Iterator
+
+import numpy as np
+import torch
+
+IDS_FILE, MASK_FILE = "input_ids.npy", "assistant_mask.npy"
+WEIGHTS, OPTIMIZER, STATE = "trainable.safetensors", "optimizer.pt", "trainer_state.json"
+
+
+def save_packed(directory: Path, ids: np.ndarray, mask: np.ndarray) -> None:
+    """Writes packed rows; the mask goes last, so its presence marks a complete directory."""
+    if ids.shape != mask.shape or ids.ndim != 2:
+        raise ValueError(f"ids {ids.shape} and mask {mask.shape} must be the same [rows, seq_len]")
+    directory = Path(directory)
+    directory.mkdir(parents=True, exist_ok=True)
+    np.save(directory / IDS_FILE, ids.astype(np.int32, copy=False))
+    np.save(directory / MASK_FILE, mask.astype(np.uint8, copy=False))
+
+
+def load_packed(directory: Path) -> tuple[np.ndarray, np.ndarray]:
+    """Memory-mapped (input_ids int32, assistant_mask uint8) of a packed directory."""
+    directory = Path(directory)
+    if not (directory / MASK_FILE).exists():
+        raise FileNotFoundError(f"{directory} holds no complete packed rows ({MASK_FILE} missing)")
+    ids = np.load(directory / IDS_FILE, mmap_mode="r")
+    mask = np.load(directory / MASK_FILE, mmap_mode="r")
+    if ids.shape != mask.shape or ids.ndim != 2:
+        raise ValueError(f"{directory}: ids {ids.shape} and mask {mask.shape} do not match")
+    if ids.dtype != np.int32 or mask.dtype != np.uint8:
+        raise ValueError(f"{directory}: expected int32 ids and uint8 mask, got {ids.dtype} / {mask.dtype}")
+    return ids, mask
+
+
+def batch_rows(num_rows: int, batch_size: int, seed: int, epoch: int, start: int = 0) -> Iterator[tuple[int, np.ndarray]]:
+    """(micro-batch index, sorted row ids) of one epoch from micro-batch ``start`` on."""
+    order = np.random.default_rng([seed, epoch]).permutation(num_rows)
+    for index in range(start, len(order) // batch_size):
+        yield index, np.sort(order[index * batch_size: (index + 1) * batch_size])
+
+
+def batches(ids: np.ndarray, mask: np.ndarray, batch_size: int, seed: int, epoch: int,
+            start: int = 0) -> Iterator[tuple[int, torch.Tensor, torch.Tensor]]:
+    """(index, input_ids int64 [batch, seq_len], assistant_mask bool) micro-batches on the host."""
+    for index, rows in batch_rows(len(ids), batch_size, seed, epoch, start):
+        yield (index, torch.from_numpy(ids[rows].astype(np.int64)),
+               torch.from_numpy(mask[rows].astype(np.bool_)))
+
+
+class DevicePrefetcher:
+    """Feeds host micro-batches to one GPU: each is copied into pinned buffers and sent with a
+    non-blocking copy on a dedicated stream, one micro-batch ahead. Iterating yields
+    (index, ids, mask) already on the device; the consumer's stream waits for the copy."""
+
+    def __init__(self, host_batches: Iterator[tuple[int, torch.Tensor, torch.Tensor]], device):
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("DevicePrefetcher feeds a CUDA device")
+        self.source = iter(host_batches)
+        self.stream = torch.cuda.Stream(self.device)
+        self.pending = None
+        self._issue()
+
+    def _issue(self) -> None:
+        item = next(self.source, None)
+        if item is None:
+            self.pending = None
+            return
+        index, ids, mask = item
+        ids_pin, mask_pin = ids.pin_memory(), mask.pin_memory()
+        with torch.cuda.stream(self.stream):
+            ids_dev = ids_pin.to(self.device, non_blocking=True)
+            mask_dev = mask_pin.to(self.device, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(self.stream)
+        self.pending = (index, ids_dev, mask_dev, done, ids_pin, mask_pin)
+
+    def __iter__(self):
+        return self
+
+    def __next__(self):
+        if self.pending is None:
+            raise StopIteration
+        index, ids_dev, mask_dev, done, _, _ = self.pending
+        consumer = torch.cuda.current_stream(self.device)
+        consumer.wait_event(done)
+        ids_dev.record_stream(consumer)
+        mask_dev.record_stream(consumer)
+        self._issue()
+        return index, ids_dev, mask_dev
+
+
+def save_checkpoint(path: Path, model, optimizer, scheduler, state: dict) -> None:
+    """Twin weights, optimizer / scheduler state and progress, written atomically."""
+    from safetensors.torch import save_file
+
+    path = Path(path)
+    tmp = path.with_name(path.name + ".tmp")
+    shutil.rmtree(tmp, ignore_errors=True)
+    tmp.mkdir(parents=True)
+    weights = {n: p.detach().contiguous() for n, p in model.named_parameters() if p.requires_grad}
+    save_file(weights, tmp / WEIGHTS)
+    torch.save({"optimizer": optimizer.state_dict(), "scheduler": scheduler.state_dict()}, tmp / OPTIMIZER)
+    (tmp / STATE).write_text(json.dumps(state, indent=2), encoding="utf-8")
+    shutil.rmtree(path, ignore_errors=True)
+    os.replace(tmp, path)
+
+
+def load_checkpoint(path: Path, model, optimizer=None, scheduler=None) -> dict:
+    """Restores the twins (their names must be exactly the model's trainable parameters) and, when
+    given, the optimizer and scheduler; returns the saved progress state."""
+    from safetensors.torch import load_file
+
+    path = Path(path)
+    device = next(model.parameters()).device
+    weights = load_file(path / WEIGHTS, device=str(device))
+    trainable = {n for n, p in model.named_parameters() if p.requires_grad}
+    if set(weights) != trainable:
+        raise RuntimeError(f"checkpoint {path} does not match the trainable parameters")
+    with torch.no_grad():
+        for name, param in model.named_parameters():
+            if name in weights:
+                param.copy_(weights[name])
+    if optimizer is not None:
+        blob = torch.load(path / OPTIMIZER, map_location=device, weights_only=False)
+        optimizer.load_state_dict(blob["optimizer"])
+        if scheduler is not None:
+            scheduler.load_state_dict(blob["scheduler"])
+    return json.loads((path / STATE).read_text(encoding="utf-8"))

@@ -2,7 +2,8 @@
 
 Run in a container that has the reference checked out (it is pure Python):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py /root/reference          # every fixture
+    python tests/golden/make_golden.py /root/reference data     # data_batches.pt only
 
 It imports the reference's own modules (orthrus.modeling_orthrus, orthrus.objective,
 orthrus.decoding, orthrus.evaluate) and stores seeded inputs together with the reference outputs,
@@ -300,15 +301,35 @@ def config1_decode(mo, ev) -> dict:
     return {"config": config_dict(model), "params": sd, "cases": cases}
 
 
-def main(reference: str) -> None:
+def data_batches(data) -> dict:
+    """The reference's micro-batch order (orthrus/data.py:89-103) for a few (seed, epoch, start)."""
+    import numpy as np
+
+    rng = np.random.default_rng(123)
+    ids = rng.integers(0, 1000, size=(37, 16), dtype=np.int32)
+    mask = (rng.random((37, 16)) < 0.5).astype(np.uint8)
+    cases = []
+    for seed, epoch, bs, start in ((0, 0, 4, 0), (3, 1, 5, 2), (7, 2, 8, 1)):
+        out = [(i, x.clone(), m.clone()) for i, x, m in data.batches(ids, mask, bs, seed, epoch, start)]
+        cases.append({"seed": seed, "epoch": epoch, "batch_size": bs, "start": start,
+                      "index": [o[0] for o in out], "ids": [o[1] for o in out], "mask": [o[2] for o in out]})
+    return {"ids": torch.from_numpy(ids), "mask": torch.from_numpy(mask), "cases": cases}
+
+
+def main(reference: str, only: str | None = None) -> None:
     sys.path.insert(0, reference)
     from orthrus import decoding as dec
     from orthrus import evaluate as ev
     from orthrus import modeling_orthrus as mo
     from orthrus import objective as ob
 
+    from orthrus import data
+
     torch.set_num_threads(4)
     meta = _versions()
+    torch.save({"meta": meta, **data_batches(data)}, HERE / "data_batches.pt")
+    if only == "data":
+        return
     torch.save({"meta": meta, **kl_kat(ob)}, HERE / "kl_kat.pt")
     torch.save({"meta": meta, **mask_kat(mo)}, HERE / "mask_kat.pt")
     torch.save({"meta": meta, **config1(mo, ob)}, HERE / "config1.pt")
@@ -319,4 +340,5 @@ def main(reference: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference",
+         sys.argv[2] if len(sys.argv) > 2 else None)

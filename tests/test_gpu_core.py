@@ -156,3 +156,19 @@ def test_no_device_error_left():
     from orthrus_training_b200 import _lib
 
     assert _lib.device_error(0) == 0
+
+
+def test_device_prefetcher_delivers_the_host_batches():
+    """Micro-batches reach the device one ahead of use, with the host order and contents."""
+    import numpy as np
+
+    from orthrus_training_b200.data_io import DevicePrefetcher, batches
+
+    rng = np.random.default_rng(1)
+    ids = rng.integers(0, 1000, size=(20, 64), dtype=np.int32)
+    mask = (rng.random((20, 64)) < 0.5).astype(np.uint8)
+    host = list(batches(ids, mask, 4, 5, 0))
+    got = list(DevicePrefetcher(batches(ids, mask, 4, 5, 0), DEV))
+    assert [g[0] for g in got] == [h[0] for h in host]
+    for (_, gi, gm), (_, hi, hm) in zip(got, host):
+        assert gi.is_cuda and torch.equal(gi.cpu(), hi) and torch.equal(gm.cpu(), hm)
