@@ -70,6 +70,22 @@ int orthrus_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, vo
                       int64_t M, int64_t N, int64_t K, int b_kn, int c_f32, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* Projection GEMM with the layer's elementwise tail in the epilogue, bf16 in and out:
+ *   ORTHRUS_LINEAR_STORE     y[M, N] = x[M, K] @ w[N, K]^T                      (F.linear)
+ *   ORTHRUS_LINEAR_RESIDUAL  y = residual + x @ w^T, fp32 sum rounded once      (torch.addmm)
+ *   ORTHRUS_LINEAR_SWIGLU    w = [gate; up] [2N, K]: y[M, N] = silu(g) * u, g and u rounded to bf16
+ *                            and silu rounded before the product (F.linear then F.silu(gate) * up)
+ * N a multiple of 128, K a multiple of 8, leading dimensions multiples of 8 elements, pointers
+ * 16-byte aligned; residual has leading dimension ldy and does not alias y. Persistent tcgen05
+ * kernel, one CTA per SM. Replaces the projections and activations of _attention_inputs and
+ * _mlp_residual (orthrus/objective.py:136-149) on the frozen teacher pass. */
+#define ORTHRUS_LINEAR_STORE 0
+#define ORTHRUS_LINEAR_RESIDUAL 1
+#define ORTHRUS_LINEAR_SWIGLU 2
+int orthrus_linear_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* residual,
+                        void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int epilogue,
+                        void* stream);
+
 /* Same contract for fp32 (or bf16-in, fp32-accumulate) operands on CUDA cores, B as [N, K]:
  * exact fp32 arithmetic with a fixed reduction order that does not depend on M. */
 size_t orthrus_gemm_simt_workspace_bytes(int64_t M, int64_t N, int64_t K);

@@ -11,6 +11,7 @@
 #include "decode.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
+#include "linear_tc.cuh"
 #include "lmhead_kl.cuh"
 #include "qkv_prep.cuh"
 #include "rowwise.cuh"
@@ -49,6 +50,11 @@ int orthrus_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, vo
                       void* stream) {
   return gemm_bf16_impl(A, lda, B, ldb, C, ldc, M, N, K, b_kn, c_f32, workspace, workspace_bytes,
                         as_stream(stream));
+}
+
+int orthrus_linear_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* residual, void* y,
+                        int64_t ldy, int64_t M, int64_t N, int64_t K, int epilogue, void* stream) {
+  return linear_bf16_impl(x, ldx, w, ldw, residual, y, ldy, M, N, K, epilogue, as_stream(stream));
 }
 
 size_t orthrus_gemm_simt_workspace_bytes(int64_t M, int64_t N, int64_t K) { return simt_ws_bytes(M, N, K); }

@@ -1,0 +1,294 @@
+// Projection GEMMs of the Qwen3 layers with their elementwise tails fused into the epilogue:
+// Y = epilogue(X[M, K] @ W^T), bf16 operands, fp32 accumulation in tensor memory.
+//
+//   kLinearStore     Y[M, N] = acc                                   (F.linear)
+//   kLinearResidual  Y[M, N] = R[M, N] + acc, one rounding            (torch.addmm(R, X, W^T))
+//   kLinearSwiGLU    W = [gate; up] of shape [2F, K]; Y[M, F] = silu(g) * u with g and u rounded
+//                    to bf16 first and silu rounded before the product (F.linear followed by
+//                    F.silu(gate) * up, orthrus/objective.py:146-149), so [gate | up] is never
+//                    written to or read back from HBM.
+//
+// One CTA per SM loops over 128-row x 256-accumulator-column tiles in m-major order (the CTAs in
+// flight share one weight panel in L2 and read each activation panel from HBM once), 320 threads:
+//   warp 0     TMA producer: X and W k-blocks of 64 (one 128-byte swizzle atom) into a 4-stage ring;
+//              W arrives as two 128-row boxes (the two halves of the tile, or gate and up rows);
+//   warp 1     TMEM allocation and the single-thread tcgen05.mma issue loop (UMMA 128 x 256 x 16)
+//              into one of two 256-column accumulators, so the epilogue of tile t overlaps the
+//              mainloop of tile t + 1;
+//   warps 2-9  epilogue, two warps per TMEM lane quarter splitting the columns: tcgen05.ld
+//              (TMEM lane = output row), the fused tail, 64-byte row stores.
+// Every wait is bounded; on a timeout the CTA records the error, drains its copies and returns.
+#pragma once
+
+#include "sm100.cuh"
+#include "rowwise.cuh"
+
+namespace orthrus {
+
+enum LinearEpilogue { kLinearStore = 0, kLinearResidual = 1, kLinearSwiGLU = 2 };
+
+struct LinearTile {
+  static constexpr int BM = 128, BN = 256, BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;    // 16 KB
+  static constexpr int B_HALF = 128 * BK * 2;    // 16 KB: one 128-row W box
+  static constexpr int B_BYTES = 2 * B_HALF;     // 32 KB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = 4;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+};
+
+// silu(g) = g / (1 + exp(-g)) with exp(-g) = 2^(-g log2 e) on ex2.approx and an approximate
+// reciprocal: within a few fp32 ulps of the IEEE form, far below the bf16 rounding that follows.
+__device__ __forceinline__ float silu_fast(float g) {
+  return __fdividef(g, 1.f + ex2_approx(-g * kLog2e));
+}
+
+// Tile t -> (m tile, n tile) and the first W row of each 128-row half of the accumulator.
+struct LinearGeometry {
+  int M, N, K, ntiles, tiles, f_rows;  // f_rows: F (up rows start there) for SwiGLU, else 0
+  __device__ __forceinline__ void tile(int t, int epi, int& m0, int& n0, int& w0, int& w1) const {
+    const int mt = t / ntiles, nt = t % ntiles;
+    m0 = mt * LinearTile::BM;
+    if (epi == kLinearSwiGLU) {
+      n0 = nt * 128;
+      w0 = n0;
+      w1 = f_rows + n0;
+    } else {
+      n0 = nt * LinearTile::BN;
+      w0 = n0;
+      // N is a multiple of 128: the upper half is either wholly inside W or wholly past its end,
+      // in which case the lower rows are loaded again and their columns never stored
+      w1 = n0 + 128 < N ? n0 + 128 : n0;
+    }
+  }
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(LinearTile::THREADS, 1)
+    linear_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                     const LinearGeometry g, __nv_bfloat16* __restrict__ Y, int64_t ldy,
+                     const __nv_bfloat16* __restrict__ R) {
+  using T = LinearTile;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + T::STAGES * T::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + T::STAGES * T::B_BYTES);
+  uint64_t* empty = full + T::STAGES;
+  uint64_t* acc_full = empty + T::STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;      // [2]
+  uint64_t* mma_drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KB = (g.K + T::BK - 1) / T::BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < T::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], T::EPI_WARPS);
+    }
+    mbar_init(mma_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      prefetch_tensormap(&tmX);
+      prefetch_tensormap(&tmW);
+      int it = 0, issued = 0;
+      for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x) {
+        int m0, n0, w0, w1;
+        g.tile(t, EPI, m0, n0, w0, w1);
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % T::STAGES;
+          if (!mbar_wait(&empty[s], ((it / T::STAGES) & 1) ^ 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], T::STAGE_BYTES);
+          tma_load_2d(sA + s * T::A_BYTES, &tmX, &full[s], kb * T::BK, m0);
+          tma_load_2d(sB + s * T::B_BYTES, &tmW, &full[s], kb * T::BK, w0);
+          tma_load_2d(sB + s * T::B_BYTES + T::B_HALF, &tmW, &full[s], kb * T::BK, w1);
+          issued = it + 1;
+        }
+      }
+      if (*abort_flag)
+        for (int i = max(0, issued - T::STAGES); i < issued; ++i)
+          mbar_wait_short(&full[i % T::STAGES], (i / T::STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = umma_idesc_bf16(128, T::BN, false, false);
+      int it = 0, tt = 0;
+      for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x, ++tt) {
+        const int b = tt & 1;
+        const uint32_t acc = tmem + b * T::BN;
+        if (!mbar_wait(&acc_empty[b], ((tt >> 1) & 1) ^ 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % T::STAGES;
+          if (!mbar_wait(&full[s], (it / T::STAGES) & 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + s * T::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + s * T::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < T::BK / 16; ++k)
+            umma_f16(acc, umma_desc_sw128(a_base + k * 32, 16, 1024), umma_desc_sw128(b_base + k * 32, 16, 1024),
+                     idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&acc_full[b]);
+      }
+      // every MMA this thread issued has completed before the accumulators are freed
+      umma_commit(mma_drain);
+      mbar_wait_short(mma_drain, 0);
+    }
+  } else {
+    const int quarter = warp & 3;          // TMEM lanes this warp may read
+    const int half = (warp - 2) >> 2;      // which half of the tile's columns it takes
+    int tt = 0;
+    for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x, ++tt) {
+      const int b = tt & 1;
+      if (!mbar_wait(&acc_full[b], (tt >> 1) & 1)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      int m0, n0, w0, w1;
+      g.tile(t, EPI, m0, n0, w0, w1);
+      const int row = m0 + quarter * 32 + lane;
+      const bool row_ok = row < g.M;
+      const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + b * T::BN;
+      if constexpr (EPI == kLinearSwiGLU) {
+#pragma unroll 1
+        for (int c = 2 * half; c < 2 * half + 2; ++c) {
+          float gv[32], uv[32];
+          tmem_ld32(base + c * 32, gv);
+          tmem_ld32(base + 128 + c * 32, uv);
+          tmem_wait_ld();
+          if (!row_ok) continue;
+          __nv_bfloat16* dst = Y + static_cast<int64_t>(row) * ldy + n0 + c * 32;
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            float h[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float gr = round_to_t<__nv_bfloat16>(gv[j + e]);
+              const float ur = round_to_t<__nv_bfloat16>(uv[j + e]);
+              h[e] = round_to_t<__nv_bfloat16>(silu_fast(gr)) * ur;
+            }
+            *reinterpret_cast<uint4*>(dst + j) = make_uint4(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]),
+                                                            pack_bf16x2(h[4], h[5]), pack_bf16x2(h[6], h[7]));
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 4 * half; c < 4 * half + 4; ++c) {
+          const int col0 = n0 + c * 32;
+          uint4 rv[4];
+          const bool store = row_ok && col0 < g.N;
+          if constexpr (EPI == kLinearResidual) {
+            if (store) {
+              const uint4* src = reinterpret_cast<const uint4*>(R + static_cast<int64_t>(row) * ldy + col0);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) rv[j] = src[j];
+            }
+          }
+          float v[32];
+          tmem_ld32(base + c * 32, v);
+          tmem_wait_ld();
+          if (!store) continue;
+          if constexpr (EPI == kLinearResidual) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t w[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                v[j * 8 + 2 * e] += __uint_as_float(w[e] << 16);
+                v[j * 8 + 2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
+              }
+            }
+          }
+          __nv_bfloat16* dst = Y + static_cast<int64_t>(row) * ldy + col0;
+#pragma unroll
+          for (int j = 0; j < 32; j += 8)
+            *reinterpret_cast<uint4*>(dst + j) = make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
+                                                            pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_free(tmem, 512);
+  }
+}
+
+// Host side. N is the number of output columns (F for SwiGLU, whose W has 2F rows); N must be a
+// multiple of 128, K a multiple of 8, leading dimensions multiples of 8 elements. R (residual) has
+// the leading dimension of Y and is a separate buffer.
+inline int linear_bf16_impl(const void* X, int64_t ldx, const void* W, int64_t ldw, const void* R, void* Y,
+                            int64_t ldy, int64_t M, int64_t N, int64_t K, int epilogue, cudaStream_t stream) {
+  ORTHRUS_CHECK_ARG(X && W && Y && M >= 0 && N > 0 && K > 0);
+  ORTHRUS_CHECK_ARG(epilogue == kLinearStore || epilogue == kLinearResidual || epilogue == kLinearSwiGLU);
+  ORTHRUS_CHECK_ARG(epilogue != kLinearResidual || (R != nullptr && R != Y));
+  ORTHRUS_CHECK_ARG(N % 128 == 0 && K % 8 == 0 && ldx >= K && ldw >= K && ldy >= N);
+  ORTHRUS_CHECK_ARG(ldx % 8 == 0 && ldw % 8 == 0 && ldy % 8 == 0);
+  ORTHRUS_CHECK_ARG(aligned16(X) && aligned16(W) && aligned16(Y) && (R == nullptr || aligned16(R)));
+  ORTHRUS_CHECK_ARG(M < (1ll << 31) && N < (1ll << 30) && K < (1ll << 31));
+  if (M == 0) return ORTHRUS_OK;
+  using T = LinearTile;
+  const int64_t w_rows = epilogue == kLinearSwiGLU ? 2 * N : N;
+  CUtensorMap tx, tw;
+  if (!make_tmap_2d_bf16(&tx, X, K, M, ldx, 64, 128)) return ORTHRUS_ECUDA;
+  if (!make_tmap_2d_bf16(&tw, W, K, w_rows, ldw, 64, 128)) return ORTHRUS_ECUDA;
+  LinearGeometry g;
+  g.M = static_cast<int>(M);
+  g.N = static_cast<int>(N);
+  g.K = static_cast<int>(K);
+  g.ntiles = static_cast<int>(epilogue == kLinearSwiGLU ? N / 128 : ceil_div(N, T::BN));
+  const int64_t tiles = ceil_div(M, T::BM) * g.ntiles;
+  ORTHRUS_CHECK_ARG(tiles < (1ll << 31));
+  g.tiles = static_cast<int>(tiles);
+  g.f_rows = epilogue == kLinearSwiGLU ? static_cast<int>(N) : 0;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, num_sms()));
+  auto* y = static_cast<__nv_bfloat16*>(Y);
+  auto* r = static_cast<const __nv_bfloat16*>(R);
+  if (epilogue == kLinearStore) {
+    ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearStore>, T::SMEM));
+    linear_tc_kernel<kLinearStore><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, g, y, ldy, nullptr);
+  } else if (epilogue == kLinearResidual) {
+    ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearResidual>, T::SMEM));
+    linear_tc_kernel<kLinearResidual><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, g, y, ldy, r);
+  } else {
+    ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearSwiGLU>, T::SMEM));
+    linear_tc_kernel<kLinearSwiGLU><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, g, y, ldy, nullptr);
+  }
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+}  // namespace orthrus

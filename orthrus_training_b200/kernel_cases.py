@@ -15,6 +15,10 @@ Cases (B = 8 rows of 2048 tokens, 16 query / 8 KV heads of 128, A = 32 anchors, 
            rows, V = 151936, d = 1024                              (orthrus/objective.py:338-392)
   prologue q/k RMSNorm + RoPE + head-major scatter of the teacher's fused q|k|v projection
            (16384 rows of 32 heads x 128), forward and backward    (orthrus/objective.py:136-143)
+  linear   the teacher layer's projections at 16384 rows (d = 1024, q|k|v 4096, o 2048 -> 1024, gate|up
+           2 x 3072, down 3072 -> 1024), each through torch / cuBLAS (plus orthrus_swiglu_fwd for
+           the MLP) and through the fused persistent kernel orthrus_linear_bf16
+                                                                   (orthrus/objective.py:136-149)
   sweep    dual-view attention forward + backward over L in {1024, 2048, 4096, 8192}, K in
            {16, 32, 64}, A in {8, 32, 64} (batch filling 16384 query tokens, capped at 65536 keys
            per head), and the fused LM head + KL over N in {4096, 16384, 65536} student rows
@@ -105,6 +109,27 @@ def run(case: str, iters: int, warmup: int) -> dict:
         timed.append(("qkv_prep_bwd", lambda: ops.qkv_prep_backward(qkv, pos, inv, qw, kw, rstd, dq, dk, dv, B, L,
                                                                     HQ, HKV, HD, HD),
                       rows * H * HD * (2 + 4 + 2)))
+    elif case == "linear":
+        rows, d, ff, hq = B * L, 1024, 3072, HQ * HD
+        x = torch.randn(rows, d, device=dev, generator=gen).bfloat16()
+        o = torch.randn(rows, hq, device=dev, generator=gen).bfloat16()
+        a = torch.randn(rows, ff, device=dev, generator=gen).bfloat16()
+        w_qkv = (torch.randn((HQ + 2 * HKV) * HD, d, device=dev, generator=gen) * 0.03).bfloat16()
+        w_o = (torch.randn(d, hq, device=dev, generator=gen) * 0.02).bfloat16()
+        w_gu = (torch.randn(2 * ff, d, device=dev, generator=gen) * 0.03).bfloat16()
+        w_d = (torch.randn(d, ff, device=dev, generator=gen) * 0.02).bfloat16()
+        fl = lambda n, k: 2.0 * rows * n * k
+        timed += [
+            ("qkv_cublas", lambda: x @ w_qkv.t(), fl(w_qkv.shape[0], d)),
+            ("qkv_fused", lambda: ops.linear(x, w_qkv), fl(w_qkv.shape[0], d)),
+            ("o_residual_cublas", lambda: torch.addmm(x, o, w_o.t()), fl(d, hq)),
+            ("o_residual_fused", lambda: ops.linear(o, w_o, residual=x), fl(d, hq)),
+            ("gate_up_cublas", lambda: x @ w_gu.t(), fl(2 * ff, d)),
+            ("gate_up_swiglu_cublas", lambda: ops.silu_mul(x @ w_gu.t()), fl(2 * ff, d)),
+            ("gate_up_swiglu_fused", lambda: ops.linear_swiglu(x, w_gu), fl(2 * ff, d)),
+            ("down_residual_cublas", lambda: torch.addmm(x, a, w_d.t()), fl(d, ff)),
+            ("down_residual_fused", lambda: ops.linear(a, w_d, residual=x), fl(d, ff)),
+        ]
     else:
         raise ValueError(f"unknown case {case!r}")
     out = {}
@@ -163,7 +188,7 @@ def sweep(iters: int, warmup: int):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("case", choices=["causal", "dual", "dualbwd", "lmhead", "prologue", "sweep"])
+    ap.add_argument("case", choices=["causal", "dual", "dualbwd", "lmhead", "prologue", "linear", "sweep"])
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=2)
     args = ap.parse_args()

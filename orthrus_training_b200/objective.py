@@ -163,7 +163,13 @@ def _teacher_layer(model, i, x, pos, B, L, inv):
     # residual adds ride in the GEMM epilogue (beta = 1)
     x = torch.addmm(x, o.view(B * L, Hq * hd), attn.o_proj.weight.t())
     h = ops.rms_norm(x, layer.post_attention_layernorm.weight, eps)
-    x = torch.addmm(x, ops.silu_mul(h @ model._packed_mlp(i).t()), layer.mlp.down_proj.weight.t())
+    w_gu = model._packed_mlp(i)
+    if ops.fused_linear_supported(h, w_gu, w_gu.shape[0] // 2):
+        # gate/up GEMM with SwiGLU in its epilogue: [gate | up] never goes through HBM
+        act = ops.linear_swiglu(h, w_gu)
+    else:
+        act = ops.silu_mul(h @ w_gu.t())
+    x = torch.addmm(x, act, layer.mlp.down_proj.weight.t())
     return x, k, v
 
 

@@ -85,6 +85,55 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, b_kn: bool = False, out_dtype=None
     return c
 
 
+LINEAR_STORE, LINEAR_RESIDUAL, LINEAR_SWIGLU = 0, 1, 2
+
+
+def fused_linear_supported(x: torch.Tensor, w: torch.Tensor, n_out: int) -> bool:
+    """Shapes and dtypes orthrus_linear_bf16 takes (bf16, N a multiple of 128, K of 8)."""
+    return (x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2
+            and n_out % 128 == 0 and x.shape[1] % 8 == 0)
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+    """x [M, K] @ w [N, K]^T, plus residual [M, N] in the epilogue when given (torch.addmm with
+    beta = 1), on the persistent tcgen05 projection kernel."""
+    _require_cuda(x, w, residual)
+    x = x.contiguous()
+    w = w.contiguous()
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K or not fused_linear_supported(x, w, N):
+        raise ValueError(f"linear takes bf16 x [M, K] and w [N, K] with N % 128 == 0, K % 8 == 0; "
+                         f"got {tuple(x.shape)} {x.dtype} x {tuple(w.shape)} {w.dtype}")
+    y = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    epi = LINEAR_STORE
+    if residual is not None:
+        residual = residual.contiguous()
+        if residual.shape != (M, N) or residual.dtype != x.dtype:
+            raise ValueError("residual must be [M, N] in the dtype of x")
+        epi = LINEAR_RESIDUAL
+    L.check(L.lib().orthrus_linear_bf16(x.data_ptr(), K, w.data_ptr(), K, L.ptr(residual), y.data_ptr(),
+                                        N, M, N, K, epi, L.stream_of(x.device)), "linear_bf16")
+    return y
+
+
+def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor) -> torch.Tensor:
+    """silu(x @ gate^T) * (x @ up^T) for w_gate_up = [gate; up] [2F, K], without writing the
+    [gate | up] projection (same roundings as silu_mul(x @ w_gate_up^T))."""
+    _require_cuda(x, w_gate_up)
+    x = x.contiguous()
+    w_gate_up = w_gate_up.contiguous()
+    M, K = x.shape
+    F = w_gate_up.shape[0] // 2
+    if w_gate_up.shape != (2 * F, K) or not fused_linear_supported(x, w_gate_up, F):
+        raise ValueError(f"linear_swiglu takes bf16 x [M, K] and w [2F, K] with F % 128 == 0; got "
+                         f"{tuple(x.shape)} x {tuple(w_gate_up.shape)}")
+    y = torch.empty(M, F, dtype=x.dtype, device=x.device)
+    L.check(L.lib().orthrus_linear_bf16(x.data_ptr(), K, w_gate_up.data_ptr(), K, None, y.data_ptr(), F,
+                                        M, F, K, LINEAR_SWIGLU, L.stream_of(x.device)), "linear_swiglu")
+    return y
+
+
 def lmhead_kl(student, teacher, index, weight, row_weight=None, offsets=None, num_offsets=0,
               need_grad=True, chunk_rows=4096):
     """Fused LM head + log-softmax + KL(teacher || student) (FusedLinearForwardKL.forward math).

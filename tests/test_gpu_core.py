@@ -60,6 +60,62 @@ def test_gemm_simt_fp32_exact_and_batch_invariant():
         assert torch.equal(_ops().gemm(x[:rows].contiguous(), w), full[:rows])
 
 
+def _bf16(t):
+    return t.bfloat16().float()
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 512, 320), (16384 // 8, 4096, 1024), (129, 1024, 3072),
+                                   (1000, 384, 72)])
+def test_fused_linear_store_and_residual(M, N, K):
+    """orthrus_linear_bf16 (persistent tcgen05 kernel) against fp32 torch: ragged M, N with a
+    half-empty last tile (384 = 256 + 128), K not a multiple of 64. Store: one rounding of the fp32
+    product; residual: the fp32 sum rounded once (torch.addmm with beta = 1)."""
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    x = torch.randn(M, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=DEV, generator=g) / K ** 0.5).bfloat16()
+    r = torch.randn(M, N, device=DEV, generator=g).bfloat16()
+    ref = x.double() @ w.double().t()
+    y = _ops().linear(x, w)
+    yr = _ops().linear(x, w, residual=r)
+    torch.cuda.synchronize()
+    # fp32 accumulation in another order: compare within a bf16 rounding of the result
+    assert (y.double() - ref).abs().max().item() <= 8e-3 * ref.abs().max().item() + 1e-3
+    ref_r = ref + r.double()
+    assert (yr.double() - ref_r).abs().max().item() <= 8e-3 * ref_r.abs().max().item() + 1e-3
+    # the epilogue rounds once: residual form equals rounding (fp32 product + residual)
+    prod = (x.float() @ w.float().t())
+    assert (yr.float() - (prod + r.float()).bfloat16().float()).abs().max().item() <= \
+        2e-2 * ref_r.abs().max().item()
+
+
+@pytest.mark.parametrize("M,F,K", [(300, 256, 320), (2048, 3072, 1024), (77, 768, 256)])
+def test_fused_linear_swiglu_matches_silu_mul(M, F, K):
+    """SwiGLU epilogue against the unfused path silu_mul(x @ [gate; up]^T): the same roundings
+    (gate and up to bf16, silu to bf16, product to bf16), so the two agree to one bf16 ulp of the
+    inputs' accumulation-order differences."""
+    g = torch.Generator(device=DEV).manual_seed(M + F)
+    x = torch.randn(M, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(2 * F, K, device=DEV, generator=g) / K ** 0.5).bfloat16()
+    h = _ops().linear_swiglu(x, w)
+    gu = (x.double() @ w.double().t()).float()
+    gate, up = _bf16(gu[:, :F]), _bf16(gu[:, F:])
+    ref = _bf16(_bf16(torch.nn.functional.silu(gate)) * up)
+    torch.cuda.synchronize()
+    err = (h.float() - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item(), err
+    # agreement with the two-kernel path on the same GPU (GEMM then orthrus_swiglu_fwd)
+    two = _ops().silu_mul(_ops().linear(x, w))
+    assert (h.float() - two.float()).abs().max().item() <= 2e-2 * ref.abs().max().item()
+
+
+def test_fused_linear_rejects_bad_shapes():
+    x = torch.randn(8, 64, device=DEV).bfloat16()
+    with pytest.raises(ValueError):
+        _ops().linear(x, torch.randn(100, 64, device=DEV).bfloat16())  # N not a multiple of 128
+    with pytest.raises(ValueError):
+        _ops().linear_swiglu(x, torch.randn(2 * 100, 64, device=DEV).bfloat16())
+
+
 def _lmhead_case(n, m, V, d, dtype, seed, weighted):
     g = torch.Generator().manual_seed(seed)
     student = torch.randn(n, d, generator=g)
