@@ -47,6 +47,11 @@ extern "C" {
 #define ORTHRUS_MASK_DUAL 1    /* blk = t / block: e1 = min(anchors[b, blk], L1),               */
                                /* [s2, e2) = [blk*block, blk*block + block)                     */
 #define ORTHRUS_MASK_DRAFT 2   /* e1 = offset[b]; [s2, e2) = [0, min(L2, limit2[b]))             */
+#define ORTHRUS_MASK_TREE 3    /* tree verification over a cache holding the new tokens at rows   */
+                               /* offset[b] + t, passed as both sources: e1 = offset[b] + 1 (the  */
+                               /* prefix and the root t = 0), [s2, e2) = [offset[b] + limit2[t],  */
+                               /* offset[b] + t + 1) (the query's own branch up to itself; limit2 */
+                               /* is per query here, >= 1). Forward only.                         */
 
 /* Library version (major*10000 + minor*100 + patch). */
 int orthrus_version(void);

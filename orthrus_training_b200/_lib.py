@@ -16,7 +16,7 @@ LIB_PATH = Path(__file__).resolve().parent / "liborthrus_b200.so"
 
 OK, EINVAL, ECUDA, EWORKSPACE, EDEVICE = 0, -1, -2, -3, -4
 BF16, F32 = 0, 1
-MASK_CAUSAL, MASK_DUAL, MASK_DRAFT = 0, 1, 2
+MASK_CAUSAL, MASK_DUAL, MASK_DRAFT, MASK_TREE = 0, 1, 2, 3
 ERR_TIMEOUT, ERR_BOUNDS = 1, 2
 
 _P = c_void_p

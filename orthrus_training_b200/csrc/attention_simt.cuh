@@ -39,6 +39,12 @@ __device__ __forceinline__ void query_ranges(const MaskParams& mp, int64_t b, in
     e1 = min(mp.L1, mp.anchors[b * mp.A + blk]);
     s2 = blk * mp.block;
     e2 = min(mp.L2, s2 + mp.block);
+  } else if (mp.mode == ORTHRUS_MASK_TREE) {
+    // the new tokens sit in the cache at rows base + t; source 2 is that same buffer
+    const int64_t base = mp.offset ? mp.offset[b] : 0;
+    e1 = min(mp.L1, base + 1);
+    s2 = base + mp.limit2[t];
+    e2 = min(mp.L2, base + t + 1);
   } else {
     e1 = min(mp.L1, static_cast<int64_t>(mp.offset ? mp.offset[b] : mp.L1));
     s2 = 0;

@@ -147,7 +147,7 @@ __global__ void attn_tilemap_kernel(const int64_t* __restrict__ anchors, int64_t
 // sequence's cached length must be finite (the caches start zeroed).
 bool use_tensor_cores(int dtype, int hd, int D, int mask, const int32_t*) {
   return dtype == ORTHRUS_BF16 && hd == D && (D == 64 || D == 128) && mask >= ORTHRUS_MASK_CAUSAL &&
-         mask <= ORTHRUS_MASK_DRAFT;
+         mask <= ORTHRUS_MASK_TREE;
 }
 
 template <typename Kern>
@@ -234,9 +234,10 @@ int orthrus_attn_fwd(const void* q, const void* k1, const void* v1, int64_t s1h,
                      int64_t Tq, int hd, int D, float scale, int mask, const int64_t* anchors, int64_t A, int block,
                      const int32_t* offset, const int32_t* limit2, void* o, float* lse, int dtype, void* stream) {
   ORTHRUS_CHECK_ARG(q && k1 && v1 && o && B > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && Tq > 0 && L1 >= 0);
-  ORTHRUS_CHECK_ARG(hd > 0 && hd <= D && D <= 128 && mask >= 0 && mask <= 2);
+  ORTHRUS_CHECK_ARG(hd > 0 && hd <= D && D <= 128 && mask >= 0 && mask <= ORTHRUS_MASK_TREE);
   ORTHRUS_CHECK_ARG(mask != ORTHRUS_MASK_DUAL || (anchors && A > 0 && block > 0 && k2 && v2));
   ORTHRUS_CHECK_ARG(mask != ORTHRUS_MASK_DRAFT || k2 != nullptr);
+  ORTHRUS_CHECK_ARG(mask != ORTHRUS_MASK_TREE || (k2 && v2 && offset && limit2));
   ORTHRUS_CHECK_ARG(B < 65536 && Hq < 65536);
   const bool has2 = k2 != nullptr && mask != ORTHRUS_MASK_CAUSAL;
   MaskParams mp{mask, anchors, A, block, offset, limit2, L1, has2 ? L2 : 0};

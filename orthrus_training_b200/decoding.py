@@ -1,5 +1,6 @@
-"""Orthrus parallel block decoding on the Blackwell kernels: drop-in for orthrus/decoding.py (base
-strategy and plain greedy) plus a batched, device-resident decode loop.
+"""Orthrus parallel block decoding on the Blackwell kernels: drop-in for orthrus/decoding.py (the
+base, tail and reuse strategies with tree verification, plain greedy, replay from a draft table,
+draft_table) plus a batched, device-resident decode loop for the base strategy.
 
 ``block_decode`` keeps every piece of the cycle state on the GPU: per-sequence committed cache
 length (``start``), anchor token, done flag, output buffer, accepted counts. One cycle is
@@ -35,7 +36,8 @@ KINDS = ("base", "tail", "reuse")
 
 @dataclass(frozen=True)
 class Strategy:
-    """A decoding strategy (orthrus/decoding.py:41-70). The device path implements kind "base"."""
+    """A decoding strategy (orthrus/decoding.py:41-70): base, tail (extra tree-verified passes over
+    the rejected tail) or reuse (the rejected tail rides along in the next verification)."""
 
     name: str
     kind: str = "base"
@@ -75,14 +77,48 @@ def parse_strategies(specs: list[dict]) -> list[Strategy]:
 
 @dataclass
 class Hypothesis:
+    """A continuation to verify (orthrus/decoding.py:82-86): shift None for the fresh drafts of a
+    block, else the tail shift it was cut with; confidence = diffusion probability of each token."""
+
     shift: int | None
     tokens: list[int]
     confidence: list[float] | None = None
 
 
+def tail_hypotheses(source: Hypothesis, accepted: int, shifts: tuple[int, ...],
+                    room: int) -> list[Hypothesis]:
+    """Tails after a rejection (orthrus/decoding.py:89-107). source.tokens[accepted] lost to the
+    AR token (the bonus); the shift-s continuation of the bonus is source.tokens[accepted + 1 - s:]
+    (s = 0 substitution, 1 insertion, -j deletion of j spurious drafts), at most `room` tokens.
+    Empty continuations and repeats of an earlier shift's tokens are left out; order is kept."""
+    out: list[Hypothesis] = []
+    seen: set[tuple[int, ...]] = set()
+    for shift in shifts:
+        begin = accepted + 1 - shift
+        tokens = list(source.tokens[begin: begin + room])
+        if not tokens or tuple(tokens) in seen:
+            continue
+        seen.add(tuple(tokens))
+        conf = None if source.confidence is None else list(source.confidence[begin: begin + room])
+        out.append(Hypothesis(shift, tokens, conf))
+    return out
+
+
+def expected_tokens(hypothesis: Hypothesis) -> float:
+    """1 + sum_j prod_{i <= j} confidence_i: the tokens a verification of the hypothesis keeps in
+    expectation, the confidences taken as independent acceptance probabilities
+    (orthrus/decoding.py:110-116)."""
+    total = prefix = 1.0
+    for p in hypothesis.confidence or ():
+        prefix *= p
+        total += prefix
+    return total
+
+
 @dataclass
 class Generation:
-    """One decoded output with its pass accounting (orthrus/decoding.py:119-142)."""
+    """One decoded output with its pass accounting (orthrus/decoding.py:119-142). tails holds per
+    tail pass (cycle, shift of the kept hypothesis, accepted, hypotheses, longest hypothesis)."""
 
     strategy: str
     tokens: list[int] = field(default_factory=list)
@@ -106,7 +142,9 @@ class Generation:
 class ModelBackend:
     """Forward passes of an OrthrusLM, batch 1, greedy, with per-kind pass / token / time counts
     (orthrus/decoding.py:145-264). The AR cache holds the committed prefix; the anchor is not in
-    it yet. Verification of several hypotheses (tree masks) is not implemented yet."""
+    it yet. Several hypotheses are verified in one pass with the tree mask of the attention
+    kernels (orthrus_attn_fwd mask TREE); commit() moves the kept branch's cache rows behind the
+    root and drops the rest."""
 
     def __init__(self, model, prompt_ids: list[int], record_drafts: bool = False):
         self.model = model
@@ -120,11 +158,11 @@ class ModelBackend:
         self.passes, self.input_tokens, self.seconds = Counter(), Counter(), Counter()
         self.record_drafts = record_drafts
         self.drafts: dict[int, list[int]] = {}
-        self._layout = None
+        self._layout: tuple[int, list[int]] | None = None
 
     def _timed(self, kind: str, tokens: int, run):
         begin = time.perf_counter()
-        result = run()
+        result = run()  # ends in a host read of the argmax, which synchronises the device
         self.seconds[kind] += time.perf_counter() - begin
         self.passes[kind] += 1
         self.input_tokens[kind] += tokens
@@ -158,42 +196,125 @@ class ModelBackend:
         return drafts
 
     def verify(self, kind: str, start: int, root: int, hypotheses: list[Hypothesis]) -> list:
-        if len(hypotheses) != 1:
-            raise NotImplementedError("tree verification of several hypotheses is not implemented")
-        tokens = [root] + list(hypotheses[0].tokens)
+        """AR pass over the root (position `start`) and every hypothesis after it, all written to
+        the cache at rows start + index; one hypothesis is a causal chain, several a tree (each
+        token sees the prefix, the root and its own branch up to itself, at position start +
+        depth). Returns per hypothesis the AR argmax after the root and after each of its tokens
+        (orthrus/decoding.py:208-241)."""
+        branches = [list(h.tokens) for h in hypotheses]
+        tokens = [root] + [t for b in branches for t in b]
+        depth = [0] + [i + 1 for b in branches for i in range(len(b))]
+        begins, at = [], 1
+        for b in branches:
+            begins.append(at)
+            at += len(b)
+        lo = [1] + [begin for begin, b in zip(begins, branches) for _ in b] if len(branches) > 1 else None
 
         def run():
             ids = torch.tensor([tokens], device=self.device)
-            positions = torch.arange(start, start + len(tokens), device=self.device)[None]
+            positions = torch.tensor([[start + d for d in depth]], device=self.device)
+            tree_lo = None if lo is None else torch.tensor(lo, dtype=torch.int32, device=self.device)
             self.cache.reserve(start + len(tokens))
             logits = self.model(input_ids=ids, position_ids=positions, past_key_values=self.cache,
-                                use_cache=True).logits[0]
+                                use_cache=True, tree_lo=tree_lo).logits[0]
             return ops.argmax_rows(logits.contiguous()).tolist()
 
         preds = self._timed(kind, len(tokens), run)
-        self._layout = start
-        return [preds]
+        self._layout = (start, begins)
+        return [[preds[0]] + preds[begin: begin + len(b)] for begin, b in zip(begins, branches)]
 
     def commit(self, best: int, accepted: int) -> None:
-        """Keep the root and the first `accepted` tokens of the verified chain (a length update)."""
-        self.cache.crop(self._layout + 1 + accepted)
+        """Keep the prefix, the root and the first `accepted` tokens of hypothesis `best` of the
+        last verification (orthrus/decoding.py:243-264): a length update when that hypothesis
+        followed the root, else its K/V rows are first copied behind the root in every layer."""
+        start, begins = self._layout
+        src = start + begins[best]
+        if src != start + 1 and accepted > 0:
+            dst = slice(start + 1, start + 1 + accepted)
+            for k, v in self.cache.buffers():
+                k[:, :, dst] = k[:, :, src: src + accepted].clone()
+                v[:, :, dst] = v[:, :, src: src + accepted].clone()
+        self.cache.crop(start + 1 + accepted)
+
+
+class OracleBackend:
+    """Greedy decoding replayed without a model (orthrus/decoding.py:267-333): AR predictions come
+    from the reference output, drafts from a draft table (row i: the drafts of the block anchored
+    at reference[i]). Exact when real decoding produced the reference with these drafts."""
+
+    def __init__(self, prompt_len: int, reference: list[int], drafts: list[list[int]],
+                 confidence: list[list[float]] | None, block_size: int):
+        self.prompt_len, self.reference, self.block_size = prompt_len, list(reference), block_size
+        self.drafts, self.confidence = drafts, confidence
+        self.passes, self.input_tokens, self.seconds = Counter(), Counter(), Counter()
+
+    def _count(self, kind: str, tokens: int) -> None:
+        self.passes[kind] += 1
+        self.input_tokens[kind] += tokens
+
+    def _index(self, start: int, token: int) -> int:
+        i = start - self.prompt_len
+        if not 0 <= i < len(self.reference) or self.reference[i] != token:
+            raise RuntimeError(f"replay left the reference output at position {start}")
+        return i
+
+    def prefill(self) -> int:
+        self._count("prefill", self.prompt_len)
+        return self.reference[0]
+
+    def draft(self, start: int, anchor: int, block_len: int, confidence: bool) -> Hypothesis:
+        i = self._index(start, anchor)
+        tokens = list(self.drafts[i][: block_len - 1])
+        if len(tokens) != block_len - 1 or min(tokens, default=0) < 0:
+            raise RuntimeError(f"draft table has no block of {block_len} at position {start}")
+        probs = list(self.confidence[i][: block_len - 1]) if confidence else None
+        self._count("draft", block_len)
+        return Hypothesis(None, tokens, probs)
+
+    def verify(self, kind: str, start: int, root: int, hypotheses: list[Hypothesis]) -> list:
+        i = self._index(start, root)
+        self._count(kind, 1 + sum(len(h.tokens) for h in hypotheses))
+        ref = self.reference
+        # the prediction after depth d is the reference token there; past the end: never accepted
+        return [[ref[i + 1 + d] if i + 1 + d < len(ref) else -1 for d in range(len(h.tokens) + 1)]
+                for h in hypotheses]
+
+    def commit(self, best: int, accepted: int) -> None:
+        pass
+
+    def peek(self, start: int, hypotheses: list[Hypothesis]) -> int:
+        """Tokens a verification at `start` would keep (most accepted + 1), without a pass."""
+        i = start - self.prompt_len
+        most = 0
+        for h in hypotheses:
+            n = 0
+            while (n < len(h.tokens) and i + 1 + n < len(self.reference)
+                   and h.tokens[n] == self.reference[i + 1 + n]):
+                n += 1
+            most = max(most, n)
+        return most + 1
 
 
 def _verify(backend, kind, start, root, hypotheses, eos):
-    """Greedy accept of one chain: acceptance ends after an accepted EOS (orthrus/decoding.py:336-351)."""
+    """Verify and keep the hypothesis with the most accepted tokens, the first on ties; acceptance
+    ends after an accepted EOS (orthrus/decoding.py:336-351). Returns (index, accepted, bonus)."""
     preds = backend.verify(kind, start, root, hypotheses)
-    tokens, pred = hypotheses[0].tokens, preds[0]
-    accepted = 0
-    while accepted < len(tokens) and tokens[accepted] == pred[accepted]:
-        accepted += 1
-        if tokens[accepted - 1] in eos:
-            break
-    backend.commit(0, accepted)
-    return 0, accepted, pred[accepted]
+    best, best_accepted = 0, -1
+    for index, (hyp, pred) in enumerate(zip(hypotheses, preds)):
+        n = 0
+        while n < len(hyp.tokens) and hyp.tokens[n] == pred[n]:
+            n += 1
+            if hyp.tokens[n - 1] in eos:
+                break
+        if n > best_accepted:
+            best, best_accepted = index, n
+    backend.commit(best, best_accepted)
+    return best, best_accepted, preds[best][best_accepted]
 
 
 def _advance(gen, start, kept, bonus, eos, max_length):
-    """Append the accepted tokens and the AR bonus (orthrus/decoding.py:354-369)."""
+    """Append the accepted tokens and the AR bonus (orthrus/decoding.py:354-369); returns
+    (finished, position of the new anchor)."""
     for i, token in enumerate(kept):
         if token in eos:
             gen.tokens.extend(kept[: i + 1])
@@ -209,6 +330,20 @@ def _advance(gen, start, kept, bonus, eos, max_length):
     return start >= max_length - 1, start
 
 
+def _worth_a_pass(strategy: Strategy, hypotheses: list[Hypothesis], backend, start: int) -> bool:
+    """The tail-pass gate (orthrus/decoding.py:372-381): a long enough hypothesis, enough expected
+    tokens when min_expected is set, and for replay-only strategies enough tokens kept."""
+    if not hypotheses or max(len(h.tokens) for h in hypotheses) < strategy.min_tail:
+        return False
+    if strategy.min_expected > 0 and max(map(expected_tokens, hypotheses)) < strategy.min_expected:
+        return False
+    if strategy.oracle_min_tokens:
+        if not hasattr(backend, "peek"):
+            raise ValueError(f"strategy {strategy.name} (oracle_min_tokens) is replay-only")
+        return backend.peek(start, hypotheses) >= strategy.oracle_min_tokens
+    return True
+
+
 def _finish(gen, backend):
     gen.passes = dict(backend.passes)
     gen.input_tokens = dict(backend.input_tokens)
@@ -217,22 +352,40 @@ def _finish(gen, backend):
 
 
 def decode(backend, strategy: Strategy, prompt_len: int, max_new_tokens: int, eos: set[int]) -> Generation:
-    """Greedy Orthrus decoding with the base strategy (orthrus/decoding.py:391-429)."""
-    if strategy.kind != "base":
-        raise NotImplementedError("tail / reuse strategies are not implemented on the device path")
+    """Greedy Orthrus decoding with `strategy` on a ModelBackend or OracleBackend
+    (orthrus/decoding.py:391-429). Each cycle drafts a block and verifies it together with the
+    stale tails (reuse); a rejection then yields tail hypotheses that a tail strategy verifies in
+    up to max_tail_passes extra passes, or that reuse carries into the next verification."""
     gen = Generation(strategy.name)
     max_length = prompt_len + max_new_tokens
     gen.tokens.append(backend.prefill())
     gen.eos = done = gen.tokens[-1] in eos
-    start = prompt_len
+    start = prompt_len  # position of the anchor gen.tokens[-1], not in the cache yet
+    stale: list[Hypothesis] = []
     while not done and start < max_length - 1:
         block_len = min(backend.block_size, max_length - start)
         root = gen.tokens[-1]
-        hypotheses = [backend.draft(start, root, block_len, strategy.needs_confidence)]
-        _, accepted, bonus = _verify(backend, "verify", start, root, hypotheses, eos)
+        fresh = backend.draft(start, root, block_len, strategy.needs_confidence)
+        hypotheses = [fresh] + [h for h in stale if h.tokens != fresh.tokens]
+        best, accepted, bonus = _verify(backend, "verify", start, root, hypotheses, eos)
+        kept = hypotheses[best]
         gen.accepted.append(accepted)
-        gen.branch.append(None)
-        done, start = _advance(gen, start, hypotheses[0].tokens[:accepted], bonus, eos, max_length)
+        gen.branch.append(kept.shift)
+        done, start = _advance(gen, start, kept.tokens[:accepted], bonus, eos, max_length)
+        stale, tail_passes = [], 0
+        while strategy.kind != "base" and not done and accepted < len(kept.tokens):
+            tails = tail_hypotheses(kept, accepted, strategy.shifts, max_length - 1 - start)
+            if strategy.kind == "reuse":
+                stale = tails
+                break
+            if tail_passes == strategy.max_tail_passes or not _worth_a_pass(strategy, tails, backend, start):
+                break
+            tail_passes += 1
+            best, accepted, bonus = _verify(backend, "tail", start, gen.tokens[-1], tails, eos)
+            kept = tails[best]
+            gen.tails.append((len(gen.accepted) - 1, kept.shift, accepted, len(tails),
+                              max(len(h.tokens) for h in tails)))
+            done, start = _advance(gen, start, kept.tokens[:accepted], bonus, eos, max_length)
     return _finish(gen, backend)
 
 
@@ -248,6 +401,56 @@ def ar_decode(backend, prompt_len: int, max_new_tokens: int, eos: set[int]) -> G
         start += 1
     gen.eos = gen.tokens[-1] in eos
     return _finish(gen, backend)
+
+
+@torch.inference_mode()
+def draft_table(model, prompt_ids: list[int], reference: list[int], max_new_tokens: int,
+                chunk_blocks: int = 64):
+    """Diffusion drafts at every anchor of a reference output, as decoding draws them after
+    committing reference[: i + 1] (orthrus/decoding.py:447-503): row i holds the block_size - 1
+    drafts of the block anchored at reference[i] (fewer where max_new_tokens cuts the block).
+
+    One AR pass caches the whole output; full blocks then go chunk_blocks at a time through one
+    diffusion pass with the dual-view training mask (orthrus_attn_fwd mask DUAL: AR keys before
+    the anchor, the block's own keys), short blocks one by one. Returns numpy (drafts int32,
+    confidence float32), both [len(reference), block_size - 1], padded with -1 and 0."""
+    from orthrus_training_b200.modeling_orthrus import DualViewMask
+
+    dev = next(model.parameters()).device
+    dtype = next(model.parameters()).dtype
+    K, mask_id = model.config.block_size, model.config.mask_token_id
+    P, max_length = len(prompt_ids), len(prompt_ids) + max_new_tokens
+    full = torch.tensor([list(prompt_ids) + list(reference)], device=dev)
+    total = full.shape[1]
+    cache = KVCache(model.config, batch=1, capacity=total + 8, device=dev, dtype=dtype)
+    model(input_ids=full, past_key_values=cache, use_cache=True, logits_to_keep=1)
+    drafts = torch.full((len(reference), K - 1), -1, dtype=torch.int32)
+    confidence = torch.zeros((len(reference), K - 1), dtype=torch.float32)
+
+    def run(anchors: list[int], block_len: int) -> None:
+        n = len(anchors)
+        a = torch.tensor(anchors, device=dev)
+        ids = torch.full((n, block_len), mask_id, dtype=torch.long, device=dev)
+        ids[:, 0] = full[0, a]
+        positions = (a[:, None] + torch.arange(block_len, device=dev)).view(1, -1)
+        logits = model(input_ids=ids.view(1, -1), position_ids=positions, past_key_values=cache,
+                       use_cache=False, is_diffusion_pass=True, ar_seq_len=total,
+                       flex_block_mask=DualViewMask(a[None], total, block_len)).logits[0]
+        logits = logits.view(n, block_len, -1)[:, :-1].contiguous()
+        tokens = ops.argmax_rows(logits.view(-1, logits.shape[-1])).view(n, block_len - 1)
+        probs = torch.softmax(logits.float(), -1).gather(-1, tokens[..., None])[..., 0]
+        rows = (a - P).cpu()
+        drafts[rows, : block_len - 1] = tokens.to(torch.int32).cpu()
+        confidence[rows, : block_len - 1] = probs.cpu()
+
+    starts = range(P, min(P + len(reference), max_length - 1))
+    full_blocks = [s for s in starts if s + K <= max_length]
+    for i in range(0, len(full_blocks), chunk_blocks):
+        run(full_blocks[i: i + chunk_blocks], K)
+    for s in starts:
+        if s + K > max_length:
+            run([s], max_length - s)
+    return drafts.numpy(), confidence.numpy()
 
 
 # --- batched device-resident decoding ----------------------------------------------------------

@@ -23,7 +23,7 @@ import torch
 from torch import nn
 
 from orthrus_training_b200 import ops
-from orthrus_training_b200._lib import MASK_CAUSAL, MASK_DRAFT, MASK_DUAL
+from orthrus_training_b200._lib import MASK_CAUSAL, MASK_DRAFT, MASK_DUAL, MASK_TREE
 from orthrus_training_b200.kv_cache import KVCache
 
 try:  # the reference configures the model with a plain Qwen3Config plus two fields
@@ -142,6 +142,29 @@ class GenerationStats:
     @property
     def forward_passes(self) -> int:
         return 1 + 2 * self.cycles
+
+
+def tree_mask_to_lo(mask: torch.Tensor, seen: int, T: int) -> torch.Tensor:
+    """int32 [T] branch starts of a dense tree-verification mask [1, 1, T, seen + T] (the form
+    orthrus/decoding.py:222-231 builds): every query sees the whole prefix and the root, and among
+    the other new tokens exactly a contiguous run [lo, t] ending at itself. Raises otherwise."""
+    m = mask.detach().to("cpu", torch.bool)
+    if m.shape != (1, 1, T, seen + T):
+        raise ValueError(f"tree mask must be [1, 1, {T}, {seen + T}], got {tuple(m.shape)}")
+    m = m[0, 0]
+    if not bool(m[:, : seen + 1].all()):
+        raise ValueError("a tree mask shows every query the prefix and the root")
+    lo = torch.ones(T, dtype=torch.int32)
+    for t in range(1, T):
+        row = m[t, seen + 1:]
+        visible = torch.nonzero(row).flatten() + 1
+        start = int(visible.min()) if visible.numel() else t + 1
+        if visible.numel() == 0 or int(visible.max()) != t or visible.numel() != t - start + 1:
+            raise ValueError("each tree-mask query must see a contiguous run of new tokens ending at itself")
+        lo[t] = start
+    if bool(m[0, seen + 1:].any()):
+        raise ValueError("the root sees no other new token")
+    return lo
 
 
 class DualViewMask:
@@ -295,18 +318,28 @@ class OrthrusLM(nn.Module):
         is_diffusion_pass: bool = False,
         ar_seq_len: int | None = None,
         flex_block_mask: DualViewMask | None = None,
+        tree_lo: torch.Tensor | None = None,
         **kwargs,
     ) -> ModelOutput:
         """OrthrusLM.forward (orthrus/modeling_orthrus.py:327-362) for inference: the AR view
         (causal over the cache plus the new tokens, appended to the cache when use_cache) or the
         diffusion view (twin projections over cat([cache[:ar_seq_len], block]); full attention, or
-        the dual-view training mask when flex_block_mask is given). Logits are fp32."""
+        the dual-view training mask when flex_block_mask is given). Logits are fp32.
+
+        Tree verification (orthrus/decoding.py:208-241): an AR pass whose new tokens are a root and
+        several branches, each token seeing the cached prefix, the root and its own branch up to
+        itself. Give either ``tree_lo`` (int32 [T]: the index among the new tokens where each
+        token's branch begins, >= 1) or the reference's dense 4-D boolean mask [1, 1, T, seen + T],
+        which is checked to have that form and converted."""
         if (input_ids is None) == (inputs_embeds is None):
             raise ValueError("pass exactly one of input_ids or inputs_embeds")
-        if attention_mask is not None and attention_mask.dim() == 4:
-            raise ValueError("dense 4-D attention masks (tree verification) are not supported yet")
         x = inputs_embeds if inputs_embeds is not None else self.model.embed_tokens(input_ids)
         B, T, _ = x.shape
+        if attention_mask is not None and attention_mask.dim() == 4:
+            if tree_lo is not None:
+                raise ValueError("pass a 4-D tree mask or tree_lo, not both")
+            seen0 = past_key_values.get_seq_length() if past_key_values is not None else 0
+            tree_lo = tree_mask_to_lo(attention_mask, seen0, T).to(x.device)
         if use_cache and past_key_values is None:
             past_key_values = KVCache(self.config, batch=B, device=x.device, dtype=x.dtype)
         cache = past_key_values
@@ -328,10 +361,16 @@ class OrthrusLM(nn.Module):
             mode = "ar"
             if not use_cache and cache is not None:
                 raise ValueError("an AR pass over a cache must append to it (use_cache=True)")
+            if tree_lo is not None:
+                if cache is None or B != 1:
+                    raise ValueError("tree verification runs on a cache, batch 1")
+                mode = "tree"
         else:
+            if tree_lo is not None:
+                raise ValueError("tree masks belong to AR verification passes")
             mode = "dual" if flex_block_mask is not None else "draft"
         hidden = self.run_layers(x, position_ids, mode, kv=kv, offsets=offsets, ar_len=ar_seq_len,
-                                 block_mask=flex_block_mask)
+                                 block_mask=flex_block_mask, tree_lo=tree_lo)
         if cache is not None and use_cache and not is_diffusion_pass:
             cache.length += T
         if isinstance(logits_to_keep, int):
@@ -353,7 +392,7 @@ class OrthrusLM(nn.Module):
         return logits.view(*shape, -1)
 
     def run_layers(self, x, positions, mode: str, *, kv=None, offsets=None, ar_len=None,
-                   limit2=None, block_mask=None):
+                   limit2=None, block_mask=None, tree_lo=None):
         """The decoder stack over x [B, T, d] at positions [B, T] (int64) -> final-norm hidden.
 
         mode "ar":    AR view; with kv (per-layer [B, Hkv, cap, D] buffers) the new K/V are written
@@ -362,6 +401,8 @@ class OrthrusLM(nn.Module):
         mode "draft": diffusion view over kv rows < offsets[b] plus the block's own keys
                       [0, limit2[b]) (the generation-time draft, orthrus/modeling_orthrus.py:469-481).
         mode "dual":  diffusion view with the training mask (block_mask) over kv rows < ar_len.
+        mode "tree":  AR view writing the new K/V like "ar"; query t sees kv rows
+                      < offsets[b] + 1 and rows [offsets[b] + tree_lo[t], offsets[b] + t + 1).
         """
         cfg = self.config
         B, T, d = x.shape
@@ -376,12 +417,17 @@ class OrthrusLM(nn.Module):
             _, _, _, wo, qn, kn = attn.view_weights(diffusion)
             h = ops.rms_norm(x, layer.input_layernorm.weight, eps)
             qkv = ops.gemm(h, self.packed_qkv(i, diffusion))
-            if mode == "ar" and kv is not None:
+            if mode in ("ar", "tree") and kv is not None:
                 kb, vb = kv[i]
                 q, _, _, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps,
                                           k_cache=kb, v_cache=vb, offset=offsets)
-                o, _ = ops.attention_fwd(q, kb, vb, mask=MASK_CAUSAL, hd=hd, scale=attn.scaling,
-                                         offset=offsets, want_lse=False)
+                if mode == "tree":
+                    o, _ = ops.attention_fwd(q, kb, vb, kb, vb, mask=MASK_TREE, hd=hd,
+                                             scale=attn.scaling, offset=offsets, limit2=tree_lo,
+                                             want_lse=False)
+                else:
+                    o, _ = ops.attention_fwd(q, kb, vb, mask=MASK_CAUSAL, hd=hd, scale=attn.scaling,
+                                             offset=offsets, want_lse=False)
             elif mode == "ar":
                 q, k, v, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps)
                 o, _ = ops.attention_fwd(q, k, v, mask=MASK_CAUSAL, hd=hd, scale=attn.scaling,

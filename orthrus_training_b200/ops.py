@@ -264,10 +264,15 @@ def _src(t):
 def attention_fwd(q, k1, v1, k2=None, v2=None, *, mask: int, hd: int, scale: float,
                   anchors=None, block: int = 0, offset=None, limit2=None, L1: int | None = None,
                   want_lse: bool = True):
-    """Dual-view / causal / draft attention. q [B, Hq, Tq, D]; sources [B, Hkv, rows, D].
+    """Dual-view / causal / draft / tree attention. q [B, Hq, Tq, D]; sources [B, Hkv, rows, D].
+    For the tree mask (3) k2/v2 are the cache k1/v1 holding the new tokens at rows offset[b] + t
+    and limit2 is int32 [Tq]: the first new-token index of each query's branch (>= 1).
     Returns (o [B, Tq, Hq, hd] token-major, lse [B, Hq, Tq] fp32 or None)."""
     _require_cuda(q, k1, v1, k2, v2, anchors, offset, limit2)
     B, Hq, Tq, D = q.shape
+    if mask == 3 and (offset is None or limit2 is None or limit2.dtype != torch.int32
+                      or limit2.numel() != Tq or not limit2.is_contiguous()):
+        raise ValueError("the tree mask takes offset int32 [B] and limit2 int32 [Tq] (branch starts)")
     Hkv = k1.shape[1]
     s1h, s1b, rows1 = _src(k1)
     if v1.stride() != k1.stride():
@@ -287,7 +292,7 @@ def attention_fwd(q, k1, v1, k2=None, v2=None, *, mask: int, hd: int, scale: flo
         L.ptr(limit2), o.data_ptr(), L.ptr(lse), L.dtype_code(q.dtype), L.stream_of(q.device)),
         "attn_fwd")
     if t0 is not None:
-        TIMER.end(f"attn_fwd_{'dual' if mask == 1 else 'causal' if mask == 0 else 'draft'}", t0,
+        TIMER.end(f"attn_fwd_{('causal', 'dual', 'draft', 'tree')[mask]}", t0,
                   attention_flops(mask, B, Hq, Tq, hd, anchors, block, L1))
     return o, lse
 

@@ -275,6 +275,85 @@ def decode_cases(mo, dec, ev) -> dict:
             "eos_case": eos_case}
 
 
+STRATEGY_SPECS = [  # tests/test_decoding.py:20-29
+    {"name": "base"},
+    {"name": "tail-s0", "kind": "tail", "shifts": [0]},
+    {"name": "tail-tree", "kind": "tail", "shifts": [1, 0, -1, -2]},
+    {"name": "tail-x2", "kind": "tail", "shifts": [1, 0, -1], "max_tail_passes": 2},
+    {"name": "tail-gated", "kind": "tail", "shifts": [0], "min_tail": 3, "min_expected": 2.5},
+    {"name": "reuse-tree", "kind": "reuse", "shifts": [1, 0, -1, -2]},
+]
+
+
+def _prompt(seed: int, length: int = 9) -> list[int]:
+    return torch.randint(0, 500, (length,), generator=torch.Generator().manual_seed(seed)).tolist()
+
+
+def _trace(gen) -> dict:
+    return {"tokens": list(gen.tokens), "eos": bool(gen.eos), "passes": dict(gen.passes),
+            "input_tokens": dict(gen.input_tokens), "accepted": list(gen.accepted),
+            "branch": list(gen.branch), "tails": [list(t) for t in gen.tails]}
+
+
+def strategy_cases(mo, dec) -> dict:
+    """orthrus.decoding traces on the lively tiny model (the weights of tiny_decode.pt) for every
+    strategy of tests/test_decoding.py: real decoding with its draft tables
+    (test_replay_from_draft_table_matches_real_decoding), scripted drafts with each edit kind and
+    an EOS (test_tail_strategies_*, test_eos_inside_a_tail_*), a draft table cut into chunks of 4
+    blocks (test_draft_table_matches_decoding_drafts) and one tree verification."""
+    model = lively_model(mo)
+    strategies = dec.parse_strategies(STRATEGY_SPECS)
+    K = model.config.block_size
+
+    class ScriptedBackend(dec.ModelBackend):
+        def __init__(self, model, prompt_ids, table):
+            super().__init__(model, prompt_ids)
+            self.table, self.prompt_len = table, len(prompt_ids)
+
+        def draft(self, start, anchor, block_len, confidence):
+            self._timed("draft", block_len, lambda: None)
+            tokens = self.table[start - self.prompt_len][: block_len - 1]
+            return dec.Hypothesis(None, list(tokens), [0.9] * len(tokens) if confidence else None)
+
+    real = []
+    for seed in range(3):
+        prompt, new = _prompt(20 + seed), 40
+        eos = {_prompt(100 + seed, 1)[0]}
+        traces = {st.name: _trace(dec.decode(dec.ModelBackend(model, prompt), st, len(prompt), new, eos))
+                  for st in strategies}
+        reference = traces["base"]["tokens"]
+        drafts, confidence = dec.draft_table(model, prompt, reference, new)
+        real.append({"prompt": prompt, "max_new": new, "eos": sorted(eos), "traces": traces,
+                     "drafts": torch.from_numpy(drafts), "confidence": torch.from_numpy(confidence)})
+    scripted = []
+    for seed, new, edit, stop_at in ((11, 60, None, None), (12, 60, 0, None), (12, 60, 1, None),
+                                     (12, 60, 2, None), (5, 50, None, 23)):
+        prompt = _prompt(seed)
+        free = dec.ar_decode(dec.ModelBackend(model, prompt), len(prompt), new, set()).tokens
+        eos = set() if stop_at is None else {free[stop_at]}
+        table = scripted_table(free, K, edit)
+        traces = {st.name: _trace(dec.decode(ScriptedBackend(model, prompt, table), st, len(prompt), new, eos))
+                  for st in strategies}
+        scripted.append({"prompt": prompt, "max_new": new, "edit": edit, "eos": sorted(eos),
+                         "free": free, "table": table, "traces": traces})
+    prompt, new = _prompt(2), 30
+    reference = dec.ar_decode(dec.ModelBackend(model, prompt), len(prompt), new, set()).tokens
+    drafts, confidence = dec.draft_table(model, prompt, reference, new, chunk_blocks=4)
+    chunked = {"prompt": prompt, "max_new": new, "reference": reference,
+               "drafts": torch.from_numpy(drafts), "confidence": torch.from_numpy(confidence)}
+    prompt = _prompt(3)
+    g = torch.Generator().manual_seed(7)
+    hyps = [dec.Hypothesis(sh, torch.randint(0, 500, (n,), generator=g).tolist())
+            for sh, n in ((1, 5), (0, 3), (-1, 6))]
+    tree = dec.ModelBackend(model, prompt)
+    root = tree.prefill()
+    preds = tree.verify("tail", len(prompt), root, hyps)
+    tree_case = {"prompt": prompt, "root": root, "hypotheses": [(h.shift, h.tokens) for h in hyps],
+                 "preds": preds}
+    return {"config": config_dict(model), "strategies": STRATEGY_SPECS, "real": real,
+            "scripted": scripted, "chunked": chunked, "tree": tree_case}
+
+
 def config1_decode(mo, ev) -> dict:
     """Config-1 shape (hd 32, K=8), lively weights: diffusion_generate == ar_generate."""
     model = make_model(mo, vocab=1024, hidden=128, inter=384, layers=2, heads=4, kv_heads=2,
@@ -329,6 +408,9 @@ def main(reference: str, only: str | None = None) -> None:
     meta = _versions()
     torch.save({"meta": meta, **data_batches(data)}, HERE / "data_batches.pt")
     if only == "data":
+        return
+    torch.save({"meta": meta, **strategy_cases(mo, dec)}, HERE / "tiny_strategies.pt")
+    if only == "strategies":
         return
     torch.save({"meta": meta, **kl_kat(ob)}, HERE / "kl_kat.pt")
     torch.save({"meta": meta, **mask_kat(mo)}, HERE / "mask_kat.pt")

@@ -109,6 +109,55 @@ def test_teacher_causal_attention(dtype, hd):
     assert (o.float().cpu().transpose(1, 2) - ref).abs().max().item() <= tol
 
 
+def _tree_lo(branches):
+    return [1] + [1 + sum(branches[:g]) for g, n in enumerate(branches) for _ in range(n)]
+
+
+@pytest.mark.parametrize("dtype,hd,offsets,branches", [
+    (torch.bfloat16, 128, [150], [5, 3, 6]),            # tensor-core path, one query tile
+    (torch.bfloat16, 128, [97, 260], [70, 60, 69]),     # two query tiles, per-row offsets
+    (torch.bfloat16, 64, [33], [31]),                   # one branch: the causal verification
+    (torch.float32, 64, [150, 40], [5, 3, 6]),          # CUDA-core path
+])
+def test_tree_mask_attention(dtype, hd, offsets, branches):
+    """Tree verification (mask TREE): the new tokens sit in the cache at rows offset[b] + t;
+    query t sees rows < offset[b] + 1 and its own branch [offset[b] + lo[t], offset[b] + t + 1).
+    Against the dense-mask oracle: bf16 2e-2, fp32 1e-5."""
+    B, Hq, Hkv = len(offsets), 4, 2
+    lo = _tree_lo(branches)
+    T = len(lo)
+    cap = max(offsets) + T + 40
+    g = torch.Generator().manual_seed(T + hd)
+    q = torch.randn(B, Hq, T, hd, generator=g).to(dtype).float()
+    k = torch.randn(B, Hkv, cap, hd, generator=g).to(dtype).float()
+    v = torch.randn(B, Hkv, cap, hd, generator=g).to(dtype).float()
+    mask = torch.zeros(B, T, cap, dtype=torch.bool)
+    for b, off in enumerate(offsets):
+        for t in range(T):
+            mask[b, t, : off + 1] = True
+            mask[b, t, off + lo[t]: off + t + 1] = True
+    ref = O.masked_attention(q.double(), k.double(), v.double(), mask).float()
+    kd, vd = k.to(DEV).to(dtype), v.to(DEV).to(dtype)
+    o, _ = _ops().attention_fwd(q.to(DEV).to(dtype), kd, vd, kd, vd, mask=3, hd=hd, scale=hd ** -0.5,
+                                offset=torch.tensor(offsets, dtype=torch.int32, device=DEV),
+                                limit2=torch.tensor(lo, dtype=torch.int32, device=DEV))
+    torch.cuda.synchronize()
+    got = o.float().cpu().permute(0, 2, 1, 3)
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-5
+    assert (got - ref).abs().max().item() <= tol * max(1.0, ref.abs().max().item())
+
+
+def test_tree_mask_needs_branch_starts():
+    q = torch.zeros(1, 2, 4, 64, device=DEV).bfloat16()
+    k = torch.zeros(1, 2, 16, 64, device=DEV).bfloat16()
+    off = torch.tensor([3], dtype=torch.int32, device=DEV)
+    with pytest.raises(ValueError):
+        _ops().attention_fwd(q, k, k, k, k, mask=3, hd=64, scale=0.125, offset=off)
+    with pytest.raises(ValueError):
+        _ops().attention_fwd(q, k, k, k, k, mask=3, hd=64, scale=0.125, offset=off,
+                             limit2=torch.ones(3, dtype=torch.int32, device=DEV))
+
+
 def test_tilemap_matches_mask():
     anchors = torch.tensor([[3, 10, 30, 200], [1, 2, 36, 500]])
     tm = _ops().attention_tilemap(anchors.to(DEV), 32, 400).cpu()
