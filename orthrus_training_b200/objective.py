@@ -42,23 +42,31 @@ def sample_anchors(assistant_mask: torch.Tensor, block_size: int, num_anchors: i
                    generator: torch.Generator) -> tuple[torch.Tensor, torch.Tensor]:
     """Sorted anchors drawn without replacement from assistant positions in [1, L-K]; spare slots
     repeat the last anchor and are invalid (orthrus/objective.py:37-63). The same torch RNG calls
-    as the reference, so one generator state yields the reference's anchors."""
+    as the reference (one randperm per row over its candidate count), so one generator state
+    yields the reference's anchors. The candidate counts of all rows come to the host in one read;
+    each row's candidates are its assistant positions in ascending order, taken on the device
+    from a stable sort instead of a boolean gather (which would read back a size per row)."""
     batch, seq_len = assistant_mask.shape
     slots = min(num_anchors, seq_len - block_size)
+    span = seq_len - block_size  # candidate positions 1 .. span
     device = assistant_mask.device
-    positions = torch.arange(1, seq_len - block_size + 1, device=device)
+    positions = torch.arange(1, span + 1, device=device)
+    eligible = assistant_mask[:, 1: span + 1].bool()
+    counts = eligible.sum(1).tolist()
+    # per row: the eligible positions first, ascending (stable sort on "not eligible")
+    ranked = torch.sort((~eligible).to(torch.uint8), dim=1, stable=True).indices + 1
     anchors = torch.zeros((batch, slots), dtype=torch.long, device=device)
     valid = torch.zeros((batch, slots), dtype=torch.bool, device=device)
     for row in range(batch):
-        candidates = positions[assistant_mask[row, positions]]
-        has_targets = candidates.numel() > 0
-        if not has_targets:
-            candidates = positions
-        order = torch.randperm(candidates.numel(), generator=generator, device=device)
+        has_targets = counts[row] > 0
+        n = counts[row] if has_targets else span
+        candidates = ranked[row] if has_targets else positions
+        order = torch.randperm(n, generator=generator, device=device)
+        taken = min(slots, n)
         picked = candidates[order[:slots]].sort().values
-        anchors[row, : len(picked)] = picked
-        anchors[row, len(picked):] = picked[-1]
-        valid[row, : len(picked)] = has_targets
+        anchors[row, :taken] = picked
+        anchors[row, taken:] = picked[-1]
+        valid[row, :taken] = has_targets
     return anchors, valid
 
 
@@ -289,19 +297,25 @@ def orthrus_loss(model: OrthrusLM, input_ids: torch.Tensor, assistant_mask: torc
     statistics (orthrus/objective.py:395-453)."""
     K = model.config.block_size
     batch, seq_len = input_ids.shape
-    student, teacher = model_states(model, input_ids, anchors, compiled, kernel_options)
-    hidden = student.shape[-1]
-    student = student.view(batch, -1, K, hidden)[:, :, :-1]
+    # The supervised rows depend on the inputs only. Their layout is settled before the forward is
+    # queued, so its host reads (the kept-row and unique-target counts, bincount's size) happen
+    # while the device is idle rather than between the forward and the LM head.
     keep = supervision_mask(assistant_mask, anchors, valid, K)
     targets = anchors[:, :, None] + torch.arange(K - 1, device=anchors.device)
     targets = targets + seq_len * torch.arange(batch, device=anchors.device)[:, None, None]
-    positions, index = torch.unique(targets[keep], return_inverse=True)
+    kept = torch.nonzero(keep.flatten()).squeeze(1)  # flat (row, anchor, offset) indices
+    positions, index = torch.unique(targets.flatten()[kept], return_inverse=True)
     order = torch.argsort(index, stable=True)
-    offsets = torch.arange(K - 1, device=keep.device).expand_as(keep)[keep][order]
+    kept = kept[order]
+    offsets = kept % (K - 1)
+    student_rows = (kept // (K - 1)) * K + offsets  # row of the block position in [B * A * K]
+    tokens_by_offset = torch.bincount(offsets, minlength=K - 1)
     weights = position_weights(K, gamma, keep.device)
     row_weight = weights[offsets] if weights is not None else None
+    student, teacher = model_states(model, input_ids, anchors, compiled, kernel_options)
+    hidden = student.shape[-1]
     total, kl_rows, agree, kl_by_offset, agree_by_offset = _FusedKL.apply(
-        student[keep][order],
+        student.reshape(-1, hidden).index_select(0, student_rows),
         teacher.flatten(0, 1)[positions].to(student.dtype),
         index[order],
         model.lm_head.weight,
@@ -320,7 +334,7 @@ def orthrus_loss(model: OrthrusLM, input_ids: torch.Tensor, assistant_mask: torc
         "agree": agree.sum(),
         "kl_by_offset": kl_by_offset,
         "agree_by_offset": agree_by_offset,
-        "tokens_by_offset": torch.bincount(offsets, minlength=K - 1),
+        "tokens_by_offset": tokens_by_offset,
         "valid_anchors": valid.float().mean(),
     }
     return total / norm.clamp_min(1e-6), stats

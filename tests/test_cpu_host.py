@@ -37,6 +37,21 @@ def test_anchor_edge_cases():
     assert keep.tolist() == [[[True, True, True], [True, False, False]]]
 
 
+@pytest.mark.parametrize("seed", range(6))
+def test_sample_anchors_equal_the_oracle_draws(seed):
+    """One generator state gives the oracle's anchors (the reference's per-row boolean gather and
+    randperm) for dense, sparse, empty and shorter-than-slots candidate rows."""
+    g = torch.Generator().manual_seed(seed)
+    L, K, A = 160, 8, 12
+    density = torch.tensor([0.9, 0.3, 0.0, 0.04, 0.6])[:, None]
+    mask = torch.rand(5, L, generator=g) < density
+    mask[3, :] = False
+    mask[3, [7, 40, 41]] = True  # three candidates for twelve slots
+    ours = ob.sample_anchors(mask, K, A, torch.Generator().manual_seed(100 + seed))
+    ref = O.sample_anchors(mask, K, A, torch.Generator().manual_seed(100 + seed))
+    assert torch.equal(ours[0], ref[0]) and torch.equal(ours[1], ref[1])
+
+
 def test_position_weights_and_lr_schedule():
     assert ob.position_weights(32, 0.0) is None
     assert torch.allclose(ob.position_weights(32, 4.0), O.position_weights(32, 4.0))
