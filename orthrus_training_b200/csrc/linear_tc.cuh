@@ -16,7 +16,8 @@
 //              into one of two 256-column accumulators, so the epilogue of tile t overlaps the
 //              mainloop of tile t + 1;
 //   warps 2-9  epilogue, two warps per TMEM lane quarter splitting the columns: tcgen05.ld
-//              (TMEM lane = output row), the fused tail, 64-byte row stores.
+//              (TMEM lane = output row), the fused tail, bf16 rows into a per-warp 32 x 64 staging
+//              tile (128-byte swizzle) that one TMA store writes out (clipped at M and N).
 // Every wait is bounded; on a timeout the CTA records the error, drains its copies and returns.
 #pragma once
 
@@ -34,9 +35,10 @@ struct LinearTile {
   static constexpr int B_BYTES = 2 * B_HALF;     // 32 KB
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = 4;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
   static constexpr int EPI_WARPS = 8;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int STAGING = 32 * 64 * 2;  // per epilogue warp: 32 rows x 64 bf16
+  static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_WARPS * STAGING + 1024 + 256;
 };
 
 // silu(g) = g / (1 + exp(-g)) with exp(-g) = 2^(-g log2 e) on ex2.approx and an approximate
@@ -68,14 +70,15 @@ struct LinearGeometry {
 template <int EPI>
 __global__ void __launch_bounds__(LinearTile::THREADS, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                     const LinearGeometry g, __nv_bfloat16* __restrict__ Y, int64_t ldy,
+                     const __grid_constant__ CUtensorMap tmY, const LinearGeometry g, int64_t ldr,
                      const __nv_bfloat16* __restrict__ R) {
   using T = LinearTile;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + T::STAGES * T::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + T::STAGES * T::B_BYTES);
+  uint8_t* staging = sB + T::STAGES * T::B_BYTES;  // 1024-aligned: the ring is a multiple of 1 KB
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + T::EPI_WARPS * T::STAGING);
   uint64_t* empty = full + T::STAGES;
   uint64_t* acc_full = empty + T::STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;      // [2]
@@ -165,7 +168,22 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
   } else {
     const int quarter = warp & 3;          // TMEM lanes this warp may read
     const int half = (warp - 2) >> 2;      // which half of the tile's columns it takes
+    const uint32_t stage = smem_u32(staging + (warp - 2) * T::STAGING);
     int tt = 0;
+    // 64 output columns [col0, col0 + 64) of this warp's 32 rows from the staging tile; a box
+    // that starts past the last row or column is not stored at all (the rest is clipped by TMA)
+    auto flush = [&](int col0, int row0) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && row0 < g.M && col0 < g.N) {
+        tma_store_2d(&tmY, staging + (warp - 2) * T::STAGING, col0, row0);
+        tma_store_commit();
+      }
+    };
+    auto reuse = [&]() {  // the previous store has finished reading the staging tile
+      if (lane == 0) tma_store_wait_read_all();
+      __syncwarp();
+    };
     for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x, ++tt) {
       const int b = tt & 1;
       if (!mbar_wait(&acc_full[b], (tt >> 1) & 1)) {
@@ -175,70 +193,82 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
       tc_fence_after();
       int m0, n0, w0, w1;
       g.tile(t, EPI, m0, n0, w0, w1);
-      const int row = m0 + quarter * 32 + lane;
-      const bool row_ok = row < g.M;
+      const int row0 = m0 + quarter * 32;
+      const int row = row0 + lane;
       const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + b * T::BN;
       if constexpr (EPI == kLinearSwiGLU) {
+        reuse();
 #pragma unroll 1
         for (int c = 2 * half; c < 2 * half + 2; ++c) {
           float gv[32], uv[32];
           tmem_ld32(base + c * 32, gv);
           tmem_ld32(base + 128 + c * 32, uv);
           tmem_wait_ld();
-          if (!row_ok) continue;
-          __nv_bfloat16* dst = Y + static_cast<int64_t>(row) * ldy + n0 + c * 32;
+          uint32_t pk[16];
 #pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            float h[8];
+          for (int j = 0; j < 32; j += 2) {
+            float h[2];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
+            for (int e = 0; e < 2; ++e) {
               const float gr = round_to_t<__nv_bfloat16>(gv[j + e]);
               const float ur = round_to_t<__nv_bfloat16>(uv[j + e]);
               h[e] = round_to_t<__nv_bfloat16>(silu_fast(gr)) * ur;
             }
-            *reinterpret_cast<uint4*>(dst + j) = make_uint4(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]),
-                                                            pack_bf16x2(h[4], h[5]), pack_bf16x2(h[6], h[7]));
+            pk[j / 2] = pack_bf16x2(h[0], h[1]);
           }
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            st_shared_v4(stage + sw128_offset(lane, (c & 1) * 4 + q), pk[4 * q], pk[4 * q + 1], pk[4 * q + 2],
+                         pk[4 * q + 3]);
         }
+        flush(n0 + half * 64, row0);
       } else {
 #pragma unroll 1
-        for (int c = 4 * half; c < 4 * half + 4; ++c) {
-          const int col0 = n0 + c * 32;
-          uint4 rv[4];
-          const bool store = row_ok && col0 < g.N;
-          if constexpr (EPI == kLinearResidual) {
-            if (store) {
-              const uint4* src = reinterpret_cast<const uint4*>(R + static_cast<int64_t>(row) * ldy + col0);
+        for (int pair = 0; pair < 2; ++pair) {
+          reuse();
+#pragma unroll 1
+          for (int cc = 0; cc < 2; ++cc) {
+            const int c = 4 * half + 2 * pair + cc;
+            const int col0 = n0 + c * 32;
+            uint4 rv[4];
+            if constexpr (EPI == kLinearResidual) {
+              if (row < g.M && col0 < g.N) {
+                const uint4* src = reinterpret_cast<const uint4*>(R + static_cast<int64_t>(row) * ldr + col0);
 #pragma unroll
-              for (int j = 0; j < 4; ++j) rv[j] = src[j];
-            }
-          }
-          float v[32];
-          tmem_ld32(base + c * 32, v);
-          tmem_wait_ld();
-          if (!store) continue;
-          if constexpr (EPI == kLinearResidual) {
+                for (int j = 0; j < 4; ++j) rv[j] = src[j];
+              } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint32_t w[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                v[j * 8 + 2 * e] += __uint_as_float(w[e] << 16);
-                v[j * 8 + 2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
+                for (int j = 0; j < 4; ++j) rv[j] = make_uint4(0u, 0u, 0u, 0u);
               }
             }
-          }
-          __nv_bfloat16* dst = Y + static_cast<int64_t>(row) * ldy + col0;
+            float v[32];
+            tmem_ld32(base + c * 32, v);
+            tmem_wait_ld();
+            if constexpr (EPI == kLinearResidual) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 8)
-            *reinterpret_cast<uint4*>(dst + j) = make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
-                                                            pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t w[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  v[j * 8 + 2 * e] += __uint_as_float(w[e] << 16);
+                  v[j * 8 + 2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
+                }
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              st_shared_v4(stage + sw128_offset(lane, cc * 4 + q), pack_bf16x2(v[8 * q], v[8 * q + 1]),
+                           pack_bf16x2(v[8 * q + 2], v[8 * q + 3]), pack_bf16x2(v[8 * q + 4], v[8 * q + 5]),
+                           pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+          }
+          flush(n0 + (4 * half + 2 * pair) * 32, row0);
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
+    if (lane == 0) tma_store_wait_all();
   }
   __syncthreads();
   if (warp == 1) {
@@ -262,9 +292,10 @@ inline int linear_bf16_impl(const void* X, int64_t ldx, const void* W, int64_t l
   if (M == 0) return ORTHRUS_OK;
   using T = LinearTile;
   const int64_t w_rows = epilogue == kLinearSwiGLU ? 2 * N : N;
-  CUtensorMap tx, tw;
+  CUtensorMap tx, tw, ty;
   if (!make_tmap_2d_bf16(&tx, X, K, M, ldx, 64, 128)) return ORTHRUS_ECUDA;
   if (!make_tmap_2d_bf16(&tw, W, K, w_rows, ldw, 64, 128)) return ORTHRUS_ECUDA;
+  if (!make_tmap_2d_bf16(&ty, Y, N, M, ldy, 64, 32)) return ORTHRUS_ECUDA;
   LinearGeometry g;
   g.M = static_cast<int>(M);
   g.N = static_cast<int>(N);
@@ -275,17 +306,16 @@ inline int linear_bf16_impl(const void* X, int64_t ldx, const void* W, int64_t l
   g.tiles = static_cast<int>(tiles);
   g.f_rows = epilogue == kLinearSwiGLU ? static_cast<int>(N) : 0;
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, num_sms()));
-  auto* y = static_cast<__nv_bfloat16*>(Y);
   auto* r = static_cast<const __nv_bfloat16*>(R);
   if (epilogue == kLinearStore) {
     ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearStore>, T::SMEM));
-    linear_tc_kernel<kLinearStore><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, g, y, ldy, nullptr);
+    linear_tc_kernel<kLinearStore><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, g, ldy, nullptr);
   } else if (epilogue == kLinearResidual) {
     ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearResidual>, T::SMEM));
-    linear_tc_kernel<kLinearResidual><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, g, y, ldy, r);
+    linear_tc_kernel<kLinearResidual><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, g, ldy, r);
   } else {
     ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearSwiGLU>, T::SMEM));
-    linear_tc_kernel<kLinearSwiGLU><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, g, y, ldy, nullptr);
+    linear_tc_kernel<kLinearSwiGLU><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, g, ldy, nullptr);
   }
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
