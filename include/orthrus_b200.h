@@ -91,6 +91,24 @@ int orthrus_linear_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, 
                         void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int epilogue,
                         void* stream);
 
+/* RoPE table: cos_out / sin_out [positions][half] bf16 = cos / sin(p * inv_freq[i]) by sincosf,
+ * rounded to bf16 (the rotary table of the attention prologue, orthrus/objective.py:136-143). */
+int orthrus_rope_table_bf16(const float* inv_freq, int64_t positions, int half, void* cos_out,
+                            void* sin_out, void* stream);
+
+/* q|k|v projection with the attention prologue in the epilogue, bf16, head dim 128:
+ * x [B*L, K] @ w_qkv[(Hq + 2 Hkv) * 128, K]^T, then per q / k head the RMSNorm (q_norm_w /
+ * k_norm_w [128], eps) and RoPE at position t (rope_cos / rope_sin [L][64] from
+ * orthrus_rope_table_bf16), written head-major: q_out [B, Hq, L, 128], k_out and v_out
+ * [B, Hkv, L, 128]. The same arithmetic and roundings as orthrus_gemm_bf16 followed by
+ * orthrus_qkv_prep_fwd, without the token-major projection in HBM. L a multiple of 128, K of 8,
+ * Hq + 2 Hkv even. Replaces _attention_inputs of the frozen AR pass (orthrus/objective.py:136-143,
+ * 152-157). */
+int orthrus_linear_qkv_rope_bf16(const void* x, const void* w_qkv, const void* q_norm_w,
+                                 const void* k_norm_w, const void* rope_cos, const void* rope_sin,
+                                 int64_t B, int64_t L, int64_t K, int Hq, int Hkv, float eps,
+                                 void* q_out, void* k_out, void* v_out, void* stream);
+
 /* Same contract for fp32 (or bf16-in, fp32-accumulate) operands on CUDA cores, B as [N, K]:
  * exact fp32 arithmetic with a fixed reduction order that does not depend on M. */
 size_t orthrus_gemm_simt_workspace_bytes(int64_t M, int64_t N, int64_t K);

@@ -57,6 +57,18 @@ int orthrus_linear_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, 
   return linear_bf16_impl(x, ldx, w, ldw, residual, y, ldy, M, N, K, epilogue, as_stream(stream));
 }
 
+int orthrus_rope_table_bf16(const float* inv_freq, int64_t positions, int half, void* cos_out, void* sin_out,
+                            void* stream) {
+  return rope_table_impl(inv_freq, positions, half, cos_out, sin_out, as_stream(stream));
+}
+
+int orthrus_linear_qkv_rope_bf16(const void* x, const void* w_qkv, const void* q_norm_w, const void* k_norm_w,
+                                 const void* rope_cos, const void* rope_sin, int64_t B, int64_t L, int64_t K, int Hq,
+                                 int Hkv, float eps, void* q_out, void* k_out, void* v_out, void* stream) {
+  return linear_qkv_rope_impl(x, w_qkv, q_norm_w, k_norm_w, rope_cos, rope_sin, B, L, K, Hq, Hkv, eps, q_out,
+                              k_out, v_out, as_stream(stream));
+}
+
 size_t orthrus_gemm_simt_workspace_bytes(int64_t M, int64_t N, int64_t K) { return simt_ws_bytes(M, N, K); }
 
 int orthrus_gemm_simt(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M,

@@ -7,6 +7,11 @@
 //                    to bf16 first and silu rounded before the product (F.linear followed by
 //                    F.silu(gate) * up, orthrus/objective.py:146-149), so [gate | up] is never
 //                    written to or read back from HBM.
+//   kLinearQkvRope   W = [q; k; v] heads of 128: the q and k heads get the per-head RMSNorm and
+//                    RoPE of the attention prologue (orthrus/objective.py:136-143, the arithmetic
+//                    and roundings of qkv_prep_fwd_row_kernel) and every head is written head-major
+//                    ([B, H, L, 128]) for the attention kernels; the token-major q|k|v projection
+//                    is never written.
 //
 // One CTA per SM loops over 128-row x 256-accumulator-column tiles in m-major order (the CTAs in
 // flight share one weight panel in L2 and read each activation panel from HBM once), 320 threads:
@@ -22,11 +27,23 @@
 #pragma once
 
 #include "sm100.cuh"
+#include "qkv_prep.cuh"
 #include "rowwise.cuh"
 
 namespace orthrus {
 
-enum LinearEpilogue { kLinearStore = 0, kLinearResidual = 1, kLinearSwiGLU = 2 };
+enum LinearEpilogue { kLinearStore = 0, kLinearResidual = 1, kLinearSwiGLU = 2, kLinearQkvRope = 3 };
+
+// Operands of the q|k|v epilogue: rows are tokens t of L per sequence (M = B * L, L a multiple of
+// 128, RoPE position = t); cos / sin [L][64] hold cos(t * inv_freq[i]) rounded to bf16.
+struct QkvRopeParams {
+  const __nv_bfloat16* q_norm_w;
+  const __nv_bfloat16* k_norm_w;
+  const __nv_bfloat16* rope_cos;
+  const __nv_bfloat16* rope_sin;
+  int L, Hq, Hkv;
+  float eps;
+};
 
 struct LinearTile {
   static constexpr int BM = 128, BN = 256, BK = 64;
@@ -70,8 +87,9 @@ struct LinearGeometry {
 template <int EPI>
 __global__ void __launch_bounds__(LinearTile::THREADS, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                     const __grid_constant__ CUtensorMap tmY, const LinearGeometry g, int64_t ldr,
-                     const __nv_bfloat16* __restrict__ R) {
+                     const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const LinearGeometry g, int64_t ldr,
+                     const __nv_bfloat16* __restrict__ R, const QkvRopeParams qp) {
   using T = LinearTile;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -196,7 +214,102 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
       const int row0 = m0 + quarter * 32;
       const int row = row0 + lane;
       const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + b * T::BN;
-      if constexpr (EPI == kLinearSwiGLU) {
+      if constexpr (EPI == kLinearQkvRope) {
+        // this warp: head n0 / 128 + half, 32 tokens t0 .. t0 + 31 of sequence bq
+        const int head = n0 / 128 + half;
+        const int kind = head < qp.Hq ? 0 : head < qp.Hq + qp.Hkv ? 1 : 2;
+        const int bq = m0 / qp.L, t0 = m0 % qp.L + quarter * 32, tok = t0 + lane;
+        const int hk = kind == 0 ? head : kind == 1 ? head - qp.Hq : head - qp.Hq - qp.Hkv;
+        const int out_row0 = (bq * (kind == 0 ? qp.Hq : qp.Hkv) + hk) * qp.L + t0;
+        const CUtensorMap* omap = kind == 0 ? &tmY : kind == 1 ? &tmK : &tmV;
+        const uint32_t hbase = base + half * 128;
+        float rstd = 1.f;
+        if (kind < 2) {
+          // the prologue's sum of squares: lane l of its warp held elements 4l..4l+3, then an xor
+          // butterfly over the 32 lanes; replayed in the same order on this thread's row
+          float part[32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float v[32];
+            tmem_ld32(hbase + c * 32, v);
+            tmem_wait_ld();
+            round_all<__nv_bfloat16, 32>(v);
+#pragma unroll
+            for (int l = 0; l < 8; ++l) {
+              float ss = 0.f;
+#pragma unroll
+              for (int k = 0; k < 4; ++k) ss = fmaf(v[4 * l + k], v[4 * l + k], ss);
+              part[c * 8 + l] = ss;
+            }
+          }
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+            for (int l = 0; l < off; ++l) part[l] += part[l + off];
+          rstd = rsqrtf(part[0] / 128.f + qp.eps);
+        }
+        const __nv_bfloat16* wn = kind == 0 ? qp.q_norm_w : qp.k_norm_w;
+#pragma unroll 1
+        for (int cp = 0; cp < 2; ++cp) {  // elements i = cp*32 + j and their RoPE partners i + 64
+          reuse();
+          float lo[32], hi[32];
+          tmem_ld32(hbase + cp * 32, lo);
+          tmem_ld32(hbase + (cp + 2) * 32, hi);
+          tmem_wait_ld();
+          round_all<__nv_bfloat16, 32>(lo);
+          round_all<__nv_bfloat16, 32>(hi);
+          if (kind < 2) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              lo[j] *= rstd;
+              hi[j] *= rstd;
+            }
+            round_all<__nv_bfloat16, 32>(lo);
+            round_all<__nv_bfloat16, 32>(hi);
+#pragma unroll
+            for (int g8 = 0; g8 < 4; ++g8) {
+              float wl[8], wh[8], cs[8], sn[8];
+              load_elems<__nv_bfloat16, 8>(wn + cp * 32 + g8 * 8, wl);
+              load_elems<__nv_bfloat16, 8>(wn + 64 + cp * 32 + g8 * 8, wh);
+              load_elems<__nv_bfloat16, 8>(qp.rope_cos + static_cast<int64_t>(tok) * 64 + cp * 32 + g8 * 8, cs);
+              load_elems<__nv_bfloat16, 8>(qp.rope_sin + static_cast<int64_t>(tok) * 64 + cp * 32 + g8 * 8, sn);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                lo[g8 * 8 + e] *= wl[e];
+                hi[g8 * 8 + e] *= wh[e];
+              }
+              round_all<__nv_bfloat16, 8>(lo + g8 * 8);
+              round_all<__nv_bfloat16, 8>(hi + g8 * 8);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float a = lo[g8 * 8 + e], bb = hi[g8 * 8 + e];
+                const float ra = -bb, rb = a;  // rotate_half: the lower half takes -upper
+                lo[g8 * 8 + e] = a * cs[e] + ra * sn[e];
+                hi[g8 * 8 + e] = bb * cs[e] + rb * sn[e];
+              }
+            }
+          }
+          // two 32 x 32 staging boxes (64-byte rows): columns cp*32.. and 64 + cp*32..
+          const uint32_t box_lo = stage, box_hi = stage + 2048;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            st_shared_v4(box_lo + lane * 64 + q * 16, pack_bf16x2(lo[8 * q], lo[8 * q + 1]),
+                         pack_bf16x2(lo[8 * q + 2], lo[8 * q + 3]), pack_bf16x2(lo[8 * q + 4], lo[8 * q + 5]),
+                         pack_bf16x2(lo[8 * q + 6], lo[8 * q + 7]));
+            st_shared_v4(box_hi + lane * 64 + q * 16, pack_bf16x2(hi[8 * q], hi[8 * q + 1]),
+                         pack_bf16x2(hi[8 * q + 2], hi[8 * q + 3]), pack_bf16x2(hi[8 * q + 4], hi[8 * q + 5]),
+                         pack_bf16x2(hi[8 * q + 6], hi[8 * q + 7]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            uint8_t* sbuf = staging + (warp - 2) * T::STAGING;
+            tma_store_2d(omap, sbuf, cp * 32, out_row0);
+            tma_store_2d(omap, sbuf + 2048, 64 + cp * 32, out_row0);
+            tma_store_commit();
+          }
+        }
+      } else if constexpr (EPI == kLinearSwiGLU) {
         reuse();
 #pragma unroll 1
         for (int c = 2 * half; c < 2 * half + 2; ++c) {
@@ -277,13 +390,37 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
   }
 }
 
+// cos / sin [P][half] of the RoPE angle p * inv_freq[i], rounded to bf16, by sincosf as the
+// attention prologue computes them.
+__global__ void rope_table_kernel(const float* __restrict__ inv_freq, int64_t P, int half,
+                                  __nv_bfloat16* __restrict__ cos_out, __nv_bfloat16* __restrict__ sin_out) {
+  const int64_t n = P * half;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float sv, cv;
+    sincosf(static_cast<float>(i / half) * inv_freq[i % half], &sv, &cv);
+    cos_out[i] = __float2bfloat16_rn(cv);
+    sin_out[i] = __float2bfloat16_rn(sv);
+  }
+}
+
+inline int rope_table_impl(const float* inv_freq, int64_t P, int half, void* cos_out, void* sin_out,
+                           cudaStream_t stream) {
+  ORTHRUS_CHECK_ARG(inv_freq && cos_out && sin_out && P > 0 && half > 0 && P * half < (1ll << 40));
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(ceil_div(P * half, 256), 148 * 8));
+  rope_table_kernel<<<blocks, 256, 0, stream>>>(inv_freq, P, half, static_cast<__nv_bfloat16*>(cos_out),
+                                                static_cast<__nv_bfloat16*>(sin_out));
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
 // Host side. N is the number of output columns (F for SwiGLU, whose W has 2F rows); N must be a
 // multiple of 128, K a multiple of 8, leading dimensions multiples of 8 elements. R (residual) has
 // the leading dimension of Y and is a separate buffer.
 inline int linear_bf16_impl(const void* X, int64_t ldx, const void* W, int64_t ldw, const void* R, void* Y,
                             int64_t ldy, int64_t M, int64_t N, int64_t K, int epilogue, cudaStream_t stream) {
   ORTHRUS_CHECK_ARG(X && W && Y && M >= 0 && N > 0 && K > 0);
-  ORTHRUS_CHECK_ARG(epilogue == kLinearStore || epilogue == kLinearResidual || epilogue == kLinearSwiGLU);
+  ORTHRUS_CHECK_ARG(epilogue == kLinearStore || epilogue == kLinearResidual || epilogue == kLinearSwiGLU);  // q|k|v: linear_qkv_rope_impl
   ORTHRUS_CHECK_ARG(epilogue != kLinearResidual || (R != nullptr && R != Y));
   ORTHRUS_CHECK_ARG(N % 128 == 0 && K % 8 == 0 && ldx >= K && ldw >= K && ldy >= N);
   ORTHRUS_CHECK_ARG(ldx % 8 == 0 && ldw % 8 == 0 && ldy % 8 == 0);
@@ -307,16 +444,61 @@ inline int linear_bf16_impl(const void* X, int64_t ldx, const void* W, int64_t l
   g.f_rows = epilogue == kLinearSwiGLU ? static_cast<int>(N) : 0;
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, num_sms()));
   auto* r = static_cast<const __nv_bfloat16*>(R);
+  const QkvRopeParams none{};
   if (epilogue == kLinearStore) {
     ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearStore>, T::SMEM));
-    linear_tc_kernel<kLinearStore><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, g, ldy, nullptr);
+    linear_tc_kernel<kLinearStore><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, ty, ty, g, ldy, nullptr, none);
   } else if (epilogue == kLinearResidual) {
     ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearResidual>, T::SMEM));
-    linear_tc_kernel<kLinearResidual><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, g, ldy, r);
+    linear_tc_kernel<kLinearResidual><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, ty, ty, g, ldy, r, none);
   } else {
     ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearSwiGLU>, T::SMEM));
-    linear_tc_kernel<kLinearSwiGLU><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, g, ldy, nullptr);
+    linear_tc_kernel<kLinearSwiGLU><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, ty, ty, g, ldy, nullptr, none);
   }
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+// q|k|v projection of x [B*L, K] by w [(Hq + 2 Hkv) * 128, K] with the attention prologue in the
+// epilogue; q_out [B, Hq, L, 128], k_out / v_out [B, Hkv, L, 128] (head dim 128, positions 0..L-1).
+inline int linear_qkv_rope_impl(const void* X, const void* W, const void* q_norm_w, const void* k_norm_w,
+                                const void* rope_cos, const void* rope_sin, int64_t B, int64_t L, int64_t K,
+                                int Hq, int Hkv, float eps, void* q_out, void* k_out, void* v_out,
+                                cudaStream_t stream) {
+  ORTHRUS_CHECK_ARG(X && W && q_norm_w && k_norm_w && rope_cos && rope_sin && q_out && k_out && v_out);
+  ORTHRUS_CHECK_ARG(B > 0 && L > 0 && L % 128 == 0 && K > 0 && K % 8 == 0 && Hq > 0 && Hkv > 0);
+  ORTHRUS_CHECK_ARG((Hq + 2 * Hkv) % 2 == 0);  // two whole heads per 256-column tile
+  ORTHRUS_CHECK_ARG(aligned16(X) && aligned16(W) && aligned16(q_norm_w) && aligned16(k_norm_w) &&
+                    aligned16(rope_cos) && aligned16(rope_sin) && aligned16(q_out) && aligned16(k_out) &&
+                    aligned16(v_out));
+  const int64_t M = B * L, N = static_cast<int64_t>(Hq + 2 * Hkv) * 128;
+  ORTHRUS_CHECK_ARG(M < (1ll << 31) && B * Hq * L < (1ll << 31) && N < (1ll << 30) && K < (1ll << 31));
+  using T = LinearTile;
+  CUtensorMap tx, tw, tq, tk, tv;
+  if (!make_tmap_2d_bf16(&tx, X, K, M, K, 64, 128)) return ORTHRUS_ECUDA;
+  if (!make_tmap_2d_bf16(&tw, W, K, N, K, 64, 128)) return ORTHRUS_ECUDA;
+  if (!make_tmap_2d_bf16(&tq, q_out, 128, B * Hq * L, 128, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) return ORTHRUS_ECUDA;
+  if (!make_tmap_2d_bf16(&tk, k_out, 128, B * Hkv * L, 128, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) return ORTHRUS_ECUDA;
+  if (!make_tmap_2d_bf16(&tv, v_out, 128, B * Hkv * L, 128, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) return ORTHRUS_ECUDA;
+  LinearGeometry g;
+  g.M = static_cast<int>(M);
+  g.N = static_cast<int>(N);
+  g.K = static_cast<int>(K);
+  g.ntiles = static_cast<int>(N / T::BN);  // two heads per tile
+  g.tiles = static_cast<int>(ceil_div(M, T::BM) * g.ntiles);
+  g.f_rows = 0;
+  QkvRopeParams qp;
+  qp.q_norm_w = static_cast<const __nv_bfloat16*>(q_norm_w);
+  qp.k_norm_w = static_cast<const __nv_bfloat16*>(k_norm_w);
+  qp.rope_cos = static_cast<const __nv_bfloat16*>(rope_cos);
+  qp.rope_sin = static_cast<const __nv_bfloat16*>(rope_sin);
+  qp.L = static_cast<int>(L);
+  qp.Hq = Hq;
+  qp.Hkv = Hkv;
+  qp.eps = eps;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(g.tiles, num_sms()));
+  ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearQkvRope>, T::SMEM));
+  linear_tc_kernel<kLinearQkvRope><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, tq, tk, tv, g, 0, nullptr, qp);
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
 }

@@ -16,8 +16,9 @@ Cases (B = 8 rows of 2048 tokens, 16 query / 8 KV heads of 128, A = 32 anchors, 
   prologue q/k RMSNorm + RoPE + head-major scatter of the teacher's fused q|k|v projection
            (16384 rows of 32 heads x 128), forward and backward    (orthrus/objective.py:136-143)
   linear   the teacher layer's projections at 16384 rows (d = 1024, q|k|v 4096, o 2048 -> 1024, gate|up
-           2 x 3072, down 3072 -> 1024), each through torch / cuBLAS (plus orthrus_swiglu_fwd for
-           the MLP) and through the fused persistent kernel orthrus_linear_bf16
+           2 x 3072, down 3072 -> 1024), each through torch / cuBLAS (plus orthrus_qkv_prep_fwd or
+           orthrus_swiglu_fwd) and through the fused persistent kernels orthrus_linear_qkv_rope_bf16
+           and orthrus_linear_bf16
                                                                    (orthrus/objective.py:136-149)
   sweep    dual-view attention forward + backward over L in {1024, 2048, 4096, 8192}, K in
            {16, 32, 64}, A in {8, 32, 64} (batch filling 16384 query tokens, capped at 65536 keys
@@ -119,6 +120,17 @@ def run(case: str, iters: int, warmup: int) -> dict:
         w_gu = (torch.randn(2 * ff, d, device=dev, generator=gen) * 0.03).bfloat16()
         w_d = (torch.randn(d, ff, device=dev, generator=gen) * 0.02).bfloat16()
         fl = lambda n, k: 2.0 * rows * n * k
+        pos = torch.arange(L, device=dev).repeat(B).view(B, L)
+        inv = ops.rope_inv_freq(HD, 1_000_000.0, dev)
+        rope = ops.rope_table(inv, L)
+        qw = (1 + 0.1 * torch.randn(HD, device=dev, generator=gen)).bfloat16()
+        kw = (1 + 0.1 * torch.randn(HD, device=dev, generator=gen)).bfloat16()
+        timed += [
+            ("qkv_prologue_cublas", lambda: ops.qkv_prep(x @ w_qkv.t(), pos, inv, qw, kw, B, L, HQ, HKV, HD, HD,
+                                                         1e-6), fl(w_qkv.shape[0], d)),
+            ("qkv_prologue_fused", lambda: ops.linear_qkv_rope(x, w_qkv, qw, kw, rope, B, L, HQ, HKV, 1e-6),
+             fl(w_qkv.shape[0], d)),
+        ]
         timed += [
             ("qkv_cublas", lambda: x @ w_qkv.t(), fl(w_qkv.shape[0], d)),
             ("qkv_fused", lambda: ops.linear(x, w_qkv), fl(w_qkv.shape[0], d)),

@@ -156,7 +156,7 @@ class DualViewAttention(torch.autograd.Function):
         return dqkv, dqw.to(qn.dtype), dkw.to(kn.dtype), None, None, None, None, None, None
 
 
-def _teacher_layer(model, i, x, pos, B, L, inv):
+def _teacher_layer(model, i, x, pos, B, L, inv, rope=None):
     cfg = model.config
     layer = model.model.layers[i]
     attn = layer.self_attn
@@ -164,9 +164,14 @@ def _teacher_layer(model, i, x, pos, B, L, inv):
     D = padded_head_dim(hd)
     eps = cfg.rms_norm_eps
     h = ops.rms_norm(x, layer.input_layernorm.weight, eps)
-    qkv = h @ model.packed_qkv(i, False).t()
-    q, k, v, _ = ops.qkv_prep(qkv, pos, inv, attn.q_norm.weight, attn.k_norm.weight, B, L, Hq, Hkv,
-                              hd, D, eps)
+    if rope is not None:
+        # q|k|v GEMM with the q/k norm + RoPE prologue in its epilogue, written head-major
+        q, k, v = ops.linear_qkv_rope(h, model.packed_qkv(i, False), attn.q_norm.weight,
+                                      attn.k_norm.weight, rope, B, L, Hq, Hkv, eps)
+    else:
+        qkv = h @ model.packed_qkv(i, False).t()
+        q, k, v, _ = ops.qkv_prep(qkv, pos, inv, attn.q_norm.weight, attn.k_norm.weight, B, L, Hq,
+                                  Hkv, hd, D, eps)
     o, _ = ops.attention_fwd(q, k, v, mask=MASK_CAUSAL, hd=hd, scale=hd ** -0.5, want_lse=False)
     # residual adds ride in the GEMM epilogue (beta = 1)
     x = torch.addmm(x, o.view(B * L, Hq * hd), attn.o_proj.weight.t())
@@ -218,9 +223,14 @@ def model_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tenso
     with torch.no_grad():
         x = F.embedding(input_ids, embed).reshape(B * L, d)
         pos = torch.arange(L, device=x.device)[None].expand(B, L).contiguous()
+        hd = cfg.head_dim
+        rope = None
+        if ops.fused_qkv_rope_supported(x, hd, padded_head_dim(hd), L, cfg.num_attention_heads,
+                                        cfg.num_key_value_heads):
+            rope = ops.rope_table(inv, L)
         cache = []
         for i in range(cfg.num_hidden_layers):
-            x, k, v = _teacher_layer(model, i, x, pos, B, L, inv)
+            x, k, v = _teacher_layer(model, i, x, pos, B, L, inv, rope)
             cache.append((k, v))
         teacher = ops.rms_norm(x, model.model.norm.weight, cfg.rms_norm_eps).view(B, L, d)
     anchors = anchors.to(torch.int64).contiguous()

@@ -134,6 +134,44 @@ def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor) -> torch.Tensor:
     return y
 
 
+def rope_table(inv_freq: torch.Tensor, positions: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """bf16 (cos, sin) [positions, hd/2] of p * inv_freq[i] (sincosf, rounded to bf16)."""
+    _require_cuda(inv_freq)
+    inv_freq = inv_freq.float().contiguous()
+    half = inv_freq.numel()
+    cos = torch.empty(positions, half, dtype=torch.bfloat16, device=inv_freq.device)
+    sin = torch.empty_like(cos)
+    L.check(L.lib().orthrus_rope_table_bf16(inv_freq.data_ptr(), positions, half, cos.data_ptr(),
+                                            sin.data_ptr(), L.stream_of(inv_freq.device)), "rope_table")
+    return cos, sin
+
+
+def fused_qkv_rope_supported(x: torch.Tensor, hd: int, D: int, L_: int, Hq: int, Hkv: int) -> bool:
+    """Shapes the q|k|v projection with the prologue epilogue takes."""
+    return (x.dtype == torch.bfloat16 and hd == 128 and D == 128 and L_ % 128 == 0
+            and x.shape[1] % 8 == 0 and (Hq + 2 * Hkv) % 2 == 0)
+
+
+def linear_qkv_rope(x, w_qkv, q_norm_w, k_norm_w, rope, B: int, L_: int, Hq: int, Hkv: int, eps: float):
+    """Teacher q|k|v projection with q/k RMSNorm + RoPE (positions 0..L-1) in the GEMM epilogue.
+    Returns head-major q [B, Hq, L, 128], k, v [B, Hkv, L, 128] (same values as
+    qkv_prep(x @ w_qkv^T, ...) up to the GEMM's accumulation order)."""
+    _require_cuda(x, w_qkv, q_norm_w, k_norm_w)
+    x, w_qkv = x.contiguous(), w_qkv.contiguous()
+    cos, sin = rope
+    if cos.shape[0] < L_:
+        raise ValueError("the RoPE table is shorter than the sequence")
+    dev, dt = x.device, x.dtype
+    q = torch.empty(B, Hq, L_, 128, dtype=dt, device=dev)
+    k = torch.empty(B, Hkv, L_, 128, dtype=dt, device=dev)
+    v = torch.empty(B, Hkv, L_, 128, dtype=dt, device=dev)
+    L.check(L.lib().orthrus_linear_qkv_rope_bf16(
+        x.data_ptr(), w_qkv.data_ptr(), q_norm_w.contiguous().data_ptr(), k_norm_w.contiguous().data_ptr(),
+        cos.data_ptr(), sin.data_ptr(), B, L_, x.shape[1], Hq, Hkv, float(eps), q.data_ptr(), k.data_ptr(),
+        v.data_ptr(), L.stream_of(dev)), "linear_qkv_rope")
+    return q, k, v
+
+
 def lmhead_kl(student, teacher, index, weight, row_weight=None, offsets=None, num_offsets=0,
               need_grad=True, chunk_rows=4096):
     """Fused LM head + log-softmax + KL(teacher || student) (FusedLinearForwardKL.forward math).

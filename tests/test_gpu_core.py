@@ -108,6 +108,56 @@ def test_fused_linear_swiglu_matches_silu_mul(M, F, K):
     assert (h.float() - two.float()).abs().max().item() <= 2e-2 * ref.abs().max().item()
 
 
+@pytest.mark.parametrize("B,L,K,Hq,Hkv", [(2, 256, 1024, 16, 8), (1, 384, 320, 4, 2), (3, 128, 256, 6, 1)])
+def test_fused_qkv_rope_matches_the_prologue(B, L, K, Hq, Hkv):
+    """q|k|v GEMM with the q/k RMSNorm + RoPE prologue in its epilogue against the two-kernel path
+    through the same GEMM mainloop (orthrus_linear_bf16 store, then orthrus_qkv_prep_fwd): the
+    same fp32 accumulators and the same arithmetic, so bit-identical outputs are expected; and
+    against an fp32 torch restatement of the prologue within bf16 rounding."""
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(B * L + K)
+    H = Hq + 2 * Hkv
+    x = torch.randn(B * L, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(H * 128, K, device=DEV, generator=g) / K ** 0.5).bfloat16()
+    qn = (1 + 0.2 * torch.randn(128, device=DEV, generator=g)).bfloat16()
+    kn = (1 + 0.2 * torch.randn(128, device=DEV, generator=g)).bfloat16()
+    inv = ops.rope_inv_freq(128, 1_000_000.0, torch.device(DEV))
+    rope = ops.rope_table(inv, L)
+    q, k, v = ops.linear_qkv_rope(x, w, qn, kn, rope, B, L, Hq, Hkv, 1e-6)
+    pos = torch.arange(L, device=DEV).repeat(B).view(B, L)
+    rq, rk, rv, _ = ops.qkv_prep(ops.linear(x, w), pos, inv, qn, kn, B, L, Hq, Hkv, 128, 128, 1e-6)
+    torch.cuda.synchronize()
+    for got, ref in ((q, rq), (k, rk), (v, rv)):
+        assert got.shape == ref.shape
+        assert torch.equal(got, ref), (got.float() - ref.float()).abs().max().item()
+    # fp32 restatement: RMSNorm per head, weight, rotate_half RoPE, bf16 roundings between steps
+    qkv = (x.float() @ w.float().t()).bfloat16().float().view(B, L, H, 128)
+    ang = torch.arange(L, device=DEV).float()[:, None] * inv[None]
+    cos, sin = ang.cos().bfloat16().float(), ang.sin().bfloat16().float()
+    cos, sin = torch.cat([cos, cos], -1), torch.cat([sin, sin], -1)
+
+    def prep(t, wn):
+        t = (t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-6)).bfloat16().float()
+        t = (t * wn.float()).bfloat16().float()
+        rot = torch.cat([-t[..., 64:], t[..., :64]], -1)
+        return t * cos[None, :, None] + rot * sin[None, :, None]
+
+    ref_q = prep(qkv[:, :, :Hq], qn).permute(0, 2, 1, 3)
+    ref_k = prep(qkv[:, :, Hq:Hq + Hkv], kn).permute(0, 2, 1, 3)
+    ref_v = qkv[:, :, Hq + Hkv:].permute(0, 2, 1, 3)
+    for got, ref in ((q, ref_q), (k, ref_k), (v, ref_v)):
+        assert (got.float() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item() + 1e-2
+
+
+def test_rope_table_matches_sincos():
+    ops = _ops()
+    inv = ops.rope_inv_freq(128, 1_000_000.0, torch.device(DEV))
+    cos, sin = ops.rope_table(inv, 300)
+    ang = torch.arange(300, device=DEV, dtype=torch.float64)[:, None] * inv.double()[None]
+    assert (cos.float() - ang.cos().float()).abs().max().item() <= 4e-3
+    assert (sin.float() - ang.sin().float()).abs().max().item() <= 4e-3
+
+
 def test_fused_linear_rejects_bad_shapes():
     x = torch.randn(8, 64, device=DEV).bfloat16()
     with pytest.raises(ValueError):
