@@ -13,6 +13,11 @@
   ``<path>.tmp`` and renamed when complete. Checkpoints move between the reference and this
   package unchanged, since the parameter names are the same.
 
+- Model export (orthrus/checkpoint.py:98-105): a Hugging Face model directory with the bf16
+  weights (``model.safetensors``, the reference's parameter names, the tied ``lm_head.weight``
+  left out), ``config.json`` (the Qwen3 config plus ``block_size`` / ``mask_token_id`` and the
+  ``auto_map`` entry to ``modeling_orthrus.OrthrusLM``) and the tokenizer files.
+
 ``DevicePrefetcher`` is this package's loader side: it copies each micro-batch into pinned host
 buffers and on to the GPU on a copy stream, one micro-batch ahead of the step that consumes it.
 """
@@ -151,3 +156,31 @@ def load_checkpoint(path: Path, model, optimizer=None, scheduler=None) -> dict:
         if scheduler is not None:
             scheduler.load_state_dict(blob["scheduler"])
     return json.loads((path / STATE).read_text(encoding="utf-8"))
+
+
+def export_model(model, tokenizer, out_dir: Path, modeling_file: Path | None = None) -> None:
+    """Writes the model as a Hugging Face directory in the reference's export format. The
+    reference also copies its own modeling_orthrus.py beside the weights (the ``auto_map``
+    target); pass that file as ``modeling_file`` to do the same."""
+    from safetensors.torch import save_file
+
+    out_dir = Path(out_dir)
+    out_dir.mkdir(parents=True, exist_ok=True)
+    cfg = model.config
+    state = {k: v.detach().to(torch.bfloat16).contiguous().cpu() for k, v in model.state_dict().items()}
+    head, embed = model.state_dict().get("lm_head.weight"), model.state_dict().get("model.embed_tokens.weight")
+    if getattr(cfg, "tie_word_embeddings", False) and head is not None and embed is not None \
+            and head.data_ptr() == embed.data_ptr():
+        state.pop("lm_head.weight")  # tied: restored from the embedding on load
+    save_file(state, out_dir / "model.safetensors", metadata={"format": "pt"})
+    config = cfg.to_dict()
+    config["auto_map"] = {"AutoModelForCausalLM": "modeling_orthrus.OrthrusLM"}
+    config["torch_dtype"] = "bfloat16"
+    for key in ("block_size", "mask_token_id"):
+        config[key] = getattr(cfg, key)
+    (out_dir / "config.json").write_text(json.dumps(config, indent=2, sort_keys=True), encoding="utf-8")
+    if tokenizer is not None:
+        tokenizer.save_pretrained(out_dir)
+    if modeling_file is not None:
+        shutil.copy(modeling_file, out_dir / "modeling_orthrus.py")
+

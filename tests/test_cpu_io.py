@@ -110,3 +110,33 @@ def test_checkpoint_of_another_model_is_refused(tmp_path):
         p.requires_grad_(True)  # a different trainable set
     with pytest.raises(RuntimeError):
         load_checkpoint(tmp_path / "c", other)
+
+
+def test_export_writes_an_hf_directory(tmp_path):
+    """bf16 weights under the reference's names (tied head left out), config with the Orthrus
+    fields and auto_map; the weights load back into a fresh model."""
+    from safetensors.torch import load_file
+
+    from orthrus_training_b200.data_io import export_model
+
+    torch.manual_seed(0)
+    model, _ = _tiny_model()
+    modeling = tmp_path / "src.py"
+    modeling.write_text("# modeling file\n")
+    export_model(model, None, tmp_path / "out", modeling_file=modeling)
+    out = tmp_path / "out"
+    cfg = json.loads((out / "config.json").read_text())
+    assert cfg["auto_map"] == {"AutoModelForCausalLM": "modeling_orthrus.OrthrusLM"}
+    assert cfg["block_size"] == 4 and cfg["mask_token_id"] == 95 and cfg["tie_word_embeddings"]
+    assert (out / "modeling_orthrus.py").read_text() == "# modeling file\n"
+    weights = load_file(out / "model.safetensors")
+    assert "lm_head.weight" not in weights and all(v.dtype == torch.bfloat16 for v in weights.values())
+    names = set(dict(model.named_parameters())) - {"lm_head.weight"}
+    assert names <= set(weights)
+    torch.manual_seed(1)
+    fresh, _ = _tiny_model()
+    missing, unexpected = fresh.load_state_dict({k: v.float() for k, v in weights.items()}, strict=False)
+    assert not unexpected and set(missing) <= {"lm_head.weight"}
+    for n, p in fresh.named_parameters():
+        assert torch.equal(p, dict(model.named_parameters())[n].bfloat16().float()), n
+
