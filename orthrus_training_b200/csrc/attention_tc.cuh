@@ -870,9 +870,11 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t q0 = static_cast<int64_t>(gridDim.x - 1 - blockIdx.x) * 128;  // heavy tiles first
-  const int pair = blockIdx.y;
-  const int64_t b = blockIdx.z;
+  // grid (pair, row, query tile): the query tile varies slowest and runs backwards, so every
+  // CTA of the heaviest tiles (most visible keys) is dispatched before any lighter one
+  const int64_t q0 = static_cast<int64_t>(gridDim.z - 1 - blockIdx.z) * 128;
+  const int pair = blockIdx.x;
+  const int64_t b = blockIdx.y;
   const int G = Hq / Hkv;
   const int hk = (2 * pair) / G;
   const int wg = warp >= 2 ? (warp - 2) / 4 : -1;  // softmax warpgroup = head of the pair
@@ -1184,9 +1186,9 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t q0 = static_cast<int64_t>(gridDim.x - 1 - blockIdx.x) * 128;
-  const int pair = blockIdx.y;
-  const int64_t b = blockIdx.z;
+  const int64_t q0 = static_cast<int64_t>(gridDim.z - 1 - blockIdx.z) * 128;  // heaviest tiles first
+  const int pair = blockIdx.x;
+  const int64_t b = blockIdx.y;
   const int G = Hq / Hkv;
   const int hk = (2 * pair) / G;
   const int wg = warp >= 2 ? (warp - 2) / 4 : -1;

@@ -263,7 +263,8 @@ int orthrus_attn_fwd(const void* q, const void* k1, const void* v1, int64_t s1h,
       return ORTHRUS_ECUDA;
     const float sl2 = scale * kLog2e;
     if ((Hq / Hkv) % 2 == 0) {  // two query heads of one KV head per CTA
-      dim3 grid2(static_cast<unsigned>(ceil_div(Tq, 128)), Hq / 2, static_cast<unsigned>(B));
+      ORTHRUS_CHECK_ARG(ceil_div(Tq, 128) < 65536);
+      dim3 grid2(Hq / 2, static_cast<unsigned>(B), static_cast<unsigned>(ceil_div(Tq, 128)));
       if (D == 128) {
         if (set_smem(attn_fwd_tc2_kernel<128>, Fwd2Smem<128>::SMEM)) return ORTHRUS_ECUDA;
         attn_fwd_tc2_kernel<128><<<grid2, 320, Fwd2Smem<128>::SMEM, st>>>(
@@ -383,7 +384,8 @@ int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h,
       AttnMaps m64;
       if (!make_attn_maps(m64, q, k1, v1, s1h, L1, k2, v2, s2h, L2, B, Hq, Hkv, Tq, hd, D, do_, 64))
         return ORTHRUS_ECUDA;
-      dim3 grid2(static_cast<unsigned>(ceil_div(Tq, 128)), Hq / 2, static_cast<unsigned>(B));
+      ORTHRUS_CHECK_ARG(ceil_div(Tq, 128) < 65536);
+      dim3 grid2(Hq / 2, static_cast<unsigned>(B), static_cast<unsigned>(ceil_div(Tq, 128)));
       // dQ on the caller's stream, dK/dV on the side stream (both only read delta and the inputs)
       SideStream* side = side_stream_on_current_device();
       if (side == nullptr) return ORTHRUS_ECUDA;
