@@ -211,6 +211,28 @@ inline int gemm_splits(int64_t N, int64_t K, int BN) {
   return splits;
 }
 
+// Split-K factor chosen with M known, for callers that do not need batch invariance (the LM-head
+// gradient GEMM of the training step): the power of two up to gemm_splits that minimises
+// (waves of CTAs) x (k-blocks per CTA) plus the fp32 partials' round trip through HBM, both in
+// units of one 128 x BN x 64 MMA step (about 0.47 us per SM; partials at about 6 TB/s).
+inline int gemm_splits_for_m(int64_t M, int64_t N, int64_t K, int BN) {
+  const int cap = gemm_splits(N, K, BN);
+  const int64_t tiles = ceil_div(M, 128) * ceil_div(N, BN), kb = ceil_div(K, 64), sms = num_sms();
+  int best = 1;
+  double best_cost = 0.0;
+  for (int s = 1; s <= cap; s *= 2) {
+    const double waves = static_cast<double>(ceil_div(tiles * s, sms));
+    const double steps = waves * static_cast<double>(ceil_div(kb, s));
+    const double partials = s > 1 ? static_cast<double>(s) * M * N * 8.0 / 6.0e12 / 0.47e-6 : 0.0;
+    const double cost = steps + partials;
+    if (s == 1 || cost < best_cost) {
+      best = s;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
 inline int gemm_bn(int64_t N) { return N >= 256 ? 256 : 128; }
 
 inline size_t gemm_ws_bytes(int64_t M, int64_t N, int64_t K) {
@@ -250,7 +272,7 @@ int launch_gemm_tc(const CUtensorMap& ta, const CUtensorMap& tb, void* C, int64_
 
 inline int gemm_bf16_impl(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
                           int64_t M, int64_t N, int64_t K, int b_kn, int c_f32, void* ws, size_t ws_bytes,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, bool batch_invariant = true) {
   ORTHRUS_CHECK_ARG(A && B && C && M > 0 && N > 0 && K > 0);
   ORTHRUS_CHECK_ARG(lda >= K && ldc >= N && lda % 8 == 0 && ldb % 8 == 0);
   ORTHRUS_CHECK_ARG(b_kn ? ldb >= N : ldb >= K);
@@ -258,9 +280,10 @@ inline int gemm_bf16_impl(const void* A, int64_t lda, const void* B, int64_t ldb
   ORTHRUS_CHECK_ARG(c_f32 ? (ldc % 4 == 0) : (ldc % 8 == 0));
   ORTHRUS_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31));
   const int bn = gemm_bn(N);
-  const int splits = gemm_splits(N, K, bn);
+  // at most gemm_splits(N, K): the workspace gemm_ws_bytes reports always suffices
+  const int splits = batch_invariant ? gemm_splits(N, K, bn) : gemm_splits_for_m(M, N, K, bn);
   if (splits > 1) {
-    if (ws == nullptr || ws_bytes < gemm_ws_bytes(M, N, K)) return ORTHRUS_EWORKSPACE;
+    if (ws == nullptr || ws_bytes < static_cast<size_t>(splits) * M * N * sizeof(float)) return ORTHRUS_EWORKSPACE;
   }
   CUtensorMap ta, tb;
   if (!make_tmap_2d_bf16(&ta, A, K, M, lda, 64, 128)) return ORTHRUS_ECUDA;

@@ -884,7 +884,7 @@ int lmhead_kl_fwd_impl(const T* student, int64_t n, const T* teacher, int64_t m,
       int rc;
       if constexpr (kBf16)
         rc = gemm_bf16_impl(diff, Vp, weight, D, grad + c0 * D, D, rows, D, V, /*b_kn=*/1, /*c_f32=*/0, gws,
-                            gemm_ws_bytes(p.chunk, D, V), stream);
+                            gemm_ws_bytes(p.chunk, D, V), stream, /*batch_invariant=*/false);
       else
         rc = gemm_simt_impl<T, true>(diff, Vp, weight, D, grad + c0 * D, D, rows, D, V, gws,
                                      simt_ws_bytes(p.chunk, D, V), stream);
