@@ -256,7 +256,7 @@ def run_decode(args):
             mean_ctx = sum(len(p) for p in prompts) / batch + new / 2
             pass_bytes = weight_bytes + kv_per_token * mean_ctx * batch
             gbs = pass_bytes / per_pass / 1e9
-            print(json.dumps({
+            emit(json.dumps({
                 "metric": "decode tok/s (Qwen3-0.6B-shape Orthrus block decode, greedy)", "mode": name,
                 "value": round(gen / dec_s, 1), "unit": "generated tok/s", "batch": batch,
                 "new_tokens": new, "K": K, "dtype": args.decode_dtype, "tpf": round(res.tpf, 3),
@@ -279,7 +279,7 @@ def run_decode(args):
         with torch.no_grad():
             toks, _ = O.diffusion_generate(params, ocfg, prompt, 8)
         sec = time.perf_counter() - t0
-        print(json.dumps({"metric": "decode tok/s (reference algorithm on the host cores)",
+        emit(json.dumps({"metric": "decode tok/s (reference algorithm on the host cores)",
                           "value": round(8 / sec, 3), "unit": "generated tok/s", "cores": threads,
                           "kind": "port", "sample": f"batch 1, 128-token prompt, 8 new tokens, K={BLOCK}, "
                                                      f"fp32 diffusion_generate of the CPU port ({sec:.1f} s)"}),
@@ -344,7 +344,7 @@ def run_reference(args):
                          "sample": f"1 row x {SEQ} tokens per step, fp32 orthrus_loss fwd+bwd"},
         "e2e": {"value": value, "unit": "input tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(json.dumps(line))
 
 
 def run_ours(args):
@@ -447,7 +447,7 @@ def run_ours(args):
     if err:
         line["device_error"] = err
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(json.dumps(line))
     if world > 1:
         import torch.distributed as dist
 
@@ -455,7 +455,20 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+_RESULT_FD: int | None = None  # the process's original stdout while a run is in progress
+
+
+def emit(line: str) -> None:
+    """Prints a result line on the original stdout, which carries nothing else during a run."""
+    sys.stdout.flush()
+    if _RESULT_FD is None:
+        print(line, flush=True)
+    else:
+        os.write(_RESULT_FD, (line + "\n").encode())
+
+
 def main():
+    global _RESULT_FD
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -469,12 +482,23 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if args.decode:
-        run_decode(args)
-    elif args.impl == "reference":
-        run_reference(args)
-    else:
-        run_ours(args)
+    # native libraries may print on file descriptor 1 (NCCL's version banner at communicator
+    # set-up): send all of that to stderr so stdout holds only the JSON result line
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        if args.decode:
+            run_decode(args)
+        elif args.impl == "reference":
+            run_reference(args)
+        else:
+            run_ours(args)
+    finally:
+        sys.stdout.flush()
+        os.dup2(_RESULT_FD, 1)
+        os.close(_RESULT_FD)
+        _RESULT_FD = None
 
 
 if __name__ == "__main__":
