@@ -937,6 +937,17 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int c = 0; c < S::BOXES; ++c)
           tma_load_3d(dst + c * kAttnTileBytes, map, &slot_full[slot], c * 64, key0, z);
+        // the ring holds one tile of lookahead; tile j + 2 goes to L2 now, so its loads do not
+        // wait on HBM (the AR keys of the dual view were written long before this kernel)
+        if (!is_v && j + 2 < nt) {
+          const bool pf2 = j + 2 >= n1;
+          const int pkey = (pf2 ? t2a + (j + 2 - n1) : j + 2) * 128;
+#pragma unroll
+          for (int c = 0; c < S::BOXES; ++c) {
+            tma_prefetch_l2_3d(pf2 ? &tmK2 : &tmK1, c * 64, pkey, z);
+            tma_prefetch_l2_3d(pf2 ? &tmV2 : &tmV1, c * 64, pkey, z);
+          }
+        }
         issued = idx + 1;
       }
       if (*abort_flag) {
@@ -1253,6 +1264,16 @@ __global__ void __launch_bounds__(320, 1)
                       static_cast<int>(b * Hkv + hk));
           tma_load_3d(vt + c * kKeyBox64, src2 ? &tmV2 : &tmV1, &kv_full[s], c * 64, key0,
                       static_cast<int>(b * Hkv + hk));
+        }
+        // two stages of 64 keys: tile j + 3 goes to L2 now (the AR keys come from HBM otherwise)
+        if (j + 3 < nt) {
+          const bool pf2 = j + 3 >= n1b;
+          const int pkey = (pf2 ? t2b + (j + 3 - n1b) : j + 3) * 64;
+#pragma unroll
+          for (int c = 0; c < S::BOXES; ++c) {
+            tma_prefetch_l2_3d(pf2 ? &tmK2 : &tmK1, c * 64, pkey, static_cast<int>(b * Hkv + hk));
+            tma_prefetch_l2_3d(pf2 ? &tmV2 : &tmV1, c * 64, pkey, static_cast<int>(b * Hkv + hk));
+          }
         }
         issued = j + 1;
       }
