@@ -7,9 +7,10 @@ reference module. The arithmetic behind them runs in ``liborthrus_b200.so``:
 - q/k RMSNorm + RoPE + cache write: ``ops.qkv_prep`` (orthrus/modeling_orthrus.py:153-159),
 - attention: ``ops.attention_fwd`` with the causal, dual-view or draft mask
   (orthrus/modeling_orthrus.py:58-85,167-188),
-- projections and the LM head: ``ops.gemm`` (tcgen05 for bf16, exact CUDA-core fp32), whose
-  per-row results do not depend on the number of rows, so a K-token verification reproduces a
-  one-token greedy pass bit for bit,
+- projections: ``ops.linear`` / ``ops.linear_swiglu`` for bf16 (the persistent tcgen05 kernel, no
+  split-K, the residual add and SwiGLU in its epilogue) and ``ops.gemm`` otherwise; the LM head:
+  ``ops.gemm`` (fp32 logits). Every one gives per-row results that do not depend on the number of
+  rows, so a K-token verification reproduces a one-token greedy pass bit for bit,
 - RMSNorm and the SwiGLU activation: row-local kernels of fixed reduction order.
 
 There is no CPU path: every forward requires CUDA tensors and the built library.
@@ -410,13 +411,22 @@ class OrthrusLM(nn.Module):
         D = padded_head_dim(hd)
         eps = cfg.rms_norm_eps
         inv = self.inv_freq(x.device)
-        diffusion = mode != "ar"
+        diffusion = mode not in ("ar", "tree")
         x = x.reshape(B * T, d).contiguous()
+        fused = x.dtype == torch.bfloat16
+
+        def proj(a, w, residual=None):
+            # both kernels are batch-invariant (a row's result does not depend on the others)
+            if fused and ops.fused_linear_supported(a, w, w.shape[0]):
+                return ops.linear(a, w, residual=residual)
+            y = ops.gemm(a, w)
+            return y if residual is None else ops.add(residual, y)
+
         for i, layer in enumerate(self.model.layers[: cfg.num_hidden_layers]):
             attn = layer.self_attn
             _, _, _, wo, qn, kn = attn.view_weights(diffusion)
             h = ops.rms_norm(x, layer.input_layernorm.weight, eps)
-            qkv = ops.gemm(h, self.packed_qkv(i, diffusion))
+            qkv = proj(h, self.packed_qkv(i, diffusion))
             if mode in ("ar", "tree") and kv is not None:
                 kb, vb = kv[i]
                 q, _, _, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps,
@@ -444,10 +454,14 @@ class OrthrusLM(nn.Module):
                     o, _ = ops.attention_fwd(q, kb, vb, k2, v2, mask=MASK_DRAFT, hd=hd,
                                              scale=attn.scaling, offset=offsets, limit2=limit2,
                                              want_lse=False)
-            x = ops.add(x, ops.gemm(o.reshape(B * T, Hq * hd), wo))
+            x = proj(o.reshape(B * T, Hq * hd), wo, residual=x)
             h = ops.rms_norm(x, layer.post_attention_layernorm.weight, eps)
-            gu = ops.gemm(h, self._packed_mlp(i))
-            x = ops.add(x, ops.gemm(ops.silu_mul(gu), layer.mlp.down_proj.weight))
+            w_gu = self._packed_mlp(i)
+            if fused and ops.fused_linear_supported(h, w_gu, w_gu.shape[0] // 2):
+                act = ops.linear_swiglu(h, w_gu)
+            else:
+                act = ops.silu_mul(ops.gemm(h, w_gu))
+            x = proj(act, layer.mlp.down_proj.weight, residual=x)
         x = ops.rms_norm(x, self.model.norm.weight, eps)
         return x.view(B, T, d)
 

@@ -136,3 +136,24 @@ def test_draft_table_matches_the_reference(setup):
         drafts, conf = D.draft_table(model, case["prompt"], reference, case["max_new"])
         assert torch.equal(torch.from_numpy(drafts), case["drafts"])
         assert torch.allclose(torch.from_numpy(conf), case["confidence"], atol=1e-5)
+
+
+def test_tree_verification_runs_the_ar_view_when_the_twins_differ():
+    """Tree verification is an AR pass: with diffusion twins that differ from the AR weights, the
+    tree's predictions still equal separate AR chains (a pass on the twins would not)."""
+    D = _dec()
+    model = _model()
+    with torch.no_grad():
+        g = torch.Generator(device=DEV).manual_seed(3)
+        for n, p in model.named_parameters():
+            if "_diff." in n:
+                p.add_(torch.randn(p.shape, device=DEV, generator=g) * p.abs().mean())
+    prompt = list(range(3, 14))
+    hyps = [D.Hypothesis(1, [5, 9, 2, 7]), D.Hypothesis(0, [11, 4]), D.Hypothesis(-1, [8, 8, 1])]
+    tree = D.ModelBackend(model, prompt)
+    root = tree.prefill()
+    preds = tree.verify("tail", len(prompt), root, hyps)
+    for i, h in enumerate(hyps):
+        chain = D.ModelBackend(model, prompt)
+        chain.prefill()
+        assert chain.verify("tail", len(prompt), root, [h])[0] == preds[i]
