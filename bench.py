@@ -266,7 +266,7 @@ def run_decode(args):
                         "peak_gbs": pk["hbm_gbs"], "frac": round(gbs / pk["hbm_gbs"], 4)},
                 "lossless_vs_plain_greedy": bool(lossless) if name == "scripted" else True,
                 "prefill_s": round(res.prefill_seconds, 3), "data": "synthetic Zipf(1.1) prompts, random-init weights",
-            }), flush=True)
+            }))
     if not args.no_cpu_baseline:
         import oracle as O
 
@@ -282,8 +282,7 @@ def run_decode(args):
         emit(json.dumps({"metric": "decode tok/s (reference algorithm on the host cores)",
                           "value": round(8 / sec, 3), "unit": "generated tok/s", "cores": threads,
                           "kind": "port", "sample": f"batch 1, 128-token prompt, 8 new tokens, K={BLOCK}, "
-                                                     f"fp32 diffusion_generate of the CPU port ({sec:.1f} s)"}),
-              flush=True)
+                                                     f"fp32 diffusion_generate of the CPU port ({sec:.1f} s)"}))
 
 
 def step_roofline(cfg, kernels: dict, steps: int, ms_per_step: float, pk: dict) -> dict:
