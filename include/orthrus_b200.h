@@ -91,6 +91,13 @@ int orthrus_linear_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, 
                         void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int epilogue,
                         void* stream);
 
+/* SwiGLU projection that also keeps the projection for the backward of the activation:
+ * y [M, F] = silu(g) * u as ORTHRUS_LINEAR_SWIGLU, and gate_up [M, 2F] = x @ w_gate_up^T rounded
+ * to bf16 (the F.linear output). F a multiple of 128, K of 8, contiguous rows. Replaces F.linear +
+ * the activation of _mlp_residual in the trainable view (orthrus/objective.py:146-149,160-165). */
+int orthrus_linear_swiglu_keep_bf16(const void* x, const void* w_gate_up, int64_t M, int64_t F,
+                                    int64_t K, void* y, void* gate_up, void* stream);
+
 /* RoPE table: cos_out / sin_out [positions][half] bf16 = cos / sin(p * inv_freq[i]) by sincosf,
  * rounded to bf16 (the rotary table of the attention prologue, orthrus/objective.py:136-143). */
 int orthrus_rope_table_bf16(const float* inv_freq, int64_t positions, int half, void* cos_out,

@@ -57,6 +57,11 @@ int orthrus_linear_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, 
   return linear_bf16_impl(x, ldx, w, ldw, residual, y, ldy, M, N, K, epilogue, as_stream(stream));
 }
 
+int orthrus_linear_swiglu_keep_bf16(const void* x, const void* w_gate_up, int64_t M, int64_t F, int64_t K, void* y,
+                                    void* gate_up, void* stream) {
+  return linear_swiglu_keep_impl(x, w_gate_up, M, F, K, y, gate_up, as_stream(stream));
+}
+
 int orthrus_rope_table_bf16(const float* inv_freq, int64_t positions, int half, void* cos_out, void* sin_out,
                             void* stream) {
   return rope_table_impl(inv_freq, positions, half, cos_out, sin_out, as_stream(stream));

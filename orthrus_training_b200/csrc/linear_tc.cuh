@@ -7,6 +7,8 @@
 //                    to bf16 first and silu rounded before the product (F.linear followed by
 //                    F.silu(gate) * up, orthrus/objective.py:146-149), so [gate | up] is never
 //                    written to or read back from HBM.
+//   kLinearSwiGLUKeep  the SwiGLU form that also writes [gate | up] (bf16, the F.linear output),
+//                    which the backward of the activation needs (the trainable view's MLP).
 //   kLinearQkvRope   W = [q; k; v] heads of 128: the q and k heads get the per-head RMSNorm and
 //                    RoPE of the attention prologue (orthrus/objective.py:136-143, the arithmetic
 //                    and roundings of qkv_prep_fwd_row_kernel) and every head is written head-major
@@ -32,7 +34,13 @@
 
 namespace orthrus {
 
-enum LinearEpilogue { kLinearStore = 0, kLinearResidual = 1, kLinearSwiGLU = 2, kLinearQkvRope = 3 };
+enum LinearEpilogue {
+  kLinearStore = 0,
+  kLinearResidual = 1,
+  kLinearSwiGLU = 2,
+  kLinearQkvRope = 3,
+  kLinearSwiGLUKeep = 4
+};
 
 // Operands of the q|k|v epilogue: rows are tokens t of L per sequence (M = B * L, L a multiple of
 // 128, RoPE position = t); cos / sin [L][64] hold cos(t * inv_freq[i]) rounded to bf16.
@@ -70,7 +78,7 @@ struct LinearGeometry {
   __device__ __forceinline__ void tile(int t, int epi, int& m0, int& n0, int& w0, int& w1) const {
     const int mt = t / ntiles, nt = t % ntiles;
     m0 = mt * LinearTile::BM;
-    if (epi == kLinearSwiGLU) {
+    if (epi == kLinearSwiGLU || epi == kLinearSwiGLUKeep) {
       n0 = nt * 128;
       w0 = n0;
       w1 = f_rows + n0;
@@ -309,6 +317,50 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
             tma_store_commit();
           }
         }
+      } else if constexpr (EPI == kLinearSwiGLUKeep) {
+        // per 32-column chunk: silu(g) * u to Y and g to [gate | up], then u, through two 32 x 32
+        // staging boxes (64-byte rows)
+        uint8_t* sbuf = staging + (warp - 2) * T::STAGING;
+#pragma unroll 1
+        for (int c = 2 * half; c < 2 * half + 2; ++c) {
+          float gv[32], uv[32];
+          tmem_ld32(base + c * 32, gv);
+          tmem_ld32(base + 128 + c * 32, uv);
+          tmem_wait_ld();
+          round_all<__nv_bfloat16, 32>(gv);
+          round_all<__nv_bfloat16, 32>(uv);
+          reuse();
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float hq[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) hq[e] = round_to_t<__nv_bfloat16>(silu_fast(gv[8 * q + e])) * uv[8 * q + e];
+            st_shared_v4(stage + lane * 64 + q * 16, pack_bf16x2(hq[0], hq[1]), pack_bf16x2(hq[2], hq[3]),
+                         pack_bf16x2(hq[4], hq[5]), pack_bf16x2(hq[6], hq[7]));
+            st_shared_v4(stage + 2048 + lane * 64 + q * 16, pack_bf16x2(gv[8 * q], gv[8 * q + 1]),
+                         pack_bf16x2(gv[8 * q + 2], gv[8 * q + 3]), pack_bf16x2(gv[8 * q + 4], gv[8 * q + 5]),
+                         pack_bf16x2(gv[8 * q + 6], gv[8 * q + 7]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < g.M) {
+            tma_store_2d(&tmY, sbuf, n0 + c * 32, row0);
+            tma_store_2d(&tmK, sbuf + 2048, n0 + c * 32, row0);
+            tma_store_commit();
+          }
+          reuse();
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            st_shared_v4(stage + lane * 64 + q * 16, pack_bf16x2(uv[8 * q], uv[8 * q + 1]),
+                         pack_bf16x2(uv[8 * q + 2], uv[8 * q + 3]), pack_bf16x2(uv[8 * q + 4], uv[8 * q + 5]),
+                         pack_bf16x2(uv[8 * q + 6], uv[8 * q + 7]));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < g.M) {
+            tma_store_2d(&tmK, sbuf, g.f_rows + n0 + c * 32, row0);
+            tma_store_commit();
+          }
+        }
       } else if constexpr (EPI == kLinearSwiGLU) {
         reuse();
 #pragma unroll 1
@@ -455,6 +507,37 @@ inline int linear_bf16_impl(const void* X, int64_t ldx, const void* W, int64_t l
     ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearSwiGLU>, T::SMEM));
     linear_tc_kernel<kLinearSwiGLU><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, ty, ty, g, ldy, nullptr, none);
   }
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+// silu(x gate^T) * (x up^T) into y [M, F] and the projection [gate | up] into gate_up [M, 2F].
+inline int linear_swiglu_keep_impl(const void* X, const void* W, int64_t M, int64_t F, int64_t K, void* Y,
+                                   void* GU, cudaStream_t stream) {
+  ORTHRUS_CHECK_ARG(X && W && Y && GU && M >= 0 && F > 0 && F % 128 == 0 && K > 0 && K % 8 == 0);
+  ORTHRUS_CHECK_ARG(aligned16(X) && aligned16(W) && aligned16(Y) && aligned16(GU));
+  ORTHRUS_CHECK_ARG(M < (1ll << 31) && F < (1ll << 29) && K < (1ll << 31));
+  if (M == 0) return ORTHRUS_OK;
+  using T = LinearTile;
+  CUtensorMap tx, tw, ty, tgu;
+  if (!make_tmap_2d_bf16(&tx, X, K, M, K, 64, 128)) return ORTHRUS_ECUDA;
+  if (!make_tmap_2d_bf16(&tw, W, K, 2 * F, K, 64, 128)) return ORTHRUS_ECUDA;
+  if (!make_tmap_2d_bf16(&ty, Y, F, M, F, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) return ORTHRUS_ECUDA;
+  if (!make_tmap_2d_bf16(&tgu, GU, 2 * F, M, 2 * F, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) return ORTHRUS_ECUDA;
+  LinearGeometry g;
+  g.M = static_cast<int>(M);
+  g.N = static_cast<int>(F);
+  g.K = static_cast<int>(K);
+  g.ntiles = static_cast<int>(F / 128);
+  const int64_t tiles = ceil_div(M, T::BM) * g.ntiles;
+  ORTHRUS_CHECK_ARG(tiles < (1ll << 31));
+  g.tiles = static_cast<int>(tiles);
+  g.f_rows = static_cast<int>(F);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, num_sms()));
+  const QkvRopeParams none{};
+  ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearSwiGLUKeep>, T::SMEM));
+  linear_tc_kernel<kLinearSwiGLUKeep><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, tgu, tgu, g, 0, nullptr,
+                                                                           none);
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
 }

@@ -115,6 +115,26 @@ class _SwiGLU(torch.autograd.Function):
         return ops.silu_mul_backward(gate_up, dout)
 
 
+class _GateUpSwiGLU(torch.autograd.Function):
+    """F.linear(h, [gate; up]) followed by the SwiGLU activation in one persistent kernel that also
+    keeps [gate | up] for the backward (orthrus/objective.py:146-149). The MLP weights are frozen,
+    so the backward returns dh = dgate_up @ W only."""
+
+    @staticmethod
+    def forward(ctx, h, w_gate_up):
+        if w_gate_up.requires_grad:
+            raise ValueError("the MLP weights of the dual-view model are frozen")
+        act, gate_up = ops.linear_swiglu(h, w_gate_up, keep_gate_up=True)
+        ctx.save_for_backward(gate_up, w_gate_up)
+        return act
+
+    @staticmethod
+    def backward(ctx, dact):
+        gate_up, w = ctx.saved_tensors
+        dgu = ops.silu_mul_backward(gate_up, dact.contiguous())
+        return dgu @ w, None
+
+
 def _rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     """Qwen3RMSNorm with autograd for the student path (frozen weight)."""
     if weight.requires_grad:
@@ -200,8 +220,12 @@ def _diffusion_layer(model, i, x, ar_k, ar_v, positions, anchors, inv, B, Q):
                                 positions, anchors, inv, meta)
     x = torch.addmm(x, o, attn.o_proj_diff.weight.t())
     h = _rms_norm(x, layer.post_attention_layernorm.weight, eps)
-    gu = F.linear(h, model._packed_mlp(i))
-    return torch.addmm(x, _SwiGLU.apply(gu), layer.mlp.down_proj.weight.t())
+    w_gu = model._packed_mlp(i)
+    if ops.fused_linear_supported(h, w_gu, w_gu.shape[0] // 2):
+        act = _GateUpSwiGLU.apply(h, w_gu)
+    else:
+        act = _SwiGLU.apply(F.linear(h, w_gu))
+    return torch.addmm(x, act, layer.mlp.down_proj.weight.t())
 
 
 def model_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tensor,

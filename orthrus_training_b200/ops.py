@@ -117,9 +117,10 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = Non
     return y
 
 
-def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor) -> torch.Tensor:
+def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, keep_gate_up: bool = False):
     """silu(x @ gate^T) * (x @ up^T) for w_gate_up = [gate; up] [2F, K], without writing the
-    [gate | up] projection (same roundings as silu_mul(x @ w_gate_up^T))."""
+    [gate | up] projection (same roundings as silu_mul(x @ w_gate_up^T)). With keep_gate_up the
+    projection [M, 2F] is written as well and (y, gate_up) is returned."""
     _require_cuda(x, w_gate_up)
     x = x.contiguous()
     w_gate_up = w_gate_up.contiguous()
@@ -129,6 +130,12 @@ def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor) -> torch.Tensor:
         raise ValueError(f"linear_swiglu takes bf16 x [M, K] and w [2F, K] with F % 128 == 0; got "
                          f"{tuple(x.shape)} x {tuple(w_gate_up.shape)}")
     y = torch.empty(M, F, dtype=x.dtype, device=x.device)
+    if keep_gate_up:
+        gu = torch.empty(M, 2 * F, dtype=x.dtype, device=x.device)
+        L.check(L.lib().orthrus_linear_swiglu_keep_bf16(x.data_ptr(), w_gate_up.data_ptr(), M, F, K,
+                                                        y.data_ptr(), gu.data_ptr(), L.stream_of(x.device)),
+                "linear_swiglu_keep")
+        return y, gu
     L.check(L.lib().orthrus_linear_bf16(x.data_ptr(), K, w_gate_up.data_ptr(), K, None, y.data_ptr(), F,
                                         M, F, K, LINEAR_SWIGLU, L.stream_of(x.device)), "linear_swiglu")
     return y

@@ -158,6 +158,35 @@ def test_rope_table_matches_sincos():
     assert (sin.float() - ang.sin().float()).abs().max().item() <= 4e-3
 
 
+@pytest.mark.parametrize("M,F,K", [(8192 // 16, 3072, 1024), (300, 256, 320)])
+def test_fused_linear_swiglu_keep(M, F, K):
+    """The SwiGLU form that also writes [gate | up]: the activation equals the plain SwiGLU form
+    and the kept projection equals the store form (same mainloop, same roundings: bit-identical)."""
+    g = torch.Generator(device=DEV).manual_seed(M + F)
+    x = torch.randn(M, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(2 * F, K, device=DEV, generator=g) / K ** 0.5).bfloat16()
+    y, gu = _ops().linear_swiglu(x, w, keep_gate_up=True)
+    torch.cuda.synchronize()
+    assert torch.equal(y, _ops().linear_swiglu(x, w))
+    assert torch.equal(gu, _ops().linear(x, w))
+
+
+def test_student_mlp_backward_through_the_fused_swiglu():
+    """dh of the fused gate/up + SwiGLU equals the autograd of F.linear + the activation kernels."""
+    from orthrus_training_b200 import objective as ob
+
+    g = torch.Generator(device=DEV).manual_seed(11)
+    h = torch.randn(640, 256, device=DEV, generator=g).bfloat16().requires_grad_(True)
+    w = (torch.randn(2 * 384, 256, device=DEV, generator=g) / 16).bfloat16()
+    dact = torch.randn(640, 384, device=DEV, generator=g).bfloat16()
+    ob._GateUpSwiGLU.apply(h, w).backward(dact)
+    fused = h.grad.clone()
+    h.grad = None
+    ob._SwiGLU.apply(torch.nn.functional.linear(h, w)).backward(dact)
+    ref = h.grad
+    assert (fused.float() - ref.float()).abs().max().item() <= 2e-2 * ref.float().abs().max().item()
+
+
 def test_fused_linear_rejects_bad_shapes():
     x = torch.randn(8, 64, device=DEV).bfloat16()
     with pytest.raises(ValueError):
