@@ -91,6 +91,20 @@ int orthrus_linear_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, 
                         void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int epilogue,
                         void* stream);
 
+/* The same for the trainable view, whose prologue has a backward: RoPE at positions [B*L] (int64,
+ * below table_rows, the rows of rope_cos / rope_sin; a position outside is clamped and reported
+ * through ORTHRUS_ERR_BOUNDS) instead of t, and the q / k columns of the token-major projection
+ * qkv_out [B*L, (Hq + 2 Hkv) * 128] (bf16, the F.linear output; v columns untouched) and rstd_out
+ * [B*L, Hq + Hkv] fp32 are kept for orthrus_qkv_prep_bwd. Replaces F.linear + the prologue of
+ * the diffusion layer (orthrus/objective.py:136-143,160-165). */
+int orthrus_linear_qkv_rope_keep_bf16(const void* x, const void* w_qkv, const void* q_norm_w,
+                                      const void* k_norm_w, const void* rope_cos,
+                                      const void* rope_sin, int64_t table_rows,
+                                      const int64_t* positions, int64_t B,
+                                      int64_t L, int64_t K, int Hq, int Hkv, float eps, void* q_out,
+                                      void* k_out, void* v_out, void* qkv_out, float* rstd_out,
+                                      void* stream);
+
 /* SwiGLU projection that also keeps the projection for the backward of the activation:
  * y [M, F] = silu(g) * u as ORTHRUS_LINEAR_SWIGLU, and gate_up [M, 2F] = x @ w_gate_up^T rounded
  * to bf16 (the F.linear output). F a multiple of 128, K of 8, contiguous rows. Replaces F.linear +

@@ -62,6 +62,16 @@ int orthrus_linear_swiglu_keep_bf16(const void* x, const void* w_gate_up, int64_
   return linear_swiglu_keep_impl(x, w_gate_up, M, F, K, y, gate_up, as_stream(stream));
 }
 
+int orthrus_linear_qkv_rope_keep_bf16(const void* x, const void* w_qkv, const void* q_norm_w, const void* k_norm_w,
+                                      const void* rope_cos, const void* rope_sin, int64_t table_rows,
+                                      const int64_t* positions, int64_t B,
+                                      int64_t L, int64_t K, int Hq, int Hkv, float eps, void* q_out, void* k_out,
+                                      void* v_out, void* qkv_out, float* rstd_out, void* stream) {
+  ORTHRUS_CHECK_ARG(positions && qkv_out && rstd_out);
+  return linear_qkv_rope_impl(x, w_qkv, q_norm_w, k_norm_w, rope_cos, rope_sin, B, L, K, Hq, Hkv, eps, q_out,
+                              k_out, v_out, as_stream(stream), table_rows, positions, qkv_out, rstd_out);
+}
+
 int orthrus_rope_table_bf16(const float* inv_freq, int64_t positions, int half, void* cos_out, void* sin_out,
                             void* stream) {
   return rope_table_impl(inv_freq, positions, half, cos_out, sin_out, as_stream(stream));
@@ -71,7 +81,7 @@ int orthrus_linear_qkv_rope_bf16(const void* x, const void* w_qkv, const void* q
                                  const void* rope_cos, const void* rope_sin, int64_t B, int64_t L, int64_t K, int Hq,
                                  int Hkv, float eps, void* q_out, void* k_out, void* v_out, void* stream) {
   return linear_qkv_rope_impl(x, w_qkv, q_norm_w, k_norm_w, rope_cos, rope_sin, B, L, K, Hq, Hkv, eps, q_out,
-                              k_out, v_out, as_stream(stream));
+                              k_out, v_out, as_stream(stream), L);
 }
 
 size_t orthrus_gemm_simt_workspace_bytes(int64_t M, int64_t N, int64_t K) { return simt_ws_bytes(M, N, K); }

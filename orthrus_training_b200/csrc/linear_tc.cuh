@@ -12,8 +12,9 @@
 //   kLinearQkvRope   W = [q; k; v] heads of 128: the q and k heads get the per-head RMSNorm and
 //                    RoPE of the attention prologue (orthrus/objective.py:136-143, the arithmetic
 //                    and roundings of qkv_prep_fwd_row_kernel) and every head is written head-major
-//                    ([B, H, L, 128]) for the attention kernels; the token-major q|k|v projection
-//                    is never written.
+//                    ([B, H, L, 128]) for the attention kernels. The frozen view writes nothing
+//                    else; the trainable view also keeps the q / k columns of the token-major
+//                    projection and rstd, which the prologue's backward reads.
 //
 // One CTA per SM loops over 128-row x 256-accumulator-column tiles in m-major order (the CTAs in
 // flight share one weight panel in L2 and read each activation panel from HBM once), 320 threads:
@@ -49,7 +50,11 @@ struct QkvRopeParams {
   const __nv_bfloat16* k_norm_w;
   const __nv_bfloat16* rope_cos;
   const __nv_bfloat16* rope_sin;
+  const int64_t* positions;  // RoPE position per row, or null for t
+  float* rstd_out;           // [rows, Hq + Hkv] rsqrt(mean(x^2) + eps) per q / k head, or null
+  bool keep;                 // also write the q / k columns of the projection token-major (tmP)
   int L, Hq, Hkv;
+  int64_t table_rows;        // rows of rope_cos / rope_sin
   float eps;
 };
 
@@ -96,8 +101,9 @@ template <int EPI>
 __global__ void __launch_bounds__(LinearTile::THREADS, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmK,
-                     const __grid_constant__ CUtensorMap tmV, const LinearGeometry g, int64_t ldr,
-                     const __nv_bfloat16* __restrict__ R, const QkvRopeParams qp) {
+                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmP,
+                     const LinearGeometry g, int64_t ldr, const __nv_bfloat16* __restrict__ R,
+                     const QkvRopeParams qp) {
   using T = LinearTile;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -226,7 +232,12 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
         // this warp: head n0 / 128 + half, 32 tokens t0 .. t0 + 31 of sequence bq
         const int head = n0 / 128 + half;
         const int kind = head < qp.Hq ? 0 : head < qp.Hq + qp.Hkv ? 1 : 2;
-        const int bq = m0 / qp.L, t0 = m0 % qp.L + quarter * 32, tok = t0 + lane;
+        const int bq = m0 / qp.L, t0 = m0 % qp.L + quarter * 32;
+        int64_t tok = qp.positions != nullptr ? qp.positions[row] : static_cast<int64_t>(t0 + lane);
+        if (tok < 0 || tok >= qp.table_rows) {  // a position past the table: clamp and report
+          record_error(ORTHRUS_ERR_BOUNDS);
+          tok = tok < 0 ? 0 : qp.table_rows - 1;
+        }
         const int hk = kind == 0 ? head : kind == 1 ? head - qp.Hq : head - qp.Hq - qp.Hkv;
         const int out_row0 = (bq * (kind == 0 ? qp.Hq : qp.Hkv) + hk) * qp.L + t0;
         const CUtensorMap* omap = kind == 0 ? &tmY : kind == 1 ? &tmK : &tmV;
@@ -255,6 +266,7 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
 #pragma unroll
             for (int l = 0; l < off; ++l) part[l] += part[l + off];
           rstd = rsqrtf(part[0] / 128.f + qp.eps);
+          if (qp.rstd_out != nullptr) qp.rstd_out[static_cast<int64_t>(row) * (qp.Hq + qp.Hkv) + head] = rstd;
         }
         const __nv_bfloat16* wn = kind == 0 ? qp.q_norm_w : qp.k_norm_w;
 #pragma unroll 1
@@ -266,6 +278,26 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
           tmem_wait_ld();
           round_all<__nv_bfloat16, 32>(lo);
           round_all<__nv_bfloat16, 32>(hi);
+          if (qp.keep && kind < 2) {  // the projection itself, token-major, for the backward
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              st_shared_v4(stage + lane * 64 + q * 16, pack_bf16x2(lo[8 * q], lo[8 * q + 1]),
+                           pack_bf16x2(lo[8 * q + 2], lo[8 * q + 3]), pack_bf16x2(lo[8 * q + 4], lo[8 * q + 5]),
+                           pack_bf16x2(lo[8 * q + 6], lo[8 * q + 7]));
+              st_shared_v4(stage + 2048 + lane * 64 + q * 16, pack_bf16x2(hi[8 * q], hi[8 * q + 1]),
+                           pack_bf16x2(hi[8 * q + 2], hi[8 * q + 3]), pack_bf16x2(hi[8 * q + 4], hi[8 * q + 5]),
+                           pack_bf16x2(hi[8 * q + 6], hi[8 * q + 7]));
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              uint8_t* sbuf = staging + (warp - 2) * T::STAGING;
+              tma_store_2d(&tmP, sbuf, head * 128 + cp * 32, row0);
+              tma_store_2d(&tmP, sbuf + 2048, head * 128 + 64 + cp * 32, row0);
+              tma_store_commit();
+            }
+            reuse();
+          }
           if (kind < 2) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
@@ -499,13 +531,13 @@ inline int linear_bf16_impl(const void* X, int64_t ldx, const void* W, int64_t l
   const QkvRopeParams none{};
   if (epilogue == kLinearStore) {
     ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearStore>, T::SMEM));
-    linear_tc_kernel<kLinearStore><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, ty, ty, g, ldy, nullptr, none);
+    linear_tc_kernel<kLinearStore><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, ty, ty, ty, g, ldy, nullptr, none);
   } else if (epilogue == kLinearResidual) {
     ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearResidual>, T::SMEM));
-    linear_tc_kernel<kLinearResidual><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, ty, ty, g, ldy, r, none);
+    linear_tc_kernel<kLinearResidual><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, ty, ty, ty, g, ldy, r, none);
   } else {
     ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearSwiGLU>, T::SMEM));
-    linear_tc_kernel<kLinearSwiGLU><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, ty, ty, g, ldy, nullptr, none);
+    linear_tc_kernel<kLinearSwiGLU><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, ty, ty, ty, g, ldy, nullptr, none);
   }
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
@@ -536,8 +568,8 @@ inline int linear_swiglu_keep_impl(const void* X, const void* W, int64_t M, int6
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, num_sms()));
   const QkvRopeParams none{};
   ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearSwiGLUKeep>, T::SMEM));
-  linear_tc_kernel<kLinearSwiGLUKeep><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, tgu, tgu, g, 0, nullptr,
-                                                                           none);
+  linear_tc_kernel<kLinearSwiGLUKeep><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, tgu, tgu, tgu, g, 0,
+                                                                           nullptr, none);
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
 }
@@ -547,10 +579,12 @@ inline int linear_swiglu_keep_impl(const void* X, const void* W, int64_t M, int6
 inline int linear_qkv_rope_impl(const void* X, const void* W, const void* q_norm_w, const void* k_norm_w,
                                 const void* rope_cos, const void* rope_sin, int64_t B, int64_t L, int64_t K,
                                 int Hq, int Hkv, float eps, void* q_out, void* k_out, void* v_out,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, int64_t table_rows, const int64_t* positions = nullptr,
+                                void* qkv_keep = nullptr, float* rstd_out = nullptr) {
   ORTHRUS_CHECK_ARG(X && W && q_norm_w && k_norm_w && rope_cos && rope_sin && q_out && k_out && v_out);
   ORTHRUS_CHECK_ARG(B > 0 && L > 0 && L % 128 == 0 && K > 0 && K % 8 == 0 && Hq > 0 && Hkv > 0);
   ORTHRUS_CHECK_ARG((Hq + 2 * Hkv) % 2 == 0);  // two whole heads per 256-column tile
+  ORTHRUS_CHECK_ARG(table_rows >= (positions == nullptr ? L : 1));
   ORTHRUS_CHECK_ARG(aligned16(X) && aligned16(W) && aligned16(q_norm_w) && aligned16(k_norm_w) &&
                     aligned16(rope_cos) && aligned16(rope_sin) && aligned16(q_out) && aligned16(k_out) &&
                     aligned16(v_out));
@@ -563,6 +597,11 @@ inline int linear_qkv_rope_impl(const void* X, const void* W, const void* q_norm
   if (!make_tmap_2d_bf16(&tq, q_out, 128, B * Hq * L, 128, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) return ORTHRUS_ECUDA;
   if (!make_tmap_2d_bf16(&tk, k_out, 128, B * Hkv * L, 128, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) return ORTHRUS_ECUDA;
   if (!make_tmap_2d_bf16(&tv, v_out, 128, B * Hkv * L, 128, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) return ORTHRUS_ECUDA;
+  CUtensorMap tp = tv;
+  ORTHRUS_CHECK_ARG(qkv_keep == nullptr || aligned16(qkv_keep));
+  if (qkv_keep != nullptr &&
+      !make_tmap_2d_bf16(&tp, qkv_keep, N, M, N, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return ORTHRUS_ECUDA;
   LinearGeometry g;
   g.M = static_cast<int>(M);
   g.N = static_cast<int>(N);
@@ -575,13 +614,17 @@ inline int linear_qkv_rope_impl(const void* X, const void* W, const void* q_norm
   qp.k_norm_w = static_cast<const __nv_bfloat16*>(k_norm_w);
   qp.rope_cos = static_cast<const __nv_bfloat16*>(rope_cos);
   qp.rope_sin = static_cast<const __nv_bfloat16*>(rope_sin);
+  qp.positions = positions;
+  qp.table_rows = table_rows;
+  qp.rstd_out = rstd_out;
+  qp.keep = qkv_keep != nullptr;
   qp.L = static_cast<int>(L);
   qp.Hq = Hq;
   qp.Hkv = Hkv;
   qp.eps = eps;
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(g.tiles, num_sms()));
   ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearQkvRope>, T::SMEM));
-  linear_tc_kernel<kLinearQkvRope><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, tq, tk, tv, g, 0, nullptr, qp);
+  linear_tc_kernel<kLinearQkvRope><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, tq, tk, tv, tp, g, 0, nullptr, qp);
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
 }

@@ -176,6 +176,42 @@ class DualViewAttention(torch.autograd.Function):
         return dqkv, dqw.to(qn.dtype), dkw.to(kn.dtype), None, None, None, None, None, None
 
 
+class DualViewAttentionFused(torch.autograd.Function):
+    """DualViewAttention with the twin q|k|v projection folded in (orthrus/objective.py:136-143,
+    160-165): forward = the projection GEMM with the q/k RMSNorm + RoPE prologue in its epilogue
+    (orthrus_linear_qkv_rope_keep_bf16, which also keeps the q / k columns of the projection and
+    rstd), then the dual-view attention; backward = the attention backward, the prologue backward,
+    then dh = dqkv W and dW = dqkv^T h. One Function, so the fp32 dq / dk / dv of the attention
+    backward reach the prologue backward without a cast."""
+
+    @staticmethod
+    def forward(ctx, h, w_qkv, q_norm_w, k_norm_w, ar_k, ar_v, positions, anchors, inv_freq, rope_cos,
+                rope_sin, meta):
+        B, Q, Hq, Hkv, hd, D, K, eps = meta
+        q, k2, v2, qkv, rstd = ops.linear_qkv_rope(h, w_qkv, q_norm_w, k_norm_w, (rope_cos, rope_sin), B, Q,
+                                                   Hq, Hkv, eps, positions=positions, keep=True)
+        o, lse = ops.attention_fwd(q, ar_k, ar_v, k2, v2, mask=MASK_DUAL, hd=hd, scale=hd ** -0.5,
+                                   anchors=anchors, block=K)
+        ctx.save_for_backward(h, w_qkv, qkv, q_norm_w, k_norm_w, ar_k, ar_v, positions, anchors, inv_freq,
+                              q, k2, v2, o, lse, rstd)
+        ctx.meta = meta
+        return o.view(B * Q, Hq * hd)
+
+    @staticmethod
+    def backward(ctx, grad_o):
+        h, w, qkv, qn, kn, ar_k, ar_v, positions, anchors, inv, q, k2, v2, o, lse, rstd = ctx.saved_tensors
+        B, Q, Hq, Hkv, hd, D, K, eps = ctx.meta
+        dout = grad_o.contiguous().view(B, Q, Hq, hd).to(q.dtype)
+        dq, dk2, dv2 = ops.attention_bwd(q, ar_k, ar_v, k2, v2, anchors, K, o, lse, dout, hd=hd,
+                                         scale=hd ** -0.5)
+        dqkv, dqw, dkw = ops.qkv_prep_backward(qkv, positions, inv, qn, kn, rstd, dq, dk2, dv2, B,
+                                               Q, Hq, Hkv, hd, D)
+        dh = dqkv @ w
+        dw = dqkv.t() @ h
+        return (dh, dw, dqw.to(qn.dtype), dkw.to(kn.dtype), None, None, None, None, None, None, None,
+                None)
+
+
 def _teacher_layer(model, i, x, pos, B, L, inv, rope=None):
     cfg = model.config
     layer = model.model.layers[i]
@@ -206,7 +242,7 @@ def _teacher_layer(model, i, x, pos, B, L, inv, rope=None):
     return x, k, v
 
 
-def _diffusion_layer(model, i, x, ar_k, ar_v, positions, anchors, inv, B, Q):
+def _diffusion_layer(model, i, x, ar_k, ar_v, positions, anchors, inv, B, Q, rope=None):
     cfg = model.config
     layer = model.model.layers[i]
     attn = layer.self_attn
@@ -215,9 +251,13 @@ def _diffusion_layer(model, i, x, ar_k, ar_v, positions, anchors, inv, B, Q):
     meta = (B, Q, Hq, Hkv, hd, padded_head_dim(hd), cfg.block_size, eps)
     h = _rms_norm(x, layer.input_layernorm.weight, eps)
     w_qkv = torch.cat([attn.q_proj_diff.weight, attn.k_proj_diff.weight, attn.v_proj_diff.weight], 0)
-    qkv = F.linear(h, w_qkv)
-    o = DualViewAttention.apply(qkv, attn.q_norm_diff.weight, attn.k_norm_diff.weight, ar_k, ar_v,
-                                positions, anchors, inv, meta)
+    if rope is not None and ops.fused_qkv_rope_supported(h, hd, padded_head_dim(hd), Q, Hq, Hkv):
+        o = DualViewAttentionFused.apply(h, w_qkv, attn.q_norm_diff.weight, attn.k_norm_diff.weight, ar_k,
+                                         ar_v, positions, anchors, inv, rope[0], rope[1], meta)
+    else:
+        qkv = F.linear(h, w_qkv)
+        o = DualViewAttention.apply(qkv, attn.q_norm_diff.weight, attn.k_norm_diff.weight, ar_k, ar_v,
+                                    positions, anchors, inv, meta)
     x = torch.addmm(x, o, attn.o_proj_diff.weight.t())
     h = _rms_norm(x, layer.post_attention_layernorm.weight, eps)
     w_gu = model._packed_mlp(i)
@@ -266,7 +306,7 @@ def model_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tenso
     x = F.embedding(block_ids.flatten(1), embed).reshape(B * Q, d)
     checkpoint = model.is_gradient_checkpointing and torch.is_grad_enabled()
     for i, (k, v) in enumerate(cache):
-        args = (model, i, x, k, v, positions, anchors, inv, B, Q)
+        args = (model, i, x, k, v, positions, anchors, inv, B, Q, rope)
         if checkpoint:
             x = torch.utils.checkpoint.checkpoint(_diffusion_layer, *args, use_reentrant=False)
         else:

@@ -159,11 +159,14 @@ def fused_qkv_rope_supported(x: torch.Tensor, hd: int, D: int, L_: int, Hq: int,
             and x.shape[1] % 8 == 0 and (Hq + 2 * Hkv) % 2 == 0)
 
 
-def linear_qkv_rope(x, w_qkv, q_norm_w, k_norm_w, rope, B: int, L_: int, Hq: int, Hkv: int, eps: float):
-    """Teacher q|k|v projection with q/k RMSNorm + RoPE (positions 0..L-1) in the GEMM epilogue.
-    Returns head-major q [B, Hq, L, 128], k, v [B, Hkv, L, 128] (same values as
-    qkv_prep(x @ w_qkv^T, ...) up to the GEMM's accumulation order)."""
-    _require_cuda(x, w_qkv, q_norm_w, k_norm_w)
+def linear_qkv_rope(x, w_qkv, q_norm_w, k_norm_w, rope, B: int, L_: int, Hq: int, Hkv: int, eps: float,
+                    positions: torch.Tensor | None = None, keep: bool = False):
+    """q|k|v projection with q/k RMSNorm + RoPE in the GEMM epilogue (positions 0..L-1 per
+    sequence, or the int64 [B, L] positions given). Returns head-major q [B, Hq, L, 128], k, v
+    [B, Hkv, L, 128] (same values as qkv_prep(x @ w_qkv^T, ...) up to the GEMM's accumulation
+    order); with keep also the token-major projection [B*L, (Hq + 2 Hkv) * 128] (q / k columns
+    written, for the prologue's backward) and rstd [B*L, Hq + Hkv]."""
+    _require_cuda(x, w_qkv, q_norm_w, k_norm_w, positions)
     x, w_qkv = x.contiguous(), w_qkv.contiguous()
     cos, sin = rope
     if cos.shape[0] < L_:
@@ -172,6 +175,23 @@ def linear_qkv_rope(x, w_qkv, q_norm_w, k_norm_w, rope, B: int, L_: int, Hq: int
     q = torch.empty(B, Hq, L_, 128, dtype=dt, device=dev)
     k = torch.empty(B, Hkv, L_, 128, dtype=dt, device=dev)
     v = torch.empty(B, Hkv, L_, 128, dtype=dt, device=dev)
+    if keep:
+        if positions is None:
+            raise ValueError("keep needs the positions of the rows")
+        positions = positions.to(torch.int64).contiguous()
+        if positions.numel() != B * L_:
+            raise ValueError("positions must hold one int64 per row")
+        qkv = torch.empty(B * L_, w_qkv.shape[0], dtype=dt, device=dev)
+        rstd = torch.empty(B * L_, Hq + Hkv, dtype=torch.float32, device=dev)
+        L.check(L.lib().orthrus_linear_qkv_rope_keep_bf16(
+            x.data_ptr(), w_qkv.data_ptr(), q_norm_w.contiguous().data_ptr(), k_norm_w.contiguous().data_ptr(),
+            cos.data_ptr(), sin.data_ptr(), cos.shape[0], positions.data_ptr(), B, L_, x.shape[1], Hq, Hkv,
+            float(eps),
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), qkv.data_ptr(), rstd.data_ptr(), L.stream_of(dev)),
+            "linear_qkv_rope_keep")
+        return q, k, v, qkv, rstd
+    if positions is not None:
+        raise ValueError("positions other than 0..L-1 are taken with keep=True only")
     L.check(L.lib().orthrus_linear_qkv_rope_bf16(
         x.data_ptr(), w_qkv.data_ptr(), q_norm_w.contiguous().data_ptr(), k_norm_w.contiguous().data_ptr(),
         cos.data_ptr(), sin.data_ptr(), B, L_, x.shape[1], Hq, Hkv, float(eps), q.data_ptr(), k.data_ptr(),

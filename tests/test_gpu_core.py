@@ -149,6 +149,36 @@ def test_fused_qkv_rope_matches_the_prologue(B, L, K, Hq, Hkv):
         assert (got.float() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item() + 1e-2
 
 
+@pytest.mark.parametrize("B,Q,K,Hq,Hkv", [(2, 256, 1024, 16, 8), (1, 384, 320, 4, 2)])
+def test_fused_qkv_rope_keep_for_the_trainable_view(B, Q, K, Hq, Hkv):
+    """The trainable view's form: RoPE at given positions (anchor + offset per block), and the q / k
+    columns of the projection and rstd kept for the backward; all bit-identical to the projection
+    kernel followed by the prologue kernel."""
+    ops = _ops()
+    g = torch.Generator(device=DEV).manual_seed(Q + K + Hq)
+    H = Hq + 2 * Hkv
+    L = 2048
+    x = torch.randn(B * Q, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(H * 128, K, device=DEV, generator=g) / K ** 0.5).bfloat16()
+    qn = (1 + 0.2 * torch.randn(128, device=DEV, generator=g)).bfloat16()
+    kn = (1 + 0.2 * torch.randn(128, device=DEV, generator=g)).bfloat16()
+    inv = ops.rope_inv_freq(128, 1_000_000.0, torch.device(DEV))
+    rope = ops.rope_table(inv, L)
+    blocks = Q // 32
+    anchors = torch.randint(1, L - 32, (B, blocks), device=DEV, generator=g).sort(-1).values
+    pos = (anchors[:, :, None] + torch.arange(32, device=DEV)).reshape(B, Q).contiguous()
+    q, k, v, qkv, rstd = ops.linear_qkv_rope(x, w, qn, kn, rope, B, Q, Hq, Hkv, 1e-6, positions=pos,
+                                             keep=True)
+    proj = ops.linear(x, w)
+    rq, rk, rv, rr = ops.qkv_prep(proj, pos, inv, qn, kn, B, Q, Hq, Hkv, 128, 128, 1e-6, want_rstd=True)
+    torch.cuda.synchronize()
+    assert torch.equal(q, rq) and torch.equal(k, rk) and torch.equal(v, rv)
+    assert torch.equal(qkv[:, : (Hq + Hkv) * 128], proj[:, : (Hq + Hkv) * 128])
+    assert torch.equal(rstd, rr.view_as(rstd))
+    from orthrus_training_b200 import _lib
+    assert _lib.device_error(0) == 0
+
+
 def test_rope_table_matches_sincos():
     ops = _ops()
     inv = ops.rope_inv_freq(128, 1_000_000.0, torch.device(DEV))
