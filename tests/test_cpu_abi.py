@@ -48,3 +48,48 @@ def test_ops_refuse_cpu_tensors():
         ops.gemm(torch.zeros(4, 4), torch.zeros(4, 4))
     with pytest.raises(ValueError):
         ops.rms_norm(torch.zeros(2, 8), torch.ones(8), 1e-6)
+
+
+def test_new_ops_refuse_cpu_tensors():
+    """The fused projections, the RoPE table and the tree-mask attention have no CPU path either."""
+    import pytest
+    import torch
+
+    from orthrus_training_b200 import ops
+
+    x = torch.zeros(128, 64, dtype=torch.bfloat16)
+    w = torch.zeros(256, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        ops.linear(x, w)
+    with pytest.raises(ValueError):
+        ops.linear(x, w, residual=torch.zeros(128, 256, dtype=torch.bfloat16))
+    with pytest.raises(ValueError):
+        ops.linear_swiglu(x, w)
+    with pytest.raises(ValueError):
+        ops.linear_swiglu(x, w, keep_gate_up=True)
+    with pytest.raises(ValueError):
+        ops.rope_table(torch.ones(64), 16)
+    n = torch.ones(128, dtype=torch.bfloat16)
+    rope = (torch.zeros(128, 64, dtype=torch.bfloat16), torch.zeros(128, 64, dtype=torch.bfloat16))
+    with pytest.raises(ValueError):
+        ops.linear_qkv_rope(x, torch.zeros(4 * 128, 64, dtype=torch.bfloat16), n, n, rope, 1, 128, 2, 1, 1e-6)
+    q = torch.zeros(1, 2, 4, 64, dtype=torch.bfloat16)
+    k = torch.zeros(1, 1, 16, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        ops.attention_fwd(q, k, k, k, k, mask=3, hd=64, scale=0.125,
+                          offset=torch.zeros(1, dtype=torch.int32), limit2=torch.ones(4, dtype=torch.int32))
+
+
+def test_fused_shape_predicates():
+    import torch
+
+    from orthrus_training_b200 import ops
+
+    x = torch.zeros(8, 1024, dtype=torch.bfloat16)
+    assert ops.fused_linear_supported(x, torch.zeros(4096, 1024, dtype=torch.bfloat16), 4096)
+    assert not ops.fused_linear_supported(x, torch.zeros(4000, 1024, dtype=torch.bfloat16), 4000)
+    assert not ops.fused_linear_supported(x.float(), torch.zeros(4096, 1024), 4096)
+    assert ops.fused_qkv_rope_supported(x, 128, 128, 2048, 16, 8)
+    assert not ops.fused_qkv_rope_supported(x, 64, 64, 2048, 16, 8)       # head dim 128 only
+    assert not ops.fused_qkv_rope_supported(x, 128, 128, 2000, 16, 8)     # whole 128-row tiles
+    assert not ops.fused_qkv_rope_supported(x, 128, 128, 2048, 15, 8)     # two heads per tile
