@@ -285,6 +285,200 @@ def run_decode(args):
                                                      f"fp32 diffusion_generate of the CPU port ({sec:.1f} s)"}))
 
 
+# --- isolated kernel cases (--kernel-case) -----------------------------------------------------
+#
+# Each hot entry point alone at the shapes of one training micro-batch (8 rows x 2048 tokens,
+# 16 query / 8 KV heads of 128, 32 anchors, K = 32), timed with CUDA events per call. With small
+# --steps these are also the programs the ncu captures profile: each keeps a few GB on the device
+# and launches its kernels a handful of times.
+#   causal   teacher attention forward, causal over 2048 keys          (orthrus/objective.py:155)
+#   dual     dual-view attention forward, A*K queries over the AR prefix and own blocks (:163)
+#   dualbwd  dual-view attention forward, then backward (dQ; dK/dV of the own-block keys)
+#   lmhead   fused LM head + KL of one step: 7936 = 8 * 32 * 31 student rows against 7936 teacher
+#            rows, V = 151936, d = 1024                                   (:338-392)
+#   prologue q/k RMSNorm + RoPE + head-major scatter of the teacher's q|k|v projection, fwd + bwd
+#   linear   the projections of a layer at 16384 rows through torch (cuBLAS) and through this
+#            library's tcgen05 kernels                                    (:136-149)
+#   sweep    dual-view attention fwd + bwd over L in {1024..8192}, K in {16, 32, 64}, A in
+#            {8, 32, 64} (batch filling 16384 query tokens, at most 65536 keys per head), and the
+#            fused LM head + KL over N in {4096, 16384, 65536} student rows
+
+KC_HQ, KC_HKV, KC_HD = 16, 8, 128
+KC_LM_N = ROWS * ANCHORS * (BLOCK - 1)
+KC_LM_V, KC_LM_D = 151936, 1024
+
+
+def _kc_time(fn, iters: int, warmup: int) -> float:
+    """Milliseconds per call of fn: CUDA events around `iters` back-to-back calls."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def _kc_dual_inputs(gen, dev, B, L, A, K):
+    Tq = A * K
+    rnd = lambda *shape: torch.randn(*shape, device=dev, generator=gen).bfloat16()  # noqa: E731
+    q = rnd(B, KC_HQ, Tq, KC_HD)
+    k1, v1 = rnd(B, KC_HKV, L, KC_HD), rnd(B, KC_HKV, L, KC_HD)
+    k2, v2 = rnd(B, KC_HKV, Tq, KC_HD), rnd(B, KC_HKV, Tq, KC_HD)
+    anchors = torch.stack([torch.randperm(L - K, device=dev, generator=gen)[:A].add(1).sort().values
+                           for _ in range(B)])
+    return q, k1, v1, k2, v2, anchors
+
+
+def kernel_case(case: str, iters: int, warmup: int) -> dict:
+    """{entry point: {"ms_per_call", "tflops" or "gbs"}} for one case."""
+    import math
+
+    from orthrus_training_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    B, L, A, K, HQ, HKV, HD = ROWS, SEQ, ANCHORS, BLOCK, KC_HQ, KC_HKV, KC_HD
+    sc = 1.0 / math.sqrt(HD)
+    rnd = lambda *shape, scale=1.0: (torch.randn(*shape, device=dev, generator=gen) * scale).bfloat16()  # noqa
+    timed = []  # (name, fn, algorithmic work per call, "tflops" | "gbs")
+    if case == "causal":
+        q, k, v = rnd(B, HQ, L, HD), rnd(B, HKV, L, HD), rnd(B, HKV, L, HD)
+        timed.append(("attn_fwd_causal", lambda: ops.attention_fwd(q, k, v, mask=0, hd=HD, scale=sc),
+                      ops.attention_flops(0, B, HQ, L, HD), "tflops"))
+    elif case in ("dual", "dualbwd"):
+        q, k1, v1, k2, v2, anchors = _kc_dual_inputs(gen, dev, B, L, A, K)
+        fwd = lambda: ops.attention_fwd(q, k1, v1, k2, v2, mask=1, hd=HD, scale=sc, anchors=anchors,  # noqa
+                                        block=K)
+        flops = float(ops.attention_flops(1, B, HQ, A * K, HD, anchors, K, L))
+        timed.append(("attn_fwd_dual", fwd, flops, "tflops"))
+        if case == "dualbwd":
+            o, lse = fwd()
+            dout = rnd(B, A * K, HQ, HD)
+            timed.append(("attn_bwd_dual", lambda: ops.attention_bwd(q, k1, v1, k2, v2, anchors, K, o, lse, dout,
+                                                                     hd=HD, scale=sc), 1.5 * flops, "tflops"))
+    elif case == "lmhead":
+        n = m = KC_LM_N
+        s, t = rnd(n, KC_LM_D), rnd(m, KC_LM_D)
+        idx = torch.randint(0, m, (n,), device=dev, generator=gen).sort().values
+        w = rnd(KC_LM_V, KC_LM_D, scale=0.05)
+        # logits of the student and unique teacher rows once each, plus the grad GEMM diff @ W
+        timed.append(("lmhead_kl", lambda: ops.lmhead_kl(s, t, idx, w),
+                      2.0 * KC_LM_D * KC_LM_V * (2 * n + m), "tflops"))
+    elif case == "prologue":
+        rows, H = B * L, HQ + 2 * HKV
+        qkv = rnd(rows, H * HD)
+        pos = torch.arange(L, device=dev).repeat(B)
+        inv = ops.rope_inv_freq(HD, 1_000_000.0, dev)
+        qw, kw = (1 + rnd(HD, scale=0.1).float()).bfloat16(), (1 + rnd(HD, scale=0.1).float()).bfloat16()
+        q, k, v, rstd = ops.qkv_prep(qkv, pos, inv, qw, kw, B, L, HQ, HKV, HD, HD, 1e-6, want_rstd=True)
+        dq, dk, dv = (torch.randn(t.shape, device=dev, generator=gen) for t in (q, k, v))
+        timed.append(("qkv_prep_fwd", lambda: ops.qkv_prep(qkv, pos, inv, qw, kw, B, L, HQ, HKV, HD, HD, 1e-6),
+                      2 * rows * H * HD * 2, "gbs"))  # bf16 in and out
+        timed.append(("qkv_prep_bwd", lambda: ops.qkv_prep_backward(qkv, pos, inv, qw, kw, rstd, dq, dk, dv, B, L,
+                                                                    HQ, HKV, HD, HD),
+                      rows * H * HD * (2 + 4 + 2), "gbs"))
+    elif case == "linear":
+        rows, d, ff, hq = B * L, 1024, 3072, HQ * HD
+        x, o, a = rnd(rows, d), rnd(rows, hq), rnd(rows, ff)
+        w_qkv = rnd((HQ + 2 * HKV) * HD, d, scale=0.03)
+        w_o, w_gu, w_d = rnd(d, hq, scale=0.02), rnd(2 * ff, d, scale=0.03), rnd(d, ff, scale=0.02)
+        fl = lambda n, k: 2.0 * rows * n * k  # noqa: E731
+        pos = torch.arange(L, device=dev).repeat(B).view(B, L)
+        inv = ops.rope_inv_freq(HD, 1_000_000.0, dev)
+        rope = ops.rope_table(inv, L)
+        qw, kw = (1 + rnd(HD, scale=0.1).float()).bfloat16(), (1 + rnd(HD, scale=0.1).float()).bfloat16()
+        nq = w_qkv.shape[0]
+        timed += [
+            ("qkv_prologue_cublas", lambda: ops.qkv_prep(x @ w_qkv.t(), pos, inv, qw, kw, B, L, HQ, HKV, HD, HD,
+                                                         1e-6), fl(nq, d), "tflops"),
+            ("qkv_prologue_fused", lambda: ops.linear_qkv_rope(x, w_qkv, qw, kw, rope, B, L, HQ, HKV, 1e-6),
+             fl(nq, d), "tflops"),
+            ("qkv_cublas", lambda: x @ w_qkv.t(), fl(nq, d), "tflops"),
+            ("qkv_fused", lambda: ops.linear(x, w_qkv), fl(nq, d), "tflops"),
+            ("o_residual_cublas", lambda: torch.addmm(x, o, w_o.t()), fl(d, hq), "tflops"),
+            ("o_residual_fused", lambda: ops.linear(o, w_o, residual=x), fl(d, hq), "tflops"),
+            ("gate_up_cublas", lambda: x @ w_gu.t(), fl(2 * ff, d), "tflops"),
+            ("gate_up_swiglu_cublas", lambda: ops.silu_mul(x @ w_gu.t()), fl(2 * ff, d), "tflops"),
+            ("gate_up_swiglu_fused", lambda: ops.linear_swiglu(x, w_gu), fl(2 * ff, d), "tflops"),
+            ("down_residual_cublas", lambda: torch.addmm(x, a, w_d.t()), fl(d, ff), "tflops"),
+            ("down_residual_fused", lambda: ops.linear(a, w_d, residual=x), fl(d, ff), "tflops"),
+        ]
+    else:
+        raise ValueError(f"unknown kernel case {case!r}")
+    out = {}
+    for name, fn, work, unit in timed:
+        ms = _kc_time(fn, iters, warmup)
+        rate = work / (ms / 1e3) / (1e9 if unit == "gbs" else 1e12)
+        out[name] = {"ms_per_call": round(ms, 4), unit: round(float(rate), 1)}
+    return out
+
+
+def kernel_sweep(iters: int, warmup: int):
+    """Yields one record per configuration as it is measured: dual-view attention forward and
+    backward, then the fused LM head + KL."""
+    import math
+
+    from orthrus_training_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    sc = 1.0 / math.sqrt(KC_HD)
+    for L1 in (1024, 2048, 4096, 8192):
+        for K1 in (16, 32, 64):
+            for A1 in (8, 32, 64):
+                if A1 * K1 > L1:
+                    continue
+                B1 = max(1, min(16384 // (A1 * K1), 65536 // L1))
+                gen = torch.Generator(device=dev).manual_seed(L1 + K1 + A1)
+                Tq = A1 * K1
+                q, k1, v1, k2, v2, anchors = _kc_dual_inputs(gen, dev, B1, L1, A1, K1)
+                fwd = lambda: ops.attention_fwd(q, k1, v1, k2, v2, mask=1, hd=KC_HD, scale=sc,  # noqa: E731
+                                                anchors=anchors, block=K1)
+                flops = float(ops.attention_flops(1, B1, KC_HQ, Tq, KC_HD, anchors, K1, L1))
+                o, lse = fwd()
+                dout = torch.randn(B1, Tq, KC_HQ, KC_HD, device=dev, generator=gen).bfloat16()
+                bwd = lambda: ops.attention_bwd(q, k1, v1, k2, v2, anchors, K1, o, lse, dout,  # noqa: E731
+                                                hd=KC_HD, scale=sc)
+                tf, tb = _kc_time(fwd, iters, warmup), _kc_time(bwd, iters, warmup)
+                yield {"case": "attention", "L": L1, "K": K1, "A": A1, "B": B1, "query_tokens": B1 * Tq,
+                       "fwd_ms": round(tf, 4), "fwd_tflops": round(flops / tf / 1e9, 1),
+                       "bwd_ms": round(tb, 4), "bwd_tflops": round(1.5 * flops / tb / 1e9, 1)}
+                del q, k1, v1, k2, v2, o, lse, dout
+    for n in (4096, 16384, 65536):
+        gen = torch.Generator(device=dev).manual_seed(n)
+        s = torch.randn(n, KC_LM_D, device=dev, generator=gen).bfloat16()
+        t = torch.randn(n, KC_LM_D, device=dev, generator=gen).bfloat16()
+        idx = torch.arange(n, device=dev)
+        w = (torch.randn(KC_LM_V, KC_LM_D, device=dev, generator=gen) * 0.05).bfloat16()
+        ms = _kc_time(lambda: ops.lmhead_kl(s, t, idx, w), max(1, iters // 4), max(1, warmup // 2))
+        flops = 2.0 * KC_LM_D * KC_LM_V * (2 * n + n)
+        yield {"case": "lmhead_kl", "N": n, "teacher_rows": n, "ms": round(ms, 3),
+               "tflops": round(flops / ms / 1e9, 1)}
+        del s, t, w
+
+
+def run_kernel_case(args) -> None:
+    """--kernel-case NAME: one isolated case on cuda:0 (--steps calls after --warmup), one JSON
+    line per entry point (per configuration for the sweep); exits 1 if the device error word is
+    set afterwards."""
+    from orthrus_training_b200 import _lib
+
+    torch.cuda.set_device(0)
+    if args.kernel_case == "sweep":
+        for rec in kernel_sweep(args.steps, args.warmup):
+            emit(json.dumps(rec))
+    else:
+        for name, rec in kernel_case(args.kernel_case, args.steps, args.warmup).items():
+            emit(json.dumps({"kernel_case": args.kernel_case, "entry_point": name, **rec}))
+    err = _lib.device_error(0)
+    if err:
+        emit(json.dumps({"device_error": err}))
+        raise SystemExit(1)
+
+
 def step_roofline(cfg, kernels: dict, steps: int, ms_per_step: float, pk: dict) -> dict:
     """The whole step against its algorithmic work per GPU: projection GEMMs of the teacher
     (forward over every token) and of the diffusion view (forward, dX, and dW of the twins only),
@@ -478,8 +672,11 @@ def main():
     ap.add_argument("--decode-batch", type=int, nargs="+", default=[1, 32])
     ap.add_argument("--decode-new", type=int, default=512)
     ap.add_argument("--decode-dtype", default="bf16", choices=["bf16", "fp32"])
+    ap.add_argument("--kernel-case", default=None,
+                    choices=["causal", "dual", "dualbwd", "lmhead", "prologue", "linear", "sweep"],
+                    help="time one hot entry point alone (--steps calls after --warmup)")
     args = ap.parse_args()
-    if args.warmup < 3:
+    if args.warmup < 3 and args.kernel_case is None:
         raise SystemExit("--warmup must be >= 3")
     # native libraries may print on file descriptor 1 (NCCL's version banner at communicator
     # set-up): send all of that to stderr so stdout holds only the JSON result line
@@ -487,7 +684,9 @@ def main():
     _RESULT_FD = os.dup(1)
     os.dup2(2, 1)
     try:
-        if args.decode:
+        if args.kernel_case is not None:
+            run_kernel_case(args)
+        elif args.decode:
             run_decode(args)
         elif args.impl == "reference":
             run_reference(args)

@@ -216,7 +216,10 @@ int orthrus_attn_fwd(const void* q, const void* k1, const void* v1, int64_t s1h,
 /* Backward of the DUAL mask (training): from do_ [B, Tq, Hq, hd] (token-major), o, lse, q and the
  * two sources, writes dq [B, Hq, Tq, D] fp32 and dk2 / dv2 [B, Hkv, L2, D] fp32 (source-2 keys
  * only: source-1 keys are the frozen teacher's and get no gradient).
- * workspace: orthrus_attn_bwd_workspace_bytes(). */
+ * workspace: orthrus_attn_bwd_workspace_bytes().
+ * bf16 with an even GQA group runs dK/dV on a library-owned side stream of the device, forked
+ * from and joined back into `stream` inside the call; the fork/join events are shared per device
+ * and guarded by a mutex, so host threads may call this concurrently with their own workspaces. */
 size_t orthrus_attn_bwd_workspace_bytes(int64_t B, int Hq, int64_t Tq);
 int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b,
                      int64_t L1, const void* k2, const void* v2, int64_t s2h, int64_t s2b,
@@ -236,7 +239,10 @@ int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h,
  * The first call on a device looks up the array's device address with that device current; make
  * that first call before any stream capture. Every call reuses the same array and fully rewrites
  * the part it reads, so nothing needs clearing, but calls that overlap on the GPU (two streams,
- * two threads) race on it. Arguments and outputs as orthrus_attn_bwd. */
+ * two threads) race on it. Like orthrus_attn_bwd, a bf16 call with an even GQA group runs its
+ * dK/dV kernel on the library's per-device side stream, which every backward on that device
+ * shares: "overlapping calls" includes any other backward whose dK/dV is still in flight there.
+ * Arguments and outputs as orthrus_attn_bwd. */
 #define ORTHRUS_ATTN_BWD_NOALLOC_MAX_ROWS 262144
 int orthrus_attn_bwd_noalloc(const void* q, const void* k1, const void* v1, int64_t s1h,
                              int64_t s1b, int64_t L1, const void* k2, const void* v2, int64_t s2h,

@@ -335,9 +335,13 @@ namespace {
 // backward runs beside the dQ kernel and fills the SMs its last partial wave leaves idle. Created
 // on the first backward on each device; the join makes the caller's stream wait for the side
 // stream, so the caller sees one ordered call (stream capture records it as a fork and a join).
+// The events are shared by every caller on the device, so `use` is held from the fork record to
+// the join wait: another host thread cannot re-record the fork between one call's record and its
+// side-stream wait (which would make that call's dK/dV wait on the other caller's stream instead).
 struct SideStream {
   cudaStream_t stream = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
+  std::mutex use;
 };
 
 SideStream* side_stream_on_current_device() {
@@ -404,6 +408,7 @@ int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h,
       // dQ on the caller's stream, dK/dV on the side stream (both only read delta and the inputs)
       SideStream* side = side_stream_on_current_device();
       if (side == nullptr) return ORTHRUS_ECUDA;
+      std::lock_guard<std::mutex> in_use(side->use);  // fork record .. join wait (launches only)
       ORTHRUS_CHECK_CUDA(cudaEventRecord(side->fork, st));
       if (D == 128) {
         if (set_smem(attn_dq_tc2_kernel<128>, Dq2Smem<128>::SMEM)) return ORTHRUS_ECUDA;

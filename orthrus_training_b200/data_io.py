@@ -9,9 +9,9 @@
   same generator calls so that a run resumed here sees the rows the reference would have fed.
 - Training checkpoints (orthrus/checkpoint.py:27,68-97): a directory holding
   ``trainable.safetensors`` (the diffusion twins under their parameter names),
-  ``optimizer.pt`` (optimizer and scheduler state) and ``trainer_state.json``, written to
-  ``<path>.tmp`` and renamed when complete. Checkpoints move between the reference and this
-  package unchanged, since the parameter names are the same.
+  ``optimizer.pt`` (optimizer and scheduler state) and ``trainer_state.json``, built in a hidden
+  staging directory and swapped in once complete. Checkpoints move between the reference and this
+  package unchanged, since the file names and parameter names are the same.
 
 - Model export (orthrus/checkpoint.py:98-105): a Hugging Face model directory with the bf16
   weights (``model.safetensors``, the reference's parameter names, the tied ``lm_head.weight``
@@ -119,37 +119,74 @@ class DevicePrefetcher:
         return index, ids_dev, mask_dev
 
 
+def _trainable(model) -> dict[str, torch.nn.Parameter]:
+    return {name: p for name, p in model.named_parameters() if p.requires_grad}
+
+
+def _publish(staging: Path, path: Path) -> None:
+    """Swaps a completed staging directory in at `path`. An older checkpoint there is first moved
+    aside and deleted only after the new one is in place, so at every instant `path` is either the
+    old complete checkpoint or the new one."""
+    retired = None
+    if path.exists():
+        retired = path.with_name(f".{path.name}.retired-{os.getpid()}")
+        shutil.rmtree(retired, ignore_errors=True)
+        os.replace(path, retired)
+    os.replace(staging, path)
+    if retired is not None:
+        shutil.rmtree(retired, ignore_errors=True)
+
+
 def save_checkpoint(path: Path, model, optimizer, scheduler, state: dict) -> None:
-    """Twin weights, optimizer / scheduler state and progress, written atomically."""
+    """Writes the trainable twins (safetensors, under their parameter names), the optimizer and
+    scheduler state and the progress dict as the reference's checkpoint directory. The files are
+    built in a hidden staging directory beside `path` (a name the reference's ``step-*`` listing
+    never matches) and flushed to disk before the directory is swapped in."""
+    import tempfile
+
     from safetensors.torch import save_file
 
     path = Path(path)
-    tmp = path.with_name(path.name + ".tmp")
-    shutil.rmtree(tmp, ignore_errors=True)
-    tmp.mkdir(parents=True)
-    weights = {n: p.detach().contiguous() for n, p in model.named_parameters() if p.requires_grad}
-    save_file(weights, tmp / WEIGHTS)
-    torch.save({"optimizer": optimizer.state_dict(), "scheduler": scheduler.state_dict()}, tmp / OPTIMIZER)
-    (tmp / STATE).write_text(json.dumps(state, indent=2), encoding="utf-8")
-    shutil.rmtree(path, ignore_errors=True)
-    os.replace(tmp, path)
+    path.parent.mkdir(parents=True, exist_ok=True)
+    staging = Path(tempfile.mkdtemp(prefix=f".{path.name}.staging-", dir=path.parent))
+    try:
+        tensors = {name: p.detach().contiguous() for name, p in _trainable(model).items()}
+        save_file(tensors, staging / WEIGHTS)
+        torch.save({"optimizer": optimizer.state_dict(), "scheduler": scheduler.state_dict()},
+                   staging / OPTIMIZER)
+        (staging / STATE).write_text(json.dumps(state, indent=2), encoding="utf-8")
+        for name in (WEIGHTS, OPTIMIZER, STATE):
+            with open(staging / name, "rb") as f:
+                os.fsync(f.fileno())
+        _publish(staging, path)
+    except BaseException:
+        shutil.rmtree(staging, ignore_errors=True)
+        raise
 
 
 def load_checkpoint(path: Path, model, optimizer=None, scheduler=None) -> dict:
-    """Restores the twins (their names must be exactly the model's trainable parameters) and, when
-    given, the optimizer and scheduler; returns the saved progress state."""
-    from safetensors.torch import load_file
+    """Loads a checkpoint directory into the model's trainable twins (the stored names must be
+    exactly those parameters, with their shapes) and, when given, the optimizer and scheduler.
+    Returns the stored progress dict."""
+    from safetensors import safe_open
 
     path = Path(path)
+    params = _trainable(model)
     device = next(model.parameters()).device
-    weights = load_file(path / WEIGHTS, device=str(device))
-    trainable = {n for n, p in model.named_parameters() if p.requires_grad}
-    if set(weights) != trainable:
-        raise RuntimeError(f"checkpoint {path} does not match the trainable parameters")
-    with torch.no_grad():
-        for name, param in model.named_parameters():
-            if name in weights:
-                param.copy_(weights[name])
+    with safe_open(str(path / WEIGHTS), framework="pt", device=str(device)) as stored:
+        names = set(stored.keys())
+        missing, unexpected = sorted(set(params) - names), sorted(names - set(params))
+        if missing or unexpected:
+            raise RuntimeError(f"{path}: the stored tensors are not the model's trainable parameters "
+                               f"(missing {missing[:3]}{'...' if len(missing) > 3 else ''}, "
+                               f"unexpected {unexpected[:3]}{'...' if len(unexpected) > 3 else ''})")
+        with torch.no_grad():
+            for name, param in params.items():
+                value = stored.get_tensor(name)
+                if value.shape != param.shape:
+                    raise RuntimeError(f"{path}: {name} is stored as {tuple(value.shape)}, the model "
+                                       f"has {tuple(param.shape)}")
+                param.copy_(value)
     if optimizer is not None:
         blob = torch.load(path / OPTIMIZER, map_location=device, weights_only=False)
         optimizer.load_state_dict(blob["optimizer"])

@@ -169,7 +169,9 @@ def linear_qkv_rope(x, w_qkv, q_norm_w, k_norm_w, rope, B: int, L_: int, Hq: int
     _require_cuda(x, w_qkv, q_norm_w, k_norm_w, positions)
     x, w_qkv = x.contiguous(), w_qkv.contiguous()
     cos, sin = rope
-    if cos.shape[0] < L_:
+    if positions is None and cos.shape[0] < L_:
+        # rows take positions 0..L-1; with explicit positions (the trainable view's block rows,
+        # whose count A*K may exceed the sequence) the kernel bounds-checks each position instead
         raise ValueError("the RoPE table is shorter than the sequence")
     dev, dt = x.device, x.dtype
     q = torch.empty(B, Hq, L_, 128, dtype=dt, device=dev)

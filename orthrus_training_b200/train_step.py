@@ -100,7 +100,8 @@ class Trainer:
 
     def __init__(self, model, *, lr=1e-4, betas=(0.9, 0.95), weight_decay=0.0, total_steps=1000,
                  warmup_ratio=0.05, min_lr_ratio=0.1, max_grad_norm=1.0, num_anchors=32,
-                 kl_chunk_size=4096, gamma=0.0, seed=42, world=1, rank=0, group=None):
+                 kl_chunk_size=4096, gamma=0.0, seed=42, world=1, rank=0, group=None,
+                 check_device_every=50):
         from orthrus_training_b200.modeling_orthrus import freeze_to_diffusion
 
         self.model = model
@@ -119,18 +120,32 @@ class Trainer:
         self.seed = seed
         self.world, self.rank = world, rank
         self.step_index = 0
-        self.skipped = 0
+        self.fused = fused
+        # skipped updates, counted on the device (no host read per step)
+        self.skipped = torch.zeros((), dtype=torch.int64, device=self.params[0].device)
+        # every this many steps the library's device error word is read (a host sync): a bounded
+        # wait that ran out or a clamped out-of-range index then raises instead of passing silently
+        self.check_device_every = check_device_every
 
-    def step(self, micro_batches: list[tuple[torch.Tensor, torch.Tensor]], epoch: int = 0) -> dict:
+    def step(self, micro_batches: list[tuple[torch.Tensor, torch.Tensor]], epoch: int = 0,
+             indices: list[int] | None = None) -> dict:
         """One optimizer step over this rank's micro-batches [(input_ids, assistant_mask), ...]
-        (already on the device). Returns loss (device tensor), grad_norm, skipped."""
+        (already on the device). `indices` are the micro-batches' indices in the epoch (the keys of
+        their anchor generators, as data_io.batches yields them); by default the global
+        micro-batch count of this trainer. Returns loss, grad_norm and skipped as device tensors
+        (nothing is read back to the host)."""
         model = self.model
         accum = len(micro_batches)
+        if indices is not None and len(indices) != accum:
+            raise ValueError("one index per micro-batch")
         self.buckets.zero()
         losses = []
         for j, (ids, mask) in enumerate(micro_batches):
             self.buckets.arm(j == accum - 1)
-            index = (self.step_index * accum + j) * self.world + self.rank  # global micro-batch
+            if indices is not None:
+                index = indices[j]
+            else:
+                index = (self.step_index * accum + j) * self.world + self.rank  # global micro-batch
             rng = anchor_rng(self.seed, epoch, index, device=ids.device)
             anchors, valid = sample_anchors(mask, model.config.block_size, self.num_anchors, rng)
             loss, stats = orthrus_loss(model, ids, mask, anchors, valid, self.kl_chunk_size,
@@ -139,11 +154,22 @@ class Trainer:
             losses.append(loss.detach())
         self.buckets.wait()
         grad_norm = torch.nn.utils.clip_grad_norm_(self.params, self.max_grad_norm)
-        finite = bool(torch.isfinite(grad_norm))
-        if finite:
+        nonfinite = ~torch.isfinite(grad_norm)
+        if self.fused:
+            # the fused AdamW kernel leaves parameters, moments and step counts untouched when
+            # found_inf is 1: the reference's "skip the update if the norm is not finite"
+            # (orthrus/train.py:364-368) decided on the device, without reading the norm back
+            self.optimizer.found_inf = nonfinite.to(torch.float32)
             self.optimizer.step()
+        elif bool(nonfinite):
+            pass
         else:
-            self.skipped += 1
+            self.optimizer.step()
+        self.skipped += nonfinite.to(torch.int64)
         self.scheduler.step()
         self.step_index += 1
-        return {"loss": torch.stack(losses).mean(), "grad_norm": grad_norm, "skipped": not finite}
+        if self.check_device_every and self.step_index % self.check_device_every == 0:
+            from orthrus_training_b200 import _lib
+
+            _lib.raise_on_device_error(grad_norm.device.index or 0)
+        return {"loss": torch.stack(losses).mean(), "grad_norm": grad_norm, "skipped": nonfinite}

@@ -2,8 +2,8 @@
 
 Run in a container that has the reference checked out (it is pure Python):
 
-    python tests/golden/make_golden.py /root/reference          # every fixture
-    python tests/golden/make_golden.py /root/reference data     # data_batches.pt only
+    python tests/golden/make_golden.py <reference checkout>          # every fixture
+    python tests/golden/make_golden.py <reference checkout> data     # data_batches.pt only
 
 It imports the reference's own modules (orthrus.modeling_orthrus, orthrus.objective,
 orthrus.decoding, orthrus.evaluate) and stores seeded inputs together with the reference outputs,
@@ -422,5 +422,6 @@ def main(reference: str, only: str | None = None) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference",
-         sys.argv[2] if len(sys.argv) > 2 else None)
+    if len(sys.argv) < 2:
+        raise SystemExit("usage: make_golden.py <reference checkout> [data]")
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else None)

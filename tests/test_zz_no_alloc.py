@@ -18,10 +18,10 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-def _case(dtype, hd, seed):
+def _case(dtype, hd, seed, Hq=4, Hkv=2):
     from orthrus_training_b200 import ops
 
-    B, Hq, Hkv, L, A, K = 2, 4, 2, 300, 8, 32
+    B, L, A, K = 2, 300, 8, 32
     g = torch.Generator().manual_seed(seed)
     Tq = A * K
     q = torch.randn(B, Hq, Tq, hd, generator=g).to(DEV, dtype)
@@ -76,20 +76,24 @@ def _without_allocation(c, code):
     return dq, dk, dv
 
 
-@pytest.mark.parametrize("dtype,hd", [(torch.bfloat16, 128), (torch.float32, 32)])
-def test_noalloc_backward_matches_workspace_backward_twice(dtype, hd):
+# (bf16, 4/2 heads): dQ two heads per CTA with dK/dV on the side stream; (bf16, 6/2 heads): the odd
+# GQA group runs dQ and dK/dV on the caller's stream; (fp32): the exact CUDA-core kernels.
+@pytest.mark.parametrize("dtype,hd,Hq,Hkv", [(torch.bfloat16, 128, 4, 2), (torch.bfloat16, 128, 6, 2),
+                                             (torch.float32, 32, 4, 2)])
+def test_noalloc_backward_matches_workspace_backward_twice(dtype, hd, Hq, Hkv):
     from orthrus_training_b200 import _lib
 
     code = _lib.dtype_code(dtype)
-    tol = 3e-2 if dtype == torch.bfloat16 else 2e-5  # the attention tests' tolerances
     for seed in (0, 1):  # two calls in a row; the second reuses the fixed scratch
-        c = _case(dtype, hd, seed)
+        c = _case(dtype, hd, seed, Hq, Hkv)
         ref = _with_workspace(c, code)
         got = _without_allocation(c, code)
         torch.cuda.synchronize()
         for a, r in zip(got, ref):
+            # the same kernels on the same inputs: only where delta lives differs, so the results
+            # are identical bit for bit (a stale or misaddressed scratch row would show here)
             assert torch.isfinite(a).all()
-            assert (a - r).abs().max().item() <= tol * max(1.0, r.abs().max().item())
+            assert torch.equal(a, r)
     assert _lib.device_error(0) == 0
 
 
