@@ -187,6 +187,16 @@ int orthrus_qkv_prep_bwd(const void* qkv, const int64_t* positions, const float*
                          float* dk_norm_w, void* workspace, size_t workspace_bytes, int dtype,
                          void* stream);
 
+/* ---- failure detection ------------------------------------------------------------------- */
+/* Self-test of the bounded-wait protocol of the tcgen05 / TMA kernels (no reference counterpart:
+ * the reference has no device code). One CTA issues a TMA load of the 64 x 64 bf16 tile at
+ * tile64x64 (16-byte aligned, row pitch 64), then waits limit_ns (at most 0.1 s) on an mbarrier
+ * that nothing arrives on; the wait runs out and sets ORTHRUS_ERR_TIMEOUT in the device error word,
+ * the kernel drains its copy, frees its TMEM and returns. *status (device, zeroed by the caller)
+ * receives bit 1 = timed out, 2 = copy drained, 4 = TMEM freed. The context stays usable. */
+int orthrus_selftest_bounded_wait(const void* tile64x64, uint64_t limit_ns, unsigned int* status,
+                                  void* stream);
+
 /* ---- dual-view attention --------------------------------------------------------------- */
 /* Per-anchor tile map of the dual-view mask (K3): for every 128-query tile of each row,
  * tilemap[b, tile] = {source-1 key tiles to visit, source-1 keys visible to the tile (largest

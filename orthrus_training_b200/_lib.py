@@ -24,6 +24,7 @@ _SIGNATURES = {
     "orthrus_version": (c_int, []),
     "orthrus_launch_count": (ctypes.c_ulonglong, []),
     "orthrus_device_error": (c_int, [c_int, ctypes.POINTER(c_uint), c_int]),
+    "orthrus_selftest_bounded_wait": (c_int, [_P, ctypes.c_uint64, _P, _P]),
     "orthrus_gemm_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
     "orthrus_gemm_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int64, c_int64, c_int64,
                                   c_int, c_int, _P, c_size_t, _P]),

@@ -15,6 +15,7 @@
 #include "lmhead_kl.cuh"
 #include "qkv_prep.cuh"
 #include "rowwise.cuh"
+#include "selftest.cuh"
 
 using namespace orthrus;
 
@@ -41,6 +42,15 @@ int orthrus_device_error(int device, unsigned int* word, int clear) {
   ORTHRUS_CHECK_CUDA(cudaSetDevice(prev));
   *word = w;
   return w ? ORTHRUS_EDEVICE : ORTHRUS_OK;
+}
+
+int orthrus_selftest_bounded_wait(const void* tile64x64, uint64_t limit_ns, unsigned int* status, void* stream) {
+  ORTHRUS_CHECK_ARG(tile64x64 && status && aligned16(tile64x64) && limit_ns > 0 && limit_ns <= 100000000ull);
+  CUtensorMap tm;
+  if (!make_tmap_2d_bf16(&tm, tile64x64, 64, 64, 64, 64, 64)) return ORTHRUS_ECUDA;
+  bounded_wait_selftest_kernel<<<1, 64, 0, as_stream(stream)>>>(tm, limit_ns, status);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
 }
 
 size_t orthrus_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) { return gemm_ws_bytes(M, N, K); }

@@ -81,19 +81,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Slow path of mbar_wait, out of line so that the hot loops carry no call unless the first
-// try_wait (which itself suspends the thread for a while) came back empty.
-__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity) {
+// Waits for the phase with the given parity for at most limit_ns of wall time; on timeout records
+// ORTHRUS_ERR_TIMEOUT in the device error word and returns false.
+__device__ __noinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   const uint64_t t0 = global_timer_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       record_error(ORTHRUS_ERR_TIMEOUT);
       return false;
     }
   }
+}
+
+// Slow path of mbar_wait, out of line so that the hot loops carry no call unless the first
+// try_wait (which itself suspends the thread for a while) came back empty.
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity) {
+  return mbar_wait_limit(bar, parity, kWaitLimitNs);
 }
 
 // Waits for the phase with the given parity to complete; false after kWaitLimitNs (error recorded).

@@ -2,6 +2,22 @@
 base, tail and reuse strategies with tree verification, plain greedy, replay from a draft table,
 draft_table) plus a batched, device-resident decode loop for the base strategy.
 
+Decoding with a strategy is a small state machine (``_Decoder``) over a backend that offers four
+calls, the protocol of orthrus/decoding.py:145-333:
+
+    prefill()                                  -> first generated token (the first anchor)
+    draft(start, anchor, block_len, confidence) -> Hypothesis of the block's drafts
+    verify(kind, start, root, hypotheses)       -> per hypothesis, the AR argmax after the root
+                                                   and after each of its tokens
+    commit(best, accepted)                      -> keep the root and `accepted` tokens of one
+
+``ModelBackend`` runs an OrthrusLM on the device (several hypotheses share one pass through the
+TREE mask of the attention kernels); ``OracleBackend`` replays a strategy without the model from
+a reference output and a draft table. The bookkeeping rules are fixed by the reference's traces
+(kept pass for pass): the hypothesis with the most accepted tokens wins and the first listed wins
+ties, acceptance stops after an accepted EOS, the AR token after the accepted run (the bonus) is
+always kept, and a tail pass happens only while the strategy's gate allows it.
+
 ``block_decode`` keeps every piece of the cycle state on the GPU: per-sequence committed cache
 length (``start``), anchor token, done flag, output buffer, accepted counts. One cycle is
 
@@ -22,8 +38,12 @@ computes there, and the output equals plain greedy decoding token for token.
 from __future__ import annotations
 
 import dataclasses
+import functools
+import itertools
+import operator
 import time
 from collections import Counter
+from contextlib import contextmanager
 from dataclasses import dataclass, field
 
 import torch
@@ -34,10 +54,23 @@ from orthrus_training_b200.kv_cache import KVCache
 KINDS = ("base", "tail", "reuse")
 
 
+# --- strategies and hypotheses -----------------------------------------------------------------
+
+
 @dataclass(frozen=True)
 class Strategy:
-    """A decoding strategy (orthrus/decoding.py:41-70): base, tail (extra tree-verified passes over
-    the rejected tail) or reuse (the rejected tail rides along in the next verification)."""
+    """One decoding strategy, configured by the reference's fields (orthrus/decoding.py:41-70):
+
+    kind               base: draft then verify; tail: after a rejection, verify the rest of the
+                       block behind the bonus in extra passes; reuse: carry that rest into the
+                       next block's verification instead
+    shifts             the tail hypotheses, in tie-breaking order (0 substitution, 1 insertion,
+                       -j deletion of j drafts)
+    min_tail           a tail pass needs a hypothesis of at least this many tokens
+    min_expected       ... and, when > 0, an expected kept-token count of at least this
+    max_tail_passes    tail passes per cycle
+    oracle_min_tokens  replay only: a tail pass only when it would keep at least this many tokens
+    """
 
     name: str
     kind: str = "base"
@@ -48,37 +81,52 @@ class Strategy:
     oracle_min_tokens: int = 0
 
     def __post_init__(self):
-        shifts = tuple(int(s) for s in self.shifts)
-        object.__setattr__(self, "shifts", shifts)
+        object.__setattr__(self, "shifts", tuple(int(s) for s in self.shifts))
+        problem = next(self._problems(), None)
+        if problem is not None:
+            raise ValueError(f"decoding strategy {self.name!r}: {problem}")
+
+    def _problems(self):
         if self.kind not in KINDS:
-            raise ValueError(f"strategy {self.name}: kind must be one of {KINDS}")
-        if not shifts or len(set(shifts)) != len(shifts) or max(shifts) > 1:
-            raise ValueError(f"strategy {self.name}: shifts must be distinct and <= 1")
-        if self.min_tail < 1 or self.max_tail_passes < 1:
-            raise ValueError(f"strategy {self.name}: min_tail and max_tail_passes must be >= 1")
+            yield f"kind {self.kind!r} is not one of {', '.join(KINDS)}"
+        if not self.shifts:
+            yield "at least one tail shift is needed"
+        elif len(set(self.shifts)) < len(self.shifts):
+            yield f"tail shifts repeat: {self.shifts}"
+        elif max(self.shifts) > 1:
+            yield f"a tail shift above 1 has no meaning: {self.shifts}"
+        if self.min_tail < 1:
+            yield f"min_tail is {self.min_tail}, it must be at least 1"
+        if self.max_tail_passes < 1:
+            yield f"max_tail_passes is {self.max_tail_passes}, it must be at least 1"
         if self.oracle_min_tokens and self.kind != "tail":
-            raise ValueError(f"strategy {self.name}: oracle_min_tokens needs kind tail")
+            yield "oracle_min_tokens gates tail passes, so the kind must be 'tail'"
 
     @property
     def needs_confidence(self) -> bool:
+        """Whether drafts must carry their probabilities (the min_expected gate of a tail pass)."""
         return self.kind == "tail" and self.min_expected > 0
 
     def to_dict(self) -> dict:
-        return {**dataclasses.asdict(self), "shifts": list(self.shifts)}
+        out = dataclasses.asdict(self)
+        out["shifts"] = list(self.shifts)
+        return out
 
 
 def parse_strategies(specs: list[dict]) -> list[Strategy]:
+    """Strategies from their field dicts; names must be distinct."""
     strategies = [Strategy(**spec) for spec in specs]
-    names = [s.name for s in strategies]
-    if len(set(names)) != len(names):
-        raise ValueError(f"strategy names must be unique: {names}")
+    repeated = sorted(n for n, c in Counter(s.name for s in strategies).items() if c > 1)
+    if repeated:
+        raise ValueError(f"strategy names must be distinct; repeated: {repeated}")
     return strategies
 
 
 @dataclass
 class Hypothesis:
-    """A continuation to verify (orthrus/decoding.py:82-86): shift None for the fresh drafts of a
-    block, else the tail shift it was cut with; confidence = diffusion probability of each token."""
+    """A continuation to verify (orthrus/decoding.py:82-86): shift None for a block's fresh
+    drafts, else the tail shift it was cut with; confidence: the diffusion probability of each
+    token, when the strategy needs it."""
 
     shift: int | None
     tokens: list[int]
@@ -87,38 +135,35 @@ class Hypothesis:
 
 def tail_hypotheses(source: Hypothesis, accepted: int, shifts: tuple[int, ...],
                     room: int) -> list[Hypothesis]:
-    """Tails after a rejection (orthrus/decoding.py:89-107). source.tokens[accepted] lost to the
-    AR token (the bonus); the shift-s continuation of the bonus is source.tokens[accepted + 1 - s:]
-    (s = 0 substitution, 1 insertion, -j deletion of j spurious drafts), at most `room` tokens.
-    Empty continuations and repeats of an earlier shift's tokens are left out; order is kept."""
-    out: list[Hypothesis] = []
-    seen: set[tuple[int, ...]] = set()
+    """Continuations of the bonus after source.tokens[accepted] lost to it (orthrus/decoding.py:
+    89-107): for shift s the tokens from index accepted + 1 - s on, at most `room` of them.
+    An empty continuation, or one equal to an earlier shift's, is not a hypothesis."""
+    kept: dict[tuple[int, ...], Hypothesis] = {}
     for shift in shifts:
-        begin = accepted + 1 - shift
-        tokens = list(source.tokens[begin: begin + room])
-        if not tokens or tuple(tokens) in seen:
-            continue
-        seen.add(tuple(tokens))
-        conf = None if source.confidence is None else list(source.confidence[begin: begin + room])
-        out.append(Hypothesis(shift, tokens, conf))
-    return out
+        cut = slice(accepted + 1 - shift, accepted + 1 - shift + room)
+        tokens = tuple(source.tokens[cut])
+        if tokens and tokens not in kept:
+            conf = None if source.confidence is None else list(source.confidence[cut])
+            kept[tokens] = Hypothesis(shift, list(tokens), conf)
+    return list(kept.values())
 
 
 def expected_tokens(hypothesis: Hypothesis) -> float:
-    """1 + sum_j prod_{i <= j} confidence_i: the tokens a verification of the hypothesis keeps in
-    expectation, the confidences taken as independent acceptance probabilities
-    (orthrus/decoding.py:110-116)."""
-    total = prefix = 1.0
-    for p in hypothesis.confidence or ():
-        prefix *= p
-        total += prefix
-    return total
+    """Tokens a verification of the hypothesis keeps in expectation when each confidence is an
+    independent acceptance probability: 1 (the bonus) + the sum of the running products
+    (orthrus/decoding.py:110-116). Summed left to right from 1, the order the gate's threshold
+    comparison was pinned with."""
+    running = itertools.accumulate(hypothesis.confidence or (), operator.mul)
+    return functools.reduce(operator.add, running, 1.0)
 
 
 @dataclass
 class Generation:
-    """One decoded output with its pass accounting (orthrus/decoding.py:119-142). tails holds per
-    tail pass (cycle, shift of the kept hypothesis, accepted, hypotheses, longest hypothesis)."""
+    """One decoded output and its pass accounting, with the reference's fields
+    (orthrus/decoding.py:119-142): accepted and branch per cycle (branch: None for the fresh
+    drafts, else the shift of a reused tail), tails per tail pass (cycle, shift of the kept
+    hypothesis, accepted, number of hypotheses, longest hypothesis), and per pass kind the
+    passes, input tokens and host-synchronised seconds."""
 
     strategy: str
     tokens: list[int] = field(default_factory=list)
@@ -139,14 +184,49 @@ class Generation:
         return len(self.tokens) / max(self.forward_passes, 1)
 
 
-class ModelBackend:
-    """Forward passes of an OrthrusLM, batch 1, greedy, with per-kind pass / token / time counts
-    (orthrus/decoding.py:145-264). The AR cache holds the committed prefix; the anchor is not in
-    it yet. Several hypotheses are verified in one pass with the tree mask of the attention
-    kernels (orthrus_attn_fwd mask TREE); commit() moves the kept branch's cache rows behind the
-    root and drops the rest."""
+# --- backends ------------------------------------------------------------------------------------
+
+
+class _PassLedger:
+    """Per-kind pass, input-token and time counts shared by the backends."""
+
+    def __init__(self):
+        self.passes, self.input_tokens, self.seconds = Counter(), Counter(), Counter()
+
+    def _count(self, kind: str, tokens: int) -> None:
+        self.passes[kind] += 1
+        self.input_tokens[kind] += tokens
+
+    @contextmanager
+    def _pass(self, kind: str, tokens: int):
+        began = time.perf_counter()
+        yield
+        self.seconds[kind] += time.perf_counter() - began
+        self._count(kind, tokens)
+
+
+def _tree_layout(hypotheses: list[Hypothesis]):
+    """Verification input of a root plus hypotheses: the new tokens after the root, each token's
+    depth below the root, where each hypothesis begins among the new tokens (the root is 0), and,
+    for more than one hypothesis, each token's branch start (the tree mask's int32 form)."""
+    starts = list(itertools.accumulate((len(h.tokens) for h in hypotheses[:-1]), initial=1))
+    tokens, depth, branch_lo = [], [0], [1]
+    for begin, h in zip(starts, hypotheses):
+        tokens += h.tokens
+        depth += range(1, len(h.tokens) + 1)
+        branch_lo += [begin] * len(h.tokens)
+    return tokens, depth, starts, (branch_lo if len(hypotheses) > 1 else None)
+
+
+class ModelBackend(_PassLedger):
+    """An OrthrusLM decoding one prompt greedily on the device, the backend of
+    orthrus/decoding.py:145-264. The cache holds the committed prefix; the newest token (the
+    anchor) enters it only with the next verification. Hypotheses verified together share one
+    pass under the TREE mask of the attention kernels; commit() moves the kept branch's K/V rows
+    behind the root when it was not the first branch."""
 
     def __init__(self, model, prompt_ids: list[int], record_drafts: bool = False):
+        super().__init__()
         self.model = model
         self.device = next(model.parameters()).device
         self.block_size = model.config.block_size
@@ -155,196 +235,242 @@ class ModelBackend:
         dtype = next(model.parameters()).dtype
         self.cache = KVCache(model.config, batch=1, capacity=len(prompt_ids) + 64,
                              device=self.device, dtype=dtype)
-        self.passes, self.input_tokens, self.seconds = Counter(), Counter(), Counter()
         self.record_drafts = record_drafts
         self.drafts: dict[int, list[int]] = {}
-        self._layout: tuple[int, list[int]] | None = None
+        self._last: tuple[int, list[int]] | None = None  # (root position, hypothesis starts)
 
     def _timed(self, kind: str, tokens: int, run):
-        begin = time.perf_counter()
-        result = run()  # ends in a host read of the argmax, which synchronises the device
-        self.seconds[kind] += time.perf_counter() - begin
-        self.passes[kind] += 1
-        self.input_tokens[kind] += tokens
-        return result
+        """Runs `run` as one counted, timed pass of `kind` (the hook a scripted subclass such as
+        the reference tests' ScriptedBackend calls)."""
+        with self._pass(kind, tokens):
+            return run()
+
+    def _argmax(self, logits: torch.Tensor) -> torch.Tensor:
+        return ops.argmax_rows(logits.reshape(-1, logits.shape[-1]).contiguous())
 
     def prefill(self) -> int:
-        def run():
+        with self._pass("prefill", self.prompt.shape[1]):
             out = self.model(input_ids=self.prompt, past_key_values=self.cache, use_cache=True,
                              logits_to_keep=1)
-            return int(ops.argmax_rows(out.logits[0]).item())
-
-        return self._timed("prefill", self.prompt.shape[1], run)
+            return int(self._argmax(out.logits[0]).item())  # the host read ends the timed pass
 
     def draft(self, start: int, anchor: int, block_len: int, confidence: bool) -> Hypothesis:
-        def run():
-            block = torch.full((1, block_len), self.mask_token_id, dtype=torch.long,
-                               device=self.device)
-            block[0, 0] = anchor
-            positions = torch.arange(start, start + block_len, device=self.device)[None]
-            logits = self.model(input_ids=block, position_ids=positions, past_key_values=self.cache,
+        """The diffusion view over [anchor, mask x (block_len - 1)] at positions start.. : the
+        drafts for positions start + 1 .. start + block_len - 1."""
+        with self._pass("draft", block_len):
+            ids = torch.full((1, block_len), self.mask_token_id, dtype=torch.long, device=self.device)
+            ids[0, 0] = anchor
+            pos = torch.arange(start, start + block_len, device=self.device)[None]
+            logits = self.model(input_ids=ids, position_ids=pos, past_key_values=self.cache,
                                 use_cache=False, is_diffusion_pass=True, ar_seq_len=start).logits[0, :-1]
-            tokens = ops.argmax_rows(logits.contiguous())
+            best = self._argmax(logits)
             probs = None
             if confidence:
-                probs = torch.softmax(logits.float(), -1).gather(-1, tokens[:, None])[:, 0].tolist()
-            return Hypothesis(None, tokens.tolist(), probs)
-
-        drafts = self._timed("draft", block_len, run)
+                probs = torch.softmax(logits.float(), -1).gather(-1, best[:, None])[:, 0].tolist()
+            hyp = Hypothesis(None, best.tolist(), probs)
         if self.record_drafts:
-            self.drafts[start] = drafts.tokens
-        return drafts
+            self.drafts[start] = hyp.tokens
+        return hyp
 
     def verify(self, kind: str, start: int, root: int, hypotheses: list[Hypothesis]) -> list:
-        """AR pass over the root (position `start`) and every hypothesis after it, all written to
-        the cache at rows start + index; one hypothesis is a causal chain, several a tree (each
-        token sees the prefix, the root and its own branch up to itself, at position start +
-        depth). Returns per hypothesis the AR argmax after the root and after each of its tokens
-        (orthrus/decoding.py:208-241)."""
-        branches = [list(h.tokens) for h in hypotheses]
-        tokens = [root] + [t for b in branches for t in b]
-        depth = [0] + [i + 1 for b in branches for i in range(len(b))]
-        begins, at = [], 1
-        for b in branches:
-            begins.append(at)
-            at += len(b)
-        lo = [1] + [begin for begin, b in zip(begins, branches) for _ in b] if len(branches) > 1 else None
-
-        def run():
-            ids = torch.tensor([tokens], device=self.device)
-            positions = torch.tensor([[start + d for d in depth]], device=self.device)
-            tree_lo = None if lo is None else torch.tensor(lo, dtype=torch.int32, device=self.device)
-            self.cache.reserve(start + len(tokens))
-            logits = self.model(input_ids=ids, position_ids=positions, past_key_values=self.cache,
+        """One AR pass over the root (position `start`) and every hypothesis behind it, all written
+        to the cache at rows start + their index; each token sits at position start + its depth
+        and sees the prefix, the root and its own branch up to itself. Returns per hypothesis the
+        AR argmax after the root and after each of its tokens (orthrus/decoding.py:208-241)."""
+        new, depth, starts, branch_lo = _tree_layout(hypotheses)
+        with self._pass(kind, 1 + len(new)):
+            ids = torch.tensor([[root] + new], device=self.device)
+            pos = torch.tensor([depth], device=self.device) + start
+            tree_lo = None if branch_lo is None else torch.tensor(branch_lo, dtype=torch.int32,
+                                                                  device=self.device)
+            self.cache.reserve(start + ids.shape[1])
+            logits = self.model(input_ids=ids, position_ids=pos, past_key_values=self.cache,
                                 use_cache=True, tree_lo=tree_lo).logits[0]
-            return ops.argmax_rows(logits.contiguous()).tolist()
-
-        preds = self._timed(kind, len(tokens), run)
-        self._layout = (start, begins)
-        return [[preds[0]] + preds[begin: begin + len(b)] for begin, b in zip(begins, branches)]
+            preds = self._argmax(logits).tolist()
+        self._last = (start, starts)
+        return [[preds[0]] + preds[b: b + len(h.tokens)] for b, h in zip(starts, hypotheses)]
 
     def commit(self, best: int, accepted: int) -> None:
-        """Keep the prefix, the root and the first `accepted` tokens of hypothesis `best` of the
-        last verification (orthrus/decoding.py:243-264): a length update when that hypothesis
-        followed the root, else its K/V rows are first copied behind the root in every layer."""
-        start, begins = self._layout
-        src = start + begins[best]
-        if src != start + 1 and accepted > 0:
-            dst = slice(start + 1, start + 1 + accepted)
+        """Keeps the prefix, the root and the first `accepted` tokens of hypothesis `best` of the
+        last verification (orthrus/decoding.py:243-264)."""
+        root_at, starts = self._last
+        kept_from = root_at + starts[best]
+        if accepted and kept_from != root_at + 1:  # not directly behind the root: move its rows
+            dst = slice(root_at + 1, root_at + 1 + accepted)
+            src = slice(kept_from, kept_from + accepted)
             for k, v in self.cache.buffers():
-                k[:, :, dst] = k[:, :, src: src + accepted].clone()
-                v[:, :, dst] = v[:, :, src: src + accepted].clone()
-        self.cache.crop(start + 1 + accepted)
+                k[:, :, dst] = k[:, :, src].clone()
+                v[:, :, dst] = v[:, :, src].clone()
+        self.cache.crop(root_at + 1 + accepted)
 
 
-class OracleBackend:
-    """Greedy decoding replayed without a model (orthrus/decoding.py:267-333): AR predictions come
-    from the reference output, drafts from a draft table (row i: the drafts of the block anchored
-    at reference[i]). Exact when real decoding produced the reference with these drafts."""
+class OracleBackend(_PassLedger):
+    """Greedy decoding replayed without a model (orthrus/decoding.py:267-333): the AR argmax at
+    every position is the reference output's next token, and drafts come from a draft table
+    (row i: the drafts of the block anchored at reference[i]). A replay is exact when real
+    decoding produced that output and drew those drafts."""
 
     def __init__(self, prompt_len: int, reference: list[int], drafts: list[list[int]],
                  confidence: list[list[float]] | None, block_size: int):
-        self.prompt_len, self.reference, self.block_size = prompt_len, list(reference), block_size
+        super().__init__()
+        self.prompt_len, self.block_size = prompt_len, block_size
+        self.reference = list(reference)
         self.drafts, self.confidence = drafts, confidence
-        self.passes, self.input_tokens, self.seconds = Counter(), Counter(), Counter()
 
-    def _count(self, kind: str, tokens: int) -> None:
-        self.passes[kind] += 1
-        self.input_tokens[kind] += tokens
+    def _row(self, position: int, token: int) -> int:
+        """Index of `position` in the reference output, checking that it holds `token`."""
+        row = position - self.prompt_len
+        if row < 0 or row >= len(self.reference) or self.reference[row] != token:
+            raise RuntimeError(f"the replay no longer follows the reference output (position {position})")
+        return row
 
-    def _index(self, start: int, token: int) -> int:
-        i = start - self.prompt_len
-        if not 0 <= i < len(self.reference) or self.reference[i] != token:
-            raise RuntimeError(f"replay left the reference output at position {start}")
-        return i
+    def _after(self, row: int, n: int) -> list[int]:
+        """The reference tokens after row, n + 1 of them, -1 (never accepted) past its end."""
+        tail = self.reference[row + 1: row + 2 + n]
+        return tail + [-1] * (n + 1 - len(tail))
 
     def prefill(self) -> int:
         self._count("prefill", self.prompt_len)
         return self.reference[0]
 
     def draft(self, start: int, anchor: int, block_len: int, confidence: bool) -> Hypothesis:
-        i = self._index(start, anchor)
-        tokens = list(self.drafts[i][: block_len - 1])
-        if len(tokens) != block_len - 1 or min(tokens, default=0) < 0:
-            raise RuntimeError(f"draft table has no block of {block_len} at position {start}")
-        probs = list(self.confidence[i][: block_len - 1]) if confidence else None
+        row = self._row(start, anchor)
+        tokens = list(self.drafts[row][: block_len - 1])
+        if len(tokens) < block_len - 1 or any(t < 0 for t in tokens):
+            raise RuntimeError(f"the draft table holds no full block of {block_len} at position {start}")
+        probs = list(self.confidence[row][: block_len - 1]) if confidence else None
         self._count("draft", block_len)
         return Hypothesis(None, tokens, probs)
 
     def verify(self, kind: str, start: int, root: int, hypotheses: list[Hypothesis]) -> list:
-        i = self._index(start, root)
+        row = self._row(start, root)
         self._count(kind, 1 + sum(len(h.tokens) for h in hypotheses))
-        ref = self.reference
-        # the prediction after depth d is the reference token there; past the end: never accepted
-        return [[ref[i + 1 + d] if i + 1 + d < len(ref) else -1 for d in range(len(h.tokens) + 1)]
-                for h in hypotheses]
+        return [self._after(row, len(h.tokens)) for h in hypotheses]
 
     def commit(self, best: int, accepted: int) -> None:
         pass
 
     def peek(self, start: int, hypotheses: list[Hypothesis]) -> int:
-        """Tokens a verification at `start` would keep (most accepted + 1), without a pass."""
-        i = start - self.prompt_len
-        most = 0
-        for h in hypotheses:
-            n = 0
-            while (n < len(h.tokens) and i + 1 + n < len(self.reference)
-                   and h.tokens[n] == self.reference[i + 1 + n]):
-                n += 1
-            most = max(most, n)
-        return most + 1
+        """Tokens a verification at `start` would keep (the longest accepted run + the bonus),
+        without counting a pass."""
+        row = start - self.prompt_len
+        truth = self.reference[row + 1:]
+        runs = (sum(1 for _ in itertools.takewhile(lambda pair: pair[0] == pair[1], zip(h.tokens, truth)))
+                for h in hypotheses)
+        return max(runs, default=0) + 1
 
 
-def _verify(backend, kind, start, root, hypotheses, eos):
-    """Verify and keep the hypothesis with the most accepted tokens, the first on ties; acceptance
-    ends after an accepted EOS (orthrus/decoding.py:336-351). Returns (index, accepted, bonus)."""
-    preds = backend.verify(kind, start, root, hypotheses)
-    best, best_accepted = 0, -1
-    for index, (hyp, pred) in enumerate(zip(hypotheses, preds)):
-        n = 0
-        while n < len(hyp.tokens) and hyp.tokens[n] == pred[n]:
-            n += 1
-            if hyp.tokens[n - 1] in eos:
-                break
-        if n > best_accepted:
-            best, best_accepted = index, n
-    backend.commit(best, best_accepted)
-    return best, best_accepted, preds[best][best_accepted]
+# --- the decoding state machine ------------------------------------------------------------------
 
 
-def _advance(gen, start, kept, bonus, eos, max_length):
-    """Append the accepted tokens and the AR bonus (orthrus/decoding.py:354-369); returns
-    (finished, position of the new anchor)."""
-    for i, token in enumerate(kept):
+def _accepted_run(tokens: list[int], preds: list[int], eos: set[int]) -> int:
+    """Leading tokens equal to the AR argmax before them, ending after an accepted EOS."""
+    n = 0
+    for token, pred in zip(tokens, preds):
+        if token != pred:
+            break
+        n += 1
         if token in eos:
-            gen.tokens.extend(kept[: i + 1])
-            gen.eos = True
-            return True, start + i + 1
-    gen.tokens.extend(kept)
-    start += len(kept) + 1
-    if start < max_length:
-        gen.tokens.append(bonus)
-        if bonus in eos:
-            gen.eos = True
-            return True, start
-    return start >= max_length - 1, start
+            break
+    return n
 
 
-def _worth_a_pass(strategy: Strategy, hypotheses: list[Hypothesis], backend, start: int) -> bool:
-    """The tail-pass gate (orthrus/decoding.py:372-381): a long enough hypothesis, enough expected
-    tokens when min_expected is set, and for replay-only strategies enough tokens kept."""
+def _gate_open(strategy: Strategy, hypotheses: list[Hypothesis], backend, start: int) -> bool:
+    """Whether a tail pass over `hypotheses` is worth it (orthrus/decoding.py:372-381): a long
+    enough hypothesis, enough expected tokens when min_expected is set, and for a replay-only
+    strategy enough tokens actually kept."""
     if not hypotheses or max(len(h.tokens) for h in hypotheses) < strategy.min_tail:
         return False
-    if strategy.min_expected > 0 and max(map(expected_tokens, hypotheses)) < strategy.min_expected:
+    if strategy.min_expected > 0 and max(expected_tokens(h) for h in hypotheses) < strategy.min_expected:
         return False
     if strategy.oracle_min_tokens:
-        if not hasattr(backend, "peek"):
-            raise ValueError(f"strategy {strategy.name} (oracle_min_tokens) is replay-only")
-        return backend.peek(start, hypotheses) >= strategy.oracle_min_tokens
+        peek = getattr(backend, "peek", None)
+        if peek is None:
+            raise ValueError(f"strategy {strategy.name!r} gates on oracle_min_tokens, which only a "
+                             f"replay backend (one with peek) can evaluate")
+        return peek(start, hypotheses) >= strategy.oracle_min_tokens
     return True
 
 
-def _finish(gen, backend):
+class _Decoder:
+    """One greedy Orthrus generation (orthrus/decoding.py:391-429) as a state machine over a
+    backend: `anchor_at` is the position of the newest token (the anchor, not in the cache yet),
+    `limit` the first position past the output, `pending` the previous block's rejected tails
+    that a reuse strategy verifies again."""
+
+    def __init__(self, backend, strategy: Strategy, prompt_len: int, max_new_tokens: int, eos):
+        self.backend, self.strategy, self.eos = backend, strategy, eos
+        self.limit = prompt_len + max_new_tokens
+        self.anchor_at = prompt_len
+        self.gen = Generation(strategy.name)
+        self.finished = False
+        self.pending: list[Hypothesis] = []
+
+    def run(self) -> Generation:
+        first = self.backend.prefill()
+        self.gen.tokens.append(first)
+        self.finished = self.gen.eos = first in self.eos
+        while not self.finished and self.anchor_at < self.limit - 1:
+            self._cycle()
+        return _with_accounting(self.gen, self.backend)
+
+    def _select(self, kind: str, hypotheses: list[Hypothesis]) -> tuple[Hypothesis, int]:
+        """Verifies the hypotheses behind the current anchor, keeps the one with the longest
+        accepted run (the first listed on ties), appends its run and the bonus."""
+        preds = self.backend.verify(kind, self.anchor_at, self.gen.tokens[-1], hypotheses)
+        runs = [_accepted_run(h.tokens, p, self.eos) for h, p in zip(hypotheses, preds)]
+        best = max(range(len(runs)), key=runs.__getitem__)  # max() keeps the first maximum
+        self.backend.commit(best, runs[best])
+        self._extend(hypotheses[best].tokens[: runs[best]], preds[best][runs[best]])
+        return hypotheses[best], runs[best]
+
+    def _extend(self, run: list[int], bonus: int) -> None:
+        """Appends an accepted run and the AR bonus behind it (orthrus/decoding.py:354-369): the
+        output ends at an EOS in the run, at an EOS bonus, or when the next anchor would leave no
+        room for a block."""
+        gen = self.gen
+        for i, token in enumerate(run):
+            if token in self.eos:
+                gen.tokens += run[: i + 1]
+                gen.eos = self.finished = True
+                self.anchor_at += i + 1
+                return
+        gen.tokens += run
+        self.anchor_at += len(run) + 1
+        if self.anchor_at < self.limit:
+            gen.tokens.append(bonus)
+            if bonus in self.eos:
+                gen.eos = self.finished = True
+                return
+        self.finished = self.anchor_at >= self.limit - 1
+
+    def _cycle(self) -> None:
+        strategy, backend = self.strategy, self.backend
+        block_len = min(backend.block_size, self.limit - self.anchor_at)
+        fresh = backend.draft(self.anchor_at, self.gen.tokens[-1], block_len, strategy.needs_confidence)
+        candidates = [fresh, *(h for h in self.pending if h.tokens != fresh.tokens)]
+        kept, accepted = self._select("verify", candidates)
+        self.gen.accepted.append(accepted)
+        self.gen.branch.append(kept.shift)
+        self.pending = []
+        if strategy.kind == "base":
+            return
+        tail_passes = 0
+        while not self.finished and accepted < len(kept.tokens):
+            tails = tail_hypotheses(kept, accepted, strategy.shifts, self.limit - 1 - self.anchor_at)
+            if strategy.kind == "reuse":
+                self.pending = tails
+                return
+            if tail_passes >= strategy.max_tail_passes or not _gate_open(strategy, tails, backend,
+                                                                          self.anchor_at):
+                return
+            tail_passes += 1
+            kept, accepted = self._select("tail", tails)
+            self.gen.tails.append((len(self.gen.accepted) - 1, kept.shift, accepted, len(tails),
+                                   max(len(h.tokens) for h in tails)))
+
+
+def _with_accounting(gen: Generation, backend) -> Generation:
     gen.passes = dict(backend.passes)
     gen.input_tokens = dict(backend.input_tokens)
     gen.seconds = dict(backend.seconds)
@@ -353,103 +479,72 @@ def _finish(gen, backend):
 
 def decode(backend, strategy: Strategy, prompt_len: int, max_new_tokens: int, eos: set[int]) -> Generation:
     """Greedy Orthrus decoding with `strategy` on a ModelBackend or OracleBackend
-    (orthrus/decoding.py:391-429). Each cycle drafts a block and verifies it together with the
-    stale tails (reuse); a rejection then yields tail hypotheses that a tail strategy verifies in
-    up to max_tail_passes extra passes, or that reuse carries into the next verification."""
-    gen = Generation(strategy.name)
-    max_length = prompt_len + max_new_tokens
-    gen.tokens.append(backend.prefill())
-    gen.eos = done = gen.tokens[-1] in eos
-    start = prompt_len  # position of the anchor gen.tokens[-1], not in the cache yet
-    stale: list[Hypothesis] = []
-    while not done and start < max_length - 1:
-        block_len = min(backend.block_size, max_length - start)
-        root = gen.tokens[-1]
-        fresh = backend.draft(start, root, block_len, strategy.needs_confidence)
-        hypotheses = [fresh] + [h for h in stale if h.tokens != fresh.tokens]
-        best, accepted, bonus = _verify(backend, "verify", start, root, hypotheses, eos)
-        kept = hypotheses[best]
-        gen.accepted.append(accepted)
-        gen.branch.append(kept.shift)
-        done, start = _advance(gen, start, kept.tokens[:accepted], bonus, eos, max_length)
-        stale, tail_passes = [], 0
-        while strategy.kind != "base" and not done and accepted < len(kept.tokens):
-            tails = tail_hypotheses(kept, accepted, strategy.shifts, max_length - 1 - start)
-            if strategy.kind == "reuse":
-                stale = tails
-                break
-            if tail_passes == strategy.max_tail_passes or not _worth_a_pass(strategy, tails, backend, start):
-                break
-            tail_passes += 1
-            best, accepted, bonus = _verify(backend, "tail", start, gen.tokens[-1], tails, eos)
-            kept = tails[best]
-            gen.tails.append((len(gen.accepted) - 1, kept.shift, accepted, len(tails),
-                              max(len(h.tokens) for h in tails)))
-            done, start = _advance(gen, start, kept.tokens[:accepted], bonus, eos, max_length)
-    return _finish(gen, backend)
+    (orthrus/decoding.py:391-429)."""
+    return _Decoder(backend, strategy, prompt_len, max_new_tokens, set(eos)).run()
 
 
 def ar_decode(backend, prompt_len: int, max_new_tokens: int, eos: set[int]) -> Generation:
-    """Plain greedy AR decoding through the same backend, one pass per token (orthrus/decoding.py:432-444)."""
+    """Plain greedy decoding through the same backend, one verification of the newest token per
+    generated token (orthrus/decoding.py:432-444): the reference for losslessness."""
     gen = Generation("ar")
-    gen.tokens.append(backend.prefill())
-    start = prompt_len
-    while gen.tokens[-1] not in eos and len(gen.tokens) < max_new_tokens:
-        (pred,) = backend.verify("ar", start, gen.tokens[-1], [Hypothesis(None, [])])
+    position, token = prompt_len, backend.prefill()
+    gen.tokens.append(token)
+    while token not in eos and len(gen.tokens) < max_new_tokens:
+        token = backend.verify("ar", position, token, [Hypothesis(None, [])])[0][0]
         backend.commit(0, 0)
-        gen.tokens.append(pred[0])
-        start += 1
-    gen.eos = gen.tokens[-1] in eos
-    return _finish(gen, backend)
+        gen.tokens.append(token)
+        position += 1
+    gen.eos = token in eos
+    return _with_accounting(gen, backend)
 
 
 @torch.inference_mode()
 def draft_table(model, prompt_ids: list[int], reference: list[int], max_new_tokens: int,
                 chunk_blocks: int = 64):
-    """Diffusion drafts at every anchor of a reference output, as decoding draws them after
-    committing reference[: i + 1] (orthrus/decoding.py:447-503): row i holds the block_size - 1
-    drafts of the block anchored at reference[i] (fewer where max_new_tokens cuts the block).
+    """The diffusion drafts decoding would draw at every anchor of a reference output, each
+    after committing reference[: i + 1] (orthrus/decoding.py:447-503): row i holds the
+    block_size - 1 drafts of the block anchored at reference[i] (fewer where max_new_tokens cuts
+    the block). Returns numpy (drafts int32, confidence float32), [len(reference), block_size - 1],
+    padded with -1 and 0.
 
-    One AR pass caches the whole output; full blocks then go chunk_blocks at a time through one
-    diffusion pass with the dual-view training mask (orthrus_attn_fwd mask DUAL: AR keys before
-    the anchor, the block's own keys), short blocks one by one. Returns numpy (drafts int32,
-    confidence float32), both [len(reference), block_size - 1], padded with -1 and 0."""
+    One AR pass caches the prompt and the whole output. The anchors are then grouped into passes:
+    full blocks chunk_blocks at a time, each pass one diffusion forward over all its blocks under
+    the dual-view mask (orthrus_attn_fwd mask DUAL: AR keys strictly before each block's anchor,
+    plus the block's own keys), and each block that max_new_tokens cuts short in a pass of its own.
+    """
     from orthrus_training_b200.modeling_orthrus import DualViewMask
 
     dev = next(model.parameters()).device
     dtype = next(model.parameters()).dtype
     K, mask_id = model.config.block_size, model.config.mask_token_id
-    P, max_length = len(prompt_ids), len(prompt_ids) + max_new_tokens
-    full = torch.tensor([list(prompt_ids) + list(reference)], device=dev)
-    total = full.shape[1]
+    P = len(prompt_ids)
+    limit = P + max_new_tokens
+    sequence = torch.tensor([list(prompt_ids) + list(reference)], device=dev)
+    total = sequence.shape[1]
     cache = KVCache(model.config, batch=1, capacity=total + 8, device=dev, dtype=dtype)
-    model(input_ids=full, past_key_values=cache, use_cache=True, logits_to_keep=1)
+    model(input_ids=sequence, past_key_values=cache, use_cache=True, logits_to_keep=1)
+
+    anchors = range(P, min(P + len(reference), limit - 1))
+    full = [a for a in anchors if a + K <= limit]
+    passes = [(full[i: i + chunk_blocks], K) for i in range(0, len(full), chunk_blocks)]
+    passes += [([a], limit - a) for a in anchors if a + K > limit]
+
     drafts = torch.full((len(reference), K - 1), -1, dtype=torch.int32)
     confidence = torch.zeros((len(reference), K - 1), dtype=torch.float32)
-
-    def run(anchors: list[int], block_len: int) -> None:
-        n = len(anchors)
-        a = torch.tensor(anchors, device=dev)
-        ids = torch.full((n, block_len), mask_id, dtype=torch.long, device=dev)
-        ids[:, 0] = full[0, a]
-        positions = (a[:, None] + torch.arange(block_len, device=dev)).view(1, -1)
-        logits = model(input_ids=ids.view(1, -1), position_ids=positions, past_key_values=cache,
-                       use_cache=False, is_diffusion_pass=True, ar_seq_len=total,
-                       flex_block_mask=DualViewMask(a[None], total, block_len)).logits[0]
-        logits = logits.view(n, block_len, -1)[:, :-1].contiguous()
-        tokens = ops.argmax_rows(logits.view(-1, logits.shape[-1])).view(n, block_len - 1)
-        probs = torch.softmax(logits.float(), -1).gather(-1, tokens[..., None])[..., 0]
-        rows = (a - P).cpu()
-        drafts[rows, : block_len - 1] = tokens.to(torch.int32).cpu()
-        confidence[rows, : block_len - 1] = probs.cpu()
-
-    starts = range(P, min(P + len(reference), max_length - 1))
-    full_blocks = [s for s in starts if s + K <= max_length]
-    for i in range(0, len(full_blocks), chunk_blocks):
-        run(full_blocks[i: i + chunk_blocks], K)
-    for s in starts:
-        if s + K > max_length:
-            run([s], max_length - s)
+    for group, width in passes:
+        at = torch.tensor(group, device=dev)
+        ids = torch.full((len(group), width), mask_id, dtype=torch.long, device=dev)
+        ids[:, 0] = sequence[0, at]
+        pos = (at[:, None] + torch.arange(width, device=dev)).reshape(1, -1)
+        out = model(input_ids=ids.reshape(1, -1), position_ids=pos, past_key_values=cache, use_cache=False,
+                    is_diffusion_pass=True, ar_seq_len=total,
+                    flex_block_mask=DualViewMask(at[None], total, width))
+        logits = out.logits[0].view(len(group), width, -1)[:, :-1].contiguous()
+        best = ops.argmax_rows(logits.view(-1, logits.shape[-1])).view(len(group), width - 1)
+        prob = torch.softmax(logits.float(), -1).gather(-1, best[..., None])[..., 0]
+        rows = (at - P).cpu()
+        drafts[rows, : width - 1] = best.to(torch.int32).cpu()
+        confidence[rows, : width - 1] = prob.cpu()
     return drafts.numpy(), confidence.numpy()
 
 

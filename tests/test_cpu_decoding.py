@@ -133,7 +133,7 @@ def test_replay_gates_and_errors():
         pass
 
     with pytest.raises(ValueError):
-        D._worth_a_pass(D.Strategy("t", kind="tail", oracle_min_tokens=2),
+        D._gate_open(D.Strategy("t", kind="tail", oracle_min_tokens=2),
                         [D.Hypothesis(0, [1, 2])], NoPeek(), 0)
     oracle = D.OracleBackend(3, [7, 8, 9], [[8, 9]], None, 3)
     with pytest.raises(RuntimeError):
