@@ -63,20 +63,82 @@ class RMSNorm(nn.Module):
         return ops.rms_norm(x, self.weight, self.variance_epsilon)
 
 
+def _positions_of(position_ids, B: int, T: int, start: int, device) -> torch.Tensor:
+    """int64 [B, T] positions: the given ids broadcast over the batch, else start .. start + T."""
+    if position_ids is None:
+        position_ids = torch.arange(start, start + T, device=device)[None]
+    return position_ids.to(device=device, dtype=torch.int64).expand(B, T).contiguous()
+
+
+def _cached_weight(owner: nn.Module, key, tensors: list[torch.Tensor]) -> torch.Tensor:
+    """torch.cat(tensors) cached on the module (inference only), rebuilt when one of them changes
+    (its version counter or storage)."""
+    stamp = tuple((t._version, t.data_ptr()) for t in tensors)
+    cache = owner.__dict__.setdefault("_packed_weights", {})
+    hit = cache.get(key)
+    if hit is None or hit[0] != stamp:
+        with torch.no_grad():
+            hit = (stamp, torch.cat(list(tensors), 0).contiguous())
+        cache[key] = hit
+    return hit[1]
+
+
+def _project(a: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+    """a @ w^T (+ residual). Both kernels are batch-invariant: a row's result does not depend on
+    how many rows the call has."""
+    if a.dtype == torch.bfloat16 and ops.fused_linear_supported(a, w, w.shape[0]):
+        return ops.linear(a, w, residual=residual)
+    y = ops.gemm(a, w)
+    return y if residual is None else ops.add(residual, y)
+
+
 class OrthrusMLP(nn.Module):
+    """Qwen3MLP (down(silu(gate(x)) * up(x))) on the fused gate/up + SwiGLU kernel."""
+
     def __init__(self, config):
         super().__init__()
         self.gate_proj = nn.Linear(config.hidden_size, config.intermediate_size, bias=False)
         self.up_proj = nn.Linear(config.hidden_size, config.intermediate_size, bias=False)
         self.down_proj = nn.Linear(config.intermediate_size, config.hidden_size, bias=False)
 
+    def packed_gate_up(self) -> torch.Tensor:
+        """[gate; up] as one [2F, d] weight (cached)."""
+        return _cached_weight(self, "gate_up", [self.gate_proj.weight, self.up_proj.weight])
+
+    def activation(self, h: torch.Tensor) -> torch.Tensor:
+        """silu(h @ gate^T) * (h @ up^T) for h [rows, d]."""
+        w = self.packed_gate_up()
+        if h.dtype == torch.bfloat16 and ops.fused_linear_supported(h, w, w.shape[0] // 2):
+            return ops.linear_swiglu(h, w)
+        return ops.silu_mul(ops.gemm(h, w))
+
+    @torch.no_grad()
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        shape = x.shape
+        h = x.reshape(-1, shape[-1]).contiguous()
+        r = None if residual is None else residual.reshape(-1, shape[-1]).contiguous()
+        return _project(self.activation(h), self.down_proj.weight, r).view(shape)
+
 
 class OrthrusAttention(nn.Module):
     """Frozen autoregressive attention and its trainable diffusion twin (*_diff), with the
-    parameter layout of orthrus/modeling_orthrus.py:114-127."""
+    parameter layout and forward signature of orthrus/modeling_orthrus.py:114-189.
+
+    forward() runs one layer's attention for inference on this package's kernels:
+    - AR pass (is_diffusion_pass False): q|k|v projection, q/k RMSNorm + RoPE, the new keys and
+      values appended to past_key_values at this layer's committed length, causal attention over
+      the cache and the new tokens (a 4-D tree-verification mask is accepted and converted);
+    - diffusion pass: the twin projections, keys = cat[cache[:ar_seq_len], block], with the
+      dual-view training mask (flex_block_mask, or the equivalent dense 4-D attention_mask of
+      orthrus/decoding.py:463-481) or, with no mask, full attention of the block over the cache
+      and itself (generation).
+    RoPE positions come from the position_ids / cache_position the decoder passes down (the kernels
+    compute cos / sin from them, the values position_embeddings holds for the default RoPE), else
+    they continue the cache. Returns (output [B, T, d], None)."""
 
     def __init__(self, config, layer_idx: int):
         super().__init__()
+        self.config = config
         self.layer_idx = layer_idx
         self.head_dim = config.head_dim
         self.num_heads = config.num_attention_heads
@@ -100,25 +162,238 @@ class OrthrusAttention(nn.Module):
         return g("q_proj").weight, g("k_proj").weight, g("v_proj").weight, g("o_proj").weight, \
             g("q_norm").weight, g("k_norm").weight
 
+    def packed_qkv(self, diffusion: bool) -> torch.Tensor:
+        """[q; k; v] weights of one view as a single [(Hq + 2 Hkv) hd, d] matrix (cached)."""
+        wq, wk, wv, *_ = self.view_weights(diffusion)
+        return _cached_weight(self, ("qkv", diffusion), [wq, wk, wv])
+
+    def attend(self, h, positions, mode: str, *, kv=None, offsets=None, ar_len=None, limit2=None,
+               block_mask=None, tree_lo=None, inv_freq=None) -> torch.Tensor:
+        """Attention output [B*T, Hq*hd] (the o projection's input) of h [B*T, d] at positions
+        [B, T]; the modes of OrthrusModel.run_layers, kv = this layer's (key, value) buffers."""
+        cfg = self.config
+        B, T = positions.shape
+        Hq, Hkv, hd = self.num_heads, self.num_kv_heads, self.head_dim
+        D = padded_head_dim(hd)
+        eps = cfg.rms_norm_eps
+        diffusion = mode not in ("ar", "tree")
+        _, _, _, _, qn, kn = self.view_weights(diffusion)
+        inv = inv_freq if inv_freq is not None else ops.rope_inv_freq(hd, _theta(cfg), h.device)
+        qkv = _project(h, self.packed_qkv(diffusion))
+        if mode in ("ar", "tree") and kv is not None:
+            kb, vb = kv
+            q, _, _, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps,
+                                      k_cache=kb, v_cache=vb, offset=offsets)
+            if mode == "tree":
+                o, _ = ops.attention_fwd(q, kb, vb, kb, vb, mask=MASK_TREE, hd=hd, scale=self.scaling,
+                                         offset=offsets, limit2=tree_lo, want_lse=False)
+            else:
+                o, _ = ops.attention_fwd(q, kb, vb, mask=MASK_CAUSAL, hd=hd, scale=self.scaling,
+                                         offset=offsets, want_lse=False)
+        elif mode == "ar":
+            q, k, v, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps)
+            o, _ = ops.attention_fwd(q, k, v, mask=MASK_CAUSAL, hd=hd, scale=self.scaling, want_lse=False)
+        else:
+            q, k2, v2, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps)
+            kb, vb = kv
+            if mode == "dual":
+                o, _ = ops.attention_fwd(q, kb, vb, k2, v2, mask=MASK_DUAL, hd=hd, scale=self.scaling,
+                                         anchors=block_mask.anchors, block=block_mask.block_size,
+                                         L1=ar_len, want_lse=False)
+            else:
+                o, _ = ops.attention_fwd(q, kb, vb, k2, v2, mask=MASK_DRAFT, hd=hd, scale=self.scaling,
+                                         offset=offsets, limit2=limit2, want_lse=False)
+        return o.reshape(B * T, Hq * hd)
+
+    @torch.no_grad()
+    def forward(self, hidden_states: torch.Tensor, position_embeddings=None, attention_mask=None,
+                past_key_values: KVCache | None = None, is_diffusion_pass: bool = False,
+                ar_seq_len: int | None = None, flex_block_mask: "DualViewMask | None" = None,
+                **kwargs):
+        B, T, d = hidden_states.shape
+        cache = past_key_values
+        if cache is not None and not isinstance(cache, KVCache):
+            raise ValueError("past_key_values must be this package's KVCache (exported as DynamicCache)")
+        seen = cache.get_seq_length(self.layer_idx) if cache is not None else 0
+        position_ids = kwargs.get("position_ids")
+        if position_ids is None:
+            position_ids = kwargs.get("cache_position")
+        positions = _positions_of(position_ids, B, T, seen, hidden_states.device)
+        h = hidden_states.reshape(B * T, d).contiguous()
+        common = dict(inv_freq=None)
+        if not is_diffusion_pass:
+            tree_lo = None
+            if attention_mask is not None and attention_mask.dim() == 4:
+                tree_lo = tree_mask_to_lo(attention_mask, seen, T).to(h.device)
+            if cache is None:
+                if tree_lo is not None:
+                    raise ValueError("tree verification runs over a cache")
+                o = self.attend(h, positions, "ar", **common)
+            else:
+                cache.allocate(B, h.dtype, h.device)
+                cache.reserve(seen + T)
+                kv = (cache.k[self.layer_idx], cache.v[self.layer_idx])
+                o = self.attend(h, positions, "tree" if tree_lo is not None else "ar", kv=kv,
+                                offsets=cache.offsets(B, self.layer_idx), tree_lo=tree_lo, **common)
+                cache.lengths[self.layer_idx] = seen + T
+        else:
+            if cache is None or ar_seq_len is None:
+                raise ValueError("the diffusion pass needs the AR cache (past_key_values) and ar_seq_len")
+            if seen != ar_seq_len:
+                raise ValueError(f"AR cache holds {seen} positions, expected {ar_seq_len}")
+            kv = (cache.k[self.layer_idx][:, :, :ar_seq_len], cache.v[self.layer_idx][:, :, :ar_seq_len])
+            if flex_block_mask is None and attention_mask is not None:
+                flex_block_mask = dense_mask_to_dual(attention_mask, ar_seq_len, T)
+            if flex_block_mask is not None:
+                o = self.attend(h, positions, "dual", kv=kv, ar_len=ar_seq_len, block_mask=flex_block_mask,
+                                **common)
+            else:
+                offsets = cache.offsets(B, self.layer_idx)
+                limit2 = torch.full((B,), T, dtype=torch.int32, device=h.device)
+                o = self.attend(h, positions, "draft", kv=kv, offsets=offsets, limit2=limit2, **common)
+        wo = self.view_weights(is_diffusion_pass)[3]
+        return _project(o, wo).view(B, T, d), None
+
 
 class OrthrusDecoderLayer(nn.Module):
+    """Pre-norm Qwen3 decoder layer (orthrus/modeling_orthrus.py:192-221): x + attn(norm(x)), then
+    + mlp(norm(x)); the residual adds ride in the projection epilogues."""
+
     def __init__(self, config, layer_idx: int):
         super().__init__()
+        self.hidden_size = config.hidden_size
         self.self_attn = OrthrusAttention(config, layer_idx)
         self.mlp = OrthrusMLP(config)
         self.input_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
         self.post_attention_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
 
+    @torch.no_grad()
+    def forward(self, hidden_states: torch.Tensor, attention_mask=None, position_embeddings=None,
+                past_key_values: KVCache | None = None, **kwargs) -> torch.Tensor:
+        attn, _ = self.self_attn(hidden_states=self.input_layernorm(hidden_states),
+                                 attention_mask=attention_mask, position_embeddings=position_embeddings,
+                                 past_key_values=past_key_values, **kwargs)
+        x = hidden_states + attn
+        return self.mlp(self.post_attention_layernorm(x), residual=x)
+
 
 class OrthrusModel(nn.Module):
+    """The decoder stack (orthrus/modeling_orthrus.py:224-296). forward() has the reference's
+    signature and returns last_hidden_state (final norm applied) and the cache. The AR pass and
+    generation-time diffusion passes run the fused no-grad layer loop (run_layers); a diffusion
+    pass with the training mask and gradients enabled runs the differentiable dual-view layers of
+    objective.model_states, so its output backpropagates into the twins."""
+
     def __init__(self, config):
         super().__init__()
         self.config = config
+        self.padding_idx = getattr(config, "pad_token_id", None)
+        self.vocab_size = config.vocab_size
         self.embed_tokens = nn.Embedding(config.vocab_size, config.hidden_size)
         self.layers = nn.ModuleList(
             [OrthrusDecoderLayer(config, i) for i in range(config.num_hidden_layers)])
         self.norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
         self.gradient_checkpointing = False
+        self._inv_freq = None
+
+    def inv_freq(self, device) -> torch.Tensor:
+        if self._inv_freq is None or self._inv_freq.device != torch.device(device):
+            self._inv_freq = ops.rope_inv_freq(self.config.head_dim, _theta(self.config), device)
+        return self._inv_freq
+
+    def forward(self, input_ids=None, attention_mask=None, position_ids=None,
+                past_key_values: KVCache | None = None, inputs_embeds=None, use_cache: bool | None = None,
+                cache_position=None, is_diffusion_pass: bool = False, ar_seq_len: int | None = None,
+                flex_block_mask: "DualViewMask | None" = None, tree_lo: torch.Tensor | None = None,
+                **kwargs) -> "ModelOutput":
+        if (input_ids is None) == (inputs_embeds is None):
+            raise ValueError("pass exactly one of input_ids or inputs_embeds")
+        if past_key_values is not None and not isinstance(past_key_values, KVCache):
+            raise ValueError("past_key_values must be this package's KVCache (exported as DynamicCache)")
+        x = inputs_embeds if inputs_embeds is not None else self.embed_tokens(input_ids)
+        B, T, _ = x.shape
+        if use_cache and past_key_values is None:
+            past_key_values = KVCache(self.config)
+        cache = past_key_values
+        seen = cache.get_seq_length() if cache is not None else 0
+        if position_ids is None and cache_position is not None:
+            position_ids = cache_position[None]
+        positions = _positions_of(position_ids, B, T, seen, x.device)
+        if attention_mask is not None and attention_mask.dim() == 4:
+            if tree_lo is not None:
+                raise ValueError("pass a 4-D mask or tree_lo, not both")
+            if is_diffusion_pass:
+                if flex_block_mask is None:
+                    flex_block_mask = dense_mask_to_dual(attention_mask, ar_seq_len, T)
+            else:
+                tree_lo = tree_mask_to_lo(attention_mask, seen, T).to(x.device)
+        if is_diffusion_pass:
+            if cache is None or ar_seq_len is None:
+                raise ValueError("the diffusion pass needs the AR cache (past_key_values) and ar_seq_len")
+            if seen != ar_seq_len:
+                raise ValueError(f"AR cache holds {seen} positions, expected {ar_seq_len}")
+            if tree_lo is not None:
+                raise ValueError("tree masks belong to AR verification passes")
+            mode = "dual" if flex_block_mask is not None else "draft"
+        else:
+            mode = "ar"
+            if cache is not None and not use_cache:
+                raise ValueError("an AR pass over a cache must append to it (use_cache=True)")
+            if tree_lo is not None:
+                if cache is None or B != 1:
+                    raise ValueError("tree verification runs on a cache, batch 1")
+                mode = "tree"
+        if cache is not None:
+            cache.allocate(B, x.dtype, x.device)
+            cache.reserve(seen + T)
+        if mode == "dual" and torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()):
+            from orthrus_training_b200.objective import diffusion_states
+
+            hidden = diffusion_states(self, x.reshape(B * T, -1), cache, positions, flex_block_mask)
+            hidden = hidden.view(B, T, -1)
+        else:
+            with torch.no_grad():
+                kv = cache.buffers() if cache is not None else None
+                offsets = cache.offsets(B) if cache is not None else None
+                hidden = self.run_layers(x, positions, mode, kv=kv, offsets=offsets, ar_len=ar_seq_len,
+                                         block_mask=flex_block_mask, tree_lo=tree_lo)
+        if cache is not None and mode in ("ar", "tree"):
+            cache.length = seen + T
+        return ModelOutput(last_hidden_state=hidden, past_key_values=cache if use_cache else None,
+                           hidden_states=(hidden,))
+
+    @torch.no_grad()
+    def run_layers(self, x, positions, mode: str, *, kv=None, offsets=None, ar_len=None,
+                   limit2=None, block_mask=None, tree_lo=None):
+        """The decoder stack over x [B, T, d] at positions [B, T] (int64) -> final-norm hidden.
+
+        mode "ar":    AR view; with kv (per-layer [B, Hkv, cap, D] buffers) the new K/V are written
+                      at rows offsets[b] + t and queries attend causally over rows < offsets[b]+t+1
+                      (a verification or plain greedy pass); without kv, plain causal attention.
+        mode "draft": diffusion view over kv rows < offsets[b] plus the block's own keys
+                      [0, limit2[b]) (the generation-time draft, orthrus/modeling_orthrus.py:469-481).
+        mode "dual":  diffusion view with the training mask (block_mask) over kv rows < ar_len.
+        mode "tree":  AR view writing the new K/V like "ar"; query t sees kv rows
+                      < offsets[b] + 1 and rows [offsets[b] + tree_lo[t], offsets[b] + t + 1).
+        The residual adds ride in the o / down projection epilogues.
+        """
+        cfg = self.config
+        B, T, d = x.shape
+        eps = cfg.rms_norm_eps
+        inv = self.inv_freq(x.device)
+        diffusion = mode not in ("ar", "tree")
+        x = x.reshape(B * T, d).contiguous()
+        for i, layer in enumerate(self.layers[: cfg.num_hidden_layers]):
+            attn = layer.self_attn
+            h = ops.rms_norm(x, layer.input_layernorm.weight, eps)
+            o = attn.attend(h, positions, mode, kv=kv[i] if kv is not None else None, offsets=offsets,
+                            ar_len=ar_len, limit2=limit2, block_mask=block_mask, tree_lo=tree_lo,
+                            inv_freq=inv)
+            x = _project(o, attn.view_weights(diffusion)[3], residual=x)
+            h = ops.rms_norm(x, layer.post_attention_layernorm.weight, eps)
+            x = _project(layer.mlp.activation(h), layer.mlp.down_proj.weight, residual=x)
+        x = ops.rms_norm(x, self.norm.weight, eps)
+        return x.view(B, T, d)
 
 
 @dataclass
@@ -166,6 +441,34 @@ def tree_mask_to_lo(mask: torch.Tensor, seen: int, T: int) -> torch.Tensor:
     if bool(m[0, seen + 1:].any()):
         raise ValueError("the root sees no other new token")
     return lo
+
+
+def dense_mask_to_dual(mask: torch.Tensor, ar_len: int, T: int) -> "DualViewMask":
+    """The dual-view mask object of a dense 4-D boolean mask [1, 1, T, ar_len + T] of the form
+    orthrus/decoding.py:463-481 builds for packed draft blocks: the T queries form consecutive
+    blocks of K; every query of block b sees the AR keys [0, anchor_b) and all K keys of its own
+    block, nothing else. Checks that form (anchors non-decreasing) and raises ValueError otherwise."""
+    m = mask.detach().to("cpu", torch.bool)
+    if m.shape != (1, 1, T, ar_len + T):
+        raise ValueError(f"a dual-view mask must be [1, 1, {T}, {ar_len + T}], got {tuple(m.shape)}")
+    m = m[0, 0]
+    own, ar = m[:, ar_len:], m[:, :ar_len]
+    K = int(own[0].sum())
+    if K < 1 or T % K != 0:
+        raise ValueError("the new keys of a dual-view mask form equal blocks")
+    blocks = torch.arange(T) // K
+    if not torch.equal(own, blocks[:, None] == blocks[None, :]):
+        raise ValueError("each query of a dual-view mask sees exactly its own block among the new keys")
+    anchors = ar.sum(1).view(T // K, K)
+    if not bool((anchors == anchors[:, :1]).all()):
+        raise ValueError("all queries of a block see the same AR prefix")
+    anchors = anchors[:, 0]
+    prefix = torch.arange(ar_len)[None, :] < anchors.repeat_interleave(K)[:, None]
+    if not torch.equal(ar, prefix):
+        raise ValueError("the AR keys a query sees form a prefix [0, anchor)")
+    if bool((anchors[1:] < anchors[:-1]).any()):
+        raise ValueError("dual-view anchors must be non-decreasing")
+    return DualViewMask(anchors[None].to(mask.device), ar_len, K)
 
 
 class DualViewMask:
@@ -260,8 +563,6 @@ class OrthrusLM(nn.Module):
         if getattr(config, "tie_word_embeddings", True):
             self.lm_head.weight = self.model.embed_tokens.weight
         self.init_weights()
-        self._inv_freq = None
-        self._packed = {}
 
     # -- weights ------------------------------------------------------------------------------
 
@@ -284,27 +585,18 @@ class OrthrusLM(nn.Module):
         self.model.gradient_checkpointing = True
 
     def inv_freq(self, device) -> torch.Tensor:
-        if self._inv_freq is None or self._inv_freq.device != torch.device(device):
-            self._inv_freq = ops.rope_inv_freq(self.config.head_dim, _theta(self.config), device)
-        return self._inv_freq
+        return self.model.inv_freq(device)
 
     def packed_qkv(self, layer: int, diffusion: bool) -> torch.Tensor:
         """[q; k; v] projection weights of a layer's view as one [(Hq+2Hkv) hd, d] matrix, cached
-        for inference (rebuilt when a weight's version changes)."""
-        attn = self.model.layers[layer].self_attn
-        wq, wk, wv, *_ = attn.view_weights(diffusion)
-        key = (layer, diffusion)
-        versions = (wq._version, wk._version, wv._version, wq.data_ptr())
-        hit = self._packed.get(key)
-        if hit is None or hit[0] != versions:
-            with torch.no_grad():
-                hit = (versions, torch.cat([wq, wk, wv], 0).contiguous())
-            self._packed[key] = hit
-        return hit[1]
+        for inference (rebuilt when a weight changes)."""
+        return self.model.layers[layer].self_attn.packed_qkv(diffusion)
+
+    def _packed_mlp(self, layer: int) -> torch.Tensor:
+        return self.model.layers[layer].mlp.packed_gate_up()
 
     # -- forward ------------------------------------------------------------------------------
 
-    @torch.no_grad()
     def forward(
         self,
         input_ids: torch.LongTensor | None = None,
@@ -322,65 +614,28 @@ class OrthrusLM(nn.Module):
         tree_lo: torch.Tensor | None = None,
         **kwargs,
     ) -> ModelOutput:
-        """OrthrusLM.forward (orthrus/modeling_orthrus.py:327-362) for inference: the AR view
-        (causal over the cache plus the new tokens, appended to the cache when use_cache) or the
-        diffusion view (twin projections over cat([cache[:ar_seq_len], block]); full attention, or
-        the dual-view training mask when flex_block_mask is given). Logits are fp32.
+        """OrthrusLM.forward (orthrus/modeling_orthrus.py:327-362): the decoder stack
+        (OrthrusModel.forward), then fp32 logits of the last `logits_to_keep` positions (all when
+        0) or of the given indices.
 
         Tree verification (orthrus/decoding.py:208-241): an AR pass whose new tokens are a root and
         several branches, each token seeing the cached prefix, the root and its own branch up to
         itself. Give either ``tree_lo`` (int32 [T]: the index among the new tokens where each
         token's branch begins, >= 1) or the reference's dense 4-D boolean mask [1, 1, T, seen + T],
         which is checked to have that form and converted."""
-        if (input_ids is None) == (inputs_embeds is None):
-            raise ValueError("pass exactly one of input_ids or inputs_embeds")
-        x = inputs_embeds if inputs_embeds is not None else self.model.embed_tokens(input_ids)
-        B, T, _ = x.shape
-        if attention_mask is not None and attention_mask.dim() == 4:
-            if tree_lo is not None:
-                raise ValueError("pass a 4-D tree mask or tree_lo, not both")
-            seen0 = past_key_values.get_seq_length() if past_key_values is not None else 0
-            tree_lo = tree_mask_to_lo(attention_mask, seen0, T).to(x.device)
-        if use_cache and past_key_values is None:
-            past_key_values = KVCache(self.config, batch=B, device=x.device, dtype=x.dtype)
-        cache = past_key_values
-        seen = cache.get_seq_length() if cache is not None else 0
-        if position_ids is None:
-            position_ids = torch.arange(seen, seen + T, device=x.device)[None]
-        position_ids = position_ids.expand(B, T).contiguous()
-        if is_diffusion_pass:
-            if cache is None or ar_seq_len is None:
-                raise ValueError("the diffusion pass needs the AR cache (past_key_values) and ar_seq_len")
-            if cache.get_seq_length() != ar_seq_len:
-                raise ValueError(f"AR cache holds {cache.get_seq_length()} positions, expected {ar_seq_len}")
-        kv = cache.buffers() if cache is not None else None
-        if cache is not None:
-            cache.reserve(seen + T)
-            kv = cache.buffers()
-        offsets = cache.offsets(B) if cache is not None else None
-        if not is_diffusion_pass:
-            mode = "ar"
-            if not use_cache and cache is not None:
-                raise ValueError("an AR pass over a cache must append to it (use_cache=True)")
-            if tree_lo is not None:
-                if cache is None or B != 1:
-                    raise ValueError("tree verification runs on a cache, batch 1")
-                mode = "tree"
-        else:
-            if tree_lo is not None:
-                raise ValueError("tree masks belong to AR verification passes")
-            mode = "dual" if flex_block_mask is not None else "draft"
-        hidden = self.run_layers(x, position_ids, mode, kv=kv, offsets=offsets, ar_len=ar_seq_len,
-                                 block_mask=flex_block_mask, tree_lo=tree_lo)
-        if cache is not None and use_cache and not is_diffusion_pass:
-            cache.length += T
+        out = self.model(input_ids=input_ids, attention_mask=attention_mask, position_ids=position_ids,
+                         past_key_values=past_key_values, inputs_embeds=inputs_embeds, use_cache=use_cache,
+                         cache_position=cache_position, is_diffusion_pass=is_diffusion_pass,
+                         ar_seq_len=ar_seq_len, flex_block_mask=flex_block_mask, tree_lo=tree_lo, **kwargs)
+        hidden = out.last_hidden_state
         if isinstance(logits_to_keep, int):
             keep = hidden[:, -logits_to_keep:] if logits_to_keep else hidden
         else:
             keep = hidden[:, logits_to_keep]
-        logits = self.lm_logits(keep)
-        return ModelOutput(logits=logits, last_hidden_state=hidden,
-                           past_key_values=cache if use_cache else None, hidden_states=(hidden,))
+        with torch.no_grad():
+            logits = self.lm_logits(keep.detach())
+        return ModelOutput(logits=logits, last_hidden_state=hidden, past_key_values=out.past_key_values,
+                           hidden_states=(hidden,))
 
     def lm_logits(self, hidden: torch.Tensor) -> torch.Tensor:
         shape = hidden.shape[:-1]
@@ -392,90 +647,9 @@ class OrthrusLM(nn.Module):
             logits = ops.gemm(h, w)
         return logits.view(*shape, -1)
 
-    def run_layers(self, x, positions, mode: str, *, kv=None, offsets=None, ar_len=None,
-                   limit2=None, block_mask=None, tree_lo=None):
-        """The decoder stack over x [B, T, d] at positions [B, T] (int64) -> final-norm hidden.
-
-        mode "ar":    AR view; with kv (per-layer [B, Hkv, cap, D] buffers) the new K/V are written
-                      at rows offsets[b] + t and queries attend causally over rows < offsets[b]+t+1
-                      (a verification or plain greedy pass); without kv, plain causal attention.
-        mode "draft": diffusion view over kv rows < offsets[b] plus the block's own keys
-                      [0, limit2[b]) (the generation-time draft, orthrus/modeling_orthrus.py:469-481).
-        mode "dual":  diffusion view with the training mask (block_mask) over kv rows < ar_len.
-        mode "tree":  AR view writing the new K/V like "ar"; query t sees kv rows
-                      < offsets[b] + 1 and rows [offsets[b] + tree_lo[t], offsets[b] + t + 1).
-        """
-        cfg = self.config
-        B, T, d = x.shape
-        Hq, Hkv, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
-        D = padded_head_dim(hd)
-        eps = cfg.rms_norm_eps
-        inv = self.inv_freq(x.device)
-        diffusion = mode not in ("ar", "tree")
-        x = x.reshape(B * T, d).contiguous()
-        fused = x.dtype == torch.bfloat16
-
-        def proj(a, w, residual=None):
-            # both kernels are batch-invariant (a row's result does not depend on the others)
-            if fused and ops.fused_linear_supported(a, w, w.shape[0]):
-                return ops.linear(a, w, residual=residual)
-            y = ops.gemm(a, w)
-            return y if residual is None else ops.add(residual, y)
-
-        for i, layer in enumerate(self.model.layers[: cfg.num_hidden_layers]):
-            attn = layer.self_attn
-            _, _, _, wo, qn, kn = attn.view_weights(diffusion)
-            h = ops.rms_norm(x, layer.input_layernorm.weight, eps)
-            qkv = proj(h, self.packed_qkv(i, diffusion))
-            if mode in ("ar", "tree") and kv is not None:
-                kb, vb = kv[i]
-                q, _, _, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps,
-                                          k_cache=kb, v_cache=vb, offset=offsets)
-                if mode == "tree":
-                    o, _ = ops.attention_fwd(q, kb, vb, kb, vb, mask=MASK_TREE, hd=hd,
-                                             scale=attn.scaling, offset=offsets, limit2=tree_lo,
-                                             want_lse=False)
-                else:
-                    o, _ = ops.attention_fwd(q, kb, vb, mask=MASK_CAUSAL, hd=hd, scale=attn.scaling,
-                                             offset=offsets, want_lse=False)
-            elif mode == "ar":
-                q, k, v, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps)
-                o, _ = ops.attention_fwd(q, k, v, mask=MASK_CAUSAL, hd=hd, scale=attn.scaling,
-                                         want_lse=False)
-            else:
-                q, k2, v2, _ = ops.qkv_prep(qkv, positions, inv, qn, kn, B, T, Hq, Hkv, hd, D, eps)
-                kb, vb = kv[i]
-                if mode == "dual":
-                    o, _ = ops.attention_fwd(q, kb, vb, k2, v2, mask=MASK_DUAL, hd=hd,
-                                             scale=attn.scaling, anchors=block_mask.anchors,
-                                             block=block_mask.block_size, L1=ar_len,
-                                             want_lse=False)
-                else:
-                    o, _ = ops.attention_fwd(q, kb, vb, k2, v2, mask=MASK_DRAFT, hd=hd,
-                                             scale=attn.scaling, offset=offsets, limit2=limit2,
-                                             want_lse=False)
-            x = proj(o.reshape(B * T, Hq * hd), wo, residual=x)
-            h = ops.rms_norm(x, layer.post_attention_layernorm.weight, eps)
-            w_gu = self._packed_mlp(i)
-            if fused and ops.fused_linear_supported(h, w_gu, w_gu.shape[0] // 2):
-                act = ops.linear_swiglu(h, w_gu)
-            else:
-                act = ops.silu_mul(ops.gemm(h, w_gu))
-            x = proj(act, layer.mlp.down_proj.weight, residual=x)
-        x = ops.rms_norm(x, self.model.norm.weight, eps)
-        return x.view(B, T, d)
-
-    def _packed_mlp(self, layer: int) -> torch.Tensor:
-        mlp = self.model.layers[layer].mlp
-        key = (layer, "mlp")
-        versions = (mlp.gate_proj.weight._version, mlp.up_proj.weight._version,
-                    mlp.gate_proj.weight.data_ptr())
-        hit = self._packed.get(key)
-        if hit is None or hit[0] != versions:
-            with torch.no_grad():
-                hit = (versions, torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight], 0).contiguous())
-            self._packed[key] = hit
-        return hit[1]
+    def run_layers(self, x, positions, mode: str, **kwargs):
+        """The fused layer loop of OrthrusModel.run_layers (used by the device decode loop)."""
+        return self.model.run_layers(x, positions, mode, **kwargs)
 
     # -- generation ---------------------------------------------------------------------------
 

@@ -212,9 +212,9 @@ class DualViewAttentionFused(torch.autograd.Function):
                 None)
 
 
-def _teacher_layer(model, i, x, pos, B, L, inv, rope=None):
-    cfg = model.config
-    layer = model.model.layers[i]
+def _teacher_layer(backbone, i, x, pos, B, L, inv, rope=None):
+    cfg = backbone.config
+    layer = backbone.layers[i]
     attn = layer.self_attn
     Hq, Hkv, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
     D = padded_head_dim(hd)
@@ -222,17 +222,17 @@ def _teacher_layer(model, i, x, pos, B, L, inv, rope=None):
     h = ops.rms_norm(x, layer.input_layernorm.weight, eps)
     if rope is not None:
         # q|k|v GEMM with the q/k norm + RoPE prologue in its epilogue, written head-major
-        q, k, v = ops.linear_qkv_rope(h, model.packed_qkv(i, False), attn.q_norm.weight,
+        q, k, v = ops.linear_qkv_rope(h, attn.packed_qkv(False), attn.q_norm.weight,
                                       attn.k_norm.weight, rope, B, L, Hq, Hkv, eps)
     else:
-        qkv = h @ model.packed_qkv(i, False).t()
+        qkv = h @ attn.packed_qkv(False).t()
         q, k, v, _ = ops.qkv_prep(qkv, pos, inv, attn.q_norm.weight, attn.k_norm.weight, B, L, Hq,
                                   Hkv, hd, D, eps)
     o, _ = ops.attention_fwd(q, k, v, mask=MASK_CAUSAL, hd=hd, scale=hd ** -0.5, want_lse=False)
     # residual adds ride in the GEMM epilogue (beta = 1)
     x = torch.addmm(x, o.view(B * L, Hq * hd), attn.o_proj.weight.t())
     h = ops.rms_norm(x, layer.post_attention_layernorm.weight, eps)
-    w_gu = model._packed_mlp(i)
+    w_gu = layer.mlp.packed_gate_up()
     if ops.fused_linear_supported(h, w_gu, w_gu.shape[0] // 2):
         # gate/up GEMM with SwiGLU in its epilogue: [gate | up] never goes through HBM
         act = ops.linear_swiglu(h, w_gu)
@@ -242,9 +242,9 @@ def _teacher_layer(model, i, x, pos, B, L, inv, rope=None):
     return x, k, v
 
 
-def _diffusion_layer(model, i, x, ar_k, ar_v, positions, anchors, inv, B, Q, rope=None):
-    cfg = model.config
-    layer = model.model.layers[i]
+def _diffusion_layer(backbone, i, x, ar_k, ar_v, positions, anchors, inv, B, Q, rope=None):
+    cfg = backbone.config
+    layer = backbone.layers[i]
     attn = layer.self_attn
     Hq, Hkv, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
     eps = cfg.rms_norm_eps
@@ -260,7 +260,7 @@ def _diffusion_layer(model, i, x, ar_k, ar_v, positions, anchors, inv, B, Q, rop
                                     positions, anchors, inv, meta)
     x = torch.addmm(x, o, attn.o_proj_diff.weight.t())
     h = _rms_norm(x, layer.post_attention_layernorm.weight, eps)
-    w_gu = model._packed_mlp(i)
+    w_gu = layer.mlp.packed_gate_up()
     if ops.fused_linear_supported(h, w_gu, w_gu.shape[0] // 2):
         act = _GateUpSwiGLU.apply(h, w_gu)
     else:
@@ -268,12 +268,58 @@ def _diffusion_layer(model, i, x, ar_k, ar_v, positions, anchors, inv, B, Q, rop
     return torch.addmm(x, act, layer.mlp.down_proj.weight.t())
 
 
+def _backbone(model):
+    """The decoder stack of an OrthrusLM, or the stack itself."""
+    return model.model if isinstance(model, OrthrusLM) else model
+
+
+def _student_stack(backbone, x, cache, anchors, positions, rope, inv):
+    """The differentiable diffusion view: every layer over x [B*Q, d] (the block embeddings) with
+    the teacher's keys / values cache[i] = (k, v) [B, Hkv, >= L, D], then the final norm."""
+    B, Q = positions.shape
+    checkpoint = backbone.gradient_checkpointing and torch.is_grad_enabled()
+    for i, (k, v) in enumerate(cache):
+        args = (backbone, i, x, k, v, positions, anchors, inv, B, Q, rope)
+        if checkpoint:
+            x = torch.utils.checkpoint.checkpoint(_diffusion_layer, *args, use_reentrant=False)
+        else:
+            x = _diffusion_layer(*args)
+    return _rms_norm(x, backbone.norm.weight, backbone.config.rms_norm_eps)
+
+
+def _rope_for(x, backbone, rows: int, Q: int):
+    cfg = backbone.config
+    hd = cfg.head_dim
+    if ops.fused_qkv_rope_supported(x, hd, padded_head_dim(hd), Q, cfg.num_attention_heads,
+                                    cfg.num_key_value_heads):
+        return ops.rope_table(backbone.inv_freq(x.device), rows)
+    return None
+
+
+def diffusion_states(backbone, x: torch.Tensor, cache, positions: torch.Tensor,
+                     block_mask) -> torch.Tensor:
+    """The diffusion view of OrthrusModel.forward with the training mask and gradients enabled:
+    block embeddings x [B*Q, d] at positions [B, Q] over the AR cache (a KVCache holding the
+    teacher's keys and values of block_mask.ar_len positions), differentiable w.r.t. the twins
+    (orthrus/modeling_orthrus.py:129-189 through flex attention). Returns [B*Q, d]."""
+    ar_len = block_mask.ar_len
+    if block_mask.block_size != backbone.config.block_size:
+        raise ValueError("the mask's block size differs from the model's")
+    B, Q = positions.shape
+    anchors = block_mask.anchors.to(torch.int64).contiguous()
+    layers = [(k[:, :, :ar_len], v[:, :, :ar_len]) for k, v in cache.buffers()]
+    rope = _rope_for(x, backbone, ar_len, Q)
+    return _student_stack(backbone, x, layers, anchors, positions.contiguous(), rope,
+                          backbone.inv_freq(x.device))
+
+
 def model_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tensor,
                  compiled: bool = False, kernel_options: dict | None = None):
     """Final hidden states of the diffusion view over all anchor blocks [B, A*K, d] and of the
     frozen AR view over the clean rows [B, L, d] (orthrus/objective.py:228-272). `compiled` and
     `kernel_options` are accepted for signature compatibility; the kernels are fixed."""
-    cfg = model.config
+    backbone = _backbone(model)
+    cfg = backbone.config
     if any(t != "full_attention" for t in getattr(cfg, "layer_types", ["full_attention"])
            [: cfg.num_hidden_layers]):
         raise ValueError("model_states supports full attention layers only (no sliding window)")
@@ -282,21 +328,17 @@ def model_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tenso
     K = cfg.block_size
     B, L = input_ids.shape
     d = cfg.hidden_size
-    inv = model.inv_freq(input_ids.device)
-    embed = model.model.embed_tokens.weight
+    inv = backbone.inv_freq(input_ids.device)
+    embed = backbone.embed_tokens.weight
     with torch.no_grad():
         x = F.embedding(input_ids, embed).reshape(B * L, d)
         pos = torch.arange(L, device=x.device)[None].expand(B, L).contiguous()
-        hd = cfg.head_dim
-        rope = None
-        if ops.fused_qkv_rope_supported(x, hd, padded_head_dim(hd), L, cfg.num_attention_heads,
-                                        cfg.num_key_value_heads):
-            rope = ops.rope_table(inv, L)
+        rope = _rope_for(x, backbone, L, L)
         cache = []
         for i in range(cfg.num_hidden_layers):
-            x, k, v = _teacher_layer(model, i, x, pos, B, L, inv, rope)
+            x, k, v = _teacher_layer(backbone, i, x, pos, B, L, inv, rope)
             cache.append((k, v))
-        teacher = ops.rms_norm(x, model.model.norm.weight, cfg.rms_norm_eps).view(B, L, d)
+        teacher = ops.rms_norm(x, backbone.norm.weight, cfg.rms_norm_eps).view(B, L, d)
     anchors = anchors.to(torch.int64).contiguous()
     positions = (anchors[:, :, None] + torch.arange(K, device=anchors.device)).flatten(1).contiguous()
     block_ids = torch.full((B, anchors.shape[1], K), cfg.mask_token_id, dtype=torch.long,
@@ -304,14 +346,7 @@ def model_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tenso
     block_ids[:, :, 0] = input_ids.gather(1, anchors)
     Q = anchors.shape[1] * K
     x = F.embedding(block_ids.flatten(1), embed).reshape(B * Q, d)
-    checkpoint = model.is_gradient_checkpointing and torch.is_grad_enabled()
-    for i, (k, v) in enumerate(cache):
-        args = (model, i, x, k, v, positions, anchors, inv, B, Q, rope)
-        if checkpoint:
-            x = torch.utils.checkpoint.checkpoint(_diffusion_layer, *args, use_reentrant=False)
-        else:
-            x = _diffusion_layer(*args)
-    student = _rms_norm(x, model.model.norm.weight, cfg.rms_norm_eps)
+    student = _student_stack(backbone, x, cache, anchors, positions, rope, inv)
     return student.view(B, Q, d), teacher
 
 

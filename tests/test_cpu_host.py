@@ -126,3 +126,37 @@ def test_ar_decode_cycle():
     assert gen.tokens == ref and gen.forward_passes == 6
     gen = D.ar_decode(ReplayBackend(3, ref, [[0] * 7] * 10, 8), 3, 6, {8})
     assert gen.tokens == [5, 6, 7, 8] and gen.eos
+
+
+def test_cache_has_the_dynamic_cache_surface():
+    """KVCache(config=...) allocates on its first write like DynamicCache; update() appends one
+    layer and returns its committed keys / values; lengths are per layer; crop() truncates all
+    (orthrus/modeling_orthrus.py:107-111,162-166)."""
+    from transformers import Qwen3Config
+
+    from orthrus_training_b200.kv_cache import KVCache
+    from orthrus_training_b200.modeling_orthrus import DynamicCache, truncate_cache
+
+    cfg = Qwen3Config(vocab_size=64, hidden_size=32, intermediate_size=64, num_hidden_layers=2,
+                      num_attention_heads=2, num_key_value_heads=1, head_dim=16)
+    assert DynamicCache is KVCache
+    cache = DynamicCache(config=cfg)
+    assert not cache.allocated and cache.get_seq_length() == 0
+    k = torch.randn(1, 1, 5, 16, dtype=torch.float64)
+    v = torch.randn(1, 1, 5, 16, dtype=torch.float64)
+    keys, values = cache.update(k, v, 0)
+    assert cache.allocated and cache.dtype == torch.float64
+    assert torch.equal(keys, k) and torch.equal(values, v)
+    assert cache.get_seq_length(0) == 5 and cache.get_seq_length(1) == 0
+    cache.update(k, v, 1)
+    cache.update(k[:, :, :2], v[:, :, :2], 0)
+    assert torch.equal(cache.layers[0].keys, torch.cat([k, k[:, :, :2]], 2))
+    truncate_cache(cache, 4)
+    assert [cache.get_seq_length(i) for i in range(2)] == [4, 4]
+    cache.crop(-1)
+    assert cache.layers[1].values.shape == (1, 1, 3, 16)
+    big = torch.randn(1, 1, 2000, 16, dtype=torch.float64)
+    cache.update(big, big, 0)  # grows past the initial capacity, keeping the committed rows
+    assert cache.get_seq_length(0) == 2003 and torch.equal(cache.layers[0].keys[:, :, :3], k[:, :, :3])
+    with pytest.raises(ValueError):
+        cache.update(k.float(), v.float(), 0)  # the cache holds float64
