@@ -197,13 +197,15 @@ def cpu_baseline_sample() -> dict:
 
 
 def run_decode(args):
-    """--decode: parallel block decoding of the 0.6B shape (random init) on cuda:0. For each batch
-    size, prompts of U[128, 512] Zipf ids, 512 new tokens, K = 32:
+    """--decode: parallel block decoding of the 0.6B shape (random init). For each batch size,
+    prompts of U[128, 512] Zipf ids, 512 new tokens, K = 32:
     - plain: the diffusion drafts of a random-init model are rejected, so every cycle commits one
       token (TPF below 1 is expected and is not a quality figure);
     - scripted: the drafts are the greedy continuation with seeded edits (the device analogue of
       the reference tests' ScriptedBackend), which exercises accept / rollback; the output must
       equal the plain run's tokens.
+    Under torchrun every rank decodes its own prompts on its own GPU (replicas, no collective on
+    the data path); `value` is the tokens of all ranks over the slowest rank's device time.
     One JSON line per configuration; achieved HBM bandwidth per pass = (weights + the KV read at
     the mean context) / time per pass. A CPU line times the reference algorithm (the oracle port,
     fp32) on a bounded sample."""
@@ -213,8 +215,8 @@ def run_decode(args):
     from orthrus_training_b200.modeling_orthrus import OrthrusLM, copy_diff_from_ar
     from orthrus_training_b200.synthetic import zipf_ids
 
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
     dtype = torch.bfloat16 if args.decode_dtype == "bf16" else torch.float32
     torch.manual_seed(2)
     cfg = qwen3_06b_config()
@@ -230,44 +232,68 @@ def run_decode(args):
                                                                  "q_norm", "k_norm"))) * esize
     kv_per_token = 2 * L * Hkv * hd * esize
     pk = peaks()
+
+    def timed_decode(prompts, **kw):
+        barrier(world)
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        res = block_decode(model, prompts, new, **kw)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return res, e0.elapsed_time(e1) / 1e3
+
+    def total_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        import torch.distributed as dist
+
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        return float(t.item())
+
     with torch.inference_mode():
         block_decode(model, [[1, 2, 3, 4] * 40], 16)  # kernel set-up outside the timed runs
     for batch in args.decode_batch:
-        rng = np.random.default_rng(2 + batch)
+        rng = np.random.default_rng(2 + batch + 1000 * rank)
         prompts = [zipf_ids(rng, int(rng.integers(128, 513)), REAL_VOCAB).tolist() for _ in range(batch)]
         with torch.inference_mode():
-            plain = block_decode(model, prompts, new)
+            plain, plain_s = timed_decode(prompts)
             ref = plain.tokens
             # scripted drafts: the true continuation after each anchor, 5 % of tokens edited
             table = torch.zeros(batch, new, K - 1, dtype=torch.int64)
-            erng = np.random.default_rng(7 + batch)
+            erng = np.random.default_rng(7 + batch + 1000 * rank)
             for b, toks in enumerate(ref):
                 for i in range(new):
                     nxt = toks[i + 1: i + K]
                     row = [t if erng.random() >= 0.05 else int(erng.integers(0, REAL_VOCAB)) for t in nxt]
                     table[b, i, : len(row)] = torch.tensor(row, dtype=torch.int64)
-            scripted = block_decode(model, prompts, new, draft_table=table.to(dev))
-        lossless = scripted.tokens == ref
-        for name, res in (("plain", plain), ("scripted", scripted)):
-            dec_s = res.seconds - res.prefill_seconds
-            gen = res.total_tokens
+            scripted, scripted_s = timed_decode(prompts, draft_table=table.to(dev))
+        lossless = total_over_ranks(float(scripted.tokens == ref)) == world
+        for name, res, dev_s in (("plain", plain, plain_s), ("scripted", scripted, scripted_s)):
             # one batched cycle = a draft pass and a verify pass; time the replayed cycles only
-            per_pass = res.steady_seconds / max(2 * res.steady_cycles, 1)
+            per_pass = max_over_ranks(res.steady_seconds / max(2 * res.steady_cycles, 1), world)
+            seconds = max_over_ranks(dev_s - res.prefill_seconds, world)
+            gen = total_over_ranks(float(res.total_tokens))
+            passes = total_over_ranks(float(sum(res.passes)))
             mean_ctx = sum(len(p) for p in prompts) / batch + new / 2
             pass_bytes = weight_bytes + kv_per_token * mean_ctx * batch
             gbs = pass_bytes / per_pass / 1e9
-            emit(json.dumps({
+            line = {
                 "metric": "decode tok/s (Qwen3-0.6B-shape Orthrus block decode, greedy)", "mode": name,
-                "value": round(gen / dec_s, 1), "unit": "generated tok/s", "batch": batch,
-                "new_tokens": new, "K": K, "dtype": args.decode_dtype, "tpf": round(res.tpf, 3),
+                "value": round(gen / seconds, 1), "unit": "generated tok/s", "n_gpus": world,
+                "scaling": "weak", "batch_per_gpu": batch, "new_tokens": new, "K": K,
+                "dtype": args.decode_dtype, "tpf": round(gen / max(passes, 1), 3),
                 "mean_accepted": round(sum(sum(a) for a in res.accepted) / max(sum(res.cycles), 1), 3),
                 "ms_per_pass": round(per_pass * 1e3, 4),
                 "hbm": {"bytes_per_pass": int(pass_bytes), "achieved_gbs": round(gbs, 1),
                         "peak_gbs": pk["hbm_gbs"], "frac": round(gbs / pk["hbm_gbs"], 4)},
                 "lossless_vs_plain_greedy": bool(lossless) if name == "scripted" else True,
-                "prefill_s": round(res.prefill_seconds, 3), "data": "synthetic Zipf(1.1) prompts, random-init weights",
-            }))
-    if not args.no_cpu_baseline:
+                "timing": "CUDA events around each rank's decode call (prefill excluded), max over ranks",
+                "data": "synthetic Zipf(1.1) prompts, random-init weights",
+            }
+            if rank == 0:
+                emit(json.dumps(line))
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle as O
 
         threads = os.cpu_count() or 1
@@ -283,7 +309,11 @@ def run_decode(args):
                           "value": round(8 / sec, 3), "unit": "generated tok/s", "cores": threads,
                           "kind": "port", "sample": f"batch 1, 128-token prompt, 8 new tokens, K={BLOCK}, "
                                                      f"fp32 diffusion_generate of the CPU port ({sec:.1f} s)"}))
+    if world > 1:
+        import torch.distributed as dist
 
+        dist.barrier()
+        dist.destroy_process_group()
 
 # --- isolated kernel cases (--kernel-case) -----------------------------------------------------
 #
@@ -299,6 +329,8 @@ def run_decode(args):
 #   prologue q/k RMSNorm + RoPE + head-major scatter of the teacher's q|k|v projection, fwd + bwd
 #   linear   the projections of a layer at 16384 rows through torch (cuBLAS) and through this
 #            library's tcgen05 kernels                                    (:136-149)
+#   linear2  every projection GEMM of the step (forward with residual, dX, dW) through cuBLAS and
+#            through the CTA-pair kernel orthrus_gemm2_bf16
 #   sweep    dual-view attention fwd + bwd over L in {1024..8192}, K in {16, 32, 64}, A in
 #            {8, 32, 64} (batch filling 16384 query tokens, at most 65536 keys per head), and the
 #            fused LM head + KL over N in {4096, 16384, 65536} student rows
@@ -407,6 +439,36 @@ def kernel_case(case: str, iters: int, warmup: int) -> dict:
             ("down_residual_cublas", lambda: torch.addmm(x, a, w_d.t()), fl(d, ff), "tflops"),
             ("down_residual_fused", lambda: ops.linear(a, w_d, residual=x), fl(d, ff), "tflops"),
         ]
+    elif case == "linear2":
+        # every cuBLAS projection of the step against the CTA-pair kernel (forward with the
+        # residual, dX = dY W, dW = dY^T X), teacher rows 16384 and trainable-view rows 8192
+        d, ff, hq, qkv_n = 1024, 3072, HQ * HD, (HQ + 2 * HKV) * HD
+        T_, S_ = B * L, B * A * K
+        w_o, w_d = rnd(d, hq, scale=0.02), rnd(d, ff, scale=0.02)
+        w_gu, w_qkv = rnd(2 * ff, d, scale=0.03), rnd(qkv_n, d, scale=0.03)
+        xt_o, xt_a, rt = rnd(T_, hq), rnd(T_, ff), rnd(T_, d)
+        xs_o, xs_a, rs = rnd(S_, hq), rnd(S_, ff), rnd(S_, d)
+        dys, dgu, dqkv, hs = rnd(S_, d), rnd(S_, 2 * ff), rnd(S_, qkv_n), rnd(S_, d)
+        fl = lambda m, n, k: 2.0 * m * n * k  # noqa: E731
+        pairs = [
+            ("o_residual_16384", lambda: torch.addmm(rt, xt_o, w_o.t()),
+             lambda: ops.gemm2(xt_o, w_o, residual=rt), fl(T_, d, hq)),
+            ("down_residual_16384", lambda: torch.addmm(rt, xt_a, w_d.t()),
+             lambda: ops.gemm2(xt_a, w_d, residual=rt), fl(T_, d, ff)),
+            ("o_residual_8192", lambda: torch.addmm(rs, xs_o, w_o.t()),
+             lambda: ops.gemm2(xs_o, w_o, residual=rs), fl(S_, d, hq)),
+            ("down_residual_8192", lambda: torch.addmm(rs, xs_a, w_d.t()),
+             lambda: ops.gemm2(xs_a, w_d, residual=rs), fl(S_, d, ff)),
+            ("down_dx_8192", lambda: dys @ w_d, lambda: ops.gemm2(dys, w_d, b_t=True), fl(S_, ff, d)),
+            ("gate_up_dx_8192", lambda: dgu @ w_gu, lambda: ops.gemm2(dgu, w_gu, b_t=True), fl(S_, d, 2 * ff)),
+            ("o_dx_8192", lambda: dys @ w_o, lambda: ops.gemm2(dys, w_o, b_t=True), fl(S_, hq, d)),
+            ("o_dw_8192", lambda: dys.t() @ xs_o, lambda: ops.gemm2(dys, xs_o, a_t=True, b_t=True), fl(d, hq, S_)),
+            ("qkv_dx_8192", lambda: dqkv @ w_qkv, lambda: ops.gemm2(dqkv, w_qkv, b_t=True), fl(S_, d, qkv_n)),
+            ("qkv_dw_8192", lambda: dqkv.t() @ hs, lambda: ops.gemm2(dqkv, hs, a_t=True, b_t=True),
+             fl(qkv_n, d, S_)),
+        ]
+        for name, ref_fn, own_fn, work in pairs:
+            timed += [(name + "_cublas", ref_fn, work, "tflops"), (name + "_pair", own_fn, work, "tflops")]
     else:
         raise ValueError(f"unknown kernel case {case!r}")
     out = {}
@@ -482,7 +544,7 @@ def run_kernel_case(args) -> None:
 def step_roofline(cfg, kernels: dict, steps: int, ms_per_step: float, pk: dict) -> dict:
     """The whole step against its algorithmic work per GPU: projection GEMMs of the teacher
     (forward over every token) and of the diffusion view (forward, dX, and dW of the twins only),
-    plus the attention and LM-head FLOPs the kernels counted in the timed region."""
+    plus the attention and LM-head FLOPs the kernels counted in the breakdown pass."""
     d, inter, L = cfg.hidden_size, cfg.intermediate_size, cfg.num_hidden_layers
     qkv = (cfg.num_attention_heads + 2 * cfg.num_key_value_heads) * cfg.head_dim * d
     o = d * cfg.num_attention_heads * cfg.head_dim
@@ -490,7 +552,8 @@ def step_roofline(cfg, kernels: dict, steps: int, ms_per_step: float, pk: dict) 
     teacher_tokens, student_tokens = ROWS * SEQ, ROWS * ANCHORS * BLOCK
     linear = 2.0 * L * (teacher_tokens * per_layer + 2 * student_tokens * per_layer
                         + student_tokens * (qkv + o))
-    kernel_flops = sum(v["flops"] for v in kernels.values()) / steps
+    # the projections are counted in `linear` above, whichever kernel ran them
+    kernel_flops = sum(v["flops"] for k, v in kernels.items() if k != "projections") / steps
     total = linear + kernel_flops
     achieved = total / (ms_per_step / 1e3) / 1e12
     return {"tflop_per_step": round(total / 1e12, 2), "achieved": round(achieved, 1),
@@ -564,8 +627,7 @@ def run_ours(args):
         trainer.step([(ids_dev, mask_dev)])
     barrier(world)
 
-    # device-resident inputs, kernel timing on
-    ops.TIMER = ops.KernelTimer()
+    # device-resident inputs: the headline number, nothing else recorded in the timed region
     launches0 = _lib.launch_count()
     with ClockSampler(local) as clocks:
         barrier(world)
@@ -577,9 +639,38 @@ def run_ours(args):
         barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1), world)
     launches = (_lib.launch_count() - launches0) // max(args.steps, 1)
+    loss = float(out["loss"])
+
+    # the same steps again with CUDA events around every timed entry point (on its launching
+    # stream) for the per-kernel breakdown; recording the events adds host work, so this pass is
+    # kept out of the headline number
+    ops.TIMER = ops.KernelTimer()
+    barrier(world)
+    for _ in range(args.steps):
+        trainer.step([(ids_dev, mask_dev)])
+    barrier(world)
     kernels = ops.TIMER.summary()
     ops.TIMER = None
-    loss = float(out["loss"])
+
+    comm = None
+    if world > 1:
+        # the same steps without the gradient all-reduce: the difference is the communication the
+        # backward does not hide (every rank skips it, so all ranks still take the same collectives)
+        trainer.buckets.world = 1
+        barrier(world)
+        c0, c1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        c0.record()
+        for _ in range(args.steps):
+            trainer.step([(ids_dev, mask_dev)])
+        c1.record()
+        barrier(world)
+        trainer.buckets.world = world
+        ms_nocomm = max_over_ranks(c0.elapsed_time(c1), world)
+        grad_bytes = sum(p.numel() * p.element_size() for p in trainer.params)
+        comm = {"ms_per_step_without_allreduce": round(ms_nocomm / args.steps, 3),
+                "exposed_ms_per_step": round((ms - ms_nocomm) / args.steps, 3),
+                "allreduce_bytes_per_step": grad_bytes, "collective": "NCCL all-reduce (AVG) of the twin "
+                "gradients, one bucket per layer, launched from grad hooks during the backward"}
 
     # end to end through the public API: rows from pinned host memory, loss read back each step
     barrier(world)
@@ -634,6 +725,8 @@ def run_ours(args):
         "loss": round(loss, 5),
         "clocks": clocks.summary(),
     }
+    if comm is not None:
+        line["comm"] = comm
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample()
     err = _lib.device_error(local)
@@ -673,7 +766,7 @@ def main():
     ap.add_argument("--decode-new", type=int, default=512)
     ap.add_argument("--decode-dtype", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--kernel-case", default=None,
-                    choices=["causal", "dual", "dualbwd", "lmhead", "prologue", "linear", "sweep"],
+                    choices=["causal", "dual", "dualbwd", "lmhead", "prologue", "linear", "linear2", "sweep"],
                     help="time one hot entry point alone (--steps calls after --warmup)")
     args = ap.parse_args()
     if args.warmup < 3 and args.kernel_case is None:

@@ -75,6 +75,24 @@ int orthrus_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, vo
                       int64_t M, int64_t N, int64_t K, int b_kn, int c_f32, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* Projection GEMM on CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles over two SMs):
+ * C[M, N] (pitch ldc) = A @ B^T, or R + A @ B^T with epilogue ORTHRUS_GEMM2_RESIDUAL (one
+ * rounding, R [M, N] pitch ldr, not aliasing C). A is [M, K] row-major (a_mn = 0) or stored
+ * transposed as [K, M] (a_mn = 1); B is [N, K] (b_mn = 0) or stored transposed as [K, N]
+ * (b_mn = 1). All bf16 with fp32 accumulation; pitches multiples of 8 elements, N a multiple of
+ * 32, pointers 16-byte aligned; the residual form takes a row-major A.
+ * Replaces the F.linear projections of the training step and their autograd backward
+ * (orthrus/objective.py:136-149,160-165): y = x W^T (+ residual), dX = dY W (b_mn = 1),
+ * dW = dY^T X (a_mn = b_mn = 1). A problem whose tiles fill less than one wave of SM pairs is
+ * split over K into fp32 partials in the workspace (orthrus_gemm2_workspace_bytes, 0 when not
+ * split) and reduced in a fixed order, so results do not depend on timing. */
+#define ORTHRUS_GEMM2_STORE 0
+#define ORTHRUS_GEMM2_RESIDUAL 1
+size_t orthrus_gemm2_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int orthrus_gemm2_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
+                       void* C, int64_t ldc, const void* R, int64_t ldr, int64_t M, int64_t N,
+                       int64_t K, int epilogue, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Projection GEMM with the layer's elementwise tail in the epilogue, bf16 in and out:
  *   ORTHRUS_LINEAR_STORE     y[M, N] = x[M, K] @ w[N, K]^T                      (F.linear)
  *   ORTHRUS_LINEAR_RESIDUAL  y = residual + x @ w^T, fp32 sum rounded once      (torch.addmm)

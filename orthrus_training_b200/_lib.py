@@ -28,6 +28,9 @@ _SIGNATURES = {
     "orthrus_gemm_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
     "orthrus_gemm_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int64, c_int64, c_int64,
                                   c_int, c_int, _P, c_size_t, _P]),
+    "orthrus_gemm2_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
+    "orthrus_gemm2_bf16": (c_int, [_P, c_int64, c_int, _P, c_int64, c_int, _P, c_int64, _P, c_int64,
+                                   c_int64, c_int64, c_int64, c_int, _P, c_size_t, _P]),
     "orthrus_linear_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, _P, c_int64, c_int64, c_int64,
                                     c_int64, c_int, _P]),
     "orthrus_linear_swiglu_keep_bf16": (c_int, [_P, _P, c_int64, c_int64, c_int64, _P, _P, _P]),

@@ -11,6 +11,7 @@
 #include "decode.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
+#include "gemm2_tc.cuh"
 #include "linear_tc.cuh"
 #include "lmhead_kl.cuh"
 #include "qkv_prep.cuh"
@@ -60,6 +61,15 @@ int orthrus_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, vo
                       void* stream) {
   return gemm_bf16_impl(A, lda, B, ldb, C, ldc, M, N, K, b_kn, c_f32, workspace, workspace_bytes,
                         as_stream(stream));
+}
+
+size_t orthrus_gemm2_workspace_bytes(int64_t M, int64_t N, int64_t K) { return gemm2_ws_bytes(M, N, K); }
+
+int orthrus_gemm2_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn, void* C,
+                       int64_t ldc, const void* R, int64_t ldr, int64_t M, int64_t N, int64_t K, int epilogue,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  return gemm2_bf16_impl(A, lda, a_mn, B, ldb, b_mn, C, ldc, R, ldr, M, N, K, epilogue, workspace,
+                         workspace_bytes, as_stream(stream));
 }
 
 int orthrus_linear_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* residual, void* y,

@@ -110,6 +110,22 @@ inline bool make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner
   return r == CUDA_SUCCESS;
 }
 
+// 2-D fp32 tensor map over a row-major [outer, inner] matrix (pitch elements), 128-byte swizzle
+// (box_inner * 4 must be 128).
+inline bool make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch,
+                             uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch * 4};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // 3-D bf16 tensor map over [d2][d1][d0] with element strides s1 (between d1 rows) and s2.
 inline bool make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                               uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1) {

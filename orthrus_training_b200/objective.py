@@ -13,8 +13,11 @@ Same functions, signatures and return values as the reference module. Both views
 - KL: ``FusedLinearForwardKL`` over the fused LM-head + log-softmax + KL kernels, which also emit the
   per-offset KL / agreement sums (orthrus/objective.py:298-392,440-452).
 
-Projection GEMMs of the training step use torch (cuBLAS) matmuls; every attention, norm + RoPE,
-LM-head and KL computation is a kernel of this package. There is no CPU path.
+Every projection GEMM of the bf16 training step (forward, dX and dW) runs on this package's tcgen05
+kernels: the persistent one-CTA kernel where an epilogue fuses the q/k prologue or SwiGLU, the
+CTA-pair kernel (orthrus_gemm2_bf16) for the rest; every attention, norm + RoPE, LM-head and KL
+computation is a kernel of this package as well. The fp32 path keeps torch matmuls for its
+projections (exact fp32 parity runs). There is no CPU path.
 """
 
 from __future__ import annotations
@@ -132,7 +135,7 @@ class _GateUpSwiGLU(torch.autograd.Function):
     def backward(ctx, dact):
         gate_up, w = ctx.saved_tensors
         dgu = ops.silu_mul_backward(gate_up, dact.contiguous())
-        return dgu @ w, None
+        return _dx(dgu, w), None
 
 
 def _rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
@@ -140,6 +143,58 @@ def _rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor
     if weight.requires_grad:
         raise ValueError("the RMSNorm weights of the dual-view model are frozen")
     return _RMSNorm.apply(x, weight, eps)
+
+
+def _pair_gemm_ok(*tensors) -> bool:
+    """Whether the CTA-pair GEMM takes these operands (bf16, sizes multiples of 32)."""
+    return all(t.dtype == torch.bfloat16 and t.shape[-1] % 32 == 0 for t in tensors)
+
+
+def _add_projection(x: torch.Tensor, a: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """x + a @ w^T (torch.addmm(x, a, w.t())) without autograd, on the CTA-pair GEMM with the
+    residual in its epilogue for bf16."""
+    if _pair_gemm_ok(x, a, w):
+        return ops.gemm2(a, w, residual=x)
+    return torch.addmm(x, a, w.t())
+
+
+class _ProjectionResidual(torch.autograd.Function):
+    """x + a @ w^T (orthrus/objective.py:160-165 o projection, :146-149 down projection) on the
+    CTA-pair GEMM: the forward carries the residual in its epilogue; the backward is dx = dy,
+    da = dy @ w and, for a trainable w, dw = dy^T @ a (the two GEMMs autograd runs for
+    torch.addmm), on the same kernel."""
+
+    @staticmethod
+    def forward(ctx, x, a, w):
+        ctx.save_for_backward(a, w)
+        return ops.gemm2(a, w, residual=x)
+
+    @staticmethod
+    def backward(ctx, dy):
+        a, w = ctx.saved_tensors
+        dy = dy.contiguous()
+        da = ops.gemm2(dy, w, b_t=True) if ctx.needs_input_grad[1] else None
+        dw = ops.gemm2(dy, a, a_t=True, b_t=True) if ctx.needs_input_grad[2] else None
+        return dy, da, dw
+
+
+def _projection_residual(x: torch.Tensor, a: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    if _pair_gemm_ok(x, a, w):
+        return _ProjectionResidual.apply(x, a, w)
+    return torch.addmm(x, a, w.t())
+
+
+def _dx(dy: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """dy @ w: the input gradient of a projection with weight w [N, K]."""
+    dy = dy.contiguous()
+    return ops.gemm2(dy, w, b_t=True) if _pair_gemm_ok(dy, w) else dy @ w
+
+
+def _dw(dy: torch.Tensor, a: torch.Tensor) -> torch.Tensor:
+    """dy^T @ a: the weight gradient of a projection of the rows a."""
+    dy = dy.contiguous()
+    return ops.gemm2(dy, a, a_t=True, b_t=True) if _pair_gemm_ok(dy, a) and dy.shape[1] % 8 == 0 \
+        else dy.t() @ a
 
 
 class DualViewAttention(torch.autograd.Function):
@@ -206,8 +261,8 @@ class DualViewAttentionFused(torch.autograd.Function):
                                          scale=hd ** -0.5)
         dqkv, dqw, dkw = ops.qkv_prep_backward(qkv, positions, inv, qn, kn, rstd, dq, dk2, dv2, B,
                                                Q, Hq, Hkv, hd, D)
-        dh = dqkv @ w
-        dw = dqkv.t() @ h
+        dh = _dx(dqkv, w)
+        dw = _dw(dqkv, h)
         return (dh, dw, dqw.to(qn.dtype), dkw.to(kn.dtype), None, None, None, None, None, None, None,
                 None)
 
@@ -229,8 +284,8 @@ def _teacher_layer(backbone, i, x, pos, B, L, inv, rope=None):
         q, k, v, _ = ops.qkv_prep(qkv, pos, inv, attn.q_norm.weight, attn.k_norm.weight, B, L, Hq,
                                   Hkv, hd, D, eps)
     o, _ = ops.attention_fwd(q, k, v, mask=MASK_CAUSAL, hd=hd, scale=hd ** -0.5, want_lse=False)
-    # residual adds ride in the GEMM epilogue (beta = 1)
-    x = torch.addmm(x, o.view(B * L, Hq * hd), attn.o_proj.weight.t())
+    # residual adds ride in the GEMM epilogue
+    x = _add_projection(x, o.view(B * L, Hq * hd), attn.o_proj.weight)
     h = ops.rms_norm(x, layer.post_attention_layernorm.weight, eps)
     w_gu = layer.mlp.packed_gate_up()
     if ops.fused_linear_supported(h, w_gu, w_gu.shape[0] // 2):
@@ -238,7 +293,7 @@ def _teacher_layer(backbone, i, x, pos, B, L, inv, rope=None):
         act = ops.linear_swiglu(h, w_gu)
     else:
         act = ops.silu_mul(h @ w_gu.t())
-    x = torch.addmm(x, act, layer.mlp.down_proj.weight.t())
+    x = _add_projection(x, act, layer.mlp.down_proj.weight)
     return x, k, v
 
 
@@ -258,14 +313,14 @@ def _diffusion_layer(backbone, i, x, ar_k, ar_v, positions, anchors, inv, B, Q, 
         qkv = F.linear(h, w_qkv)
         o = DualViewAttention.apply(qkv, attn.q_norm_diff.weight, attn.k_norm_diff.weight, ar_k, ar_v,
                                     positions, anchors, inv, meta)
-    x = torch.addmm(x, o, attn.o_proj_diff.weight.t())
+    x = _projection_residual(x, o, attn.o_proj_diff.weight)
     h = _rms_norm(x, layer.post_attention_layernorm.weight, eps)
     w_gu = layer.mlp.packed_gate_up()
     if ops.fused_linear_supported(h, w_gu, w_gu.shape[0] // 2):
         act = _GateUpSwiGLU.apply(h, w_gu)
     else:
         act = _SwiGLU.apply(F.linear(h, w_gu))
-    return torch.addmm(x, act, layer.mlp.down_proj.weight.t())
+    return _projection_residual(x, act, layer.mlp.down_proj.weight)
 
 
 def _backbone(model):

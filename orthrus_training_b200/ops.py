@@ -85,6 +85,39 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, b_kn: bool = False, out_dtype=None
     return c
 
 
+def gemm2(a: torch.Tensor, b: torch.Tensor, *, a_t: bool = False, b_t: bool = False,
+          residual: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 GEMM on CTA pairs (orthrus_gemm2_bf16): C = A @ B^T (+ residual), where A is `a`
+    [M, K], or `a`^T when a_t (a stored as [K, M]), and B is `b` [N, K], or `b`^T when b_t (b
+    stored as [K, N]). So y = x W^T is gemm2(x, W), dX = dY W is gemm2(dY, W, b_t=True) and
+    dW = dY^T X is gemm2(dY, X, a_t=True, b_t=True)."""
+    _require_cuda(a, b, residual)
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16 or a.dim() != 2 or b.dim() != 2:
+        raise ValueError("gemm2 takes 2-D bf16 operands")
+    a, b = a.contiguous(), b.contiguous()
+    M, K = (a.shape[1], a.shape[0]) if a_t else a.shape
+    N, Kb = (b.shape[1], b.shape[0]) if b_t else b.shape
+    if Kb != K:
+        raise ValueError(f"gemm2 shape mismatch: A {tuple(a.shape)} (t={a_t}), B {tuple(b.shape)} (t={b_t})")
+    c = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
+    epi = 0
+    if residual is not None:
+        residual = residual.contiguous()
+        if residual.shape != (M, N) or residual.dtype != torch.bfloat16:
+            raise ValueError("residual must be bf16 [M, N]")
+        epi = 1
+    lib = L.lib()
+    ws = _workspace(lib.orthrus_gemm2_workspace_bytes(M, N, K), a.device)
+    t0 = TIMER.begin() if TIMER is not None else None
+    L.check(lib.orthrus_gemm2_bf16(a.data_ptr(), a.stride(0), int(a_t), b.data_ptr(), b.stride(0), int(b_t),
+                                   c.data_ptr(), N, L.ptr(residual), N if residual is not None else 0,
+                                   M, N, K, epi, L.ptr(ws), 0 if ws is None else ws.numel(),
+                                   L.stream_of(a.device)), "gemm2_bf16")
+    if t0 is not None:
+        TIMER.end("projections", t0, 2.0 * M * N * K)
+    return c
+
+
 LINEAR_STORE, LINEAR_RESIDUAL, LINEAR_SWIGLU = 0, 1, 2
 
 

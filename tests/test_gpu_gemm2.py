@@ -1,0 +1,54 @@
+"""The projection GEMM on CTA pairs (orthrus_gemm2_bf16, tcgen05 cta_group::2) against fp32 torch:
+every operand layout of the forward, dX and dW forms, the residual epilogue, ragged sizes and
+run-to-run determinism."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _rand(*shape, seed, scale=1.0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return (torch.randn(*shape, device=DEV, generator=g) * scale).bfloat16()
+
+
+# (1024, 2048, 8192) and (256, 512, 4096) fill less than one wave of SM pairs and are split over K
+@pytest.mark.parametrize("M,N,K", [(512, 256, 128), (300, 96, 200), (1000, 1024, 3072), (256, 512, 64),
+                                   (2048, 1024, 2048), (1024, 2048, 8192), (256, 512, 4096)])
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, True), (True, False)])
+def test_gemm2_layouts_match_fp32(M, N, K, a_t, b_t):
+    from orthrus_training_b200 import ops
+
+    if a_t and M % 8:
+        pytest.skip("a transposed A needs M to be a multiple of 8")
+    a = _rand(*((K, M) if a_t else (M, K)), seed=M + K)
+    b = _rand(*((K, N) if b_t else (N, K)), seed=N + 3 * K, scale=0.05)
+    got = ops.gemm2(a, b, a_t=a_t, b_t=b_t)
+    A = a.float().t() if a_t else a.float()
+    B = b.float() if b_t else b.float().t()
+    ref = A @ B
+    err = (got.float() - ref).abs().max().item()
+    assert err <= 8e-3 * ref.abs().max().item(), err
+    again = ops.gemm2(a, b, a_t=a_t, b_t=b_t)
+    assert torch.equal(got, again)
+
+
+@pytest.mark.parametrize("M,N,K,b_t", [(512, 256, 128, False), (300, 96, 200, True), (2048, 1024, 3072, False),
+                                       (256, 512, 4096, False)])
+def test_gemm2_residual_epilogue(M, N, K, b_t):
+    from orthrus_training_b200 import _lib as lib_
+
+    if (M, N, K) == (256, 512, 4096):
+        assert lib_.lib().orthrus_gemm2_workspace_bytes(M, N, K) > 0  # the split-K path
+    from orthrus_training_b200 import _lib, ops
+
+    a = _rand(M, K, seed=1)
+    b = _rand(*((K, N) if b_t else (N, K)), seed=2, scale=0.05)
+    r = _rand(M, N, seed=3)
+    got = ops.gemm2(a, b, b_t=b_t, residual=r)
+    ref = r.float() + a.float() @ (b.float() if b_t else b.float().t())
+    err = (got.float() - ref).abs().max().item()
+    assert err <= 8e-3 * ref.abs().max().item(), err
+    assert _lib.device_error(0) == 0
