@@ -88,6 +88,9 @@ int orthrus_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, vo
  * split) and reduced in a fixed order, so results do not depend on timing. */
 #define ORTHRUS_GEMM2_STORE 0
 #define ORTHRUS_GEMM2_RESIDUAL 1
+#define ORTHRUS_GEMM2_SWIGLU_BWD 2  /* R = [gate | up] [M, 2N] of the MLP forward (pitch ldr); C = [dgate | dup]
+                                      [M, 2N] (pitch ldc), from the accumulator dact = dY @ W_down, with the
+                                      arithmetic of orthrus_swiglu_bwd */
 size_t orthrus_gemm2_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int orthrus_gemm2_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
                        void* C, int64_t ldc, const void* R, int64_t ldr, int64_t M, int64_t N,
@@ -168,6 +171,12 @@ int orthrus_rmsnorm(const void* x, const void* w, int64_t rows, int d, float eps
  * Replaces the autograd backward of _rms_norm (orthrus/objective.py:128-133). */
 int orthrus_rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy,
                         int64_t rows, int d, void* dx, int dtype, void* stream);
+/* The same backward (bf16, d a multiple of 256) plus the gradient dres [rows, d] that reaches x
+ * through a residual connection, summed before the single rounding: dx = dres + dnorm. Replaces
+ * the sum autograd forms for x used both by the pre-norm and by the residual add of a Qwen3 layer
+ * (orthrus/objective.py:146-149,160-165). */
+int orthrus_rmsnorm_bwd_add(const void* x, const void* w, const float* rstd, const void* dy,
+                            const void* dres, int64_t rows, int d, void* dx, void* stream);
 
 /* SwiGLU activation of the fused [gate | up] projection gate_up [rows, 2 * inter]:
  * out [rows, inter] = silu(gate) * up (silu rounded to dtype first, as F.silu(gate) * up), and its

@@ -43,6 +43,7 @@ _SIGNATURES = {
     "orthrus_gemm_simt": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, c_int64, c_int64, c_int64,
                                   c_int, _P, c_size_t, _P]),
     "orthrus_rmsnorm": (c_int, [_P, _P, c_int64, c_int, c_float, _P, _P, c_int, _P]),
+    "orthrus_rmsnorm_bwd_add": (c_int, [_P, _P, _P, _P, _P, c_int64, c_int, _P, _P]),
     "orthrus_rmsnorm_bwd": (c_int, [_P, _P, _P, _P, c_int64, c_int, _P, c_int, _P]),
     "orthrus_swiglu_fwd": (c_int, [_P, c_int64, c_int, _P, c_int, _P]),
     "orthrus_swiglu_bwd": (c_int, [_P, _P, c_int64, c_int, _P, c_int, _P]),

@@ -568,6 +568,19 @@ extern "C" int orthrus_rmsnorm(const void* x, const void* w, int64_t rows, int d
   return ORTHRUS_OK;
 }
 
+extern "C" int orthrus_rmsnorm_bwd_add(const void* x, const void* w, const float* rstd, const void* dy,
+                                       const void* dres, int64_t rows, int d, void* dx, void* stream) {
+  ORTHRUS_CHECK_ARG(x && w && rstd && dy && dres && dx && rows >= 0 && d > 0 && d % 256 == 0);
+  ORTHRUS_CHECK_ARG(aligned16(x) && aligned16(w) && aligned16(dy) && aligned16(dres) && aligned16(dx));
+  if (rows == 0) return ORTHRUS_OK;
+  using T = __nv_bfloat16;
+  rmsnorm_bwd_vec_kernel<T><<<static_cast<unsigned>(ceil_div(rows, 8)), 256, 0, as_stream(stream)>>>(
+      static_cast<const T*>(x), static_cast<const T*>(w), rstd, static_cast<const T*>(dy), rows, d,
+      static_cast<T*>(dx), static_cast<const T*>(dres));
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
 extern "C" int orthrus_rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy, int64_t rows,
                                    int d, void* dx, int dtype, void* stream) {
   ORTHRUS_CHECK_ARG(x && w && rstd && dy && dx && rows >= 0 && d > 0);

@@ -12,7 +12,10 @@
 //   A MN-major [K, M] row-major, i.e. A^T stored (dy for dW = dy^T x)              dW
 //   B K-major  [N, K] row-major (the weight W for y = x W^T)                       forward
 //   B MN-major [K, N] row-major (W for dX = dy W; x for dW)                        dX, dW
-// Epilogues: store (bf16) and residual (bf16 R + acc, one rounding: torch.addmm(R, x, W^T)).
+// Epilogues: store (bf16); residual (bf16 R + acc, one rounding: torch.addmm(R, x, W^T)); and the
+// SwiGLU backward, where acc = dact = dy @ W_down of the MLP and R = [gate | up] [M, 2N] kept by the
+// forward: the epilogue writes C = [dgate | dup] [M, 2N] (the arithmetic and roundings of
+// swiglu_bwd_kernel), so dact never goes through HBM.
 //
 // Persistent: one cluster per SM pair loops over pair tiles (n fastest). 320 threads per CTA:
 //   warp 0     TMA producer (both CTAs): this CTA's A and B k-blocks of 64 into a 6-stage ring;
@@ -26,10 +29,11 @@
 #pragma once
 
 #include "sm100.cuh"
+#include "qkv_prep.cuh"
 
 namespace orthrus {
 
-enum Gemm2Epilogue { kGemm2Store = 0, kGemm2Residual = 1, kGemm2Partial = 2 };
+enum Gemm2Epilogue { kGemm2Store = 0, kGemm2Residual = 1, kGemm2Partial = 2, kGemm2SwiGLUBwd = 3 };
 
 struct Gemm2Tile {
   static constexpr int BM = 128;                  // rows per CTA (256 per pair)
@@ -246,6 +250,64 @@ __global__ void __launch_bounds__(Gemm2Tile::THREADS, 1)
             tma_store_commit();
           }
         }
+      } else if constexpr (EPI == kGemm2SwiGLUBwd) {
+        // 64 columns at a time: dgate through the staging tile to columns [n, n + 64) of C, then
+        // dup (kept packed in registers meanwhile) to columns [N + n, N + n + 64)
+#pragma unroll 1
+        for (int pair = 0; pair < 2; ++pair) {
+          reuse();
+          uint32_t dup[2][16];
+#pragma unroll 1
+          for (int cc = 0; cc < 2; ++cc) {
+            const int col0 = n0 + (4 * half + 2 * pair + cc) * 32;
+            float v[32], gv[32], uv[32];
+            if (row < g.M && col0 < g.N) {
+              const __nv_bfloat16* gsrc = R + static_cast<int64_t>(row) * ldr + col0;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {  // 16-byte loads
+                load_elems<__nv_bfloat16, 8>(gsrc + 8 * q, gv + 8 * q);
+                load_elems<__nv_bfloat16, 8>(gsrc + g.N + 8 * q, uv + 8 * q);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) gv[i] = uv[i] = 0.f;
+            }
+            tmem_ld32(base + (4 * half + 2 * pair + cc) * 32, v);
+            tmem_wait_ld();
+            float dg[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float d = __bfloat162float(__float2bfloat16_rn(v[i]));  // dact as the GEMM output
+              const float sg = 1.f / (1.f + expf(-gv[i]));
+              const float sl = __bfloat162float(__float2bfloat16_rn(gv[i] * sg));
+              const float ds = __bfloat162float(__float2bfloat16_rn(d * uv[i]));
+              dg[i] = ds * sg * (1.f + gv[i] * (1.f - sg));
+              v[i] = d * sl;  // dup
+            }
+#pragma unroll
+            for (int q = 0; q < 16; ++q) dup[cc][q] = pack_bf16x2(v[2 * q], v[2 * q + 1]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              st_shared_v4(stage + sw128_offset(lane, cc * 4 + q), pack_bf16x2(dg[8 * q], dg[8 * q + 1]),
+                           pack_bf16x2(dg[8 * q + 2], dg[8 * q + 3]), pack_bf16x2(dg[8 * q + 4], dg[8 * q + 5]),
+                           pack_bf16x2(dg[8 * q + 6], dg[8 * q + 7]));
+          }
+          const int col0 = n0 + (4 * half + 2 * pair) * 32;
+          flush(col0, row0);
+          reuse();
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              st_shared_v4(stage + sw128_offset(lane, cc * 4 + q), dup[cc][4 * q], dup[cc][4 * q + 1],
+                           dup[cc][4 * q + 2], dup[cc][4 * q + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < g.M && col0 < g.N) {
+            tma_store_2d(&tmC, staging + (warp - 2) * T::STAGING, g.N + col0, row0);
+            tma_store_commit();
+          }
+        }
       } else {
 #pragma unroll 1
       for (int pair = 0; pair < 2; ++pair) {
@@ -415,14 +477,18 @@ inline int gemm2_bf16_impl(const void* A, int64_t lda, int a_mn, const void* B, 
                            int64_t ldc, const void* R, int64_t ldr, int64_t M, int64_t N, int64_t K, int epilogue,
                            void* ws, size_t ws_bytes, cudaStream_t stream) {
   ORTHRUS_CHECK_ARG(A && B && C && M >= 0 && N > 0 && K > 0);
-  ORTHRUS_CHECK_ARG(epilogue == kGemm2Store || (epilogue == kGemm2Residual && R != nullptr && R != C));
+  // ABI epilogue 2 is the SwiGLU backward: R = [gate | up] and C = [dgate | dup], both [M, 2N]
+  const bool swiglu_bwd = epilogue == 2;
+  ORTHRUS_CHECK_ARG(epilogue == kGemm2Store || ((epilogue == kGemm2Residual || swiglu_bwd) && R != nullptr && R != C));
+  ORTHRUS_CHECK_ARG(!swiglu_bwd || (!a_mn && N % 64 == 0 && ldr >= 2 * N && ldc >= 2 * N));
   ORTHRUS_CHECK_ARG(lda % 8 == 0 && ldb % 8 == 0 && ldc % 8 == 0 && (R == nullptr || ldr % 8 == 0));
   ORTHRUS_CHECK_ARG(lda >= (a_mn ? M : K) && ldb >= (b_mn ? N : K) && ldc >= N && (R == nullptr || ldr >= N));
   ORTHRUS_CHECK_ARG(N % 32 == 0 && K % 8 == 0 && (!a_mn || M % 8 == 0));
   ORTHRUS_CHECK_ARG(aligned16(A) && aligned16(B) && aligned16(C) && (R == nullptr || aligned16(R)));
   ORTHRUS_CHECK_ARG(M < (1ll << 31) && N < (1ll << 30) && K < (1ll << 31));
   if (M == 0) return ORTHRUS_OK;
-  if (ws_bytes < gemm2_ws_bytes(M, N, K) || (gemm2_ws_bytes(M, N, K) > 0 && ws == nullptr)) return ORTHRUS_EWORKSPACE;
+  if (!swiglu_bwd && (ws_bytes < gemm2_ws_bytes(M, N, K) || (gemm2_ws_bytes(M, N, K) > 0 && ws == nullptr)))
+    return ORTHRUS_EWORKSPACE;
   CUtensorMap ta, tb, tc;
   const bool ok_a = a_mn ? make_tmap_2d_bf16(&ta, A, M, K, lda, 64, 64) : make_tmap_2d_bf16(&ta, A, K, M, lda, 64, 128);
   const bool ok_b = b_mn ? make_tmap_2d_bf16(&tb, B, N, K, ldb, 64, 64) : make_tmap_2d_bf16(&tb, B, K, N, ldb, 64, 128);
@@ -432,7 +498,7 @@ inline int gemm2_bf16_impl(const void* A, int64_t lda, int a_mn, const void* B, 
   g.N = static_cast<int>(N);
   g.K = static_cast<int>(K);
   g.npairs = static_cast<int>(ceil_div(N, 256));
-  g.splits = gemm2_splits(M, N, K, num_sms() / 2);
+  g.splits = swiglu_bwd ? 1 : gemm2_splits(M, N, K, num_sms() / 2);
   g.kb_split = static_cast<int>(ceil_div(ceil_div(K, 64), g.splits));
   g.m_pad = static_cast<int>(ceil_div(M, 256) * 256);
   const int64_t tiles = ceil_div(M, 256) * g.npairs * g.splits;
@@ -454,7 +520,10 @@ inline int gemm2_bf16_impl(const void* A, int64_t lda, int a_mn, const void* B, 
     ORTHRUS_CHECK_LAUNCH();
     return ORTHRUS_OK;
   }
-  if (!make_tmap_2d_bf16(&tc, C, N, M, ldc, 64, 32)) return ORTHRUS_ECUDA;
+  if (!make_tmap_2d_bf16(&tc, C, swiglu_bwd ? 2 * N : N, M, ldc, 64, 32)) return ORTHRUS_ECUDA;
+  if (swiglu_bwd)
+    return b_mn ? gemm2_launch<kGemm2SwiGLUBwd, false, true>(ta, tb, tc, g, r, ldr, stream)
+                : gemm2_launch<kGemm2SwiGLUBwd, false, false>(ta, tb, tc, g, r, ldr, stream);
   const int key = (epilogue == kGemm2Residual ? 4 : 0) | (a_mn ? 2 : 0) | (b_mn ? 1 : 0);
   switch (key) {
     case 0: return gemm2_launch<kGemm2Store, false, false>(ta, tb, tc, g, r, ldr, stream);

@@ -84,10 +84,13 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_vec_kernel(const T* __restric
 }
 
 // dx = rstd * (w dy - xhat * mean(w dy xhat)), xhat = x * rstd.
+// With dres (the gradient arriving at x through the residual path) it is added before the one
+// rounding: dx = dres + rstd * (...), the sum autograd would form for a tensor used twice.
 template <typename T>
 __global__ void __launch_bounds__(256) rmsnorm_bwd_vec_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                               const float* __restrict__ rstd, const T* __restrict__ dy,
-                                                              int64_t rows, int d, T* __restrict__ dx) {
+                                                              int64_t rows, int d, T* __restrict__ dx,
+                                                              const T* __restrict__ dres = nullptr) {
   constexpr int N = Vec16<T>::N;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + warp;
@@ -115,6 +118,12 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_vec_kernel(const T* __restric
     load16<T>(w + c, wv);
 #pragma unroll
     for (int i = 0; i < N; ++i) v[i] = rs * (g[i] * wv[i] - v[i] * rs * mean);
+    if (dres != nullptr) {
+      float a[N];
+      load16<T>(dres + r * d + c, a);
+#pragma unroll
+      for (int i = 0; i < N; ++i) v[i] += a[i];
+    }
     store16<T>(out + c, v);
   }
 }

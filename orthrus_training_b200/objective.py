@@ -197,6 +197,35 @@ def _dw(dy: torch.Tensor, a: torch.Tensor) -> torch.Tensor:
         else dy.t() @ a
 
 
+class _MLPBlock(torch.autograd.Function):
+    """The MLP half of a trainable-view layer, x + down(silu(gate(n(x))) * up(n(x))) with n the
+    post-attention RMSNorm (orthrus/objective.py:146-149), as one Function so that its backward
+    fuses what autograd would run as separate passes: the SwiGLU backward rides in the epilogue of
+    the dact = dy @ W_down GEMM (dact never reaches HBM), and the residual gradient dy is added in
+    the RMSNorm backward kernel. The MLP and norm weights are frozen: only dx is returned."""
+
+    @staticmethod
+    def forward(ctx, x, norm_w, w_gate_up, w_down, eps):
+        h, rstd = ops.rms_norm(x, norm_w, eps, want_rstd=True)
+        act, gate_up = ops.linear_swiglu(h, w_gate_up, keep_gate_up=True)
+        ctx.save_for_backward(x, norm_w, rstd, gate_up, w_gate_up, w_down)
+        return ops.gemm2(act, w_down, residual=x)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, norm_w, rstd, gate_up, w_gate_up, w_down = ctx.saved_tensors
+        dy = dy.contiguous()
+        dgu = ops.gemm2_swiglu_backward(dy, w_down, gate_up)
+        dh = _dx(dgu, w_gate_up)
+        return ops.rms_norm_backward(x, norm_w, rstd, dh, dres=dy), None, None, None, None
+
+
+def _mlp_block_ok(x, w_gu, w_down) -> bool:
+    F = w_gu.shape[0] // 2
+    return (_pair_gemm_ok(x, w_down) and ops.fused_linear_supported(x, w_gu, F) and F % 64 == 0
+            and x.shape[-1] % 256 == 0 and not w_gu.requires_grad and not w_down.requires_grad)
+
+
 class DualViewAttention(torch.autograd.Function):
     """Diffusion-view attention of one layer from the twin projection output.
 
@@ -314,13 +343,15 @@ def _diffusion_layer(backbone, i, x, ar_k, ar_v, positions, anchors, inv, B, Q, 
         o = DualViewAttention.apply(qkv, attn.q_norm_diff.weight, attn.k_norm_diff.weight, ar_k, ar_v,
                                     positions, anchors, inv, meta)
     x = _projection_residual(x, o, attn.o_proj_diff.weight)
+    w_gu, w_down = layer.mlp.packed_gate_up(), layer.mlp.down_proj.weight
+    if _mlp_block_ok(x, w_gu, w_down) and not layer.post_attention_layernorm.weight.requires_grad:
+        return _MLPBlock.apply(x, layer.post_attention_layernorm.weight, w_gu, w_down, eps)
     h = _rms_norm(x, layer.post_attention_layernorm.weight, eps)
-    w_gu = layer.mlp.packed_gate_up()
     if ops.fused_linear_supported(h, w_gu, w_gu.shape[0] // 2):
         act = _GateUpSwiGLU.apply(h, w_gu)
     else:
         act = _SwiGLU.apply(F.linear(h, w_gu))
-    return _projection_residual(x, act, layer.mlp.down_proj.weight)
+    return _projection_residual(x, act, w_down)
 
 
 def _backbone(model):

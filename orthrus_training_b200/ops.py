@@ -108,14 +108,28 @@ def gemm2(a: torch.Tensor, b: torch.Tensor, *, a_t: bool = False, b_t: bool = Fa
         epi = 1
     lib = L.lib()
     ws = _workspace(lib.orthrus_gemm2_workspace_bytes(M, N, K), a.device)
-    t0 = TIMER.begin() if TIMER is not None else None
     L.check(lib.orthrus_gemm2_bf16(a.data_ptr(), a.stride(0), int(a_t), b.data_ptr(), b.stride(0), int(b_t),
                                    c.data_ptr(), N, L.ptr(residual), N if residual is not None else 0,
                                    M, N, K, epi, L.ptr(ws), 0 if ws is None else ws.numel(),
                                    L.stream_of(a.device)), "gemm2_bf16")
-    if t0 is not None:
-        TIMER.end("projections", t0, 2.0 * M * N * K)
     return c
+
+
+def gemm2_swiglu_backward(dy: torch.Tensor, w_down: torch.Tensor, gate_up: torch.Tensor) -> torch.Tensor:
+    """[dgate | dup] [M, 2F] of the MLP from the gradient dy [M, d] of its output: the CTA-pair
+    GEMM dact = dy @ w_down (w_down [d, F]) with the SwiGLU backward of gate_up [M, 2F] in its
+    epilogue (silu_mul_backward(gate_up, dy @ w_down) without writing dact)."""
+    _require_cuda(dy, w_down, gate_up)
+    dy, w_down, gate_up = dy.contiguous(), w_down.contiguous(), gate_up.contiguous()
+    M, d = dy.shape
+    F = w_down.shape[1]
+    if w_down.shape[0] != d or gate_up.shape != (M, 2 * F) or F % 64 or dy.dtype != torch.bfloat16:
+        raise ValueError("gemm2_swiglu_backward takes bf16 dy [M, d], w_down [d, F], gate_up [M, 2F]")
+    dgu = torch.empty(M, 2 * F, dtype=torch.bfloat16, device=dy.device)
+    L.check(L.lib().orthrus_gemm2_bf16(dy.data_ptr(), d, 0, w_down.data_ptr(), F, 1, dgu.data_ptr(), 2 * F,
+                                       gate_up.data_ptr(), 2 * F, M, F, d, 2, None, 0, L.stream_of(dy.device)),
+            "gemm2_swiglu_bwd")
+    return dgu
 
 
 LINEAR_STORE, LINEAR_RESIDUAL, LINEAR_SWIGLU = 0, 1, 2
@@ -499,9 +513,22 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, want_rstd: bool 
 
 
 def rms_norm_backward(x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor,
-                      dy: torch.Tensor) -> torch.Tensor:
-    """dx of rms_norm (the weight is frozen)."""
+                      dy: torch.Tensor, dres: torch.Tensor | None = None) -> torch.Tensor:
+    """dx of rms_norm (the weight is frozen); with dres, dres + dx in one rounding (the gradient
+    of a tensor that also feeds a residual add)."""
     shape = x.shape
+    if dres is not None:
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        if x.dtype != torch.bfloat16 or shape[-1] % 256:
+            return rms_norm_backward(x, weight, rstd, dy) + dres
+        dy2 = dy.reshape(-1, shape[-1]).contiguous().to(x.dtype)
+        r2 = dres.reshape(-1, shape[-1]).contiguous().to(x.dtype)
+        w = weight.to(x.dtype).contiguous()
+        dx = torch.empty_like(x2)
+        L.check(L.lib().orthrus_rmsnorm_bwd_add(x2.data_ptr(), w.data_ptr(), rstd.data_ptr(), dy2.data_ptr(),
+                                                r2.data_ptr(), x2.shape[0], x2.shape[1], dx.data_ptr(),
+                                                L.stream_of(x.device)), "rmsnorm_bwd_add")
+        return dx.view(shape)
     x2 = x.reshape(-1, shape[-1]).contiguous()
     dy2 = dy.reshape(-1, shape[-1]).contiguous().to(x.dtype)
     w = weight.to(x.dtype).contiguous()

@@ -52,3 +52,29 @@ def test_gemm2_residual_epilogue(M, N, K, b_t):
     err = (got.float() - ref).abs().max().item()
     assert err <= 8e-3 * ref.abs().max().item(), err
     assert _lib.device_error(0) == 0
+
+
+@pytest.mark.parametrize("M,d,F", [(1000, 256, 512), (8192, 1024, 3072)])
+def test_swiglu_backward_epilogue_matches_the_separate_kernels(M, d, F):
+    """[dgate | dup] from the GEMM epilogue equals silu_mul_backward(gate_up, dy @ W_down) up to
+    the accumulation order of dact (one bf16 unit in its rounding)."""
+    from orthrus_training_b200 import _lib, ops
+
+    dy, w_down, gu = _rand(M, d, seed=11), _rand(d, F, seed=12, scale=0.05), _rand(M, 2 * F, seed=13)
+    got = ops.gemm2_swiglu_backward(dy, w_down, gu)
+    dact = (dy.float() @ w_down.float()).bfloat16()
+    ref = ops.silu_mul_backward(gu, dact).float()
+    err = (got.float() - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item(), err
+    assert _lib.device_error(0) == 0
+
+
+def test_rmsnorm_backward_adds_the_residual_gradient():
+    from orthrus_training_b200 import ops
+
+    x, w = _rand(777, 1024, seed=21), (1 + 0.1 * _rand(1024, seed=22).float()).bfloat16()
+    dy, dres = _rand(777, 1024, seed=23), _rand(777, 1024, seed=24)
+    _, rstd = ops.rms_norm(x, w, 1e-6, want_rstd=True)
+    got = ops.rms_norm_backward(x, w, rstd, dy, dres=dres).float()
+    ref = ops.rms_norm_backward(x, w, rstd, dy).float() + dres.float()
+    assert (got - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()
