@@ -270,8 +270,10 @@ def run_decode(args):
             scripted, scripted_s = timed_decode(prompts, draft_table=table.to(dev))
         lossless = total_over_ranks(float(scripted.tokens == ref)) == world
         for name, res, dev_s in (("plain", plain, plain_s), ("scripted", scripted, scripted_s)):
-            # one batched cycle = a draft pass and a verify pass; time the replayed cycles only
-            per_pass = max_over_ranks(res.steady_seconds / max(2 * res.steady_cycles, 1), world)
+            # time the replayed cycles only; a plain cycle runs two model passes (draft, verify),
+            # a scripted one only the verify pass (its drafts come from the table)
+            model_passes = 2 if name == "plain" else 1
+            per_pass = max_over_ranks(res.steady_seconds / max(model_passes * res.steady_cycles, 1), world)
             seconds = max_over_ranks(dev_s - res.prefill_seconds, world)
             gen = total_over_ranks(float(res.total_tokens))
             passes = total_over_ranks(float(sum(res.passes)))
@@ -284,7 +286,7 @@ def run_decode(args):
                 "scaling": "weak", "batch_per_gpu": batch, "new_tokens": new, "K": K,
                 "dtype": args.decode_dtype, "tpf": round(gen / max(passes, 1), 3),
                 "mean_accepted": round(sum(sum(a) for a in res.accepted) / max(sum(res.cycles), 1), 3),
-                "ms_per_pass": round(per_pass * 1e3, 4),
+                "ms_per_pass": round(per_pass * 1e3, 4), "model_passes_per_cycle": model_passes,
                 "hbm": {"bytes_per_pass": int(pass_bytes), "achieved_gbs": round(gbs, 1),
                         "peak_gbs": pk["hbm_gbs"], "frac": round(gbs / pk["hbm_gbs"], 4)},
                 "lossless_vs_plain_greedy": bool(lossless) if name == "scripted" else True,
@@ -331,6 +333,8 @@ def run_decode(args):
 #            library's tcgen05 kernels                                    (:136-149)
 #   linear2  every projection GEMM of the step (forward with residual, dX, dW) through cuBLAS and
 #            through the CTA-pair kernel orthrus_gemm2_bf16
+#   decode_proj the projections of a decode pass (32 and 1024 rows) on the persistent and the
+#            128 x 64-tile kernels (weight bytes streamed per call)
 #   sweep    dual-view attention fwd + bwd over L in {1024..8192}, K in {16, 32, 64}, A in
 #            {8, 32, 64} (batch filling 16384 query tokens, at most 65536 keys per head), and the
 #            fused LM head + KL over N in {4096, 16384, 65536} student rows
@@ -469,6 +473,26 @@ def kernel_case(case: str, iters: int, warmup: int) -> dict:
         ]
         for name, ref_fn, own_fn, work in pairs:
             timed += [(name + "_cublas", ref_fn, work, "tflops"), (name + "_pair", own_fn, work, "tflops")]
+    elif case == "decode_proj":
+        # the projections of one decode pass (32 rows per sequence: batch 1 and 32) on the
+        # persistent 128 x 256-tile kernel and on the 128 x 64-tile kernel
+        d, ff, hq, qkv_n = 1024, 3072, HQ * HD, (HQ + 2 * HKV) * HD
+        w_qkv, w_o = rnd(qkv_n, d, scale=0.03), rnd(d, hq, scale=0.02)
+        w_gu, w_d = rnd(2 * ff, d, scale=0.03), rnd(d, ff, scale=0.02)
+        for rows in (32, 1024):
+            x, o, a, r = rnd(rows, d), rnd(rows, hq), rnd(rows, ff), rnd(rows, d)
+            for sk in (False, True):
+                tag = f"{rows}_{'skinny' if sk else 'persistent'}"
+                # bytes of weights streamed per call: what bounds a pass of a few rows
+                timed += [
+                    (f"qkv_{tag}", lambda x=x, sk=sk: ops.linear(x, w_qkv, skinny=sk), w_qkv.numel() * 2, "gbs"),
+                    (f"o_res_{tag}", lambda o=o, r=r, sk=sk: ops.linear(o, w_o, residual=r, skinny=sk),
+                     w_o.numel() * 2, "gbs"),
+                    (f"gate_up_swiglu_{tag}", lambda x=x, sk=sk: ops.linear_swiglu(x, w_gu, skinny=sk),
+                     w_gu.numel() * 2, "gbs"),
+                    (f"down_res_{tag}", lambda a=a, r=r, sk=sk: ops.linear(a, w_d, residual=r, skinny=sk),
+                     w_d.numel() * 2, "gbs"),
+                ]
     else:
         raise ValueError(f"unknown kernel case {case!r}")
     out = {}
@@ -766,7 +790,8 @@ def main():
     ap.add_argument("--decode-new", type=int, default=512)
     ap.add_argument("--decode-dtype", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--kernel-case", default=None,
-                    choices=["causal", "dual", "dualbwd", "lmhead", "prologue", "linear", "linear2", "sweep"],
+                    choices=["causal", "dual", "dualbwd", "lmhead", "prologue", "linear", "linear2", "decode_proj",
+                             "sweep"],
                     help="time one hot entry point alone (--steps calls after --warmup)")
     args = ap.parse_args()
     if args.warmup < 3 and args.kernel_case is None:

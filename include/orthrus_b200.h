@@ -108,9 +108,20 @@ int orthrus_gemm2_bf16(const void* A, int64_t lda, int a_mn, const void* B, int6
 #define ORTHRUS_LINEAR_STORE 0
 #define ORTHRUS_LINEAR_RESIDUAL 1
 #define ORTHRUS_LINEAR_SWIGLU 2
+#define ORTHRUS_LINEAR_PAIR 0x100  /* flag: the same kernel on CTA pairs (tcgen05 cta_group::2, 256-row tiles) */
 int orthrus_linear_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* residual,
                         void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int epilogue,
                         void* stream);
+
+/* The same three epilogues (STORE, RESIDUAL, SWIGLU) on 128-row x 64-column tiles (32 output
+ * columns for SWIGLU), one tile per CTA with the full K: many CTAs stream weights when M is a
+ * few rows (the decode passes). N a multiple of 64 (SWIGLU: 32). Per-row results depend only on
+ * the row's inputs and the fixed k order, as for orthrus_linear_bf16.
+ * Replaces the F.linear projections of the generation passes (orthrus/modeling_orthrus.py:469-497
+ * through Qwen3Attention / Qwen3MLP). */
+int orthrus_linear_skinny_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                               const void* residual, void* y, int64_t ldy, int64_t M, int64_t N,
+                               int64_t K, int epilogue, void* stream);
 
 /* The same for the trainable view, whose prologue has a backward: RoPE at positions [B*L] (int64,
  * below table_rows, the rows of rope_cos / rope_sin; a position outside is clamped and reported

@@ -33,6 +33,8 @@ _SIGNATURES = {
                                    c_int64, c_int64, c_int64, c_int, _P, c_size_t, _P]),
     "orthrus_linear_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, _P, c_int64, c_int64, c_int64,
                                     c_int64, c_int, _P]),
+    "orthrus_linear_skinny_bf16": (c_int, [_P, c_int64, _P, c_int64, _P, _P, c_int64, c_int64, c_int64,
+                                           c_int64, c_int, _P]),
     "orthrus_linear_swiglu_keep_bf16": (c_int, [_P, _P, c_int64, c_int64, c_int64, _P, _P, _P]),
     "orthrus_linear_qkv_rope_keep_bf16": (c_int, [_P, _P, _P, _P, _P, _P, c_int64, _P, c_int64, c_int64,
                                                   c_int64, c_int, c_int, c_float, _P, _P, _P, _P, _P, _P]),

@@ -13,6 +13,7 @@
 #include "gemm_tc.cuh"
 #include "gemm2_tc.cuh"
 #include "linear_tc.cuh"
+#include "linear_skinny.cuh"
 #include "lmhead_kl.cuh"
 #include "qkv_prep.cuh"
 #include "rowwise.cuh"
@@ -75,6 +76,11 @@ int orthrus_gemm2_bf16(const void* A, int64_t lda, int a_mn, const void* B, int6
 int orthrus_linear_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* residual, void* y,
                         int64_t ldy, int64_t M, int64_t N, int64_t K, int epilogue, void* stream) {
   return linear_bf16_impl(x, ldx, w, ldw, residual, y, ldy, M, N, K, epilogue, as_stream(stream));
+}
+
+int orthrus_linear_skinny_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* residual, void* y,
+                               int64_t ldy, int64_t M, int64_t N, int64_t K, int epilogue, void* stream) {
+  return linear_skinny_impl(x, ldx, w, ldw, residual, y, ldy, M, N, K, epilogue, as_stream(stream));
 }
 
 int orthrus_linear_swiglu_keep_bf16(const void* x, const void* w_gate_up, int64_t M, int64_t F, int64_t K, void* y,

@@ -80,9 +80,11 @@ __device__ __forceinline__ float silu_fast(float g) {
 // Tile t -> (m tile, n tile) and the first W row of each 128-row half of the accumulator.
 struct LinearGeometry {
   int M, N, K, ntiles, tiles, f_rows;  // f_rows: F (up rows start there) for SwiGLU, else 0
-  __device__ __forceinline__ void tile(int t, int epi, int& m0, int& n0, int& w0, int& w1) const {
+  // pair: tiles of 256 rows over a CTA pair, this CTA's 128 rows at rank * 128
+  __device__ __forceinline__ void tile(int t, int epi, int& m0, int& n0, int& w0, int& w1, bool pair = false,
+                                       int rank = 0) const {
     const int mt = t / ntiles, nt = t % ntiles;
-    m0 = mt * LinearTile::BM;
+    m0 = pair ? mt * 2 * LinearTile::BM + rank * LinearTile::BM : mt * LinearTile::BM;
     if (epi == kLinearSwiGLU || epi == kLinearSwiGLUKeep) {
       n0 = nt * 128;
       w0 = n0;
@@ -97,7 +99,12 @@ struct LinearGeometry {
   }
 };
 
-template <int EPI>
+// PAIR: the same kernel on CTA pairs (tcgen05 cta_group::2, UMMA 256 x 256 x 16): each CTA of the
+// pair loads its own 128 rows of X and one of the two 128-row W boxes (no multicast), the leader
+// issues the MMA over both CTAs' shared memory, and each CTA's TMEM holds the accumulator of its
+// rows with exactly the one-CTA column layout, so every epilogue is unchanged. Per k-block a CTA
+// loads 32 KB instead of 48 KB for the same MACs.
+template <int EPI, bool PAIR = false>
 __global__ void __launch_bounds__(LinearTile::THREADS, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmK,
@@ -105,14 +112,19 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
                      const LinearGeometry g, int64_t ldr, const __nv_bfloat16* __restrict__ R,
                      const QkvRopeParams qp) {
   using T = LinearTile;
+  // one-CTA ring: 4 stages of X (16 KB) + both W boxes (32 KB); pair ring: 6 stages of X + one box
+  constexpr int STAGES = PAIR ? 6 : T::STAGES;
+  constexpr int B_STAGE = PAIR ? T::B_HALF : T::B_BYTES;
+  constexpr int STAGE_BYTES = T::A_BYTES + B_STAGE;
+  static_assert(STAGES * STAGE_BYTES == T::STAGES * T::STAGE_BYTES, "both rings fill the same space");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + T::STAGES * T::A_BYTES;
-  uint8_t* staging = sB + T::STAGES * T::B_BYTES;  // 1024-aligned: the ring is a multiple of 1 KB
+  uint8_t* sB = smem + STAGES * T::A_BYTES;
+  uint8_t* staging = sB + STAGES * B_STAGE;  // 1024-aligned: the ring is a multiple of 1 KB
   uint64_t* full = reinterpret_cast<uint64_t*>(staging + T::EPI_WARPS * T::STAGING);
-  uint64_t* empty = full + T::STAGES;
-  uint64_t* acc_full = empty + T::STAGES;  // [2]
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;      // [2]
   uint64_t* mma_drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
@@ -120,22 +132,32 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = (g.K + T::BK - 1) / T::BK;
+  const int rank = PAIR ? static_cast<int>(cluster_ctarank()) : 0;
+  const bool leader = rank == 0;
+  const int first = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int stride = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < T::STAGES; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], T::EPI_WARPS);
+      mbar_init(&acc_empty[b], (PAIR ? 2 : 1) * T::EPI_WARPS);
     }
     mbar_init(mma_drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  if (warp == 1) {
+    if constexpr (PAIR)
+      tmem_alloc_pair(tmem_slot, 512);
+    else
+      tmem_alloc(tmem_slot, 512);
+  }
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();  // the peer's barriers exist before anyone signals them
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -144,58 +166,85 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
       prefetch_tensormap(&tmX);
       prefetch_tensormap(&tmW);
       int it = 0, issued = 0;
-      for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x) {
+      for (int t = first; t < g.tiles && !*abort_flag; t += stride) {
         int m0, n0, w0, w1;
-        g.tile(t, EPI, m0, n0, w0, w1);
+        g.tile(t, EPI, m0, n0, w0, w1, PAIR, rank);
         for (int kb = 0; kb < KB; ++kb, ++it) {
-          const int s = it % T::STAGES;
-          if (!mbar_wait(&empty[s], ((it / T::STAGES) & 1) ^ 1)) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1)) {
             *abort_flag = 1;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], T::STAGE_BYTES);
-          tma_load_2d(sA + s * T::A_BYTES, &tmX, &full[s], kb * T::BK, m0);
-          tma_load_2d(sB + s * T::B_BYTES, &tmW, &full[s], kb * T::BK, w0);
-          tma_load_2d(sB + s * T::B_BYTES + T::B_HALF, &tmW, &full[s], kb * T::BK, w1);
+          if constexpr (PAIR) {
+            // this CTA's rows and its W box (rank 0: the first 128 accumulator columns); the leader
+            // posts the bytes of both CTAs on its own barrier, which both CTAs' copies complete
+            const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * STAGE_BYTES);
+            tma_load_2d_pair(sA + s * T::A_BYTES, &tmX, bar, kb * T::BK, m0);
+            tma_load_2d_pair(sB + s * B_STAGE, &tmW, bar, kb * T::BK, rank == 0 ? w0 : w1);
+          } else {
+            mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+            tma_load_2d(sA + s * T::A_BYTES, &tmX, &full[s], kb * T::BK, m0);
+            tma_load_2d(sB + s * B_STAGE, &tmW, &full[s], kb * T::BK, w0);
+            tma_load_2d(sB + s * B_STAGE + T::B_HALF, &tmW, &full[s], kb * T::BK, w1);
+          }
           issued = it + 1;
         }
       }
-      if (*abort_flag)
-        for (int i = max(0, issued - T::STAGES); i < issued; ++i)
-          mbar_wait_short(&full[i % T::STAGES], (i / T::STAGES) & 1);
+      if (*abort_flag && leader)
+        for (int i = max(0, issued - STAGES); i < issued; ++i)
+          mbar_wait_short(&full[i % STAGES], (i / STAGES) & 1);
     }
   } else if (warp == 1) {
-    if (elect_one()) {
-      constexpr uint32_t idesc = umma_idesc_bf16(128, T::BN, false, false);
+    if (leader && elect_one()) {
+      constexpr uint32_t idesc = umma_idesc_bf16(PAIR ? 256 : 128, T::BN, false, false);
       int it = 0, tt = 0;
-      for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x, ++tt) {
+      for (int t = first; t < g.tiles && !*abort_flag; t += stride, ++tt) {
         const int b = tt & 1;
         const uint32_t acc = tmem + b * T::BN;
-        if (!mbar_wait(&acc_empty[b], ((tt >> 1) & 1) ^ 1)) {
+        const bool free_acc = PAIR ? mbar_wait_cluster(&acc_empty[b], ((tt >> 1) & 1) ^ 1)
+                                   : mbar_wait(&acc_empty[b], ((tt >> 1) & 1) ^ 1);
+        if (!free_acc) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
         for (int kb = 0; kb < KB; ++kb, ++it) {
-          const int s = it % T::STAGES;
-          if (!mbar_wait(&full[s], (it / T::STAGES) & 1)) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&full[s], (it / STAGES) & 1)) {
             *abort_flag = 1;
             break;
           }
           tc_fence_after();
           const uint32_t a_base = smem_u32(sA + s * T::A_BYTES);
-          const uint32_t b_base = smem_u32(sB + s * T::B_BYTES);
+          const uint32_t b_base = smem_u32(sB + s * B_STAGE);
 #pragma unroll
-          for (int k = 0; k < T::BK / 16; ++k)
-            umma_f16(acc, umma_desc_sw128(a_base + k * 32, 16, 1024), umma_desc_sw128(b_base + k * 32, 16, 1024),
-                     idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          umma_commit(&empty[s]);
+          for (int k = 0; k < T::BK / 16; ++k) {
+            const uint64_t ad = umma_desc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t bd = umma_desc_sw128(b_base + k * 32, 16, 1024);
+            if constexpr (PAIR)
+              umma_f16_pair(acc, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            else
+              umma_f16(acc, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          if constexpr (PAIR)
+            umma_commit_pair(&empty[s], 3);
+          else
+            umma_commit(&empty[s]);
         }
-        umma_commit(&acc_full[b]);
+        if constexpr (PAIR)
+          umma_commit_pair(&acc_full[b], 3);
+        else
+          umma_commit(&acc_full[b]);
       }
       // every MMA this thread issued has completed before the accumulators are freed
-      umma_commit(mma_drain);
+      if constexpr (PAIR)
+        umma_commit_pair(mma_drain, 3);
+      else
+        umma_commit(mma_drain);
       mbar_wait_short(mma_drain, 0);
+    } else if (PAIR && !leader && elect_one()) {
+      mbar_wait(mma_drain, 0);  // the leader's MMAs also write this CTA's TMEM
     }
   } else {
     const int quarter = warp & 3;          // TMEM lanes this warp may read
@@ -216,7 +265,7 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
       if (lane == 0) tma_store_wait_read_all();
       __syncwarp();
     };
-    for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x, ++tt) {
+    for (int t = first; t < g.tiles && !*abort_flag; t += stride, ++tt) {
       const int b = tt & 1;
       if (!mbar_wait(&acc_full[b], (tt >> 1) & 1)) {
         *abort_flag = 1;
@@ -224,7 +273,7 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
       }
       tc_fence_after();
       int m0, n0, w0, w1;
-      g.tile(t, EPI, m0, n0, w0, w1);
+      g.tile(t, EPI, m0, n0, w0, w1, PAIR, rank);
       const int row0 = m0 + quarter * 32;
       const int row = row0 + lane;
       const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + b * T::BN;
@@ -463,15 +512,85 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[b]), 0));
+        else
+          mbar_arrive(&acc_empty[b]);
+      }
     }
     if (lane == 0) tma_store_wait_all();
   }
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();  // neither CTA frees TMEM or leaves while the other may signal it
   if (warp == 1) {
     tc_fence_after();
-    tmem_free(tmem, 512);
+    if constexpr (PAIR)
+      tmem_free_pair(tmem, 512);
+    else
+      tmem_free(tmem, 512);
   }
+}
+
+// Largest number of co-resident clusters of two of a pair-mode linear kernel (cached per kernel).
+template <typename Kern>
+inline int linear_pair_max_clusters(Kern kernel) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, int> cache;
+  const void* key = reinterpret_cast<const void*>(kernel);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * 74);
+  cfg.blockDim = dim3(LinearTile::THREADS);
+  cfg.dynamicSmemBytes = LinearTile::SMEM;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) n = num_sms() / 2;
+  cache[key] = n;
+  return n;
+}
+
+// Launches linear_tc_kernel<EPI> on g.tiles tiles of 128 rows, or, with pair, linear_tc_kernel<EPI,
+// true> on clusters of two over tiles of 256 rows (g.tiles recomputed for them).
+template <int EPI>
+inline int linear_launch(bool pair, const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ty,
+                         const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tp, LinearGeometry g,
+                         int64_t ldr, const __nv_bfloat16* R, const QkvRopeParams& qp, cudaStream_t stream) {
+  using T = LinearTile;
+  if (!pair) {
+    ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<EPI>, T::SMEM));
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(g.tiles, num_sms()));
+    linear_tc_kernel<EPI><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, tk, tv, tp, g, ldr, R, qp);
+    ORTHRUS_CHECK_LAUNCH();
+    return ORTHRUS_OK;
+  }
+  auto kernel = linear_tc_kernel<EPI, true>;
+  ORTHRUS_CHECK_CUDA(ensure_smem(kernel, T::SMEM));
+  g.tiles = static_cast<int>(ceil_div(g.M, 2 * T::BM) * g.ntiles);
+  const int clusters = std::min(g.tiles, linear_pair_max_clusters(kernel));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters));
+  cfg.blockDim = dim3(T::THREADS);
+  cfg.dynamicSmemBytes = T::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ORTHRUS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kernel, tx, tw, ty, tk, tv, tp, g, ldr, R, qp));
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
 }
 
 // cos / sin [P][half] of the RoPE angle p * inv_freq[i], rounded to bf16, by sincosf as the
@@ -501,8 +620,14 @@ inline int rope_table_impl(const float* inv_freq, int64_t P, int half, void* cos
 // Host side. N is the number of output columns (F for SwiGLU, whose W has 2F rows); N must be a
 // multiple of 128, K a multiple of 8, leading dimensions multiples of 8 elements. R (residual) has
 // the leading dimension of Y and is a separate buffer.
+// epilogue | kLinearPairFlag runs the kernel on CTA pairs (the training step's sizes; inference
+// keeps the one-CTA kernel, so its per-row results never depend on the launch form).
+constexpr int kLinearPairFlag = 0x100;
+
 inline int linear_bf16_impl(const void* X, int64_t ldx, const void* W, int64_t ldw, const void* R, void* Y,
                             int64_t ldy, int64_t M, int64_t N, int64_t K, int epilogue, cudaStream_t stream) {
+  const bool pair = (epilogue & kLinearPairFlag) != 0;
+  epilogue &= ~kLinearPairFlag;
   ORTHRUS_CHECK_ARG(X && W && Y && M >= 0 && N > 0 && K > 0);
   ORTHRUS_CHECK_ARG(epilogue == kLinearStore || epilogue == kLinearResidual || epilogue == kLinearSwiGLU);  // q|k|v: linear_qkv_rope_impl
   ORTHRUS_CHECK_ARG(epilogue != kLinearResidual || (R != nullptr && R != Y));
@@ -526,21 +651,13 @@ inline int linear_bf16_impl(const void* X, int64_t ldx, const void* W, int64_t l
   ORTHRUS_CHECK_ARG(tiles < (1ll << 31));
   g.tiles = static_cast<int>(tiles);
   g.f_rows = epilogue == kLinearSwiGLU ? static_cast<int>(N) : 0;
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, num_sms()));
   auto* r = static_cast<const __nv_bfloat16*>(R);
   const QkvRopeParams none{};
-  if (epilogue == kLinearStore) {
-    ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearStore>, T::SMEM));
-    linear_tc_kernel<kLinearStore><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, ty, ty, ty, g, ldy, nullptr, none);
-  } else if (epilogue == kLinearResidual) {
-    ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearResidual>, T::SMEM));
-    linear_tc_kernel<kLinearResidual><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, ty, ty, ty, g, ldy, r, none);
-  } else {
-    ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearSwiGLU>, T::SMEM));
-    linear_tc_kernel<kLinearSwiGLU><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, ty, ty, ty, g, ldy, nullptr, none);
-  }
-  ORTHRUS_CHECK_LAUNCH();
-  return ORTHRUS_OK;
+  if (epilogue == kLinearStore)
+    return linear_launch<kLinearStore>(pair, tx, tw, ty, ty, ty, ty, g, ldy, nullptr, none, stream);
+  if (epilogue == kLinearResidual)
+    return linear_launch<kLinearResidual>(pair, tx, tw, ty, ty, ty, ty, g, ldy, r, none, stream);
+  return linear_launch<kLinearSwiGLU>(pair, tx, tw, ty, ty, ty, ty, g, ldy, nullptr, none, stream);
 }
 
 // silu(x gate^T) * (x up^T) into y [M, F] and the projection [gate | up] into gate_up [M, 2F].
@@ -565,13 +682,9 @@ inline int linear_swiglu_keep_impl(const void* X, const void* W, int64_t M, int6
   ORTHRUS_CHECK_ARG(tiles < (1ll << 31));
   g.tiles = static_cast<int>(tiles);
   g.f_rows = static_cast<int>(F);
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, num_sms()));
   const QkvRopeParams none{};
-  ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearSwiGLUKeep>, T::SMEM));
-  linear_tc_kernel<kLinearSwiGLUKeep><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, tgu, tgu, tgu, g, 0,
-                                                                           nullptr, none);
-  ORTHRUS_CHECK_LAUNCH();
-  return ORTHRUS_OK;
+  // the trainable view's MLP (thousands of rows): CTA pairs
+  return linear_launch<kLinearSwiGLUKeep>(M >= 2048, tx, tw, ty, tgu, tgu, tgu, g, 0, nullptr, none, stream);
 }
 
 // q|k|v projection of x [B*L, K] by w [(Hq + 2 Hkv) * 128, K] with the attention prologue in the
@@ -622,11 +735,8 @@ inline int linear_qkv_rope_impl(const void* X, const void* W, const void* q_norm
   qp.Hq = Hq;
   qp.Hkv = Hkv;
   qp.eps = eps;
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(g.tiles, num_sms()));
-  ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<kLinearQkvRope>, T::SMEM));
-  linear_tc_kernel<kLinearQkvRope><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, tq, tk, tv, tp, g, 0, nullptr, qp);
-  ORTHRUS_CHECK_LAUNCH();
-  return ORTHRUS_OK;
+  // the training step's q|k|v projections (thousands of rows): CTA pairs
+  return linear_launch<kLinearQkvRope>(M >= 2048, tx, tw, tq, tk, tv, tp, g, 0, nullptr, qp, stream);
 }
 
 }  // namespace orthrus

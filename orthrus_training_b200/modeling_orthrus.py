@@ -83,11 +83,18 @@ def _cached_weight(owner: nn.Module, key, tensors: list[torch.Tensor]) -> torch.
     return hit[1]
 
 
+def _few_tiles(rows: int, cols: int) -> bool:
+    """Whether a projection of `rows` rows and `cols` output columns (accumulator columns for
+    SwiGLU) would leave most SMs idle on 128 x 256 tiles: then the 128 x 64-tile kernel runs it.
+    The two kernels give every row the same bits, so the choice never changes a result."""
+    return -(-rows // 128) * -(-cols // 256) < 74
+
+
 def _project(a: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
-    """a @ w^T (+ residual). Both kernels are batch-invariant: a row's result does not depend on
-    how many rows the call has."""
+    """a @ w^T (+ residual). Every kernel here is batch-invariant: a row's result does not depend
+    on how many rows the call has."""
     if a.dtype == torch.bfloat16 and ops.fused_linear_supported(a, w, w.shape[0]):
-        return ops.linear(a, w, residual=residual)
+        return ops.linear(a, w, residual=residual, skinny=_few_tiles(a.shape[0], w.shape[0]))
     y = ops.gemm(a, w)
     return y if residual is None else ops.add(residual, y)
 
@@ -109,7 +116,7 @@ class OrthrusMLP(nn.Module):
         """silu(h @ gate^T) * (h @ up^T) for h [rows, d]."""
         w = self.packed_gate_up()
         if h.dtype == torch.bfloat16 and ops.fused_linear_supported(h, w, w.shape[0] // 2):
-            return ops.linear_swiglu(h, w)
+            return ops.linear_swiglu(h, w, skinny=_few_tiles(h.shape[0], w.shape[0]))
         return ops.silu_mul(ops.gemm(h, w))
 
     @torch.no_grad()

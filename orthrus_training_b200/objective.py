@@ -319,7 +319,7 @@ def _teacher_layer(backbone, i, x, pos, B, L, inv, rope=None):
     w_gu = layer.mlp.packed_gate_up()
     if ops.fused_linear_supported(h, w_gu, w_gu.shape[0] // 2):
         # gate/up GEMM with SwiGLU in its epilogue: [gate | up] never goes through HBM
-        act = ops.linear_swiglu(h, w_gu)
+        act = ops.linear_swiglu(h, w_gu, pair=h.shape[0] >= 2048)
     else:
         act = ops.silu_mul(h @ w_gu.t())
     x = _add_projection(x, act, layer.mlp.down_proj.weight)

@@ -141,9 +141,14 @@ def fused_linear_supported(x: torch.Tensor, w: torch.Tensor, n_out: int) -> bool
             and n_out % 128 == 0 and x.shape[1] % 8 == 0)
 
 
-def linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+LINEAR_PAIR = 0x100  # epilogue flag of orthrus_linear_bf16: run on CTA pairs
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None,
+           skinny: bool = False, pair: bool = False) -> torch.Tensor:
     """x [M, K] @ w [N, K]^T, plus residual [M, N] in the epilogue when given (torch.addmm with
-    beta = 1), on the persistent tcgen05 projection kernel."""
+    beta = 1), on the persistent tcgen05 projection kernel, or with skinny on 128 x 64 tiles (many
+    CTAs for a few rows; N a multiple of 64)."""
     _require_cuda(x, w, residual)
     x = x.contiguous()
     w = w.contiguous()
@@ -159,12 +164,14 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = Non
         if residual.shape != (M, N) or residual.dtype != x.dtype:
             raise ValueError("residual must be [M, N] in the dtype of x")
         epi = LINEAR_RESIDUAL
-    L.check(L.lib().orthrus_linear_bf16(x.data_ptr(), K, w.data_ptr(), K, L.ptr(residual), y.data_ptr(),
-                                        N, M, N, K, epi, L.stream_of(x.device)), "linear_bf16")
+    fn = L.lib().orthrus_linear_skinny_bf16 if skinny else L.lib().orthrus_linear_bf16
+    L.check(fn(x.data_ptr(), K, w.data_ptr(), K, L.ptr(residual), y.data_ptr(), N, M, N, K,
+               epi | (LINEAR_PAIR if pair and not skinny else 0), L.stream_of(x.device)), "linear_bf16")
     return y
 
 
-def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, keep_gate_up: bool = False):
+def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, keep_gate_up: bool = False,
+                  skinny: bool = False, pair: bool = False):
     """silu(x @ gate^T) * (x @ up^T) for w_gate_up = [gate; up] [2F, K], without writing the
     [gate | up] projection (same roundings as silu_mul(x @ w_gate_up^T)). With keep_gate_up the
     projection [M, 2F] is written as well and (y, gate_up) is returned."""
@@ -183,8 +190,10 @@ def linear_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, keep_gate_up: bool =
                                                         y.data_ptr(), gu.data_ptr(), L.stream_of(x.device)),
                 "linear_swiglu_keep")
         return y, gu
-    L.check(L.lib().orthrus_linear_bf16(x.data_ptr(), K, w_gate_up.data_ptr(), K, None, y.data_ptr(), F,
-                                        M, F, K, LINEAR_SWIGLU, L.stream_of(x.device)), "linear_swiglu")
+    fn = L.lib().orthrus_linear_skinny_bf16 if skinny else L.lib().orthrus_linear_bf16
+    L.check(fn(x.data_ptr(), K, w_gate_up.data_ptr(), K, None, y.data_ptr(), F, M, F, K,
+               LINEAR_SWIGLU | (LINEAR_PAIR if pair and not skinny else 0), L.stream_of(x.device)),
+            "linear_swiglu")
     return y
 
 

@@ -39,11 +39,19 @@ def anchor_rng(seed: int, *keys, device) -> torch.Generator:
 
 
 class GradBuckets:
-    """Flat per-layer gradient buffers of the trainable parameters with all-reduce hooks."""
+    """Flat per-layer gradient buffers of the trainable parameters with all-reduce hooks. With one
+    rank there is nothing to reduce: the parameters keep no preassigned gradient buffers, so the
+    first micro-batch's gradients are stored by autograd as they come (no zeroing pass and no
+    accumulating add into a zeroed buffer)."""
 
     def __init__(self, model, params: list[torch.nn.Parameter], world: int, group=None):
         self.world = world
         self.group = group
+        self.params = list(params)
+        self.buckets = []
+        self.armed = False
+        if world == 1:
+            return
         by_layer: dict[int, list] = {}
         names = {id(p): n for n, p in model.named_parameters()}
         for p in params:
@@ -60,11 +68,9 @@ class GradBuckets:
                 p.grad = flat[off: off + p.numel()].view_as(p)
                 off += p.numel()
             self.buckets.append({"params": ps, "flat": flat, "ready": 0, "handle": None})
-        self.armed = False
-        if world > 1:
-            for bucket in self.buckets:
-                for p in bucket["params"]:
-                    p.register_post_accumulate_grad_hook(self._hook(bucket))
+        for bucket in self.buckets:
+            for p in bucket["params"]:
+                p.register_post_accumulate_grad_hook(self._hook(bucket))
 
     def _hook(self, bucket):
         def fn(param):
@@ -91,6 +97,10 @@ class GradBuckets:
         self.armed = False
 
     def zero(self) -> None:
+        if self.world == 1:
+            for p in self.params:
+                p.grad = None
+            return
         for b in self.buckets:
             b["flat"].zero_()
 

@@ -78,3 +78,55 @@ def test_rmsnorm_backward_adds_the_residual_gradient():
     got = ops.rms_norm_backward(x, w, rstd, dy, dres=dres).float()
     ref = ops.rms_norm_backward(x, w, rstd, dy).float() + dres.float()
     assert (got - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()
+
+
+@pytest.mark.parametrize("M", [1, 32, 300, 1024])
+@pytest.mark.parametrize("epi", ["store", "residual", "swiglu"])
+def test_skinny_projection_equals_the_persistent_kernel(M, epi):
+    """The 128 x 64-tile projection kernel of the decode passes gives every row bit for bit what
+    the 128 x 256-tile persistent kernel gives it (same k order per output element), so the two may
+    serve passes of different row counts without breaking the batch invariance of decoding."""
+    from orthrus_training_b200 import ops
+
+    K, N = 1024, (1536 if epi == "swiglu" else 1024)
+    x = _rand(M, K, seed=M)
+    w = _rand(2 * N if epi == "swiglu" else N, K, seed=7, scale=0.03)
+    if epi == "swiglu":
+        a, b = ops.linear_swiglu(x, w), ops.linear_swiglu(x, w, skinny=True)
+    else:
+        r = _rand(M, N, seed=9) if epi == "residual" else None
+        a, b = ops.linear(x, w, residual=r), ops.linear(x, w, residual=r, skinny=True)
+    assert torch.equal(a, b)
+
+
+def test_pair_mode_of_the_fused_projection_kernel_matches_one_cta():
+    """The fused-epilogue projection kernel on CTA pairs (the training step's launch form) against
+    its one-CTA form: store, residual and SwiGLU through the pair flag; the q|k|v + prologue and
+    the kept SwiGLU forms at training sizes (which take the pair form) against the one-CTA store
+    kernel followed by the prologue / activation."""
+    from orthrus_training_b200 import _lib, ops
+
+    M, K = 4096, 1024
+    x = _rand(M, K, seed=31)
+    w = _rand(1024, K, seed=32, scale=0.03)
+    r = _rand(M, 1024, seed=33)
+    for res in (None, r):
+        a, b = ops.linear(x, w, residual=res), ops.linear(x, w, residual=res, pair=True)
+        assert (a.float() - b.float()).abs().max().item() <= 1e-2 * a.float().abs().max().item()
+    wg = _rand(2 * 1536, K, seed=34, scale=0.03)
+    a, b = ops.linear_swiglu(x, wg), ops.linear_swiglu(x, wg, pair=True)
+    assert (a.float() - b.float()).abs().max().item() <= 2e-2 * a.float().abs().max().item()
+    y, gu = ops.linear_swiglu(x, wg, keep_gate_up=True)
+    assert torch.equal(y, b) and torch.equal(gu, ops.linear(x, wg, pair=True))
+    B, L, Hq, Hkv = 2, 2048, 16, 8
+    xq = _rand(B * L, K, seed=35)
+    wq = _rand((Hq + 2 * Hkv) * 128, K, seed=36, scale=0.03)
+    qn = (1 + 0.2 * _rand(128, seed=37).float()).bfloat16()
+    inv = ops.rope_inv_freq(128, 1e6, DEV)
+    rope = ops.rope_table(inv, L)
+    q, k, v = ops.linear_qkv_rope(xq, wq, qn, qn, rope, B, L, Hq, Hkv, 1e-6)
+    pos = torch.arange(L, device=DEV).repeat(B).view(B, L)
+    rq, rk, rv, _ = ops.qkv_prep(ops.linear(xq, wq, pair=True), pos, inv, qn, qn, B, L, Hq, Hkv, 128, 128, 1e-6)
+    assert torch.equal(q, rq) and torch.equal(k, rk) and torch.equal(v, rv)
+    print("pair vs one-CTA store bit-identical:", torch.equal(ops.linear(x, w), ops.linear(x, w, pair=True)))
+    assert _lib.device_error(0) == 0
