@@ -79,7 +79,9 @@ def batches(ids: np.ndarray, mask: np.ndarray, batch_size: int, seed: int, epoch
 class DevicePrefetcher:
     """Feeds host micro-batches to one GPU: each is copied into pinned buffers and sent with a
     non-blocking copy on a dedicated stream, one micro-batch ahead. Iterating yields
-    (index, ids, mask) already on the device; the consumer's stream waits for the copy."""
+    (index, ids, mask) already on the device; the consumer's stream waits for the copy, and
+    `ready` is the copy's event (Trainer.step(..., ready=...) lets its side stream wait for that
+    event alone rather than for everything the consumer's stream has queued)."""
 
     def __init__(self, host_batches: Iterator[tuple[int, torch.Tensor, torch.Tensor]], device):
         self.device = torch.device(device)
@@ -88,6 +90,7 @@ class DevicePrefetcher:
         self.source = iter(host_batches)
         self.stream = torch.cuda.Stream(self.device)
         self.pending = None
+        self.ready = None
         self._issue()
 
     def _issue(self) -> None:
@@ -115,6 +118,7 @@ class DevicePrefetcher:
         consumer.wait_event(done)
         ids_dev.record_stream(consumer)
         mask_dev.record_stream(consumer)
+        self.ready = done
         self._issue()
         return index, ids_dev, mask_dev
 

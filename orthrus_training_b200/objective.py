@@ -399,11 +399,20 @@ def diffusion_states(backbone, x: torch.Tensor, cache, positions: torch.Tensor,
                           backbone.inv_freq(x.device))
 
 
-def model_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tensor,
-                 compiled: bool = False, kernel_options: dict | None = None):
-    """Final hidden states of the diffusion view over all anchor blocks [B, A*K, d] and of the
-    frozen AR view over the clean rows [B, L, d] (orthrus/objective.py:228-272). `compiled` and
-    `kernel_options` are accepted for signature compatibility; the kernels are fixed."""
+class TeacherPass:
+    """The frozen AR view over the clean rows: final hidden states [B, L, d] and every layer's
+    keys / values, plus the rotary tables the diffusion view reuses."""
+
+    def __init__(self, states, cache, rope, inv, input_ids):
+        self.states, self.cache, self.rope, self.inv = states, cache, rope, inv
+        self.input_ids = input_ids
+
+
+@torch.no_grad()
+def teacher_pass(model: OrthrusLM, input_ids: torch.Tensor) -> TeacherPass:
+    """The AR half of model_states (orthrus/objective.py:247-254, the frozen teacher over the clean
+    rows). It depends on the input ids only, so a caller may queue it before the anchors are
+    drawn and let the host-side anchor work overlap it."""
     backbone = _backbone(model)
     cfg = backbone.config
     if any(t != "full_attention" for t in getattr(cfg, "layer_types", ["full_attention"])
@@ -411,29 +420,45 @@ def model_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tenso
         raise ValueError("model_states supports full attention layers only (no sliding window)")
     if not input_ids.is_cuda:
         raise ValueError("model_states runs on CUDA tensors only (no CPU fallback)")
-    K = cfg.block_size
     B, L = input_ids.shape
     d = cfg.hidden_size
     inv = backbone.inv_freq(input_ids.device)
-    embed = backbone.embed_tokens.weight
-    with torch.no_grad():
-        x = F.embedding(input_ids, embed).reshape(B * L, d)
-        pos = torch.arange(L, device=x.device)[None].expand(B, L).contiguous()
-        rope = _rope_for(x, backbone, L, L)
-        cache = []
-        for i in range(cfg.num_hidden_layers):
-            x, k, v = _teacher_layer(backbone, i, x, pos, B, L, inv, rope)
-            cache.append((k, v))
-        teacher = ops.rms_norm(x, backbone.norm.weight, cfg.rms_norm_eps).view(B, L, d)
+    x = F.embedding(input_ids, backbone.embed_tokens.weight).reshape(B * L, d)
+    pos = torch.arange(L, device=x.device)[None].expand(B, L).contiguous()
+    rope = _rope_for(x, backbone, L, L)
+    cache = []
+    for i in range(cfg.num_hidden_layers):
+        x, k, v = _teacher_layer(backbone, i, x, pos, B, L, inv, rope)
+        cache.append((k, v))
+    states = ops.rms_norm(x, backbone.norm.weight, cfg.rms_norm_eps).view(B, L, d)
+    return TeacherPass(states, cache, rope, inv, input_ids)
+
+
+def model_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tensor,
+                 compiled: bool = False, kernel_options: dict | None = None, *,
+                 teacher: TeacherPass | None = None):
+    """Final hidden states of the diffusion view over all anchor blocks [B, A*K, d] and of the
+    frozen AR view over the clean rows [B, L, d] (orthrus/objective.py:228-272). `compiled` and
+    `kernel_options` are accepted for signature compatibility; the kernels are fixed. `teacher`
+    is the result of teacher_pass(model, input_ids) when the caller queued it already."""
+    backbone = _backbone(model)
+    cfg = backbone.config
+    if teacher is None:
+        teacher = teacher_pass(model, input_ids)
+    elif teacher.input_ids is not input_ids:
+        raise ValueError("the teacher pass was run on other input ids")
+    K = cfg.block_size
+    B, L = input_ids.shape
+    d = cfg.hidden_size
     anchors = anchors.to(torch.int64).contiguous()
     positions = (anchors[:, :, None] + torch.arange(K, device=anchors.device)).flatten(1).contiguous()
     block_ids = torch.full((B, anchors.shape[1], K), cfg.mask_token_id, dtype=torch.long,
                            device=anchors.device)
     block_ids[:, :, 0] = input_ids.gather(1, anchors)
     Q = anchors.shape[1] * K
-    x = F.embedding(block_ids.flatten(1), embed).reshape(B * Q, d)
-    student = _student_stack(backbone, x, cache, anchors, positions, rope, inv)
-    return student.view(B, Q, d), teacher
+    x = F.embedding(block_ids.flatten(1), backbone.embed_tokens.weight).reshape(B * Q, d)
+    student = _student_stack(backbone, x, teacher.cache, anchors, positions, teacher.rope, teacher.inv)
+    return student.view(B, Q, d), teacher.states
 
 
 @torch.no_grad()
@@ -485,41 +510,62 @@ class FusedLinearForwardKL:
         return _FusedKL.apply(student, teacher, index, weight, chunk_size, row_weight, None, 0)
 
 
+class SupervisedLayout:
+    """The supervised block positions of a batch, settled before the forward: kept (row, anchor,
+    offset) indices ordered by their unique target position, the gather indices of the student
+    and teacher rows, per-offset counts and weights (orthrus/objective.py:418-429,448)."""
+
+    def __init__(self, assistant_mask, anchors, valid, K, gamma):
+        batch, seq_len = assistant_mask.shape
+        self.keep = supervision_mask(assistant_mask, anchors, valid, K)
+        targets = anchors[:, :, None] + torch.arange(K - 1, device=anchors.device)
+        targets = targets + seq_len * torch.arange(batch, device=anchors.device)[:, None, None]
+        kept = torch.nonzero(self.keep.flatten()).squeeze(1)  # flat (row, anchor, offset) indices
+        self.positions, index = torch.unique(targets.flatten()[kept], return_inverse=True)
+        order = torch.argsort(index, stable=True)
+        kept = kept[order]
+        self.index = index[order]
+        self.offsets = kept % (K - 1)
+        self.student_rows = (kept // (K - 1)) * K + self.offsets  # row in [B * A * K]
+        self.tokens_by_offset = torch.bincount(self.offsets, minlength=K - 1)
+        weights = position_weights(K, gamma, self.keep.device)
+        self.row_weight = weights[self.offsets] if weights is not None else None
+        self.count = self.keep.sum()
+
+    def tensors(self) -> list[torch.Tensor]:
+        return [t for t in (self.keep, self.positions, self.index, self.offsets, self.student_rows,
+                            self.tokens_by_offset, self.row_weight, self.count) if t is not None]
+
+
 def orthrus_loss(model: OrthrusLM, input_ids: torch.Tensor, assistant_mask: torch.Tensor,
                  anchors: torch.Tensor, valid: torch.Tensor, kl_chunk_size: int,
-                 compiled: bool = False, kernel_options: dict | None = None, gamma: float = 0.0):
+                 compiled: bool = False, kernel_options: dict | None = None, gamma: float = 0.0, *,
+                 teacher: TeacherPass | None = None, layout: SupervisedLayout | None = None):
     """Mean (or position-weighted mean) forward KL over supervised block positions and its
-    statistics (orthrus/objective.py:395-453)."""
+    statistics (orthrus/objective.py:395-453). `teacher` (teacher_pass) and `layout`
+    (SupervisedLayout) may be prepared by the caller: the training step queues the teacher first
+    and settles the layout's host reads on a side stream meanwhile."""
     K = model.config.block_size
-    batch, seq_len = input_ids.shape
     # The supervised rows depend on the inputs only. Their layout is settled before the forward is
     # queued, so its host reads (the kept-row and unique-target counts, bincount's size) happen
     # while the device is idle rather than between the forward and the LM head.
-    keep = supervision_mask(assistant_mask, anchors, valid, K)
-    targets = anchors[:, :, None] + torch.arange(K - 1, device=anchors.device)
-    targets = targets + seq_len * torch.arange(batch, device=anchors.device)[:, None, None]
-    kept = torch.nonzero(keep.flatten()).squeeze(1)  # flat (row, anchor, offset) indices
-    positions, index = torch.unique(targets.flatten()[kept], return_inverse=True)
-    order = torch.argsort(index, stable=True)
-    kept = kept[order]
-    offsets = kept % (K - 1)
-    student_rows = (kept // (K - 1)) * K + offsets  # row of the block position in [B * A * K]
-    tokens_by_offset = torch.bincount(offsets, minlength=K - 1)
-    weights = position_weights(K, gamma, keep.device)
-    row_weight = weights[offsets] if weights is not None else None
-    student, teacher = model_states(model, input_ids, anchors, compiled, kernel_options)
+    if layout is None:
+        layout = SupervisedLayout(assistant_mask, anchors, valid, K, gamma)
+    student, teacher = model_states(model, input_ids, anchors, compiled, kernel_options,
+                                    teacher=teacher)
     hidden = student.shape[-1]
+    row_weight = layout.row_weight
     total, kl_rows, agree, kl_by_offset, agree_by_offset = _FusedKL.apply(
-        student.reshape(-1, hidden).index_select(0, student_rows),
-        teacher.flatten(0, 1)[positions].to(student.dtype),
-        index[order],
+        student.reshape(-1, hidden).index_select(0, layout.student_rows),
+        teacher.flatten(0, 1)[layout.positions].to(student.dtype),
+        layout.index,
         model.lm_head.weight,
         kl_chunk_size,
         row_weight,
-        offsets,
+        layout.offsets,
         K - 1,
     )
-    count = keep.sum()
+    count = layout.count
     norm = row_weight.sum() if row_weight is not None else count.float()
     stats = {
         "tokens": count.detach(),
@@ -529,7 +575,7 @@ def orthrus_loss(model: OrthrusLM, input_ids: torch.Tensor, assistant_mask: torc
         "agree": agree.sum(),
         "kl_by_offset": kl_by_offset,
         "agree_by_offset": agree_by_offset,
-        "tokens_by_offset": tokens_by_offset,
+        "tokens_by_offset": layout.tokens_by_offset,
         "valid_anchors": valid.float().mean(),
     }
     return total / norm.clamp_min(1e-6), stats

@@ -21,7 +21,8 @@ import math
 import torch
 import torch.distributed as dist
 
-from orthrus_training_b200.objective import orthrus_loss, sample_anchors
+from orthrus_training_b200.objective import (SupervisedLayout, orthrus_loss, sample_anchors,
+                                              teacher_pass)
 
 
 def lr_scale(step: int, warmup: int, total: int, min_ratio: float) -> float:
@@ -136,14 +137,44 @@ class Trainer:
         # every this many steps the library's device error word is read (a host sync): a bounded
         # wait that ran out or a clamped out-of-range index then raises instead of passing silently
         self.check_device_every = check_device_every
+        self._side = None  # stream of the anchor draw and the supervised layout
+
+    def _prepare(self, model, ids, mask, rng, ready):
+        """Queues the teacher pass (it needs the input ids only) and draws the anchors and
+        settles the supervised layout on a side stream beside it. Their host reads (candidate
+        counts, kept rows, unique targets) then wait only for the side stream's few small
+        kernels: with `ready` (an event after which the inputs are complete) those do not wait
+        for the previous step's work either, so the device is never drained between steps."""
+        main = torch.cuda.current_stream(ids.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(ids.device)
+        side = self._side
+        if ready is None:
+            side.wait_stream(main)  # the inputs are complete in the main stream's order
+        else:
+            side.wait_event(ready)
+            main.wait_event(ready)
+        teacher = teacher_pass(model, ids)
+        with torch.cuda.stream(side):
+            anchors, valid = sample_anchors(mask, model.config.block_size, self.num_anchors, rng)
+            layout = SupervisedLayout(mask, anchors, valid, model.config.block_size, self.gamma)
+        main.wait_stream(side)
+        # made on the side stream, read on the main one: keep their memory from the side
+        # stream's pool until the main stream is done with them
+        for t in (anchors, valid, *layout.tensors()):
+            t.record_stream(main)
+        return anchors, valid, teacher, layout
 
     def step(self, micro_batches: list[tuple[torch.Tensor, torch.Tensor]], epoch: int = 0,
-             indices: list[int] | None = None) -> dict:
+             indices: list[int] | None = None, ready: torch.cuda.Event | None = None) -> dict:
         """One optimizer step over this rank's micro-batches [(input_ids, assistant_mask), ...]
         (already on the device). `indices` are the micro-batches' indices in the epoch (the keys of
         their anchor generators, as data_io.batches yields them); by default the global
-        micro-batch count of this trainer. Returns loss, grad_norm and skipped as device tensors
-        (nothing is read back to the host)."""
+        micro-batch count of this trainer. `ready` is an optional CUDA event after which the
+        micro-batches are complete on the device (DevicePrefetcher.ready, or one recorded after
+        device-resident inputs were written); without it they are taken as complete in the
+        current stream's order. Returns loss, grad_norm and skipped as device tensors (nothing is
+        read back to the host)."""
         model = self.model
         accum = len(micro_batches)
         if indices is not None and len(indices) != accum:
@@ -157,9 +188,9 @@ class Trainer:
             else:
                 index = (self.step_index * accum + j) * self.world + self.rank  # global micro-batch
             rng = anchor_rng(self.seed, epoch, index, device=ids.device)
-            anchors, valid = sample_anchors(mask, model.config.block_size, self.num_anchors, rng)
+            anchors, valid, teacher, layout = self._prepare(model, ids, mask, rng, ready)
             loss, stats = orthrus_loss(model, ids, mask, anchors, valid, self.kl_chunk_size,
-                                       gamma=self.gamma)
+                                       gamma=self.gamma, teacher=teacher, layout=layout)
             (loss / accum).backward()
             losses.append(loss.detach())
         self.buckets.wait()

@@ -221,6 +221,43 @@ def test_qkv_prep_backward_matches_autograd():
     assert torch.allclose(dkw.cpu(), kw_.grad, rtol=1e-4, atol=1e-4)
 
 
+def test_qkv_prep_backward_bf16_0_6b_heads_matches_autograd():
+    """bf16 at the Qwen3-0.6B head layout (16 / 8 heads of 128: the pipelined backward kernel),
+    67 rows per sequence so the warps' row counts are ragged, against fp32 autograd of the same
+    bf16 inputs with the bf16-rounded rotary table the kernel uses."""
+    B, T, Hq, Hkv, hd, D = 2, 67, 16, 8, 128, 128
+    g = torch.Generator().manual_seed(8)
+    qkv = torch.randn(B * T, (Hq + 2 * Hkv) * hd, generator=g).bfloat16()
+    pos = torch.randint(0, 2000, (B, T), generator=g)
+    qw = (1 + 0.1 * torch.randn(hd, generator=g)).bfloat16()
+    kw = (1 + 0.1 * torch.randn(hd, generator=g)).bfloat16()
+    gq = torch.randn(B, Hq, T, hd, generator=g)
+    gk = torch.randn(B, Hkv, T, hd, generator=g)
+    gv = torch.randn(B, Hkv, T, hd, generator=g)
+    inv = _ops().rope_inv_freq(hd, 1e6, DEV)
+    _, _, _, rstd = _ops().qkv_prep(qkv.to(DEV), pos.to(DEV), inv, qw.to(DEV), kw.to(DEV), B, T, Hq, Hkv,
+                                    hd, D, 1e-6, want_rstd=True)
+    dqkv, dqw, dkw = _ops().qkv_prep_backward(qkv.to(DEV), pos.to(DEV), inv, qw.to(DEV), kw.to(DEV), rstd,
+                                              gq.to(DEV), gk.to(DEV), gv.to(DEV), B, T, Hq, Hkv, hd, D)
+    x = qkv.float().requires_grad_(True)
+    qw_, kw_ = qw.float().requires_grad_(True), kw.float().requires_grad_(True)
+    xv = x.view(B, T, -1)
+    cos, sin = O.rope_cos_sin(pos, hd, 1e6, torch.bfloat16)
+    cos, sin = cos.float(), sin.float()
+    rq = O.apply_rope(O.rms_norm(xv[..., :Hq * hd].view(B, T, Hq, hd), qw_, 1e-6).transpose(1, 2), cos, sin)
+    rk = O.apply_rope(O.rms_norm(xv[..., Hq * hd:(Hq + Hkv) * hd].view(B, T, Hkv, hd), kw_, 1e-6).transpose(1, 2),
+                      cos, sin)
+    rv = xv[..., (Hq + Hkv) * hd:].view(B, T, Hkv, hd).transpose(1, 2)
+    ((rq * gq).sum() + (rk * gk).sum() + (rv * gv).sum()).backward()
+    got, want = dqkv.float().cpu(), x.grad
+    assert (got - want).abs().max().item() <= 1e-2 * want.abs().max().item()
+    # the v part is the incoming gradient rounded to bf16
+    assert torch.equal(dqkv.cpu().view(B, T, -1)[..., (Hq + Hkv) * hd:],
+                       gv.transpose(1, 2).reshape(B, T, Hkv * hd).bfloat16())
+    assert (dqw.cpu() - qw_.grad).abs().max().item() <= 1e-3 * qw_.grad.abs().max().item()
+    assert (dkw.cpu() - kw_.grad).abs().max().item() <= 1e-3 * kw_.grad.abs().max().item()
+
+
 def test_argmax_lowest_index_on_ties():
     x = torch.zeros(3, 151936, device=DEV)
     x[0, 5] = x[0, 99] = 1.0

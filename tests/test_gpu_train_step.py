@@ -162,3 +162,29 @@ def test_resume_from_a_checkpoint_is_bit_exact(tmp_path):
         tr_c.step(steps[s])
     for (n, a), (_, c) in zip(model_a.named_parameters(), model_c.named_parameters()):
         assert torch.equal(a, c), n
+
+
+def test_inputs_through_the_prefetcher_with_a_ready_event_step_identically():
+    """Trainer.step(..., ready=event) lets the anchor draw and the supervised layout wait for the
+    inputs' copy event alone (on a side stream, beside the teacher pass); it gives the same steps,
+    bit for bit, as rows already on the device without an event."""
+    from orthrus_training_b200.data_io import DevicePrefetcher
+    from orthrus_training_b200.train_step import Trainer
+
+    hp = dict(lr=1e-3, total_steps=10, warmup_ratio=0.2, num_anchors=8, kl_chunk_size=256, seed=4)
+    host = _micro_batches(300, 3)
+
+    def fresh():
+        from test_gpu_model import _bf16_tiny
+
+        model, _ = _bf16_tiny(seed=5)
+        return model, Trainer(model, **hp)
+
+    model_a, tr_a = fresh()
+    losses_a = [tr_a.step([(i.to(DEV), m.to(DEV))])["loss"] for i, m in host]
+    model_b, tr_b = fresh()
+    feed = DevicePrefetcher(((j, i, m) for j, (i, m) in enumerate(host)), DEV)
+    losses_b = [tr_b.step([(i, m)], ready=feed.ready)["loss"] for _, i, m in feed]
+    assert torch.equal(torch.stack(losses_a), torch.stack(losses_b))
+    for (n, a), (_, b) in zip(model_a.named_parameters(), model_b.named_parameters()):
+        assert torch.equal(a, b), n
