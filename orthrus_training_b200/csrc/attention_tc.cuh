@@ -166,6 +166,10 @@ __global__ void __launch_bounds__(192, 1)
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   __syncthreads();
+  // a programmatic dependent launch may start this kernel during the previous one: the tile map,
+  // the operands and the outputs belong to the stream order only after griddep_wait()
+  griddep_launch_dependents();
+  griddep_wait();
   attn_tile_map(mp, b, q0, Tq, has2, row_thread, red, tiles);
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -432,6 +436,10 @@ __global__ void __launch_bounds__(192, 1)
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   __syncthreads();
+  // a programmatic dependent launch may start this kernel during the previous one: the tile map,
+  // the operands and the outputs belong to the stream order only after griddep_wait()
+  griddep_launch_dependents();
+  griddep_wait();
   attn_tile_map(mp, b, q0, Tq, has2, row_thread, red, tiles);
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;  // S: [0,128), dP: [128,256), dQ: [256, 256+D)
@@ -901,6 +909,10 @@ __global__ void __launch_bounds__(320, 1)
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   __syncthreads();
+  // a programmatic dependent launch may start this kernel during the previous one: the tile map,
+  // the operands and the outputs belong to the stream order only after griddep_wait()
+  griddep_launch_dependents();
+  griddep_wait();
   attn_tile_map(mp, b, q0, Tq, has2, wg == 0 ? row : -1, red, tiles);
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -1223,6 +1235,10 @@ __global__ void __launch_bounds__(320, 1)
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   __syncthreads();
+  // a programmatic dependent launch may start this kernel during the previous one: the tile map,
+  // the operands and the outputs belong to the stream order only after griddep_wait()
+  griddep_launch_dependents();
+  griddep_wait();
   attn_tile_map(mp, b, q0, Tq, has2, wg == 0 ? row : -1, red, tiles);
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;

@@ -8,6 +8,7 @@
 
 #include "attention_simt.cuh"
 #include "attention_tc.cuh"
+#include "attention_blockkv.cuh"
 #include "decode.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
@@ -308,12 +309,14 @@ int orthrus_attn_fwd(const void* q, const void* k1, const void* v1, int64_t s1h,
       dim3 grid2(Hq / 2, static_cast<unsigned>(B), static_cast<unsigned>(ceil_div(Tq, 128)));
       if (D == 128) {
         if (set_smem(attn_fwd_tc2_kernel<128>, Fwd2Smem<128>::SMEM)) return ORTHRUS_ECUDA;
-        attn_fwd_tc2_kernel<128><<<grid2, 320, Fwd2Smem<128>::SMEM, st>>>(
-            m.q, m.k1, m.v1, m.k2, m.v2, Hq, Hkv, Tq, hd, sl2, mp, has2, static_cast<__nv_bfloat16*>(o), lse);
+        ORTHRUS_CHECK_CUDA(launch_pdl(attn_fwd_tc2_kernel<128>, grid2, dim3(320), Fwd2Smem<128>::SMEM, st, m.q,
+                                      m.k1, m.v1, m.k2, m.v2, Hq, Hkv, Tq, hd, sl2, mp, has2,
+                                      static_cast<__nv_bfloat16*>(o), lse));
       } else {
         if (set_smem(attn_fwd_tc2_kernel<64>, Fwd2Smem<64>::SMEM)) return ORTHRUS_ECUDA;
-        attn_fwd_tc2_kernel<64><<<grid2, 320, Fwd2Smem<64>::SMEM, st>>>(
-            m.q, m.k1, m.v1, m.k2, m.v2, Hq, Hkv, Tq, hd, sl2, mp, has2, static_cast<__nv_bfloat16*>(o), lse);
+        ORTHRUS_CHECK_CUDA(launch_pdl(attn_fwd_tc2_kernel<64>, grid2, dim3(320), Fwd2Smem<64>::SMEM, st, m.q, m.k1,
+                                      m.v1, m.k2, m.v2, Hq, Hkv, Tq, hd, sl2, mp, has2,
+                                      static_cast<__nv_bfloat16*>(o), lse));
       }
       ORTHRUS_CHECK_LAUNCH();
       return ORTHRUS_OK;
@@ -321,13 +324,14 @@ int orthrus_attn_fwd(const void* q, const void* k1, const void* v1, int64_t s1h,
     dim3 grid(static_cast<unsigned>(ceil_div(Tq, 128)), Hq, static_cast<unsigned>(B));
     if (D == 128) {
       if (set_smem(attn_fwd_tc_kernel<128>, FwdSmem<128>::SMEM)) return ORTHRUS_ECUDA;
-      attn_fwd_tc_kernel<128><<<grid, 192, FwdSmem<128>::SMEM, st>>>(m.q, m.k1, m.v1, m.k2, m.v2, Hq, Hkv, Tq, hd,
-                                                                       sl2, mp, has2, static_cast<__nv_bfloat16*>(o),
-                                                                       lse);
+      ORTHRUS_CHECK_CUDA(launch_pdl(attn_fwd_tc_kernel<128>, grid, dim3(192), FwdSmem<128>::SMEM, st, m.q, m.k1,
+                                    m.v1, m.k2, m.v2, Hq, Hkv, Tq, hd, sl2, mp, has2,
+                                    static_cast<__nv_bfloat16*>(o), lse));
     } else {
       if (set_smem(attn_fwd_tc_kernel<64>, FwdSmem<64>::SMEM)) return ORTHRUS_ECUDA;
-      attn_fwd_tc_kernel<64><<<grid, 192, FwdSmem<64>::SMEM, st>>>(m.q, m.k1, m.v1, m.k2, m.v2, Hq, Hkv, Tq, hd, sl2,
-                                                                     mp, has2, static_cast<__nv_bfloat16*>(o), lse);
+      ORTHRUS_CHECK_CUDA(launch_pdl(attn_fwd_tc_kernel<64>, grid, dim3(192), FwdSmem<64>::SMEM, st, m.q, m.k1,
+                                    m.v1, m.k2, m.v2, Hq, Hkv, Tq, hd, sl2, mp, has2,
+                                    static_cast<__nv_bfloat16*>(o), lse));
     }
     ORTHRUS_CHECK_LAUNCH();
     return ORTHRUS_OK;
@@ -443,8 +447,28 @@ int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h,
             m64.q, m64.dout, m64.k1, m64.v1, m64.k2, m64.v2, Hq, Hkv, Tq, hd, scale, mp, true, lse, delta, dq);
         ORTHRUS_CHECK_LAUNCH();
         ORTHRUS_CHECK_CUDA(cudaStreamWaitEvent(side->stream, side->fork, 0));
-        attn_dkdv_tc_kernel<128><<<grid_kv, 192, DkvSmem<128>::SMEM, side->stream>>>(
-            m.q, m.dout, m.k2, m.v2, Hq, Hkv, Tq, L2, hd, block, scale, lse, delta, dk2, dv2);
+        const int G = Hq / Hkv;
+        if (block == 32 && hd == 128 && Tq % 32 == 0 && (G == 2 || G == 4) && s2h % 8 == 0 && s2b % 8 == 0 &&
+            Tq / 32 < (1ll << 31)) {
+          // 32-key blocks: the HBM-bound own-block kernel (32 x 32 problems, no 128-row padding)
+          const dim3 grid_b(static_cast<unsigned>(Tq / 32), Hkv, static_cast<unsigned>(B));
+          auto* qb = static_cast<const __nv_bfloat16*>(q);
+          auto* k2b = static_cast<const __nv_bfloat16*>(k2);
+          auto* v2b = static_cast<const __nv_bfloat16*>(v2);
+          auto* dob = static_cast<const __nv_bfloat16*>(do_);
+          if (G == 2) {
+            if (set_smem(attn_dkdv_block32_kernel<2>, BlockKvSmem::bytes<2>())) return ORTHRUS_ECUDA;
+            attn_dkdv_block32_kernel<2><<<grid_b, 128, BlockKvSmem::bytes<2>(), side->stream>>>(
+                qb, k2b, v2b, s2h, s2b, dob, lse, delta, Hq, Hkv, Tq, L2, scale, dk2, dv2);
+          } else {
+            if (set_smem(attn_dkdv_block32_kernel<4>, BlockKvSmem::bytes<4>())) return ORTHRUS_ECUDA;
+            attn_dkdv_block32_kernel<4><<<grid_b, 128, BlockKvSmem::bytes<4>(), side->stream>>>(
+                qb, k2b, v2b, s2h, s2b, dob, lse, delta, Hq, Hkv, Tq, L2, scale, dk2, dv2);
+          }
+        } else {
+          attn_dkdv_tc_kernel<128><<<grid_kv, 192, DkvSmem<128>::SMEM, side->stream>>>(
+              m.q, m.dout, m.k2, m.v2, Hq, Hkv, Tq, L2, hd, block, scale, lse, delta, dk2, dv2);
+        }
       } else {
         if (set_smem(attn_dq_tc2_kernel<64>, Dq2Smem<64>::SMEM)) return ORTHRUS_ECUDA;
         if (set_smem(attn_dkdv_tc_kernel<64>, DkvSmem<64>::SMEM)) return ORTHRUS_ECUDA;
@@ -554,8 +578,9 @@ extern "C" int orthrus_rmsnorm(const void* x, const void* w, int64_t rows, int d
   if (dtype == ORTHRUS_BF16) {
     using T = __nv_bfloat16;
     if (vec)
-      rmsnorm_fwd_vec_kernel<T><<<blocks, 256, 0, as_stream(stream)>>>(
-          static_cast<const T*>(x), static_cast<const T*>(w), rows, d, eps, static_cast<T*>(y), rstd);
+      ORTHRUS_CHECK_CUDA(launch_pdl(rmsnorm_fwd_vec_kernel<T>, dim3(blocks), dim3(256), 0, as_stream(stream),
+                                    static_cast<const T*>(x), static_cast<const T*>(w), rows, d, eps,
+                                    static_cast<T*>(y), rstd));
     else
       rmsnorm_kernel<T><<<blocks, 256, 0, as_stream(stream)>>>(static_cast<const T*>(x), static_cast<const T*>(w), rows,
                                                               d, eps, static_cast<T*>(y), rstd);

@@ -35,19 +35,27 @@ namespace orthrus {
 
 enum Gemm2Epilogue { kGemm2Store = 0, kGemm2Residual = 1, kGemm2Partial = 2, kGemm2SwiGLUBwd = 3 };
 
-struct Gemm2Tile {
+struct Gemm2Base {
   static constexpr int BM = 128;                  // rows per CTA (256 per pair)
   static constexpr int BN = 256;                  // accumulator columns per tile
   static constexpr int BK = 64;
   static constexpr int A_BYTES = BM * BK * 2;     // 16 KB
   static constexpr int B_BYTES = 128 * BK * 2;    // 16 KB: this CTA's 128 columns of B
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = 6;
   static constexpr int EPI_WARPS = 8;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int STAGING = 32 * 64 * 2;     // per epilogue warp: 32 rows x 64 bf16
   static constexpr int BOX_MN = 64 * 64 * 2;      // one [64 k][64 mn] box of an MN-major operand
-  static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_WARPS * STAGING + 1024 + 256;
+};
+
+// The SwiGLU-backward epilogue also reads [gate | up]: per epilogue warp a 4 KB buffer that TMA
+// fills with the next 32 x 32 gate and up boxes, paid for with one stage of the ring (its K is
+// short: the MLP's hidden size).
+template <int EPI>
+struct Gemm2Tile : Gemm2Base {
+  static constexpr int STAGES = EPI == 3 ? 5 : 6;
+  static constexpr int IN_STAGING = EPI == 3 ? 2 * 32 * 32 * 2 : 0;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_WARPS * (STAGING + IN_STAGING) + 1024 + 256;
 };
 
 struct Gemm2Geometry {
@@ -65,26 +73,28 @@ __device__ __forceinline__ uint64_t g2_desc_k(uint32_t base, int kk) {
 }
 // MN-major operand tile [64 k][128 mn] stored as two [64 k][64 mn] boxes: k-step kk = 16 rows.
 __device__ __forceinline__ uint64_t g2_desc_mn(uint32_t base, int kk) {
-  return umma_desc_sw128(base + kk * 2048, Gemm2Tile::BOX_MN, 1024);
+  return umma_desc_sw128(base + kk * 2048, Gemm2Base::BOX_MN, 1024);
 }
 
 template <int EPI, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(Gemm2Tile::THREADS, 1)
+__global__ void __launch_bounds__(Gemm2Base::THREADS, 1)
     gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC, const Gemm2Geometry g,
-                    const __nv_bfloat16* __restrict__ R, int64_t ldr) {
-  using T = Gemm2Tile;
+                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR,
+                    const Gemm2Geometry g, const __nv_bfloat16* __restrict__ R, int64_t ldr) {
+  using T = Gemm2Tile<EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + T::STAGES * T::A_BYTES;
   uint8_t* staging = sB + T::STAGES * T::B_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(staging + T::EPI_WARPS * T::STAGING);
+  uint8_t* in_staging = staging + T::EPI_WARPS * T::STAGING;  // kGemm2SwiGLUBwd only
+  uint64_t* full = reinterpret_cast<uint64_t*>(in_staging + T::EPI_WARPS * T::IN_STAGING);
   uint64_t* empty = full + T::STAGES;
   uint64_t* acc_full = empty + T::STAGES;  // [2]
   uint64_t* acc_empty = acc_full + 2;      // [2], leader only: both CTAs' epilogue warps arrive
   uint64_t* mma_drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
+  uint64_t* in_full = mma_drain + 1;       // [EPI_WARPS], kGemm2SwiGLUBwd: [gate | up] boxes landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(in_full + T::EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -103,6 +113,7 @@ __global__ void __launch_bounds__(Gemm2Tile::THREADS, 1)
       mbar_init(&acc_empty[b], 2 * T::EPI_WARPS);
     }
     mbar_init(mma_drain, 1);
+    for (int w = 0; w < T::EPI_WARPS; ++w) mbar_init(&in_full[w], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -217,6 +228,32 @@ __global__ void __launch_bounds__(Gemm2Tile::THREADS, 1)
       if (lane == 0) tma_store_wait_read_all();
       __syncwarp();
     };
+    // kGemm2SwiGLUBwd: this warp's [gate | up] buffer, one 32 x 32 box of each, one load in flight
+    uint8_t* inb = in_staging + (warp - 2) * T::IN_STAGING;
+    uint64_t* ib = &in_full[warp - 2];
+    uint32_t in_issued = 0, in_used = 0;
+    auto in_issue = [&](int col0, int r0) {
+      if (lane == 0) {
+        fence_proxy_async_smem();  // the lanes' reads of the previous chunk precede the overwrite
+        mbar_arrive_expect_tx(ib, T::IN_STAGING);
+        tma_load_2d(inb, &tmR, ib, col0, r0);
+        tma_load_2d(inb + T::IN_STAGING / 2, &tmR, ib, g.N + col0, r0);
+      }
+      ++in_issued;
+    };
+    auto in_issue_tile = [&](int u, int j) {  // chunk j of this warp's rows in work unit u
+      int um0, un0, ukb0, unkb;
+      tile_coords(u, um0, un0, ukb0, unkb);
+      in_issue(un0 + (4 * half + j) * 32, um0 + quarter * 32);
+    };
+    auto in_wait = [&]() -> bool {  // the oldest chunk issued has landed
+      const bool ok = mbar_wait(ib, in_used & 1);
+      ++in_used;
+      if (!ok) *abort_flag = 1;
+      return ok;
+    };
+    if constexpr (EPI == kGemm2SwiGLUBwd)
+      if (cluster < g.tiles) in_issue_tile(cluster, 0);
     for (int t = cluster; t < g.tiles && !*abort_flag; t += nclusters, ++tt) {
       const int b = tt & 1;
       if (!mbar_wait(&acc_full[b], (tt >> 1) & 1)) {
@@ -251,38 +288,49 @@ __global__ void __launch_bounds__(Gemm2Tile::THREADS, 1)
           }
         }
       } else if constexpr (EPI == kGemm2SwiGLUBwd) {
-        // 64 columns at a time: dgate through the staging tile to columns [n, n + 64) of C, then
-        // dup (kept packed in registers meanwhile) to columns [N + n, N + n + 64)
+        // [gate | up] of this warp's 32 rows arrives 32 columns at a time by TMA into its own
+        // buffer, one chunk ahead of the one being computed (across tiles too). dgate leaves
+        // through the staging tile 64 columns at a time, then dup (kept packed meanwhile).
 #pragma unroll 1
         for (int pair = 0; pair < 2; ++pair) {
           reuse();
           uint32_t dup[2][16];
-#pragma unroll 1
+#pragma unroll
           for (int cc = 0; cc < 2; ++cc) {
-            const int col0 = n0 + (4 * half + 2 * pair + cc) * 32;
-            float v[32], gv[32], uv[32];
-            if (row < g.M && col0 < g.N) {
-              const __nv_bfloat16* gsrc = R + static_cast<int64_t>(row) * ldr + col0;
+            const int j = 2 * pair + cc;  // chunk of this warp's four
+            uint4 gq[4], uq[4];
+            const bool have = in_wait();
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {  // 16-byte loads
-                load_elems<__nv_bfloat16, 8>(gsrc + 8 * q, gv + 8 * q);
-                load_elems<__nv_bfloat16, 8>(gsrc + g.N + 8 * q, uv + 8 * q);
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) gv[i] = uv[i] = 0.f;
+            for (int q = 0; q < 4; ++q) {  // 64-byte swizzle: 16-byte unit q of row `lane`
+              const uint32_t off = lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4);
+              gq[q] = ld_shared_v4(smem_u32(inb) + off);
+              uq[q] = ld_shared_v4(smem_u32(inb) + 2048 + off);
             }
-            tmem_ld32(base + (4 * half + 2 * pair + cc) * 32, v);
+            __syncwarp();
+            if (j < 3)
+              in_issue(n0 + (4 * half + j + 1) * 32, row0);
+            else if (t + nclusters < g.tiles)
+              in_issue_tile(t + nclusters, 0);
+            float v[32];
+            tmem_ld32(base + (4 * half + j) * 32, v);
             tmem_wait_ld();
             float dg[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float d = __bfloat162float(__float2bfloat16_rn(v[i]));  // dact as the GEMM output
-              const float sg = 1.f / (1.f + expf(-gv[i]));
-              const float sl = __bfloat162float(__float2bfloat16_rn(gv[i] * sg));
-              const float ds = __bfloat162float(__float2bfloat16_rn(d * uv[i]));
-              dg[i] = ds * sg * (1.f + gv[i] * (1.f - sg));
-              v[i] = d * sl;  // dup
+            for (int q = 0; q < 4; ++q) {
+              const uint32_t gw[4] = {gq[q].x, gq[q].y, gq[q].z, gq[q].w};
+              const uint32_t uw[4] = {uq[q].x, uq[q].y, uq[q].z, uq[q].w};
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const int i = 8 * q + e;
+                const float gv = have ? __uint_as_float((e & 1) ? (gw[e / 2] & 0xffff0000u) : (gw[e / 2] << 16)) : 0.f;
+                const float uv = have ? __uint_as_float((e & 1) ? (uw[e / 2] & 0xffff0000u) : (uw[e / 2] << 16)) : 0.f;
+                const float d = bf16_round(v[i]);  // dact as the GEMM output
+                const float sg = sigmoid_fast(gv);
+                const float sl = bf16_round(gv * sg);
+                const float ds = bf16_round(d * uv);
+                dg[i] = ds * sg * (1.f + gv * (1.f - sg));
+                v[i] = d * sl;  // dup
+              }
             }
 #pragma unroll
             for (int q = 0; q < 16; ++q) dup[cc][q] = pack_bf16x2(v[2 * q], v[2 * q + 1]);
@@ -354,6 +402,8 @@ __global__ void __launch_bounds__(Gemm2Tile::THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[b]), 0));
     }
+    if constexpr (EPI == kGemm2SwiGLUBwd)
+      for (; in_used < in_issued; ++in_used) mbar_wait_short(ib, in_used & 1);  // no copy outlives the CTA
     if (lane == 0) tma_store_wait_all();
   }
   __syncthreads();
@@ -395,7 +445,7 @@ __global__ void gemm2_reduce_kernel(const float* __restrict__ part, int splits, 
 }
 
 // Largest number of co-resident 2-CTA clusters of a gemm2 kernel (cached per kernel).
-template <typename Kern>
+template <int EPI, typename Kern>
 inline int gemm2_max_clusters(Kern kernel) {
   static std::mutex mu;
   static std::unordered_map<const void*, int> cache;
@@ -405,8 +455,8 @@ inline int gemm2_max_clusters(Kern kernel) {
   if (it != cache.end()) return it->second;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * 74);
-  cfg.blockDim = dim3(Gemm2Tile::THREADS);
-  cfg.dynamicSmemBytes = Gemm2Tile::SMEM;
+  cfg.blockDim = dim3(Gemm2Base::THREADS);
+  cfg.dynamicSmemBytes = Gemm2Tile<EPI>::SMEM;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
@@ -421,15 +471,15 @@ inline int gemm2_max_clusters(Kern kernel) {
 }
 
 template <int EPI, bool A_MN, bool B_MN>
-inline int gemm2_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Gemm2Geometry& g,
-                        const __nv_bfloat16* R, int64_t ldr, cudaStream_t stream) {
+inline int gemm2_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& tr,
+                        const Gemm2Geometry& g, const __nv_bfloat16* R, int64_t ldr, cudaStream_t stream) {
   auto kernel = gemm2_tc_kernel<EPI, A_MN, B_MN>;
-  ORTHRUS_CHECK_CUDA(ensure_smem(kernel, Gemm2Tile::SMEM));
-  const int clusters = std::min(g.tiles, gemm2_max_clusters(kernel));  // g.tiles: work units
+  ORTHRUS_CHECK_CUDA(ensure_smem(kernel, Gemm2Tile<EPI>::SMEM));
+  const int clusters = std::min(g.tiles, gemm2_max_clusters<EPI>(kernel));  // g.tiles: work units
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters));
-  cfg.blockDim = dim3(Gemm2Tile::THREADS);
-  cfg.dynamicSmemBytes = Gemm2Tile::SMEM;
+  cfg.blockDim = dim3(Gemm2Base::THREADS);
+  cfg.dynamicSmemBytes = Gemm2Tile<EPI>::SMEM;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -438,7 +488,7 @@ inline int gemm2_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  ORTHRUS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, g, R, ldr));
+  ORTHRUS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, tr, g, R, ldr));
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
 }
@@ -489,7 +539,7 @@ inline int gemm2_bf16_impl(const void* A, int64_t lda, int a_mn, const void* B, 
   if (M == 0) return ORTHRUS_OK;
   if (!swiglu_bwd && (ws_bytes < gemm2_ws_bytes(M, N, K) || (gemm2_ws_bytes(M, N, K) > 0 && ws == nullptr)))
     return ORTHRUS_EWORKSPACE;
-  CUtensorMap ta, tb, tc;
+  CUtensorMap ta, tb, tc, tr{};
   const bool ok_a = a_mn ? make_tmap_2d_bf16(&ta, A, M, K, lda, 64, 64) : make_tmap_2d_bf16(&ta, A, K, M, lda, 64, 128);
   const bool ok_b = b_mn ? make_tmap_2d_bf16(&tb, B, N, K, ldb, 64, 64) : make_tmap_2d_bf16(&tb, B, K, N, ldb, 64, 128);
   if (!ok_a || !ok_b) return ORTHRUS_ECUDA;
@@ -509,10 +559,10 @@ inline int gemm2_bf16_impl(const void* A, int64_t lda, int a_mn, const void* B, 
     float* part = static_cast<float*>(ws);
     if (!make_tmap_2d_f32(&tc, part, N, static_cast<uint64_t>(g.splits) * g.m_pad, N, 32, 32)) return ORTHRUS_ECUDA;
     const int key = (a_mn ? 2 : 0) | (b_mn ? 1 : 0);
-    int rc = key == 0   ? gemm2_launch<kGemm2Partial, false, false>(ta, tb, tc, g, nullptr, 0, stream)
-             : key == 1 ? gemm2_launch<kGemm2Partial, false, true>(ta, tb, tc, g, nullptr, 0, stream)
-             : key == 2 ? gemm2_launch<kGemm2Partial, true, false>(ta, tb, tc, g, nullptr, 0, stream)
-                        : gemm2_launch<kGemm2Partial, true, true>(ta, tb, tc, g, nullptr, 0, stream);
+    int rc = key == 0   ? gemm2_launch<kGemm2Partial, false, false>(ta, tb, tc, tr, g, nullptr, 0, stream)
+             : key == 1 ? gemm2_launch<kGemm2Partial, false, true>(ta, tb, tc, tr, g, nullptr, 0, stream)
+             : key == 2 ? gemm2_launch<kGemm2Partial, true, false>(ta, tb, tc, tr, g, nullptr, 0, stream)
+                        : gemm2_launch<kGemm2Partial, true, true>(ta, tb, tc, tr, g, nullptr, 0, stream);
     if (rc != ORTHRUS_OK) return rc;
     const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(ceil_div(M * (N / 4), 256), num_sms() * 8));
     gemm2_reduce_kernel<<<blocks, 256, 0, stream>>>(part, g.splits, g.m_pad, g.M, g.N, r, ldr,
@@ -521,17 +571,19 @@ inline int gemm2_bf16_impl(const void* A, int64_t lda, int a_mn, const void* B, 
     return ORTHRUS_OK;
   }
   if (!make_tmap_2d_bf16(&tc, C, swiglu_bwd ? 2 * N : N, M, ldc, 64, 32)) return ORTHRUS_ECUDA;
+  // [gate | up] boxes of 32 rows x 32 columns (64 bytes, 64-byte swizzle) for the SwiGLU backward
+  if (swiglu_bwd && !make_tmap_2d_bf16(&tr, R, 2 * N, M, ldr, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) return ORTHRUS_ECUDA;
   if (swiglu_bwd)
-    return b_mn ? gemm2_launch<kGemm2SwiGLUBwd, false, true>(ta, tb, tc, g, r, ldr, stream)
-                : gemm2_launch<kGemm2SwiGLUBwd, false, false>(ta, tb, tc, g, r, ldr, stream);
+    return b_mn ? gemm2_launch<kGemm2SwiGLUBwd, false, true>(ta, tb, tc, tr, g, r, ldr, stream)
+                : gemm2_launch<kGemm2SwiGLUBwd, false, false>(ta, tb, tc, tr, g, r, ldr, stream);
   const int key = (epilogue == kGemm2Residual ? 4 : 0) | (a_mn ? 2 : 0) | (b_mn ? 1 : 0);
   switch (key) {
-    case 0: return gemm2_launch<kGemm2Store, false, false>(ta, tb, tc, g, r, ldr, stream);
-    case 1: return gemm2_launch<kGemm2Store, false, true>(ta, tb, tc, g, r, ldr, stream);
-    case 2: return gemm2_launch<kGemm2Store, true, false>(ta, tb, tc, g, r, ldr, stream);
-    case 3: return gemm2_launch<kGemm2Store, true, true>(ta, tb, tc, g, r, ldr, stream);
-    case 4: return gemm2_launch<kGemm2Residual, false, false>(ta, tb, tc, g, r, ldr, stream);
-    case 5: return gemm2_launch<kGemm2Residual, false, true>(ta, tb, tc, g, r, ldr, stream);
+    case 0: return gemm2_launch<kGemm2Store, false, false>(ta, tb, tc, tr, g, r, ldr, stream);
+    case 1: return gemm2_launch<kGemm2Store, false, true>(ta, tb, tc, tr, g, r, ldr, stream);
+    case 2: return gemm2_launch<kGemm2Store, true, false>(ta, tb, tc, tr, g, r, ldr, stream);
+    case 3: return gemm2_launch<kGemm2Store, true, true>(ta, tb, tc, tr, g, r, ldr, stream);
+    case 4: return gemm2_launch<kGemm2Residual, false, false>(ta, tb, tc, tr, g, r, ldr, stream);
+    case 5: return gemm2_launch<kGemm2Residual, false, true>(ta, tb, tc, tr, g, r, ldr, stream);
     default: return ORTHRUS_EINVAL;  // a residual needs A in its row-major form
   }
 }

@@ -9,6 +9,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <utility>
 #include <unordered_map>
 
 #include "orthrus_b200.h"
@@ -59,6 +60,25 @@ inline cudaError_t ensure_smem(Kern kernel, int bytes) {
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e == cudaSuccess) done[key] = bytes;
   return e;
+}
+
+// Launches `kernel` with the programmatic stream serialization attribute: it may begin (its
+// prologue, loads of constant operands) while the previous kernel on the stream finishes. The
+// kernel must call griddep_wait() before it touches anything that kernel reads or writes.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

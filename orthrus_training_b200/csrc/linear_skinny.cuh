@@ -9,32 +9,42 @@
 // fixed k order, never on M: a K-token verification reproduces a one-token greedy pass bit for
 // bit, which is what keeps block decoding lossless.
 //
-// 192 threads: warp 0 TMA producer (8-stage ring of X [128 x 64] and W [64 x 64] k-blocks; for
-// at most 32 rows only 32 rows of X are loaded),
-// warp 1 TMEM (64 columns) and the single-thread UMMA 128 x 64 x 16 issue, warps 2-5 epilogue
-// (tcgen05.ld, residual add or SwiGLU, 16-byte stores of bf16 rows). Every wait is bounded.
+// 192 threads: warp 0 TMA producer (ring of X [rows x 64] and W [BN x 64] k-blocks, as many stages
+// as about 196 KB holds; for at most 32 rows only 32 rows of X are loaded and stored per stage),
+// warp 1 TMEM (max(BN, 32) columns) and the single-thread UMMA 128 x BN x 16 issue, warps 2-5
+// epilogue (tcgen05.ld, residual add or SwiGLU, 16-byte stores of bf16 rows). Every wait is
+// bounded.
 #pragma once
 
 #include "linear_tc.cuh"
 
 namespace orthrus {
 
+template <int BN_, int AROWS_>
 struct SkinnyTile {
-  static constexpr int BM = 128, BN = 64, BK = 64;
-  static constexpr int A_BYTES = BM * BK * 2;  // 16 KB
-  static constexpr int B_BYTES = BN * BK * 2;  // 8 KB
+  static constexpr int BM = 128, BN = BN_, BK = 64, AROWS = AROWS_;
+  static constexpr int A_BYTES = AROWS * BK * 2;  // the rows of X a stage holds: 4 KB (32) or 16 KB (128)
+  static constexpr int B_BYTES = BN * BK * 2;     // 2 / 4 / 8 KB (a whole number of 1 KB swizzle atoms)
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = 8;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  // as many stages as about 196 KB holds (at most 32): what a CTA keeps in flight sets how fast
+  // its SM pulls weight rows
+  static constexpr int STAGES = (196 * 1024) / STAGE_BYTES < 32 ? (196 * 1024) / STAGE_BYTES : 32;
+  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 1024;
+  // the UMMA reads 128 rows (16 KB) from a stage's A slot: with 32-row slots the rows past 32 come
+  // from the slots after it (and, for the last, the B slots), all inside the allocation
+  static_assert(AROWS == 128 || STAGES * B_BYTES >= 12 * 1024, "UMMA A reads stay in shared memory");
 };
 
-// grid (N / 64 output tiles, or F / 32 for SwiGLU; ceil(M / 128)).
-template <int EPI>
+// grid (N / BN output tiles, or F / (BN / 2) for SwiGLU; ceil(M / 128)). Launched as a
+// programmatic dependent: the barriers, TMEM and the first STAGES k-blocks of W are set up while
+// the previous kernel finishes; X, the residual and Y are touched only after griddep_wait().
+template <int EPI, int BN, int AROWS>
 __global__ void __launch_bounds__(192, 1)
     linear_skinny_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, int M,
                             int N, int K, int f_rows, const __nv_bfloat16* __restrict__ R, int64_t ldr,
                             __nv_bfloat16* __restrict__ Y, int64_t ldy, int a_rows) {
-  using T = SkinnyTile;
+  using T = SkinnyTile<BN, AROWS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -49,7 +59,8 @@ __global__ void __launch_bounds__(192, 1)
   const int KB = (K + T::BK - 1) / T::BK;
   const int m0 = blockIdx.y * T::BM;
   constexpr bool kSwiGLU = EPI == kLinearSwiGLU;
-  const int n0 = blockIdx.x * (kSwiGLU ? T::BN / 2 : T::BN);  // first output column
+  constexpr int OUT = kSwiGLU ? BN / 2 : BN;  // output columns of this CTA
+  const int n0 = blockIdx.x * OUT;            // first output column
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < T::STAGES; ++s) {
@@ -60,32 +71,46 @@ __global__ void __launch_bounds__(192, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 64);
+  if (warp == 1) tmem_alloc(tmem_slot, T::TMEM_COLS);
   __syncthreads();
   tc_fence_after();
+  griddep_launch_dependents();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
     if (elect_one()) {
       prefetch_tensormap(&tmX);
       prefetch_tensormap(&tmW);
-      int issued = 0;
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % T::STAGES;
-        if (!mbar_wait(&empty[s], ((kb / T::STAGES) & 1) ^ 1)) {
-          *abort_flag = 1;
-          break;
-        }
-        // with at most 32 rows only the first 32 rows of the A tile are loaded: the other lanes of
-        // the accumulator are computed from stale shared memory and never stored
-        mbar_arrive_expect_tx(&full[s], a_rows * T::BK * 2 + T::B_BYTES);
-        tma_load_2d(sA + s * T::A_BYTES, &tmX, &full[s], kb * T::BK, m0);
-        if constexpr (kSwiGLU) {  // gate rows [n0, n0 + 32) then up rows [F + n0, F + n0 + 32)
+      auto load_w = [&](int kb, int s) {
+        if constexpr (kSwiGLU) {  // gate rows [n0, n0 + BN/2) then up rows [F + n0, F + n0 + BN/2)
           tma_load_2d(sB + s * T::B_BYTES, &tmW, &full[s], kb * T::BK, n0);
           tma_load_2d(sB + s * T::B_BYTES + T::B_BYTES / 2, &tmW, &full[s], kb * T::BK, f_rows + n0);
         } else {
           tma_load_2d(sB + s * T::B_BYTES, &tmW, &full[s], kb * T::BK, n0);
         }
+      };
+      // with at most 32 rows only the first 32 rows of the A tile are loaded: the other lanes of
+      // the accumulator are computed from stale shared memory and never stored
+      const uint32_t stage_tx = a_rows * T::BK * 2 + T::B_BYTES;
+      // the weights do not depend on the previous kernel: the first ring's worth streams in
+      // before griddep_wait(), the activations after it
+      const int pre = KB < T::STAGES ? KB : T::STAGES;
+      for (int kb = 0; kb < pre; ++kb) {
+        mbar_arrive_expect_tx(&full[kb], stage_tx);
+        load_w(kb, kb);
+      }
+      griddep_wait();
+      for (int kb = 0; kb < pre; ++kb) tma_load_2d(sA + kb * T::A_BYTES, &tmX, &full[kb], kb * T::BK, m0);
+      int issued = pre;
+      for (int kb = pre; kb < KB; ++kb) {
+        const int s = kb % T::STAGES;
+        if (!mbar_wait(&empty[s], ((kb / T::STAGES) & 1) ^ 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], stage_tx);
+        tma_load_2d(sA + s * T::A_BYTES, &tmX, &full[s], kb * T::BK, m0);
+        load_w(kb, s);
         issued = kb + 1;
       }
       if (*abort_flag)
@@ -94,7 +119,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      constexpr uint32_t idesc = umma_idesc_bf16(128, T::BN, false, false);
+      constexpr uint32_t idesc = umma_idesc_bf16(128, BN, false, false);
       bool ok = true;
       for (int kb = 0; kb < KB; ++kb) {
         const int s = kb % T::STAGES;
@@ -115,39 +140,40 @@ __global__ void __launch_bounds__(192, 1)
       umma_commit(acc_full);  // also the drain: every MMA issued has completed when it fires
     }
   } else {
+    griddep_wait();  // the residual and Y belong to the stream order from here on
     const int quarter = warp & 3;
     const int row = m0 + quarter * 32 + lane;
     const bool done = mbar_wait(acc_full, 0) && !*abort_flag;
     tc_fence_after();
     const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    float v[64];
+    float v[BN < 32 ? 32 : BN];  // columns past BN (BN = 16) are allocated but never written
     tmem_ld32(base, v);
-    tmem_ld32(base + 32, v + 32);
+    if constexpr (BN == 64) tmem_ld32(base + 32, v + 32);
     tmem_wait_ld();
     if (done && row < M) {
       if constexpr (kSwiGLU) {
         // the roundings of silu_mul(x @ [gate; up]^T): g and u rounded, silu rounded, product
-        uint32_t pk[16];
+        uint32_t pk[OUT / 2];
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
+        for (int j = 0; j < OUT; j += 2) {
           float h[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const float gr = round_to_t<__nv_bfloat16>(v[j + e]);
-            const float ur = round_to_t<__nv_bfloat16>(v[32 + j + e]);
+            const float ur = round_to_t<__nv_bfloat16>(v[OUT + j + e]);
             h[e] = round_to_t<__nv_bfloat16>(silu_fast(gr)) * ur;
           }
           pk[j / 2] = pack_bf16x2(h[0], h[1]);
         }
         uint4* dst = reinterpret_cast<uint4*>(Y + static_cast<int64_t>(row) * ldy + n0);
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+        for (int q = 0; q < OUT / 8; ++q)
           if (n0 + 8 * q < N) dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
       } else {
         if constexpr (EPI == kLinearResidual) {
           const uint4* src = reinterpret_cast<const uint4*>(R + static_cast<int64_t>(row) * ldr + n0);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
+          for (int j = 0; j < OUT / 8; ++j) {
             if (n0 + 8 * j >= N) break;
             const uint4 r = src[j];
             const uint32_t w[4] = {r.x, r.y, r.z, r.w};
@@ -160,7 +186,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         uint4* dst = reinterpret_cast<uint4*>(Y + static_cast<int64_t>(row) * ldy + n0);
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
+        for (int q = 0; q < OUT / 8; ++q)
           if (n0 + 8 * q < N)
             dst[q] = make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
                                 pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
@@ -171,8 +197,31 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_free(tmem, 64);
+    tmem_free(tmem, T::TMEM_COLS);
   }
+}
+
+template <int EPI, int BN, int AROWS>
+inline cudaError_t skinny_launch(const CUtensorMap& tx, const CUtensorMap& tw, int M, int N, int K, int f_rows,
+                                 const __nv_bfloat16* R, int64_t ldr, __nv_bfloat16* Y, int64_t ldy, int a_rows,
+                                 cudaStream_t stream) {
+  using T = SkinnyTile<BN, AROWS>;
+  auto kernel = linear_skinny_tc_kernel<EPI, BN, AROWS>;
+  cudaError_t e = ensure_smem(kernel, T::SMEM);
+  if (e != cudaSuccess) return e;
+  const int out = EPI == kLinearSwiGLU ? BN / 2 : BN;
+  const dim3 grid(static_cast<unsigned>(N / out), static_cast<unsigned>(ceil_div(M, T::BM)));
+  return launch_pdl(kernel, grid, dim3(192), T::SMEM, stream, tx, tw, M, N, K, f_rows, R, ldr, Y, ldy, a_rows);
+}
+
+// Output columns per CTA: the widest tile (64, 32 or 16 accumulator columns) that still gives at
+// least 128 CTAs, else 16. A narrower tile only splits the columns: every output element keeps the
+// same k order, so all widths (and the 128 x 256 persistent kernel) give the same bits.
+inline int skinny_tile_n(int64_t M, int64_t acc_cols) {
+  const int64_t mt = ceil_div(M, 128);
+  for (int bn : {64, 32})
+    if ((acc_cols / bn) * mt >= 128) return bn;
+  return 16;
 }
 
 // Y [M, N] (pitch ldy) = X [M, K] @ W^T (+ R), or for SwiGLU Y [M, F] = silu(X gate^T) * (X up^T)
@@ -187,28 +236,42 @@ inline int linear_skinny_impl(const void* X, int64_t ldx, const void* W, int64_t
   ORTHRUS_CHECK_ARG(epilogue != kLinearResidual || (R != nullptr && aligned16(R)));
   ORTHRUS_CHECK_ARG(aligned16(X) && aligned16(W) && aligned16(Y));
   ORTHRUS_CHECK_ARG(M < (1ll << 31) && N < (1ll << 30) && K < (1ll << 31));
+  ORTHRUS_CHECK_ARG(ceil_div(M, 128) < 65536);
   if (M == 0) return ORTHRUS_OK;
-  using T = SkinnyTile;
   const bool swiglu = epilogue == kLinearSwiGLU;
+  const int bn = skinny_tile_n(M, swiglu ? 2 * N : N);
   CUtensorMap tx, tw;
   const int a_rows = M <= 32 ? 32 : 128;  // rows of X per A box
   if (!make_tmap_2d_bf16(&tx, X, K, M, ldx, 64, a_rows)) return ORTHRUS_ECUDA;
-  if (!make_tmap_2d_bf16(&tw, W, K, swiglu ? 2 * N : N, ldw, 64, swiglu ? 32 : 64)) return ORTHRUS_ECUDA;
-  dim3 grid(static_cast<unsigned>(N / (swiglu ? 32 : 64)), static_cast<unsigned>(ceil_div(M, T::BM)));
-  ORTHRUS_CHECK_ARG(grid.y < 65536);
+  if (!make_tmap_2d_bf16(&tw, W, K, swiglu ? 2 * N : N, ldw, 64, swiglu ? bn / 2 : bn)) return ORTHRUS_ECUDA;
   auto* r = static_cast<const __nv_bfloat16*>(R);
   auto* y = static_cast<__nv_bfloat16*>(Y);
   const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
-  if (epilogue == kLinearStore) {
-    ORTHRUS_CHECK_CUDA(ensure_smem(linear_skinny_tc_kernel<kLinearStore>, T::SMEM));
-    linear_skinny_tc_kernel<kLinearStore><<<grid, 192, T::SMEM, stream>>>(tx, tw, m, n, k, 0, nullptr, 0, y, ldy, a_rows);
-  } else if (epilogue == kLinearResidual) {
-    ORTHRUS_CHECK_CUDA(ensure_smem(linear_skinny_tc_kernel<kLinearResidual>, T::SMEM));
-    linear_skinny_tc_kernel<kLinearResidual><<<grid, 192, T::SMEM, stream>>>(tx, tw, m, n, k, 0, r, ldy, y, ldy, a_rows);
-  } else {
-    ORTHRUS_CHECK_CUDA(ensure_smem(linear_skinny_tc_kernel<kLinearSwiGLU>, T::SMEM));
-    linear_skinny_tc_kernel<kLinearSwiGLU><<<grid, 192, T::SMEM, stream>>>(tx, tw, m, n, k, n, nullptr, 0, y, ldy, a_rows);
+  cudaError_t e;
+#define ORTHRUS_SKINNY3(EPI_, BN_, AR_)                                                                          \
+  e = skinny_launch<EPI_, BN_, AR_>(tx, tw, m, n, k, EPI_ == kLinearSwiGLU ? n : 0,                              \
+                                    EPI_ == kLinearResidual ? r : nullptr, ldy, y, ldy, a_rows, stream)
+#define ORTHRUS_SKINNY(EPI_, BN_) \
+  if (a_rows == 32) ORTHRUS_SKINNY3(EPI_, BN_, 32); else ORTHRUS_SKINNY3(EPI_, BN_, 128)
+#define ORTHRUS_SKINNY_BN(EPI_)                      \
+  if (bn == 64) {                                    \
+    ORTHRUS_SKINNY(EPI_, 64);                        \
+  } else if (bn == 32) {                             \
+    ORTHRUS_SKINNY(EPI_, 32);                        \
+  } else {                                           \
+    ORTHRUS_SKINNY(EPI_, 16);                        \
   }
+  if (epilogue == kLinearStore) {
+    ORTHRUS_SKINNY_BN(kLinearStore);
+  } else if (epilogue == kLinearResidual) {
+    ORTHRUS_SKINNY_BN(kLinearResidual);
+  } else {
+    ORTHRUS_SKINNY_BN(kLinearSwiGLU);
+  }
+#undef ORTHRUS_SKINNY_BN
+#undef ORTHRUS_SKINNY
+#undef ORTHRUS_SKINNY3
+  ORTHRUS_CHECK_CUDA(e);
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
 }

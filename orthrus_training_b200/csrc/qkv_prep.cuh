@@ -346,6 +346,8 @@ __global__ void __launch_bounds__(256, 4) qkv_prep_fwd_row_kernel(
   // ... with the same per-head arithmetic, so the result does not depend on wpr
   const int warp = threadIdx.x >> 5, sub = warp % wpr;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (8 / wpr) + warp / wpr;
+  griddep_launch_dependents();  // launched as a programmatic dependent
+  griddep_wait();
   if (row >= rows) return;
   const int64_t b = row / Tn, t = row % Tn;
   const int heads = Hq + 2 * Hkv;
@@ -507,6 +509,147 @@ __global__ void __launch_bounds__(256, 3) qkv_prep_bwd_row_kernel(
 }
 
 
+// Backward of the row prologue for bf16, head dim 128, with the next group's loads in flight while
+// the current group is computed. Same per-element arithmetic as qkv_prep_bwd_row_kernel; the work
+// of a warp is its rows (fixed grid, fixed order) split into groups of kPipePer heads of one kind
+// (q, k or v; the host checks Hq and Hkv are multiples of kPipePer). Group i + 1's gradient and
+// input rows are loaded into a second register set before group i is computed, so each warp keeps
+// a group's bytes in flight without a gap between groups and rows. The loaded words are converted
+// only when their group is computed, so the loads never stall the warp early.
+constexpr int kPipePer = 4;
+constexpr int kPipeBlocks = 296;  // 2 x 148: two CTAs of 8 warps per SM, one wave
+
+struct PipeGroup {
+  float4 g[kPipePer];   // incoming gradient, 4 fp32 elements of each head for this lane
+  uint2 x[kPipePer];    // projection input, 4 bf16 elements of each q / k head
+  float r[kPipePer];    // rstd of each q / k head
+  float pos;            // the row's position (read for the first group of a row)
+};
+
+struct PipeShape {
+  const __nv_bfloat16* qkv; const int64_t* positions; const float* rstd;
+  const float* dq; const float* dk; const float* dv;
+  int64_t rows, Tn, first, stride; int Hq, Hkv, D, heads, groups;
+};
+
+__device__ __forceinline__ void pipe_where(const PipeShape& s, int64_t i, int64_t& row, int& head0, int& kind,
+                                           int& h) {
+  row = s.first + (i / s.groups) * s.stride;
+  head0 = static_cast<int>(i % s.groups) * kPipePer;
+  kind = head0 < s.Hq ? 0 : head0 < s.Hq + s.Hkv ? 1 : 2;  // q, k, v
+  h = kind == 0 ? head0 : kind == 1 ? head0 - s.Hq : head0 - s.Hq - s.Hkv;
+}
+
+__device__ __forceinline__ void pipe_load(const PipeShape& s, int64_t i, int lane, PipeGroup& G) {
+  int64_t row;
+  int head0, kind, h;
+  pipe_where(s, i, row, head0, kind, h);
+  const int64_t b = row / s.Tn, t = row % s.Tn;
+  const float* gsrc = kind == 0 ? s.dq : kind == 1 ? s.dk : s.dv;
+  const int H = kind == 0 ? s.Hq : s.Hkv;
+#pragma unroll
+  for (int j = 0; j < kPipePer; ++j) {
+    G.g[j] = gsrc ? __ldg(reinterpret_cast<const float4*>(gsrc + ((b * H + h + j) * s.Tn + t) * s.D) + lane)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (kind != 2 && gsrc) {
+      G.x[j] = __ldg(reinterpret_cast<const uint2*>(s.qkv + row * static_cast<int64_t>(s.heads) * 128 +
+                                                    (head0 + j) * 128) + lane);
+      G.r[j] = __ldg(s.rstd + row * (s.Hq + s.Hkv) + head0 + j);
+    }
+  }
+  if (head0 == 0) G.pos = static_cast<float>(__ldg(s.positions + row));
+}
+
+__device__ __forceinline__ void pipe_compute(const PipeShape& s, int64_t i, int lane, const PipeGroup& G,
+                                             const float* __restrict__ inv_freq, const float* nq, const float* nk,
+                                             float* cs, float* sn, float* wq, float* wk,
+                                             __nv_bfloat16* __restrict__ dqkv) {
+  constexpr int NE = 4, HALF = 64;
+  int64_t row;
+  int head0, kind, h;
+  pipe_where(s, i, row, head0, kind, h);
+  if (head0 == 0) rope_lane_table<__nv_bfloat16, 128>(G.pos, inv_freq, lane, cs, sn);
+  const float* gsrc = kind == 0 ? s.dq : kind == 1 ? s.dk : s.dv;
+#pragma unroll
+  for (int j = 0; j < kPipePer; ++j) {
+    __nv_bfloat16* out = dqkv + row * static_cast<int64_t>(s.heads) * 128 + (head0 + j) * 128 + lane * NE;
+    const float gv[NE] = {G.g[j].x, G.g[j].y, G.g[j].z, G.g[j].w};
+    if (kind == 2 || gsrc == nullptr) {
+      store_elems<__nv_bfloat16, NE>(out, gv);  // dV passes through; a missing gradient is zero
+      continue;
+    }
+    const float xv[NE] = {__uint_as_float(G.x[j].x << 16), __uint_as_float(G.x[j].x & 0xffff0000u),
+                          __uint_as_float(G.x[j].y << 16), __uint_as_float(G.x[j].y & 0xffff0000u)};
+    const float r = G.r[j];
+    const float* w = kind == 0 ? nq : nk;
+    float xh[NE], gr[NE], o[NE];
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < NE; ++k) {
+      xh[k] = xv[k] * r;
+      const float partner = __shfl_xor_sync(0xffffffffu, gv[k], 16);
+      const float other = (lane * NE + k) < HALF ? partner : -partner;
+      gr[k] = gv[k] * cs[k] + other * sn[k];
+      dot = fmaf(gr[k] * w[k], xh[k], dot);
+      if (kind == 0)
+        wq[k] = fmaf(gr[k], xh[k], wq[k]);
+      else
+        wk[k] = fmaf(gr[k], xh[k], wk[k]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    const float mean = dot / 128.f;
+#pragma unroll
+    for (int k = 0; k < NE; ++k) o[k] = r * (gr[k] * w[k] - xh[k] * mean);
+    store_elems<__nv_bfloat16, NE>(out, o);
+  }
+}
+
+__global__ void __launch_bounds__(256, 2) qkv_prep_bwd_pipe_kernel(
+    const __nv_bfloat16* __restrict__ qkv, const int64_t* __restrict__ positions, const float* __restrict__ inv_freq,
+    const __nv_bfloat16* __restrict__ q_norm_w, const __nv_bfloat16* __restrict__ k_norm_w,
+    const float* __restrict__ rstd, const float* __restrict__ dq, const float* __restrict__ dk,
+    const float* __restrict__ dv, int64_t rows, int64_t Tn, int Hq, int Hkv, int D,
+    __nv_bfloat16* __restrict__ dqkv, float* __restrict__ part_q, float* __restrict__ part_k) {
+  constexpr int NE = 4;
+  __shared__ float wpart[2][8][128];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  PipeShape s{qkv, positions, rstd, dq, dk, dv, rows, Tn, static_cast<int64_t>(blockIdx.x) * 8 + warp,
+              static_cast<int64_t>(gridDim.x) * 8, Hq, Hkv, D, Hq + 2 * Hkv, (Hq + 2 * Hkv) / kPipePer};
+  const int64_t my_rows = s.first < rows ? (rows - 1 - s.first) / s.stride + 1 : 0;
+  const int64_t iters = my_rows * s.groups;
+  float wq[NE], wk[NE], nq[NE], nk[NE], cs[NE], sn[NE];
+#pragma unroll
+  for (int k = 0; k < NE; ++k) wq[k] = wk[k] = cs[k] = sn[k] = 0.f;
+  load_elems<__nv_bfloat16, NE>(q_norm_w + lane * NE, nq);
+  load_elems<__nv_bfloat16, NE>(k_norm_w + lane * NE, nk);
+  PipeGroup A, B;
+  if (iters > 0) pipe_load(s, 0, lane, A);
+  for (int64_t i = 0; i < iters; i += 2) {
+    if (i + 1 < iters) pipe_load(s, i + 1, lane, B);
+    pipe_compute(s, i, lane, A, inv_freq, nq, nk, cs, sn, wq, wk, dqkv);
+    if (i + 1 < iters) {
+      if (i + 2 < iters) pipe_load(s, i + 2, lane, A);
+      pipe_compute(s, i + 1, lane, B, inv_freq, nq, nk, cs, sn, wq, wk, dqkv);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NE; ++k) {
+    wpart[0][warp][lane * NE + k] = wq[k];
+    wpart[1][warp][lane * NE + k] = wk[k];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < 128; e += blockDim.x) {
+    float aq = 0.f, ak = 0.f;
+    for (int w = 0; w < 8; ++w) {
+      aq += wpart[0][w][e];
+      ak += wpart[1][w][e];
+    }
+    part_q[static_cast<int64_t>(blockIdx.x) * 128 + e] = aq;
+    part_k[static_cast<int64_t>(blockIdx.x) * 128 + e] = ak;
+  }
+}
+
 template <typename T>
 int qkv_prep_fwd_impl(const T* qkv, const int64_t* positions, const float* inv_freq, const T* qw, const T* kw,
                       int64_t B, int64_t Tn, int Hq, int Hkv, int hd, int D, float eps, T* q_out, T* k_out,
@@ -522,14 +665,17 @@ int qkv_prep_fwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
     const int wpr = rows < 4 * 148 * 8 ? 8 : 1;  // few rows: a CTA per row, its 8 warps share the heads
     const unsigned grid = static_cast<unsigned>(ceil_div(rows, 8 / wpr));
     if (hd == 128)
-      qkv_prep_fwd_row_kernel<T, 128><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
-                                                               q_out, k_out, v_out, cap, offset, rstd, wpr);
+      ORTHRUS_CHECK_CUDA(launch_pdl(qkv_prep_fwd_row_kernel<T, 128>, dim3(grid), dim3(256), 0, stream, qkv, positions,
+                                    inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps, q_out, k_out, v_out, cap,
+                                    offset, rstd, wpr));
     else if (hd == 64)
-      qkv_prep_fwd_row_kernel<T, 64><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
-                                                              q_out, k_out, v_out, cap, offset, rstd, wpr);
+      ORTHRUS_CHECK_CUDA(launch_pdl(qkv_prep_fwd_row_kernel<T, 64>, dim3(grid), dim3(256), 0, stream, qkv, positions,
+                                    inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps, q_out, k_out, v_out, cap,
+                                    offset, rstd, wpr));
     else
-      qkv_prep_fwd_row_kernel<T, 32><<<grid, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps,
-                                                              q_out, k_out, v_out, cap, offset, rstd, wpr);
+      ORTHRUS_CHECK_CUDA(launch_pdl(qkv_prep_fwd_row_kernel<T, 32>, dim3(grid), dim3(256), 0, stream, qkv, positions,
+                                    inv_freq, qw, kw, rows, Tn, Hq, Hkv, D, eps, q_out, k_out, v_out, cap,
+                                    offset, rstd, wpr));
     ORTHRUS_CHECK_LAUNCH();
     return ORTHRUS_OK;
   }
@@ -556,6 +702,18 @@ int qkv_prep_bwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
   const int64_t rows = B * Tn;
   const bool vec_ok = D % 8 == 0 && aligned16(qkv) && aligned16(qw) && aligned16(kw) && aligned16(dqkv) &&
                       (!dq || aligned16(dq)) && (!dk || aligned16(dk)) && (!dv || aligned16(dv));
+  if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+    if (vec_ok && hd == 128 && D % 4 == 0 && Hq % kPipePer == 0 && Hkv % kPipePer == 0) {
+      qkv_prep_bwd_pipe_kernel<<<kPipeBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rstd, dq, dk, dv,
+                                                                rows, Tn, Hq, Hkv, D, dqkv, part_q, part_k);
+      ORTHRUS_CHECK_LAUNCH();
+      sum_partials_kernel<<<(hd + 7) / 8, 256, 0, stream>>>(part_q, kPipeBlocks, hd, dqw);
+      ORTHRUS_CHECK_LAUNCH();
+      sum_partials_kernel<<<(hd + 7) / 8, 256, 0, stream>>>(part_k, kPipeBlocks, hd, dkw);
+      ORTHRUS_CHECK_LAUNCH();
+      return ORTHRUS_OK;
+    }
+  }
   if (vec_ok && (hd == 128 || hd == 64 || hd == 32)) {
     if (hd == 128)
       qkv_prep_bwd_row_kernel<T, 128><<<kPrepBwdBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rstd, dq, dk,

@@ -59,6 +59,8 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_vec_kernel(const T* __restric
   constexpr int N = Vec16<T>::N;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  griddep_launch_dependents();  // launched as a programmatic dependent
+  griddep_wait();
   if (r >= rows) return;
   const T* xr = x + r * d;
   float ss = 0.f;
@@ -189,7 +191,7 @@ __global__ void swiglu_bwd_kernel(const T* __restrict__ gu, const T* __restrict_
     load16<T>(dout + r * I + c, d);
 #pragma unroll
     for (int i = 0; i < N; ++i) {
-      const float sg = 1.f / (1.f + expf(-g[i]));
+      const float sg = sigmoid_fast(g[i]);
       const float s = round_to_t<T>(g[i] * sg);
       const float ds = round_to_t<T>(d[i] * u[i]);
       dg[i] = ds * sg * (1.f + g[i] * (1.f - sg));

@@ -37,6 +37,18 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 
 __device__ __forceinline__ void record_error(unsigned int code) { atomicOr(&g_device_error, code); }
 
+// Programmatic dependent launch. A kernel launched with the programmatic stream serialization
+// attribute may start while the kernel before it on the stream is still running; griddep_wait()
+// blocks (in hardware, no spinning) until that kernel has completed and its memory operations are
+// visible, and returns at once for a kernel launched without the attribute. Every read of data the
+// previous kernel may write, and every write of data it may read, comes after griddep_wait().
+// griddep_launch_dependents() lets the next such kernel start once every CTA of this grid has
+// called it (or exited); it never makes that kernel skip its own griddep_wait().
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(
@@ -317,9 +329,23 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// 1 / (1 + exp(-g)) from ex2.approx and an approximate reciprocal (within a few fp32 ulps of the
+// IEEE form; 0 and 1 at the extremes).
+__device__ __forceinline__ float sigmoid_fast(float g) { return __fdividef(1.f, 1.f + ex2_approx(-g * kLog2e)); }
+
+// x rounded to bf16 and back (round to nearest even).
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {

@@ -576,3 +576,65 @@ def silu_mul_backward(gate_up: torch.Tensor, dout: torch.Tensor) -> torch.Tensor
                                        dgu.data_ptr(), L.dtype_code(gate_up.dtype),
                                        L.stream_of(gate_up.device)), "swiglu_bwd")
     return dgu.view(shape)
+
+
+# --- per-entry-point timing (the breakdown pass of bench.py) -------------------------------------
+# Every public op below records CUDA events on its launching stream around the call when ops.TIMER
+# is set (attention and the LM head record their own, with their FLOP counts). Projections carry
+# their GEMM FLOPs and the "proj_" prefix; the row kernels report time only. Nested timed calls
+# are not counted twice.
+
+_timing_depth = 0
+
+
+def _timed(fn, label, work):
+    import functools
+
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        global _timing_depth
+        if TIMER is None or _timing_depth:
+            return fn(*args, **kwargs)
+        _timing_depth += 1
+        try:
+            t0 = TIMER.begin()
+            out = fn(*args, **kwargs)
+            TIMER.end(label, t0, work(*args, **kwargs) if work is not None else 0.0)
+        finally:
+            _timing_depth -= 1
+        return out
+
+    return wrapper
+
+
+def _gemm2_work(a, b, *, a_t=False, b_t=False, residual=None):
+    M, K = (a.shape[1], a.shape[0]) if a_t else a.shape
+    return 2.0 * M * (b.shape[1] if b_t else b.shape[0]) * K
+
+
+def _rows_cols_work(x, w, *args, **kwargs):  # x [M, K] @ w [N, K]^T
+    return 2.0 * x.shape[0] * w.shape[0] * x.shape[1]
+
+
+def _gemm_work(a, b, *, b_kn=False, **kwargs):
+    return 2.0 * a.shape[0] * (b.shape[1] if b_kn else b.shape[0]) * a.shape[1]
+
+
+for _name, _label, _work in (
+        ("gemm2", "proj_gemm2", _gemm2_work),
+        ("gemm2_swiglu_backward", "proj_gemm2_swiglu_bwd",
+         lambda dy, w, gu: 2.0 * dy.shape[0] * w.shape[1] * dy.shape[1]),
+        ("linear", "proj_linear", _rows_cols_work),
+        ("linear_swiglu", "proj_linear_swiglu", _rows_cols_work),
+        ("linear_qkv_rope", "proj_linear_qkv_rope", _rows_cols_work),
+        ("gemm", "proj_gemm", _gemm_work),
+        ("qkv_prep", "qkv_prep", None),
+        ("qkv_prep_backward", "qkv_prep_bwd", None),
+        ("rms_norm", "rms_norm", None),
+        ("rms_norm_backward", "rms_norm_bwd", None),
+        ("silu_mul", "swiglu", None),
+        ("silu_mul_backward", "swiglu_bwd", None),
+        ("lmhead_kl_backward", "lmhead_kl_bwd_scale", None),
+        ("add", "add", None),
+        ("rope_table", "rope_table", None)):
+    globals()[_name] = _timed(globals()[_name], _label, _work)

@@ -159,6 +159,32 @@ def test_sweep_shape_dual_view_attention_vs_fp32(L, K, A):
     assert _lib.device_error(0) == 0
 
 
+@pytest.mark.parametrize("Hq,Hkv", [(16, 8), (16, 4)])
+def test_own_block_key_gradients_of_32_key_blocks(Hq, Hkv):
+    """dK / dV of the own-block keys with 32-key blocks (the HBM-bound 32 x 32 kernel) for two and
+    four query heads per KV head, against the fp32 dense-mask backward: relative to the largest
+    gradient, within the bf16 rounding of P and dS."""
+    from orthrus_training_b200 import _lib, ops
+
+    B, L, K, A, hd = 2, 1024, 32, 24, 128
+    gen = torch.Generator(device=DEV).manual_seed(Hq * 31 + Hkv)
+    Tq = A * K
+    rnd = lambda *s: torch.randn(*s, device=DEV, generator=gen).bfloat16()  # noqa: E731
+    q, k1, v1, k2, v2 = rnd(B, Hq, Tq, hd), rnd(B, Hkv, L, hd), rnd(B, Hkv, L, hd), rnd(B, Hkv, Tq, hd), \
+        rnd(B, Hkv, Tq, hd)
+    anchors = torch.stack([torch.randperm(L - K, device=DEV, generator=gen)[:A].add(1).sort().values
+                           for _ in range(B)])
+    scale = 1.0 / math.sqrt(hd)
+    o, lse = ops.attention_fwd(q, k1, v1, k2, v2, mask=1, hd=hd, scale=scale, anchors=anchors, block=K)
+    dout = rnd(B, Tq, Hq, hd)
+    _, dk2, dv2 = ops.attention_bwd(q, k1, v1, k2, v2, anchors, K, o, lse, dout, hd=hd, scale=scale)
+    _, _, rdk, rdv = _dense_dual_reference(q, k1, v1, k2, v2, anchors, K, dout, scale)
+    for name, got, want in (("dk2", dk2, rdk), ("dv2", dv2, rdv)):
+        err = (got - want).abs().max().item()
+        assert err <= 2e-2 * want.abs().max().item(), (name, err, want.abs().max().item())
+    assert _lib.device_error(0) == 0
+
+
 def test_06b_fp32_block_decode_equals_oracle_greedy():
     """fp32, Qwen3-0.6B layer shape with 2 layers, random init: block decoding with the model's
     own drafts and with scripted drafts (the oracle's greedy continuation, 5 % of tokens edited)
