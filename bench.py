@@ -257,6 +257,11 @@ def run_decode(args):
         rng = np.random.default_rng(2 + batch + 1000 * rank)
         prompts = [zipf_ids(rng, int(rng.integers(128, 513)), REAL_VOCAB).tolist() for _ in range(batch)]
         with torch.inference_mode():
+            # the kernels and graph shapes of this batch size are loaded / captured once before the
+            # timed calls (lazy module loading would otherwise land inside them)
+            block_decode(model, prompts, 16)
+            block_decode(model, prompts, 16, draft_table=torch.zeros(batch, 16, K - 1, dtype=torch.int64,
+                                                                   device=dev))
             plain, plain_s = timed_decode(prompts)
             ref = plain.tokens
             # scripted drafts: the true continuation after each anchor, 5 % of tokens edited
@@ -577,7 +582,7 @@ def step_roofline(cfg, kernels: dict, steps: int, ms_per_step: float, pk: dict) 
     linear = 2.0 * L * (teacher_tokens * per_layer + 2 * student_tokens * per_layer
                         + student_tokens * (qkv + o))
     # the projections are counted in `linear` above, whichever kernel ran them
-    kernel_flops = sum(v["flops"] for k, v in kernels.items() if k != "projections") / steps
+    kernel_flops = sum(v["flops"] for k, v in kernels.items() if not k.startswith("proj_")) / steps
     total = linear + kernel_flops
     achieved = total / (ms_per_step / 1e3) / 1e12
     return {"tflop_per_step": round(total / 1e12, 2), "achieved": round(achieved, 1),
@@ -667,12 +672,15 @@ def run_ours(args):
     launches = (_lib.launch_count() - launches0) // max(args.steps, 1)
     loss = float(out["loss"])
 
-    # the same steps again with CUDA events around every timed entry point (on its launching
-    # stream) for the per-kernel breakdown; recording the events adds host work, so this pass is
-    # kept out of the headline number
+    # the same steps again with CUDA events around every entry point (on its launching stream)
+    # for the per-kernel breakdown, kept out of the headline number. Recording ~1700 events a step
+    # makes the host the slower side, and an event pair would then also time the host's gap before
+    # the launch; so each step starts behind a ~60 ms device sleep that lets the host queue the
+    # whole step first, and the pairs time device work only.
     ops.TIMER = ops.KernelTimer()
     barrier(world)
     for _ in range(args.steps):
+        torch.cuda._sleep(100_000_000)
         trainer.step([(ids_dev, mask_dev)], ready=resident)
     barrier(world)
     kernels = ops.TIMER.summary()
@@ -720,14 +728,15 @@ def run_ours(args):
         name, rec = dominant
         per_launch_ms = rec["ms"] / rec["launches"]
         achieved = rec["flops"] / rec["launches"] / (per_launch_ms / 1e3) / 1e12
-        peak = pk["bf16_tflops"]
+        # the kernel is timed inside seconds of back-to-back steps: the sustained peak applies
+        peak = pk["bf16_tflops_sustained"]
         traffic = None
         tfile = ROOT / "profiles" / "traffic.json"
         if tfile.exists():
             traffic = json.loads(tfile.read_text()).get(name)
         roofline = {"bound": "tensor", "kernel": name, "achieved": round(achieved, 1),
                     "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                    "traffic": traffic, "peak_source": pk["source"],
+                    "traffic": traffic, "peak_source": pk["source"], "peak_kind": "sustained",
                     "ms_per_launch": round(per_launch_ms, 4), "launches_per_step": rec["launches"] // args.steps}
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "input tok/s", "n_gpus": world,
@@ -747,7 +756,10 @@ def run_ours(args):
         "kernels": {k: {"launches_per_step": v["launches"] // args.steps,
                         "ms_per_step": round(v["ms"] / args.steps, 3),
                         "tflops": round(v["flops"] / (v["ms"] / 1e3) / 1e12, 1) if v["ms"] else None}
-                    for k, v in kernels.items()},
+                    for k, v in sorted(kernels.items(), key=lambda kv: -kv[1]["ms"])},
+        # step time not inside any library entry point: torch's AdamW, clipping, gathers and the
+        # gaps between launches
+        "unattributed_ms_per_step": round(ms / args.steps - sum(v["ms"] for v in kernels.values()) / args.steps, 3),
         "loss": round(loss, 5),
         "clocks": clocks.summary(),
     }

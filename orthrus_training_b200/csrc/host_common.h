@@ -161,4 +161,35 @@ inline bool make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, u
   return r == CUDA_SUCCESS;
 }
 
+// K-blocked view of a row-major bf16 matrix [rows, K] (pitch elements, K a multiple of 64) for
+// TMA boxes that carry several 64-column k-blocks at once: dims (64, rows, K / 64) with strides
+// (pitch, 64) elements, box (64, box_rows, kblocks), 128-byte swizzle. A box lands in shared
+// memory as kblocks consecutive [box_rows][64] K-major tiles, the layout a UMMA operand takes.
+// With halves > 1 the rows are split into `halves` groups `half_stride` rows apart (dims (64,
+// rows / halves, halves, K / 64)): a box then holds box_rows rows from each group in turn.
+inline bool make_tmap_kblocked_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t K, uint64_t pitch,
+                                    uint32_t box_rows, uint32_t kblocks, uint32_t halves = 1,
+                                    uint64_t half_stride = 0) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (fn == nullptr || K % 64 != 0) return false;
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r;
+  if (halves == 1) {
+    cuuint64_t dims[3] = {64, rows, K / 64};
+    cuuint64_t strides[2] = {pitch * 2, 128};
+    cuuint32_t box[3] = {64, box_rows, kblocks};
+    r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[4] = {64, rows / halves, halves, K / 64};
+    cuuint64_t strides[3] = {pitch * 2, half_stride * pitch * 2, 128};
+    cuuint32_t box[4] = {64, box_rows, halves, kblocks};
+    r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  return r == CUDA_SUCCESS;
+}
+
 }  // namespace orthrus

@@ -3,11 +3,13 @@
 //
 // A decode pass multiplies 32 rows (one block) per sequence by every weight of the model, so a
 // projection is a stream of its weights: what bounds it is how many SMs pull weight rows at once.
-// Each CTA here owns a 128-row x 64-column output tile (for SwiGLU 32 output columns: 32 gate and
-// 32 up rows of W) and the full K, so a [32, 1024] x [1024, 3072] projection runs on 48 CTAs
-// instead of the 12 of a 256-column tile. A row's result depends only on its own inputs and the
-// fixed k order, never on M: a K-token verification reproduces a one-token greedy pass bit for
-// bit, which is what keeps block decoding lossless.
+// Each CTA here owns a 128-row x BN-column output tile (BN = 64, 32 or 16 accumulator columns; for
+// SwiGLU BN/2 gate and BN/2 up rows of W) and the full K, so a [32, 1024] x [1024, 3072]
+// projection runs on 96-192 CTAs instead of the 12 of a 256-column tile. A row's result depends
+// only on its own inputs and the k order, never on M or BN, and equals what the persistent
+// 128 x 256 kernel gives it: a K-token verification reproduces one-token greedy passes bit for
+// bit whichever of the two kernels a pass's row count selects, which keeps block decoding
+// lossless.
 //
 // 192 threads: warp 0 TMA producer (ring of X [rows x 64] and W [BN x 64] k-blocks, as many stages
 // as about 196 KB holds; for at most 32 rows only 32 rows of X are loaded and stored per stage),
@@ -23,16 +25,25 @@ namespace orthrus {
 template <int BN_, int AROWS_>
 struct SkinnyTile {
   static constexpr int BM = 128, BN = BN_, BK = 64, AROWS = AROWS_;
-  static constexpr int A_BYTES = AROWS * BK * 2;  // the rows of X a stage holds: 4 KB (32) or 16 KB (128)
-  static constexpr int B_BYTES = BN * BK * 2;     // 2 / 4 / 8 KB (a whole number of 1 KB swizzle atoms)
+  // k-blocks of 64 per stage: a stage is one TMA box of X and one of W spanning KSUB k-blocks (the
+  // boxes of a K-blocked tensor map). With 32-row slots four k-blocks per box: a CTA's time is set
+  // by how many TMA copies it issues one after another, and this quarters them.
+  static constexpr int KSUB = AROWS == 32 ? 4 : 1;
+  static constexpr int A_SUB = AROWS * BK * 2;     // one k-block of X: 4 KB (32 rows) or 16 KB (128)
+  static constexpr int B_SUB = BN * BK * 2;        // one k-block of W: 2 / 4 / 8 KB (1 KB swizzle atoms)
+  static constexpr int A_BYTES = KSUB * A_SUB;
+  static constexpr int B_BYTES = KSUB * B_SUB;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  // as many stages as about 196 KB holds (at most 32): what a CTA keeps in flight sets how fast
-  // its SM pulls weight rows
+  // as many stages as about 196 KB holds (at most 32)
   static constexpr int STAGES = (196 * 1024) / STAGE_BYTES < 32 ? (196 * 1024) / STAGE_BYTES : 32;
-  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  // One accumulation chain over all k-blocks in order: the k order of the persistent 128 x 256
+  // kernel, so the two give a row the same bits. (Four interleaved chains summed at the end were
+  // measured: no faster, since a CTA's time here is its TMA and UMMA issue, not UMMA latency.)
+  static constexpr int CHAINS = 1;
+  static constexpr int TMEM_COLS = CHAINS * BN < 32 ? 32 : CHAINS * BN;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 1024;
-  // the UMMA reads 128 rows (16 KB) from a stage's A slot: with 32-row slots the rows past 32 come
-  // from the slots after it (and, for the last, the B slots), all inside the allocation
+  // the UMMA reads 128 rows (16 KB) from a k-block's A slot: with 32-row slots the rows past 32
+  // come from the slots after it (and, for the last, the B slots), all inside the allocation
   static_assert(AROWS == 128 || STAGES * B_BYTES >= 12 * 1024, "UMMA A reads stay in shared memory");
 };
 
@@ -56,7 +67,8 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KB = (K + T::BK - 1) / T::BK;
+  const int KB = K / T::BK;                        // k-blocks (K is a multiple of 64)
+  const int NST = (KB + T::KSUB - 1) / T::KSUB;   // stage loads
   const int m0 = blockIdx.y * T::BM;
   constexpr bool kSwiGLU = EPI == kLinearSwiGLU;
   constexpr int OUT = kSwiGLU ? BN / 2 : BN;  // output columns of this CTA
@@ -81,37 +93,38 @@ __global__ void __launch_bounds__(192, 1)
     if (elect_one()) {
       prefetch_tensormap(&tmX);
       prefetch_tensormap(&tmW);
-      auto load_w = [&](int kb, int s) {
-        if constexpr (kSwiGLU) {  // gate rows [n0, n0 + BN/2) then up rows [F + n0, F + n0 + BN/2)
-          tma_load_2d(sB + s * T::B_BYTES, &tmW, &full[s], kb * T::BK, n0);
-          tma_load_2d(sB + s * T::B_BYTES + T::B_BYTES / 2, &tmW, &full[s], kb * T::BK, f_rows + n0);
-        } else {
-          tma_load_2d(sB + s * T::B_BYTES, &tmW, &full[s], kb * T::BK, n0);
-        }
+      // stage st holds k-blocks [st * KSUB, st * KSUB + KSUB): X box (64, rows, KSUB) and W box
+      // (64, BN, KSUB), or for SwiGLU (64, BN/2, gate | up, KSUB): per k-block the BN/2 gate rows
+      // [n0, n0 + BN/2) and then the BN/2 up rows [F + n0, ...)
+      auto load_w = [&](int st, int s) {
+        if constexpr (kSwiGLU)
+          tma_load_4d(sB + s * T::B_BYTES, &tmW, &full[s], 0, n0, 0, st * T::KSUB);
+        else
+          tma_load_3d(sB + s * T::B_BYTES, &tmW, &full[s], 0, n0, st * T::KSUB);
       };
-      // with at most 32 rows only the first 32 rows of the A tile are loaded: the other lanes of
-      // the accumulator are computed from stale shared memory and never stored
-      const uint32_t stage_tx = a_rows * T::BK * 2 + T::B_BYTES;
+      auto load_x = [&](int st, int s) { tma_load_3d(sA + s * T::A_BYTES, &tmX, &full[s], 0, m0, st * T::KSUB); };
+      // full boxes are counted even where k-blocks past K are filled with zeros
+      const uint32_t stage_tx = T::STAGE_BYTES;
       // the weights do not depend on the previous kernel: the first ring's worth streams in
       // before griddep_wait(), the activations after it
-      const int pre = KB < T::STAGES ? KB : T::STAGES;
-      for (int kb = 0; kb < pre; ++kb) {
-        mbar_arrive_expect_tx(&full[kb], stage_tx);
-        load_w(kb, kb);
+      const int pre = NST < T::STAGES ? NST : T::STAGES;
+      for (int st = 0; st < pre; ++st) {
+        mbar_arrive_expect_tx(&full[st], stage_tx);
+        load_w(st, st);
       }
       griddep_wait();
-      for (int kb = 0; kb < pre; ++kb) tma_load_2d(sA + kb * T::A_BYTES, &tmX, &full[kb], kb * T::BK, m0);
+      for (int st = 0; st < pre; ++st) load_x(st, st);
       int issued = pre;
-      for (int kb = pre; kb < KB; ++kb) {
-        const int s = kb % T::STAGES;
-        if (!mbar_wait(&empty[s], ((kb / T::STAGES) & 1) ^ 1)) {
+      for (int st = pre; st < NST; ++st) {
+        const int s = st % T::STAGES;
+        if (!mbar_wait(&empty[s], ((st / T::STAGES) & 1) ^ 1)) {
           *abort_flag = 1;
           break;
         }
         mbar_arrive_expect_tx(&full[s], stage_tx);
-        tma_load_2d(sA + s * T::A_BYTES, &tmX, &full[s], kb * T::BK, m0);
-        load_w(kb, s);
-        issued = kb + 1;
+        load_x(st, s);
+        load_w(st, s);
+        issued = st + 1;
       }
       if (*abort_flag)
         for (int i = max(0, issued - T::STAGES); i < issued; ++i)
@@ -121,19 +134,25 @@ __global__ void __launch_bounds__(192, 1)
     if (elect_one()) {
       constexpr uint32_t idesc = umma_idesc_bf16(128, BN, false, false);
       bool ok = true;
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % T::STAGES;
-        if (*abort_flag || !mbar_wait(&full[s], (kb / T::STAGES) & 1)) {
+      for (int st = 0; st < NST; ++st) {
+        const int s = st % T::STAGES;
+        if (*abort_flag || !mbar_wait(&full[s], (st / T::STAGES) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t a_base = smem_u32(sA + s * T::A_BYTES);
-        const uint32_t b_base = smem_u32(sB + s * T::B_BYTES);
 #pragma unroll
-        for (int k = 0; k < T::BK / 16; ++k)
-          umma_f16(tmem, umma_desc_sw128(a_base + k * 32, 16, 1024), umma_desc_sw128(b_base + k * 32, 16, 1024),
-                   idesc, (kb > 0 || k > 0) ? 1u : 0u);
+        for (int j = 0; j < T::KSUB; ++j) {
+          const int kb = st * T::KSUB + j;
+          if (kb >= KB) break;
+          const uint32_t a_base = smem_u32(sA + s * T::A_BYTES + j * T::A_SUB);
+          const uint32_t b_base = smem_u32(sB + s * T::B_BYTES + j * T::B_SUB);
+          const uint32_t acc = tmem + (kb % T::CHAINS) * BN;
+#pragma unroll
+          for (int k = 0; k < T::BK / 16; ++k)
+            umma_f16(acc, umma_desc_sw128(a_base + k * 32, 16, 1024), umma_desc_sw128(b_base + k * 32, 16, 1024),
+                     idesc, (kb >= T::CHAINS || k > 0) ? 1u : 0u);
+        }
         umma_commit(&empty[s]);
       }
       if (!ok) *abort_flag = 1;
@@ -146,10 +165,26 @@ __global__ void __launch_bounds__(192, 1)
     const bool done = mbar_wait(acc_full, 0) && !*abort_flag;
     tc_fence_after();
     const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    float v[BN < 32 ? 32 : BN];  // columns past BN (BN = 16) are allocated but never written
-    tmem_ld32(base, v);
-    if constexpr (BN == 64) tmem_ld32(base + 32, v + 32);
-    tmem_wait_ld();
+    // the chains that received k-blocks, summed in chain order (a fixed order for a given K)
+    const int nch = KB < T::CHAINS ? KB : T::CHAINS;
+    float v[BN];
+    auto load_chain = [&](int c, float* dst) {
+      if constexpr (BN == 16) {
+        tmem_ld16(base + c * BN, dst);
+      } else {
+        tmem_ld32(base + c * BN, dst);
+        if constexpr (BN == 64) tmem_ld32(base + c * BN + 32, dst + 32);
+      }
+      tmem_wait_ld();
+    };
+    load_chain(0, v);
+#pragma unroll 1
+    for (int c = 1; c < nch; ++c) {
+      float t[BN];
+      load_chain(c, t);
+#pragma unroll
+      for (int i = 0; i < BN; ++i) v[i] += t[i];
+    }
     if (done && row < M) {
       if constexpr (kSwiGLU) {
         // the roundings of silu_mul(x @ [gate; up]^T): g and u rounded, silu rounded, product
@@ -216,7 +251,7 @@ inline cudaError_t skinny_launch(const CUtensorMap& tx, const CUtensorMap& tw, i
 
 // Output columns per CTA: the widest tile (64, 32 or 16 accumulator columns) that still gives at
 // least 128 CTAs, else 16. A narrower tile only splits the columns: every output element keeps the
-// same k order, so all widths (and the 128 x 256 persistent kernel) give the same bits.
+// same k order, so all widths, all row counts (and the persistent kernel) give the same bits.
 inline int skinny_tile_n(int64_t M, int64_t acc_cols) {
   const int64_t mt = ceil_div(M, 128);
   for (int bn : {64, 32})
@@ -225,13 +260,13 @@ inline int skinny_tile_n(int64_t M, int64_t acc_cols) {
 }
 
 // Y [M, N] (pitch ldy) = X [M, K] @ W^T (+ R), or for SwiGLU Y [M, F] = silu(X gate^T) * (X up^T)
-// with W = [gate; up] [2F, K] (N = F). N a multiple of 64 (SwiGLU: 32), K of 8, pitches of 8.
+// with W = [gate; up] [2F, K] (N = F). N a multiple of 64 (SwiGLU: 32), K of 64, pitches of 8.
 inline int linear_skinny_impl(const void* X, int64_t ldx, const void* W, int64_t ldw, const void* R, void* Y,
                               int64_t ldy, int64_t M, int64_t N, int64_t K, int epilogue, cudaStream_t stream) {
   ORTHRUS_CHECK_ARG(X && W && Y && M >= 0 && N > 0 && K > 0);
   ORTHRUS_CHECK_ARG(epilogue == kLinearStore || epilogue == kLinearResidual || epilogue == kLinearSwiGLU);
   ORTHRUS_CHECK_ARG(epilogue != kLinearResidual || (R != nullptr && R != Y));
-  ORTHRUS_CHECK_ARG(N % (epilogue == kLinearSwiGLU ? 32 : 64) == 0 && K % 8 == 0);
+  ORTHRUS_CHECK_ARG(N % (epilogue == kLinearSwiGLU ? 32 : 64) == 0 && K % 64 == 0);
   ORTHRUS_CHECK_ARG(ldx >= K && ldw >= K && ldy >= N && ldx % 8 == 0 && ldw % 8 == 0 && ldy % 8 == 0);
   ORTHRUS_CHECK_ARG(epilogue != kLinearResidual || (R != nullptr && aligned16(R)));
   ORTHRUS_CHECK_ARG(aligned16(X) && aligned16(W) && aligned16(Y));
@@ -241,9 +276,12 @@ inline int linear_skinny_impl(const void* X, int64_t ldx, const void* W, int64_t
   const bool swiglu = epilogue == kLinearSwiGLU;
   const int bn = skinny_tile_n(M, swiglu ? 2 * N : N);
   CUtensorMap tx, tw;
-  const int a_rows = M <= 32 ? 32 : 128;  // rows of X per A box
-  if (!make_tmap_2d_bf16(&tx, X, K, M, ldx, 64, a_rows)) return ORTHRUS_ECUDA;
-  if (!make_tmap_2d_bf16(&tw, W, K, swiglu ? 2 * N : N, ldw, 64, swiglu ? bn / 2 : bn)) return ORTHRUS_ECUDA;
+  const int a_rows = M <= 32 ? 32 : 128;   // rows of X per box
+  const int ksub = a_rows == 32 ? 4 : 1;   // k-blocks per box (SkinnyTile::KSUB)
+  if (!make_tmap_kblocked_bf16(&tx, X, M, K, ldx, a_rows, ksub)) return ORTHRUS_ECUDA;
+  if (!(swiglu ? make_tmap_kblocked_bf16(&tw, W, 2 * N, K, ldw, bn / 2, ksub, 2, N)
+               : make_tmap_kblocked_bf16(&tw, W, N, K, ldw, bn, ksub)))
+    return ORTHRUS_ECUDA;
   auto* r = static_cast<const __nv_bfloat16*>(R);
   auto* y = static_cast<__nv_bfloat16*>(Y);
   const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);

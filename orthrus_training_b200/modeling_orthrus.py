@@ -83,18 +83,18 @@ def _cached_weight(owner: nn.Module, key, tensors: list[torch.Tensor]) -> torch.
     return hit[1]
 
 
-def _few_tiles(rows: int, cols: int) -> bool:
-    """Whether a projection of `rows` rows and `cols` output columns (accumulator columns for
-    SwiGLU) would leave most SMs idle on 128 x 256 tiles: then the 128 x 64-tile kernel runs it.
+def _few_row_kernel(rows: int, cols: int, K: int) -> bool:
+    """Whether a projection of `rows` rows, `cols` output (accumulator) columns and depth K runs on
+    the few-row kernel: when 128 x 256 tiles would leave most SMs idle and K is a multiple of 64.
     The two kernels give every row the same bits, so the choice never changes a result."""
-    return -(-rows // 128) * -(-cols // 256) < 74
+    return K % 64 == 0 and -(-rows // 128) * -(-cols // 256) < 74
 
 
 def _project(a: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
     """a @ w^T (+ residual). Every kernel here is batch-invariant: a row's result does not depend
     on how many rows the call has."""
     if a.dtype == torch.bfloat16 and ops.fused_linear_supported(a, w, w.shape[0]):
-        return ops.linear(a, w, residual=residual, skinny=_few_tiles(a.shape[0], w.shape[0]))
+        return ops.linear(a, w, residual=residual, skinny=_few_row_kernel(a.shape[0], w.shape[0], a.shape[1]))
     y = ops.gemm(a, w)
     return y if residual is None else ops.add(residual, y)
 
@@ -116,7 +116,7 @@ class OrthrusMLP(nn.Module):
         """silu(h @ gate^T) * (h @ up^T) for h [rows, d]."""
         w = self.packed_gate_up()
         if h.dtype == torch.bfloat16 and ops.fused_linear_supported(h, w, w.shape[0] // 2):
-            return ops.linear_swiglu(h, w, skinny=_few_tiles(h.shape[0], w.shape[0]))
+            return ops.linear_swiglu(h, w, skinny=_few_row_kernel(h.shape[0], w.shape[0], h.shape[1]))
         return ops.silu_mul(ops.gemm(h, w))
 
     @torch.no_grad()

@@ -147,8 +147,9 @@ LINEAR_PAIR = 0x100  # epilogue flag of orthrus_linear_bf16: run on CTA pairs
 def linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None,
            skinny: bool = False, pair: bool = False) -> torch.Tensor:
     """x [M, K] @ w [N, K]^T, plus residual [M, N] in the epilogue when given (torch.addmm with
-    beta = 1), on the persistent tcgen05 projection kernel, or with skinny on 128 x 64 tiles (many
-    CTAs for a few rows; N a multiple of 64)."""
+    beta = 1), on the persistent tcgen05 projection kernel, or with skinny on the inference
+    passes' kernel (128-row tiles of 16-64 columns, many CTAs for a few rows; K a multiple of 64;
+    a row's result independent of the row count)."""
     _require_cuda(x, w, residual)
     x = x.contiguous()
     w = w.contiguous()

@@ -106,13 +106,58 @@ class GradBuckets:
             b["flat"].zero_()
 
 
+class PeerLost(RuntimeError):
+    """A data-parallel peer left or stopped answering; raised before any collective is launched."""
+
+
+class PeerMonitor:
+    """Host-side liveness of the data-parallel ranks through the process group's key-value store.
+
+    Each rank posts a heartbeat (its step number) before the step's collectives, and a rank that
+    leaves posts that it left. Before launching a step's collectives a rank waits until every peer
+    has posted the same step; a peer that left, or stayed silent for `timeout_s`, raises PeerLost.
+    So no rank launches an all-reduce that a peer will never join (on the GPU that collective
+    would otherwise wait for the peer until the process group's own timeout)."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 30.0, poll_s: float = 0.005,
+                 prefix: str = "orthrus"):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.poll_s, self.prefix = timeout_s, poll_s, prefix
+
+    def _key(self, kind: str, rank: int) -> str:
+        return f"{self.prefix}/{kind}/{rank}"
+
+    def beat(self, step: int) -> None:
+        self.store.set(self._key("step", self.rank), str(step))
+
+    def leave(self) -> None:
+        self.store.set(self._key("left", self.rank), "1")
+
+    def check(self, step: int) -> None:
+        import time
+
+        deadline = time.monotonic() + self.timeout_s
+        for peer in range(self.world):
+            if peer == self.rank:
+                continue
+            while True:
+                if self.store.check([self._key("left", peer)]):
+                    raise PeerLost(f"rank {peer} left before step {step}")
+                key = self._key("step", peer)
+                if self.store.check([key]) and int(self.store.get(key)) >= step:
+                    break
+                if time.monotonic() > deadline:
+                    raise PeerLost(f"rank {peer} posted no heartbeat for step {step} in {self.timeout_s} s")
+                time.sleep(self.poll_s)
+
+
 class Trainer:
     """Optimizer state and the step of one rank."""
 
     def __init__(self, model, *, lr=1e-4, betas=(0.9, 0.95), weight_decay=0.0, total_steps=1000,
                  warmup_ratio=0.05, min_lr_ratio=0.1, max_grad_norm=1.0, num_anchors=32,
                  kl_chunk_size=4096, gamma=0.0, seed=42, world=1, rank=0, group=None,
-                 check_device_every=50):
+                 check_device_every=50, monitor: PeerMonitor | None = None):
         from orthrus_training_b200.modeling_orthrus import freeze_to_diffusion
 
         self.model = model
@@ -138,6 +183,8 @@ class Trainer:
         # wait that ran out or a clamped out-of-range index then raises instead of passing silently
         self.check_device_every = check_device_every
         self._side = None  # stream of the anchor draw and the supervised layout
+        # optional liveness check of the peers before each step's collectives (world > 1)
+        self.monitor = monitor
 
     def _prepare(self, model, ids, mask, rng, ready):
         """Queues the teacher pass (it needs the input ids only) and draws the anchors and
@@ -179,6 +226,9 @@ class Trainer:
         accum = len(micro_batches)
         if indices is not None and len(indices) != accum:
             raise ValueError("one index per micro-batch")
+        if self.monitor is not None and self.world > 1:
+            self.monitor.beat(self.step_index)
+            self.monitor.check(self.step_index)  # raises PeerLost before any collective
         self.buckets.zero()
         losses = []
         for j, (ids, mask) in enumerate(micro_batches):

@@ -96,3 +96,46 @@ def test_missing_rank_ends_the_collective_with_an_error():
     mp.start_processes(_failing_worker, args=(2, port, out), nprocs=2, join=True, start_method="spawn")
     assert out[1] == "left"
     assert out[0].startswith("error")
+
+
+def _monitored_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    from orthrus_training_b200.train_step import PeerLost, PeerMonitor
+
+    store = dist.distributed_c10d._get_default_store()
+    mon = PeerMonitor(store, rank, world, timeout_s=5.0)
+    model = TwinModel()
+    steps_done = 0
+    try:
+        for step in range(3):
+            if rank == 1 and step == 1:
+                mon.leave()  # between steps, with nothing in flight
+                out[1] = "left"
+                return
+            mon.beat(step)
+            mon.check(step)  # before the step's collective
+            x = torch.ones(2, 4)
+            loss = model(x)
+            loss.backward()
+            for p in model.parameters():
+                dist.all_reduce(p.grad)
+            steps_done += 1
+        out[rank] = "completed"
+    except PeerLost as e:
+        out[rank] = f"peer lost after {steps_done} steps: {e}"
+    finally:
+        if rank == 0:
+            dist.destroy_process_group()
+
+
+def test_peer_monitor_stops_before_the_collective_a_departed_rank_would_not_join():
+    """The heartbeat check raises PeerLost on the surviving rank before it launches the next
+    step's collective (no collective times out), after one step completed on both ranks."""
+    port = _free_port()
+    manager = mp.Manager()
+    out = manager.dict()
+    mp.start_processes(_monitored_worker, args=(2, port, out), nprocs=2, join=True, start_method="spawn")
+    assert out[1] == "left"
+    assert out[0].startswith("peer lost after 1 steps"), out[0]
