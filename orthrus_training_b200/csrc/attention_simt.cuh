@@ -172,6 +172,8 @@ __global__ void attn_delta128_bf16_kernel(const __nv_bfloat16* __restrict__ o, c
                                           int64_t B, int Hq, int64_t Tq, float* __restrict__ delta) {
   const int sub = threadIdx.x & 15;
   const int64_t item = static_cast<int64_t>(blockIdx.x) * 16 + (threadIdx.x >> 4);  // (b, t, h)
+  griddep_launch_dependents();  // launched as a programmatic dependent
+  griddep_wait();
   const bool live = item < B * Tq * Hq;
   const int64_t it = live ? item : 0;
   const uint4 a = *reinterpret_cast<const uint4*>(o + it * 128 + sub * 8);

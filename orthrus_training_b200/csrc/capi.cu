@@ -408,8 +408,9 @@ int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h,
   const bool tc = use_tensor_cores(dtype, hd, D, ORTHRUS_MASK_DUAL, nullptr) && (128 % block == 0) &&
                   (Hq / Hkv) <= DkvSmem<128>::MAX_GROUP;
   if (dtype == ORTHRUS_BF16 && hd == 128 && aligned16(o) && aligned16(do_)) {
-    attn_delta128_bf16_kernel<<<static_cast<unsigned>(ceil_div(items, 16)), 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(do_), B, Hq, Tq, delta);
+    ORTHRUS_CHECK_CUDA(launch_pdl(attn_delta128_bf16_kernel, dim3(static_cast<unsigned>(ceil_div(items, 16))),
+                                  dim3(256), 0, st, static_cast<const __nv_bfloat16*>(o),
+                                  static_cast<const __nv_bfloat16*>(do_), B, Hq, Tq, delta));
   } else if (dtype == ORTHRUS_BF16) {
     using T = __nv_bfloat16;
     attn_delta_kernel<T><<<static_cast<unsigned>(ceil_div(items, 8)), 256, 0, st>>>(
@@ -443,8 +444,9 @@ int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h,
       if (D == 128) {
         if (set_smem(attn_dq_tc2_kernel<128>, Dq2Smem<128>::SMEM)) return ORTHRUS_ECUDA;
         if (set_smem(attn_dkdv_tc_kernel<128>, DkvSmem<128>::SMEM)) return ORTHRUS_ECUDA;
-        attn_dq_tc2_kernel<128><<<grid2, 320, Dq2Smem<128>::SMEM, st>>>(
-            m64.q, m64.dout, m64.k1, m64.v1, m64.k2, m64.v2, Hq, Hkv, Tq, hd, scale, mp, true, lse, delta, dq);
+        ORTHRUS_CHECK_CUDA(launch_pdl(attn_dq_tc2_kernel<128>, grid2, dim3(320), Dq2Smem<128>::SMEM, st, m64.q,
+                                      m64.dout, m64.k1, m64.v1, m64.k2, m64.v2, Hq, Hkv, Tq, hd, scale, mp, true,
+                                      lse, static_cast<const float*>(delta), dq));
         ORTHRUS_CHECK_LAUNCH();
         ORTHRUS_CHECK_CUDA(cudaStreamWaitEvent(side->stream, side->fork, 0));
         const int G = Hq / Hkv;
@@ -605,9 +607,10 @@ extern "C" int orthrus_rmsnorm_bwd_add(const void* x, const void* w, const float
   ORTHRUS_CHECK_ARG(aligned16(x) && aligned16(w) && aligned16(dy) && aligned16(dres) && aligned16(dx));
   if (rows == 0) return ORTHRUS_OK;
   using T = __nv_bfloat16;
-  rmsnorm_bwd_vec_kernel<T><<<static_cast<unsigned>(ceil_div(rows, 8)), 256, 0, as_stream(stream)>>>(
-      static_cast<const T*>(x), static_cast<const T*>(w), rstd, static_cast<const T*>(dy), rows, d,
-      static_cast<T*>(dx), static_cast<const T*>(dres));
+  ORTHRUS_CHECK_CUDA(launch_pdl(rmsnorm_bwd_vec_kernel<T>, dim3(static_cast<unsigned>(ceil_div(rows, 8))),
+                                dim3(256), 0, as_stream(stream), static_cast<const T*>(x),
+                                static_cast<const T*>(w), rstd, static_cast<const T*>(dy), rows, d,
+                                static_cast<T*>(dx), static_cast<const T*>(dres)));
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
 }
@@ -622,9 +625,10 @@ extern "C" int orthrus_rmsnorm_bwd(const void* x, const void* w, const float* rs
   if (dtype == ORTHRUS_BF16) {
     using T = __nv_bfloat16;
     if (vec)
-      rmsnorm_bwd_vec_kernel<T><<<blocks, 256, 0, as_stream(stream)>>>(
-          static_cast<const T*>(x), static_cast<const T*>(w), rstd, static_cast<const T*>(dy), rows, d,
-          static_cast<T*>(dx));
+      ORTHRUS_CHECK_CUDA(launch_pdl(rmsnorm_bwd_vec_kernel<T>, dim3(blocks), dim3(256), 0, as_stream(stream),
+                                    static_cast<const T*>(x), static_cast<const T*>(w), rstd,
+                                    static_cast<const T*>(dy), rows, d, static_cast<T*>(dx),
+                                    static_cast<const T*>(nullptr)));
     else
       rmsnorm_bwd_kernel<T><<<blocks, 256, 0, as_stream(stream)>>>(
           static_cast<const T*>(x), static_cast<const T*>(w), rstd, static_cast<const T*>(dy), rows, d,

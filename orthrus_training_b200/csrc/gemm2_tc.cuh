@@ -120,6 +120,10 @@ __global__ void __launch_bounds__(Gemm2Base::THREADS, 1)
   if (warp == 1) tmem_alloc_pair(tmem_slot, 512);
   __syncthreads();
   cluster_sync_all();  // the peer's barriers are initialised before anyone signals them
+  // launched as a programmatic dependent: the set-up above overlaps the previous kernel's tail;
+  // operands, the residual and C belong to the stream order from here on
+  griddep_launch_dependents();
+  griddep_wait();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -419,6 +423,8 @@ __global__ void gemm2_reduce_kernel(const float* __restrict__ part, int splits, 
                                     const __nv_bfloat16* __restrict__ R, int64_t ldr, __nv_bfloat16* __restrict__ C,
                                     int64_t ldc) {
   const int64_t groups = static_cast<int64_t>(M) * (N / 4);
+  griddep_launch_dependents();  // launched as a programmatic dependent
+  griddep_wait();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < groups;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t m = i / (N / 4);
@@ -481,13 +487,15 @@ inline int gemm2_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   cfg.blockDim = dim3(Gemm2Base::THREADS);
   cfg.dynamicSmemBytes = Gemm2Tile<EPI>::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   ORTHRUS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, tr, g, R, ldr));
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
@@ -565,8 +573,9 @@ inline int gemm2_bf16_impl(const void* A, int64_t lda, int a_mn, const void* B, 
                         : gemm2_launch<kGemm2Partial, true, true>(ta, tb, tc, tr, g, nullptr, 0, stream);
     if (rc != ORTHRUS_OK) return rc;
     const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(ceil_div(M * (N / 4), 256), num_sms() * 8));
-    gemm2_reduce_kernel<<<blocks, 256, 0, stream>>>(part, g.splits, g.m_pad, g.M, g.N, r, ldr,
-                                                    static_cast<__nv_bfloat16*>(C), ldc);
+    ORTHRUS_CHECK_CUDA(launch_pdl(gemm2_reduce_kernel, dim3(blocks), dim3(256), 0, stream,
+                                  static_cast<const float*>(part), g.splits, static_cast<int64_t>(g.m_pad), g.M,
+                                  g.N, r, ldr, static_cast<__nv_bfloat16*>(C), ldc));
     ORTHRUS_CHECK_LAUNCH();
     return ORTHRUS_OK;
   }

@@ -158,6 +158,10 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
   }
   __syncthreads();
   if constexpr (PAIR) cluster_sync_all();  // the peer's barriers exist before anyone signals them
+  // launched as a programmatic dependent: the set-up above overlaps the previous kernel's tail;
+  // operands and outputs belong to the stream order from here on
+  griddep_launch_dependents();
+  griddep_wait();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -330,10 +334,10 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
           if (qp.keep && kind < 2) {  // the projection itself, token-major, for the backward
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              st_shared_v4(stage + lane * 64 + q * 16, pack_bf16x2(lo[8 * q], lo[8 * q + 1]),
+              st_shared_v4(stage + sw64_offset(lane, q), pack_bf16x2(lo[8 * q], lo[8 * q + 1]),
                            pack_bf16x2(lo[8 * q + 2], lo[8 * q + 3]), pack_bf16x2(lo[8 * q + 4], lo[8 * q + 5]),
                            pack_bf16x2(lo[8 * q + 6], lo[8 * q + 7]));
-              st_shared_v4(stage + 2048 + lane * 64 + q * 16, pack_bf16x2(hi[8 * q], hi[8 * q + 1]),
+              st_shared_v4(stage + 2048 + sw64_offset(lane, q), pack_bf16x2(hi[8 * q], hi[8 * q + 1]),
                            pack_bf16x2(hi[8 * q + 2], hi[8 * q + 3]), pack_bf16x2(hi[8 * q + 4], hi[8 * q + 5]),
                            pack_bf16x2(hi[8 * q + 6], hi[8 * q + 7]));
             }
@@ -382,10 +386,10 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
           const uint32_t box_lo = stage, box_hi = stage + 2048;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            st_shared_v4(box_lo + lane * 64 + q * 16, pack_bf16x2(lo[8 * q], lo[8 * q + 1]),
+            st_shared_v4(box_lo + sw64_offset(lane, q), pack_bf16x2(lo[8 * q], lo[8 * q + 1]),
                          pack_bf16x2(lo[8 * q + 2], lo[8 * q + 3]), pack_bf16x2(lo[8 * q + 4], lo[8 * q + 5]),
                          pack_bf16x2(lo[8 * q + 6], lo[8 * q + 7]));
-            st_shared_v4(box_hi + lane * 64 + q * 16, pack_bf16x2(hi[8 * q], hi[8 * q + 1]),
+            st_shared_v4(box_hi + sw64_offset(lane, q), pack_bf16x2(hi[8 * q], hi[8 * q + 1]),
                          pack_bf16x2(hi[8 * q + 2], hi[8 * q + 3]), pack_bf16x2(hi[8 * q + 4], hi[8 * q + 5]),
                          pack_bf16x2(hi[8 * q + 6], hi[8 * q + 7]));
           }
@@ -416,9 +420,9 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
             float hq[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) hq[e] = round_to_t<__nv_bfloat16>(silu_fast(gv[8 * q + e])) * uv[8 * q + e];
-            st_shared_v4(stage + lane * 64 + q * 16, pack_bf16x2(hq[0], hq[1]), pack_bf16x2(hq[2], hq[3]),
+            st_shared_v4(stage + sw64_offset(lane, q), pack_bf16x2(hq[0], hq[1]), pack_bf16x2(hq[2], hq[3]),
                          pack_bf16x2(hq[4], hq[5]), pack_bf16x2(hq[6], hq[7]));
-            st_shared_v4(stage + 2048 + lane * 64 + q * 16, pack_bf16x2(gv[8 * q], gv[8 * q + 1]),
+            st_shared_v4(stage + 2048 + sw64_offset(lane, q), pack_bf16x2(gv[8 * q], gv[8 * q + 1]),
                          pack_bf16x2(gv[8 * q + 2], gv[8 * q + 3]), pack_bf16x2(gv[8 * q + 4], gv[8 * q + 5]),
                          pack_bf16x2(gv[8 * q + 6], gv[8 * q + 7]));
           }
@@ -432,7 +436,7 @@ __global__ void __launch_bounds__(LinearTile::THREADS, 1)
           reuse();
 #pragma unroll
           for (int q = 0; q < 4; ++q)
-            st_shared_v4(stage + lane * 64 + q * 16, pack_bf16x2(uv[8 * q], uv[8 * q + 1]),
+            st_shared_v4(stage + sw64_offset(lane, q), pack_bf16x2(uv[8 * q], uv[8 * q + 1]),
                          pack_bf16x2(uv[8 * q + 2], uv[8 * q + 3]), pack_bf16x2(uv[8 * q + 4], uv[8 * q + 5]),
                          pack_bf16x2(uv[8 * q + 6], uv[8 * q + 7]));
           fence_proxy_async_smem();
@@ -568,7 +572,8 @@ inline int linear_launch(bool pair, const CUtensorMap& tx, const CUtensorMap& tw
   if (!pair) {
     ORTHRUS_CHECK_CUDA(ensure_smem(linear_tc_kernel<EPI>, T::SMEM));
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(g.tiles, num_sms()));
-    linear_tc_kernel<EPI><<<grid, T::THREADS, T::SMEM, stream>>>(tx, tw, ty, tk, tv, tp, g, ldr, R, qp);
+    ORTHRUS_CHECK_CUDA(launch_pdl(linear_tc_kernel<EPI>, dim3(grid), dim3(T::THREADS), T::SMEM, stream, tx, tw, ty, tk,
+                                  tv, tp, g, ldr, R, qp));
     ORTHRUS_CHECK_LAUNCH();
     return ORTHRUS_OK;
   }
@@ -581,13 +586,15 @@ inline int linear_launch(bool pair, const CUtensorMap& tx, const CUtensorMap& tw
   cfg.blockDim = dim3(T::THREADS);
   cfg.dynamicSmemBytes = T::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   ORTHRUS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kernel, tx, tw, ty, tk, tv, tp, g, ldr, R, qp));
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
@@ -671,8 +678,9 @@ inline int linear_swiglu_keep_impl(const void* X, const void* W, int64_t M, int6
   CUtensorMap tx, tw, ty, tgu;
   if (!make_tmap_2d_bf16(&tx, X, K, M, K, 64, 128)) return ORTHRUS_ECUDA;
   if (!make_tmap_2d_bf16(&tw, W, K, 2 * F, K, 64, 128)) return ORTHRUS_ECUDA;
-  if (!make_tmap_2d_bf16(&ty, Y, F, M, F, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) return ORTHRUS_ECUDA;
-  if (!make_tmap_2d_bf16(&tgu, GU, 2 * F, M, 2 * F, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) return ORTHRUS_ECUDA;
+  // 32 x 32 boxes of 64-byte rows, 64-byte swizzle (bank-conflict-free staging stores)
+  if (!make_tmap_2d_bf16(&ty, Y, F, M, F, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) return ORTHRUS_ECUDA;
+  if (!make_tmap_2d_bf16(&tgu, GU, 2 * F, M, 2 * F, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) return ORTHRUS_ECUDA;
   LinearGeometry g;
   g.M = static_cast<int>(M);
   g.N = static_cast<int>(F);
@@ -707,14 +715,15 @@ inline int linear_qkv_rope_impl(const void* X, const void* W, const void* q_norm
   CUtensorMap tx, tw, tq, tk, tv;
   if (!make_tmap_2d_bf16(&tx, X, K, M, K, 64, 128)) return ORTHRUS_ECUDA;
   if (!make_tmap_2d_bf16(&tw, W, K, N, K, 64, 128)) return ORTHRUS_ECUDA;
-  if (!make_tmap_2d_bf16(&tq, q_out, 128, B * Hq * L, 128, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) return ORTHRUS_ECUDA;
-  if (!make_tmap_2d_bf16(&tk, k_out, 128, B * Hkv * L, 128, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) return ORTHRUS_ECUDA;
-  if (!make_tmap_2d_bf16(&tv, v_out, 128, B * Hkv * L, 128, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) return ORTHRUS_ECUDA;
+  // 32 x 32 boxes of 64-byte rows with 64-byte swizzle: the epilogue's staging stores (one row
+  // per lane) then fall on distinct shared-memory banks
+  const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_64B;
+  if (!make_tmap_2d_bf16(&tq, q_out, 128, B * Hq * L, 128, 32, 32, sw)) return ORTHRUS_ECUDA;
+  if (!make_tmap_2d_bf16(&tk, k_out, 128, B * Hkv * L, 128, 32, 32, sw)) return ORTHRUS_ECUDA;
+  if (!make_tmap_2d_bf16(&tv, v_out, 128, B * Hkv * L, 128, 32, 32, sw)) return ORTHRUS_ECUDA;
   CUtensorMap tp = tv;
   ORTHRUS_CHECK_ARG(qkv_keep == nullptr || aligned16(qkv_keep));
-  if (qkv_keep != nullptr &&
-      !make_tmap_2d_bf16(&tp, qkv_keep, N, M, N, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE))
-    return ORTHRUS_ECUDA;
+  if (qkv_keep != nullptr && !make_tmap_2d_bf16(&tp, qkv_keep, N, M, N, 32, 32, sw)) return ORTHRUS_ECUDA;
   LinearGeometry g;
   g.M = static_cast<int>(M);
   g.N = static_cast<int>(N);

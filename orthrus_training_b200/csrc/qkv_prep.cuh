@@ -215,6 +215,8 @@ __global__ void zero_heads_kernel(int64_t rows, int heads, int hd, int head0, in
 __global__ void sum_partials_kernel(const float* __restrict__ part, int nparts, int hd, float* __restrict__ out) {
   const int e = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  griddep_launch_dependents();  // launched as a programmatic dependent
+  griddep_wait();
   if (e >= hd) return;
   float acc = 0.f;
   for (int p = lane; p < nparts; p += 32) acc += part[static_cast<int64_t>(p) * hd + e];
@@ -614,6 +616,8 @@ __global__ void __launch_bounds__(256, 2) qkv_prep_bwd_pipe_kernel(
   constexpr int NE = 4;
   __shared__ float wpart[2][8][128];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  griddep_launch_dependents();  // launched as a programmatic dependent
+  griddep_wait();
   PipeShape s{qkv, positions, rstd, dq, dk, dv, rows, Tn, static_cast<int64_t>(blockIdx.x) * 8 + warp,
               static_cast<int64_t>(gridDim.x) * 8, Hq, Hkv, D, Hq + 2 * Hkv, (Hq + 2 * Hkv) / kPipePer};
   const int64_t my_rows = s.first < rows ? (rows - 1 - s.first) / s.stride + 1 : 0;
@@ -704,12 +708,15 @@ int qkv_prep_bwd_impl(const T* qkv, const int64_t* positions, const float* inv_f
                       (!dq || aligned16(dq)) && (!dk || aligned16(dk)) && (!dv || aligned16(dv));
   if constexpr (std::is_same_v<T, __nv_bfloat16>) {
     if (vec_ok && hd == 128 && D % 4 == 0 && Hq % kPipePer == 0 && Hkv % kPipePer == 0) {
-      qkv_prep_bwd_pipe_kernel<<<kPipeBlocks, 256, 0, stream>>>(qkv, positions, inv_freq, qw, kw, rstd, dq, dk, dv,
-                                                                rows, Tn, Hq, Hkv, D, dqkv, part_q, part_k);
+      ORTHRUS_CHECK_CUDA(launch_pdl(qkv_prep_bwd_pipe_kernel, dim3(kPipeBlocks), dim3(256), 0, stream, qkv, positions,
+                                    inv_freq, qw, kw, rstd, dq, dk, dv, rows, Tn, Hq, Hkv, D, dqkv, part_q,
+                                    part_k));
       ORTHRUS_CHECK_LAUNCH();
-      sum_partials_kernel<<<(hd + 7) / 8, 256, 0, stream>>>(part_q, kPipeBlocks, hd, dqw);
+      ORTHRUS_CHECK_CUDA(launch_pdl(sum_partials_kernel, dim3((hd + 7) / 8), dim3(256), 0, stream,
+                                    static_cast<const float*>(part_q), kPipeBlocks, hd, dqw));
       ORTHRUS_CHECK_LAUNCH();
-      sum_partials_kernel<<<(hd + 7) / 8, 256, 0, stream>>>(part_k, kPipeBlocks, hd, dkw);
+      ORTHRUS_CHECK_CUDA(launch_pdl(sum_partials_kernel, dim3((hd + 7) / 8), dim3(256), 0, stream,
+                                    static_cast<const float*>(part_k), kPipeBlocks, hd, dkw));
       ORTHRUS_CHECK_LAUNCH();
       return ORTHRUS_OK;
     }

@@ -96,6 +96,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_vec_kernel(const T* __restric
   constexpr int N = Vec16<T>::N;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  griddep_launch_dependents();  // launched as a programmatic dependent
+  griddep_wait();
   if (r >= rows) return;
   const float rs = rstd[r];
   const T* xr = x + r * d;

@@ -329,6 +329,12 @@ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t chunk) {
   return row * 128u + ((chunk ^ (row & 7u)) << 4);
 }
 
+// Byte offset of 16-byte unit `chunk` (0..3) of row `row` in a tile of 64-byte rows written with
+// the 64-byte swizzle (TMA SWIZZLE_64B): the unit index is XORed with bits 1-2 of the row.
+__device__ __forceinline__ uint32_t sw64_offset(uint32_t row, uint32_t chunk) {
+  return row * 64u + ((chunk ^ ((row >> 1) & 3u)) << 4);
+}
+
 // 2^x by the hardware approximation (PTX ex2.approx.ftz.f32: one instruction, relative error
 // about 2^-22, results below 2^-126 flushed to zero). Used for softmax probabilities, which are
 // rounded to bf16 before they reach a tensor core.
