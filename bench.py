@@ -712,14 +712,20 @@ def run_ours(args):
                 "gradients, one bucket per layer, launched from grad hooks during the backward"}
 
     # end to end through the public API: host rows through DevicePrefetcher (pinned buffers, a
-    # copy stream one micro-batch ahead), the loss read back to the host every step
+    # copy stream one micro-batch ahead), every step's loss read back to the host. A training
+    # loop logs step i's loss once step i + 1 is queued, so the read does not drain the device
+    # between steps; the last loss is read before the end event.
     barrier(world)
     f0, f1 = torch.cuda.Event(True), torch.cuda.Event(True)
     f0.record()
     feed = DevicePrefetcher(((i, ids, mask) for i in range(args.steps)), dev)
+    pending = None
     for _, b_ids, b_mask in feed:
         o = trainer.step([(b_ids, b_mask)], ready=feed.ready)
-        float(o["loss"])
+        if pending is not None:
+            float(pending)
+        pending = o["loss"]
+    float(pending)
     f1.record()
     barrier(world)
     ms_e2e = max_over_ranks(f0.elapsed_time(f1), world)

@@ -276,6 +276,26 @@ int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h,
                      const void* do_, float* dq, float* dk2, float* dv2, void* workspace,
                      size_t workspace_bytes, int dtype, void* stream);
 
+/* Opt-in document mask for packed rows of several documents (the reference runs without one:
+ * SDPA is_causal over the whole row, orthrus/objective.py:155, and the block mask's AR prefix
+ * kv < anchor, orthrus/modeling_orthrus.py:58-74). doc_start is int32 [B, L1]: the first position
+ * of each position's document. With it a causal query t sees source-1 keys [doc_start[t], t] and
+ * a dual-view query of the block anchored at a sees [doc_start[a], a) plus its own block; the
+ * other masks are unchanged. Otherwise as orthrus_attn_fwd / orthrus_attn_bwd. */
+int orthrus_attn_fwd_doc(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b,
+                         int64_t L1, const void* k2, const void* v2, int64_t s2h, int64_t s2b,
+                         int64_t L2, int64_t B, int Hq, int Hkv, int64_t Tq, int hd, int D,
+                         float scale, int mask, const int64_t* anchors, int64_t A, int block,
+                         const int32_t* offset, const int32_t* limit2, const int32_t* doc_start,
+                         void* o, float* lse, int dtype, void* stream);
+int orthrus_attn_bwd_doc(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b,
+                         int64_t L1, const void* k2, const void* v2, int64_t s2h, int64_t s2b,
+                         int64_t L2, int64_t B, int Hq, int Hkv, int64_t Tq, int hd, int D,
+                         float scale, const int64_t* anchors, int64_t A, int block,
+                         const int32_t* doc_start, const void* o, const float* lse, const void* do_,
+                         float* dq, float* dk2, float* dv2, void* workspace, size_t workspace_bytes,
+                         int dtype, void* stream);
+
 /* The same backward for callers that must not allocate device memory at all: no workspace
  * argument, and no cudaMalloc, cudaFree or allocating library call inside. It exists for hosts
  * that cannot hand this library a workspace: a runtime that owns every device byte in its own pool

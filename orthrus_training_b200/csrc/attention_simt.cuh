@@ -26,6 +26,9 @@ struct MaskParams {
   const int32_t* offset;
   const int32_t* limit2;
   int64_t L1, L2;
+  // opt-in document mask: int32 [B, L1], the first position of each position's document (packed
+  // rows of several documents); null keeps the reference's mask over the whole row
+  const int32_t* doc_start = nullptr;
 };
 
 __device__ __forceinline__ void query_ranges(const MaskParams& mp, int64_t b, int64_t t, int64_t& e1, int64_t& s2,
@@ -53,6 +56,23 @@ __device__ __forceinline__ void query_ranges(const MaskParams& mp, int64_t b, in
   if (e1 < 0) e1 = 0;
 }
 
+// First visible source-1 key of query t: 0, or with the document mask the start of the document
+// of the query's own position (CAUSAL) or of its block's anchor (DUAL: the AR prefix keeps to the
+// anchor's document).
+__device__ __forceinline__ int64_t source1_start(const MaskParams& mp, int64_t b, int64_t t) {
+  if (mp.doc_start == nullptr || mp.L1 <= 0) return 0;
+  int64_t p;
+  if (mp.mode == ORTHRUS_MASK_CAUSAL) {
+    p = t + (mp.offset ? mp.offset[b] : 0);
+  } else if (mp.mode == ORTHRUS_MASK_DUAL) {
+    p = mp.anchors[b * mp.A + min(t / mp.block, mp.A - 1)];
+  } else {
+    return 0;
+  }
+  p = min(max(p, static_cast<int64_t>(0)), mp.L1 - 1);
+  return mp.doc_start[b * mp.L1 + p];
+}
+
 constexpr int kSimtQ = 4;  // queries (warps) per CTA
 
 // grid (ceil(Tq / kSimtQ), Hq, B), block 32 * kSimtQ. Source strides in elements.
@@ -72,6 +92,7 @@ __global__ void __launch_bounds__(32 * kSimtQ) attn_fwd_simt_kernel(
   const bool live = t < Tq;
   int64_t e1 = 0, s2 = 0, e2 = 0;
   if (live) query_ranges(mp, b, t, e1, s2, e2);
+  const int64_t s1 = live ? source1_start(mp, b, t) : 0;
   const T* qrow = q + ((b * Hq + h) * Tq + (live ? t : 0)) * D;
   for (int e = lane; e < hd; e += 32) sq[warp][e] = live ? to_f32<T>(qrow[e]) : 0.f;
   // CTA-wide key ranges
@@ -97,7 +118,7 @@ __global__ void __launch_bounds__(32 * kSimtQ) attn_fwd_simt_kernel(
     const T* Vv = src == 0 ? v1 + b * s1b + hk * s1h : v2 + b * s2b + hk * s2h;
     const int64_t lo = src == 0 ? 0 : (r2min / 32) * 32;
     const int64_t hi = src == 0 ? r1max : r2max;
-    const int64_t my_lo = src == 0 ? 0 : s2, my_hi = src == 0 ? e1 : e2;
+    const int64_t my_lo = src == 0 ? s1 : s2, my_hi = src == 0 ? e1 : e2;
     if (src == 1 && (k2 == nullptr || r2max <= r2min)) break;
     for (int64_t k0 = lo; k0 < hi; k0 += 32) {
       __syncthreads();
@@ -109,7 +130,8 @@ __global__ void __launch_bounds__(32 * kSimtQ) attn_fwd_simt_kernel(
         sv[r][e] = ok ? to_f32<T>(Vv[key * D + e]) : 0.f;
       }
       __syncthreads();
-      if (!live || k0 + 32 <= my_lo || k0 >= my_hi) continue;  // no visible key in this tile
+      // no visible key in this tile (an empty range: a document starting at the block's anchor)
+      if (!live || my_hi <= my_lo || k0 + 32 <= my_lo || k0 >= my_hi) continue;
       const int64_t key = k0 + lane;
       const bool vis = key >= my_lo && key < my_hi;
       float s = 0.f;
@@ -213,6 +235,7 @@ __global__ void __launch_bounds__(32 * kSimtQ) attn_dq_simt_kernel(
   const bool live = t < Tq;
   int64_t e1 = 0, s2 = 0, e2 = 0;
   if (live) query_ranges(mp, b, t, e1, s2, e2);
+  const int64_t s1 = live ? source1_start(mp, b, t) : 0;
   const int64_t qi = (b * Hq + h) * Tq + (live ? t : 0);
   for (int e = lane; e < hd; e += 32) {
     sq[warp][e] = live ? to_f32<T>(q[qi * D + e]) : 0.f;
@@ -242,7 +265,7 @@ __global__ void __launch_bounds__(32 * kSimtQ) attn_dq_simt_kernel(
     const T* Vv = src == 0 ? v1 + b * s1b + hk * s1h : v2 + b * s2b + hk * s2h;
     const int64_t lo = src == 0 ? 0 : (r2min / 32) * 32;
     const int64_t hi = src == 0 ? r1max : r2max;
-    const int64_t my_lo = src == 0 ? 0 : s2, my_hi = src == 0 ? e1 : e2;
+    const int64_t my_lo = src == 0 ? s1 : s2, my_hi = src == 0 ? e1 : e2;
     for (int64_t k0 = lo; k0 < hi; k0 += 32) {
       __syncthreads();
       for (int i = threadIdx.x; i < 32 * hd; i += blockDim.x) {
@@ -253,7 +276,7 @@ __global__ void __launch_bounds__(32 * kSimtQ) attn_dq_simt_kernel(
         sv[r][e] = ok ? to_f32<T>(Vv[key * D + e]) : 0.f;
       }
       __syncthreads();
-      if (!live || k0 + 32 <= my_lo || k0 >= my_hi) continue;
+      if (!live || my_hi <= my_lo || k0 + 32 <= my_lo || k0 >= my_hi) continue;
       const int64_t key = k0 + lane;
       const bool vis = key >= my_lo && key < my_hi;
       float s = 0.f, dp = 0.f;

@@ -259,6 +259,7 @@ __global__ void __launch_bounds__(192, 1)
     const bool live = t < Tq;
     int64_t e1 = 0, s2 = 0, e2 = 0;
     if (live) query_ranges(mp, b, t, e1, s2, e2);
+    const int64_t s1 = live ? source1_start(mp, b, t) : 0;
     if (!has2) e2 = s2 = 0;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const uint32_t p_base = smem_u32(smem + S::OFF_P);
@@ -292,7 +293,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const bool src2 = j >= n1;
       const int64_t key0 = (src2 ? t2a + (j - n1) : j) * 128;
-      const int64_t lo = src2 ? s2 : 0, hi = src2 ? e2 : e1;
+      const int64_t lo = src2 ? s2 : s1, hi = src2 ? e2 : e1;
       const uint32_t sb = lane_base + (j & 1) * 128;
       // pass 1: masked row max (log2 units)
       float tmax = -INFINITY;
@@ -526,6 +527,7 @@ __global__ void __launch_bounds__(192, 1)
     const bool live = t < Tq;
     int64_t e1 = 0, s2 = 0, e2 = 0;
     if (live) query_ranges(mp, b, t, e1, s2, e2);
+    const int64_t s1 = live ? source1_start(mp, b, t) : 0;
     if (!has2) e2 = s2 = 0;
     const int64_t qi = (b * Hq + h) * Tq + (live ? t : 0);
     const float L2e = live ? lse[qi] * kLog2e : 0.f;
@@ -542,7 +544,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const bool src2 = j >= n1;
       const int64_t key0 = (src2 ? t2a + (j - n1) : j) * 128;
-      const int64_t lo = src2 ? s2 : 0, hi = src2 ? e2 : e1;
+      const int64_t lo = src2 ? s2 : s1, hi = src2 ? e2 : e1;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float x[32], y[32];
@@ -1030,6 +1032,7 @@ __global__ void __launch_bounds__(320, 1)
     const bool live = t < Tq;
     int64_t e1 = 0, s2 = 0, e2 = 0;
     if (live) query_ranges(mp, b, t, e1, s2, e2);
+    const int64_t s1 = live ? source1_start(mp, b, t) : 0;
     if (!has2) e2 = s2 = 0;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const uint32_t s_col = lane_base + h * 128;
@@ -1053,7 +1056,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_arrive(&s_free[h]);  // the MMA warp may overwrite S with the next tile's scores
       const bool src2 = j >= n1;
       const int64_t key0 = (src2 ? t2a + (j - n1) : j) * 128;
-      const int64_t lo = (src2 ? s2 : 0) - key0, hi = (src2 ? e2 : e1) - key0;  // visible columns
+      const int64_t lo = (src2 ? s2 : s1) - key0, hi = (src2 ? e2 : e1) - key0;  // visible columns
       const bool full = lo <= 0 && hi >= 128;
       // row max of the raw scores (scale > 0 commutes with max), four independent chains
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -1359,6 +1362,7 @@ __global__ void __launch_bounds__(320, 1)
     const bool live = t < Tq;
     int64_t e1 = 0, s2 = 0, e2 = 0;
     if (live) query_ranges(mp, b, t, e1, s2, e2);
+    const int64_t s1 = live ? source1_start(mp, b, t) : 0;
     if (!has2) e2 = s2 = 0;
     const int64_t qi = (b * Hq + hh) * Tq + (live ? t : 0);
     const float L2e = live ? lse[qi] * kLog2e : 0.f;
@@ -1375,7 +1379,7 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
       const bool src2 = j >= n1b;
       const int64_t key0 = (src2 ? t2b + (j - n1b) : j) * 64;
-      const int64_t lo = (src2 ? s2 : 0) - key0, hi = (src2 ? e2 : e1) - key0;
+      const int64_t lo = (src2 ? s2 : s1) - key0, hi = (src2 ? e2 : e1) - key0;
       float x[64];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {

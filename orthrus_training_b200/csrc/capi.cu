@@ -283,10 +283,11 @@ int orthrus_attn_tilemap(const int64_t* anchors, int64_t B, int64_t A, int block
   return ORTHRUS_OK;
 }
 
-int orthrus_attn_fwd(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b, int64_t L1,
-                     const void* k2, const void* v2, int64_t s2h, int64_t s2b, int64_t L2, int64_t B, int Hq, int Hkv,
-                     int64_t Tq, int hd, int D, float scale, int mask, const int64_t* anchors, int64_t A, int block,
-                     const int32_t* offset, const int32_t* limit2, void* o, float* lse, int dtype, void* stream) {
+static int attn_fwd_impl(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b, int64_t L1,
+                         const void* k2, const void* v2, int64_t s2h, int64_t s2b, int64_t L2, int64_t B, int Hq,
+                         int Hkv, int64_t Tq, int hd, int D, float scale, int mask, const int64_t* anchors, int64_t A,
+                         int block, const int32_t* offset, const int32_t* limit2, const int32_t* doc_start, void* o,
+                         float* lse, int dtype, void* stream) {
   ORTHRUS_CHECK_ARG(q && k1 && v1 && o && B > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && Tq > 0 && L1 >= 0);
   ORTHRUS_CHECK_ARG(hd > 0 && hd <= D && D <= 128 && mask >= 0 && mask <= ORTHRUS_MASK_TREE);
   ORTHRUS_CHECK_ARG(mask != ORTHRUS_MASK_DUAL || (anchors && A > 0 && block > 0 && k2 && v2));
@@ -295,6 +296,7 @@ int orthrus_attn_fwd(const void* q, const void* k1, const void* v1, int64_t s1h,
   ORTHRUS_CHECK_ARG(B < 65536 && Hq < 65536);
   const bool has2 = k2 != nullptr && mask != ORTHRUS_MASK_CAUSAL;
   MaskParams mp{mask, anchors, A, block, offset, limit2, L1, has2 ? L2 : 0};
+  mp.doc_start = doc_start;
   cudaStream_t st = as_stream(stream);
   if (use_tensor_cores(dtype, hd, D, mask, offset)) {
     ORTHRUS_CHECK_ARG(s1b == Hkv * s1h && (!has2 || s2b == Hkv * s2h));
@@ -392,11 +394,11 @@ SideStream* side_stream_on_current_device() {
 
 }  // namespace
 
-int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b, int64_t L1,
-                     const void* k2, const void* v2, int64_t s2h, int64_t s2b, int64_t L2, int64_t B, int Hq, int Hkv,
-                     int64_t Tq, int hd, int D, float scale, const int64_t* anchors, int64_t A, int block,
-                     const void* o, const float* lse, const void* do_, float* dq, float* dk2, float* dv2,
-                     void* workspace, size_t workspace_bytes, int dtype, void* stream) {
+static int attn_bwd_impl(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b, int64_t L1,
+                         const void* k2, const void* v2, int64_t s2h, int64_t s2b, int64_t L2, int64_t B, int Hq,
+                         int Hkv, int64_t Tq, int hd, int D, float scale, const int64_t* anchors, int64_t A, int block,
+                         const int32_t* doc_start, const void* o, const float* lse, const void* do_, float* dq,
+                         float* dk2, float* dv2, void* workspace, size_t workspace_bytes, int dtype, void* stream) {
   ORTHRUS_CHECK_ARG(q && k1 && v1 && k2 && v2 && anchors && o && lse && do_ && dq && dk2 && dv2);
   ORTHRUS_CHECK_ARG(B > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && Tq > 0 && hd > 0 && hd <= D && D <= 128);
   ORTHRUS_CHECK_ARG(A > 0 && block > 0 && L2 >= Tq && B < 65536 && Hq < 65536);
@@ -404,6 +406,7 @@ int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h,
   float* delta = static_cast<float*>(workspace);
   cudaStream_t st = as_stream(stream);
   MaskParams mp{ORTHRUS_MASK_DUAL, anchors, A, block, nullptr, nullptr, L1, L2};
+  mp.doc_start = doc_start;
   const int64_t items = B * Tq * Hq;
   const bool tc = use_tensor_cores(dtype, hd, D, ORTHRUS_MASK_DUAL, nullptr) && (128 % block == 0) &&
                   (Hq / Hkv) <= DkvSmem<128>::MAX_GROUP;
@@ -567,6 +570,44 @@ int orthrus_decode_verify_accept(const float* logits, int64_t B, int K, int64_t 
       accepted_log, cycle, log_cap);
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
+}
+
+int orthrus_attn_fwd(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b, int64_t L1,
+                     const void* k2, const void* v2, int64_t s2h, int64_t s2b, int64_t L2, int64_t B, int Hq, int Hkv,
+                     int64_t Tq, int hd, int D, float scale, int mask, const int64_t* anchors, int64_t A, int block,
+                     const int32_t* offset, const int32_t* limit2, void* o, float* lse, int dtype, void* stream) {
+  return attn_fwd_impl(q, k1, v1, s1h, s1b, L1, k2, v2, s2h, s2b, L2, B, Hq, Hkv, Tq, hd, D, scale, mask, anchors, A,
+                       block, offset, limit2, nullptr, o, lse, dtype, stream);
+}
+
+int orthrus_attn_fwd_doc(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b, int64_t L1,
+                         const void* k2, const void* v2, int64_t s2h, int64_t s2b, int64_t L2, int64_t B, int Hq,
+                         int Hkv, int64_t Tq, int hd, int D, float scale, int mask, const int64_t* anchors, int64_t A,
+                         int block, const int32_t* offset, const int32_t* limit2, const int32_t* doc_start, void* o,
+                         float* lse, int dtype, void* stream) {
+  ORTHRUS_CHECK_ARG(doc_start != nullptr && L1 > 0);
+  return attn_fwd_impl(q, k1, v1, s1h, s1b, L1, k2, v2, s2h, s2b, L2, B, Hq, Hkv, Tq, hd, D, scale, mask, anchors, A,
+                       block, offset, limit2, doc_start, o, lse, dtype, stream);
+}
+
+int orthrus_attn_bwd(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b, int64_t L1,
+                     const void* k2, const void* v2, int64_t s2h, int64_t s2b, int64_t L2, int64_t B, int Hq, int Hkv,
+                     int64_t Tq, int hd, int D, float scale, const int64_t* anchors, int64_t A, int block,
+                     const void* o, const float* lse, const void* do_, float* dq, float* dk2, float* dv2,
+                     void* workspace, size_t workspace_bytes, int dtype, void* stream) {
+  return attn_bwd_impl(q, k1, v1, s1h, s1b, L1, k2, v2, s2h, s2b, L2, B, Hq, Hkv, Tq, hd, D, scale, anchors, A, block,
+                       nullptr, o, lse, do_, dq, dk2, dv2, workspace, workspace_bytes, dtype, stream);
+}
+
+int orthrus_attn_bwd_doc(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b, int64_t L1,
+                         const void* k2, const void* v2, int64_t s2h, int64_t s2b, int64_t L2, int64_t B, int Hq,
+                         int Hkv, int64_t Tq, int hd, int D, float scale, const int64_t* anchors, int64_t A,
+                         int block, const int32_t* doc_start, const void* o, const float* lse, const void* do_,
+                         float* dq, float* dk2, float* dv2, void* workspace, size_t workspace_bytes, int dtype,
+                         void* stream) {
+  ORTHRUS_CHECK_ARG(doc_start != nullptr && L1 > 0);
+  return attn_bwd_impl(q, k1, v1, s1h, s1b, L1, k2, v2, s2h, s2b, L2, B, Hq, Hkv, Tq, hd, D, scale, anchors, A, block,
+                       doc_start, o, lse, do_, dq, dk2, dv2, workspace, workspace_bytes, dtype, stream);
 }
 
 }  // extern "C"

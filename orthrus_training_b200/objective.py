@@ -237,12 +237,14 @@ class DualViewAttention(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, qkv, q_norm_w, k_norm_w, ar_k, ar_v, positions, anchors, inv_freq, meta):
+    def forward(ctx, qkv, q_norm_w, k_norm_w, ar_k, ar_v, positions, anchors, inv_freq, meta,
+                doc_start=None):
         B, Q, Hq, Hkv, hd, D, K, eps = meta
         q, k2, v2, rstd = ops.qkv_prep(qkv, positions, inv_freq, q_norm_w, k_norm_w, B, Q, Hq, Hkv,
                                        hd, D, eps, want_rstd=True)
         o, lse = ops.attention_fwd(q, ar_k, ar_v, k2, v2, mask=MASK_DUAL, hd=hd, scale=hd ** -0.5,
-                                   anchors=anchors, block=K)
+                                   anchors=anchors, block=K, doc_start=doc_start)
+        ctx.doc_start = doc_start
         ctx.save_for_backward(qkv, q_norm_w, k_norm_w, ar_k, ar_v, positions, anchors, inv_freq, q,
                               k2, v2, o, lse, rstd)
         ctx.meta = meta
@@ -254,10 +256,10 @@ class DualViewAttention(torch.autograd.Function):
         B, Q, Hq, Hkv, hd, D, K, eps = ctx.meta
         dout = grad_o.contiguous().view(B, Q, Hq, hd).to(q.dtype)
         dq, dk2, dv2 = ops.attention_bwd(q, ar_k, ar_v, k2, v2, anchors, K, o, lse, dout, hd=hd,
-                                         scale=hd ** -0.5)
+                                         scale=hd ** -0.5, doc_start=ctx.doc_start)
         dqkv, dqw, dkw = ops.qkv_prep_backward(qkv, positions, inv, qn, kn, rstd, dq, dk2, dv2, B,
                                                Q, Hq, Hkv, hd, D)
-        return dqkv, dqw.to(qn.dtype), dkw.to(kn.dtype), None, None, None, None, None, None
+        return dqkv, dqw.to(qn.dtype), dkw.to(kn.dtype), None, None, None, None, None, None, None
 
 
 class DualViewAttentionFused(torch.autograd.Function):
@@ -270,12 +272,13 @@ class DualViewAttentionFused(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, h, w_qkv, q_norm_w, k_norm_w, ar_k, ar_v, positions, anchors, inv_freq, rope_cos,
-                rope_sin, meta):
+                rope_sin, meta, doc_start=None):
         B, Q, Hq, Hkv, hd, D, K, eps = meta
         q, k2, v2, qkv, rstd = ops.linear_qkv_rope(h, w_qkv, q_norm_w, k_norm_w, (rope_cos, rope_sin), B, Q,
                                                    Hq, Hkv, eps, positions=positions, keep=True)
         o, lse = ops.attention_fwd(q, ar_k, ar_v, k2, v2, mask=MASK_DUAL, hd=hd, scale=hd ** -0.5,
-                                   anchors=anchors, block=K)
+                                   anchors=anchors, block=K, doc_start=doc_start)
+        ctx.doc_start = doc_start
         ctx.save_for_backward(h, w_qkv, qkv, q_norm_w, k_norm_w, ar_k, ar_v, positions, anchors, inv_freq,
                               q, k2, v2, o, lse, rstd)
         ctx.meta = meta
@@ -287,16 +290,16 @@ class DualViewAttentionFused(torch.autograd.Function):
         B, Q, Hq, Hkv, hd, D, K, eps = ctx.meta
         dout = grad_o.contiguous().view(B, Q, Hq, hd).to(q.dtype)
         dq, dk2, dv2 = ops.attention_bwd(q, ar_k, ar_v, k2, v2, anchors, K, o, lse, dout, hd=hd,
-                                         scale=hd ** -0.5)
+                                         scale=hd ** -0.5, doc_start=ctx.doc_start)
         dqkv, dqw, dkw = ops.qkv_prep_backward(qkv, positions, inv, qn, kn, rstd, dq, dk2, dv2, B,
                                                Q, Hq, Hkv, hd, D)
         dh = _dx(dqkv, w)
         dw = _dw(dqkv, h)
         return (dh, dw, dqw.to(qn.dtype), dkw.to(kn.dtype), None, None, None, None, None, None, None,
-                None)
+                None, None)
 
 
-def _teacher_layer(backbone, i, x, pos, B, L, inv, rope=None):
+def _teacher_layer(backbone, i, x, pos, B, L, inv, rope=None, doc_start=None):
     cfg = backbone.config
     layer = backbone.layers[i]
     attn = layer.self_attn
@@ -312,7 +315,8 @@ def _teacher_layer(backbone, i, x, pos, B, L, inv, rope=None):
         qkv = h @ attn.packed_qkv(False).t()
         q, k, v, _ = ops.qkv_prep(qkv, pos, inv, attn.q_norm.weight, attn.k_norm.weight, B, L, Hq,
                                   Hkv, hd, D, eps)
-    o, _ = ops.attention_fwd(q, k, v, mask=MASK_CAUSAL, hd=hd, scale=hd ** -0.5, want_lse=False)
+    o, _ = ops.attention_fwd(q, k, v, mask=MASK_CAUSAL, hd=hd, scale=hd ** -0.5, want_lse=False,
+                             doc_start=doc_start)
     # residual adds ride in the GEMM epilogue
     x = _add_projection(x, o.view(B * L, Hq * hd), attn.o_proj.weight)
     h = ops.rms_norm(x, layer.post_attention_layernorm.weight, eps)
@@ -326,7 +330,7 @@ def _teacher_layer(backbone, i, x, pos, B, L, inv, rope=None):
     return x, k, v
 
 
-def _diffusion_layer(backbone, i, x, ar_k, ar_v, positions, anchors, inv, B, Q, rope=None):
+def _diffusion_layer(backbone, i, x, ar_k, ar_v, positions, anchors, inv, B, Q, rope=None, doc_start=None):
     cfg = backbone.config
     layer = backbone.layers[i]
     attn = layer.self_attn
@@ -337,11 +341,11 @@ def _diffusion_layer(backbone, i, x, ar_k, ar_v, positions, anchors, inv, B, Q, 
     w_qkv = torch.cat([attn.q_proj_diff.weight, attn.k_proj_diff.weight, attn.v_proj_diff.weight], 0)
     if rope is not None and ops.fused_qkv_rope_supported(h, hd, padded_head_dim(hd), Q, Hq, Hkv):
         o = DualViewAttentionFused.apply(h, w_qkv, attn.q_norm_diff.weight, attn.k_norm_diff.weight, ar_k,
-                                         ar_v, positions, anchors, inv, rope[0], rope[1], meta)
+                                         ar_v, positions, anchors, inv, rope[0], rope[1], meta, doc_start)
     else:
         qkv = F.linear(h, w_qkv)
         o = DualViewAttention.apply(qkv, attn.q_norm_diff.weight, attn.k_norm_diff.weight, ar_k, ar_v,
-                                    positions, anchors, inv, meta)
+                                    positions, anchors, inv, meta, doc_start)
     x = _projection_residual(x, o, attn.o_proj_diff.weight)
     w_gu, w_down = layer.mlp.packed_gate_up(), layer.mlp.down_proj.weight
     if _mlp_block_ok(x, w_gu, w_down) and not layer.post_attention_layernorm.weight.requires_grad:
@@ -359,13 +363,13 @@ def _backbone(model):
     return model.model if isinstance(model, OrthrusLM) else model
 
 
-def _student_stack(backbone, x, cache, anchors, positions, rope, inv):
+def _student_stack(backbone, x, cache, anchors, positions, rope, inv, doc_start=None):
     """The differentiable diffusion view: every layer over x [B*Q, d] (the block embeddings) with
     the teacher's keys / values cache[i] = (k, v) [B, Hkv, >= L, D], then the final norm."""
     B, Q = positions.shape
     checkpoint = backbone.gradient_checkpointing and torch.is_grad_enabled()
     for i, (k, v) in enumerate(cache):
-        args = (backbone, i, x, k, v, positions, anchors, inv, B, Q, rope)
+        args = (backbone, i, x, k, v, positions, anchors, inv, B, Q, rope, doc_start)
         if checkpoint:
             x = torch.utils.checkpoint.checkpoint(_diffusion_layer, *args, use_reentrant=False)
         else:
@@ -399,20 +403,38 @@ def diffusion_states(backbone, x: torch.Tensor, cache, positions: torch.Tensor,
                           backbone.inv_freq(x.device))
 
 
+def document_starts(assistant_mask: torch.Tensor) -> torch.Tensor:
+    """First position of each position's document in packed rows, int32 [B, L]. Rows concatenate
+    conversations as prompt then response (orthrus/data.py:43-69), so a new document begins at
+    position 0 and wherever an unsupervised token follows a supervised one. A conversation whose
+    response is empty shows no boundary and stays joined to its neighbour."""
+    m = assistant_mask.to(torch.bool)
+    B, L = m.shape
+    boundary = torch.zeros_like(m)
+    boundary[:, 0] = True
+    boundary[:, 1:] = m[:, :-1] & ~m[:, 1:]
+    pos = torch.arange(L, device=m.device, dtype=torch.int32).expand(B, L)
+    starts = torch.where(boundary, pos, torch.zeros_like(pos))
+    return starts.cummax(dim=1).values.to(torch.int32).contiguous()
+
+
 class TeacherPass:
     """The frozen AR view over the clean rows: final hidden states [B, L, d] and every layer's
-    keys / values, plus the rotary tables the diffusion view reuses."""
+    keys / values, plus the rotary tables the diffusion view reuses and the document starts
+    (document_starts) both views were masked with, or None."""
 
-    def __init__(self, states, cache, rope, inv, input_ids):
+    def __init__(self, states, cache, rope, inv, input_ids, doc_start=None):
         self.states, self.cache, self.rope, self.inv = states, cache, rope, inv
-        self.input_ids = input_ids
+        self.input_ids, self.doc_start = input_ids, doc_start
 
 
 @torch.no_grad()
-def teacher_pass(model: OrthrusLM, input_ids: torch.Tensor) -> TeacherPass:
+def teacher_pass(model: OrthrusLM, input_ids: torch.Tensor,
+                 doc_start: torch.Tensor | None = None) -> TeacherPass:
     """The AR half of model_states (orthrus/objective.py:247-254, the frozen teacher over the clean
     rows). It depends on the input ids only, so a caller may queue it before the anchors are
-    drawn and let the host-side anchor work overlap it."""
+    drawn and let the host-side anchor work overlap it. `doc_start` (document_starts, int32
+    [B, L]) keeps each query inside its own document; the reference has no such mask (None)."""
     backbone = _backbone(model)
     cfg = backbone.config
     if any(t != "full_attention" for t in getattr(cfg, "layer_types", ["full_attention"])
@@ -428,25 +450,28 @@ def teacher_pass(model: OrthrusLM, input_ids: torch.Tensor) -> TeacherPass:
     rope = _rope_for(x, backbone, L, L)
     cache = []
     for i in range(cfg.num_hidden_layers):
-        x, k, v = _teacher_layer(backbone, i, x, pos, B, L, inv, rope)
+        x, k, v = _teacher_layer(backbone, i, x, pos, B, L, inv, rope, doc_start)
         cache.append((k, v))
     states = ops.rms_norm(x, backbone.norm.weight, cfg.rms_norm_eps).view(B, L, d)
-    return TeacherPass(states, cache, rope, inv, input_ids)
+    return TeacherPass(states, cache, rope, inv, input_ids, doc_start)
 
 
 def model_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tensor,
                  compiled: bool = False, kernel_options: dict | None = None, *,
-                 teacher: TeacherPass | None = None):
+                 teacher: TeacherPass | None = None, doc_start: torch.Tensor | None = None):
     """Final hidden states of the diffusion view over all anchor blocks [B, A*K, d] and of the
     frozen AR view over the clean rows [B, L, d] (orthrus/objective.py:228-272). `compiled` and
     `kernel_options` are accepted for signature compatibility; the kernels are fixed. `teacher`
-    is the result of teacher_pass(model, input_ids) when the caller queued it already."""
+    is the result of teacher_pass(model, input_ids) when the caller queued it already; otherwise
+    `doc_start` (document_starts) opts both views into the document mask."""
     backbone = _backbone(model)
     cfg = backbone.config
     if teacher is None:
-        teacher = teacher_pass(model, input_ids)
+        teacher = teacher_pass(model, input_ids, doc_start)
     elif teacher.input_ids is not input_ids:
         raise ValueError("the teacher pass was run on other input ids")
+    elif doc_start is not None and teacher.doc_start is not doc_start:
+        raise ValueError("the teacher pass was run with other document starts")
     K = cfg.block_size
     B, L = input_ids.shape
     d = cfg.hidden_size
@@ -457,7 +482,8 @@ def model_states(model: OrthrusLM, input_ids: torch.Tensor, anchors: torch.Tenso
     block_ids[:, :, 0] = input_ids.gather(1, anchors)
     Q = anchors.shape[1] * K
     x = F.embedding(block_ids.flatten(1), backbone.embed_tokens.weight).reshape(B * Q, d)
-    student = _student_stack(backbone, x, teacher.cache, anchors, positions, teacher.rope, teacher.inv)
+    student = _student_stack(backbone, x, teacher.cache, anchors, positions, teacher.rope, teacher.inv,
+                             teacher.doc_start)
     return student.view(B, Q, d), teacher.states
 
 
@@ -540,19 +566,25 @@ class SupervisedLayout:
 def orthrus_loss(model: OrthrusLM, input_ids: torch.Tensor, assistant_mask: torch.Tensor,
                  anchors: torch.Tensor, valid: torch.Tensor, kl_chunk_size: int,
                  compiled: bool = False, kernel_options: dict | None = None, gamma: float = 0.0, *,
-                 teacher: TeacherPass | None = None, layout: SupervisedLayout | None = None):
+                 teacher: TeacherPass | None = None, layout: SupervisedLayout | None = None,
+                 document_mask: bool = False):
     """Mean (or position-weighted mean) forward KL over supervised block positions and its
     statistics (orthrus/objective.py:395-453). `teacher` (teacher_pass) and `layout`
     (SupervisedLayout) may be prepared by the caller: the training step queues the teacher first
-    and settles the layout's host reads on a side stream meanwhile."""
+    and settles the layout's host reads on a side stream meanwhile. `document_mask` (off, as in
+    the reference) keeps attention inside each packed conversation (document_starts); a prepared
+    teacher carries its own choice."""
     K = model.config.block_size
     # The supervised rows depend on the inputs only. Their layout is settled before the forward is
     # queued, so its host reads (the kept-row and unique-target counts, bincount's size) happen
     # while the device is idle rather than between the forward and the LM head.
     if layout is None:
         layout = SupervisedLayout(assistant_mask, anchors, valid, K, gamma)
+    doc_start = None
+    if document_mask and teacher is None:
+        doc_start = document_starts(assistant_mask)
     student, teacher = model_states(model, input_ids, anchors, compiled, kernel_options,
-                                    teacher=teacher)
+                                    teacher=teacher, doc_start=doc_start)
     hidden = student.shape[-1]
     row_weight = layout.row_weight
     total, kl_rows, agree, kl_by_offset, agree_by_offset = _FusedKL.apply(

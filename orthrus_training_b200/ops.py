@@ -387,12 +387,14 @@ def _src(t):
 
 def attention_fwd(q, k1, v1, k2=None, v2=None, *, mask: int, hd: int, scale: float,
                   anchors=None, block: int = 0, offset=None, limit2=None, L1: int | None = None,
-                  want_lse: bool = True):
+                  want_lse: bool = True, doc_start=None):
     """Dual-view / causal / draft / tree attention. q [B, Hq, Tq, D]; sources [B, Hkv, rows, D].
     For the tree mask (3) k2/v2 are the cache k1/v1 holding the new tokens at rows offset[b] + t
     and limit2 is int32 [Tq]: the first new-token index of each query's branch (>= 1).
+    doc_start (opt-in document mask, int32 [B, L1], see objective.document_starts) keeps the
+    source-1 keys of a query to its own document (causal) or to its anchor's document (dual).
     Returns (o [B, Tq, Hq, hd] token-major, lse [B, Hq, Tq] fp32 or None)."""
-    _require_cuda(q, k1, v1, k2, v2, anchors, offset, limit2)
+    _require_cuda(q, k1, v1, k2, v2, anchors, offset, limit2, doc_start)
     B, Hq, Tq, D = q.shape
     if mask == 3 and (offset is None or limit2 is None or limit2.dtype != torch.int32
                       or limit2.numel() != Tq or not limit2.is_contiguous()):
@@ -410,11 +412,19 @@ def attention_fwd(q, k1, v1, k2=None, v2=None, *, mask: int, hd: int, scale: flo
     if anchors is not None:
         anchors = anchors.to(torch.int64).contiguous()
     t0 = TIMER.begin() if TIMER is not None else None
-    L.check(L.lib().orthrus_attn_fwd(
-        q.data_ptr(), k1.data_ptr(), v1.data_ptr(), s1h, s1b, L1, L.ptr(k2), L.ptr(v2), s2h, s2b,
-        L2, B, Hq, Hkv, Tq, hd, D, float(scale), mask, L.ptr(anchors), A, block, L.ptr(offset),
-        L.ptr(limit2), o.data_ptr(), L.ptr(lse), L.dtype_code(q.dtype), L.stream_of(q.device)),
-        "attn_fwd")
+    if doc_start is None:
+        L.check(L.lib().orthrus_attn_fwd(
+            q.data_ptr(), k1.data_ptr(), v1.data_ptr(), s1h, s1b, L1, L.ptr(k2), L.ptr(v2), s2h, s2b,
+            L2, B, Hq, Hkv, Tq, hd, D, float(scale), mask, L.ptr(anchors), A, block, L.ptr(offset),
+            L.ptr(limit2), o.data_ptr(), L.ptr(lse), L.dtype_code(q.dtype), L.stream_of(q.device)),
+            "attn_fwd")
+    else:
+        doc_start = _doc_start_arg(doc_start, B, L1)
+        L.check(L.lib().orthrus_attn_fwd_doc(
+            q.data_ptr(), k1.data_ptr(), v1.data_ptr(), s1h, s1b, L1, L.ptr(k2), L.ptr(v2), s2h, s2b,
+            L2, B, Hq, Hkv, Tq, hd, D, float(scale), mask, L.ptr(anchors), A, block, L.ptr(offset),
+            L.ptr(limit2), doc_start.data_ptr(), o.data_ptr(), L.ptr(lse), L.dtype_code(q.dtype),
+            L.stream_of(q.device)), "attn_fwd_doc")
     if t0 is not None:
         TIMER.end(f"attn_fwd_{('causal', 'dual', 'draft', 'tree')[mask]}", t0,
                   attention_flops(mask, B, Hq, Tq, hd, anchors, block, L1))
@@ -432,8 +442,19 @@ def attention_flops(mask, B, Hq, Tq, hd, anchors=None, block=0, L1=0):
     return 0.0
 
 
-def attention_bwd(q, k1, v1, k2, v2, anchors, block, o, lse, dout, *, hd: int, scale: float):
-    """Backward of the dual mask: (dq [B, Hq, Tq, D], dk2, dv2 [B, Hkv, L2, D]) fp32."""
+def _doc_start_arg(doc_start, B: int, L1: int) -> torch.Tensor:
+    """int32 [B, L1] document starts of the source-1 positions (a longer row is cut to L1)."""
+    if doc_start.dtype != torch.int32 or doc_start.dim() != 2 or doc_start.shape[0] != B \
+            or doc_start.shape[1] < L1:
+        raise ValueError(f"doc_start must be int32 [B, >= L1] = [{B}, >= {L1}], got "
+                         f"{doc_start.dtype} {tuple(doc_start.shape)}")
+    return doc_start[:, :L1].contiguous()
+
+
+def attention_bwd(q, k1, v1, k2, v2, anchors, block, o, lse, dout, *, hd: int, scale: float,
+                  doc_start=None):
+    """Backward of the dual mask: (dq [B, Hq, Tq, D], dk2, dv2 [B, Hkv, L2, D]) fp32. doc_start as
+    in attention_fwd (the same mask as the forward's)."""
     B, Hq, Tq, D = q.shape
     Hkv = k1.shape[1]
     s1h, s1b, L1 = _src(k1)
@@ -448,12 +469,21 @@ def attention_bwd(q, k1, v1, k2, v2, anchors, block, o, lse, dout, *, hd: int, s
     anchors = anchors.to(torch.int64).contiguous()
     dout = dout.contiguous()
     t0 = TIMER.begin() if TIMER is not None else None
-    L.check(lib.orthrus_attn_bwd(
-        q.data_ptr(), k1.data_ptr(), v1.data_ptr(), s1h, s1b, L1, k2.data_ptr(), v2.data_ptr(),
-        s2h, s2b, L2, B, Hq, Hkv, Tq, hd, D, float(scale), anchors.data_ptr(), anchors.shape[1],
-        block, o.data_ptr(), lse.data_ptr(), dout.data_ptr(), dq.data_ptr(), dk2.data_ptr(),
-        dv2.data_ptr(), ws.data_ptr(), ws.numel(), L.dtype_code(q.dtype), L.stream_of(dev)),
-        "attn_bwd")
+    if doc_start is None:
+        L.check(lib.orthrus_attn_bwd(
+            q.data_ptr(), k1.data_ptr(), v1.data_ptr(), s1h, s1b, L1, k2.data_ptr(), v2.data_ptr(),
+            s2h, s2b, L2, B, Hq, Hkv, Tq, hd, D, float(scale), anchors.data_ptr(), anchors.shape[1],
+            block, o.data_ptr(), lse.data_ptr(), dout.data_ptr(), dq.data_ptr(), dk2.data_ptr(),
+            dv2.data_ptr(), ws.data_ptr(), ws.numel(), L.dtype_code(q.dtype), L.stream_of(dev)),
+            "attn_bwd")
+    else:
+        doc_start = _doc_start_arg(doc_start, B, L1)
+        L.check(lib.orthrus_attn_bwd_doc(
+            q.data_ptr(), k1.data_ptr(), v1.data_ptr(), s1h, s1b, L1, k2.data_ptr(), v2.data_ptr(),
+            s2h, s2b, L2, B, Hq, Hkv, Tq, hd, D, float(scale), anchors.data_ptr(), anchors.shape[1],
+            block, doc_start.data_ptr(), o.data_ptr(), lse.data_ptr(), dout.data_ptr(), dq.data_ptr(),
+            dk2.data_ptr(), dv2.data_ptr(), ws.data_ptr(), ws.numel(), L.dtype_code(q.dtype),
+            L.stream_of(dev)), "attn_bwd_doc")
     if t0 is not None:  # QK^T recompute, dP and dQ: 1.5x the forward FLOPs
         TIMER.end("attn_bwd_dual", t0, 1.5 * attention_flops(1, B, Hq, Tq, hd, anchors, block, L1))
     return dq, dk2, dv2

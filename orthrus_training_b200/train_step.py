@@ -21,8 +21,8 @@ import math
 import torch
 import torch.distributed as dist
 
-from orthrus_training_b200.objective import (SupervisedLayout, orthrus_loss, sample_anchors,
-                                              teacher_pass)
+from orthrus_training_b200.objective import (SupervisedLayout, document_starts, orthrus_loss,
+                                              sample_anchors, teacher_pass)
 
 
 def lr_scale(step: int, warmup: int, total: int, min_ratio: float) -> float:
@@ -157,7 +157,8 @@ class Trainer:
     def __init__(self, model, *, lr=1e-4, betas=(0.9, 0.95), weight_decay=0.0, total_steps=1000,
                  warmup_ratio=0.05, min_lr_ratio=0.1, max_grad_norm=1.0, num_anchors=32,
                  kl_chunk_size=4096, gamma=0.0, seed=42, world=1, rank=0, group=None,
-                 check_device_every=50, monitor: PeerMonitor | None = None):
+                 check_device_every=50, monitor: PeerMonitor | None = None,
+                 document_mask: bool = False):
         from orthrus_training_b200.modeling_orthrus import freeze_to_diffusion
 
         self.model = model
@@ -185,6 +186,9 @@ class Trainer:
         self._side = None  # stream of the anchor draw and the supervised layout
         # optional liveness check of the peers before each step's collectives (world > 1)
         self.monitor = monitor
+        # attention kept inside each packed conversation (objective.document_starts); off, as in
+        # the reference, whose rows attend across conversation boundaries
+        self.document_mask = document_mask
 
     def _prepare(self, model, ids, mask, rng, ready):
         """Queues the teacher pass (it needs the input ids only) and draws the anchors and
@@ -201,7 +205,8 @@ class Trainer:
         else:
             side.wait_event(ready)
             main.wait_event(ready)
-        teacher = teacher_pass(model, ids)
+        doc_start = document_starts(mask) if self.document_mask else None
+        teacher = teacher_pass(model, ids, doc_start)
         with torch.cuda.stream(side):
             anchors, valid = sample_anchors(mask, model.config.block_size, self.num_anchors, rng)
             layout = SupervisedLayout(mask, anchors, valid, model.config.block_size, self.gamma)

@@ -102,7 +102,7 @@ def _bf16_tiny(seed=0):
     cfg.block_size = 32
     cfg.mask_token_id = 2047
     torch.manual_seed(seed)
-    with torch.device(DEV):
+    with torch.device("cuda", torch.cuda.current_device()):  # the rank's own GPU under spawn
         model = OrthrusLM(cfg).to(torch.bfloat16)
     copy_diff_from_ar(model)
     with torch.no_grad():
