@@ -377,6 +377,54 @@ int orthrus_decode_verify_accept(const float* logits, int64_t B, int K, int64_t 
                                  int64_t out_cap, int32_t* accepted_log, int32_t* cycle,
                                  int64_t log_cap, void* stream);
 
+/* ---- sampled decoding (temperature > 0) ----
+ * A row's sampling distribution lives on its C top candidates: cand_vals fp32 [R, C] sorted
+ * descending and cand_ids int64 [R, C] (the logits' top C, e.g. torch.topk), with
+ * 1 <= top_k <= C <= 128 and C - top_k spare candidates to keep ties at the top_k-th value.
+ * The filter is the reference's `pick` (orthrus/modeling_orthrus.py:437-449): divide by the
+ * temperature, drop values below the top_k-th, keep the smallest descending prefix whose mass
+ * exceeds top_p (the first always), softmax. Random draws are Philox4x32-10 keyed by `seed` and
+ * counted by (sequence, cycle[b], position, purpose), so a decode is reproducible from its seed
+ * and a cycle replays as a CUDA graph. */
+
+/* probs fp32 [R, C]: the filtered distribution of each candidate row (0 for dropped ones). */
+int orthrus_sample_probs(const float* cand_vals, int64_t R, int C, float temperature, int top_k,
+                         float top_p, float* probs, void* stream);
+
+/* tokens int64 [R]: one draw per row from its filtered distribution, counter (r, cycle[r] or 0 if
+ * cycle is null, 0, first): the prefill's first token (modeling_orthrus.py:460-462). */
+int orthrus_sample_rows(const float* cand_vals, const int64_t* cand_ids, int64_t R, int C,
+                        float temperature, int top_k, float top_p, uint64_t seed,
+                        const int32_t* cycle, int64_t* tokens, void* stream);
+
+/* Draft step of a sampled cycle (modeling_orthrus.py:472-483 with pick): candidate rows
+ * [B, K-1, C] of the diffusion pass; verify_ids[b] = [anchor[b], d_0 .. d_{K-2}] with d_i drawn
+ * from q_i, kept in draft_probs fp32 [B, K-1, C]. Sequences with done[b] are left alone.
+ * 2 <= K <= 64. */
+int orthrus_decode_sample_draft(const float* cand_vals, const int64_t* cand_ids, int64_t B, int K,
+                                int C, float temperature, int top_k, float top_p, uint64_t seed,
+                                const int32_t* cycle, const int64_t* anchor, const uint8_t* done,
+                                int64_t* verify_ids, float* draft_probs, void* stream);
+
+/* Verify / accept step of a sampled cycle: exact rejection sampling
+ * (modeling_orthrus.py:498-511). cand_vals / cand_ids [B, K, C] are the verify pass's rows,
+ * draft_probs / draft_ids [B, K-1, C] the draft step's. Draft i is kept while
+ * u_i < min(1, p_i(d_i) / max(q_i(d_i), 1e-8)) (and stops after an accepted EOS); the bonus token
+ * comes from the normalised max(p - q, 0) at the first rejection (p if its mass is <= 1e-5), or
+ * from p after a full accept. The commit is orthrus_decode_verify_accept's. */
+int orthrus_decode_sample_accept(const float* cand_vals, const int64_t* cand_ids,
+                                 const float* draft_probs, const int64_t* draft_ids, int64_t B,
+                                 int K, int C, float temperature, int top_k, float top_p,
+                                 uint64_t seed, const int64_t* verify_ids, const int64_t* eos,
+                                 int n_eos, const int32_t* max_len, int32_t* start,
+                                 int64_t* anchor, uint8_t* done, int64_t* out_tokens,
+                                 int32_t* out_len, int64_t out_cap, int32_t* accepted_log,
+                                 int32_t* cycle, int64_t log_cap, void* stream);
+
+/* out uint32 [n, 4] = Philox4x32-10(counter_key[r, 0:4], key counter_key[r, 4:6]): the known-answer
+ * check of the decode's generator. */
+int orthrus_philox4x32_10(const uint32_t* counter_key, int64_t n, uint32_t* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -39,6 +39,8 @@ __all__ = [
     "diffusion_generate",
     "decode_base",
     "lr_scale",
+    "sampling_probs",
+    "rejection_accept",
 ]
 
 
@@ -518,3 +520,42 @@ def decode_base(params, cfg, prompt_ids: list, max_new_tokens: int, eos=(), draf
                 break
         done = start >= max_length - 1
     return tokens, accepted_log, passes
+
+
+def sampling_probs(logits: torch.Tensor, temperature: float, top_k: int, top_p: float) -> torch.Tensor:
+    """The sampling distribution of diffusion_generate's `pick` (orthrus/modeling_orthrus.py:
+    437-449): logits / temperature; keep the values >= the top_k-th largest (ties kept); then keep
+    the smallest descending prefix whose softmax mass exceeds top_p (the first token always kept);
+    softmax over what is left. logits [..., V] -> probs [..., V] fp32."""
+    x = logits.float() / temperature
+    if top_k > 0:
+        kth = torch.topk(x, min(top_k, x.shape[-1])).values[..., -1:]
+        x = x.masked_fill(x < kth, float("-inf"))
+    if top_p < 1.0:
+        sx, order = torch.sort(x, descending=True)
+        cum = torch.cumsum(torch.softmax(sx, dim=-1), dim=-1)
+        drop = torch.zeros_like(cum, dtype=torch.bool)
+        drop[..., 1:] = cum[..., :-1] > top_p
+        x = x.masked_fill(torch.zeros_like(drop).scatter(-1, order, drop), float("-inf"))
+    return torch.softmax(x, dim=-1)
+
+
+def rejection_accept(draft_tokens, draft_probs, ar_probs, uniforms):
+    """Exact rejection sampling of one verify cycle (orthrus/modeling_orthrus.py:498-511): draft i
+    is kept while u_i < min(1, p_i(d_i) / max(q_i(d_i), 1e-8)); at the first rejection the next
+    token comes from the normalised residual max(p - q, 0) (p itself if the residual's mass is
+    <= 1e-5); after a full accept from p of the next position. draft_tokens [n], draft_probs
+    [n, V], ar_probs [n + 1, V], uniforms [n] -> (accepted, next-token distribution [V])."""
+    accepted = 0
+    for i in range(draft_tokens.shape[0]):
+        t = int(draft_tokens[i])
+        ratio = ar_probs[i, t] / draft_probs[i, t].clamp_min(1e-8)
+        if float(uniforms[i]) < float(ratio.clamp(max=1.0)):
+            accepted += 1
+        else:
+            break
+    target = ar_probs[accepted]
+    if accepted < draft_tokens.shape[0]:
+        residual = (target - draft_probs[accepted]).clamp_min(0.0)
+        target = residual / residual.sum() if residual.sum() > 1e-5 else target
+    return accepted, target

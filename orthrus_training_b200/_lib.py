@@ -82,6 +82,15 @@ _SIGNATURES = {
     "orthrus_decode_draft": (c_int, [_P, c_int64, c_int, c_int64, _P, _P, _P, _P]),
     "orthrus_decode_verify_accept": (c_int, [_P, c_int64, c_int, c_int64, _P, _P, _P, c_int, _P, _P,
                                              _P, _P, _P, _P, c_int64, _P, _P, c_int64, _P]),
+    "orthrus_sample_probs": (c_int, [_P, c_int64, c_int, c_float, c_int, c_float, _P, _P]),
+    "orthrus_sample_rows": (c_int, [_P, _P, c_int64, c_int, c_float, c_int, c_float, ctypes.c_uint64, _P,
+                                    _P, _P]),
+    "orthrus_decode_sample_draft": (c_int, [_P, _P, c_int64, c_int, c_int, c_float, c_int, c_float,
+                                            ctypes.c_uint64, _P, _P, _P, _P, _P, _P]),
+    "orthrus_decode_sample_accept": (c_int, [_P, _P, _P, _P, c_int64, c_int, c_int, c_float, c_int,
+                                             c_float, ctypes.c_uint64, _P, _P, c_int, _P, _P, _P, _P, _P,
+                                             _P, c_int64, _P, _P, c_int64, _P]),
+    "orthrus_philox4x32_10": (c_int, [_P, c_int64, _P, _P]),
 }
 
 _lib = None

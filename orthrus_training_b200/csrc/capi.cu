@@ -10,6 +10,7 @@
 #include "attention_tc.cuh"
 #include "attention_blockkv.cuh"
 #include "decode.cuh"
+#include "sampling.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
 #include "gemm2_tc.cuh"
@@ -568,6 +569,67 @@ int orthrus_decode_verify_accept(const float* logits, int64_t B, int K, int64_t 
   decode_accept_kernel<<<static_cast<unsigned>(ceil_div(B, 128)), 128, 0, st>>>(
       B, K, verify_ids, ar_tokens, eos, n_eos, max_len, start, anchor, done, out_tokens, out_len, out_cap,
       accepted_log, cycle, log_cap);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+static bool sample_args_ok(int C, float temperature, int top_k, float top_p) {
+  return C >= 1 && C <= kSampleMaxCand && temperature > 0.f && top_k >= 1 && top_k <= C && top_p > 0.f;
+}
+
+int orthrus_sample_probs(const float* cand_vals, int64_t R, int C, float temperature, int top_k, float top_p,
+                         float* probs, void* stream) {
+  ORTHRUS_CHECK_ARG(cand_vals && probs && R >= 0 && sample_args_ok(C, temperature, top_k, top_p));
+  if (R == 0) return ORTHRUS_OK;
+  sample_probs_kernel<<<static_cast<unsigned>(ceil_div(R, 128)), 128, 0, as_stream(stream)>>>(
+      cand_vals, R, C, temperature, top_k, top_p, probs);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+int orthrus_sample_rows(const float* cand_vals, const int64_t* cand_ids, int64_t R, int C, float temperature,
+                        int top_k, float top_p, uint64_t seed, const int32_t* cycle, int64_t* tokens, void* stream) {
+  ORTHRUS_CHECK_ARG(cand_vals && cand_ids && tokens && R >= 0 && sample_args_ok(C, temperature, top_k, top_p));
+  if (R == 0) return ORTHRUS_OK;
+  sample_rows_kernel<<<static_cast<unsigned>(ceil_div(R, 128)), 128, 0, as_stream(stream)>>>(
+      cand_vals, cand_ids, R, C, temperature, top_k, top_p, seed, cycle, tokens);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+int orthrus_decode_sample_draft(const float* cand_vals, const int64_t* cand_ids, int64_t B, int K, int C,
+                                float temperature, int top_k, float top_p, uint64_t seed, const int32_t* cycle,
+                                const int64_t* anchor, const uint8_t* done, int64_t* verify_ids, float* draft_probs,
+                                void* stream) {
+  ORTHRUS_CHECK_ARG(cand_vals && cand_ids && cycle && anchor && done && verify_ids && draft_probs && B > 0 &&
+                    B < (1 << 30) && K >= 2 && K <= kSampleMaxBlock && sample_args_ok(C, temperature, top_k, top_p));
+  decode_sample_draft_kernel<<<static_cast<unsigned>(B), kSampleMaxBlock, 0, as_stream(stream)>>>(
+      cand_vals, cand_ids, K, C, temperature, top_k, top_p, seed, cycle, anchor, done, verify_ids, draft_probs);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+int orthrus_decode_sample_accept(const float* cand_vals, const int64_t* cand_ids, const float* draft_probs,
+                                 const int64_t* draft_ids, int64_t B, int K, int C, float temperature, int top_k,
+                                 float top_p, uint64_t seed, const int64_t* verify_ids, const int64_t* eos, int n_eos,
+                                 const int32_t* max_len, int32_t* start, int64_t* anchor, uint8_t* done,
+                                 int64_t* out_tokens, int32_t* out_len, int64_t out_cap, int32_t* accepted_log,
+                                 int32_t* cycle, int64_t log_cap, void* stream) {
+  ORTHRUS_CHECK_ARG(cand_vals && cand_ids && draft_probs && draft_ids && verify_ids && max_len && start && anchor &&
+                    done && out_tokens && out_len && accepted_log && cycle && B > 0 && B < (1 << 30) && K >= 2 &&
+                    K <= kSampleMaxBlock && sample_args_ok(C, temperature, top_k, top_p));
+  ORTHRUS_CHECK_ARG(n_eos == 0 || eos != nullptr);
+  decode_sample_accept_kernel<<<static_cast<unsigned>(B), kSampleMaxBlock, 0, as_stream(stream)>>>(
+      cand_vals, cand_ids, draft_probs, draft_ids, K, C, temperature, top_k, top_p, seed, verify_ids, eos, n_eos,
+      max_len, start, anchor, done, out_tokens, out_len, out_cap, accepted_log, cycle, log_cap);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+int orthrus_philox4x32_10(const uint32_t* counter_key, int64_t n, uint32_t* out, void* stream) {
+  ORTHRUS_CHECK_ARG(counter_key && out && n >= 0);
+  if (n == 0) return ORTHRUS_OK;
+  philox_kernel<<<static_cast<unsigned>(ceil_div(n, 128)), 128, 0, as_stream(stream)>>>(counter_key, n, out);
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
 }

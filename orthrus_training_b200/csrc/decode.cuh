@@ -95,28 +95,20 @@ __device__ __forceinline__ bool is_eos(int64_t tok, const int64_t* eos, int n_eo
   return false;
 }
 
-// One thread per sequence: greedy longest-prefix accept, bonus token, cache rollback, EOS and
-// max-length handling (decoding._verify + _advance, orthrus/decoding.py:336-369).
-__global__ void decode_accept_kernel(int64_t B, int K, const int64_t* __restrict__ verify_ids,
-                                     const int64_t* __restrict__ ar, const int64_t* __restrict__ eos, int n_eos,
-                                     const int32_t* __restrict__ max_len, int32_t* __restrict__ start,
-                                     int64_t* __restrict__ anchor, uint8_t* __restrict__ done,
-                                     int64_t* __restrict__ out_tokens, int32_t* __restrict__ out_len,
-                                     int64_t out_cap, int32_t* __restrict__ accepted_log, int32_t* __restrict__ cycle,
-                                     int64_t log_cap) {
-  const int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (b >= B || done[b]) return;
+// The end of a cycle of sequence b once its accepted drafts and bonus token are known: log the
+// accepted count, append the kept drafts and the bonus token, stop at EOS or the length limit,
+// and roll the cache back by writing the committed length (decoding._advance,
+// orthrus/decoding.py:354-369).
+__device__ inline void commit_cycle(int64_t b, int K, int accepted, int64_t bonus,
+                                    const int64_t* __restrict__ verify_ids, const int64_t* __restrict__ eos,
+                                    int n_eos, const int32_t* __restrict__ max_len, int32_t* __restrict__ start,
+                                    int64_t* __restrict__ anchor, uint8_t* __restrict__ done,
+                                    int64_t* __restrict__ out_tokens, int32_t* __restrict__ out_len, int64_t out_cap,
+                                    int32_t* __restrict__ accepted_log, int32_t* __restrict__ cycle,
+                                    int64_t log_cap) {
   const int st = start[b];
   const int ml = max_len[b];
-  const int block_len = min(K, ml - st);
   const int64_t* drafts = verify_ids + b * K + 1;
-  const int64_t* pred = ar + b * K;
-  int accepted = 0;
-  while (accepted < block_len - 1 && drafts[accepted] == pred[accepted]) {
-    ++accepted;
-    if (is_eos(drafts[accepted - 1], eos, n_eos)) break;
-  }
-  const int64_t bonus = pred[accepted];
   const int c = cycle[b];
   if (c < log_cap) accepted_log[b * log_cap + c] = accepted;
   cycle[b] = c + 1;
@@ -143,6 +135,29 @@ __global__ void decode_accept_kernel(int64_t B, int K, const int64_t* __restrict
   start[b] = ns;
   anchor[b] = bonus;
   if (fin || ns >= ml - 1) done[b] = 1;
+}
+
+// One thread per sequence: greedy longest-prefix accept (stopping after an accepted EOS) and the
+// AR token after it as the bonus (decoding._verify, orthrus/decoding.py:336-353), then the commit.
+__global__ void decode_accept_kernel(int64_t B, int K, const int64_t* __restrict__ verify_ids,
+                                     const int64_t* __restrict__ ar, const int64_t* __restrict__ eos, int n_eos,
+                                     const int32_t* __restrict__ max_len, int32_t* __restrict__ start,
+                                     int64_t* __restrict__ anchor, uint8_t* __restrict__ done,
+                                     int64_t* __restrict__ out_tokens, int32_t* __restrict__ out_len,
+                                     int64_t out_cap, int32_t* __restrict__ accepted_log, int32_t* __restrict__ cycle,
+                                     int64_t log_cap) {
+  const int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (b >= B || done[b]) return;
+  const int block_len = min(K, max_len[b] - start[b]);
+  const int64_t* drafts = verify_ids + b * K + 1;
+  const int64_t* pred = ar + b * K;
+  int accepted = 0;
+  while (accepted < block_len - 1 && drafts[accepted] == pred[accepted]) {
+    ++accepted;
+    if (is_eos(drafts[accepted - 1], eos, n_eos)) break;
+  }
+  commit_cycle(b, K, accepted, pred[accepted], verify_ids, eos, n_eos, max_len, start, anchor, done, out_tokens,
+               out_len, out_cap, accepted_log, cycle, log_cap);
 }
 
 }  // namespace orthrus

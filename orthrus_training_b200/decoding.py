@@ -574,7 +574,7 @@ class BlockDecodeResult:
 class _DecodeState:
     """Static device buffers of a batched decode (fixed shapes, so one cycle can be graph-captured)."""
 
-    def __init__(self, model, prompts, max_new_tokens, eos, draft_table):
+    def __init__(self, model, prompts, max_new_tokens, eos, draft_table, sampler=None):
         cfg = model.config
         dev = next(model.parameters()).device
         dtype = next(model.parameters()).dtype
@@ -600,6 +600,13 @@ class _DecodeState:
         self.block_ids = torch.full((B, self.K), cfg.mask_token_id, dtype=torch.int64, device=dev)
         self.arange = torch.arange(self.K, device=dev, dtype=torch.int64)
         self.draft_table = draft_table  # [B, rows, K-1] int64 or None (scripted drafts)
+        # sampled decoding: the draft distributions q of the cycle's drafts, over their candidates
+        self.sampler = sampler
+        if sampler is not None:
+            if draft_table is not None:
+                raise ValueError("scripted drafts have no draft distribution to sample against")
+            C = sampler.candidates(cfg.vocab_size)
+            self.draft_probs = torch.zeros(B, self.K - 1, C, dtype=torch.float32, device=dev)
 
     def cycle_once(self):
         """One draft + verify + accept cycle on the current stream (no host synchronisation)."""
@@ -612,7 +619,12 @@ class _DecodeState:
             hidden = model.run_layers(x, positions, "draft", kv=self.kv, offsets=self.start,
                                       limit2=limit2)
             logits = model.lm_logits(hidden)
-            ops.decode_draft(logits, self.anchor, self.done, self.verify_ids)
+            if self.sampler is None:
+                ops.decode_draft(logits, self.anchor, self.done, self.verify_ids)
+            else:
+                draft_vals, draft_ids = ops.sample_candidates(logits[:, : K - 1], self.sampler)
+                ops.decode_sample_draft(draft_vals, draft_ids, self.sampler, self.cycle, self.anchor,
+                                        self.done, self.verify_ids, self.draft_probs)
         else:
             row = (self.start - self.prompt_len).clamp(0, self.draft_table.shape[1] - 1).to(torch.int64)
             drafts = self.draft_table[torch.arange(B, device=self.dev), row]
@@ -621,25 +633,34 @@ class _DecodeState:
         x = model.model.embed_tokens(self.verify_ids)
         hidden = model.run_layers(x, positions, "ar", kv=self.kv, offsets=self.start)
         logits = model.lm_logits(hidden)
-        ops.decode_verify_accept(logits, self.verify_ids, self.ar_tokens, self.eos, self.max_len,
-                                 self.start, self.anchor, self.done, self.out, self.out_len, self.log,
-                                 self.cycle)
+        if self.sampler is None:
+            ops.decode_verify_accept(logits, self.verify_ids, self.ar_tokens, self.eos, self.max_len,
+                                     self.start, self.anchor, self.done, self.out, self.out_len,
+                                     self.log, self.cycle)
+        else:
+            vals, ids = ops.sample_candidates(logits, self.sampler)
+            ops.decode_sample_accept(vals, ids, self.draft_probs, draft_ids, self.sampler,
+                                     self.verify_ids, self.eos, self.max_len, self.start, self.anchor,
+                                     self.done, self.out, self.out_len, self.log, self.cycle)
 
 
 @torch.inference_mode()
 def block_decode(model, prompts: list[list[int]], max_new_tokens: int, eos=(), *, draft_table=None,
-                 use_graph: bool = True, check_every: int = 4) -> BlockDecodeResult:
-    """Greedy Orthrus decoding of a batch of prompts with the cycle state on the device.
+                 use_graph: bool = True, check_every: int = 4,
+                 sampler: ops.SamplingParams | None = None) -> BlockDecodeResult:
+    """Orthrus decoding of a batch of prompts with the cycle state on the device: greedy, or with
+    `sampler` exact rejection sampling of the drafts (orthrus/modeling_orthrus.py:498-511).
 
     draft_table: optional int64 [B, max_new_tokens, K-1]; row i replaces the diffusion drafts of
     the block anchored at prompt_len + i (scripted drafts that exercise accept / rollback, the
     device counterpart of the reference tests' ScriptedBackend)."""
     eos = set(eos)
-    st = _DecodeState(model, prompts, max_new_tokens, eos, draft_table)
+    st = _DecodeState(model, prompts, max_new_tokens, eos, draft_table, sampler)
     B, dev = st.B, st.dev
     torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
     # prefill each prompt into its slice of the batched cache
+    firsts = []
     for b, p in enumerate(prompts):
         ids = torch.tensor([p], device=dev)
         x = model.model.embed_tokens(ids)
@@ -647,9 +668,18 @@ def block_decode(model, prompts: list[list[int]], max_new_tokens: int, eos=(), *
         kv_b = [(k[b: b + 1], v[b: b + 1]) for k, v in st.kv]
         zero = torch.zeros(1, dtype=torch.int32, device=dev)
         hidden = model.run_layers(x, pos, "ar", kv=kv_b, offsets=zero)
-        tok = ops.argmax_rows(model.lm_logits(hidden[:, -1:]).reshape(1, -1))
-        st.anchor[b] = tok[0]
-        st.out[b, 0] = tok[0]
+        last = model.lm_logits(hidden[:, -1:]).reshape(1, -1)
+        if sampler is None:
+            tok = ops.argmax_rows(last)
+            st.anchor[b] = tok[0]
+            st.out[b, 0] = tok[0]
+        else:
+            firsts.append(last)
+    if sampler is not None:  # one draw per sequence, counted by its index
+        vals, ids = ops.sample_candidates(torch.cat(firsts), sampler)
+        tok = ops.sample_rows(vals, ids, sampler)
+        st.anchor.copy_(tok)
+        st.out[:, 0] = tok
     st.out_len.fill_(1)
     if st.eos is not None:
         st.done |= torch.isin(st.anchor, st.eos).to(torch.uint8)

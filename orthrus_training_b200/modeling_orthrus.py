@@ -679,16 +679,21 @@ class OrthrusLM(nn.Module):
     def diffusion_generate(self, input_ids, max_new_tokens, temperature=0.0, top_k=20, top_p=0.8,
                            eos_token_id=None, streamer=None):
         """Project K tokens in parallel, verify them with the AR view, keep the agreed prefix
-        (orthrus/modeling_orthrus.py:404-534), greedy, with the cycle state on the device.
-        Batch size 1 here, as the reference; decoding.block_decode takes batches."""
+        (orthrus/modeling_orthrus.py:404-534) with the cycle state on the device, greedy by default.
+        Batch size 1 here, as the reference; decoding.block_decode takes batches. With a temperature
+        (>= 1e-5) the drafts and the AR view are sampled through the reference's top-k / top-p
+        filter and the drafts kept by exact rejection sampling (:437-449,498-511); the draws come
+        from a Philox seed taken from torch's default generator, so torch.manual_seed fixes them."""
         if input_ids.shape[0] != 1:
             raise ValueError("diffusion_generate supports batch size 1")
-        if temperature >= 1e-5:
-            raise ValueError("only greedy decoding (temperature 0) runs on the device path")
         from orthrus_training_b200.decoding import block_decode
 
+        sampler = None
+        if temperature >= 1e-5:
+            seed = int(torch.randint(0, 2 ** 62, (1,)).item())
+            sampler = ops.SamplingParams(float(temperature), int(top_k), float(top_p), seed)
         eos = {eos_token_id} if isinstance(eos_token_id, int) else set(eos_token_id or ())
-        result = block_decode(self, [input_ids[0].tolist()], max_new_tokens, eos)
+        result = block_decode(self, [input_ids[0].tolist()], max_new_tokens, eos, sampler=sampler)
         tokens = result.tokens[0]
         out = torch.tensor([input_ids[0].tolist() + tokens], device=input_ids.device)
         stats = GenerationStats(new_tokens=len(tokens), accepted=result.accepted[0])

@@ -4,6 +4,7 @@ pointers and the current stream, check the status. No computation happens in Pyt
 from __future__ import annotations
 
 from collections import defaultdict
+from dataclasses import dataclass
 
 import torch
 
@@ -532,6 +533,98 @@ def decode_verify_accept(logits, verify_ids, ar_tokens, eos, max_len, start, anc
         done.data_ptr(), out_tokens.data_ptr(), out_len.data_ptr(), out_tokens.shape[1],
         accepted_log.data_ptr(), cycle.data_ptr(), accepted_log.shape[1],
         L.stream_of(logits.device)), "decode_verify_accept")
+
+
+# --- sampled decoding ---------------------------------------------------------------------------
+
+SAMPLE_MAX_TOP_K = 112  # top_k of the device sampler (candidates: top_k + 16 spares, at most 128)
+
+
+@dataclass(frozen=True)
+class SamplingParams:
+    """The sampling knobs of diffusion_generate (orthrus/modeling_orthrus.py:405-449) and the seed
+    of the decode's Philox draws."""
+
+    temperature: float
+    top_k: int = 20
+    top_p: float = 0.8
+    seed: int = 0
+
+    def candidates(self, vocab: int) -> int:
+        """C: the top-k candidates kept per row, plus spares for ties at the k-th value."""
+        if not self.temperature > 0:
+            raise ValueError("sampling needs a temperature > 0")
+        if not 1 <= self.top_k <= SAMPLE_MAX_TOP_K:
+            raise ValueError(f"the device sampler takes 1 <= top_k <= {SAMPLE_MAX_TOP_K} (got {self.top_k})")
+        if not 0 < self.top_p <= 1:
+            raise ValueError("top_p must be in (0, 1]")
+        k = min(self.top_k, vocab)
+        return min(k + 16, vocab, 128)
+
+
+
+def sample_candidates(logits: torch.Tensor, params: SamplingParams):
+    """(values fp32 [..., C] descending, ids int64 [..., C]): each row's top C logits."""
+    _require_cuda(logits)
+    C = params.candidates(logits.shape[-1])
+    vals, ids = torch.topk(logits.float(), C, dim=-1, sorted=True)
+    return vals.contiguous(), ids.contiguous()
+
+
+def sample_probs(vals: torch.Tensor, params: SamplingParams) -> torch.Tensor:
+    """The filtered distribution [..., C] of candidate rows (the reference's `pick` filter)."""
+    _require_cuda(vals)
+    C = vals.shape[-1]
+    v = vals.reshape(-1, C).contiguous()
+    out = torch.empty_like(v)
+    L.check(L.lib().orthrus_sample_probs(v.data_ptr(), v.shape[0], C, float(params.temperature),
+                                         min(params.top_k, C), float(params.top_p),
+                                         out.data_ptr(), L.stream_of(v.device)), "sample_probs")
+    return out.view_as(vals)
+
+
+def sample_rows(vals: torch.Tensor, ids: torch.Tensor, params: SamplingParams, cycle=None) -> torch.Tensor:
+    """One token per candidate row [R, C] (draw (r, cycle[r] or 0, 0, first))."""
+    _require_cuda(vals, ids, cycle)
+    R, C = vals.shape
+    out = torch.empty(R, dtype=torch.int64, device=vals.device)
+    L.check(L.lib().orthrus_sample_rows(vals.data_ptr(), ids.data_ptr(), R, C, float(params.temperature),
+                                        min(params.top_k, C), float(params.top_p), params.seed & (2 ** 64 - 1),
+                                        L.ptr(cycle), out.data_ptr(), L.stream_of(vals.device)), "sample_rows")
+    return out
+
+
+def decode_sample_draft(vals, ids, params: SamplingParams, cycle, anchor, done, verify_ids, draft_probs):
+    """Drafts of a sampled cycle from the diffusion pass's candidate rows [B, K-1, C]."""
+    B, K1, C = vals.shape
+    L.check(L.lib().orthrus_decode_sample_draft(
+        vals.data_ptr(), ids.data_ptr(), B, K1 + 1, C, float(params.temperature), min(params.top_k, C),
+        float(params.top_p), params.seed & (2 ** 64 - 1), cycle.data_ptr(), anchor.data_ptr(), done.data_ptr(),
+        verify_ids.data_ptr(), draft_probs.data_ptr(), L.stream_of(vals.device)), "decode_sample_draft")
+
+
+def decode_sample_accept(vals, ids, draft_probs, draft_ids, params: SamplingParams, verify_ids, eos, max_len,
+                         start, anchor, done, out_tokens, out_len, accepted_log, cycle):
+    """Rejection-sampling accept of a sampled cycle from the verify pass's candidate rows [B, K, C]."""
+    B, K, C = vals.shape
+    L.check(L.lib().orthrus_decode_sample_accept(
+        vals.data_ptr(), ids.data_ptr(), draft_probs.data_ptr(), draft_ids.data_ptr(), B, K, C,
+        float(params.temperature), min(params.top_k, C), float(params.top_p), params.seed & (2 ** 64 - 1),
+        verify_ids.data_ptr(), L.ptr(eos), 0 if eos is None else eos.numel(), max_len.data_ptr(),
+        start.data_ptr(), anchor.data_ptr(), done.data_ptr(), out_tokens.data_ptr(), out_len.data_ptr(),
+        out_tokens.shape[1], accepted_log.data_ptr(), cycle.data_ptr(), accepted_log.shape[1],
+        L.stream_of(vals.device)), "decode_sample_accept")
+
+
+def philox4x32_10(counter_key: torch.Tensor) -> torch.Tensor:
+    """Philox4x32-10 of int32 [n, 6] (counter words 0-3, key words 0-1, as 32-bit patterns) ->
+    int32 [n, 4] bit patterns, on the device of the input."""
+    _require_cuda(counter_key)
+    ck = counter_key.to(torch.int32).contiguous()
+    out = torch.empty(ck.shape[0], 4, dtype=torch.int32, device=ck.device)
+    L.check(L.lib().orthrus_philox4x32_10(ck.data_ptr(), ck.shape[0], out.data_ptr(), L.stream_of(ck.device)),
+            "philox4x32_10")
+    return out
 
 
 # --- row-local elementwise pieces ---------------------------------------------------------------

@@ -4,6 +4,7 @@ Run in a container that has the reference checked out (it is pure Python):
 
     python tests/golden/make_golden.py <reference checkout>          # every fixture
     python tests/golden/make_golden.py <reference checkout> data     # data_batches.pt only
+    python tests/golden/make_golden.py <reference checkout> sampling # sampling.pt only
 
 It imports the reference's own modules (orthrus.modeling_orthrus, orthrus.objective,
 orthrus.decoding, orthrus.evaluate) and stores seeded inputs together with the reference outputs,
@@ -380,6 +381,89 @@ def config1_decode(mo, ev) -> dict:
     return {"config": config_dict(model), "params": sd, "cases": cases}
 
 
+class _FakeLogits:
+    """Stands in for OrthrusLM.forward inside the reference's diffusion_generate: returns fixed
+    logits per call kind (prefill, diffusion draft, verify) and stops the run at the second draft,
+    so exactly one sampled cycle runs through the reference's own code."""
+
+    class Stop(Exception):
+        pass
+
+    def __init__(self, config, prefill, draft, verify):
+        self.config = config
+        self.logits = {"prefill": prefill, "draft": draft, "verify": verify}
+        self.drafts = 0
+
+    def __call__(self, input_ids=None, is_diffusion_pass=False, **kwargs):
+        from types import SimpleNamespace
+
+        if is_diffusion_pass:
+            self.drafts += 1
+            if self.drafts > 1:
+                raise self.Stop()
+            return SimpleNamespace(logits=self.logits["draft"][None, : input_ids.shape[1]])
+        kind = "prefill" if kwargs.get("position_ids") is None else "verify"
+        return SimpleNamespace(logits=self.logits[kind][None, : input_ids.shape[1]])
+
+
+def sampling_cases(mo) -> dict:
+    """The reference's sampled decoding (orthrus/modeling_orthrus.py:437-449,498-511) on fixed
+    logits: the distributions `pick` hands to torch.multinomial, the uniforms of the rejection
+    test, the accepted count and the bonus token's distribution of one cycle."""
+    from transformers import Qwen3Config
+
+    V, K, P = 96, 8, 5
+    cfg = Qwen3Config(vocab_size=V, hidden_size=64, intermediate_size=128, num_hidden_layers=1,
+                      num_attention_heads=2, num_key_value_heads=1, head_dim=32)
+    cfg.block_size, cfg.mask_token_id = K, V - 1
+    cases = []
+    settings = [(0.7, 20, 0.8), (1.0, 5, 1.0), (1.3, 12, 0.9), (0.5, 40, 0.95), (0.9, 1, 0.8)]
+    for n, (temperature, top_k, top_p) in enumerate(settings * 3):
+        g = torch.Generator().manual_seed(1000 + n)
+        base = torch.randn(K, V, generator=g) * 2
+        prefill = torch.randn(P, V, generator=g) * 2
+        draft = base + torch.randn(K, V, generator=g) * (0.3 + 0.3 * (n % 3))
+        verify = base + torch.randn(K, V, generator=g) * 0.3
+        if n % 5 == 4:  # integer logits: ties at the top_k-th value
+            draft, verify = draft.round(), verify.round()
+        multinomial, rand, stats = [], [], []
+        orig_multinomial, orig_rand, orig_stats = torch.multinomial, torch.rand, mo.GenerationStats
+
+        def rec_multinomial(probs, num, *a, **k):
+            out = orig_multinomial(probs, num, *a, **k)
+            multinomial.append((probs.clone(), out.clone()))
+            return out
+
+        def rec_rand(*a, **k):
+            out = orig_rand(*a, **k)
+            rand.append(float(out))
+            return out
+
+        class RecStats(orig_stats):
+            def __init__(self, *a, **k):
+                super().__init__(*a, **k)
+                stats.append(self)
+
+        torch.manual_seed(77 + n)
+        torch.multinomial, torch.rand, mo.GenerationStats = rec_multinomial, rec_rand, RecStats
+        try:
+            fake = _FakeLogits(cfg, prefill, draft, verify)
+            mo.OrthrusLM.diffusion_generate(fake, torch.zeros(1, P, dtype=torch.long), 64,
+                                            temperature=temperature, top_k=top_k, top_p=top_p)
+        except _FakeLogits.Stop:
+            pass
+        finally:
+            torch.multinomial, torch.rand, mo.GenerationStats = orig_multinomial, orig_rand, orig_stats
+        (_, _), (q, d), (p, _), (target, _) = multinomial[:4]
+        cases.append({"temperature": temperature, "top_k": top_k, "top_p": top_p,
+                      "prefill_last": prefill[-1].clone(), "draft_logits": draft[: K - 1].clone(),
+                      "verify_logits": verify.clone(), "first_probs": multinomial[0][0].clone(),
+                      "draft_probs": q.view(K - 1, V).clone(), "draft_tokens": d.view(-1).clone(),
+                      "ar_probs": p.view(K, V).clone(), "uniforms": rand, "accepted": stats[0].accepted[0],
+                      "target": target.clone()})
+    return {"vocab": V, "block_size": K, "cases": cases}
+
+
 def data_batches(data) -> dict:
     """The reference's micro-batch order (orthrus/data.py:89-103) for a few (seed, epoch, start)."""
     import numpy as np
@@ -406,12 +490,16 @@ def main(reference: str, only: str | None = None) -> None:
 
     torch.set_num_threads(4)
     meta = _versions()
+    if only == "sampling":
+        torch.save({"meta": meta, **sampling_cases(mo)}, HERE / "sampling.pt")
+        return
     torch.save({"meta": meta, **data_batches(data)}, HERE / "data_batches.pt")
     if only == "data":
         return
     torch.save({"meta": meta, **strategy_cases(mo, dec)}, HERE / "tiny_strategies.pt")
     if only == "strategies":
         return
+    torch.save({"meta": meta, **sampling_cases(mo)}, HERE / "sampling.pt")
     torch.save({"meta": meta, **kl_kat(ob)}, HERE / "kl_kat.pt")
     torch.save({"meta": meta, **mask_kat(mo)}, HERE / "mask_kat.pt")
     torch.save({"meta": meta, **config1(mo, ob)}, HERE / "config1.pt")

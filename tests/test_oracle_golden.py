@@ -100,3 +100,20 @@ def test_config1_decode():
                                              c["max_new"])
         assert out[0, len(c["prompt"]):].tolist() == c["diffusion"] == c["ar"]
         assert accepted == c["accepted"]
+
+
+def test_sampling_filter_and_rejection_rule():
+    """sampling_probs and rejection_accept against the reference's own sampled cycle (the
+    distributions its `pick` handed to torch.multinomial, its uniforms, accepted count and bonus
+    distribution; tests/golden/sampling.pt)."""
+    g = load_golden("sampling.pt")
+    for c in g["cases"]:
+        knobs = (c["temperature"], c["top_k"], c["top_p"])
+        assert torch.equal(O.sampling_probs(c["prefill_last"][None], *knobs), c["first_probs"])
+        assert torch.equal(O.sampling_probs(c["draft_logits"], *knobs), c["draft_probs"])
+        assert torch.equal(O.sampling_probs(c["verify_logits"], *knobs), c["ar_probs"])
+        n = c["draft_tokens"].numel()
+        uniforms = torch.tensor(c["uniforms"] + [1.0] * (n - len(c["uniforms"])))
+        accepted, target = O.rejection_accept(c["draft_tokens"], c["draft_probs"], c["ar_probs"], uniforms)
+        assert accepted == c["accepted"]
+        assert torch.equal(target, c["target"])
