@@ -261,6 +261,23 @@ int orthrus_attn_fwd(const void* q, const void* k1, const void* v1, int64_t s1h,
                      int mask, const int64_t* anchors, int64_t A, int block, const int32_t* offset,
                      const int32_t* limit2, void* o, float* lse, int dtype, void* stream);
 
+/* The attention of the decode passes, bf16 with hd = D = 128: a block of Tq <= 64 query rows per
+ * sequence ((Hq / Hkv) * Tq <= 128) over its KV cache, with the CAUSAL mask (verification and
+ * one-token greedy passes: row t of sequence b sees cache rows [0, offset[b] + t]) or the DRAFT
+ * mask (the cache rows [0, offset[b]) plus the block's own keys k2 / v2 [0, limit2[b]), L2 <= 64).
+ * Same arguments and output as orthrus_attn_fwd (no lse). The keys are split into 128-key ranges
+ * from key 0, one CTA per (range, KV head, sequence), merged per row in range order: a row's
+ * result depends on its visible keys only, so a Tq-row pass equals Tq one-row passes bit for bit.
+ * workspace: orthrus_attn_decode_workspace_bytes(B, Hq, Tq, L1) (per-range partial states).
+ * Replaces the generation-time attention of OrthrusAttention (orthrus/modeling_orthrus.py:167-188)
+ * in diffusion_generate's draft and verify passes (:469-497). */
+size_t orthrus_attn_decode_workspace_bytes(int64_t B, int Hq, int64_t Tq, int64_t L1);
+int orthrus_attn_decode_fwd(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b,
+                            int64_t L1, const void* k2, const void* v2, int64_t s2h, int64_t s2b,
+                            int64_t L2, int64_t B, int Hq, int Hkv, int64_t Tq, float scale, int mask,
+                            const int32_t* offset, const int32_t* limit2, void* o, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* Backward of the DUAL mask (training): from do_ [B, Tq, Hq, hd] (token-major), o, lse, q and the
  * two sources, writes dq [B, Hq, Tq, D] fp32 and dk2 / dv2 [B, Hkv, L2, D] fp32 (source-2 keys
  * only: source-1 keys are the frozen teacher's and get no gradient).

@@ -65,6 +65,10 @@ _SIGNATURES = {
                                      c_int64, c_int64, c_int, c_int, c_int64, c_int, c_int, c_float, _P,
                                      c_int64, c_int, _P, _P, _P, _P, _P, _P, _P, _P, c_size_t, c_int, _P]),
     "orthrus_attn_bwd_workspace_bytes": (c_size_t, [c_int64, c_int, c_int64]),
+    "orthrus_attn_decode_workspace_bytes": (c_size_t, [c_int64, c_int, c_int64, c_int64]),
+    "orthrus_attn_decode_fwd": (c_int, [_P, _P, _P, c_int64, c_int64, c_int64, _P, _P, c_int64, c_int64,
+                                        c_int64, c_int64, c_int, c_int, c_int64, c_float, c_int, _P, _P, _P,
+                                        _P, c_size_t, _P]),
     "orthrus_attn_bwd": (c_int, [_P, _P, _P, c_int64, c_int64, c_int64, _P, _P, c_int64, c_int64,
                                  c_int64, c_int64, c_int, c_int, c_int64, c_int, c_int, c_float, _P,
                                  c_int64, c_int, _P, _P, _P, _P, _P, _P, _P, c_size_t, c_int, _P]),

@@ -9,6 +9,7 @@
 #include "attention_simt.cuh"
 #include "attention_tc.cuh"
 #include "attention_blockkv.cuh"
+#include "attention_decode.cuh"
 #include "decode.cuh"
 #include "sampling.cuh"
 #include "gemm_simt.cuh"
@@ -354,6 +355,49 @@ static int attn_fwd_impl(const void* q, const void* k1, const void* v1, int64_t 
   } else {
     return ORTHRUS_EINVAL;
   }
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+size_t orthrus_attn_decode_workspace_bytes(int64_t B, int Hq, int64_t Tq, int64_t L1) {
+  if (B <= 0 || Hq <= 0 || Tq <= 0 || L1 < 0) return 0;
+  const size_t rows = static_cast<size_t>(decode_splits1(L1) + 1) * B * Hq * Tq;
+  return rows * 128 * sizeof(float) + rows * 2 * sizeof(float);
+}
+
+int orthrus_attn_decode_fwd(const void* q, const void* k1, const void* v1, int64_t s1h, int64_t s1b, int64_t L1,
+                            const void* k2, const void* v2, int64_t s2h, int64_t s2b, int64_t L2, int64_t B, int Hq,
+                            int Hkv, int64_t Tq, float scale, int mask, const int32_t* offset, const int32_t* limit2,
+                            void* o, void* workspace, size_t workspace_bytes, void* stream) {
+  ORTHRUS_CHECK_ARG(q && k1 && v1 && o && workspace && B > 0 && B < 65536 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0);
+  ORTHRUS_CHECK_ARG(Tq > 0 && Tq <= kDecSub && (Hq / Hkv) * Tq <= kDecMaxRows && L1 > 0 && Hkv < 65536);
+  ORTHRUS_CHECK_ARG(mask == ORTHRUS_MASK_CAUSAL || (mask == ORTHRUS_MASK_DRAFT && k2 && v2 && L2 > 0 && L2 <= kDecSub));
+  ORTHRUS_CHECK_ARG(workspace_bytes >= orthrus_attn_decode_workspace_bytes(B, Hq, Tq, L1));
+  ORTHRUS_CHECK_ARG(aligned16(q) && aligned16(k1) && aligned16(v1) && aligned16(o) && aligned16(workspace));
+  ORTHRUS_CHECK_ARG(s1h % 8 == 0 && s1b % 8 == 0 && (mask == ORTHRUS_MASK_CAUSAL || (s2h % 8 == 0 && s2b % 8 == 0)));
+  const bool has2 = mask == ORTHRUS_MASK_DRAFT;
+  MaskParams mp{mask, nullptr, 0, 0, offset, limit2, L1, has2 ? L2 : 0};
+  const int ns1 = static_cast<int>(decode_splits1(L1));
+  const size_t rows = static_cast<size_t>(ns1 + 1) * B * Hq * Tq;
+  float* part_o = static_cast<float*>(workspace);
+  float* part_ml = part_o + rows * 128;
+  cudaStream_t st = as_stream(stream);
+  const int qrows = static_cast<int>(ceil_div((Hq / Hkv) * Tq, 16)) * 16;
+  const int smem = decode_smem_bytes(qrows);
+  if (set_smem(attn_decode_split_kernel, smem)) return ORTHRUS_ECUDA;
+  const dim3 grid(static_cast<unsigned>(ns1 + (has2 ? 1 : 0)), static_cast<unsigned>(Hkv), static_cast<unsigned>(B));
+  const auto* K2 = static_cast<const __nv_bfloat16*>(has2 ? k2 : k1);
+  const auto* V2 = static_cast<const __nv_bfloat16*>(has2 ? v2 : v1);
+  ORTHRUS_CHECK_CUDA(launch_pdl(attn_decode_split_kernel, grid, dim3(2 * qrows), smem, st,
+                                static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k1),
+                                static_cast<const __nv_bfloat16*>(v1), s1h, s1b, K2, V2, has2 ? s2h : s1h,
+                                has2 ? s2b : s1b, Hq, Hkv, static_cast<int>(Tq), scale * kLog2e, mp, ns1, part_o,
+                                part_ml));
+  ORTHRUS_CHECK_LAUNCH();
+  const int64_t items = B * Hq * Tq;
+  ORTHRUS_CHECK_CUDA(launch_pdl(attn_decode_combine_kernel, dim3(static_cast<unsigned>(ceil_div(items, 8))), dim3(256),
+                                0, st, static_cast<const float*>(part_o), static_cast<const float*>(part_ml), B, Hq,
+                                static_cast<int>(Tq), ns1, mp, static_cast<__nv_bfloat16*>(o)));
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
 }

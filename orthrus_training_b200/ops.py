@@ -413,7 +413,15 @@ def attention_fwd(q, k1, v1, k2=None, v2=None, *, mask: int, hd: int, scale: flo
     if anchors is not None:
         anchors = anchors.to(torch.int64).contiguous()
     t0 = TIMER.begin() if TIMER is not None else None
-    if doc_start is None:
+    if (not want_lse and doc_start is None and anchors is None and offset is not None
+            and _decode_attention_ok(q, mask, hd, D, Tq, Hq, Hkv, k2, L2)):
+        ws = torch.empty(int(L.lib().orthrus_attn_decode_workspace_bytes(B, Hq, Tq, L1)), dtype=torch.uint8,
+                         device=q.device)
+        L.check(L.lib().orthrus_attn_decode_fwd(
+            q.data_ptr(), k1.data_ptr(), v1.data_ptr(), s1h, s1b, L1, L.ptr(k2), L.ptr(v2), s2h, s2b, L2, B, Hq,
+            Hkv, Tq, float(scale), mask, offset.data_ptr(), L.ptr(limit2), o.data_ptr(), ws.data_ptr(), ws.numel(),
+            L.stream_of(q.device)), "attn_decode_fwd")
+    elif doc_start is None:
         L.check(L.lib().orthrus_attn_fwd(
             q.data_ptr(), k1.data_ptr(), v1.data_ptr(), s1h, s1b, L1, L.ptr(k2), L.ptr(v2), s2h, s2b,
             L2, B, Hq, Hkv, Tq, hd, D, float(scale), mask, L.ptr(anchors), A, block, L.ptr(offset),
@@ -430,6 +438,13 @@ def attention_fwd(q, k1, v1, k2=None, v2=None, *, mask: int, hd: int, scale: flo
         TIMER.end(f"attn_fwd_{('causal', 'dual', 'draft', 'tree')[mask]}", t0,
                   attention_flops(mask, B, Hq, Tq, hd, anchors, block, L1))
     return o, lse
+
+
+def _decode_attention_ok(q, mask, hd, D, Tq, Hq, Hkv, k2, L2) -> bool:
+    """The decode passes' split-key kernel takes bf16 blocks of at most 64 rows per sequence with
+    hd = 128, causal over a cache (with offsets) or the draft mask."""
+    return (q.dtype == torch.bfloat16 and hd == 128 and D == 128 and Tq <= 64 and (Hq // Hkv) * Tq <= 128
+            and (mask == 0 or (mask == 2 and k2 is not None and 0 < L2 <= 64)))
 
 
 def attention_flops(mask, B, Hq, Tq, hd, anchors=None, block=0, L1=0):
