@@ -1030,10 +1030,12 @@ __global__ void __launch_bounds__(320, 1)
     const int h = wg;
     const int64_t t = q0 + row;
     const bool live = t < Tq;
-    int64_t e1 = 0, s2 = 0, e2 = 0;
-    if (live) query_ranges(mp, b, t, e1, s2, e2);
-    const int64_t s1 = live ? source1_start(mp, b, t) : 0;
-    if (!has2) e2 = s2 = 0;
+    int64_t e1l = 0, s2l = 0, e2l = 0;
+    if (live) query_ranges(mp, b, t, e1l, s2l, e2l);
+    // key positions fit 32 bits (sources are < 2^31 rows); narrow them to spare registers for the
+    // 128 scores each row holds
+    const int s1 = live ? static_cast<int>(source1_start(mp, b, t)) : 0;
+    const int e1 = static_cast<int>(e1l), s2 = has2 ? static_cast<int>(s2l) : 0, e2 = has2 ? static_cast<int>(e2l) : 0;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const uint32_t s_col = lane_base + h * 128;
     const uint32_t o_col = lane_base + 256 + h * 128;
@@ -1055,8 +1057,8 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_before();
       mbar_arrive(&s_free[h]);  // the MMA warp may overwrite S with the next tile's scores
       const bool src2 = j >= n1;
-      const int64_t key0 = (src2 ? t2a + (j - n1) : j) * 128;
-      const int64_t lo = (src2 ? s2 : s1) - key0, hi = (src2 ? e2 : e1) - key0;  // visible columns
+      const int key0 = (src2 ? t2a + (j - n1) : j) * 128;
+      const int lo = (src2 ? s2 : s1) - key0, hi = (src2 ? e2 : e1) - key0;  // visible columns
       const bool full = lo <= 0 && hi >= 128;
       // row max of the raw scores (scale > 0 commutes with max), four independent chains
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -1079,24 +1081,27 @@ __global__ void __launch_bounds__(320, 1)
         m_ref = tmax;
       }
       const float mu = m_ref == -INFINITY ? 0.f : m_ref;
-      // P = exp2(s * scale - m_ref) as bf16 pairs in registers, before any wait
-      float sm[4] = {0.f, 0.f, 0.f, 0.f};  // independent chains
-      uint32_t pk[64];
-#pragma unroll
-      for (int i = 0; i < 128; i += 2) {
-        const float p0 = ex2_approx(fmaf(s[i], scale_log2, -mu));
-        const float p1 = ex2_approx(fmaf(s[i + 1], scale_log2, -mu));
-        sm[i & 3] += p0;
-        sm[(i + 1) & 3] += p1;
-        pk[i / 2] = pack_bf16x2(p0, p1);
-      }
       // the previous P V of this head must be done before P and O are touched again
       if (j > 0 && !mbar_wait(&p_empty[h], (j - 1) & 1)) {
         ok = false;
         break;
       }
+      // P = exp2(s * scale - m_ref) as bf16 pairs, stored 32 columns at a time: no packed copy of
+      // the whole row stays live beside the scores (that had spilled registers to local memory)
+      float sm[4] = {0.f, 0.f, 0.f, 0.f};  // independent chains
 #pragma unroll
-      for (int c = 0; c < 4; ++c) store_row32_sw128_packed(p_base, row, c * 32, pk + 16 * c);
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = ex2_approx(fmaf(s[32 * c + i], scale_log2, -mu));
+          const float p1 = ex2_approx(fmaf(s[32 * c + i + 1], scale_log2, -mu));
+          sm[i & 3] += p0;
+          sm[(i + 1) & 3] += p1;
+          pk[i / 2] = pack_bf16x2(p0, p1);
+        }
+        store_row32_sw128_packed(p_base, row, c * 32, pk);
+      }
       l = fmaf(l, alpha, (sm[0] + sm[1]) + (sm[2] + sm[3]));
       // TMEM loads and stores are warp-collective: the whole warp rescales when any of its rows
       // must (rows that need none multiply by exactly 1)
