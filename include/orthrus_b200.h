@@ -394,6 +394,26 @@ int orthrus_decode_verify_accept(const float* logits, int64_t B, int K, int64_t 
                                  int64_t out_cap, int32_t* accepted_log, int32_t* cycle,
                                  int64_t log_cap, void* stream);
 
+/* The LM head's argmax without logits, for greedy decoding: out int64 [R] = argmax over the V
+ * columns of h [R, d] @ weight [V, d]^T (bf16, fp32 accumulation, d % 64 == 0), the lowest index
+ * on ties (torch.argmax). The logits tiles are computed as orthrus_gemm_bf16 computes them and
+ * reduced on chip; nothing of size [R, V] is written. workspace:
+ * orthrus_lmhead_argmax_workspace_bytes(R). Replaces lm_head + argmax of diffusion_generate's
+ * greedy pick (orthrus/modeling_orthrus.py:437-439). */
+size_t orthrus_lmhead_argmax_workspace_bytes(int64_t R);
+int orthrus_lmhead_argmax_bf16(const void* h, int64_t R, const void* weight, int64_t V, int64_t d,
+                               int64_t* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* orthrus_decode_draft and orthrus_decode_verify_accept with the rows' argmax ids [B * K] (from
+ * orthrus_lmhead_argmax_bf16) in place of their logits. */
+int orthrus_decode_draft_ids(const int64_t* ids, int64_t B, int K, const int64_t* anchor,
+                             const uint8_t* done, int64_t* verify_ids, void* stream);
+int orthrus_decode_accept_ids(const int64_t* ar_tokens, int64_t B, int K, const int64_t* verify_ids,
+                              const int64_t* eos, int n_eos, const int32_t* max_len, int32_t* start,
+                              int64_t* anchor, uint8_t* done, int64_t* out_tokens, int32_t* out_len,
+                              int64_t out_cap, int32_t* accepted_log, int32_t* cycle, int64_t log_cap,
+                              void* stream);
+
 /* ---- sampled decoding (temperature > 0) ----
  * A row's sampling distribution lives on its C top candidates: cand_vals fp32 [R, C] sorted
  * descending and cand_ids int64 [R, C] (the logits' top C, e.g. torch.topk), with

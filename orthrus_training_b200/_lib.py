@@ -95,6 +95,11 @@ _SIGNATURES = {
                                              c_float, ctypes.c_uint64, _P, _P, c_int, _P, _P, _P, _P, _P,
                                              _P, c_int64, _P, _P, c_int64, _P]),
     "orthrus_philox4x32_10": (c_int, [_P, c_int64, _P, _P]),
+    "orthrus_lmhead_argmax_workspace_bytes": (c_size_t, [c_int64]),
+    "orthrus_lmhead_argmax_bf16": (c_int, [_P, c_int64, _P, c_int64, c_int64, _P, _P, c_size_t, _P]),
+    "orthrus_decode_draft_ids": (c_int, [_P, c_int64, c_int, _P, _P, _P, _P]),
+    "orthrus_decode_accept_ids": (c_int, [_P, c_int64, c_int, _P, _P, c_int, _P, _P, _P, _P, _P, _P, c_int64,
+                                          _P, _P, c_int64, _P]),
 }
 
 _lib = None

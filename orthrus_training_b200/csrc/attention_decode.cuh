@@ -253,11 +253,13 @@ __global__ void __launch_bounds__(256) attn_decode_combine_kernel(const float* _
   const bool has2 = mp.mode == ORTHRUS_MASK_DRAFT && e2 > s2;
   auto part = [&](int s) { return ((static_cast<int64_t>(s) * B + b) * Hq + hh) * Tq + t; };
   float M = -INFINITY;
+#pragma unroll 4
   for (int s = 0; s < n1; ++s) M = fmaxf(M, part_ml[part(s) * 2]);
   if (has2) M = fmaxf(M, part_ml[part(ns1) * 2]);
   float L = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int k = 0; k < n1 + (has2 ? 1 : 0); ++k) {
+#pragma unroll 4
+  for (int k = 0; k < n1 + (has2 ? 1 : 0); ++k) {  // unrolled so the loads of several splits are in flight
     const int s = k < n1 ? k : ns1;
     const int64_t idx = part(s);
     const float ms = part_ml[idx * 2], ls = part_ml[idx * 2 + 1];

@@ -128,6 +128,37 @@ int orthrus_gemm_simt(const void* A, int64_t lda, const void* B, int64_t ldb, vo
   return ORTHRUS_EINVAL;
 }
 
+size_t orthrus_lmhead_argmax_workspace_bytes(int64_t R) { return R > 0 ? lmhead_argmax_ws_bytes(R) : 0; }
+
+int orthrus_lmhead_argmax_bf16(const void* h, int64_t R, const void* weight, int64_t V, int64_t d, int64_t* out,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  return lmhead_argmax_bf16(static_cast<const __nv_bfloat16*>(h), R, static_cast<const __nv_bfloat16*>(weight), V, d,
+                            out, workspace, workspace_bytes, as_stream(stream));
+}
+
+int orthrus_decode_draft_ids(const int64_t* ids, int64_t B, int K, const int64_t* anchor, const uint8_t* done,
+                             int64_t* verify_ids, void* stream) {
+  ORTHRUS_CHECK_ARG(ids && anchor && verify_ids && B > 0 && K >= 1);
+  decode_draft_ids_kernel<<<static_cast<unsigned>(ceil_div(B * K, 256)), 256, 0, as_stream(stream)>>>(
+      ids, B, K, anchor, done, verify_ids);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
+int orthrus_decode_accept_ids(const int64_t* ar_tokens, int64_t B, int K, const int64_t* verify_ids,
+                              const int64_t* eos, int n_eos, const int32_t* max_len, int32_t* start, int64_t* anchor,
+                              uint8_t* done, int64_t* out_tokens, int32_t* out_len, int64_t out_cap,
+                              int32_t* accepted_log, int32_t* cycle, int64_t log_cap, void* stream) {
+  ORTHRUS_CHECK_ARG(ar_tokens && verify_ids && max_len && start && anchor && done && out_tokens && out_len &&
+                    accepted_log && cycle && B > 0 && K >= 1);
+  ORTHRUS_CHECK_ARG(n_eos == 0 || eos != nullptr);
+  decode_accept_kernel<<<static_cast<unsigned>(ceil_div(B, 128)), 128, 0, as_stream(stream)>>>(
+      B, K, verify_ids, ar_tokens, eos, n_eos, max_len, start, anchor, done, out_tokens, out_len, out_cap,
+      accepted_log, cycle, log_cap);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
 size_t orthrus_lmhead_kl_workspace_bytes(int64_t n, int64_t m, int64_t V, int64_t d, int64_t chunk_rows,
                                          int dtype) {
   return lmhead_plan(n, m, V, d, chunk_rows, dtype).total;

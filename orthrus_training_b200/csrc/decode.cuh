@@ -89,6 +89,18 @@ __global__ void __launch_bounds__(512) decode_draft_kernel(const float* __restri
   }
 }
 
+// The same from the rows' argmax ids [B * K] (the LM head's argmax without logits).
+__global__ void decode_draft_ids_kernel(const int64_t* __restrict__ ids, int64_t B, int K,
+                                        const int64_t* __restrict__ anchor, const uint8_t* __restrict__ done,
+                                        int64_t* __restrict__ verify_ids) {
+  const int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (e >= B * K) return;
+  const int64_t b = e / K;
+  const int i = static_cast<int>(e % K);
+  if (done && done[b]) return;
+  verify_ids[e] = i == 0 ? anchor[b] : ids[b * K + i - 1];
+}
+
 __device__ __forceinline__ bool is_eos(int64_t tok, const int64_t* eos, int n_eos) {
   for (int i = 0; i < n_eos; ++i)
     if (eos[i] == tok) return true;

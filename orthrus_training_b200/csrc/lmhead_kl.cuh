@@ -8,8 +8,9 @@
 //              a combine kernel gives lse and argmax per row.
 //   2. diff    per student row tile: student and gathered-teacher logits of the same vocabulary
 //              tile (two accumulators sharing the W operand), then
-//              kl += p_t (log p_t - log p_s) and diff = w (p_s - p_t) in bf16, staged in shared
-//              memory and written by TMA stores to a chunk buffer [chunk_rows, V];
+//              kl += p_t (log p_t - log p_s) and diff = w (p_s - p_t) in bf16, stored by each
+//              row's thread straight to a chunk buffer [chunk_rows, V] (no staging, so four
+//              operand stages fit in shared memory);
 //   3. grad    grad[chunk] = diff @ W (UMMA with W as the MN-major operand).
 // Finalisation (deterministic, fixed summation order): kl_rows, agree, total and the per-offset
 // KL / agreement sums of orthrus_loss (orthrus/objective.py:440-452).
@@ -248,6 +249,37 @@ __global__ void lmhead_stats_combine_kernel(const float* __restrict__ part_m, co
   amax[r] = idx;
 }
 
+// Greedy decoding's argmax of the logits h @ W^T per row from the pass-1 partials: the first
+// maximal split in split order, and inside a split the first maximal column (the lowest index on
+// ties, as torch.argmax), written as int64. One warp per row: each lane keeps the first maximum of
+// its splits (s = lane, lane + 32, ...), then the warp keeps the larger value or, on a tie, the
+// lower split, which is the first maximal split.
+__global__ void lmhead_argmax_combine_kernel(const float* __restrict__ part_m, const int* __restrict__ part_i, int R,
+                                             int splits, int64_t* __restrict__ out) {
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= R) return;
+  float M = -INFINITY;
+  int S = INT_MAX;
+  for (int s = lane; s < splits; s += 32) {
+    const float m = part_m[static_cast<int64_t>(s) * R + r];
+    if (m > M) {
+      M = m;
+      S = s;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, M, off);
+    const int os = __shfl_xor_sync(0xffffffffu, S, off);
+    if (om > M || (om == M && os < S)) {
+      M = om;
+      S = os;
+    }
+  }
+  if (lane == 0) out[r] = S == INT_MAX ? 0 : part_i[static_cast<int64_t>(S) * R + r];
+}
+
 // ------------------------------------------------------------------------------------------------
 // Pass 2 (bf16, tcgen05): KL and the bf16 probability difference of a student row chunk.
 // ------------------------------------------------------------------------------------------------
@@ -256,16 +288,15 @@ struct DiffTile {
   static constexpr int BM = 128, BN = 128, BK = 64;
   static constexpr int T_BYTES = BM * BK * 2;  // 16 KB per operand tile
   static constexpr int STAGE_BYTES = 3 * T_BYTES;
-  static constexpr int STAGES = 3;
-  static constexpr int OUT_BYTES = BM * BN * 2;  // 32 KB staging per buffer
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 2 * OUT_BYTES + 1024 + 256;
+  static constexpr int STAGES = 4;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
 };
 
 // Rows [c0, c0 + rows) of the student chunk; S rows via tmS (coordinate c0 + ...), gathered
-// teacher rows via tmT (same coordinates), W via tmW, output diff via tmD ([rows, V] chunk buffer).
+// teacher rows via tmT (same coordinates), W via tmW, output diff [rows, V] (pitch ldd elements).
 __global__ void __launch_bounds__(192, 1)
     lmhead_diff_tc_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmT,
-                          const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmD,
+                          const __grid_constant__ CUtensorMap tmW, __nv_bfloat16* __restrict__ diff, int64_t ldd,
                           int rows, int c0, int V, int D, int tiles_per_split, int rtiles, int units,
                           const float* __restrict__ lse_s, const float* __restrict__ lse_t_rows,
                           const float* __restrict__ row_weight, float* __restrict__ kl_part) {
@@ -273,14 +304,11 @@ __global__ void __launch_bounds__(192, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
-  uint8_t* sOut = smem + T::STAGES * T::STAGE_BYTES;  // 2 x [2 boxes x (128 rows x 128 B)]
-  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + 2 * T::OUT_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + T::STAGES * T::STAGE_BYTES);
   uint64_t* empty = full + T::STAGES;
   uint64_t* acc_full = empty + T::STAGES;
   uint64_t* acc_empty = acc_full + 2;
-  uint64_t* staged = acc_empty + 2;  // [2] epilogue rows written to a staging buffer (128 arrivals)
-  uint64_t* freed = staged + 2;      // [2] TMA store finished reading a staging buffer (1 arrival)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(freed + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -303,8 +331,6 @@ __global__ void __launch_bounds__(192, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4);
-      mbar_init(&staged[b], 128);
-      mbar_init(&freed[b], 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -385,7 +411,6 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     const int quarter = warp & 3;
     const int lrow = quarter * 32 + lane;  // row inside the tile (TMEM lane)
-    const bool leader = (threadIdx.x == 64);
     int tt = 0;
     for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
     int rt0, split, t0;
@@ -395,6 +420,7 @@ __global__ void __launch_bounds__(192, 1)
     const float ls_off = live ? lse_s[c0 + crow] : 0.f;
     const float lt_off = live ? lse_t_rows[c0 + crow] : 0.f;
     const float w = (live && row_weight != nullptr) ? row_weight[c0 + crow] : 1.f;
+    __nv_bfloat16* drow = diff + static_cast<int64_t>(live ? crow : 0) * ldd;
     float kl = 0.f;
     for (int t = 0; t < ntiles; ++t, ++tt) {
       const int b = tt & 1;
@@ -403,13 +429,6 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
-      // The staging buffer of this tile was last stored two tiles ago: wait until TMA read it.
-      if (!mbar_wait(&freed[b], ((tt >> 1) & 1) ^ 1)) {
-        *abort_flag = 1;
-        break;
-      }
-      uint8_t* out = sOut + b * T::OUT_BYTES;
-      const uint32_t out_base = smem_u32(out);
       const int v0 = (t0 + t) * T::BN;
       const uint32_t base_s = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + b * 256;
 #pragma unroll 1
@@ -437,35 +456,27 @@ __global__ void __launch_bounds__(192, 1)
           packed[j / 2] = pack_bf16x2(d2[0], d2[1]);
         }
         kl += (klv[0] + klv[1]) + (klv[2] + klv[3]);
-        // chunk c covers bytes [c*64, c*64+64) of this row in a 256-byte row split over two
-        // 128-byte-swizzled boxes of 64 columns each
-        const uint32_t box = out_base + (c >> 1) * (128 * 128);
+        // this row's 32 columns: four 16-byte stores (a 64-byte run of the row), or element by
+        // element at the end of the vocabulary
+        if (live && nvalid == 32) {
+          __nv_bfloat16* dst = drow + col0;
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          st_shared_v4(box + sw128_offset(lrow, (c & 1) * 4 + q), packed[4 * q], packed[4 * q + 1],
-                       packed[4 * q + 2], packed[4 * q + 3]);
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(dst + 8 * q) =
+                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+        } else if (live && nvalid > 0) {
+          __nv_bfloat16* dst = drow + col0;
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (e < nvalid) dst[e] = __ushort_as_bfloat16(static_cast<unsigned short>(packed[e >> 1] >> (16 * (e & 1))));
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
-      fence_proxy_async_smem();
-      mbar_arrive(&staged[b]);
-      if (leader) {
-        if (!mbar_wait(&staged[b], (tt >> 1) & 1)) {
-          *abort_flag = 1;
-          break;
-        }
-        tma_store_2d(&tmD, out, v0, rt0);
-        tma_store_2d(&tmD, out + 128 * 128, v0 + 64, rt0);
-        tma_store_commit();
-        // at most the store just issued may still be reading: the other buffer is free again
-        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-        if (tt >= 1) mbar_arrive(&freed[b ^ 1]);
-      }
     }
     if (live) kl_part[static_cast<int64_t>(split) * rows + crow] = kl;
     }
-    if (leader) tma_store_wait_all();
   }
   __syncthreads();
   if (warp == 1) {
@@ -768,6 +779,43 @@ inline LmheadPlan lmhead_plan(int64_t n, int64_t m, int64_t V, int64_t D, int64_
   return p;
 }
 
+// Row argmax of the logits h [R, D] @ W^T [V, D] (bf16, fp32 accumulation) without writing them:
+// pass 1 over all SMs (the vocabulary split up to kArgmaxMaxSplits ways for a few rows), then the
+// argmax merge. Workspace: three [splits, R] partial arrays.
+constexpr int kArgmaxMaxSplits = 296;
+
+inline size_t lmhead_argmax_ws_bytes(int64_t R) {
+  return 3 * align_up(static_cast<size_t>(kArgmaxMaxSplits) * R * 4, 256);
+}
+
+inline int lmhead_argmax_bf16(const __nv_bfloat16* h, int64_t R, const __nv_bfloat16* W, int64_t V, int64_t D,
+                              int64_t* out, void* ws_raw, size_t ws_bytes, cudaStream_t stream) {
+  ORTHRUS_CHECK_ARG(h && W && out && R >= 1 && V >= 1 && D >= 64 && D % 64 == 0 && R < (1ll << 31) && V < (1ll << 31));
+  ORTHRUS_CHECK_ARG(aligned16(h) && aligned16(W));
+  if (ws_raw == nullptr || ws_bytes < lmhead_argmax_ws_bytes(R)) return ORTHRUS_EWORKSPACE;
+  const size_t part = align_up(static_cast<size_t>(kArgmaxMaxSplits) * R * 4, 256);
+  float* pm = reinterpret_cast<float*>(ws_raw);
+  float* ps = reinterpret_cast<float*>(static_cast<uint8_t*>(ws_raw) + part);
+  int* pi = reinterpret_cast<int*>(static_cast<uint8_t*>(ws_raw) + 2 * part);
+  CUtensorMap tmH, tmW;
+  if (!make_tmap_2d_bf16(&tmH, h, D, R, D, 64, 128)) return ORTHRUS_ECUDA;
+  if (!make_tmap_2d_bf16(&tmW, W, D, V, D, 64, 256)) return ORTHRUS_ECUDA;
+  const int vt = static_cast<int>(ceil_div(V, 256));
+  const int rtiles = static_cast<int>(ceil_div(R, 128));
+  const int tps = static_cast<int>(ceil_div(vt, pick_splits(rtiles, vt, num_sms(), kArgmaxMaxSplits)));
+  const int splits = static_cast<int>(ceil_div(vt, tps));
+  const int units = rtiles * splits;
+  ORTHRUS_CHECK_CUDA(ensure_smem(lmhead_stats_tc_kernel, StatsTile::SMEM));
+  const unsigned grid = static_cast<unsigned>(std::min(units, num_sms()));
+  lmhead_stats_tc_kernel<<<grid, 192, StatsTile::SMEM, stream>>>(tmH, tmW, static_cast<int>(R), static_cast<int>(V),
+                                                                 static_cast<int>(D), tps, rtiles, units, pm, ps, pi);
+  ORTHRUS_CHECK_LAUNCH();
+  lmhead_argmax_combine_kernel<<<static_cast<unsigned>(ceil_div(R, 8)), 256, 0, stream>>>(
+      pm, pi, static_cast<int>(R), splits, out);
+  ORTHRUS_CHECK_LAUNCH();
+  return ORTHRUS_OK;
+}
+
 template <typename T>
 int lmhead_kl_fwd_impl(const T* student, int64_t n, const T* teacher, int64_t m, const int64_t* index,
                        const T* weight, int64_t V, int64_t D, const float* row_weight, const int64_t* offsets,
@@ -851,11 +899,10 @@ int lmhead_kl_fwd_impl(const T* student, int64_t n, const T* teacher, int64_t m,
     const int rows = static_cast<int>(std::min<int64_t>(p.chunk, n - c0));
     int splits = 1;
     if constexpr (kBf16) {
-      CUtensorMap tmS, tmT, tmW, tmD;
+      CUtensorMap tmS, tmT, tmW;
       if (!make_tmap_2d_bf16(&tmS, student, D, n, D, 64, 128)) return ORTHRUS_ECUDA;
       if (!make_tmap_2d_bf16(&tmT, tg, D, n, D, 64, 128)) return ORTHRUS_ECUDA;
       if (!make_tmap_2d_bf16(&tmW, weight, D, V, D, 64, 128)) return ORTHRUS_ECUDA;
-      if (!make_tmap_2d_bf16(&tmD, diff, V, rows, Vp, 64, 128)) return ORTHRUS_ECUDA;
       const int vt = static_cast<int>(ceil_div(V, 128));
       const int rtiles = static_cast<int>(ceil_div(rows, 128));
       const int tps = static_cast<int>(ceil_div(vt, pick_splits(rtiles, vt, num_sms(), p.diff_splits)));
@@ -863,7 +910,7 @@ int lmhead_kl_fwd_impl(const T* student, int64_t n, const T* teacher, int64_t m,
       const int units = rtiles * splits;
       ORTHRUS_CHECK_CUDA(ensure_smem(lmhead_diff_tc_kernel, DiffTile::SMEM));
       const unsigned grid = static_cast<unsigned>(std::min(units, num_sms()));  // persistent, one CTA per SM
-      lmhead_diff_tc_kernel<<<grid, 192, DiffTile::SMEM, stream>>>(tmS, tmT, tmW, tmD, rows, static_cast<int>(c0),
+      lmhead_diff_tc_kernel<<<grid, 192, DiffTile::SMEM, stream>>>(tmS, tmT, tmW, diff, Vp, rows, static_cast<int>(c0),
                                                                    static_cast<int>(V), static_cast<int>(D), tps,
                                                                    rtiles, units, lse, lset, row_weight, klp);
       ORTHRUS_CHECK_LAUNCH();

@@ -572,22 +572,21 @@ class BlockDecodeResult:
 
 
 class _DecodeState:
-    """Static device buffers of a batched decode (fixed shapes, so one cycle can be graph-captured)."""
+    """Static device buffers of a batched decode (fixed shapes, so one cycle can be graph-captured).
+    The buffers depend on the batch size, the cache capacity and the decode settings only; reset()
+    loads a new set of prompts into them, so a captured cycle can be replayed for later calls."""
 
-    def __init__(self, model, prompts, max_new_tokens, eos, draft_table, sampler=None):
+    def __init__(self, model, B, cap, max_new_tokens, eos, table_rows=None, sampler=None):
         cfg = model.config
         dev = next(model.parameters()).device
         dtype = next(model.parameters()).dtype
         self.model, self.dev, self.K = model, dev, cfg.block_size
-        B = len(prompts)
-        self.B = B
-        plens = [len(p) for p in prompts]
-        self.max_len = torch.tensor([p + max_new_tokens for p in plens], dtype=torch.int32, device=dev)
-        cap = max(plens) + max_new_tokens + self.K + 8
+        self.B, self.cap, self.max_new = B, cap, max_new_tokens
+        self.max_len = torch.zeros(B, dtype=torch.int32, device=dev)
         self.cache = KVCache(cfg, batch=B, capacity=cap, device=dev, dtype=dtype)
         self.kv = self.cache.buffers()
-        self.start = torch.tensor(plens, dtype=torch.int32, device=dev)
-        self.prompt_len = torch.tensor(plens, dtype=torch.int32, device=dev)
+        self.start = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.prompt_len = torch.zeros(B, dtype=torch.int32, device=dev)
         self.anchor = torch.zeros(B, dtype=torch.int64, device=dev)
         self.done = torch.zeros(B, dtype=torch.uint8, device=dev)
         self.out = torch.zeros(B, max_new_tokens + self.K + 1, dtype=torch.int64, device=dev)
@@ -599,14 +598,41 @@ class _DecodeState:
         self.ar_tokens = torch.zeros(B, self.K, dtype=torch.int64, device=dev)
         self.block_ids = torch.full((B, self.K), cfg.mask_token_id, dtype=torch.int64, device=dev)
         self.arange = torch.arange(self.K, device=dev, dtype=torch.int64)
-        self.draft_table = draft_table  # [B, rows, K-1] int64 or None (scripted drafts)
+        # scripted drafts: [B, rows, K-1] int64, or None
+        self.draft_table = (torch.zeros(B, table_rows, self.K - 1, dtype=torch.int64, device=dev)
+                            if table_rows is not None else None)
         # sampled decoding: the draft distributions q of the cycle's drafts, over their candidates
         self.sampler = sampler
         if sampler is not None:
-            if draft_table is not None:
+            if table_rows is not None:
                 raise ValueError("scripted drafts have no draft distribution to sample against")
             C = sampler.candidates(cfg.vocab_size)
             self.draft_probs = torch.zeros(B, self.K - 1, C, dtype=torch.float32, device=dev)
+
+    @staticmethod
+    def capacity(prompts, max_new_tokens, K) -> int:
+        """KV rows per sequence, rounded up to 128 so that calls with similar prompts share one state."""
+        need = max(len(p) for p in prompts) + max_new_tokens + K + 8
+        return -(-need // 128) * 128
+
+    @classmethod
+    def for_prompts(cls, model, prompts, max_new_tokens, eos, draft_table=None, sampler=None):
+        K = model.config.block_size
+        st = cls(model, len(prompts), cls.capacity(prompts, max_new_tokens, K), max_new_tokens, eos,
+                 None if draft_table is None else draft_table.shape[1], sampler)
+        st.reset(prompts, draft_table)
+        return st
+
+    def reset(self, prompts, draft_table=None):
+        """Loads a new batch of prompts (the KV cache rows are rewritten by their prefill)."""
+        plens = torch.tensor([len(p) for p in prompts], dtype=torch.int32)
+        self.max_len.copy_(plens + self.max_new)
+        self.start.copy_(plens)
+        self.prompt_len.copy_(plens)
+        for t in (self.anchor, self.done, self.out, self.out_len, self.log, self.cycle):
+            t.zero_()
+        if self.draft_table is not None:
+            self.draft_table.copy_(draft_table)
 
     def cycle_once(self):
         """One draft + verify + accept cycle on the current stream (no host synchronisation)."""
@@ -618,10 +644,10 @@ class _DecodeState:
             limit2 = torch.clamp(self.max_len - self.start, 1, K).to(torch.int32)
             hidden = model.run_layers(x, positions, "draft", kv=self.kv, offsets=self.start,
                                       limit2=limit2)
-            logits = model.lm_logits(hidden)
             if self.sampler is None:
-                ops.decode_draft(logits, self.anchor, self.done, self.verify_ids)
+                ops.decode_draft_ids(model.lm_argmax(hidden), self.anchor, self.done, self.verify_ids)
             else:
+                logits = model.lm_logits(hidden)
                 draft_vals, draft_ids = ops.sample_candidates(logits[:, : K - 1], self.sampler)
                 ops.decode_sample_draft(draft_vals, draft_ids, self.sampler, self.cycle, self.anchor,
                                         self.done, self.verify_ids, self.draft_probs)
@@ -632,16 +658,24 @@ class _DecodeState:
             self.verify_ids[:, 1:] = drafts
         x = model.model.embed_tokens(self.verify_ids)
         hidden = model.run_layers(x, positions, "ar", kv=self.kv, offsets=self.start)
-        logits = model.lm_logits(hidden)
         if self.sampler is None:
-            ops.decode_verify_accept(logits, self.verify_ids, self.ar_tokens, self.eos, self.max_len,
-                                     self.start, self.anchor, self.done, self.out, self.out_len,
-                                     self.log, self.cycle)
+            ops.decode_accept_ids(model.lm_argmax(hidden), self.verify_ids, self.eos, self.max_len,
+                                  self.start, self.anchor, self.done, self.out, self.out_len, self.log,
+                                  self.cycle)
         else:
-            vals, ids = ops.sample_candidates(logits, self.sampler)
+            vals, ids = ops.sample_candidates(model.lm_logits(hidden), self.sampler)
             ops.decode_sample_accept(vals, ids, self.draft_probs, draft_ids, self.sampler,
                                      self.verify_ids, self.eos, self.max_len, self.start, self.anchor,
                                      self.done, self.out, self.out_len, self.log, self.cycle)
+
+
+_STATE_CACHE: dict = {}  # insertion-ordered: the least recently used state is evicted first
+_STATE_CACHE_SIZE = 2  # e.g. plain and scripted drafts over the same prompts
+
+
+def clear_decode_cache() -> None:
+    """Drops the decode states and captured cycles kept for reuse by block_decode."""
+    _STATE_CACHE.clear()
 
 
 @torch.inference_mode()
@@ -655,7 +689,21 @@ def block_decode(model, prompts: list[list[int]], max_new_tokens: int, eos=(), *
     the block anchored at prompt_len + i (scripted drafts that exercise accept / rollback, the
     device counterpart of the reference tests' ScriptedBackend)."""
     eos = set(eos)
-    st = _DecodeState(model, prompts, max_new_tokens, eos, draft_table, sampler)
+    K = model.config.block_size
+    cap = _DecodeState.capacity(prompts, max_new_tokens, K)
+    rows = None if draft_table is None else draft_table.shape[1]
+    # a state and its captured cycle are reused by later calls with the same shapes and settings
+    # (and the same weight tensors): the capture is host work of about a tenth of a second
+    key = (id(model), tuple(p.data_ptr() for p in model.parameters()), len(prompts), cap, max_new_tokens,
+           tuple(sorted(eos)), rows, sampler)
+    entry = _STATE_CACHE.pop(key, None) if use_graph else None
+    if entry is None:
+        while len(_STATE_CACHE) >= _STATE_CACHE_SIZE:  # free the oldest state before allocating one
+            _STATE_CACHE.pop(next(iter(_STATE_CACHE)))
+        st, graph = _DecodeState(model, len(prompts), cap, max_new_tokens, eos, rows, sampler), None
+    else:
+        st, graph = entry
+    st.reset(prompts, draft_table)
     B, dev = st.B, st.dev
     torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
@@ -668,13 +716,12 @@ def block_decode(model, prompts: list[list[int]], max_new_tokens: int, eos=(), *
         kv_b = [(k[b: b + 1], v[b: b + 1]) for k, v in st.kv]
         zero = torch.zeros(1, dtype=torch.int32, device=dev)
         hidden = model.run_layers(x, pos, "ar", kv=kv_b, offsets=zero)
-        last = model.lm_logits(hidden[:, -1:]).reshape(1, -1)
         if sampler is None:
-            tok = ops.argmax_rows(last)
+            tok = model.lm_argmax(hidden[:, -1:])
             st.anchor[b] = tok[0]
             st.out[b, 0] = tok[0]
         else:
-            firsts.append(last)
+            firsts.append(model.lm_logits(hidden[:, -1:]).reshape(1, -1))
     if sampler is not None:  # one draw per sequence, counted by its index
         vals, ids = ops.sample_candidates(torch.cat(firsts), sampler)
         tok = ops.sample_rows(vals, ids, sampler)
@@ -686,8 +733,8 @@ def block_decode(model, prompts: list[list[int]], max_new_tokens: int, eos=(), *
     st.done |= (st.start >= st.max_len - 1).to(torch.uint8)
     torch.cuda.synchronize(dev)
     t1 = time.perf_counter()
-    graph = None
-    if use_graph:
+    cycles_run = 0
+    if use_graph and graph is None:
         stream = torch.cuda.Stream(dev)
         stream.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(stream):
@@ -699,7 +746,9 @@ def block_decode(model, prompts: list[list[int]], max_new_tokens: int, eos=(), *
         with torch.cuda.graph(graph):
             st.cycle_once()
         # capture recorded but did not run the cycle
-    cycles_run = 1 if use_graph else 0
+        cycles_run = 1
+    if use_graph:
+        _STATE_CACHE[key] = (st, graph)
     torch.cuda.synchronize(dev)
     t_steady = time.perf_counter()
     first_steady = cycles_run

@@ -654,6 +654,16 @@ class OrthrusLM(nn.Module):
             logits = ops.gemm(h, w)
         return logits.view(*shape, -1)
 
+    def lm_argmax(self, hidden: torch.Tensor) -> torch.Tensor:
+        """Greedy pick of every row of hidden [..., d]: int64 [rows], the argmax of lm_logits(hidden)
+        (lowest index on ties). bf16 rows take the LM-head argmax kernel, which computes the same
+        fp32 logits tiles and never writes them."""
+        h = hidden.reshape(-1, hidden.shape[-1])
+        w = self.lm_head.weight
+        if h.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and h.shape[-1] % 64 == 0:
+            return ops.lmhead_argmax(h, w)
+        return ops.argmax_rows(self.lm_logits(h).reshape(h.shape[0], -1))
+
     def run_layers(self, x, positions, mode: str, **kwargs):
         """The fused layer loop of OrthrusModel.run_layers (used by the device decode loop)."""
         return self.model.run_layers(x, positions, mode, **kwargs)

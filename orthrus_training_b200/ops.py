@@ -550,6 +550,36 @@ def decode_verify_accept(logits, verify_ids, ar_tokens, eos, max_len, start, anc
         L.stream_of(logits.device)), "decode_verify_accept")
 
 
+def lmhead_argmax(hidden: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """argmax over the vocabulary of hidden [R, d] @ weight [V, d]^T (bf16) without writing the
+    logits; int64 [R], the lowest index on ties (the argmax of gemm(..., out_dtype=fp32))."""
+    _require_cuda(hidden, weight)
+    h = hidden.reshape(-1, hidden.shape[-1]).contiguous()
+    R, d = h.shape
+    out = torch.empty(R, dtype=torch.int64, device=h.device)
+    lib = L.lib()
+    ws = torch.empty(int(lib.orthrus_lmhead_argmax_workspace_bytes(R)), dtype=torch.uint8, device=h.device)
+    L.check(lib.orthrus_lmhead_argmax_bf16(h.data_ptr(), R, weight.data_ptr(), weight.shape[0], d, out.data_ptr(),
+                                           ws.data_ptr(), ws.numel(), L.stream_of(h.device)), "lmhead_argmax")
+    return out
+
+
+def decode_draft_ids(ids, anchor, done, verify_ids):
+    B, K = verify_ids.shape
+    L.check(L.lib().orthrus_decode_draft_ids(ids.data_ptr(), B, K, anchor.data_ptr(), L.ptr(done),
+                                             verify_ids.data_ptr(), L.stream_of(ids.device)), "decode_draft_ids")
+
+
+def decode_accept_ids(ar_tokens, verify_ids, eos, max_len, start, anchor, done, out_tokens, out_len,
+                      accepted_log, cycle):
+    B, K = verify_ids.shape
+    L.check(L.lib().orthrus_decode_accept_ids(
+        ar_tokens.data_ptr(), B, K, verify_ids.data_ptr(), L.ptr(eos), 0 if eos is None else eos.numel(),
+        max_len.data_ptr(), start.data_ptr(), anchor.data_ptr(), done.data_ptr(), out_tokens.data_ptr(),
+        out_len.data_ptr(), out_tokens.shape[1], accepted_log.data_ptr(), cycle.data_ptr(), accepted_log.shape[1],
+        L.stream_of(ar_tokens.device)), "decode_accept_ids")
+
+
 # --- sampled decoding ---------------------------------------------------------------------------
 
 SAMPLE_MAX_TOP_K = 112  # top_k of the device sampler (candidates: top_k + 16 spares, at most 128)

@@ -78,3 +78,22 @@ def test_a_block_pass_equals_one_row_passes_bit_for_bit():
         done, _ = ops.attention_fwd(q[:, :, t:t + 1].contiguous(), kc, vc, k2, v2, mask=2, hd=128,
                                     scale=128 ** -0.5, offset=off, limit2=lim, want_lse=False)
         assert torch.equal(done[:, 0], dfull[:, t]), t
+
+
+@pytest.mark.parametrize("R", [1, 32, 300, 1024])
+def test_lmhead_argmax_equals_the_argmax_of_the_logits(R):
+    """Greedy decoding picks tokens with the LM-head argmax kernel (no logits written); plain greedy
+    paths take argmax_rows of the fp32 logits. Both must agree row for row (lossless decoding)."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(R)
+    V, d = 151936, 1024
+    w = (torch.randn(V, d, generator=g) * 0.05).to(torch.bfloat16).to(DEV)
+    h = torch.randn(R, d, generator=g).to(torch.bfloat16).to(DEV)
+    h[0] = h[-1]  # a repeated row
+    want = ops.argmax_rows(ops.gemm(h, w, out_dtype=torch.float32))
+    got = ops.lmhead_argmax(h, w)
+    assert torch.equal(got, want)
+    # a tie: two vocabulary rows equal, the lower index wins
+    w2 = w.clone()
+    w2[5000] = w2[123456] = h[0] * 4
+    assert ops.lmhead_argmax(h[:1], w2).item() == ops.argmax_rows(ops.gemm(h[:1], w2, out_dtype=torch.float32)).item() == 5000

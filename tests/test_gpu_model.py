@@ -223,3 +223,25 @@ def test_lossless_block_decode_06b_layers(dtype):
     res = block_decode(model, [prompt], 64)
     ref = ar_generate_batch(model, torch.tensor([prompt], device=DEV), 64)[0, 150:].tolist()
     assert res.tokens[0] == ref
+
+
+def test_block_decode_reuses_its_captured_cycle_across_calls():
+    """A second call with other prompts of the same shapes replays the first call's captured cycle
+    on the reset state: its tokens equal a fresh decode's, and so do the first prompts' again."""
+    from orthrus_training_b200 import decoding as D
+
+    g = load_golden("config1_decode.pt")
+    model = _load(g)
+    p1 = [c["prompt"] for c in g["cases"]]
+    p2 = [p[3:] + p[:3] for p in p1]  # other prompts, same lengths
+    D.clear_decode_cache()
+    fresh2 = D.block_decode(model, p2, 40)
+    D.clear_decode_cache()
+    first = D.block_decode(model, p1, 40)
+    assert len(D._STATE_CACHE) == 1
+    second = D.block_decode(model, p2, 40)
+    again = D.block_decode(model, p1, 40)
+    assert len(D._STATE_CACHE) == 1
+    assert second.tokens == fresh2.tokens and second.accepted == fresh2.accepted
+    assert again.tokens == first.tokens
+    D.clear_decode_cache()
