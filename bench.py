@@ -21,6 +21,7 @@ on the host cores: each step is one 2048-token row of the same workload.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -706,6 +707,10 @@ def run_ours(args):
     for _ in range(args.warmup):
         trainer.step([(ids_dev, mask_dev)], ready=resident)
     barrier(world)
+    # Python's cyclic garbage collector stays off through the timed loops (collected once here and
+    # re-enabled after them), so a collection pause of the host never lands inside a timed step
+    gc.collect()
+    gc.disable()
 
     # device-resident inputs: the headline number, nothing else recorded in the timed region
     launches0 = _lib.launch_count()
@@ -777,6 +782,7 @@ def run_ours(args):
     float(pending)
     f1.record()
     barrier(world)
+    gc.enable()
     ms_e2e = max_over_ranks(f0.elapsed_time(f1), world)
 
     tokens = ROWS * SEQ * world * args.steps

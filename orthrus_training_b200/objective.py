@@ -104,6 +104,23 @@ class _RMSNorm(torch.autograd.Function):
         return ops.rms_norm_backward(x, weight, rstd, dy), None, None
 
 
+class _NormWithSkip(torch.autograd.Function):
+    """RMSNorm of a block input that also feeds the block's residual add: returns (n(x), x). Its
+    backward receives both gradients of x and sums them inside the RMSNorm backward kernel (one
+    rounding), instead of autograd adding the residual gradient in a separate pass."""
+
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        y, rstd = ops.rms_norm(x, weight, eps, want_rstd=True)
+        ctx.save_for_backward(x, weight, rstd)
+        return y, x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, dy, dskip):
+        x, weight, rstd = ctx.saved_tensors
+        return ops.rms_norm_backward(x, weight, rstd, dy, dres=dskip), None, None
+
+
 class _SwiGLU(torch.autograd.Function):
     """silu(gate) * up of the fused [gate | up] projection (orthrus/objective.py:146-149)."""
 
@@ -337,7 +354,10 @@ def _diffusion_layer(backbone, i, x, ar_k, ar_v, positions, anchors, inv, B, Q, 
     Hq, Hkv, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
     eps = cfg.rms_norm_eps
     meta = (B, Q, Hq, Hkv, hd, padded_head_dim(hd), cfg.block_size, eps)
-    h = _rms_norm(x, layer.input_layernorm.weight, eps)
+    if torch.is_grad_enabled() and not layer.input_layernorm.weight.requires_grad:
+        h, x = _NormWithSkip.apply(x, layer.input_layernorm.weight, eps)
+    else:
+        h = _rms_norm(x, layer.input_layernorm.weight, eps)
     w_qkv = torch.cat([attn.q_proj_diff.weight, attn.k_proj_diff.weight, attn.v_proj_diff.weight], 0)
     if rope is not None and ops.fused_qkv_rope_supported(h, hd, padded_head_dim(hd), Q, Hq, Hkv):
         o = DualViewAttentionFused.apply(h, w_qkv, attn.q_norm_diff.weight, attn.k_norm_diff.weight, ar_k,
