@@ -21,6 +21,7 @@ on the host cores: each step is one 2048-token row of the same workload.
 from __future__ import annotations
 
 import argparse
+import datetime
 import gc
 import json
 import os
@@ -57,15 +58,24 @@ def peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region. The sampler
+    is started ahead of the region (nvidia-smi takes a while to start on a box of eight GPUs) and
+    only the samples stamped between mark_start() and mark_end() are summarised."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.proc = None
+        self.start = self.end = None
+
+    def mark_start(self):
+        self.start = datetime.datetime.now()
+
+    def mark_end(self):
+        self.end = datetime.datetime.now()
 
     def __enter__(self):
         try:
@@ -93,14 +103,17 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in getattr(self, "lines", []):
             parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
+                stamp = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+                if (self.start and stamp < self.start) or (self.end and stamp > self.end):
+                    continue
+                clock, mx = float(parts[2]), float(parts[3])
             except ValueError:
                 continue
-            for name, val in zip(names, parts[5:9]):
+            sm.append(clock)
+            for name, val in zip(names, parts[6:10]):
                 if val.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
@@ -704,18 +717,19 @@ def run_ours(args):
     resident.record()
     h2d = ids.numel() * ids.element_size() + mask.numel() * mask.element_size()
 
-    for _ in range(args.warmup):
-        trainer.step([(ids_dev, mask_dev)], ready=resident)
-    barrier(world)
-    # Python's cyclic garbage collector stays off through the timed loops (collected once here and
-    # re-enabled after them), so a collection pause of the host never lands inside a timed step
-    gc.collect()
-    gc.disable()
-
-    # device-resident inputs: the headline number, nothing else recorded in the timed region
-    launches0 = _lib.launch_count()
-    with ClockSampler(local) as clocks:
+    with ClockSampler(local) as clocks:  # started during the warm-up, summarised over the timed steps
+        for _ in range(args.warmup):
+            trainer.step([(ids_dev, mask_dev)], ready=resident)
         barrier(world)
+        # Python's cyclic garbage collector stays off through the timed loops (collected once here
+        # and re-enabled after them), so a collection pause of the host never lands in a timed step
+        gc.collect()
+        gc.disable()
+
+        # device-resident inputs: the headline number, nothing else recorded in the timed region
+        launches0 = _lib.launch_count()
+        barrier(world)
+        clocks.mark_start()
         e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
         e0.record()
         for i in range(args.steps):
@@ -727,6 +741,7 @@ def run_ours(args):
                 torch.cuda.profiler.stop()
         e1.record()
         barrier(world)
+        clocks.mark_end()
     ms = max_over_ranks(e0.elapsed_time(e1), world)
     launches = (_lib.launch_count() - launches0) // max(args.steps, 1)
     loss = float(out["loss"])
