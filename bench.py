@@ -710,7 +710,7 @@ def run_ours(args):
     copy_diff_from_ar(model)
     group = None
     trainer = Trainer(model, lr=1e-4, total_steps=1000, num_anchors=ANCHORS, kl_chunk_size=4096,
-                      seed=1, world=world, rank=rank, group=group)
+                      seed=1, world=world, rank=rank, group=group, layers_per_bucket=args.layers_per_bucket)
     ids, mask = make_rows(1 + rank)
     ids_dev, mask_dev = ids.to(dev), mask.to(dev)
     resident = torch.cuda.Event()  # the device-resident rows are complete from here on
@@ -778,7 +778,8 @@ def run_ours(args):
         comm = {"ms_per_step_without_allreduce": round(ms_nocomm / args.steps, 3),
                 "exposed_ms_per_step": round((ms - ms_nocomm) / args.steps, 3),
                 "allreduce_bytes_per_step": grad_bytes, "collective": "NCCL all-reduce (AVG) of the twin "
-                "gradients, one bucket per layer, launched from grad hooks during the backward"}
+                f"gradients, one bucket per {args.layers_per_bucket} layers, launched from grad hooks during "
+                "the backward"}
 
     # end to end through the public API: host rows through DevicePrefetcher (pinned buffers, a
     # copy stream one micro-batch ahead), every step's loss read back to the host. A training
@@ -880,6 +881,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers-per-bucket", type=int, default=4,
+                    help="decoder layers per gradient all-reduce bucket (N > 1)")
     ap.add_argument("--decode", action="store_true", help="measure parallel block decoding instead")
     ap.add_argument("--decode-batch", type=int, nargs="+", default=[1, 32])
     ap.add_argument("--decode-new", type=int, default=512)

@@ -40,12 +40,14 @@ def anchor_rng(seed: int, *keys, device) -> torch.Generator:
 
 
 class GradBuckets:
-    """Flat per-layer gradient buffers of the trainable parameters with all-reduce hooks. With one
-    rank there is nothing to reduce: the parameters keep no preassigned gradient buffers, so the
-    first micro-batch's gradients are stored by autograd as they come (no zeroing pass and no
-    accumulating add into a zeroed buffer)."""
+    """Flat gradient buffers of the trainable parameters, `layers_per_bucket` decoder layers each,
+    with all-reduce hooks: a bucket's all-reduce is launched as soon as its last gradient of the
+    step is accumulated. With one rank there is nothing to reduce: the parameters keep no
+    preassigned gradient buffers, so the first micro-batch's gradients are stored by autograd as
+    they come (no zeroing pass and no accumulating add into a zeroed buffer)."""
 
-    def __init__(self, model, params: list[torch.nn.Parameter], world: int, group=None):
+    def __init__(self, model, params: list[torch.nn.Parameter], world: int, group=None,
+                 layers_per_bucket: int = 1):
         self.world = world
         self.group = group
         self.params = list(params)
@@ -58,7 +60,7 @@ class GradBuckets:
         for p in params:
             name = names[id(p)]
             layer = int(name.split("layers.")[1].split(".")[0]) if "layers." in name else -1
-            by_layer.setdefault(layer, []).append(p)
+            by_layer.setdefault(layer // max(layers_per_bucket, 1) if layer >= 0 else -1, []).append(p)
         self.buckets = []
         for layer in sorted(by_layer, reverse=True):  # backward reaches the last layer first
             ps = by_layer[layer]
@@ -158,12 +160,12 @@ class Trainer:
                  warmup_ratio=0.05, min_lr_ratio=0.1, max_grad_norm=1.0, num_anchors=32,
                  kl_chunk_size=4096, gamma=0.0, seed=42, world=1, rank=0, group=None,
                  check_device_every=50, monitor: PeerMonitor | None = None,
-                 document_mask: bool = False):
+                 document_mask: bool = False, layers_per_bucket: int = 4):
         from orthrus_training_b200.modeling_orthrus import freeze_to_diffusion
 
         self.model = model
         self.params = freeze_to_diffusion(model)
-        self.buckets = GradBuckets(model, self.params, world, group)
+        self.buckets = GradBuckets(model, self.params, world, group, layers_per_bucket)
         fused = all(p.is_cuda for p in self.params)
         self.optimizer = torch.optim.AdamW(self.params, lr=lr, betas=betas,
                                            weight_decay=weight_decay, fused=fused)
