@@ -63,20 +63,46 @@ __global__ void __launch_bounds__(256) attn_decode_split_kernel(
   const int G = Hq / Hkv, rows = G * Tq;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nthreads = blockDim.x;
-  griddep_launch_dependents();  // launched as a programmatic dependent: inputs are ready only after the wait
-  griddep_wait();
+  griddep_launch_dependents();  // launched as a programmatic dependent
+  // Before griddep_wait() only what the kernels still running ahead of this one never write: the
+  // cycle's positions (offset, limit2) and the cache rows below offset[b], written by earlier
+  // passes. Q and this pass's own keys (the block's rows of the cache, or source 2) come after it.
   const int src = split >= ns1 ? 1 : 0;
   const int64_t key0 = src == 0 ? static_cast<int64_t>(split) * kDecSplit : 0;
   const int64_t kend = decode_source_end(mp, b, src, Tq);
   if (key0 >= kend) return;  // no row's visible keys reach this split: nobody reads its partial
   const int nkeys = static_cast<int>(min(static_cast<int64_t>(src == 0 ? kDecSplit : kDecSub), kend - key0));
+  // keys [0, nold) of this split are earlier passes' cache rows
+  const int64_t prior = src == 0 ? (mp.offset ? static_cast<int64_t>(mp.offset[b]) : 0) : 0;
+  const int nold = static_cast<int>(min(static_cast<int64_t>(nkeys), max(prior - key0, static_cast<int64_t>(0))));
   const __nv_bfloat16* K = src == 0 ? k1 + b * s1b + g * s1h : k2 + b * s2b + g * s2h;
   const __nv_bfloat16* V = src == 0 ? v1 + b * s1b + g * s1h : v2 + b * s2b + g * s2h;
   const int qrows = ((rows + 15) / 16) * 16;
   const uint32_t sQ = smem_u32(smem);
   const uint32_t sKV = sQ + qrows * kDecRow;  // sub-chunk c: K at sKV + 2c * TILE, V after it
   constexpr int TILE = kDecSub * kDecRow;
-  // stage Q (zero rows past the last), then the two sub-chunks as separate cp.async groups
+  // keys of sub-chunk c in [lo_key, hi_key) of the split: copies, or zeros past the loaded range
+  auto stage_keys = [&](int c, int lo_key, int hi_key, bool zero_rest) {
+    for (int i = threadIdx.x; i < kDecSub * 16; i += nthreads) {
+      const int kk = i >> 4, ch = i & 15;
+      const int key = c * kDecSub + kk;
+      const uint32_t dk = sKV + (2 * c) * TILE + kk * kDecRow + ch * 16, dv = dk + TILE;
+      if (key >= lo_key && key < hi_key) {
+        cp_async16(dk, K + (key0 + key) * 128 + ch * 8);
+        cp_async16(dv, V + (key0 + key) * 128 + ch * 8);
+      } else if (zero_rest && key >= nkeys) {  // masked scores, and P = 0 times a finite V
+        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dk), "r"(0) : "memory");
+        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dv), "r"(0) : "memory");
+      }
+    }
+  };
+  // groups 1, 2: the earlier passes' keys of sub-chunks 0 and 1, in flight during the wait
+  stage_keys(0, 0, nold, true);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  stage_keys(1, 0, nold, true);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  griddep_wait();
+  // groups 3, 4: Q (zero rows past the last) with this pass's keys of sub-chunk 0, then of sub-chunk 1
   for (int i = threadIdx.x; i < qrows * 16; i += nthreads) {
     const int r = i >> 4, c = i & 15;
     const uint32_t dst = sQ + r * kDecRow + c * 16;
@@ -87,21 +113,10 @@ __global__ void __launch_bounds__(256) attn_decode_split_kernel(
       asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
     }
   }
-  for (int c = 0; c < 2; ++c) {
-    for (int i = threadIdx.x; i < kDecSub * 16; i += nthreads) {
-      const int kk = i >> 4, ch = i & 15;
-      const int key = c * kDecSub + kk;
-      const uint32_t dk = sKV + (2 * c) * TILE + kk * kDecRow + ch * 16, dv = dk + TILE;
-      if (key < nkeys) {
-        cp_async16(dk, K + (key0 + key) * 128 + ch * 8);
-        cp_async16(dv, V + (key0 + key) * 128 + ch * 8);
-      } else {  // zero keys past the loaded range: masked scores, and P = 0 times a finite V
-        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dk), "r"(0) : "memory");
-        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dv), "r"(0) : "memory");
-      }
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  }
+  stage_keys(0, nold, nkeys, false);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  stage_keys(1, nold, nkeys, false);
+  asm volatile("cp.async.commit_group;" ::: "memory");
   // the two rows of this thread: 16 * warp + lane / 4 (+ 8)
   const int rA = 16 * warp + (lane >> 2), rB = rA + 8;
   int64_t lo[2] = {0, 0}, hi[2] = {0, 0};
@@ -122,7 +137,7 @@ __global__ void __launch_bounds__(256) attn_decode_split_kernel(
   for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   const bool active = 16 * warp < rows;
   for (int c = 0; c < 2; ++c) {
-    if (c == 0) {
+    if (c == 0) {  // groups 1-3: sub-chunk 0 complete (group 2, sub-chunk 1's earlier keys, too)
       asm volatile("cp.async.wait_group 1;" ::: "memory");
     } else {
       asm volatile("cp.async.wait_group 0;" ::: "memory");
