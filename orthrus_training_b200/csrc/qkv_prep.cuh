@@ -333,6 +333,38 @@ __device__ __forceinline__ void rope_lane_table(float pos, const float* __restri
 // One warp per token row (8 rows per CTA), no shared memory: every lane builds the RoPE table of
 // its own elements, then the warp walks the row's heads PER at a time, all PER head rows loaded
 // before any is computed. Lane l holds the elements [l * NE, l * NE + NE) of a head as one vector
+// The prologue of one q or k head row in place: lane holds the elements [lane * NE, lane * NE +
+// NE) of x; RMSNorm with the fixed-order butterfly (x * rstd rounded, times the q or k norm weight
+// wq / wk, rounded), then RoPE
+// with this lane's cos / sin (partner element from lane ^ 16). Returns rstd. The forward prologue
+// and the decode attention, which runs it on the block rows itself, share this arithmetic, so a
+// key or query gets the same bits on either path.
+template <typename T, int HD>
+__device__ __forceinline__ float prep_head_row(float* x, const float* wq, const float* wk, bool is_q, const float* cs,
+                                               const float* sn, float eps, int lane) {
+  constexpr int NE = HD / 32;
+  constexpr int HALF = HD / 2;
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < NE; ++k) ss = fmaf(x[k], x[k], ss);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float rstd = rsqrtf(ss / static_cast<float>(HD) + eps);
+#pragma unroll
+  for (int k = 0; k < NE; ++k) x[k] *= rstd;
+  round_all<T, NE>(x);
+#pragma unroll
+  for (int k = 0; k < NE; ++k) x[k] *= is_q ? wq[k] : wk[k];
+  round_all<T, NE>(x);
+#pragma unroll
+  for (int k = 0; k < NE; ++k) {
+    const float partner = __shfl_xor_sync(0xffffffffu, x[k], 16);
+    const float rot = (lane * NE + k) < HALF ? -partner : partner;
+    x[k] = x[k] * cs[k] + rot * sn[k];
+  }
+  return rstd;
+}
+
 // access. Requires 16-byte aligned tensors and D % 8 == 0 (checked by the host).
 template <typename T, int HD>
 __global__ void __launch_bounds__(256, 4) qkv_prep_fwd_row_kernel(
@@ -380,24 +412,7 @@ __global__ void __launch_bounds__(256, 4) qkv_prep_fwd_row_kernel(
         dst = v_out + ((b * Hkv + (head - Hq - Hkv)) * cap + orow_kv) * D;
       } else {
         const bool is_q = head < Hq;
-        float ss = 0.f;
-#pragma unroll
-        for (int k = 0; k < NE; ++k) ss = fmaf(x[k], x[k], ss);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-        const float rstd = rsqrtf(ss / static_cast<float>(HD) + eps);
-#pragma unroll
-        for (int k = 0; k < NE; ++k) x[k] *= rstd;
-        round_all<T, NE>(x);
-#pragma unroll
-        for (int k = 0; k < NE; ++k) x[k] *= is_q ? wq[k] : wk[k];
-        round_all<T, NE>(x);
-#pragma unroll
-        for (int k = 0; k < NE; ++k) {
-          const float partner = __shfl_xor_sync(0xffffffffu, x[k], 16);
-          const float rot = (lane * NE + k) < HALF ? -partner : partner;
-          x[k] = x[k] * cs[k] + rot * sn[k];
-        }
+        const float rstd = prep_head_row<T, HD>(x, wq, wk, is_q, cs, sn, eps, lane);
         if (rstd_out != nullptr && lane == 0) rstd_out[row * (Hq + Hkv) + head] = rstd;
         dst = is_q ? q_out + ((b * Hq + head) * Tn + t) * D
                    : k_out + ((b * Hkv + (head - Hq)) * cap + orow_kv) * D;
