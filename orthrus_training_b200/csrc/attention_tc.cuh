@@ -1167,9 +1167,13 @@ namespace orthrus {
 // CTA = 128 query rows of the heads 2p, 2p+1 sharing one KV head; 320 threads (warp 0 TMA, warp 1
 // MMA, warps 2-5 / 6-9 the rows of head 2p / 2p+1). Key tiles of 64 so that both heads fit in TMEM:
 // head h owns S [64h .. +64), dP [128 + 64h .. +64) and its dQ accumulator [256 + 128h .. +128).
-// Per tile: S = Q K^T, dP = dO V^T (N = 64), then dS = P (dP - delta) (bf16, [128][64] swizzled
-// in shared memory) and dQ += dS K (K as the MN-major operand). While one head's rows compute dS,
-// the tensor core runs the other head's MMAs.
+// Per tile: S = Q K^T, dP = dO V^T (N = 64), then dS = P (dP - delta), which the rows write as
+// bf16 pairs over the first 32 columns of their own dP (already read), and dQ += dS K with dS as
+// the TMEM operand and K as the MN-major shared-memory operand. A head's next S is issued right
+// after its dQ MMA, its next dP only once that dQ MMA has completed (a commit the issuing thread
+// waits on: two MMAs with different accumulators are not ordered). Keeping dS out of shared memory
+// leaves room for three K/V stages. While one head's rows compute dS, the tensor core runs the
+// other head's MMAs.
 
 constexpr int kKeyBox64 = 64 * 64 * 2;  // one [64 rows][64] bf16 box = 8 KB
 
@@ -1187,11 +1191,12 @@ struct Dq2Smem {
   static constexpr int KT = BOXES * kKeyBox64;       // [64][D]
   static constexpr int OFF_Q = 0;                    // Q of head h at h * QT
   static constexpr int OFF_DO = 2 * QT;              // dO of head h
+  static constexpr int STAGES = 3;
   static constexpr int OFF_KV = 4 * QT;              // stage s: K at s * 2KT, V at s * 2KT + KT
-  static constexpr int OFF_DS = OFF_KV + 4 * KT;     // dS of head h: [128][64] = 16 KB
-  static constexpr int OFF_BAR = OFF_DS + 2 * kAttnTileBytes;
+  static constexpr int OFF_BAR = OFF_KV + STAGES * 2 * KT;
   static constexpr int SMEM = OFF_BAR + 512 + 1024;
 };
+static_assert(Dq2Smem<128>::SMEM <= 232448, "dQ kernel shared memory");
 
 template <int D>
 __global__ void __launch_bounds__(320, 1)
@@ -1204,13 +1209,15 @@ __global__ void __launch_bounds__(320, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::OFF_BAR);
+  constexpr int NS = S::STAGES;
   uint64_t* in_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2] per head: S and dP ready
-  uint64_t* ds_full = bars + 7;   // [2] per head (128 arrivals)
-  uint64_t* ds_empty = bars + 9;  // [2] per head: dQ MMA consumed dS
-  uint64_t* mma_done = bars + 11;
+  uint64_t* kv_full = bars + 1;            // [NS]
+  uint64_t* kv_empty = bars + 1 + NS;      // [NS]
+  uint64_t* s_full = bars + 1 + 2 * NS;   // [2] per head: S and dP of the tile in TMEM
+  uint64_t* ds_full = s_full + 2;          // [2] per head (128 arrivals): dS written to TMEM
+  uint64_t* ds_empty = s_full + 4;         // [2] per head: the dQ MMA has consumed dS
+  uint64_t* mma_done = s_full + 6;
+  static_assert(1 + 2 * NS + 7 <= 16, "dQ kernel barriers");
   unsigned long long* red = reinterpret_cast<unsigned long long*>(bars + 16);
   AttnTiles* tiles = reinterpret_cast<AttnTiles*>(bars + 20);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
@@ -1227,9 +1234,11 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(in_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&ds_full[i], 128);
       mbar_init(&ds_empty[i], 1);
@@ -1272,8 +1281,8 @@ __global__ void __launch_bounds__(320, 1)
       }
       int issued = 0;
       for (int j = 0; j < nt; ++j) {
-        const int s = j & 1;
-        if (*abort_flag || !mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1)) {
+        const int s = j % NS;
+        if (*abort_flag || !mbar_wait(&kv_empty[s], ((j / NS) & 1) ^ 1)) {
           *abort_flag = 1;
           break;
         }
@@ -1289,10 +1298,10 @@ __global__ void __launch_bounds__(320, 1)
           tma_load_3d(vt + c * kKeyBox64, src2 ? &tmV2 : &tmV1, &kv_full[s], c * 64, key0,
                       static_cast<int>(b * Hkv + hk));
         }
-        // two stages of 64 keys: tile j + 3 goes to L2 now (the AR keys come from HBM otherwise)
-        if (j + 3 < nt) {
-          const bool pf2 = j + 3 >= n1b;
-          const int pkey = (pf2 ? t2b + (j + 3 - n1b) : j + 3) * 64;
+        // three stages of 64 keys: tile j + 4 goes to L2 now (the AR keys come from HBM otherwise)
+        if (j + 4 < nt) {
+          const bool pf2 = j + 4 >= n1b;
+          const int pkey = (pf2 ? t2b + (j + 4 - n1b) : j + 4) * 64;
 #pragma unroll
           for (int c = 0; c < S::BOXES; ++c) {
             tma_prefetch_l2_3d(pf2 ? &tmK2 : &tmK1, c * 64, pkey, static_cast<int>(b * Hkv + hk));
@@ -1303,32 +1312,37 @@ __global__ void __launch_bounds__(320, 1)
       }
       if (*abort_flag) {
         mbar_wait_short(in_full, 0);
-        for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait_short(&kv_full[j & 1], (j >> 1) & 1);
+        for (int j = max(0, issued - NS); j < issued; ++j) mbar_wait_short(&kv_full[j % NS], (j / NS) & 1);
       }
     }
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(128, 64, false, false);
       constexpr uint32_t idesc_q = umma_idesc_bf16(128, D, false, true);
-      auto issue_s = [&](int h, int j) {
+      auto issue_s = [&](int h, int j) {  // S = Q K^T
         const uint32_t q_base = smem_u32(smem + S::OFF_Q + h * S::QT);
-        const uint32_t do_base = smem_u32(smem + S::OFF_DO + h * S::QT);
-        const uint32_t k_base = smem_u32(smem + S::OFF_KV + (j & 1) * 2 * S::KT);
-        const uint32_t v_base = k_base + S::KT;
+        const uint32_t k_base = smem_u32(smem + S::OFF_KV + (j % NS) * 2 * S::KT);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
+        for (int kk = 0; kk < D / 16; ++kk)
           umma_f16(tmem + h * 64, desc_kmajor(q_base, kk), desc_kmajor_rows64(k_base, kk), idesc_s,
                    kk > 0 ? 1u : 0u);
+      };
+      auto issue_dp = [&](int h, int j) {  // dP = dO V^T; then S and dP of the tile are signalled
+        const uint32_t do_base = smem_u32(smem + S::OFF_DO + h * S::QT);
+        const uint32_t v_base = smem_u32(smem + S::OFF_KV + (j % NS) * 2 * S::KT) + S::KT;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
           umma_f16(tmem + 128 + h * 64, desc_kmajor(do_base, kk), desc_kmajor_rows64(v_base, kk), idesc_s,
                    kk > 0 ? 1u : 0u);
-        }
         umma_commit(&s_full[h]);
       };
       bool ok = mbar_wait(in_full, 0) && (nt == 0 || mbar_wait(&kv_full[0], 0));
       if (ok && nt > 0) {
         tc_fence_after();
         issue_s(0, 0);
+        issue_dp(0, 0);
         issue_s(1, 0);
+        issue_dp(1, 0);
       }
       for (int j = 0; ok && j < nt; ++j) {
         for (int h = 0; h < 2; ++h) {
@@ -1337,21 +1351,27 @@ __global__ void __launch_bounds__(320, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t ds_base = smem_u32(smem + S::OFF_DS + h * kAttnTileBytes);
-          const uint32_t k_base = smem_u32(smem + S::OFF_KV + (j & 1) * 2 * S::KT);
+          const uint32_t k_base = smem_u32(smem + S::OFF_KV + (j % NS) * 2 * S::KT);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_f16(tmem + 256 + h * 128, desc_kmajor(ds_base, kk), desc_mnmajor_rows64(k_base, kk), idesc_q,
-                     (j > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_tmem_a(tmem + 256 + h * 128, tmem + 128 + h * 64 + 8 * kk, desc_mnmajor_rows64(k_base, kk),
+                            idesc_q, (j > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&ds_empty[h]);
-          if (h == 1) umma_commit(&kv_empty[j & 1]);
+          if (h == 1) umma_commit(&kv_empty[j % NS]);
           if (j + 1 < nt) {
-            if (h == 0 && !mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) {
+            if (h == 0 && !mbar_wait(&kv_full[(j + 1) % NS], ((j + 1) / NS) & 1)) {
               ok = false;
               break;
             }
             tc_fence_after();
             issue_s(h, j + 1);
+            // dS lives in this head's dP columns: the next dP waits until the dQ MMA has read it
+            if (!mbar_wait(&ds_empty[h], j & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_dp(h, j + 1);
           }
         }
       }
@@ -1374,7 +1394,6 @@ __global__ void __launch_bounds__(320, 1)
     const float dl = live ? delta[qi] : 0.f;
     const float sl2 = scale * kLog2e;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const uint32_t ds_base = smem_u32(smem + S::OFF_DS + h * kAttnTileBytes);
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
       if (*abort_flag || !mbar_wait(&s_full[h], j & 1)) {
@@ -1385,40 +1404,37 @@ __global__ void __launch_bounds__(320, 1)
       const bool src2 = j >= n1b;
       const int64_t key0 = (src2 ? t2b + (j - n1b) : j) * 64;
       const int64_t lo = (src2 ? s2 : s1) - key0, hi = (src2 ? e2 : e1) - key0;
-      float x[64];
+      uint32_t pk[32];  // dS of the row's 64 keys as bf16 pairs
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int kind = chunk_kind_warp(lo, hi, 32 * c, 32);  // warp-uniform
-        float* xc = x + 32 * c;
         if (kind == 0) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) xc[i] = 0.f;
+          for (int i = 0; i < 16; ++i) pk[16 * c + i] = 0u;
           continue;
         }
-        float y[32];
-        tmem_ld32(lane_base + h * 64 + 32 * c, xc);
+        float x[32], y[32];
+        tmem_ld32(lane_base + h * 64 + 32 * c, x);
         tmem_ld32(lane_base + 128 + h * 64 + 32 * c, y);
         tmem_wait_ld();
         if (kind == 1) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) xc[i] = ex2_approx(fmaf(xc[i], sl2, -L2e)) * (y[i] - dl);
+          for (int i = 0; i < 32; ++i) x[i] = ex2_approx(fmaf(x[i], sl2, -L2e)) * (y[i] - dl);
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int col = 32 * c + i;
-            const float p = (col >= lo && col < hi) ? ex2_approx(fmaf(xc[i], sl2, -L2e)) : 0.f;
-            xc[i] = p * (y[i] - dl);
+            const float p = (col >= lo && col < hi) ? ex2_approx(fmaf(x[i], sl2, -L2e)) : 0.f;
+            x[i] = p * (y[i] - dl);
           }
         }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[16 * c + i] = pack_bf16x2(x[2 * i], x[2 * i + 1]);
       }
-      if (j > 0 && !mbar_wait(&ds_empty[h], (j - 1) & 1)) {
-        ok = false;
-        break;
-      }
-      store_row32_sw128(ds_base, row, 0, x);
-      store_row32_sw128(ds_base, row, 32, x + 32);
+      // over the dP columns this thread has just read (the tile's dP MMA is complete)
+      tmem_st32_words(lane_base + 128 + h * 64, pk);
+      tmem_wait_st();
       tc_fence_before();
-      fence_proxy_async_smem();
       mbar_arrive(&ds_full[h]);
     }
     if (!ok) *abort_flag = 1;
