@@ -1164,11 +1164,13 @@ namespace orthrus {
 // Backward dQ, two query heads per CTA (ping-pong), 64-key tiles
 // ------------------------------------------------------------------------------------------------
 //
-// CTA = 128 query rows of the heads 2p, 2p+1 sharing one KV head; 320 threads (warp 0 TMA, warp 1
-// MMA, warps 2-5 / 6-9 the rows of head 2p / 2p+1). Key tiles of 64 so that both heads fit in TMEM:
+// CTA = 128 query rows of the heads 2p, 2p+1 sharing one KV head; 576 threads (warp 0 TMA, warp 1
+// MMA, warps 2-9 / 10-17 the rows of head 2p / 2p+1: each row is shared by two warps, one per
+// 32-key half of the tile, so a thread's share of a tile's exponentials is 32). Key tiles of 64
+// so that both heads fit in TMEM:
 // head h owns S [64h .. +64), dP [128 + 64h .. +64) and its dQ accumulator [256 + 128h .. +128).
-// Per tile: S = Q K^T, dP = dO V^T (N = 64), then dS = P (dP - delta), which the rows write as
-// bf16 pairs over the first 32 columns of their own dP (already read), and dQ += dS K with dS as
+// Per tile: S = Q K^T, dP = dO V^T (N = 64), then dS = P (dP - delta), which each row warp writes
+// as bf16 pairs over the first 16 of the 32 dP columns it has just read, and dQ += dS K with dS as
 // the TMEM operand and K as the MN-major shared-memory operand. A head's next S is issued right
 // after its dQ MMA, its next dP only once that dQ MMA has completed (a commit the issuing thread
 // waits on: two MMAs with different accumulators are not ordered). Keeping dS out of shared memory
@@ -1198,8 +1200,10 @@ struct Dq2Smem {
 };
 static_assert(Dq2Smem<128>::SMEM <= 232448, "dQ kernel shared memory");
 
+constexpr int kDq2Threads = 576;
+
 template <int D>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(kDq2Threads, 1)
     attn_dq_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                        const __grid_constant__ CUtensorMap tmK1, const __grid_constant__ CUtensorMap tmV1,
                        const __grid_constant__ CUtensorMap tmK2, const __grid_constant__ CUtensorMap tmV2, int Hq,
@@ -1214,7 +1218,7 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* kv_full = bars + 1;            // [NS]
   uint64_t* kv_empty = bars + 1 + NS;      // [NS]
   uint64_t* s_full = bars + 1 + 2 * NS;   // [2] per head: S and dP of the tile in TMEM
-  uint64_t* ds_full = s_full + 2;          // [2] per head (128 arrivals): dS written to TMEM
+  uint64_t* ds_full = s_full + 2;          // [2] per head (8 warp arrivals): dS written to TMEM
   uint64_t* ds_empty = s_full + 4;         // [2] per head: the dQ MMA has consumed dS
   uint64_t* mma_done = s_full + 6;
   static_assert(1 + 2 * NS + 7 <= 16, "dQ kernel barriers");
@@ -1229,7 +1233,8 @@ __global__ void __launch_bounds__(320, 1)
   const int64_t b = blockIdx.y;
   const int G = Hq / Hkv;
   const int hk = (2 * pair) / G;
-  const int wg = warp >= 2 ? (warp - 2) / 4 : -1;
+  const int wg = warp >= 2 ? (warp - 2) / 8 : -1;        // head of a row warp
+  const int half = warp >= 2 ? ((warp - 2) / 4) & 1 : 0;  // its 32-key half of a tile
   const int row = warp >= 2 ? (warp & 3) * 32 + lane : -1;
 
   if (threadIdx.x == 0) {
@@ -1240,7 +1245,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&ds_full[i], 128);
+      mbar_init(&ds_full[i], 8);
       mbar_init(&ds_empty[i], 1);
     }
     mbar_init(mma_done, 1);
@@ -1256,7 +1261,7 @@ __global__ void __launch_bounds__(320, 1)
   // the operands and the outputs belong to the stream order only after griddep_wait()
   griddep_launch_dependents();
   griddep_wait();
-  attn_tile_map(mp, b, q0, Tq, has2, wg == 0 ? row : -1, red, tiles);
+  attn_tile_map(mp, b, q0, Tq, has2, (wg == 0 && half == 0) ? row : -1, red, tiles);
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // 64-key tiles: source 1 covers [0, 64 * n1b), source 2 [64 * t2b, 64 * (t2b + n2b))
@@ -1354,8 +1359,8 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t k_base = smem_u32(smem + S::OFF_KV + (j % NS) * 2 * S::KT);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_f16_tmem_a(tmem + 256 + h * 128, tmem + 128 + h * 64 + 8 * kk, desc_mnmajor_rows64(k_base, kk),
-                            idesc_q, (j > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_tmem_a(tmem + 256 + h * 128, tmem + 128 + h * 64 + (kk >> 1) * 32 + (kk & 1) * 8,
+                            desc_mnmajor_rows64(k_base, kk), idesc_q, (j > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&ds_empty[h]);
           if (h == 1) umma_commit(&kv_empty[j % NS]);
           if (j + 1 < nt) {
@@ -1404,18 +1409,15 @@ __global__ void __launch_bounds__(320, 1)
       const bool src2 = j >= n1b;
       const int64_t key0 = (src2 ? t2b + (j - n1b) : j) * 64;
       const int64_t lo = (src2 ? s2 : s1) - key0, hi = (src2 ? e2 : e1) - key0;
-      uint32_t pk[32];  // dS of the row's 64 keys as bf16 pairs
+      const int kind = chunk_kind_warp(lo, hi, 32 * half, 32);  // warp-uniform
+      uint32_t pk[16];  // dS of the row's 32 keys of this half as bf16 pairs
+      if (kind == 0) {
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int kind = chunk_kind_warp(lo, hi, 32 * c, 32);  // warp-uniform
-        if (kind == 0) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) pk[16 * c + i] = 0u;
-          continue;
-        }
+        for (int i = 0; i < 16; ++i) pk[i] = 0u;
+      } else {
         float x[32], y[32];
-        tmem_ld32(lane_base + h * 64 + 32 * c, x);
-        tmem_ld32(lane_base + 128 + h * 64 + 32 * c, y);
+        tmem_ld32(lane_base + h * 64 + 32 * half, x);
+        tmem_ld32(lane_base + 128 + h * 64 + 32 * half, y);
         tmem_wait_ld();
         if (kind == 1) {
 #pragma unroll
@@ -1423,33 +1425,35 @@ __global__ void __launch_bounds__(320, 1)
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const int col = 32 * c + i;
+            const int col = 32 * half + i;
             const float p = (col >= lo && col < hi) ? ex2_approx(fmaf(x[i], sl2, -L2e)) : 0.f;
             x[i] = p * (y[i] - dl);
           }
         }
 #pragma unroll
-        for (int i = 0; i < 16; ++i) pk[16 * c + i] = pack_bf16x2(x[2 * i], x[2 * i + 1]);
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(x[2 * i], x[2 * i + 1]);
       }
-      // over the dP columns this thread has just read (the tile's dP MMA is complete)
-      tmem_st32_words(lane_base + 128 + h * 64, pk);
+      // over the first 16 of the dP columns this warp has just read (the tile's dP MMA is complete)
+      tmem_st16_words(lane_base + 128 + h * 64 + 32 * half, pk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&ds_full[h]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ds_full[h]);
     }
     if (!ok) *abort_flag = 1;
     const bool done = ok && nt > 0 && mbar_wait(&ds_empty[h], (nt - 1) & 1);
     tc_fence_after();
     float* out = dq + qi * D;
 #pragma unroll 1
-    for (int c = 0; c < D / 32; ++c) {
+    for (int c = 0; c < D / 64; ++c) {  // this warp's half of the head dimension
+      const int col0 = half * (D / 2) + 32 * c;
       float v[32];
-      tmem_ld32(lane_base + 256 + h * 128 + c * 32, v);
+      tmem_ld32(lane_base + 256 + h * 128 + col0, v);
       tmem_wait_ld();
       if (live && done) {
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
-          const int e = c * 32 + i;
+          const int e = col0 + i;
           float4 w4 = make_float4(v[i] * scale, v[i + 1] * scale, v[i + 2] * scale, v[i + 3] * scale);
           if (e >= hd) w4 = make_float4(0.f, 0.f, 0.f, 0.f);
           *reinterpret_cast<float4*>(out + e) = w4;

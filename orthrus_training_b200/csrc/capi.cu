@@ -523,7 +523,7 @@ static int attn_bwd_impl(const void* q, const void* k1, const void* v1, int64_t 
       if (D == 128) {
         if (set_smem(attn_dq_tc2_kernel<128>, Dq2Smem<128>::SMEM)) return ORTHRUS_ECUDA;
         if (set_smem(attn_dkdv_tc_kernel<128>, DkvSmem<128>::SMEM)) return ORTHRUS_ECUDA;
-        ORTHRUS_CHECK_CUDA(launch_pdl(attn_dq_tc2_kernel<128>, grid2, dim3(320), Dq2Smem<128>::SMEM, st, m64.q,
+        ORTHRUS_CHECK_CUDA(launch_pdl(attn_dq_tc2_kernel<128>, grid2, dim3(kDq2Threads), Dq2Smem<128>::SMEM, st, m64.q,
                                       m64.dout, m64.k1, m64.v1, m64.k2, m64.v2, Hq, Hkv, Tq, hd, scale, mp, true,
                                       lse, static_cast<const float*>(delta), dq));
         ORTHRUS_CHECK_LAUNCH();
@@ -553,7 +553,7 @@ static int attn_bwd_impl(const void* q, const void* k1, const void* v1, int64_t 
       } else {
         if (set_smem(attn_dq_tc2_kernel<64>, Dq2Smem<64>::SMEM)) return ORTHRUS_ECUDA;
         if (set_smem(attn_dkdv_tc_kernel<64>, DkvSmem<64>::SMEM)) return ORTHRUS_ECUDA;
-        attn_dq_tc2_kernel<64><<<grid2, 320, Dq2Smem<64>::SMEM, st>>>(
+        attn_dq_tc2_kernel<64><<<grid2, kDq2Threads, Dq2Smem<64>::SMEM, st>>>(
             m64.q, m64.dout, m64.k1, m64.v1, m64.k2, m64.v2, Hq, Hkv, Tq, hd, scale, mp, true, lse, delta, dq);
         ORTHRUS_CHECK_LAUNCH();
         ORTHRUS_CHECK_CUDA(cudaStreamWaitEvent(side->stream, side->fork, 0));

@@ -278,6 +278,16 @@ __device__ __forceinline__ void tmem_st32_words(uint32_t taddr, const uint32_t* 
       : "memory");
 }
 
+// Stores 16 consecutive 32-bit words (e.g. packed bf16 pairs) into this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st16_words(uint32_t taddr, const uint32_t* w) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7]), "r"(w[8]), "r"(w[9]),
+      "r"(w[10]), "r"(w[11]), "r"(w[12]), "r"(w[13]), "r"(w[14]), "r"(w[15])
+      : "memory");
+}
+
 // Stores 16 consecutive fp32 columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
   asm volatile(
