@@ -749,6 +749,38 @@ int orthrus_attn_bwd_doc(const void* q, const void* k1, const void* v1, int64_t 
 
 }  // extern "C"
 
+namespace {
+
+// The register-resident RMSNorm kernels take bf16 rows of 256, 512, 1024 or 2048 elements (one to
+// eight 16-byte vectors per lane); other widths keep the strided kernels.
+int rmsnorm_reg_chunks(int d) { return (d == 256 || d == 512 || d == 1024 || d == 2048) ? d / 256 : 0; }
+
+cudaError_t rmsnorm_fwd_reg(int chunks, unsigned blocks, cudaStream_t st, const __nv_bfloat16* x,
+                            const __nv_bfloat16* w, int64_t rows, float eps, __nv_bfloat16* y, float* rstd) {
+  using T = __nv_bfloat16;
+  switch (chunks) {
+    case 1: return launch_pdl(rmsnorm_fwd_reg_kernel<T, 1>, dim3(blocks), dim3(256), 0, st, x, w, rows, eps, y, rstd);
+    case 2: return launch_pdl(rmsnorm_fwd_reg_kernel<T, 2>, dim3(blocks), dim3(256), 0, st, x, w, rows, eps, y, rstd);
+    case 4: return launch_pdl(rmsnorm_fwd_reg_kernel<T, 4>, dim3(blocks), dim3(256), 0, st, x, w, rows, eps, y, rstd);
+    default: return launch_pdl(rmsnorm_fwd_reg_kernel<T, 8>, dim3(blocks), dim3(256), 0, st, x, w, rows, eps, y, rstd);
+  }
+}
+
+template <bool ADD>
+cudaError_t rmsnorm_bwd_reg(int chunks, unsigned blocks, cudaStream_t st, const __nv_bfloat16* x,
+                            const __nv_bfloat16* w, const float* rstd, const __nv_bfloat16* dy, int64_t rows,
+                            __nv_bfloat16* dx, const __nv_bfloat16* dres) {
+  using T = __nv_bfloat16;
+  switch (chunks) {
+    case 1: return launch_pdl(rmsnorm_bwd_reg_kernel<T, 1, ADD>, dim3(blocks), dim3(256), 0, st, x, w, rstd, dy, rows, dx, dres);
+    case 2: return launch_pdl(rmsnorm_bwd_reg_kernel<T, 2, ADD>, dim3(blocks), dim3(256), 0, st, x, w, rstd, dy, rows, dx, dres);
+    case 4: return launch_pdl(rmsnorm_bwd_reg_kernel<T, 4, ADD>, dim3(blocks), dim3(256), 0, st, x, w, rstd, dy, rows, dx, dres);
+    default: return launch_pdl(rmsnorm_bwd_reg_kernel<T, 8, ADD>, dim3(blocks), dim3(256), 0, st, x, w, rstd, dy, rows, dx, dres);
+  }
+}
+
+}  // namespace
+
 extern "C" int orthrus_rmsnorm(const void* x, const void* w, int64_t rows, int d, float eps, void* y, float* rstd,
                                int dtype, void* stream) {
   ORTHRUS_CHECK_ARG(x && w && y && rows >= 0 && d > 0);
@@ -757,7 +789,10 @@ extern "C" int orthrus_rmsnorm(const void* x, const void* w, int64_t rows, int d
   const bool vec = aligned16(x) && aligned16(w) && aligned16(y) && d % (dtype == ORTHRUS_BF16 ? 256 : 128) == 0;
   if (dtype == ORTHRUS_BF16) {
     using T = __nv_bfloat16;
-    if (vec)
+    if (vec && rmsnorm_reg_chunks(d) > 0)
+      ORTHRUS_CHECK_CUDA(rmsnorm_fwd_reg(rmsnorm_reg_chunks(d), blocks, as_stream(stream), static_cast<const T*>(x),
+                                         static_cast<const T*>(w), rows, eps, static_cast<T*>(y), rstd));
+    else if (vec)
       ORTHRUS_CHECK_CUDA(launch_pdl(rmsnorm_fwd_vec_kernel<T>, dim3(blocks), dim3(256), 0, as_stream(stream),
                                     static_cast<const T*>(x), static_cast<const T*>(w), rows, d, eps,
                                     static_cast<T*>(y), rstd));
@@ -785,10 +820,16 @@ extern "C" int orthrus_rmsnorm_bwd_add(const void* x, const void* w, const float
   ORTHRUS_CHECK_ARG(aligned16(x) && aligned16(w) && aligned16(dy) && aligned16(dres) && aligned16(dx));
   if (rows == 0) return ORTHRUS_OK;
   using T = __nv_bfloat16;
-  ORTHRUS_CHECK_CUDA(launch_pdl(rmsnorm_bwd_vec_kernel<T>, dim3(static_cast<unsigned>(ceil_div(rows, 8))),
-                                dim3(256), 0, as_stream(stream), static_cast<const T*>(x),
-                                static_cast<const T*>(w), rstd, static_cast<const T*>(dy), rows, d,
-                                static_cast<T*>(dx), static_cast<const T*>(dres)));
+  if (rmsnorm_reg_chunks(d) > 0)
+    ORTHRUS_CHECK_CUDA(rmsnorm_bwd_reg<true>(rmsnorm_reg_chunks(d), static_cast<unsigned>(ceil_div(rows, 8)),
+                                             as_stream(stream), static_cast<const T*>(x), static_cast<const T*>(w),
+                                             rstd, static_cast<const T*>(dy), rows, static_cast<T*>(dx),
+                                             static_cast<const T*>(dres)));
+  else
+    ORTHRUS_CHECK_CUDA(launch_pdl(rmsnorm_bwd_vec_kernel<T>, dim3(static_cast<unsigned>(ceil_div(rows, 8))),
+                                  dim3(256), 0, as_stream(stream), static_cast<const T*>(x),
+                                  static_cast<const T*>(w), rstd, static_cast<const T*>(dy), rows, d,
+                                  static_cast<T*>(dx), static_cast<const T*>(dres)));
   ORTHRUS_CHECK_LAUNCH();
   return ORTHRUS_OK;
 }
@@ -802,7 +843,11 @@ extern "C" int orthrus_rmsnorm_bwd(const void* x, const void* w, const float* rs
                    d % (dtype == ORTHRUS_BF16 ? 256 : 128) == 0;
   if (dtype == ORTHRUS_BF16) {
     using T = __nv_bfloat16;
-    if (vec)
+    if (vec && rmsnorm_reg_chunks(d) > 0)
+      ORTHRUS_CHECK_CUDA(rmsnorm_bwd_reg<false>(rmsnorm_reg_chunks(d), blocks, as_stream(stream), static_cast<const T*>(x),
+                                                static_cast<const T*>(w), rstd, static_cast<const T*>(dy), rows,
+                                                static_cast<T*>(dx), static_cast<const T*>(nullptr)));
+    else if (vec)
       ORTHRUS_CHECK_CUDA(launch_pdl(rmsnorm_bwd_vec_kernel<T>, dim3(blocks), dim3(256), 0, as_stream(stream),
                                     static_cast<const T*>(x), static_cast<const T*>(w), rstd,
                                     static_cast<const T*>(dy), rows, d, static_cast<T*>(dx),

@@ -21,6 +21,19 @@ struct Vec16 {
 };
 
 template <typename T>
+__device__ __forceinline__ void unpack16(const uint4 raw, float* v) {
+  if constexpr (sizeof(T) == 2) {
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(h[i]);
+  } else {
+    const float* f = reinterpret_cast<const float*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = f[i];
+  }
+}
+
+template <typename T>
 __device__ __forceinline__ void load16(const T* p, float* v) {
   const uint4 raw = *reinterpret_cast<const uint4*>(p);
   if constexpr (sizeof(T) == 2) {
@@ -83,6 +96,107 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_vec_kernel(const T* __restric
     store16<T>(yr + c, v);
   }
   if (rstd_out != nullptr && lane == 0) rstd_out[r] = rstd;
+}
+
+// Same forward with the row held in registers, for d = CH * 32 * N: every lane issues all of its
+// 16-byte loads (x and w) before the first use, so a warp has its whole row in flight instead of
+// one vector at a time, and x is read once. The per-lane order of the sums and the arithmetic are
+// those of rmsnorm_fwd_vec_kernel, so the two give identical bits.
+template <typename T, int CH>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_reg_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                              int64_t rows, float eps, T* __restrict__ y,
+                                                              float* __restrict__ rstd_out) {
+  constexpr int N = Vec16<T>::N;
+  constexpr int D = CH * 32 * N;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  griddep_launch_dependents();  // launched as a programmatic dependent
+  griddep_wait();
+  if (r >= rows) return;
+  const T* xr = x + r * D;
+  uint4 xs[CH], ws[CH];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) xs[c] = *reinterpret_cast<const uint4*>(xr + (c * 32 + lane) * N);
+#pragma unroll
+  for (int c = 0; c < CH; ++c) ws[c] = *reinterpret_cast<const uint4*>(w + (c * 32 + lane) * N);
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    float v[N];
+    unpack16<T>(xs[c], v);
+#pragma unroll
+    for (int i = 0; i < N; ++i) ss = fmaf(v[i], v[i], ss);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float rstd = rsqrtf(ss / static_cast<float>(D) + eps);
+  T* yr = y + r * D;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    float v[N], wv[N];
+    unpack16<T>(xs[c], v);
+    unpack16<T>(ws[c], wv);
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = wv[i] * round_to_t<T>(v[i] * rstd);
+    store16<T>(yr + (c * 32 + lane) * N, v);
+  }
+  if (rstd_out != nullptr && lane == 0) rstd_out[r] = rstd;
+}
+
+// Same backward with x, dy, w (and dres) held in registers, all loads issued up front; identical
+// bits to rmsnorm_bwd_vec_kernel.
+template <typename T, int CH, bool ADD>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                              const float* __restrict__ rstd, const T* __restrict__ dy,
+                                                              int64_t rows, T* __restrict__ dx,
+                                                              const T* __restrict__ dres) {
+  constexpr int N = Vec16<T>::N;
+  constexpr int D = CH * 32 * N;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  griddep_launch_dependents();  // launched as a programmatic dependent
+  griddep_wait();
+  if (r >= rows) return;
+  const float rs = rstd[r];
+  uint4 xs[CH], gs[CH], ws[CH], as[ADD ? CH : 1];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int64_t off = r * D + (c * 32 + lane) * N;
+    xs[c] = *reinterpret_cast<const uint4*>(x + off);
+    gs[c] = *reinterpret_cast<const uint4*>(dy + off);
+    if constexpr (ADD) as[c] = *reinterpret_cast<const uint4*>(dres + off);
+  }
+#pragma unroll
+  for (int c = 0; c < CH; ++c) ws[c] = *reinterpret_cast<const uint4*>(w + (c * 32 + lane) * N);
+  float dot = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    float v[N], g[N], wv[N];
+    unpack16<T>(xs[c], v);
+    unpack16<T>(gs[c], g);
+    unpack16<T>(ws[c], wv);
+#pragma unroll
+    for (int i = 0; i < N; ++i) dot = fmaf(g[i] * wv[i], v[i] * rs, dot);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+  const float mean = dot / static_cast<float>(D);
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    float v[N], g[N], wv[N];
+    unpack16<T>(xs[c], v);
+    unpack16<T>(gs[c], g);
+    unpack16<T>(ws[c], wv);
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = rs * (g[i] * wv[i] - v[i] * rs * mean);
+    if constexpr (ADD) {
+      float a[N];
+      unpack16<T>(as[c], a);
+#pragma unroll
+      for (int i = 0; i < N; ++i) v[i] += a[i];
+    }
+    store16<T>(dx + r * D + (c * 32 + lane) * N, v);
+  }
 }
 
 // dx = rstd * (w dy - xhat * mean(w dy xhat)), xhat = x * rstd.

@@ -17,7 +17,8 @@ def _ops():
 
 
 @pytest.mark.parametrize("dtype,d", [(torch.float32, 1024), (torch.float32, 64), (torch.bfloat16, 1024),
-                                     (torch.bfloat16, 128)])
+                                     (torch.bfloat16, 128), (torch.bfloat16, 256), (torch.bfloat16, 768),
+                                     (torch.bfloat16, 2048)])
 def test_rmsnorm_forward_backward(dtype, d):
     g = torch.Generator().manual_seed(d)
     x = (torch.randn(333, d, generator=g) * 3).to(dtype)
