@@ -915,6 +915,15 @@ __global__ void __launch_bounds__(320, 1)
   // the operands and the outputs belong to the stream order only after griddep_wait()
   griddep_launch_dependents();
   griddep_wait();
+  if (warp == 0 && elect_one()) {  // Q does not depend on the tile map: its load overlaps it
+    mbar_arrive_expect_tx(q_full, 2 * S::TILE);
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int c = 0; c < S::BOXES; ++c)
+        tma_load_3d(smem + S::OFF_Q + h * S::TILE + c * kAttnTileBytes, &tmQ, q_full, c * 64,
+                    static_cast<int>(q0), static_cast<int>(b * Hq + 2 * pair + h));
+  }
   attn_tile_map(mp, b, q0, Tq, has2, wg == 0 ? row : -1, red, tiles);
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -923,13 +932,6 @@ __global__ void __launch_bounds__(320, 1)
 
   if (warp == 0) {
     if (elect_one()) {
-      mbar_arrive_expect_tx(q_full, 2 * S::TILE);
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int c = 0; c < S::BOXES; ++c)
-          tma_load_3d(smem + S::OFF_Q + h * S::TILE + c * kAttnTileBytes, &tmQ, q_full, c * 64,
-                      static_cast<int>(q0), static_cast<int>(b * Hq + 2 * pair + h));
       // K and V tiles share a ring of three slots with K one tile ahead of V: K(0), K(1), V(0),
       // K(2), V(1), ..., V(nt - 1). A load may start once the tile three places before it in this
       // order has been consumed, so K(j + 1) is in flight while tile j - 1 is still being read.
@@ -1261,6 +1263,20 @@ __global__ void __launch_bounds__(kDq2Threads, 1)
   // the operands and the outputs belong to the stream order only after griddep_wait()
   griddep_launch_dependents();
   griddep_wait();
+  if (warp == 0 && elect_one()) {  // Q and dO do not depend on the tile map: their loads overlap it
+    mbar_arrive_expect_tx(in_full, 4 * S::QT);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int hh = 2 * pair + h;
+#pragma unroll
+      for (int c = 0; c < S::BOXES; ++c) {
+        tma_load_3d(smem + S::OFF_Q + h * S::QT + c * kAttnTileBytes, &tmQ, in_full, c * 64,
+                    static_cast<int>(q0), static_cast<int>(b * Hq + hh));
+        tma_load_3d(smem + S::OFF_DO + h * S::QT + c * kAttnTileBytes, &tmDO, in_full, c * 64 + hh * hd,
+                    static_cast<int>(q0), static_cast<int>(b));
+      }
+    }
+  }
   attn_tile_map(mp, b, q0, Tq, has2, (wg == 0 && half == 0) ? row : -1, red, tiles);
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -1272,18 +1288,6 @@ __global__ void __launch_bounds__(kDq2Threads, 1)
 
   if (warp == 0) {
     if (elect_one()) {
-      mbar_arrive_expect_tx(in_full, 4 * S::QT);
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int hh = 2 * pair + h;
-#pragma unroll
-        for (int c = 0; c < S::BOXES; ++c) {
-          tma_load_3d(smem + S::OFF_Q + h * S::QT + c * kAttnTileBytes, &tmQ, in_full, c * 64,
-                      static_cast<int>(q0), static_cast<int>(b * Hq + hh));
-          tma_load_3d(smem + S::OFF_DO + h * S::QT + c * kAttnTileBytes, &tmDO, in_full, c * 64 + hh * hd,
-                      static_cast<int>(q0), static_cast<int>(b));
-        }
-      }
       int issued = 0;
       for (int j = 0; j < nt; ++j) {
         const int s = j % NS;
