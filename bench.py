@@ -426,6 +426,27 @@ def _kc_time(fn, iters: int, warmup: int) -> float:
     return e0.elapsed_time(e1) / iters
 
 
+def _kc_time_graph(fn, iters: int, warmup: int) -> float:
+    """Milliseconds per call of fn with `iters` calls captured in one CUDA graph and replayed, for
+    kernels shorter than the host's per-call cost of the Python wrapper (back-to-back eager calls
+    would time the host)."""
+    for _ in range(max(warmup, 1)):
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(iters):
+            fn()
+    graph.replay()  # the first replay uploads the graph
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
 def _kc_dual_inputs(gen, dev, B, L, A, K):
     Tq = A * K
     rnd = lambda *shape: torch.randn(*shape, device=dev, generator=gen).bfloat16()  # noqa: E731
@@ -485,6 +506,28 @@ def kernel_case(case: str, iters: int, warmup: int) -> dict:
         timed.append(("qkv_prep_bwd", lambda: ops.qkv_prep_backward(qkv, pos, inv, qw, kw, rstd, dq, dk, dv, B, L,
                                                                     HQ, HKV, HD, HD),
                       rows * H * HD * (2 + 4 + 2), "gbs"))
+    elif case == "rownorm":
+        # RMSNorm forward and backward (with the residual gradient) at the teacher's 16384 x 1024;
+        # four input sets (about 270 MB) rotate so that no call finds its rows in L2
+        import itertools
+
+        rows, d = B * L, 1024
+        sets = [(rnd(rows, d), rnd(rows, d), rnd(rows, d)) for _ in range(4)]  # x, dy, residual grad
+        w = (1 + rnd(d, scale=0.1).float()).bfloat16()
+        rstds = [ops.rms_norm(x, w, 1e-6, want_rstd=True)[1] for x, _, _ in sets]
+        turn = itertools.count()
+
+        def norm_fwd():
+            return ops.rms_norm(sets[next(turn) % 4][0], w, 1e-6)
+
+        def norm_bwd():
+            i = next(turn) % 4
+            x, dy, dres = sets[i]
+            return ops.rms_norm_backward(x, w, rstds[i], dy, dres=dres)
+
+        # timed as graph replays: an eager call of the wrapper costs the host longer than the kernel
+        timed.append(("rmsnorm_fwd", norm_fwd, 2 * rows * d * 2, "gbs", _kc_time_graph))  # x in, y out
+        timed.append(("rmsnorm_bwd_add", norm_bwd, 4 * rows * d * 2, "gbs", _kc_time_graph))  # x, dy, dres in; dx out
     elif case == "linear":
         rows, d, ff, hq = B * L, 1024, 3072, HQ * HD
         x, o, a = rnd(rows, d), rnd(rows, hq), rnd(rows, ff)
@@ -564,8 +607,8 @@ def kernel_case(case: str, iters: int, warmup: int) -> dict:
     else:
         raise ValueError(f"unknown kernel case {case!r}")
     out = {}
-    for name, fn, work, unit in timed:
-        ms = _kc_time(fn, iters, warmup)
+    for name, fn, work, unit, *how in timed:
+        ms = (how[0] if how else _kc_time)(fn, iters, warmup)
         rate = work / (ms / 1e3) / (1e9 if unit == "gbs" else 1e12)
         out[name] = {"ms_per_call": round(ms, 4), unit: round(float(rate), 1)}
     return out
@@ -891,8 +934,8 @@ def main():
                     help="run one eager draft + verify cycle at this batch between profiler start / stop "
                          "(for ncu --profile-from-start off) and print its CUDA-event time")
     ap.add_argument("--kernel-case", default=None,
-                    choices=["causal", "dual", "dualbwd", "lmhead", "prologue", "linear", "linear2", "decode_proj",
-                             "sweep"],
+                    choices=["causal", "dual", "dualbwd", "lmhead", "prologue", "rownorm", "linear", "linear2",
+                             "decode_proj", "sweep"],
                     help="time one hot entry point alone (--steps calls after --warmup)")
     args = ap.parse_args()
     if args.warmup < 3 and args.kernel_case is None:
